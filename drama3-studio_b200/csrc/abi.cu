@@ -1,0 +1,251 @@
+// extern "C" entry points: validation first, then launches on the caller's
+// stream. Status/error conventions follow the reference's native ABI v1
+// (native/src/runtime.cpp:278-290: status 0/-1 plus a thread-local message).
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace drama {
+
+namespace {
+thread_local std::string g_error;
+int g_sm_count[64] = {0};
+
+bool float_dtype(int d) { return d == DRAMA_B200_F32 || d == DRAMA_B200_F16 || d == DRAMA_B200_BF16; }
+bool index_dtype(int d) { return d == DRAMA_B200_I32 || d == DRAMA_B200_I64; }
+size_t dtype_size(int d) {
+    switch (d) {
+        case DRAMA_B200_F32: case DRAMA_B200_I32: return 4;
+        case DRAMA_B200_I64: return 8;
+        default: return 2;
+    }
+}
+bool overlaps(const void* a, size_t na, const void* b, size_t nb) {
+    if (!a || !b || !na || !nb) return false;
+    const uintptr_t x = reinterpret_cast<uintptr_t>(a), y = reinterpret_cast<uintptr_t>(b);
+    return x < y + nb && y < x + na;
+}
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int sm_count_current(int* out) {
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess) return fail("cudaGetDevice: %s", cudaGetErrorString(err));
+    if (dev < 0 || dev >= 64) return fail("device ordinal %d out of range", dev);
+    if (!g_sm_count[dev]) {
+        int major = 0, count = 0;
+        cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+        err = cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev);
+        if (err != cudaSuccess) return fail("device query: %s", cudaGetErrorString(err));
+        if (major != 10) return fail("device %d is sm_%d0; this library is built for sm_100a only", dev, major);
+        g_sm_count[dev] = count;
+    }
+    *out = g_sm_count[dev];
+    return 0;
+}
+}  // namespace
+
+void set_error(const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_error = buf;
+}
+
+int fail(const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_error = buf;
+    return -1;
+}
+
+int check_launch(const char* what) {
+    const cudaError_t err = cudaGetLastError();
+    if (err != cudaSuccess) return fail("%s launch failed: %s", what, cudaGetErrorString(err));
+    return 0;
+}
+
+namespace {
+
+int validate_decode_common(const void* x, int x_dtype, int64_t tokens, int top_k, const void* ids,
+                           int ids_dtype, const void* weights, int weights_dtype, const void* out,
+                           const float* pair_out, int hidden, int intermediate, int slots) {
+    if (!x || !ids || !weights) return fail("x, ids and weights are required");
+    if (!out && !pair_out) return fail("either out or pair_out is required");
+    if (!float_dtype(x_dtype)) return fail("x must be float32, float16 or bfloat16");
+    if (!float_dtype(weights_dtype)) return fail("routing weights must be floating point");
+    if (!index_dtype(ids_dtype)) return fail("expert IDs must be int32 or int64");
+    if (tokens < 0 || top_k < 1) return fail("tokens must be >= 0 and top_k >= 1");
+    if (tokens * top_k > kMaxDecodePairs)
+        return fail("decode supports at most %d (token, slot) pairs; got %lld", kMaxDecodePairs,
+                    static_cast<long long>(tokens * top_k));
+    if (hidden < 128 || hidden % 128 || intermediate < 128 || intermediate % 128)
+        return fail("hidden and intermediate must be positive multiples of 128");
+    if (slots < 1 || slots > kMaxSlots) return fail("slots must be in [1, %d]", kMaxSlots);
+    const size_t xb = static_cast<size_t>(tokens) * hidden * dtype_size(x_dtype);
+    if (out && overlaps(out, xb, x, xb)) return fail("output must not overlap the hidden states");
+    if (pair_out && overlaps(pair_out, static_cast<size_t>(tokens) * top_k * hidden * 4, x, xb))
+        return fail("pair output must not overlap the hidden states");
+    return 0;
+}
+
+int finish_decode(DecodeArgs& a, void* workspace, size_t workspace_bytes, void* stream) {
+    if (a.tokens == 0) return 0;
+    int sms = 0;
+    if (sm_count_current(&sms)) return -1;
+    const size_t need = decode_workspace_layout(a.tokens, a.top_k, a.hidden, a.intermediate, sms, nullptr, nullptr);
+    if (!workspace || workspace_bytes < need)
+        return fail("decode workspace too small: need %zu bytes, got %zu", need, workspace_bytes);
+    if (reinterpret_cast<uintptr_t>(workspace) & 255u) return fail("workspace must be 256-byte aligned");
+    decode_workspace_layout(a.tokens, a.top_k, a.hidden, a.intermediate, sms, static_cast<char*>(workspace), &a.ws);
+    a.ctas = sms * kDecodeCtasPerSm;
+    a.workers_up = a.workers_dn = a.ctas * kDecodeWarps;
+    const cudaError_t err = decode_launch(a, static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return fail("decode launch failed: %s", cudaGetErrorString(err));
+    return 0;
+}
+
+}  // namespace
+}  // namespace drama
+
+using namespace drama;
+
+extern "C" {
+
+int drama_b200_abi(void) { return DRAMA_B200_ABI_VERSION; }
+
+const char* drama_b200_error(void) { return g_error.c_str(); }
+
+int drama_b200_device_check(int device, int* sm_count) {
+    cudaDeviceProp prop;
+    const cudaError_t err = cudaGetDeviceProperties(&prop, device);
+    if (err != cudaSuccess) return fail("cudaGetDeviceProperties(%d): %s", device, cudaGetErrorString(err));
+    if (prop.major != 10) return fail("device %d (%s) is sm_%d%d; drama_b200 needs sm_100", device, prop.name, prop.major, prop.minor);
+    if (sm_count) *sm_count = prop.multiProcessorCount;
+    return 0;
+}
+
+int drama_b200_route_topk(const void* logits, int logits_dtype, int64_t tokens, int experts, int top_k,
+                          int renormalize, void* ids, int ids_dtype, void* weights, int weights_dtype,
+                          void* stream) {
+    if (!logits || !ids || !weights) return fail("logits, ids and weights are required");
+    if (!float_dtype(logits_dtype) || !float_dtype(weights_dtype)) return fail("logits/weights dtype must be floating point");
+    if (!index_dtype(ids_dtype)) return fail("ids must be int32 or int64");
+    if (tokens < 0 || experts < 1 || experts > 1024) return fail("experts must be in [1, 1024]");
+    if (top_k < 1 || top_k > 32 || top_k > experts) return fail("top_k must be in [1, min(32, experts)]");
+    if (renormalize != 0 && renormalize != 1) return fail("renormalize must be 0 or 1");
+    const size_t lb = static_cast<size_t>(tokens) * experts * dtype_size(logits_dtype);
+    if (overlaps(ids, tokens * top_k * dtype_size(ids_dtype), logits, lb) ||
+        overlaps(weights, tokens * top_k * dtype_size(weights_dtype), logits, lb))
+        return fail("router outputs must not overlap the logits");
+    if (tokens == 0) return 0;
+    RouteArgs a{logits, logits_dtype, tokens, experts, top_k, renormalize, ids, ids_dtype, weights, weights_dtype};
+    const cudaError_t err = route_topk(a, static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return fail("route_topk launch failed: %s", cudaGetErrorString(err));
+    return 0;
+}
+
+int drama_b200_permute_routes(const void* ids, int ids_dtype, int64_t pairs, int experts, int64_t* order,
+                              int64_t* counts, int64_t* offsets, int32_t* status, void* stream) {
+    if (!ids || !order || !counts || !offsets) return fail("ids, order, counts and offsets are required");
+    if (!index_dtype(ids_dtype)) return fail("ids must be int32 or int64");
+    if (pairs < 0 || pairs > (int64_t(1) << 24)) return fail("pairs must be in [0, 2^24]");
+    if (experts < 1 || experts > 1024) return fail("experts must be in [1, 1024]");
+    PermuteArgs a{ids, ids_dtype, pairs, experts, order, counts, offsets, status};
+    const cudaError_t err = permute_routes(a, static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return fail("permute_routes launch failed: %s", cudaGetErrorString(err));
+    return 0;
+}
+
+size_t drama_b200_decode_workspace_bytes(int64_t tokens, int top_k, int hidden, int intermediate) {
+    int sms = 0;
+    if (sm_count_current(&sms)) sms = 148;
+    return decode_workspace_layout(tokens, top_k, hidden, intermediate, sms, nullptr, nullptr);
+}
+
+size_t drama_b200_decode_status_offset(void) { return 0; }
+
+int drama_b200_fp8_decode(const DramaB200Fp8Bank* bank, const void* x, int x_dtype, int64_t tokens,
+                          int top_k, const void* ids, int ids_dtype, const void* weights, int weights_dtype,
+                          void* out, float* pair_out, void* workspace, size_t workspace_bytes, void* stream) {
+    if (!bank) return fail("bank is required");
+    const DramaB200Fp8Bank& b = *bank;
+    if (validate_decode_common(x, x_dtype, tokens, top_k, ids, ids_dtype, weights, weights_dtype, out, pair_out,
+                               b.hidden, b.intermediate, b.slots))
+        return -1;
+    if (!b.w13 || !b.w13_scale || !b.w2 || !b.w2_scale) return fail("FP8 bank pointers are required");
+    if (!aligned16(b.w13) || !aligned16(b.w2) || b.w13_row_stride % 16 || b.w2_row_stride % 16 ||
+        b.w13_slot_stride % 16 || b.w2_slot_stride % 16)
+        return fail("FP8 weight rows must start on 16-byte boundaries");
+    if (b.w13_row_stride < b.hidden || b.w2_row_stride < b.intermediate ||
+        b.w13_slot_stride < b.w13_row_stride * 2 * b.intermediate ||
+        b.w2_slot_stride < b.w2_row_stride * b.hidden)
+        return fail("FP8 weight strides are smaller than the bank geometry");
+    if (b.w13_scale_row_stride < b.hidden / 128 || b.w2_scale_row_stride < b.intermediate / 128)
+        return fail("FP8 scale strides are smaller than the bank geometry");
+    DecodeArgs a{};
+    a.format = 0;
+    a.fp8 = b;
+    a.x = x;
+    a.x_dtype = x_dtype;
+    a.tokens = tokens;
+    a.top_k = top_k;
+    a.ids = ids;
+    a.ids_dtype = ids_dtype;
+    a.weights = weights;
+    a.weights_dtype = weights_dtype;
+    a.out = out;
+    a.pair_out = pair_out;
+    a.hidden = b.hidden;
+    a.intermediate = b.intermediate;
+    a.slots = b.slots;
+    return finish_decode(a, workspace, workspace_bytes, stream);
+}
+
+int drama_b200_int4_decode(const DramaB200Int4Bank* bank, const void* x, int x_dtype, int64_t tokens,
+                           int top_k, const void* ids, int ids_dtype, const void* weights, int weights_dtype,
+                           void* out, float* pair_out, void* workspace, size_t workspace_bytes, void* stream) {
+    if (!bank) return fail("bank is required");
+    const DramaB200Int4Bank& b = *bank;
+    if (validate_decode_common(x, x_dtype, tokens, top_k, ids, ids_dtype, weights, weights_dtype, out, pair_out,
+                               b.hidden, b.intermediate, b.slots))
+        return -1;
+    if (!b.w13 || !b.w13_scale || !b.w2 || !b.w2_scale) return fail("INT4 bank pointers are required");
+    if (b.scale_dtype != DRAMA_B200_BF16 && b.scale_dtype != DRAMA_B200_F16)
+        return fail("INT4 scales must be bfloat16 or float16");
+    if (!aligned16(b.w13) || !aligned16(b.w2) || b.w13_row_stride % 4 || b.w2_row_stride % 4 ||
+        b.w13_slot_stride % 4 || b.w2_slot_stride % 4)
+        return fail("INT4 weight rows must start on 16-byte boundaries");
+    if (b.w13_row_stride < b.hidden / 8 || b.w2_row_stride < b.intermediate / 8 ||
+        b.w13_slot_stride < b.w13_row_stride * 2 * b.intermediate ||
+        b.w2_slot_stride < b.w2_row_stride * b.hidden)
+        return fail("INT4 weight strides are smaller than the bank geometry");
+    DecodeArgs a{};
+    a.format = 1;
+    a.int4 = b;
+    a.x = x;
+    a.x_dtype = x_dtype;
+    a.tokens = tokens;
+    a.top_k = top_k;
+    a.ids = ids;
+    a.ids_dtype = ids_dtype;
+    a.weights = weights;
+    a.weights_dtype = weights_dtype;
+    a.out = out;
+    a.pair_out = pair_out;
+    a.hidden = b.hidden;
+    a.intermediate = b.intermediate;
+    a.slots = b.slots;
+    return finish_decode(a, workspace, workspace_bytes, stream);
+}
+
+}  // extern "C"

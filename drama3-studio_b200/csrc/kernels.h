@@ -1,0 +1,110 @@
+// Internal kernel entry points and argument blocks (host side of the ABI).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "drama_b200.h"
+
+namespace drama {
+
+// Launch with programmatic stream serialisation: the kernel may start while
+// its predecessor drains and calls griddepcontrol.wait before reading inputs.
+template <typename Kernel, typename... Args>
+cudaError_t launch_pdl(Kernel kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+struct RouteArgs {
+    const void* logits;
+    int logits_dtype;
+    int64_t tokens;
+    int experts;
+    int top_k;
+    int renormalize;
+    void* ids;
+    int ids_dtype;
+    void* weights;
+    int weights_dtype;
+};
+cudaError_t route_topk(const RouteArgs& a, cudaStream_t s);
+
+struct PermuteArgs {
+    const void* ids;
+    int ids_dtype;
+    int64_t pairs;
+    int experts;
+    int64_t* order;
+    int64_t* counts;
+    int64_t* offsets;
+    int32_t* status;
+};
+cudaError_t permute_routes(const PermuteArgs& a, cudaStream_t s);
+size_t bucket_smem_bytes(int experts);
+
+// ---------------------------------------------------------------------------
+// Decode (K1) workspace carved out of one caller buffer.
+// ---------------------------------------------------------------------------
+constexpr int kDecodeWarps = 8;          // warps per CTA of the GEMV kernels
+constexpr int kDecodeCtasPerSm = 2;      // resident CTAs per SM
+constexpr int kGroupTokens = 8;          // tokens per expert group (one n8 MMA)
+constexpr int kMaxDecodePairs = 4096;
+constexpr int kMaxSlots = 1024;
+
+struct DecodeWorkspace {
+    int32_t* status;      // [4]
+    int32_t* num_groups;  // [1]
+    int32_t* order;       // [P]   pairs sorted by slot (stable)
+    int32_t* g_slot;      // [P]
+    int32_t* g_start;     // [P]
+    int32_t* g_count;     // [P]
+    float* xscale;        // [T]   2^e per token row
+    uint16_t* x16;        // [T][H] f16 copy of x * 2^-e (layout per format)
+    float* wts;           // [P]   route weights as fp32
+    float* h;             // [P][I] SwiGLU activations, rounded to x's dtype
+    uint32_t* hmax;       // [P]   max |h| bits per pair
+    float* pair_out;      // [P][H] weighted fp32 partials (when the caller gives none)
+    float* up_part;       // [Wu][2][32][8]
+    int32_t* up_cnt;      // [P * I/16]
+    float* dn_part;       // [Wd][2][32][4]
+    int32_t* dn_cnt;      // [P * H/16]
+    int32_t* cmb_cnt;     // [H/16]
+};
+
+size_t decode_workspace_layout(int64_t tokens, int top_k, int hidden, int intermediate,
+                               int sm_count, char* base, DecodeWorkspace* ws);
+
+struct DecodeArgs {
+    int format;  // 0 = FP8 block-scaled, 1 = INT4 group-128
+    DramaB200Fp8Bank fp8;
+    DramaB200Int4Bank int4;
+    const void* x;
+    int x_dtype;
+    int64_t tokens;
+    int top_k;
+    const void* ids;
+    int ids_dtype;
+    const void* weights;
+    int weights_dtype;
+    void* out;
+    float* pair_out;
+    const void* residual;  // optional [T][H] added before the final rounding
+    DecodeWorkspace ws;
+    int hidden, intermediate, slots;
+    int workers_up, workers_dn, ctas;
+};
+
+cudaError_t decode_launch(const DecodeArgs& a, cudaStream_t s);
+
+}  // namespace drama

@@ -1,0 +1,232 @@
+// K3: router softmax/top-k/renormalise and the stable route permutation.
+//
+// route_topk restates BackboneDecodeGraph._route_impl's routing lines
+// (src/drama_low_vram/backbone_graph.py:319-323) with torch's CUDA arithmetic
+// order, so indices (and their order, ties included) equal what the reference
+// computes on the GPU:
+//   * softmax: one warp per row, lane l holds elements l + 32*i; exp(x - max)
+//     summed per lane in i order, then a xor butterfly; p = e / sum;
+//   * topk selection: all values above the k-th largest in index order, then
+//     values equal to it in index order;
+//   * topk ordering: the 32-slot key/value bitonic network torch uses to sort
+//     k <= 32 results (descending; ties resolved by the network);
+//   * renormalisation: pairwise tree sum of the k weights (shfl_down 1,2,4..).
+// permute_routes restates the host routing of
+// ExpertOffloadManager._forward_partitioned (src/drama_low_vram/offload.py:
+// 1206-1211): stable argsort by expert plus bincount.
+#include <cstdio>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "bucket.cuh"
+
+namespace drama {
+
+namespace {
+
+constexpr unsigned kFull = 0xffffffffu;
+
+// One warp per token row; LANES lanes x ITERS values cover next_pow2(E).
+template <int LANES, int ITERS>
+__global__ void __launch_bounds__(256) route_topk_kernel(RouteArgs a) {
+    __shared__ float s_key[8][32];
+    __shared__ int s_idx[8][32];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + warp;
+    grid_dependency_wait();
+    grid_launch_dependents();
+    if (row >= a.tokens) return;
+    const int E = a.experts;
+
+    float v[ITERS];
+#pragma unroll
+    for (int i = 0; i < ITERS; ++i) {
+        const int idx = lane + i * LANES;
+        v[i] = (lane < LANES && idx < E)
+                   ? load_any(a.logits, a.logits_dtype, row * static_cast<int64_t>(E) + idx)
+                   : -INFINITY;
+    }
+    // max: exact in any order.
+    float m = v[0];
+#pragma unroll
+    for (int i = 1; i < ITERS; ++i) m = fmaxf(m, v[i]);
+#pragma unroll
+    for (int off = LANES / 2; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(kFull, m, off));
+    float sum = 0.0f;
+#pragma unroll
+    for (int i = 0; i < ITERS; ++i) {
+        v[i] = expf(v[i] - m);
+        sum += v[i];
+    }
+#pragma unroll
+    for (int off = LANES / 2; off > 0; off >>= 1) sum = sum + __shfl_xor_sync(kFull, sum, off);
+    bool live[ITERS];
+#pragma unroll
+    for (int i = 0; i < ITERS; ++i) {
+        const int idx = lane + i * LANES;
+        live[i] = lane < LANES && idx < E;
+        v[i] = live[i] ? v[i] / sum : 0.0f;
+    }
+
+    // k-th largest probability (with multiplicity).
+    const int k = a.top_k;
+    bool avail[ITERS];
+#pragma unroll
+    for (int i = 0; i < ITERS; ++i) avail[i] = live[i];
+    int need = k;
+    float kth = 0.0f;
+    for (int round = 0; round < k; ++round) {
+        float mx = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < ITERS; ++i)
+            if (avail[i]) mx = fmaxf(mx, v[i]);
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, off));
+        int cnt = 0;
+#pragma unroll
+        for (int i = 0; i < ITERS; ++i) {
+            const bool eq = avail[i] && v[i] == mx;
+            cnt += __popc(__ballot_sync(kFull, eq));
+            if (eq) avail[i] = false;
+        }
+        kth = mx;
+        if (cnt >= need) break;
+        need -= cnt;
+    }
+
+    // gatherTopK order: strictly greater in index order, then equal ones.
+    const unsigned lt = (1u << lane) - 1u;
+    int base = 0;
+#pragma unroll
+    for (int i = 0; i < ITERS; ++i) {
+        const bool pick = live[i] && v[i] > kth;
+        const unsigned b = __ballot_sync(kFull, pick);
+        if (pick) {
+            const int pos = base + __popc(b & lt);
+            s_key[warp][pos] = v[i];
+            s_idx[warp][pos] = lane + i * LANES;
+        }
+        base += __popc(b);
+    }
+#pragma unroll
+    for (int i = 0; i < ITERS; ++i) {
+        const bool eq = live[i] && v[i] == kth;
+        const unsigned b = __ballot_sync(kFull, eq);
+        const int pos = base + __popc(b & lt);
+        if (eq && pos < k) {
+            s_key[warp][pos] = v[i];
+            s_idx[warp][pos] = lane + i * LANES;
+        }
+        base += __popc(b);
+    }
+    __syncwarp();
+    float key = lane < k ? s_key[warp][lane] : 0.0f;
+    int idx = lane < k ? s_idx[warp][lane] : 0;
+    bool valid = lane < k;
+
+    // 32-slot bitonic network (lane = slot); pair (l, l ^ stride).
+    auto stage = [&](int stride, bool flag) {
+        const float pk = __shfl_xor_sync(kFull, key, stride);
+        const int pi = __shfl_xor_sync(kFull, idx, stride);
+        const bool pv = __shfl_xor_sync(kFull, valid, stride);
+        const bool is_a = (lane & stride) == 0;
+        const float ka = is_a ? key : pk, kb = is_a ? pk : key;
+        const bool va = is_a ? valid : pv, vb = is_a ? pv : valid;
+        const bool swap = ((ka > kb) && va) || !vb;
+        if (swap == flag) {
+            key = pk;
+            idx = pi;
+            valid = pv;
+        }
+    };
+    for (int size = 2; size < 32; size <<= 1) {
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            const int t = (lane / (2 * stride)) * stride + (lane % stride);
+            stage(stride, (t & (size >> 1)) != 0);
+        }
+    }
+    for (int stride = 16; stride > 0; stride >>= 1) stage(stride, false);
+
+    float w = valid ? key : 0.0f;
+    if (a.renormalize) {
+        int p2 = 1;
+        while (p2 < k) p2 <<= 1;
+        float t = (lane < k) ? key : 0.0f;
+        for (int off = 1; off < p2; off <<= 1) {
+            const float o = __shfl_down_sync(kFull, t, off);
+            t = t + o;
+        }
+        const float total = __shfl_sync(kFull, t, 0);
+        w = w / total;
+    }
+    if (lane < k) {
+        const int64_t o = row * k + lane;
+        store_index(a.ids, a.ids_dtype, o, idx);
+        store_any(a.weights, a.weights_dtype, o, w);
+    }
+}
+
+template <int LANES, int ITERS>
+cudaError_t launch_route(const RouteArgs& a, cudaStream_t s) {
+    const unsigned blocks = static_cast<unsigned>((a.tokens + 7) / 8);
+    return launch_pdl(route_topk_kernel<LANES, ITERS>, dim3(blocks), dim3(256), 0, s, a);
+}
+
+}  // namespace
+
+cudaError_t route_topk(const RouteArgs& a, cudaStream_t s) {
+    int p2 = 1;
+    while (p2 < a.experts) p2 <<= 1;
+    switch (p2) {
+        case 1: return launch_route<1, 1>(a, s);
+        case 2: return launch_route<2, 1>(a, s);
+        case 4: return launch_route<4, 1>(a, s);
+        case 8: return launch_route<8, 1>(a, s);
+        case 16: return launch_route<16, 1>(a, s);
+        case 32: return launch_route<32, 1>(a, s);
+        case 64: return launch_route<32, 2>(a, s);
+        case 128: return launch_route<32, 4>(a, s);
+        case 256: return launch_route<32, 8>(a, s);
+        case 512: return launch_route<32, 16>(a, s);
+        default: return launch_route<32, 32>(a, s);
+    }
+}
+
+namespace {
+
+__global__ void __launch_bounds__(1024) permute_kernel(PermuteArgs a) {
+    extern __shared__ int smem[];
+    __shared__ int dropped;
+    grid_dependency_wait();
+    grid_launch_dependents();
+    if (threadIdx.x == 0) dropped = 0;
+    __syncthreads();
+    stable_bucket(a.ids, a.ids_dtype, a.pairs, a.experts, smem, a.order, nullptr, &dropped);
+    // counts survive in smem[0..E); base now holds the exclusive end offsets.
+    for (int e = threadIdx.x; e < a.experts; e += blockDim.x) {
+        const int c = smem[e];
+        const int end = smem[a.experts + e];
+        a.counts[e] = c;
+        a.offsets[e] = end - c;
+        if (e == a.experts - 1) a.offsets[a.experts] = end;
+    }
+    if (threadIdx.x == 0 && a.status) a.status[0] = dropped;
+}
+
+}  // namespace
+
+size_t bucket_smem_bytes(int experts) { return static_cast<size_t>(34) * experts * sizeof(int); }
+
+cudaError_t permute_routes(const PermuteArgs& a, cudaStream_t s) {
+    const size_t smem = bucket_smem_bytes(a.experts);
+    static bool configured = false;  // benign race: same value from any thread
+    if (!configured) {
+        const cudaError_t err = cudaFuncSetAttribute(permute_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                     static_cast<int>(bucket_smem_bytes(1024)));
+        if (err != cudaSuccess) return err;
+        configured = true;
+    }
+    return launch_pdl(permute_kernel, dim3(1), dim3(1024), smem, s, a);
+}
+
+}  // namespace drama

@@ -1,0 +1,133 @@
+"""ctypes binding of ``libdrama_b200.so`` (the C ABI in ``include/drama_b200.h``).
+
+Mirrors the reference's binding style (``src/drama_low_vram/native_backend.py:
+56-173``): argtypes declared once, every call's status checked, the thread-local
+error text raised as ``RuntimeError``. There is no fallback: if the library is
+missing the import of any compute entry point fails loudly.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+import torch
+
+from .build import LIB_PATH
+
+F32, F16, BF16, I32, I64 = 0, 1, 2, 3, 4
+ABI_VERSION = 1
+
+DTYPE_CODES = {
+    torch.float32: F32,
+    torch.float16: F16,
+    torch.bfloat16: BF16,
+    torch.int32: I32,
+    torch.int64: I64,
+}
+
+EXPORTS = (
+    "drama_b200_abi",
+    "drama_b200_error",
+    "drama_b200_device_check",
+    "drama_b200_route_topk",
+    "drama_b200_permute_routes",
+    "drama_b200_decode_workspace_bytes",
+    "drama_b200_decode_status_offset",
+    "drama_b200_fp8_decode",
+    "drama_b200_int4_decode",
+)
+
+c_void_p, c_int, c_int64, c_size_t = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_size_t
+
+
+class Fp8Bank(ctypes.Structure):
+    _fields_ = [
+        ("w13", c_void_p), ("w13_scale", c_void_p), ("w2", c_void_p), ("w2_scale", c_void_p),
+        ("w13_slot_stride", c_int64), ("w13_row_stride", c_int64),
+        ("w13_scale_slot_stride", c_int64), ("w13_scale_row_stride", c_int64),
+        ("w2_slot_stride", c_int64), ("w2_row_stride", c_int64),
+        ("w2_scale_slot_stride", c_int64), ("w2_scale_row_stride", c_int64),
+        ("slots", ctypes.c_int32), ("hidden", ctypes.c_int32),
+        ("intermediate", ctypes.c_int32), ("reserved", ctypes.c_int32),
+    ]
+
+
+class Int4Bank(ctypes.Structure):
+    _fields_ = [
+        ("w13", c_void_p), ("w13_scale", c_void_p), ("w13_zeros", c_void_p),
+        ("w2", c_void_p), ("w2_scale", c_void_p), ("w2_zeros", c_void_p),
+        ("w13_slot_stride", c_int64), ("w13_row_stride", c_int64),
+        ("w13_scale_slot_stride", c_int64), ("w13_scale_row_stride", c_int64),
+        ("w13_zeros_slot_stride", c_int64), ("w13_zeros_row_stride", c_int64),
+        ("w2_slot_stride", c_int64), ("w2_row_stride", c_int64),
+        ("w2_scale_slot_stride", c_int64), ("w2_scale_row_stride", c_int64),
+        ("w2_zeros_slot_stride", c_int64), ("w2_zeros_row_stride", c_int64),
+        ("scale_dtype", ctypes.c_int32), ("slots", ctypes.c_int32),
+        ("hidden", ctypes.c_int32), ("intermediate", ctypes.c_int32),
+    ]
+
+
+class Library:
+    """Loaded ``libdrama_b200.so`` with typed entry points."""
+
+    def __init__(self, path: Path | str = LIB_PATH):
+        self.path = Path(path).resolve()
+        if not self.path.is_file():
+            raise RuntimeError(
+                f"drama_b200 CUDA library missing: {self.path}. Build it with "
+                "drama_b200.build.build() (nvcc, sm_100a); there is no CPU fallback.")
+        dll = ctypes.CDLL(str(self.path))
+        self.dll = dll
+        dll.drama_b200_abi.restype = c_int
+        dll.drama_b200_error.restype = ctypes.c_char_p
+        dll.drama_b200_device_check.argtypes = [c_int, ctypes.POINTER(c_int)]
+        dll.drama_b200_route_topk.argtypes = [c_void_p, c_int, c_int64, c_int, c_int, c_int,
+                                             c_void_p, c_int, c_void_p, c_int, c_void_p]
+        dll.drama_b200_permute_routes.argtypes = [c_void_p, c_int, c_int64, c_int, c_void_p,
+                                                 c_void_p, c_void_p, c_void_p, c_void_p]
+        dll.drama_b200_decode_workspace_bytes.argtypes = [c_int64, c_int, c_int, c_int]
+        dll.drama_b200_decode_workspace_bytes.restype = c_size_t
+        dll.drama_b200_decode_status_offset.restype = c_size_t
+        decode_args = [c_void_p, c_int, c_int64, c_int, c_void_p, c_int, c_void_p, c_int,
+                       c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]
+        dll.drama_b200_fp8_decode.argtypes = [ctypes.POINTER(Fp8Bank)] + decode_args
+        dll.drama_b200_int4_decode.argtypes = [ctypes.POINTER(Int4Bank)] + decode_args
+        for name in EXPORTS:
+            if name not in ("drama_b200_error", "drama_b200_decode_workspace_bytes",
+                            "drama_b200_decode_status_offset"):
+                getattr(dll, name).restype = c_int
+        if dll.drama_b200_abi() != ABI_VERSION:
+            raise RuntimeError("Unsupported drama_b200 ABI version")
+
+    def check(self, status: int) -> None:
+        if status:
+            message = self.dll.drama_b200_error()
+            raise RuntimeError(message.decode("utf-8", errors="replace") if message else "drama_b200 error")
+
+    def device_check(self, device: int) -> int:
+        count = c_int(0)
+        self.check(self.dll.drama_b200_device_check(device, ctypes.byref(count)))
+        return count.value
+
+
+_LIB: Library | None = None
+_LOCK = threading.Lock()
+
+
+def library() -> Library:
+    global _LIB
+    if _LIB is None:
+        with _LOCK:
+            if _LIB is None:
+                _LIB = Library()
+    return _LIB
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def stream_handle(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream

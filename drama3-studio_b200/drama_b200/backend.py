@@ -1,0 +1,263 @@
+"""Expert backends for ``ExpertOffloadManager`` running the sm_100a kernels.
+
+``B200ExpertBackend`` implements the reference's ``ExpertBackend`` protocol
+(``src/drama_low_vram/offload.py:187-196``) for FP8 128x128 block-scaled banks
+with the arithmetic of ``TorchExpertBackend`` (``offload.py:199-244``, the
+PyTorch W16A16 dequant path), plus ``forward_decode_pairs``
+(``offload.py:346-356``) which the manager calls for batch-1 partitions.
+``QuantizedB200Backend(0)`` replaces ``QuantizedExpertBackend(0)``
+(``src/drama_low_vram/quantized_kernels.py:217-248``) for GPTQ W4A16 banks and
+additionally accepts asymmetric uint4 zero-points.
+
+Both are drop-ins: ``install_expert_offload(backbone, backend=B200ExpertBackend())``
+(``offload.py:1534-1569``) needs no other change. Every call enqueues work on
+``torch.cuda.current_stream`` and, apart from the optional slot-range check,
+never synchronises, so the calls can sit inside a CUDA graph.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from dataclasses import dataclass
+
+import torch
+from torch import Tensor
+
+from . import _lib
+
+FP8_DTYPE = torch.float8_e4m3fn
+FLOAT_DTYPES = (torch.float16, torch.bfloat16, torch.float32)
+MAX_DECODE_PAIRS = 4096
+
+
+@dataclass(frozen=True)
+class QuantizedBank:
+    """INT4 bank in the reference's GPTQ layout with optional zero-points.
+
+    ``w13_weight [S, 2I, H/8] int32``, ``w13_scale_inv [S, 2I, H/128]`` bf16 or
+    fp16, ``w2_weight [S, H, I/8]``, ``w2_scale_inv [S, H, I/128]``; the
+    ``*_qzeros`` tensors are ``[S, N/8, K/128] int32`` (nibble n%8 of word n/8)
+    or None for the reference's implicit zero-point 8.
+    """
+
+    w13_weight: Tensor
+    w13_scale_inv: Tensor
+    w2_weight: Tensor
+    w2_scale_inv: Tensor
+    w13_qzeros: Tensor | None = None
+    w2_qzeros: Tensor | None = None
+
+    @property
+    def count(self) -> int:
+        return self.w13_weight.shape[0]
+
+
+class _Workspace:
+    """Zero-initialised device scratch, one per (device, stream), grown on demand."""
+
+    def __init__(self) -> None:
+        self._buffers: dict[tuple[int, int], Tensor] = {}
+        self._lock = threading.Lock()
+
+    def get(self, device: torch.device, nbytes: int) -> Tensor:
+        stream = torch.cuda.current_stream(device).cuda_stream
+        key = (device.index if device.index is not None else torch.cuda.current_device(), stream)
+        with self._lock:
+            buf = self._buffers.get(key)
+            if buf is None or buf.numel() < nbytes:
+                if torch.cuda.is_current_stream_capturing():
+                    raise RuntimeError(
+                        "drama_b200 workspace must be allocated before CUDA graph capture; "
+                        "run one eager call of the same size first")
+                buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+                self._buffers[key] = buf
+            return buf
+
+
+_WORKSPACES = _Workspace()
+
+
+def _rows(t: Tensor) -> Tensor:
+    """Innermost dimension contiguous (the kernels' only layout requirement)."""
+    return t if t.stride(-1) == 1 else t.contiguous()
+
+
+def _check_common(x: Tensor, ids: Tensor, weights: Tensor, count: int, hidden: int,
+                  validate_ids: bool) -> None:
+    if x.ndim != 2 or x.shape[-1] != hidden:
+        raise ValueError(f"Expected hidden rows [N, {hidden}], got {tuple(x.shape)}")
+    if not x.is_cuda:
+        raise RuntimeError("drama_b200 backends need CUDA tensors on an sm_100 GPU")
+    if x.dtype not in FLOAT_DTYPES:
+        raise ValueError("Expert compute dtype must be float16, bfloat16 or float32")
+    if ids.dtype not in (torch.int32, torch.int64):
+        raise ValueError("Expert IDs must have an integer dtype")
+    if not weights.is_floating_point():
+        raise ValueError("Routing weights must be floating point")
+    if ids.device != x.device or weights.device != x.device:
+        raise ValueError("Hidden states, expert IDs and routing weights must share a device")
+    if validate_ids and ids.numel() and not torch.cuda.is_current_stream_capturing():
+        bad = ((ids < 0) | (ids >= count)).any()
+        if bool(bad):
+            first = int(ids[(ids < 0) | (ids >= count)].reshape(-1)[0])
+            raise ValueError(f"Local expert slot {first} is outside the staging pool")
+
+
+def _fp8_bank(staged, hidden: int) -> tuple[_lib.Fp8Bank, tuple]:
+    w13 = _rows(staged.w13_weight)
+    w2 = _rows(staged.w2_weight)
+    s13 = _rows(staged.w13_scale_inv)
+    s2 = _rows(staged.w2_scale_inv)
+    for name, t, dt in (("w13_weight", w13, FP8_DTYPE), ("w2_weight", w2, FP8_DTYPE),
+                        ("w13_scale_inv", s13, torch.float32), ("w2_scale_inv", s2, torch.float32)):
+        if t.dtype != dt:
+            raise ValueError(f"{name} must be {dt}; got {t.dtype}")
+        if t.ndim != 3:
+            raise ValueError(f"{name} must be a stacked three-dimensional tensor")
+    slots, gate_up, h = w13.shape
+    inter = gate_up // 2
+    if h != hidden or tuple(w2.shape) != (slots, hidden, inter):
+        raise ValueError("FP8 bank geometry does not match the hidden size")
+    if tuple(s13.shape) != (slots, gate_up // 128, hidden // 128) or \
+            tuple(s2.shape) != (slots, hidden // 128, inter // 128):
+        raise ValueError("FP8 weight shape does not match its 128x128 block scales")
+    if w13.stride(1) % 16 or w13.stride(0) % 16 or w13.data_ptr() % 16:
+        w13 = w13.contiguous()
+    if w2.stride(1) % 16 or w2.stride(0) % 16 or w2.data_ptr() % 16:
+        w2 = w2.contiguous()
+    bank = _lib.Fp8Bank(
+        w13.data_ptr(), s13.data_ptr(), w2.data_ptr(), s2.data_ptr(),
+        w13.stride(0), w13.stride(1), s13.stride(0), s13.stride(1),
+        w2.stride(0), w2.stride(1), s2.stride(0), s2.stride(1),
+        slots, hidden, inter, 0)
+    return bank, (w13, w2, s13, s2)
+
+
+def _int4_bank(staged, hidden: int) -> tuple[_lib.Int4Bank, tuple]:
+    w13 = _rows(staged.w13_weight)
+    w2 = _rows(staged.w2_weight)
+    s13 = _rows(staged.w13_scale_inv)
+    s2 = _rows(staged.w2_scale_inv)
+    z13 = getattr(staged, "w13_qzeros", None)
+    z2 = getattr(staged, "w2_qzeros", None)
+    z13 = None if z13 is None else _rows(z13)
+    z2 = None if z2 is None else _rows(z2)
+    if w13.dtype != torch.int32 or w2.dtype != torch.int32:
+        raise ValueError("Quantized weight dtype mismatch")
+    if s13.dtype not in (torch.bfloat16, torch.float16) or s2.dtype != s13.dtype:
+        raise ValueError("Quantized scale dtype mismatch")
+    slots, gate_up, h8 = w13.shape
+    inter = gate_up // 2
+    if h8 * 8 != hidden or tuple(w2.shape) != (slots, hidden, inter // 8):
+        raise ValueError("Quantized weight/scale geometry mismatch")
+    if tuple(s13.shape) != (slots, gate_up, hidden // 128) or tuple(s2.shape) != (slots, hidden, inter // 128):
+        raise ValueError("Quantized weight/scale geometry mismatch")
+    for z, n, k in ((z13, gate_up, hidden), (z2, hidden, inter)):
+        if z is not None and (z.dtype != torch.int32 or tuple(z.shape) != (slots, n // 8, k // 128)):
+            raise ValueError("Quantized zero-point geometry mismatch")
+    if w13.stride(1) % 4 or w13.stride(0) % 4 or w13.data_ptr() % 16:
+        w13 = w13.contiguous()
+    if w2.stride(1) % 4 or w2.stride(0) % 4 or w2.data_ptr() % 16:
+        w2 = w2.contiguous()
+    bank = _lib.Int4Bank(
+        w13.data_ptr(), s13.data_ptr(), _lib.ptr(z13), w2.data_ptr(), s2.data_ptr(), _lib.ptr(z2),
+        w13.stride(0), w13.stride(1), s13.stride(0), s13.stride(1),
+        0 if z13 is None else z13.stride(0), 0 if z13 is None else z13.stride(1),
+        w2.stride(0), w2.stride(1), s2.stride(0), s2.stride(1),
+        0 if z2 is None else z2.stride(0), 0 if z2 is None else z2.stride(1),
+        _lib.DTYPE_CODES[s13.dtype], slots, hidden, inter)
+    return bank, (w13, w2, s13, s2, z13, z2)
+
+
+class _DecodeBackend:
+    """Shared forward / forward_pairs plumbing around one C entry point."""
+
+    entry = ""
+
+    def __init__(self, *, validate_ids: bool = True) -> None:
+        self.validate_ids = validate_ids
+
+    def _bank(self, staged, hidden):  # pragma: no cover - overridden
+        raise NotImplementedError
+
+    def _run(self, x: Tensor, ids: Tensor, weights: Tensor, staged, *, combine: bool) -> Tensor:
+        hidden = x.shape[-1]
+        bank, keep = self._bank(staged, hidden)
+        _check_common(x, ids, weights, bank.slots, hidden, self.validate_ids)
+        tokens, top_k = ids.shape
+        x = x.contiguous()
+        ids = ids.contiguous()
+        weights = weights.contiguous()
+        if weights.dtype not in FLOAT_DTYPES:
+            weights = weights.float()
+        if tokens * top_k > MAX_DECODE_PAIRS:
+            return self._chunked(x, ids, weights, staged, combine=combine)
+        lib = _lib.library()
+        if combine:
+            out, pair_out = torch.empty_like(x), None
+        else:
+            out, pair_out = None, torch.empty((tokens * top_k, hidden), device=x.device, dtype=torch.float32)
+        nbytes = lib.dll.drama_b200_decode_workspace_bytes(tokens, top_k, hidden, bank.intermediate)
+        ws = _WORKSPACES.get(x.device, nbytes)
+        fn = getattr(lib.dll, self.entry)
+        lib.check(fn(ctypes.byref(bank), x.data_ptr(), _lib.DTYPE_CODES[x.dtype], tokens, top_k,
+                     ids.data_ptr(), _lib.DTYPE_CODES[ids.dtype], weights.data_ptr(),
+                     _lib.DTYPE_CODES[weights.dtype], _lib.ptr(out), _lib.ptr(pair_out),
+                     ws.data_ptr(), ws.numel(), _lib.stream_handle(x.device)))
+        del keep
+        return out if combine else pair_out
+
+    def _chunked(self, x, ids, weights, staged, *, combine: bool) -> Tensor:
+        tokens, top_k = ids.shape
+        rows = max(1, MAX_DECODE_PAIRS // top_k)
+        parts = [self._run(x[s:s + rows], ids[s:s + rows], weights[s:s + rows], staged, combine=combine)
+                 for s in range(0, tokens, rows)]
+        return torch.cat(parts)
+
+    def forward(self, x: Tensor, ids: Tensor, weights: Tensor, staged) -> Tensor:
+        """[T,H] expert output in x's dtype (route slots summed in slot order)."""
+        if ids.ndim != 2 or ids.shape[0] != x.shape[0]:
+            raise ValueError("Expert IDs must have shape [tokens, top_k]")
+        if weights.shape != ids.shape:
+            raise ValueError("Routing weights must match IDs and top_k must be positive")
+        if x.shape[0] == 0:
+            return torch.zeros_like(x)
+        return self._run(x, ids, weights, staged, combine=True)
+
+    def forward_pairs(self, x: Tensor, ids: Tensor, weights: Tensor, staged) -> Tensor:
+        """Weighted [pairs, hidden] contributions in float32, before summing."""
+        if ids.shape != (x.shape[0], 1) or weights.shape != ids.shape:
+            raise ValueError("Pair backend expects one expert and weight per input row")
+        if x.shape[0] == 0:
+            return torch.empty_like(x, dtype=torch.float32)
+        return self._run(x, ids, weights, staged, combine=False)
+
+    def forward_decode_pairs(self, x: Tensor, ids: Tensor, weights: Tensor, staged) -> Tensor:
+        """Small partition of one decode row (offload.py:346-356); fp32 partials."""
+        return self.forward_pairs(x, ids, weights, staged)
+
+
+class B200ExpertBackend(_DecodeBackend):
+    """FP8 (E4M3, 128x128 block scales) experts; TorchExpertBackend arithmetic."""
+
+    entry = "drama_b200_fp8_decode"
+
+    def _bank(self, staged, hidden):
+        return _fp8_bank(staged, hidden)
+
+
+class QuantizedB200Backend(_DecodeBackend):
+    """GPTQ W4A16 (mode 0) experts, symmetric or with uint4 zero-points."""
+
+    entry = "drama_b200_int4_decode"
+
+    def __init__(self, mode: int = 0, *, validate_ids: bool = True) -> None:
+        if mode != 0:
+            raise ValueError("QuantizedB200Backend implements GPTQ W4A16 (mode 0)")
+        super().__init__(validate_ids=validate_ids)
+        self.mode = mode
+        self.quantized_mode = "W4A16-GPTQ"
+
+    def _bank(self, staged, hidden):
+        return _int4_bank(staged, hidden)

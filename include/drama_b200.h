@@ -1,0 +1,163 @@
+/* drama_b200 — B200 (sm_100a) routed-expert hot path behind a plain C ABI.
+ *
+ * Conventions (mirroring the reference's native ABI v1,
+ * native/include/drama_native.h:1-90 and native/src/runtime.cpp:278-290):
+ *   - every entry point returns 0 on success, -1 on failure; the failure text
+ *     is available from drama_b200_error() on the same host thread;
+ *   - all validation happens before any launch or write;
+ *   - buffers are borrowed device pointers (plain pointers, sizes, strides in
+ *     elements); nothing is retained after return;
+ *   - work is enqueued on the caller's CUDA stream (a cudaStream_t passed as
+ *     void*); no entry point allocates, synchronises or blocks, so every call
+ *     can be captured in a CUDA graph;
+ *   - kernels that need scratch take a caller-owned device workspace sized by
+ *     the matching *_workspace_bytes() query. The workspace must be zero-filled
+ *     once before its first use; every call leaves it reusable. Calls that
+ *     share one workspace must be ordered on the GPU (same stream or events).
+ */
+#ifndef DRAMA_B200_H
+#define DRAMA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define DRAMA_B200_API __attribute__((visibility("default")))
+#else
+#define DRAMA_B200_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DRAMA_B200_ABI_VERSION 1
+
+/* Element type codes used by every dtype argument. */
+enum {
+    DRAMA_B200_F32 = 0,
+    DRAMA_B200_F16 = 1,
+    DRAMA_B200_BF16 = 2,
+    DRAMA_B200_I32 = 3,
+    DRAMA_B200_I64 = 4
+};
+
+/* ABI version (DRAMA_B200_ABI_VERSION). Replaces drama_native_abi
+ * (native/include/drama_native.h:15). */
+DRAMA_B200_API int drama_b200_abi(void);
+
+/* Thread-local text of the last failure. Replaces drama_native_error
+ * (native/include/drama_native.h:18). */
+DRAMA_B200_API const char* drama_b200_error(void);
+
+/* 0 when `device` is an sm_100 GPU this library was built for; -1 otherwise.
+ * Replaces the capability gate of nvidia_policy.policy_for
+ * (src/drama_low_vram/nvidia_policy.py:21-33). */
+DRAMA_B200_API int drama_b200_device_check(int device, int* sm_count);
+
+/* ---------------------------------------------------------------------------
+ * K3 router: softmax -> top-k -> optional renormalisation -> cast.
+ * Replaces BackboneDecodeGraph._route_impl's routing lines
+ * (src/drama_low_vram/backbone_graph.py:319-323):
+ *   probs = softmax(logits.float()); w, ids = probs.topk(k);
+ *   if renormalize: w /= w.sum(-1); w = w.to(weights_dtype)
+ * logits: [tokens, experts] (F32/F16/BF16), experts <= 1024, 1 <= top_k <= 32.
+ * ids: [tokens, top_k] (I32/I64); weights: [tokens, top_k] (F32/F16/BF16).
+ * Indices and their order reproduce torch's CUDA topk, ties included.
+ * ------------------------------------------------------------------------- */
+DRAMA_B200_API int drama_b200_route_topk(const void* logits, int logits_dtype, int64_t tokens,
+                                         int experts, int top_k, int renormalize, void* ids,
+                                         int ids_dtype, void* weights, int weights_dtype,
+                                         void* stream);
+
+/* K3 gather/permute: stable argsort of flat route IDs, per-expert counts and
+ * start offsets. Replaces ExpertOffloadManager._forward_partitioned's host
+ * routing (src/drama_low_vram/offload.py:1206-1211):
+ *   order = argsort(flat_ids, stable=True); counts = bincount(flat_ids, E)
+ * ids: [pairs] (I32/I64) in [0, experts); experts <= 1024; pairs <= 2^24.
+ * order: [pairs] int64; counts: [experts] int64; offsets: [experts+1] int64.
+ * An ID outside [0, experts) makes the call fail before any launch only when
+ * it is detectable on the host; on the device such pairs are dropped from the
+ * order and counted in status[0] (int32, may be NULL). */
+DRAMA_B200_API int drama_b200_permute_routes(const void* ids, int ids_dtype, int64_t pairs,
+                                             int experts, int64_t* order, int64_t* counts,
+                                             int64_t* offsets, int32_t* status, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Expert banks. Layouts are the reference's staged views: ExpertStore /
+ * StagedExperts (src/drama_low_vram/offload.py:101-184) for FP8 and
+ * QuantizedStore mode 0 (src/drama_low_vram/quantized_model.py:26-68) for
+ * INT4. Strides are in elements; the innermost dimension is contiguous; every
+ * weight row starts on a 16-byte boundary.
+ * ------------------------------------------------------------------------- */
+typedef struct DramaB200Fp8Bank {
+    const void* w13;          /* E4M3 [slots, 2I, H]: gate rows then up rows */
+    const float* w13_scale;   /* fp32 [slots, 2I/128, H/128] */
+    const void* w2;           /* E4M3 [slots, H, I] */
+    const float* w2_scale;    /* fp32 [slots, H/128, I/128] */
+    int64_t w13_slot_stride, w13_row_stride;
+    int64_t w13_scale_slot_stride, w13_scale_row_stride;
+    int64_t w2_slot_stride, w2_row_stride;
+    int64_t w2_scale_slot_stride, w2_scale_row_stride;
+    int32_t slots, hidden, intermediate, reserved;
+} DramaB200Fp8Bank;
+
+typedef struct DramaB200Int4Bank {
+    const int32_t* w13;        /* [slots, 2I, H/8]; nibble k%8 at bit 4*(k%8) */
+    const void* w13_scale;     /* BF16 or F16 [slots, 2I, H/128] */
+    const int32_t* w13_zeros;  /* [slots, 2I/8, H/128], nibble n%8 at bit 4*(n%8); NULL = 8 */
+    const int32_t* w2;         /* [slots, H, I/8] */
+    const void* w2_scale;      /* BF16 or F16 [slots, H, I/128] */
+    const int32_t* w2_zeros;   /* [slots, H/8, I/128]; NULL = 8 */
+    int64_t w13_slot_stride, w13_row_stride;
+    int64_t w13_scale_slot_stride, w13_scale_row_stride;
+    int64_t w13_zeros_slot_stride, w13_zeros_row_stride;
+    int64_t w2_slot_stride, w2_row_stride;
+    int64_t w2_scale_slot_stride, w2_scale_row_stride;
+    int64_t w2_zeros_slot_stride, w2_zeros_row_stride;
+    int32_t scale_dtype;       /* DRAMA_B200_BF16 or DRAMA_B200_F16 */
+    int32_t slots, hidden, intermediate;
+} DramaB200Int4Bank;
+
+/* ---------------------------------------------------------------------------
+ * K1 decode: dequantising SwiGLU expert FFN with the weighted combine fused.
+ * Replaces ExpertBackend.forward / forward_pairs
+ * (src/drama_low_vram/offload.py:187-196) as TorchExpertBackend computes them
+ * (offload.py:199-244; the FP8 W16A16 dequant path) and
+ * QuantizedExpertBackend(0) (src/drama_low_vram/quantized_kernels.py:217-248):
+ *   gate, up = x @ W13^T (rounded to x's dtype); h = silu(gate) * up;
+ *   partial[p] = (h @ W2^T rounded to x's dtype) * weight[p]   (fp32)
+ *   out[t] = sum over route slots, in slot order, of partial[t*top_k + s]
+ * x: [tokens, H] (F32/F16/BF16); ids/weights: [tokens, top_k] local slots and
+ * route weights. When top_k == 1 and out == NULL the call is forward_pairs:
+ * pair_out [tokens, H] fp32 receives the weighted partials. Either output may
+ * be NULL but not both. Weight bytes are read once per (slot, <=8 tokens).
+ * pairs = tokens*top_k <= 4096, slots <= 1024.
+ * ------------------------------------------------------------------------- */
+DRAMA_B200_API size_t drama_b200_decode_workspace_bytes(int64_t tokens, int top_k, int hidden,
+                                                        int intermediate);
+
+DRAMA_B200_API int drama_b200_fp8_decode(const DramaB200Fp8Bank* bank, const void* x,
+                                         int x_dtype, int64_t tokens, int top_k,
+                                         const void* ids, int ids_dtype, const void* weights,
+                                         int weights_dtype, void* out, float* pair_out,
+                                         void* workspace, size_t workspace_bytes,
+                                         void* stream);
+
+DRAMA_B200_API int drama_b200_int4_decode(const DramaB200Int4Bank* bank, const void* x,
+                                          int x_dtype, int64_t tokens, int top_k,
+                                          const void* ids, int ids_dtype, const void* weights,
+                                          int weights_dtype, void* out, float* pair_out,
+                                          void* workspace, size_t workspace_bytes,
+                                          void* stream);
+
+/* Device status words of the last decode call on this workspace:
+ * [0] = pairs dropped for an out-of-range slot id. Copy them to the host
+ * with drama_b200_decode_status_offset() bytes into the workspace. */
+DRAMA_B200_API size_t drama_b200_decode_status_offset(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DRAMA_B200_H */
