@@ -1,0 +1,342 @@
+#!/usr/bin/env python
+"""Benchmark: MoE-layer decode tokens/s of the B200 routed-expert hot path.
+
+Workload: a stack of 48 FP8 MoE layers (hidden 2048, 128
+experts, top-8, intermediate 768, E4M3 with fp32 128x128 block scales, RMSNorm
+with gamma 1+N(0,0.01)), decode batch 1, 512 consecutive decode steps captured
+in one CUDA graph, all experts resident in HBM (29 GB). One bench step = one
+replay of that graph (512 tokens). Inputs are seeded synthetic bf16 N(0,1)
+rows; every token reads ~1.84 GB of expert weights, far more than L2.
+
+Arms:
+  python bench.py [--gpus N --steps K --warmup W]        this repository
+  python bench.py --impl reference [...]                  the reference's own
+        CPU expert core (native/src/*.cpp built under oracle/_ref) timed on
+        the host cores on a bounded sample of the same workload.
+Under torchrun each rank runs an independent replica (the decode path has no
+exchange step at batch 1); timing is the max over ranks.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "drama3-studio_b200"))
+sys.path.insert(0, str(REPO))
+
+METRIC = "MoE-layer decode tokens/s and expert-weight HBM GB/s vs ~8 TB/s at 1/2/4/8 B200"
+HIDDEN, EXPERTS, TOP_K, INTER = 2048, 128, 8, 768
+
+
+def parse_args():
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    p.add_argument("--layers", type=int, default=48)
+    p.add_argument("--decode-steps", type=int, default=512, help="decode tokens per CUDA graph")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
+    return p.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.gpu_id = gpu_id
+        self.lines: list[str] = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", self.gpu_id], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, ValueError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.thread.join(timeout=2)
+
+    def summary(self) -> dict:
+        mhz, max_mhz, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in self.lines:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                mhz.append(float(parts[1]))
+                max_mhz = float(parts[2])
+            except ValueError:
+                continue
+            for name, value in zip(names, parts[5:9]):
+                if value.lower() == "active":
+                    reasons.add(name)
+        mhz.sort()
+        return {"sm_mhz": mhz[len(mhz) // 2] if mhz else None, "sm_max_mhz": max_mhz,
+                "reasons": sorted(reasons), "samples": len(mhz)}
+
+
+def measured_peaks() -> dict:
+    path = REPO / "MEASURED_PEAKS.json"
+    if path.is_file():
+        data = json.loads(path.read_text())
+        return {"hbm_gbs": data["hbm_gbs"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def committed_traffic() -> float | None:
+    """DRAM bytes per expert-GEMV launch pair from the committed ncu summary."""
+    path = REPO / "profiles" / "decode_experts_traffic.json"
+    if path.is_file():
+        return json.loads(path.read_text()).get("dram_bytes_per_layer")
+    return None
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the reference's native expert core (W8A8 contract) plus the
+# oracle's RMSNorm/router restatement, timed on the host cores.
+# ---------------------------------------------------------------------------
+class CpuReference:
+    """One config-1 layer on the host: bank, router, and the native executor."""
+
+    def __init__(self, bank=None):
+        import torch
+
+        from drama_b200 import synthetic
+        from oracle.ref_native import ReferenceNative
+
+        self.threads = os.cpu_count() or 1
+        self.lib = ReferenceNative()
+        if bank is None:
+            bank = synthetic.fp8_bank(EXPERTS, HIDDEN, INTER, 0, chunk=EXPERTS)
+        bank = {k: v.detach().cpu() for k, v in bank.items()}
+        self.bank = {k: (v.view(torch.uint8).numpy() if v.dtype == torch.float8_e4m3fn else v.numpy())
+                     for k, v in bank.items()}
+        self.gate = synthetic.gate_weight(EXPERTS, HIDDEN, 500).float().numpy()
+        self.gamma = synthetic.norm_gamma(HIDDEN, 700).numpy()
+        self.x = synthetic.hidden_states(1, HIDDEN, 11).float().numpy()
+        self.executor = self.lib.executor(HIDDEN, INTER, capacity=TOP_K, threads=self.threads)
+
+    def layer(self) -> None:
+        from oracle import restate as R
+
+        normed = R.rms_norm(self.x, self.gamma)
+        logits = R.gate_logits(normed, self.gate)
+        ids, w, _ = R.route_topk(logits, TOP_K, True, "bfloat16")
+        partials = self.executor.forward(self.bank, R.bf16_bits(normed[0]), ids[0], w[0])
+        self.x = R.round_bf16(self.x + R.round_bf16(partials.sum(0))[None, :])
+
+    def sample(self, seconds: float, layers: int) -> dict:
+        done, start = 0, time.perf_counter()
+        while True:
+            self.layer()
+            done += 1
+            elapsed = time.perf_counter() - start
+            if elapsed >= seconds:
+                break
+        per_layer = elapsed / done
+        return {
+            "value": 1.0 / (per_layer * layers), "unit": "tokens/s", "cores": self.threads, "kind": "reference",
+            "sample": (f"{done} token-layers in {elapsed:.1f}s: the reference's native expert core "
+                       f"(native/src/*.cpp, W8A8 contract, {self.threads} threads) for the 8 routed experts "
+                       f"plus the oracle's RMSNorm/router; one config-1 layer bank stands in for every "
+                       f"layer position; value = 1 / ({layers} x mean token-layer time)"),
+        }
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    ref = CpuReference()
+    for _ in range(max(1, args.warmup)):
+        ref.layer()
+    # One bench step = one decode token through every layer position.
+    start = time.perf_counter()
+    for _ in range(args.steps):
+        for _ in range(args.layers):
+            ref.layer()
+    total = time.perf_counter() - start
+    value = args.steps / total
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * total / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp8-e4m3 weights and activations (W8A8), fp32 accumulate", "data": "synthetic",
+        "config": config_dict(args, world),
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": ref.threads, "kind": "reference",
+                         "sample": (f"{args.steps} decode tokens x {args.layers} layer positions through the "
+                                    f"reference's native expert core (native/src/*.cpp, {ref.threads} "
+                                    f"threads) with the oracle's RMSNorm/router; one layer bank reused")},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+
+
+def config_dict(args, world: int) -> dict:
+    return {
+        "workload": (f"config1: {args.layers} FP8 MoE layers (hidden {HIDDEN}, {EXPERTS} experts, top-{TOP_K}, "
+                     f"intermediate {INTER}, E4M3 128x128 block scales), decode batch 1, "
+                     f"{args.decode_steps} steps per CUDA graph, all experts resident"),
+        "layers": args.layers, "hidden": HIDDEN, "experts": EXPERTS, "top_k": TOP_K, "intermediate": INTER,
+        "batch": 1, "decode_steps_per_graph": args.decode_steps,
+        "parallelism": f"replicas{world}" if world > 1 else "single",
+        "l2": "inputs larger than L2: 29 GB of resident banks, ~1.84 GB of routed weights per token",
+    }
+
+
+# ---------------------------------------------------------------------------
+# this repository's arm
+# ---------------------------------------------------------------------------
+def run_ours(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=device, timeout=timedelta(seconds=300))
+
+    from drama_b200 import stack, synthetic
+
+    t0 = time.perf_counter()
+    layers = stack.synthetic_stack(args.layers, experts=EXPERTS, hidden=HIDDEN, intermediate=INTER,
+                                   seed=rank, device=device)
+    st = stack.DecodeStack(layers, tokens=1, top_k=TOP_K)
+    steps_per_graph = args.decode_steps
+    inputs = torch.stack([synthetic.hidden_states(1, HIDDEN, 10_000 + s, device=device)
+                          for s in range(steps_per_graph)])
+    outputs = torch.empty_like(inputs)
+    build_s = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    graph = st.capture(inputs, outputs, timed_steps=1)
+    capture_s = time.perf_counter() - t0
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+
+    for _ in range(max(3, args.warmup)):
+        graph.replay()
+    barrier()
+    props = torch.cuda.get_device_properties(device)
+    gpu_id = f"GPU-{props.uuid}" if getattr(props, "uuid", None) else str(local)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(gpu_id) as clocks:
+        e0.record()
+        for _ in range(args.steps):
+            graph.replay()
+        e1.record()
+        e1.synchronize()
+    barrier()
+    ms = e0.elapsed_time(e1)
+    expert_ms = st.expert_time_ms()
+    if world > 1:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+
+    # e2e: public API with host buffers (inputs H2D from pinned memory, outputs D2H).
+    host_in = inputs.cpu().pin_memory()
+    host_out = torch.empty_like(host_in).pin_memory()
+    barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for _ in range(args.steps):
+        inputs.copy_(host_in, non_blocking=True)
+        graph.replay()
+        host_out.copy_(outputs, non_blocking=True)
+    f1.record()
+    f1.synchronize()
+    barrier()
+    e2e_ms = f0.elapsed_time(f1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+
+    tokens = args.steps * steps_per_graph * world
+    value = tokens / (ms / 1000.0)
+    expert_bytes = synthetic.expert_nbytes_fp8(HIDDEN, INTER) * TOP_K
+    layer_bytes = expert_bytes + EXPERTS * HIDDEN * 2 + HIDDEN * 2 * 2
+    peaks = measured_peaks()
+    achieved = expert_bytes / (expert_ms / 1000.0) / 1e9
+    traffic = committed_traffic()
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": max(3, args.warmup), "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp8-e4m3 weights, bf16/f16 activations, fp32 accumulate",
+        "data": "synthetic (seeded random-init weights and hidden rows)", "config": config_dict(args, world),
+        "hbm_gbs_per_gpu": layer_bytes * args.layers * value / world / 1e9,
+        "roofline": {
+            "kernel": "expert GEMVs (decode_up_kernel + decode_down_kernel) of one layer",
+            "bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+            "frac": achieved / peaks["hbm_gbs"], "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs)",
+            "traffic": traffic, "algorithmic_bytes_per_launch": expert_bytes,
+            "launch_ms": expert_ms,
+        },
+        "e2e": {"value": tokens / (e2e_ms / 1000.0), "unit": "tokens/s",
+                "h2d_bytes_per_step": inputs.numel() * 2, "d2h_bytes_per_step": outputs.numel() * 2},
+        "gpu_launches": args.steps * steps_per_graph * args.layers * 3,
+        "clocks": clocks.summary(),
+        "setup_s": {"build": round(build_s, 1), "capture": round(capture_s, 1)},
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        ref = CpuReference({"w13_weight": layers[0].w13_weight, "w13_scale_inv": layers[0].w13_scale_inv,
+                            "w2_weight": layers[0].w2_weight, "w2_scale_inv": layers[0].w2_scale_inv})
+        ref.layer()
+        line["cpu_baseline"] = ref.sample(args.cpu_seconds, args.layers)
+    del graph
+    if world > 1:
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line))
+
+
+def main() -> None:
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -102,11 +102,11 @@ int finish_decode(DecodeArgs& a, void* workspace, size_t workspace_bytes, void* 
     if (a.tokens == 0) return 0;
     int sms = 0;
     if (sm_count_current(&sms)) return -1;
-    const size_t need = decode_workspace_layout(a.tokens, a.top_k, a.hidden, a.intermediate, sms, nullptr, nullptr);
+    const size_t need = decode_workspace_layout(a.tokens, a.top_k, a.hidden, a.intermediate, sms, 0, nullptr, nullptr);
     if (!workspace || workspace_bytes < need)
         return fail("decode workspace too small: need %zu bytes, got %zu", need, workspace_bytes);
     if (reinterpret_cast<uintptr_t>(workspace) & 255u) return fail("workspace must be 256-byte aligned");
-    decode_workspace_layout(a.tokens, a.top_k, a.hidden, a.intermediate, sms, static_cast<char*>(workspace), &a.ws);
+    decode_workspace_layout(a.tokens, a.top_k, a.hidden, a.intermediate, sms, 0, static_cast<char*>(workspace), &a.ws);
     a.ctas = sms * kDecodeCtasPerSm;
     a.workers_up = a.workers_dn = a.ctas * kDecodeWarps;
     const cudaError_t err = decode_launch(a, static_cast<cudaStream_t>(stream));
@@ -169,7 +169,7 @@ int drama_b200_permute_routes(const void* ids, int ids_dtype, int64_t pairs, int
 size_t drama_b200_decode_workspace_bytes(int64_t tokens, int top_k, int hidden, int intermediate) {
     int sms = 0;
     if (sm_count_current(&sms)) sms = 148;
-    return decode_workspace_layout(tokens, top_k, hidden, intermediate, sms, nullptr, nullptr);
+    return decode_workspace_layout(tokens, top_k, hidden, intermediate, sms, 0, nullptr, nullptr);
 }
 
 size_t drama_b200_decode_status_offset(void) { return 0; }
@@ -246,6 +246,121 @@ int drama_b200_int4_decode(const DramaB200Int4Bank* bank, const void* x, int x_d
     a.intermediate = b.intermediate;
     a.slots = b.slots;
     return finish_decode(a, workspace, workspace_bytes, stream);
+}
+
+size_t drama_b200_moe_layer_workspace_bytes(int64_t tokens, int top_k, int hidden, int intermediate,
+                                             int experts) {
+    int sms = 0;
+    if (sm_count_current(&sms)) sms = 148;
+    return decode_workspace_layout(tokens, top_k, hidden, intermediate, sms, experts, nullptr, nullptr);
+}
+
+namespace {
+// Validation and argument blocks shared by the fused layer entry points.
+int prepare_moe_layer(const DramaB200Fp8Bank* bank, const void* gate, const void* next_gate, const float* gamma,
+                      float eps, const void* hidden_in, void* hidden_out, int64_t tokens, int top_k,
+                      int64_t* ids_out, void* weights_out, void* normed_out, void* workspace,
+                      size_t workspace_bytes, MoeLayerArgs* m, DecodeArgs* d) {
+    if (!bank || !gate || !gamma || !hidden_in || !hidden_out) return fail("bank, gate, gamma and hidden buffers are required");
+    const DramaB200Fp8Bank& b = *bank;
+    const int H = b.hidden, E = b.slots;
+    if (tokens < 0 || top_k < 1 || top_k > 32 || top_k > E) return fail("top_k must be in [1, min(32, experts)]");
+    if (tokens * top_k > kMaxLayerPairs) return fail("the fused MoE layer supports at most %d (token, slot) pairs", kMaxLayerPairs);
+    if (H % 256 || H < 256 || b.intermediate % 128 || b.intermediate < 128) return fail("hidden must be a multiple of 256 and intermediate of 128");
+    if (tokens * H * 4 + 8192 > 200 * 1024) return fail("tokens * hidden too large for the router's shared memory");
+    if (E < 1 || E > 1024) return fail("experts must be in [1, 1024]");
+    if (!(eps > 0.0f)) return fail("eps must be positive");
+    if (!b.w13 || !b.w13_scale || !b.w2 || !b.w2_scale) return fail("FP8 bank pointers are required");
+    if (!aligned16(b.w13) || !aligned16(b.w2) || !aligned16(gate) || b.w13_row_stride % 16 || b.w2_row_stride % 16 ||
+        b.w13_slot_stride % 16 || b.w2_slot_stride % 16)
+        return fail("FP8 weight rows and the router weight must start on 16-byte boundaries");
+    if (next_gate && !aligned16(next_gate)) return fail("next router weight must be 16-byte aligned");
+    const size_t hb = static_cast<size_t>(tokens) * H * 2;
+    if (overlaps(hidden_out, hb, hidden_in, hb)) return fail("hidden_out must not overlap hidden_in");
+    if (tokens == 0) return 1;
+    int sms = 0;
+    if (sm_count_current(&sms)) return -1;
+    const size_t need = decode_workspace_layout(tokens, top_k, H, b.intermediate, sms, E, nullptr, nullptr);
+    if (!workspace || workspace_bytes < need)
+        return fail("MoE layer workspace too small: need %zu bytes, got %zu", need, workspace_bytes);
+    if (reinterpret_cast<uintptr_t>(workspace) & 255u) return fail("workspace must be 256-byte aligned");
+    *d = DecodeArgs{};
+    decode_workspace_layout(tokens, top_k, H, b.intermediate, sms, E, static_cast<char*>(workspace), &d->ws);
+    d->format = 0;
+    d->fp8 = b;
+    d->x = hidden_in;
+    d->x_dtype = DRAMA_B200_BF16;
+    d->tokens = tokens;
+    d->top_k = top_k;
+    d->out = hidden_out;
+    d->residual = hidden_in;
+    d->hidden = H;
+    d->intermediate = b.intermediate;
+    d->slots = E;
+    d->ctas = sms * kDecodeCtasPerSm;
+    d->workers_up = d->workers_dn = d->ctas * kDecodeWarps;
+    *m = MoeLayerArgs{};
+    m->hidden_in = static_cast<const __nv_bfloat16*>(hidden_in);
+    m->hidden_out = static_cast<__nv_bfloat16*>(hidden_out);
+    m->gamma = gamma;
+    m->gate = static_cast<const __nv_bfloat16*>(gate);
+    m->next_gate = static_cast<const __nv_bfloat16*>(next_gate);
+    m->eps = eps;
+    m->tokens = tokens;
+    m->experts = E;
+    m->top_k = top_k;
+    m->hidden = H;
+    m->intermediate = b.intermediate;
+    m->ws = d->ws;
+    m->ids_out = ids_out;
+    m->weights_out = static_cast<__nv_bfloat16*>(weights_out);
+    m->normed_out = static_cast<__nv_bfloat16*>(normed_out);
+    m->router_ctas = kRouterCtas < E ? kRouterCtas : E;
+    return 0;
+}
+}  // namespace
+
+int drama_b200_fp8_moe_layer(const DramaB200Fp8Bank* bank, const void* gate, const void* next_gate,
+                             const float* gamma, float eps, const void* hidden_in, void* hidden_out,
+                             int64_t tokens, int top_k, int64_t* ids_out, void* weights_out,
+                             void* normed_out, void* workspace, size_t workspace_bytes, void* stream) {
+    MoeLayerArgs m;
+    DecodeArgs d;
+    const int st = prepare_moe_layer(bank, gate, next_gate, gamma, eps, hidden_in, hidden_out, tokens, top_k,
+                                     ids_out, weights_out, normed_out, workspace, workspace_bytes, &m, &d);
+    if (st) return st < 0 ? -1 : 0;
+    cudaError_t err = moe_router_launch(m, static_cast<cudaStream_t>(stream));
+    if (err == cudaSuccess) err = decode_experts_launch(d, static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return fail("MoE layer launch failed: %s", cudaGetErrorString(err));
+    return 0;
+}
+
+int drama_b200_fp8_moe_router(const DramaB200Fp8Bank* bank, const void* gate, const void* next_gate,
+                              const float* gamma, float eps, const void* hidden_in, int64_t tokens, int top_k,
+                              int64_t* ids_out, void* weights_out, void* normed_out, void* workspace,
+                              size_t workspace_bytes, void* stream) {
+    MoeLayerArgs m;
+    DecodeArgs d;
+    // hidden_out is unused by the router; any non-overlapping pointer passes validation.
+    const int st = prepare_moe_layer(bank, gate, next_gate, gamma, eps, hidden_in, workspace, tokens, top_k,
+                                     ids_out, weights_out, normed_out, workspace, workspace_bytes, &m, &d);
+    if (st) return st < 0 ? -1 : 0;
+    const cudaError_t err = moe_router_launch(m, static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return fail("MoE router launch failed: %s", cudaGetErrorString(err));
+    return 0;
+}
+
+int drama_b200_fp8_moe_experts(const DramaB200Fp8Bank* bank, const void* hidden_in, void* hidden_out,
+                               int64_t tokens, int top_k, void* workspace, size_t workspace_bytes, void* stream) {
+    MoeLayerArgs m;
+    DecodeArgs d;
+    static const float one = 1.0f;
+    const int st = prepare_moe_layer(bank, hidden_in, nullptr, &one, 1e-6f, hidden_in, hidden_out, tokens, top_k,
+                                     nullptr, nullptr, nullptr, workspace, workspace_bytes, &m, &d);
+    if (st) return st < 0 ? -1 : 0;
+    const cudaError_t err = decode_experts_launch(d, static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return fail("MoE experts launch failed: %s", cudaGetErrorString(err));
+    return 0;
 }
 
 }  // extern "C"

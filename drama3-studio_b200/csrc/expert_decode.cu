@@ -90,6 +90,30 @@ __device__ __forceinline__ void fetch_group(GroupInfo& g, int id, const DecodeWo
     }
 }
 
+// Eight consecutive elements starting at a multiple of 8 (16-byte aligned for
+// 2-byte types, two 16-byte loads for fp32).
+__device__ __forceinline__ void load8(const void* base, int dtype, int64_t i, float (&v)[8]) {
+    if (dtype == DRAMA_B200_F32) {
+        const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(base) + i);
+        const float4 a = __ldg(p), b = __ldg(p + 1);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+        v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    } else {
+        const uint4 q = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(base) + i));
+        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            if (dtype == DRAMA_B200_BF16) {
+                v[2 * j] = __uint_as_float(w[j] << 16);
+                v[2 * j + 1] = __uint_as_float(w[j] & 0xffff0000u);
+            } else {
+                v[2 * j] = __half2float(__ushort_as_half(static_cast<unsigned short>(w[j] & 0xffffu)));
+                v[2 * j + 1] = __half2float(__ushort_as_half(static_cast<unsigned short>(w[j] >> 16)));
+            }
+        }
+    }
+}
+
 // ---------------------------------------------------------------------------
 // prep
 // ---------------------------------------------------------------------------
@@ -141,10 +165,12 @@ __global__ void __launch_bounds__(1024) decode_prep_kernel(DecodeArgs a) {
             ws.g_count[gbase + j] = min(kGroupTokens, c - j * kGroupTokens);
         }
     }
+    const int groups = warp_tot[31];
     if (tid == 0) {
-        ws.num_groups[0] = warp_tot[31];
+        ws.num_groups[0] = groups;
         ws.status[0] = dropped;
     }
+    zero_split_counters(ws, groups, a.hidden, a.intermediate, tid, blockDim.x);
     for (int64_t p = tid; p < P; p += blockDim.x) {
         ws.wts[p] = load_any(a.weights, a.weights_dtype, p);
         ws.hmax[p] = 0u;
@@ -158,27 +184,41 @@ __global__ void __launch_bounds__(1024) decode_prep_kernel(DecodeArgs a) {
                 for (int n = tid; n < a.hidden; n += blockDim.x) po[p * a.hidden + n] = 0.0f;
         }
     }
-    // f16 copy of every token row, scaled by 2^-e (one warp per row).
+    // f16 copy of every token row, scaled by 2^-e: all threads work on
+    // 8-element chunks of all rows; per-row amax via an order-free atomicMax.
     const int H = a.hidden;
-    for (int64_t row = warp; row < a.tokens; row += 32) {
-        float amax = 0.0f;
-        for (int k = lane; k < H; k += 32)
-            amax = fmaxf(amax, fabsf(load_any(a.x, a.x_dtype, row * H + k)));
+    unsigned* s_amax = reinterpret_cast<unsigned*>(smem + 34 * S);
+    for (int64_t t = tid; t < a.tokens; t += blockDim.x) s_amax[t] = 0u;
+    __syncthreads();
+    const int64_t chunks = a.tokens * (H / 8);
+    for (int64_t c = tid; c < chunks; c += blockDim.x) {
+        float v[8];
+        load8(a.x, a.x_dtype, c * 8, v);
+        float m = 0.0f;
 #pragma unroll
-        for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-        const int e = f16_exponent_for(amax);
-        const float inv = ldexpf(1.0f, -e);
-        if (lane == 0) ws.xscale[row] = ldexpf(1.0f, e);
-        __half* dst = reinterpret_cast<__half*>(ws.x16) + row * H;
-        for (int k = lane; k < H; k += 32) {
-            const float v = load_any(a.x, a.x_dtype, row * H + k) * inv;
-            int pos = k;
-            if (FMT == 1) {  // nibble-pair order inside each 8: [0,4,1,5,2,6,3,7]
-                const int m = k & 7;
-                pos = (k & ~7) + (m < 4 ? 2 * m : 2 * (m - 4) + 1);
-            }
-            dst[pos] = __float2half_rn(v);
+        for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(v[j]));
+        atomicMax(s_amax + c / (H / 8), __float_as_uint(m));
+    }
+    __syncthreads();
+    for (int64_t t = tid; t < a.tokens; t += blockDim.x)
+        ws.xscale[t] = ldexpf(1.0f, f16_exponent_for(__uint_as_float(s_amax[t])));
+    for (int64_t c = tid; c < chunks; c += blockDim.x) {
+        float v[8];
+        load8(a.x, a.x_dtype, c * 8, v);
+        const float inv = ldexpf(1.0f, -f16_exponent_for(__uint_as_float(s_amax[c / (H / 8)])));
+        uint4 o;
+        if (FMT == 1) {  // nibble-pair order inside each 8: [0,4,1,5,2,6,3,7]
+            o.x = pack_f16x2(v[0] * inv, v[4] * inv);
+            o.y = pack_f16x2(v[1] * inv, v[5] * inv);
+            o.z = pack_f16x2(v[2] * inv, v[6] * inv);
+            o.w = pack_f16x2(v[3] * inv, v[7] * inv);
+        } else {
+            o.x = pack_f16x2(v[0] * inv, v[1] * inv);
+            o.y = pack_f16x2(v[2] * inv, v[3] * inv);
+            o.z = pack_f16x2(v[4] * inv, v[5] * inv);
+            o.w = pack_f16x2(v[6] * inv, v[7] * inv);
         }
+        reinterpret_cast<uint4*>(ws.x16)[c] = o;
     }
 }
 
@@ -396,14 +436,13 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, kDecodeCtasPerSm) decode_up
     grid_launch_dependents();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const int groups = __ldcg(a.ws.num_groups);
-    prefetch_down_slabs(a, groups);
     const int KB = a.hidden / 128, TILES = a.intermediate / 16;
     const int64_t cells = static_cast<int64_t>(groups) * TILES * KB;
-    if (cells == 0) return;
     const int64_t workers = min(static_cast<int64_t>(a.workers_up), cells);
     const int64_t w = static_cast<int64_t>(blockIdx.x) * kDecodeWarps + warp;
-    if (w >= workers) return;
-    const int64_t c0 = range_start(w, cells, workers), c1 = range_start(w + 1, cells, workers);
+    const bool active = w < workers;
+    const int64_t c0 = active ? range_start(w, cells, workers) : 0;
+    const int64_t c1 = active ? range_start(w + 1, cells, workers) : 0;
     const uint64_t pol = policy_evict_first();
     const __half* x16 = reinterpret_cast<const __half*>(a.ws.x16);
 
@@ -417,6 +456,10 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, kDecodeCtasPerSm) decode_up
 #pragma unroll
     for (int i = 0; i < kUpDepth - 1; ++i)
         if (c0 + i < c1) issue(ring[i], c0 + i);
+    // With the first weight loads in flight, pull the down-projection slabs
+    // of this call's experts into L2 for the down kernel.
+    prefetch_down_slabs(a, groups);
+    if (!active) return;
 
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     int64_t cur_tile = c0 / KB;
@@ -702,27 +745,32 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, kDecodeCtasPerSm) decode_do
 }
 
 template <int FMT, int XDT>
+cudaError_t launch_experts(const DecodeArgs& a, cudaStream_t s) {
+    cudaError_t err = launch_pdl(decode_up_kernel<FMT, XDT>, dim3(a.ctas), dim3(kDecodeWarps * 32), 0, s, a);
+    if (err != cudaSuccess) return err;
+    return launch_pdl(decode_down_kernel<FMT, XDT>, dim3(a.ctas), dim3(kDecodeWarps * 32), 0, s, a);
+}
+
+template <int FMT, int XDT>
 cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t s) {
     const size_t smem = bucket_smem_bytes(a.slots);
     static int configured_smem = -1;  // per template instance; benign race
     cudaError_t err = cudaSuccess;
     if (static_cast<int>(smem) > configured_smem) {
         err = cudaFuncSetAttribute(decode_prep_kernel<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   static_cast<int>(bucket_smem_bytes(kMaxSlots)));
+                                   static_cast<int>(bucket_smem_bytes(kMaxSlots) + kMaxDecodePairs * sizeof(unsigned)));
         if (err != cudaSuccess) return err;
         configured_smem = static_cast<int>(bucket_smem_bytes(kMaxSlots));
     }
-    err = launch_pdl(decode_prep_kernel<FMT>, dim3(1), dim3(1024), smem, s, a);
+    err = launch_pdl(decode_prep_kernel<FMT>, dim3(1), dim3(1024), smem + a.tokens * sizeof(unsigned), s, a);
     if (err != cudaSuccess) return err;
-    err = launch_pdl(decode_up_kernel<FMT, XDT>, dim3(a.ctas), dim3(kDecodeWarps * 32), 0, s, a);
-    if (err != cudaSuccess) return err;
-    return launch_pdl(decode_down_kernel<FMT, XDT>, dim3(a.ctas), dim3(kDecodeWarps * 32), 0, s, a);
+    return launch_experts<FMT, XDT>(a, s);
 }
 
 }  // namespace
 
 size_t decode_workspace_layout(int64_t tokens, int top_k, int hidden, int intermediate, int sm_count,
-                               char* base, DecodeWorkspace* ws) {
+                               int experts, char* base, DecodeWorkspace* ws) {
     const int64_t P = tokens * top_k;
     const int64_t W = static_cast<int64_t>(sm_count) * kDecodeCtasPerSm * kDecodeWarps;
     size_t off = 0;
@@ -749,8 +797,24 @@ size_t decode_workspace_layout(int64_t tokens, int top_k, int hidden, int interm
     w.dn_part = reinterpret_cast<float*>(take(W * 2 * 32 * 4 * 4));
     w.dn_cnt = reinterpret_cast<int32_t*>(take(P * (hidden / 16) * 4));
     w.cmb_cnt = reinterpret_cast<int32_t*>(take((hidden / 16) * 4));
+    if (experts > 0) {
+        w.logits = reinterpret_cast<float*>(take(tokens * experts * 4));
+        w.router_cnt = reinterpret_cast<int32_t*>(take(4));
+    }
     if (ws) *ws = w;
     return off;
+}
+
+cudaError_t decode_experts_launch(const DecodeArgs& a, cudaStream_t s) {
+    const int key = a.format * 8 + a.x_dtype;
+    switch (key) {
+        case 0 * 8 + DRAMA_B200_BF16: return launch_experts<0, DRAMA_B200_BF16>(a, s);
+        case 0 * 8 + DRAMA_B200_F16: return launch_experts<0, DRAMA_B200_F16>(a, s);
+        case 0 * 8 + DRAMA_B200_F32: return launch_experts<0, DRAMA_B200_F32>(a, s);
+        case 1 * 8 + DRAMA_B200_BF16: return launch_experts<1, DRAMA_B200_BF16>(a, s);
+        case 1 * 8 + DRAMA_B200_F16: return launch_experts<1, DRAMA_B200_F16>(a, s);
+        default: return launch_experts<1, DRAMA_B200_F32>(a, s);
+    }
 }
 
 cudaError_t decode_launch(const DecodeArgs& a, cudaStream_t s) {

@@ -1,6 +1,7 @@
 // Internal kernel entry points and argument blocks (host side of the ABI).
 #pragma once
 
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -80,10 +81,25 @@ struct DecodeWorkspace {
     float* dn_part;       // [Wd][2][32][4]
     int32_t* dn_cnt;      // [P * H/16]
     int32_t* cmb_cnt;     // [H/16]
+    float* logits;        // [T][E] router logits (MoE layer entry point only)
+    int32_t* router_cnt;  // [1]
 };
 
+// The split-K and combine counters of one call: zeroed by whichever kernel
+// builds the expert groups, before the expert kernels run.
+#ifdef __CUDACC__
+__device__ __forceinline__ void zero_split_counters(const DecodeWorkspace& ws, int groups, int hidden,
+                                                    int intermediate, int tid, int threads) {
+    const int up = groups * (intermediate / 16), dn = groups * (hidden / 16);
+    for (int i = tid; i < up; i += threads) ws.up_cnt[i] = 0;
+    for (int i = tid; i < dn; i += threads) ws.dn_cnt[i] = 0;
+    for (int i = tid; i < hidden / 16; i += threads) ws.cmb_cnt[i] = 0;
+}
+#endif
+
+// experts > 0 adds the router scratch used by the fused MoE layer.
 size_t decode_workspace_layout(int64_t tokens, int top_k, int hidden, int intermediate,
-                               int sm_count, char* base, DecodeWorkspace* ws);
+                               int sm_count, int experts, char* base, DecodeWorkspace* ws);
 
 struct DecodeArgs {
     int format;  // 0 = FP8 block-scaled, 1 = INT4 group-128
@@ -105,6 +121,27 @@ struct DecodeArgs {
     int workers_up, workers_dn, ctas;
 };
 
-cudaError_t decode_launch(const DecodeArgs& a, cudaStream_t s);
+cudaError_t decode_launch(const DecodeArgs& a, cudaStream_t s);          // prep + up + down
+cudaError_t decode_experts_launch(const DecodeArgs& a, cudaStream_t s);  // up + down
+
+constexpr int kMaxLayerPairs = 256;
+constexpr int kRouterCtas = 16;
+
+struct MoeLayerArgs {
+    const __nv_bfloat16* hidden_in;
+    __nv_bfloat16* hidden_out;
+    const float* gamma;
+    const __nv_bfloat16* gate;
+    const __nv_bfloat16* next_gate;
+    float eps;
+    int64_t tokens;
+    int experts, top_k, hidden, intermediate;
+    DecodeWorkspace ws;
+    int64_t* ids_out;
+    __nv_bfloat16* weights_out;
+    __nv_bfloat16* normed_out;
+    int router_ctas;
+};
+cudaError_t moe_router_launch(const MoeLayerArgs& m, cudaStream_t s);
 
 }  // namespace drama

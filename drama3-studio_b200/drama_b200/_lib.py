@@ -37,6 +37,10 @@ EXPORTS = (
     "drama_b200_decode_status_offset",
     "drama_b200_fp8_decode",
     "drama_b200_int4_decode",
+    "drama_b200_moe_layer_workspace_bytes",
+    "drama_b200_fp8_moe_layer",
+    "drama_b200_fp8_moe_router",
+    "drama_b200_fp8_moe_experts",
 )
 
 c_void_p, c_int, c_int64, c_size_t = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_size_t
@@ -94,10 +98,20 @@ class Library:
                        c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]
         dll.drama_b200_fp8_decode.argtypes = [ctypes.POINTER(Fp8Bank)] + decode_args
         dll.drama_b200_int4_decode.argtypes = [ctypes.POINTER(Int4Bank)] + decode_args
-        for name in EXPORTS:
-            if name not in ("drama_b200_error", "drama_b200_decode_workspace_bytes",
-                            "drama_b200_decode_status_offset"):
-                getattr(dll, name).restype = c_int
+        dll.drama_b200_moe_layer_workspace_bytes.argtypes = [c_int64, c_int, c_int, c_int, c_int]
+        dll.drama_b200_moe_layer_workspace_bytes.restype = c_size_t
+        dll.drama_b200_fp8_moe_layer.argtypes = [
+            ctypes.POINTER(Fp8Bank), c_void_p, c_void_p, c_void_p, ctypes.c_float, c_void_p, c_void_p,
+            c_int64, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]
+        dll.drama_b200_fp8_moe_router.argtypes = [
+            ctypes.POINTER(Fp8Bank), c_void_p, c_void_p, c_void_p, ctypes.c_float, c_void_p,
+            c_int64, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]
+        dll.drama_b200_fp8_moe_experts.argtypes = [
+            ctypes.POINTER(Fp8Bank), c_void_p, c_void_p, c_int64, c_int, c_void_p, c_size_t, c_void_p]
+        for name in ("drama_b200_device_check", "drama_b200_route_topk", "drama_b200_permute_routes",
+                     "drama_b200_fp8_decode", "drama_b200_int4_decode", "drama_b200_fp8_moe_layer",
+                     "drama_b200_fp8_moe_router", "drama_b200_fp8_moe_experts"):
+            getattr(dll, name).restype = c_int
         if dll.drama_b200_abi() != ABI_VERSION:
             raise RuntimeError("Unsupported drama_b200 ABI version")
 

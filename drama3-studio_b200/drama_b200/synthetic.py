@@ -45,8 +45,11 @@ def quantize_fp8_blocks(weight: torch.Tensor):
 
 
 def fp8_bank(experts: int, hidden: int, intermediate: int, seed: int, *, device="cpu",
-             std: float = 0.02) -> dict[str, torch.Tensor]:
-    """An ``ExpertStore``-shaped FP8 bank, generated one expert at a time."""
+             std: float = 0.02, chunk: int = 1) -> dict[str, torch.Tensor]:
+    """An ``ExpertStore``-shaped FP8 bank, generated ``chunk`` experts at a time.
+
+    The random stream depends on ``chunk``; tests use the default (1).
+    """
     dev = torch.device(device)
     gen = _generator(seed, dev)
     bank = {
@@ -55,12 +58,14 @@ def fp8_bank(experts: int, hidden: int, intermediate: int, seed: int, *, device=
         "w2_weight": torch.empty(experts, hidden, intermediate, dtype=FP8, device=dev),
         "w2_scale_inv": torch.empty(experts, hidden // BLOCK, intermediate // BLOCK, device=dev),
     }
-    for e in range(experts):
+    for e in range(0, experts, chunk):
+        n = min(chunk, experts - e)
         for name, rows, cols in (("w13", 2 * intermediate, hidden), ("w2", hidden, intermediate)):
-            w = torch.randn(rows, cols, generator=gen, device=dev) * std
+            w = torch.randn(n, rows, cols, generator=gen, device=dev) * std
             q, s = quantize_fp8_blocks(w)
-            bank[f"{name}_weight"][e].copy_(q)
-            bank[f"{name}_scale_inv"][e].copy_(s)
+            bank[f"{name}_weight"][e:e + n].copy_(q)
+            bank[f"{name}_scale_inv"][e:e + n].copy_(s)
+            del w, q, s
     return bank
 
 

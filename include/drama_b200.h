@@ -151,6 +151,47 @@ DRAMA_B200_API int drama_b200_int4_decode(const DramaB200Int4Bank* bank, const v
                                           void* workspace, size_t workspace_bytes,
                                           void* stream);
 
+/* ---------------------------------------------------------------------------
+ * One decode MoE layer, fully on the device (graph-capturable):
+ *   normed = bf16(x * 1/sqrt(mean(x^2) + eps) * gamma)      (fixed fp32 order)
+ *   logits = bf16(normed @ gate^T)                           (fixed fp32 order)
+ *   w, ids = route_topk(logits, top_k, renormalize=1) ; w -> bf16
+ *   hidden_out = bf16(hidden_in + experts(normed, ids, w))   (K1 arithmetic)
+ * This is one layer of BackboneDecodeGraph (src/drama_low_vram/
+ * backbone_graph.py:306-337: router pre-graph, expert call, residual post-
+ * graph) with no mixer or shared expert and with the expert call on the
+ * device instead of ExpertOffloadManager's host routing (offload.py:1016-1063).
+ * hidden_in/hidden_out: bf16 [tokens, H] (must not overlap); gate: bf16
+ * [experts, H]; gamma: fp32 [H]; next_gate (optional) is prefetched into L2
+ * for the following layer. ids_out (int64 [tokens, top_k]), weights_out
+ * (bf16) and normed_out (bf16 [tokens, H]) are optional traces.
+ * tokens * top_k <= 256, H % 256 == 0, experts = bank->slots <= 1024.
+ * ------------------------------------------------------------------------- */
+DRAMA_B200_API size_t drama_b200_moe_layer_workspace_bytes(int64_t tokens, int top_k, int hidden,
+                                                           int intermediate, int experts);
+
+DRAMA_B200_API int drama_b200_fp8_moe_layer(const DramaB200Fp8Bank* bank, const void* gate,
+                                            const void* next_gate, const float* gamma, float eps,
+                                            const void* hidden_in, void* hidden_out,
+                                            int64_t tokens, int top_k, int64_t* ids_out,
+                                            void* weights_out, void* normed_out, void* workspace,
+                                            size_t workspace_bytes, void* stream);
+
+/* The two halves of drama_b200_fp8_moe_layer, for callers that time or
+ * interleave them: the router (RMSNorm, router GEMV, top-k, expert groups,
+ * written into the workspace) and the expert GEMVs with combine + residual
+ * (reading the groups the router left in the same workspace). Issue them on
+ * one stream, router first, with the same bank/tokens/top_k/workspace. */
+DRAMA_B200_API int drama_b200_fp8_moe_router(const DramaB200Fp8Bank* bank, const void* gate,
+                                             const void* next_gate, const float* gamma, float eps,
+                                             const void* hidden_in, int64_t tokens, int top_k,
+                                             int64_t* ids_out, void* weights_out, void* normed_out,
+                                             void* workspace, size_t workspace_bytes, void* stream);
+
+DRAMA_B200_API int drama_b200_fp8_moe_experts(const DramaB200Fp8Bank* bank, const void* hidden_in,
+                                              void* hidden_out, int64_t tokens, int top_k,
+                                              void* workspace, size_t workspace_bytes, void* stream);
+
 /* Device status words of the last decode call on this workspace:
  * [0] = pairs dropped for an out-of-range slot id. Copy them to the host
  * with drama_b200_decode_status_offset() bytes into the workspace. */
