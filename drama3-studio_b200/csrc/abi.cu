@@ -108,7 +108,6 @@ int finish_decode(DecodeArgs& a, void* workspace, size_t workspace_bytes, void* 
     if (reinterpret_cast<uintptr_t>(workspace) & 255u) return fail("workspace must be 256-byte aligned");
     decode_workspace_layout(a.tokens, a.top_k, a.hidden, a.intermediate, sms, 0, static_cast<char*>(workspace), &a.ws);
     a.ctas = sms * kDecodeCtasPerSm;
-    a.workers_up = a.workers_dn = a.ctas * kDecodeWarps;
     const cudaError_t err = decode_launch(a, static_cast<cudaStream_t>(stream));
     if (err != cudaSuccess) return fail("decode launch failed: %s", cudaGetErrorString(err));
     return 0;
@@ -259,14 +258,15 @@ namespace {
 // Validation and argument blocks shared by the fused layer entry points.
 int prepare_moe_layer(const DramaB200Fp8Bank* bank, const void* gate, const void* next_gate, const float* gamma,
                       float eps, const void* hidden_in, void* hidden_out, int64_t tokens, int top_k,
-                      int64_t* ids_out, void* weights_out, void* normed_out, void* workspace,
+                      int64_t* ids_out, void* weights_out, void* normed_out, void* moe_out, void* workspace,
                       size_t workspace_bytes, MoeLayerArgs* m, DecodeArgs* d) {
     if (!bank || !gate || !gamma || !hidden_in || !hidden_out) return fail("bank, gate, gamma and hidden buffers are required");
     const DramaB200Fp8Bank& b = *bank;
     const int H = b.hidden, E = b.slots;
     if (tokens < 0 || top_k < 1 || top_k > 32 || top_k > E) return fail("top_k must be in [1, min(32, experts)]");
     if (tokens * top_k > kMaxLayerPairs) return fail("the fused MoE layer supports at most %d (token, slot) pairs", kMaxLayerPairs);
-    if (H % 256 || H < 256 || b.intermediate % 128 || b.intermediate < 128) return fail("hidden must be a multiple of 256 and intermediate of 128");
+    if (H % 256 || H < 256 || H > 4096 || b.intermediate % 128 || b.intermediate < 128)
+        return fail("hidden must be a multiple of 256 up to 4096 and intermediate a multiple of 128");
     if (tokens * H * 4 + 8192 > 200 * 1024) return fail("tokens * hidden too large for the router's shared memory");
     if (E < 1 || E > 1024) return fail("experts must be in [1, 1024]");
     if (!(eps > 0.0f)) return fail("eps must be positive");
@@ -294,11 +294,11 @@ int prepare_moe_layer(const DramaB200Fp8Bank* bank, const void* gate, const void
     d->top_k = top_k;
     d->out = hidden_out;
     d->residual = hidden_in;
+    d->moe_out = moe_out;
     d->hidden = H;
     d->intermediate = b.intermediate;
     d->slots = E;
     d->ctas = sms * kDecodeCtasPerSm;
-    d->workers_up = d->workers_dn = d->ctas * kDecodeWarps;
     *m = MoeLayerArgs{};
     m->hidden_in = static_cast<const __nv_bfloat16*>(hidden_in);
     m->hidden_out = static_cast<__nv_bfloat16*>(hidden_out);
@@ -323,11 +323,12 @@ int prepare_moe_layer(const DramaB200Fp8Bank* bank, const void* gate, const void
 int drama_b200_fp8_moe_layer(const DramaB200Fp8Bank* bank, const void* gate, const void* next_gate,
                              const float* gamma, float eps, const void* hidden_in, void* hidden_out,
                              int64_t tokens, int top_k, int64_t* ids_out, void* weights_out,
-                             void* normed_out, void* workspace, size_t workspace_bytes, void* stream) {
+                             void* normed_out, void* moe_out, void* workspace, size_t workspace_bytes,
+                             void* stream) {
     MoeLayerArgs m;
     DecodeArgs d;
     const int st = prepare_moe_layer(bank, gate, next_gate, gamma, eps, hidden_in, hidden_out, tokens, top_k,
-                                     ids_out, weights_out, normed_out, workspace, workspace_bytes, &m, &d);
+                                     ids_out, weights_out, normed_out, moe_out, workspace, workspace_bytes, &m, &d);
     if (st) return st < 0 ? -1 : 0;
     cudaError_t err = moe_router_launch(m, static_cast<cudaStream_t>(stream));
     if (err == cudaSuccess) err = decode_experts_launch(d, static_cast<cudaStream_t>(stream));
@@ -343,7 +344,7 @@ int drama_b200_fp8_moe_router(const DramaB200Fp8Bank* bank, const void* gate, co
     DecodeArgs d;
     // hidden_out is unused by the router; any non-overlapping pointer passes validation.
     const int st = prepare_moe_layer(bank, gate, next_gate, gamma, eps, hidden_in, workspace, tokens, top_k,
-                                     ids_out, weights_out, normed_out, workspace, workspace_bytes, &m, &d);
+                                     ids_out, weights_out, normed_out, nullptr, workspace, workspace_bytes, &m, &d);
     if (st) return st < 0 ? -1 : 0;
     const cudaError_t err = moe_router_launch(m, static_cast<cudaStream_t>(stream));
     if (err != cudaSuccess) return fail("MoE router launch failed: %s", cudaGetErrorString(err));
@@ -351,12 +352,13 @@ int drama_b200_fp8_moe_router(const DramaB200Fp8Bank* bank, const void* gate, co
 }
 
 int drama_b200_fp8_moe_experts(const DramaB200Fp8Bank* bank, const void* hidden_in, void* hidden_out,
-                               int64_t tokens, int top_k, void* workspace, size_t workspace_bytes, void* stream) {
+                               int64_t tokens, int top_k, void* moe_out, void* workspace, size_t workspace_bytes,
+                               void* stream) {
     MoeLayerArgs m;
     DecodeArgs d;
     static const float one = 1.0f;
     const int st = prepare_moe_layer(bank, hidden_in, nullptr, &one, 1e-6f, hidden_in, hidden_out, tokens, top_k,
-                                     nullptr, nullptr, nullptr, workspace, workspace_bytes, &m, &d);
+                                     nullptr, nullptr, nullptr, moe_out, workspace, workspace_bytes, &m, &d);
     if (st) return st < 0 ? -1 : 0;
     const cudaError_t err = decode_experts_launch(d, static_cast<cudaStream_t>(stream));
     if (err != cudaSuccess) return fail("MoE experts launch failed: %s", cudaGetErrorString(err));

@@ -57,24 +57,23 @@ size_t bucket_smem_bytes(int experts);
 // ---------------------------------------------------------------------------
 // Decode (K1) workspace carved out of one caller buffer.
 // ---------------------------------------------------------------------------
-constexpr int kDecodeWarps = 8;          // warps per CTA of the GEMV kernels
-constexpr int kDecodeCtasPerSm = 2;      // resident CTAs per SM
+constexpr int kDecodeMaxWarps = 16;      // upper bound on warps per CTA of the GEMV kernels
+constexpr int kDecodeCtasPerSm = 1;      // resident CTAs per SM
 constexpr int kGroupTokens = 8;          // tokens per expert group (one n8 MMA)
 constexpr int kMaxDecodePairs = 4096;
+constexpr int kStageTokens = 8;          // token rows staged in shared memory by the up kernel
+constexpr int kStageGroups = 4;          // expert groups staged in shared memory by the down kernel
 constexpr int kMaxSlots = 1024;
 
 struct DecodeWorkspace {
     int32_t* status;      // [4]
     int32_t* num_groups;  // [1]
     int32_t* order;       // [P]   pairs sorted by slot (stable)
-    int32_t* g_slot;      // [P]
-    int32_t* g_start;     // [P]
-    int32_t* g_count;     // [P]
+    int4* g_rec;          // [P][2] group records: {slot, start, count, 0}, 8 x u16 pair indices
     float* xscale;        // [T]   2^e per token row
     uint16_t* x16;        // [T][H] f16 copy of x * 2^-e (layout per format)
     float* wts;           // [P]   route weights as fp32
-    float* h;             // [P][I] SwiGLU activations, rounded to x's dtype
-    uint32_t* hmax;       // [P]   max |h| bits per pair
+    void* h;              // [P][I] SwiGLU activations in x's dtype
     float* pair_out;      // [P][H] weighted fp32 partials (when the caller gives none)
     float* up_part;       // [Wu][2][32][8]
     int32_t* up_cnt;      // [P * I/16]
@@ -88,6 +87,17 @@ struct DecodeWorkspace {
 // The split-K and combine counters of one call: zeroed by whichever kernel
 // builds the expert groups, before the expert kernels run.
 #ifdef __CUDACC__
+// Group record g: rec[2g] = {slot, first sorted position, pair count, 0};
+// rec[2g+1] = pair index (token * top_k + route slot) of each of the (<= 8)
+// pairs, two u16 per word.
+__device__ __forceinline__ void write_group(const DecodeWorkspace& ws, int g, int slot, int start, int count,
+                                            const int* pairs) {
+    uint32_t t[4] = {0u, 0u, 0u, 0u};
+    for (int c = 0; c < count; ++c) t[c >> 1] |= static_cast<uint32_t>(pairs[c] & 0xffff) << (16 * (c & 1));
+    ws.g_rec[2 * g] = make_int4(slot, start, count, 0);
+    ws.g_rec[2 * g + 1] = make_int4(static_cast<int>(t[0]), static_cast<int>(t[1]), static_cast<int>(t[2]),
+                                    static_cast<int>(t[3]));
+}
 __device__ __forceinline__ void zero_split_counters(const DecodeWorkspace& ws, int groups, int hidden,
                                                     int intermediate, int tid, int threads) {
     const int up = groups * (intermediate / 16), dn = groups * (hidden / 16);
@@ -116,9 +126,10 @@ struct DecodeArgs {
     void* out;
     float* pair_out;
     const void* residual;  // optional [T][H] added before the final rounding
+    void* moe_out;         // optional [T][H] combined expert output before the residual
     DecodeWorkspace ws;
     int hidden, intermediate, slots;
-    int workers_up, workers_dn, ctas;
+    int ctas;  // one CTA per SM
 };
 
 cudaError_t decode_launch(const DecodeArgs& a, cudaStream_t s);          // prep + up + down

@@ -19,6 +19,7 @@
 //     butterfly; logits rounded to bf16.
 #include "common.cuh"
 #include "kernels.h"
+#include "route.cuh"
 
 namespace drama {
 
@@ -26,6 +27,8 @@ namespace {
 
 constexpr int kRouterThreads = 256;
 constexpr unsigned kFullMask = 0xffffffffu;
+constexpr int kMaxPer = 16;     // H <= 4096: elements of a row per router thread
+constexpr int kMaxChunks = 16;  // H <= 4096: 256-element chunks per gate row
 
 __global__ void __launch_bounds__(kRouterThreads) moe_router_kernel(MoeLayerArgs a) {
     extern __shared__ float s_norm[];  // [T][H]
@@ -35,27 +38,47 @@ __global__ void __launch_bounds__(kRouterThreads) moe_router_kernel(MoeLayerArgs
     const int H = a.hidden, E = a.experts, T = static_cast<int>(a.tokens), k = a.top_k;
     const DecodeWorkspace& ws = a.ws;
 
-    // The next layer's router weights are static: start pulling them into L2.
+    // The next layer's router weights are static: start pulling them into L2,
+    // 4 KB per request, spread over all CTAs (chunk i goes to CTA i % grid).
     if (a.next_gate) {
         const int64_t bytes = static_cast<int64_t>(E) * H * 2;
-        const int64_t chunk = 32768;
-        for (int64_t off = (static_cast<int64_t>(blockIdx.x) * blockDim.x + tid) * chunk; off < bytes;
-             off += static_cast<int64_t>(gridDim.x) * blockDim.x * chunk)
-            prefetch_l2_bulk(reinterpret_cast<const char*>(a.next_gate) + off,
-                             static_cast<uint32_t>(min(chunk, bytes - off)));
+        const int64_t chunk = 4096;
+        for (int64_t i = blockIdx.x + static_cast<int64_t>(gridDim.x) * tid; i * chunk < bytes;
+             i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+            prefetch_l2_bulk(reinterpret_cast<const char*>(a.next_gate) + i * chunk,
+                             static_cast<uint32_t>(min(chunk, bytes - i * chunk)));
     }
     grid_dependency_wait();
     grid_launch_dependents();
 
-    // RMSNorm of every token row (each CTA keeps its own copy in smem).
-    const int per = H / kRouterThreads;
+    // RMSNorm of every token row (each CTA keeps its own copy in smem). Thread
+    // `tid` owns the H/256 consecutive elements starting at tid*H/256.
+    const int per = H / kRouterThreads;  // multiple of 8 (H % 2048 == 0) or H/256 in {1,2,4}
     for (int t = 0; t < T; ++t) {
-        const __nv_bfloat16* xrow = a.hidden_in + static_cast<int64_t>(t) * H;
-        float sq = 0.0f;
-        for (int j = 0; j < per; ++j) {
-            const float v = __bfloat162float(xrow[tid * per + j]);
-            sq = __fadd_rn(sq, __fmul_rn(v, v));
+        const __nv_bfloat16* xrow = a.hidden_in + static_cast<int64_t>(t) * H + tid * per;
+        float v[kMaxPer];
+        if ((per & 7) == 0) {
+#pragma unroll
+            for (int j = 0; j < kMaxPer; j += 8) {
+                if (j < per) {
+                    const uint4 q = *reinterpret_cast<const uint4*>(xrow + j);
+                    const uint32_t wv[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        v[j + 2 * u] = __uint_as_float(wv[u] << 16);
+                        v[j + 2 * u + 1] = __uint_as_float(wv[u] & 0xffff0000u);
+                    }
+                }
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < kMaxPer; ++j)
+                if (j < per) v[j] = __bfloat162float(xrow[j]);
         }
+        float sq = 0.0f;
+#pragma unroll
+        for (int j = 0; j < kMaxPer; ++j)
+            if (j < per) sq = __fadd_rn(sq, __fmul_rn(v[j], v[j]));
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) sq = __fadd_rn(sq, __shfl_xor_sync(kFullMask, sq, off));
         if (lane == 0) s_red[warp] = sq;
@@ -65,11 +88,13 @@ __global__ void __launch_bounds__(kRouterThreads) moe_router_kernel(MoeLayerArgs
         for (int w = 0; w < kRouterThreads / 32; ++w) total = __fadd_rn(total, s_red[w]);
         const float mean = __fmul_rn(total, 1.0f / static_cast<float>(H));
         const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
-        for (int j = 0; j < per; ++j) {
-            const int i = tid * per + j;
-            const float v = __bfloat162float(xrow[i]);
-            const float y = __fmul_rn(__fmul_rn(v, inv), a.gamma[i]);
-            s_norm[t * H + i] = __bfloat162float(__float2bfloat16_rn(y));
+#pragma unroll
+        for (int j = 0; j < kMaxPer; ++j) {
+            if (j < per) {
+                const int i = tid * per + j;
+                const float y = __fmul_rn(__fmul_rn(v[j], inv), a.gamma[i]);
+                s_norm[t * H + i] = __bfloat162float(__float2bfloat16_rn(y));
+            }
         }
         __syncthreads();
     }
@@ -93,19 +118,27 @@ __global__ void __launch_bounds__(kRouterThreads) moe_router_kernel(MoeLayerArgs
         }
     }
 
-    // Router GEMV: this CTA's experts, one warp per expert.
+    // Router GEMV: this CTA's experts, one warp per expert; all of a row's
+    // 16-byte loads are issued before the first product.
     const int per_cta = (E + gridDim.x - 1) / gridDim.x;
     const int e_begin = blockIdx.x * per_cta, e_end = min(E, e_begin + per_cta);
+    const int chunks = H / 256;
     for (int e = e_begin + warp; e < e_end; e += kRouterThreads / 32) {
         const __nv_bfloat16* grow = a.gate + static_cast<int64_t>(e) * H;
+        uint4 gq[kMaxChunks];
+#pragma unroll
+        for (int i = 0; i < kMaxChunks; ++i)
+            if (i < chunks) gq[i] = __ldg(reinterpret_cast<const uint4*>(grow + 256 * i + 8 * lane));
         for (int t = 0; t < T; ++t) {
             float acc = 0.0f;
-            for (int i = 0; i < H / 256; ++i) {
-                const uint4 q = __ldg(reinterpret_cast<const uint4*>(grow + 256 * i + 8 * lane));
-                const __nv_bfloat16* gv = reinterpret_cast<const __nv_bfloat16*>(&q);
-                const float* xv = s_norm + t * H + 256 * i + 8 * lane;
 #pragma unroll
-                for (int j = 0; j < 8; ++j) acc = __fadd_rn(acc, __fmul_rn(xv[j], __bfloat162float(gv[j])));
+            for (int i = 0; i < kMaxChunks; ++i) {
+                if (i < chunks) {
+                    const __nv_bfloat16* gv = reinterpret_cast<const __nv_bfloat16*>(&gq[i]);
+                    const float* xv = s_norm + t * H + 256 * i + 8 * lane;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) acc = __fadd_rn(acc, __fmul_rn(xv[j], __bfloat162float(gv[j])));
+                }
             }
 #pragma unroll
             for (int off = 16; off > 0; off >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(kFullMask, acc, off));
@@ -114,127 +147,29 @@ __global__ void __launch_bounds__(kRouterThreads) moe_router_kernel(MoeLayerArgs
     }
 
     // The last CTA to finish routes every token and builds the expert groups.
-    __threadfence();
     __syncthreads();
-    if (tid == 0) s_last = (atomicAdd(ws.router_cnt, 1) == static_cast<int>(gridDim.x) - 1);
+    if (tid == 0) {
+        asm volatile("fence.acq_rel.gpu;" ::: "memory");
+        s_last = (atomicAdd(ws.router_cnt, 1) == static_cast<int>(gridDim.x) - 1);
+    }
     __syncthreads();
     if (!s_last) return;
-    __threadfence();
+    asm volatile("fence.acq_rel.gpu;" ::: "memory");
     if (tid == 0) *ws.router_cnt = 0;
 
     int* s_ids = reinterpret_cast<int*>(s_norm);           // [T*k]
     float* s_w = s_norm + kMaxLayerPairs;                   // [T*k]
     for (int t = warp; t < T; t += kRouterThreads / 32) {
-        // softmax in torch's persistent-warp order (E <= 1024).
+        // softmax / top-k / renormalise in torch's CUDA order (route.cuh).
         const float* lrow = ws.logits + static_cast<int64_t>(t) * E;
-        constexpr int kIt = 32;
-        float v[kIt];
-        int p2 = 1;
-        while (p2 < E) p2 <<= 1;
-        const int lanes = p2 < 32 ? p2 : 32;
-        const int iters = p2 / lanes;
-#pragma unroll
-        for (int i = 0; i < kIt; ++i) {
-            const int idx = lane + i * lanes;
-            v[i] = (i < iters && lane < lanes && idx < E) ? __ldcg(lrow + idx) : -INFINITY;
-        }
-        float m = v[0];
-#pragma unroll
-        for (int i = 1; i < kIt; ++i) m = fmaxf(m, v[i]);
-        for (int off = lanes / 2; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(kFullMask, m, off));
-        float sum = 0.0f;
-#pragma unroll
-        for (int i = 0; i < kIt; ++i) {
-            if (i < iters) {
-                v[i] = expf(v[i] - m);
-                sum += v[i];
-            }
-        }
-        for (int off = lanes / 2; off > 0; off >>= 1) sum = sum + __shfl_xor_sync(kFullMask, sum, off);
-        bool avail[kIt];
-#pragma unroll
-        for (int i = 0; i < kIt; ++i) {
-            const int idx = lane + i * lanes;
-            avail[i] = i < iters && lane < lanes && idx < E;
-            v[i] = avail[i] ? v[i] / sum : -INFINITY;
-        }
-        // k-th largest, gather order, bitonic network: as route_topk.
-        int need = k;
-        float kth = 0.0f;
-        bool rem[kIt];
-#pragma unroll
-        for (int i = 0; i < kIt; ++i) rem[i] = avail[i];
-        for (int round = 0; round < k; ++round) {
-            float mx = -INFINITY;
-#pragma unroll
-            for (int i = 0; i < kIt; ++i)
-                if (rem[i]) mx = fmaxf(mx, v[i]);
-#pragma unroll
-            for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFullMask, mx, off));
-            int cnt = 0;
-#pragma unroll
-            for (int i = 0; i < kIt; ++i) {
-                const bool eq = rem[i] && v[i] == mx;
-                cnt += __popc(__ballot_sync(kFullMask, eq));
-                if (eq) rem[i] = false;
-            }
-            kth = mx;
-            if (cnt >= need) break;
-            need -= cnt;
-        }
         float* s_key = s_w + kMaxLayerPairs + warp * 64;
         int* s_idx = reinterpret_cast<int*>(s_key + 32);
-        const unsigned lt = (1u << lane) - 1u;
-        int base = 0;
-#pragma unroll
-        for (int i = 0; i < kIt; ++i) {
-            const bool pick = avail[i] && v[i] > kth;
-            const unsigned b = __ballot_sync(kFullMask, pick);
-            if (pick) {
-                s_key[base + __popc(b & lt)] = v[i];
-                s_idx[base + __popc(b & lt)] = lane + i * lanes;
-            }
-            base += __popc(b);
-        }
-#pragma unroll
-        for (int i = 0; i < kIt; ++i) {
-            const bool eq = avail[i] && v[i] == kth;
-            const unsigned b = __ballot_sync(kFullMask, eq);
-            const int pos = base + __popc(b & lt);
-            if (eq && pos < k) {
-                s_key[pos] = v[i];
-                s_idx[pos] = lane + i * lanes;
-            }
-            base += __popc(b);
-        }
-        __syncwarp();
-        float key = lane < k ? s_key[lane] : 0.0f;
-        int idx = lane < k ? s_idx[lane] : 0;
-        bool valid = lane < k;
-        auto stage = [&](int stride, bool flag) {
-            const float pk = __shfl_xor_sync(kFullMask, key, stride);
-            const int pi = __shfl_xor_sync(kFullMask, idx, stride);
-            const bool pv = __shfl_xor_sync(kFullMask, valid, stride);
-            const bool is_a = (lane & stride) == 0;
-            const float ka = is_a ? key : pk, kb = is_a ? pk : key;
-            const bool va = is_a ? valid : pv, vb = is_a ? pv : valid;
-            const bool swap = ((ka > kb) && va) || !vb;
-            if (swap == flag) {
-                key = pk;
-                idx = pi;
-                valid = pv;
-            }
-        };
-        for (int size = 2; size < 32; size <<= 1)
-            for (int stride = size >> 1; stride > 0; stride >>= 1)
-                stage(stride, (((lane / (2 * stride)) * stride + (lane % stride)) & (size >> 1)) != 0);
-        for (int stride = 16; stride > 0; stride >>= 1) stage(stride, false);
-        int pk2 = 1;
-        while (pk2 < k) pk2 <<= 1;
-        float tsum = lane < k ? key : 0.0f;
-        for (int off = 1; off < pk2; off <<= 1) tsum = tsum + __shfl_down_sync(kFullMask, tsum, off);
-        const float total = __shfl_sync(kFullMask, tsum, 0);
-        const float w = __bfloat162float(__float2bfloat16_rn(key / total));
+        int idx = 0;
+        float wr = 0.0f;
+        dispatch_experts(E, [&]<int LANES, int ITERS>() {
+            route_row<LANES, ITERS>([&](int i) { return __ldcg(lrow + i); }, E, k, true, lane, s_key, s_idx, idx, wr);
+        });
+        const float w = __bfloat162float(__float2bfloat16_rn(wr));
         if (lane < k) {
             s_ids[t * k + lane] = idx;
             s_w[t * k + lane] = w;
@@ -258,24 +193,25 @@ __global__ void __launch_bounds__(kRouterThreads) moe_router_kernel(MoeLayerArgs
         s_order[rank] = p;
         ws.order[rank] = p;
         ws.wts[p] = s_w[p];
-        ws.hmax[p] = 0u;
     }
     __syncthreads();
     if (tid == 0) {
-        int groups = 0, run_start = 0;
+        int groups = 0, run_start = 0, gstart = 0, gcount = 0, gslot = -1;
+        int toks[kGroupTokens];
         for (int pos = 0; pos < P; ++pos) {
-            const int id = s_ids[s_order[pos]];
+            const int p = s_order[pos];
+            const int id = s_ids[p];
             const bool new_id = pos == 0 || s_ids[s_order[pos - 1]] != id;
             if (new_id) run_start = pos;
             if (new_id || (pos - run_start) % kGroupTokens == 0) {
-                ws.g_slot[groups] = id;
-                ws.g_start[groups] = pos;
-                ws.g_count[groups] = 1;
-                ++groups;
-            } else {
-                ws.g_count[groups - 1] += 1;
+                if (gcount) write_group(ws, groups++, gslot, gstart, gcount, toks);
+                gslot = id;
+                gstart = pos;
+                gcount = 0;
             }
+            toks[gcount++] = p;
         }
+        if (gcount) write_group(ws, groups++, gslot, gstart, gcount, toks);
         ws.num_groups[0] = groups;
         ws.status[0] = 0;
         s_groups = groups;

@@ -18,13 +18,13 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "route.cuh"
 #include "bucket.cuh"
 
 namespace drama {
 
 namespace {
 
-constexpr unsigned kFull = 0xffffffffu;
 
 // One warp per token row; LANES lanes x ITERS values cover next_pow2(E).
 template <int LANES, int ITERS>
@@ -38,127 +38,11 @@ __global__ void __launch_bounds__(256) route_topk_kernel(RouteArgs a) {
     if (row >= a.tokens) return;
     const int E = a.experts;
 
-    float v[ITERS];
-#pragma unroll
-    for (int i = 0; i < ITERS; ++i) {
-        const int idx = lane + i * LANES;
-        v[i] = (lane < LANES && idx < E)
-                   ? load_any(a.logits, a.logits_dtype, row * static_cast<int64_t>(E) + idx)
-                   : -INFINITY;
-    }
-    // max: exact in any order.
-    float m = v[0];
-#pragma unroll
-    for (int i = 1; i < ITERS; ++i) m = fmaxf(m, v[i]);
-#pragma unroll
-    for (int off = LANES / 2; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(kFull, m, off));
-    float sum = 0.0f;
-#pragma unroll
-    for (int i = 0; i < ITERS; ++i) {
-        v[i] = expf(v[i] - m);
-        sum += v[i];
-    }
-#pragma unroll
-    for (int off = LANES / 2; off > 0; off >>= 1) sum = sum + __shfl_xor_sync(kFull, sum, off);
-    bool live[ITERS];
-#pragma unroll
-    for (int i = 0; i < ITERS; ++i) {
-        const int idx = lane + i * LANES;
-        live[i] = lane < LANES && idx < E;
-        v[i] = live[i] ? v[i] / sum : 0.0f;
-    }
-
-    // k-th largest probability (with multiplicity).
+    int idx = 0;
+    float w = 0.0f;
+    route_row<LANES, ITERS>([&](int i) { return load_any(a.logits, a.logits_dtype, row * static_cast<int64_t>(E) + i); },
+                            E, a.top_k, a.renormalize != 0, lane, s_key[warp], s_idx[warp], idx, w);
     const int k = a.top_k;
-    bool avail[ITERS];
-#pragma unroll
-    for (int i = 0; i < ITERS; ++i) avail[i] = live[i];
-    int need = k;
-    float kth = 0.0f;
-    for (int round = 0; round < k; ++round) {
-        float mx = -INFINITY;
-#pragma unroll
-        for (int i = 0; i < ITERS; ++i)
-            if (avail[i]) mx = fmaxf(mx, v[i]);
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, off));
-        int cnt = 0;
-#pragma unroll
-        for (int i = 0; i < ITERS; ++i) {
-            const bool eq = avail[i] && v[i] == mx;
-            cnt += __popc(__ballot_sync(kFull, eq));
-            if (eq) avail[i] = false;
-        }
-        kth = mx;
-        if (cnt >= need) break;
-        need -= cnt;
-    }
-
-    // gatherTopK order: strictly greater in index order, then equal ones.
-    const unsigned lt = (1u << lane) - 1u;
-    int base = 0;
-#pragma unroll
-    for (int i = 0; i < ITERS; ++i) {
-        const bool pick = live[i] && v[i] > kth;
-        const unsigned b = __ballot_sync(kFull, pick);
-        if (pick) {
-            const int pos = base + __popc(b & lt);
-            s_key[warp][pos] = v[i];
-            s_idx[warp][pos] = lane + i * LANES;
-        }
-        base += __popc(b);
-    }
-#pragma unroll
-    for (int i = 0; i < ITERS; ++i) {
-        const bool eq = live[i] && v[i] == kth;
-        const unsigned b = __ballot_sync(kFull, eq);
-        const int pos = base + __popc(b & lt);
-        if (eq && pos < k) {
-            s_key[warp][pos] = v[i];
-            s_idx[warp][pos] = lane + i * LANES;
-        }
-        base += __popc(b);
-    }
-    __syncwarp();
-    float key = lane < k ? s_key[warp][lane] : 0.0f;
-    int idx = lane < k ? s_idx[warp][lane] : 0;
-    bool valid = lane < k;
-
-    // 32-slot bitonic network (lane = slot); pair (l, l ^ stride).
-    auto stage = [&](int stride, bool flag) {
-        const float pk = __shfl_xor_sync(kFull, key, stride);
-        const int pi = __shfl_xor_sync(kFull, idx, stride);
-        const bool pv = __shfl_xor_sync(kFull, valid, stride);
-        const bool is_a = (lane & stride) == 0;
-        const float ka = is_a ? key : pk, kb = is_a ? pk : key;
-        const bool va = is_a ? valid : pv, vb = is_a ? pv : valid;
-        const bool swap = ((ka > kb) && va) || !vb;
-        if (swap == flag) {
-            key = pk;
-            idx = pi;
-            valid = pv;
-        }
-    };
-    for (int size = 2; size < 32; size <<= 1) {
-        for (int stride = size >> 1; stride > 0; stride >>= 1) {
-            const int t = (lane / (2 * stride)) * stride + (lane % stride);
-            stage(stride, (t & (size >> 1)) != 0);
-        }
-    }
-    for (int stride = 16; stride > 0; stride >>= 1) stage(stride, false);
-
-    float w = valid ? key : 0.0f;
-    if (a.renormalize) {
-        int p2 = 1;
-        while (p2 < k) p2 <<= 1;
-        float t = (lane < k) ? key : 0.0f;
-        for (int off = 1; off < p2; off <<= 1) {
-            const float o = __shfl_down_sync(kFull, t, off);
-            t = t + o;
-        }
-        const float total = __shfl_sync(kFull, t, 0);
-        w = w / total;
-    }
     if (lane < k) {
         const int64_t o = row * k + lane;
         store_index(a.ids, a.ids_dtype, o, idx);

@@ -102,12 +102,13 @@ class Library:
         dll.drama_b200_moe_layer_workspace_bytes.restype = c_size_t
         dll.drama_b200_fp8_moe_layer.argtypes = [
             ctypes.POINTER(Fp8Bank), c_void_p, c_void_p, c_void_p, ctypes.c_float, c_void_p, c_void_p,
-            c_int64, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]
+            c_int64, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]
         dll.drama_b200_fp8_moe_router.argtypes = [
             ctypes.POINTER(Fp8Bank), c_void_p, c_void_p, c_void_p, ctypes.c_float, c_void_p,
             c_int64, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]
         dll.drama_b200_fp8_moe_experts.argtypes = [
-            ctypes.POINTER(Fp8Bank), c_void_p, c_void_p, c_int64, c_int, c_void_p, c_size_t, c_void_p]
+            ctypes.POINTER(Fp8Bank), c_void_p, c_void_p, c_int64, c_int, c_void_p, c_void_p, c_size_t,
+            c_void_p]
         for name in ("drama_b200_device_check", "drama_b200_route_topk", "drama_b200_permute_routes",
                      "drama_b200_fp8_decode", "drama_b200_int4_decode", "drama_b200_fp8_moe_layer",
                      "drama_b200_fp8_moe_router", "drama_b200_fp8_moe_experts"):

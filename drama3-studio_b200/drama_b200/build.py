@@ -24,7 +24,7 @@ BUILD_DIR = SOURCE_ROOT / "_build"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [
-    "-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr",
+    "-O3", "-lineinfo", "-std=c++20", "--expt-relaxed-constexpr",
     "-Xcompiler", "-fPIC,-fvisibility=hidden", "-Xptxas", "-warn-spills",
 ]
 

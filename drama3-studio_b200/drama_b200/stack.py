@@ -50,6 +50,7 @@ class LayerTrace:
     ids: Tensor      # int64 [T, k]
     weights: Tensor  # bf16 [T, k]
     normed: Tensor   # bf16 [T, H]
+    moe: Tensor | None = None  # bf16 [T, H] expert output before the residual
 
 
 def moe_layer_workspace(tokens: int, top_k: int, hidden: int, intermediate: int, experts: int,
@@ -77,10 +78,11 @@ def moe_layer(hidden_in: Tensor, layer: MoELayer, out: Tensor, workspace: Tensor
     stream = _lib.stream_handle(hidden_in.device)
     traced = (_lib.ptr(trace.ids if trace else None), _lib.ptr(trace.weights if trace else None),
               _lib.ptr(trace.normed if trace else None))
+    moe_out = _lib.ptr(trace.moe if trace else None)
     if expert_events is None:
         lib.check(lib.dll.drama_b200_fp8_moe_layer(
             ctypes.byref(bank), layer.gate.data_ptr(), _lib.ptr(next_gate), layer.gamma.data_ptr(),
-            ctypes.c_float(eps), hidden_in.data_ptr(), out.data_ptr(), tokens, top_k, *traced,
+            ctypes.c_float(eps), hidden_in.data_ptr(), out.data_ptr(), tokens, top_k, *traced, moe_out,
             workspace.data_ptr(), workspace.numel(), stream))
         return out
     lib.check(lib.dll.drama_b200_fp8_moe_router(
@@ -89,7 +91,7 @@ def moe_layer(hidden_in: Tensor, layer: MoELayer, out: Tensor, workspace: Tensor
         workspace.data_ptr(), workspace.numel(), stream))
     expert_events[0].record()
     lib.check(lib.dll.drama_b200_fp8_moe_experts(
-        ctypes.byref(bank), hidden_in.data_ptr(), out.data_ptr(), tokens, top_k,
+        ctypes.byref(bank), hidden_in.data_ptr(), out.data_ptr(), tokens, top_k, moe_out,
         workspace.data_ptr(), workspace.numel(), stream))
     expert_events[1].record()
     return out
@@ -144,7 +146,8 @@ class DecodeStack:
             self.step(inputs[0], outputs[0])  # eager warm-up (lazy module loading)
         torch.cuda.current_stream(self.device).wait_stream(stream)
         torch.cuda.synchronize(self.device)
-        self.expert_events = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+        self.expert_events = [[(torch.cuda.Event(enable_timing=True, external=True),
+                                torch.cuda.Event(enable_timing=True, external=True))
                                for _ in self.layers] for _ in range(timed_steps)]
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, stream=stream):

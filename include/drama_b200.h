@@ -164,7 +164,8 @@ DRAMA_B200_API int drama_b200_int4_decode(const DramaB200Int4Bank* bank, const v
  * hidden_in/hidden_out: bf16 [tokens, H] (must not overlap); gate: bf16
  * [experts, H]; gamma: fp32 [H]; next_gate (optional) is prefetched into L2
  * for the following layer. ids_out (int64 [tokens, top_k]), weights_out
- * (bf16) and normed_out (bf16 [tokens, H]) are optional traces.
+ * (bf16), normed_out (bf16 [tokens, H]) and moe_out (bf16 [tokens, H], the
+ * combined expert output before the residual add) are optional traces.
  * tokens * top_k <= 256, H % 256 == 0, experts = bank->slots <= 1024.
  * ------------------------------------------------------------------------- */
 DRAMA_B200_API size_t drama_b200_moe_layer_workspace_bytes(int64_t tokens, int top_k, int hidden,
@@ -174,8 +175,8 @@ DRAMA_B200_API int drama_b200_fp8_moe_layer(const DramaB200Fp8Bank* bank, const 
                                             const void* next_gate, const float* gamma, float eps,
                                             const void* hidden_in, void* hidden_out,
                                             int64_t tokens, int top_k, int64_t* ids_out,
-                                            void* weights_out, void* normed_out, void* workspace,
-                                            size_t workspace_bytes, void* stream);
+                                            void* weights_out, void* normed_out, void* moe_out,
+                                            void* workspace, size_t workspace_bytes, void* stream);
 
 /* The two halves of drama_b200_fp8_moe_layer, for callers that time or
  * interleave them: the router (RMSNorm, router GEMV, top-k, expert groups,
@@ -190,7 +191,8 @@ DRAMA_B200_API int drama_b200_fp8_moe_router(const DramaB200Fp8Bank* bank, const
 
 DRAMA_B200_API int drama_b200_fp8_moe_experts(const DramaB200Fp8Bank* bank, const void* hidden_in,
                                               void* hidden_out, int64_t tokens, int top_k,
-                                              void* workspace, size_t workspace_bytes, void* stream);
+                                              void* moe_out, void* workspace, size_t workspace_bytes,
+                                              void* stream);
 
 /* Device status words of the last decode call on this workspace:
  * [0] = pairs dropped for an out-of-range slot id. Copy them to the host

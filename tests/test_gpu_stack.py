@@ -30,6 +30,7 @@ def _trace(tokens, top_k, hidden, device):
 
     return LayerTrace(torch.empty(tokens, top_k, dtype=torch.int64, device=device),
                       torch.empty(tokens, top_k, dtype=torch.bfloat16, device=device),
+                      torch.empty(tokens, hidden, dtype=torch.bfloat16, device=device),
                       torch.empty(tokens, hidden, dtype=torch.bfloat16, device=device))
 
 
@@ -52,8 +53,10 @@ def test_moe_layer_matches_oracle(cuda_device, hidden, inter, experts, tokens):
     np.testing.assert_array_equal(tr.ids.cpu().numpy(), ids)
     wb = tr.weights.cpu().view(torch.int16).numpy().view(np.uint16).astype(np.int32)
     assert np.abs(wb - R.bf16_bits(weights).astype(np.int32)).max() <= 1
-    moe_gpu = np_f32(out) - np_f32(x)
-    assert_parity(moe_gpu, new_h - np_f32(x), label=f"layer {hidden}x{inter} T={tokens}")
+    bank_np = bank
+    moe_ref = R.fp8_dequant_forward(normed, ids, weights, bank_np, "bfloat16")
+    assert_parity(np_f32(tr.moe), moe_ref, label=f"layer {hidden}x{inter} T={tokens}")
+    np.testing.assert_array_equal(np_f32(out), R.round_bf16(np_f32(x) + np_f32(tr.moe)))
     assert_parity(np_f32(out), new_h, label="hidden")
     # second call on the same workspace: identical bits
     out2 = torch.empty_like(x)
@@ -85,8 +88,11 @@ def test_stack_layers_teacher_forced_and_graph_replay(cuda_device):
         h_in = np_f32(inputs[i])
         new_h, normed, ids, _ = R.stack_layer(h_in, gamma, gate, bank, top_k=8)
         np.testing.assert_array_equal(traces[i].ids.cpu().numpy(), ids, err_msg=f"layer {i}")
+        moe_ref = R.fp8_dequant_forward(normed, ids, R.from_bf16_bits(
+            traces[i].weights.cpu().view(torch.int16).numpy().view(np.uint16)), bank, "bfloat16")
+        assert_parity(np_f32(traces[i].moe), moe_ref, label=f"layer {i}")
         out_i = np_f32(inputs[i + 1]) if i + 1 < layers else np_f32(src)
-        assert_parity(out_i - h_in, new_h - h_in, label=f"layer {i}")
+        np.testing.assert_array_equal(out_i, R.round_bf16(h_in + np_f32(traces[i].moe)))
     # the same steps captured in a graph reproduce the eager bits
     steps = 3
     ins = torch.stack([x] * steps)
