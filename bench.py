@@ -115,8 +115,8 @@ def measured_peaks() -> dict:
 
 
 def committed_traffic() -> float | None:
-    """DRAM bytes per expert-GEMV launch pair from the committed ncu summary."""
-    path = REPO / "profiles" / "decode_experts_traffic.json"
+    """DRAM bytes per MoE layer (both launches) from the committed ncu summary."""
+    path = REPO / "profiles" / "moe_layer_traffic.json"
     if path.is_file():
         return json.loads(path.read_text()).get("dram_bytes_per_layer")
     return None
@@ -267,7 +267,7 @@ def run_ours(args) -> None:
         e1.synchronize()
     barrier()
     ms = e0.elapsed_time(e1)
-    expert_ms = st.expert_time_ms()
+    layer_ms = st.layer_time_ms()
     if world > 1:
         t = torch.tensor([ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -295,9 +295,10 @@ def run_ours(args) -> None:
     tokens = args.steps * steps_per_graph * world
     value = tokens / (ms / 1000.0)
     expert_bytes = synthetic.expert_nbytes_fp8(HIDDEN, INTER) * TOP_K
-    layer_bytes = expert_bytes + EXPERTS * HIDDEN * 2 + HIDDEN * 2 * 2
+    # per layer: the routed experts, the router weight, gamma, the hidden row in and out
+    layer_bytes = expert_bytes + EXPERTS * HIDDEN * 2 + HIDDEN * 4 + HIDDEN * 2 * 2
     peaks = measured_peaks()
-    achieved = expert_bytes / (expert_ms / 1000.0) / 1e9
+    achieved = layer_bytes / (layer_ms / 1000.0) / 1e9
     traffic = committed_traffic()
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
@@ -306,15 +307,14 @@ def run_ours(args) -> None:
         "data": "synthetic (seeded random-init weights and hidden rows)", "config": config_dict(args, world),
         "hbm_gbs_per_gpu": layer_bytes * args.layers * value / world / 1e9,
         "roofline": {
-            "kernel": "expert GEMVs (decode_up_kernel + decode_down_kernel) of one layer",
+            "kernel": "one MoE layer: routed_up_kernel (router + gate/up) + routed_down_kernel (down + combine)",
             "bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
             "frac": achieved / peaks["hbm_gbs"], "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs)",
-            "traffic": traffic, "algorithmic_bytes_per_launch": expert_bytes,
-            "launch_ms": expert_ms,
+            "traffic": traffic, "algorithmic_bytes_per_launch": layer_bytes, "launch_ms": layer_ms,
         },
         "e2e": {"value": tokens / (e2e_ms / 1000.0), "unit": "tokens/s",
                 "h2d_bytes_per_step": inputs.numel() * 2, "d2h_bytes_per_step": outputs.numel() * 2},
-        "gpu_launches": args.steps * steps_per_graph * args.layers * 3,
+        "gpu_launches": args.steps * steps_per_graph * args.layers * 2,
         "clocks": clocks.summary(),
         "setup_s": {"build": round(build_s, 1), "capture": round(capture_s, 1)},
     }

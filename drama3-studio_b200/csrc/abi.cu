@@ -330,8 +330,30 @@ int drama_b200_fp8_moe_layer(const DramaB200Fp8Bank* bank, const void* gate, con
     const int st = prepare_moe_layer(bank, gate, next_gate, gamma, eps, hidden_in, hidden_out, tokens, top_k,
                                      ids_out, weights_out, normed_out, moe_out, workspace, workspace_bytes, &m, &d);
     if (st) return st < 0 ? -1 : 0;
-    cudaError_t err = moe_router_launch(m, static_cast<cudaStream_t>(stream));
-    if (err == cudaSuccess) err = decode_experts_launch(d, static_cast<cudaStream_t>(stream));
+    cudaError_t err;
+    if (routed_layer_supported(tokens, top_k, m.hidden, m.experts)) {
+        // one hidden row: router + gate/up and down + combine, two launches
+        RoutedLayerArgs r{};
+        r.bank = d.fp8;
+        r.hidden_in = m.hidden_in;
+        r.hidden_out = m.hidden_out;
+        r.gamma = m.gamma;
+        r.gate = m.gate;
+        r.eps = m.eps;
+        r.E = m.experts;
+        r.k = top_k;
+        r.H = m.hidden;
+        r.I = m.intermediate;
+        r.ws = d.ws;
+        r.ids_out = m.ids_out;
+        r.weights_out = m.weights_out;
+        r.normed_out = m.normed_out;
+        r.moe_out = static_cast<__nv_bfloat16*>(moe_out);
+        err = routed_layer_launch(r, d.ctas / kDecodeCtasPerSm, static_cast<cudaStream_t>(stream));
+    } else {
+        err = moe_router_launch(m, static_cast<cudaStream_t>(stream));
+        if (err == cudaSuccess) err = decode_experts_launch(d, static_cast<cudaStream_t>(stream));
+    }
     if (err != cudaSuccess) return fail("MoE layer launch failed: %s", cudaGetErrorString(err));
     return 0;
 }

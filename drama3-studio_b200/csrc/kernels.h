@@ -155,4 +155,27 @@ struct MoeLayerArgs {
 };
 cudaError_t moe_router_launch(const MoeLayerArgs& m, cudaStream_t s);
 
+// ---------------------------------------------------------------------------
+// Single-row MoE layer in two launches (routed_layer.cu): router + gate/up in
+// thread-block clusters, then down + combine + residual per hidden tile.
+// ---------------------------------------------------------------------------
+constexpr int kRoutedMaxTopK = 16;
+
+struct RoutedLayerArgs {
+    DramaB200Fp8Bank bank;
+    const __nv_bfloat16* hidden_in;
+    __nv_bfloat16* hidden_out;
+    const float* gamma;
+    const __nv_bfloat16* gate;
+    float eps;
+    int E, k, H, I;
+    DecodeWorkspace ws;  // uses order[0..k) (expert ids), wts[0..k), h
+    int64_t* ids_out;
+    __nv_bfloat16* weights_out;
+    __nv_bfloat16* normed_out;
+    __nv_bfloat16* moe_out;
+};
+bool routed_layer_supported(int64_t tokens, int top_k, int hidden, int experts);
+cudaError_t routed_layer_launch(const RoutedLayerArgs& a, int sm_count, cudaStream_t s);
+
 }  // namespace drama

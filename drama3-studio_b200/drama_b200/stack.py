@@ -62,11 +62,13 @@ def moe_layer_workspace(tokens: int, top_k: int, hidden: int, intermediate: int,
 
 def moe_layer(hidden_in: Tensor, layer: MoELayer, out: Tensor, workspace: Tensor, *, top_k: int = 8,
               eps: float = 1e-6, next_gate: Tensor | None = None, trace: LayerTrace | None = None,
-              expert_events: tuple | None = None) -> Tensor:
+              layer_events: tuple | None = None) -> Tensor:
     """Enqueue one fused MoE layer on the current stream; returns ``out``.
 
-    ``expert_events=(start, end)`` records CUDA events around the expert GEMV
-    launches (the layer is then issued as its router and experts halves).
+    One hidden row runs as two launches (router + gate/up in thread-block
+    clusters, then down + combine + residual); more rows run the router,
+    expert-group and K1 kernels. ``layer_events=(start, end)`` records CUDA
+    events around the layer's launches.
     """
     if hidden_in.dtype != torch.bfloat16 or out.dtype != torch.bfloat16:
         raise ValueError("The fused MoE layer runs on bf16 hidden states")
@@ -79,21 +81,14 @@ def moe_layer(hidden_in: Tensor, layer: MoELayer, out: Tensor, workspace: Tensor
     traced = (_lib.ptr(trace.ids if trace else None), _lib.ptr(trace.weights if trace else None),
               _lib.ptr(trace.normed if trace else None))
     moe_out = _lib.ptr(trace.moe if trace else None)
-    if expert_events is None:
-        lib.check(lib.dll.drama_b200_fp8_moe_layer(
-            ctypes.byref(bank), layer.gate.data_ptr(), _lib.ptr(next_gate), layer.gamma.data_ptr(),
-            ctypes.c_float(eps), hidden_in.data_ptr(), out.data_ptr(), tokens, top_k, *traced, moe_out,
-            workspace.data_ptr(), workspace.numel(), stream))
-        return out
-    lib.check(lib.dll.drama_b200_fp8_moe_router(
+    if layer_events is not None:
+        layer_events[0].record()
+    lib.check(lib.dll.drama_b200_fp8_moe_layer(
         ctypes.byref(bank), layer.gate.data_ptr(), _lib.ptr(next_gate), layer.gamma.data_ptr(),
-        ctypes.c_float(eps), hidden_in.data_ptr(), tokens, top_k, *traced,
+        ctypes.c_float(eps), hidden_in.data_ptr(), out.data_ptr(), tokens, top_k, *traced, moe_out,
         workspace.data_ptr(), workspace.numel(), stream))
-    expert_events[0].record()
-    lib.check(lib.dll.drama_b200_fp8_moe_experts(
-        ctypes.byref(bank), hidden_in.data_ptr(), out.data_ptr(), tokens, top_k, moe_out,
-        workspace.data_ptr(), workspace.numel(), stream))
-    expert_events[1].record()
+    if layer_events is not None:
+        layer_events[1].record()
     return out
 
 
@@ -118,7 +113,7 @@ class DecodeStack:
         self.graph: torch.cuda.CUDAGraph | None = None
 
     def step(self, hidden: Tensor, out: Tensor, traces: list[LayerTrace] | None = None,
-             expert_events: list[tuple] | None = None) -> Tensor:
+             layer_events: list[tuple] | None = None) -> Tensor:
         """Enqueue one decode step: ``out = stack(hidden)``."""
         n = len(self.layers)
         src = hidden
@@ -127,7 +122,7 @@ class DecodeStack:
             nxt = self.layers[i + 1].gate if i + 1 < n else None
             moe_layer(src, layer, dst, self.workspace, top_k=self.top_k, eps=self.eps, next_gate=nxt,
                       trace=None if traces is None else traces[i],
-                      expert_events=None if expert_events is None else expert_events[i])
+                      layer_events=None if layer_events is None else layer_events[i])
             src = dst
         return out
 
@@ -136,8 +131,8 @@ class DecodeStack:
 
         ``inputs``/``outputs``: bf16 [steps, tokens, hidden]; step s reads
         inputs[s] and writes outputs[s]. Replaying the graph re-runs all steps.
-        The first ``timed_steps`` steps record CUDA events around every layer's
-        expert GEMVs (``self.expert_events[step][layer]``).
+        The first ``timed_steps`` steps record CUDA events around every
+        layer's launches (``self.layer_events[step][layer]``).
         """
         steps = inputs.shape[0]
         stream = torch.cuda.Stream(self.device)
@@ -146,20 +141,20 @@ class DecodeStack:
             self.step(inputs[0], outputs[0])  # eager warm-up (lazy module loading)
         torch.cuda.current_stream(self.device).wait_stream(stream)
         torch.cuda.synchronize(self.device)
-        self.expert_events = [[(torch.cuda.Event(enable_timing=True, external=True),
+        self.layer_events = [[(torch.cuda.Event(enable_timing=True, external=True),
                                 torch.cuda.Event(enable_timing=True, external=True))
                                for _ in self.layers] for _ in range(timed_steps)]
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, stream=stream):
             for s in range(steps):
                 self.step(inputs[s], outputs[s],
-                          expert_events=self.expert_events[s] if s < timed_steps else None)
+                          layer_events=self.layer_events[s] if s < timed_steps else None)
         self.graph = graph
         return graph
 
-    def expert_time_ms(self) -> float:
-        """Mean duration of one layer's expert GEMV launches in the last replay."""
-        times = [a.elapsed_time(b) for step in self.expert_events for a, b in step]
+    def layer_time_ms(self) -> float:
+        """Mean duration of one layer's launches in the last replay."""
+        times = [a.elapsed_time(b) for step in self.layer_events for a, b in step]
         return sum(times) / len(times)
 
 
