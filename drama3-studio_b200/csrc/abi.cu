@@ -4,6 +4,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 
 #include "common.cuh"
@@ -384,6 +385,108 @@ int drama_b200_fp8_moe_experts(const DramaB200Fp8Bank* bank, const void* hidden_
     if (st) return st < 0 ? -1 : 0;
     const cudaError_t err = decode_experts_launch(d, static_cast<cudaStream_t>(stream));
     if (err != cudaSuccess) return fail("MoE experts launch failed: %s", cudaGetErrorString(err));
+    return 0;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// FP8 decode for callers that cannot allocate device memory.
+//
+// Some callers cannot call cudaMalloc or hand over a workspace: a host
+// binding with no device allocator of its own, or a serving process whose
+// memory manager has reserved the device for its banks and caches and allows
+// no further allocation (a cudaMalloc there would also synchronise the
+// device). This variant of drama_b200_fp8_decode keeps its scratch in the
+// array below, which every GPU that loads the library holds until the process
+// exits. Host code cannot use the array's name as a device address; the
+// address comes from cudaGetSymbolAddress, once per device.
+// ---------------------------------------------------------------------------
+constexpr size_t kStaticScratchBytes = size_t(16) << 20;  // 16 MiB
+
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+
+namespace drama {
+namespace {
+std::mutex g_static_mutex;
+void* g_static_base[64] = {nullptr};
+
+// Set-up on the first call per device (with that device current): the
+// array's device address, and one clear of the array on the caller's stream
+// (the decode scratch contract: zero before first use; every call then
+// leaves it reusable).
+int static_scratch(int dev, cudaStream_t stream, void** out) {
+    std::lock_guard<std::mutex> lock(g_static_mutex);
+    if (!g_static_base[dev]) {
+        void* ptr = nullptr;
+        cudaError_t err = cudaGetSymbolAddress(&ptr, g_static_scratch);
+        if (err != cudaSuccess) return fail("cudaGetSymbolAddress(static scratch): %s", cudaGetErrorString(err));
+        err = cudaMemsetAsync(ptr, 0, kStaticScratchBytes, stream);
+        if (err != cudaSuccess) return fail("clearing the static scratch: %s", cudaGetErrorString(err));
+        g_static_base[dev] = ptr;
+    }
+    *out = g_static_base[dev];
+    return 0;
+}
+}  // namespace
+}  // namespace drama
+
+extern "C" {
+
+size_t drama_b200_static_scratch_bytes(void) { return kStaticScratchBytes; }
+
+int drama_b200_fp8_decode_static(const DramaB200Fp8Bank* bank, const void* x, int x_dtype, int64_t tokens,
+                                 int top_k, const void* ids, int ids_dtype, const void* weights,
+                                 int weights_dtype, void* out, float* pair_out, void* stream) {
+    if (!bank) return fail("bank is required");
+    const DramaB200Fp8Bank& b = *bank;
+    if (validate_decode_common(x, x_dtype, tokens, top_k, ids, ids_dtype, weights, weights_dtype, out, pair_out,
+                               b.hidden, b.intermediate, b.slots))
+        return -1;
+    if (!b.w13 || !b.w13_scale || !b.w2 || !b.w2_scale) return fail("FP8 bank pointers are required");
+    if (!aligned16(b.w13) || !aligned16(b.w2) || b.w13_row_stride % 16 || b.w2_row_stride % 16 ||
+        b.w13_slot_stride % 16 || b.w2_slot_stride % 16)
+        return fail("FP8 weight rows must start on 16-byte boundaries");
+    if (b.w13_row_stride < b.hidden || b.w2_row_stride < b.intermediate ||
+        b.w13_slot_stride < b.w13_row_stride * 2 * b.intermediate ||
+        b.w2_slot_stride < b.w2_row_stride * b.hidden)
+        return fail("FP8 weight strides are smaller than the bank geometry");
+    if (b.w13_scale_row_stride < b.hidden / 128 || b.w2_scale_row_stride < b.intermediate / 128)
+        return fail("FP8 scale strides are smaller than the bank geometry");
+    if (tokens == 0) return 0;
+    int sms = 0;
+    if (sm_count_current(&sms)) return -1;
+    const size_t need = decode_workspace_layout(tokens, top_k, b.hidden, b.intermediate, sms, 0, nullptr, nullptr);
+    if (need > kStaticScratchBytes)
+        return fail("decode of %lld tokens x top-%d at hidden %d, intermediate %d needs %zu bytes of scratch; "
+                    "the library's static scratch holds %zu (use drama_b200_fp8_decode with a workspace)",
+                    static_cast<long long>(tokens), top_k, b.hidden, b.intermediate, need, kStaticScratchBytes);
+    int dev = 0;
+    const cudaError_t derr = cudaGetDevice(&dev);
+    if (derr != cudaSuccess) return fail("cudaGetDevice: %s", cudaGetErrorString(derr));
+    if (dev < 0 || dev >= 64) return fail("device ordinal %d out of range", dev);
+    void* base = nullptr;
+    if (static_scratch(dev, static_cast<cudaStream_t>(stream), &base)) return -1;
+    DecodeArgs a{};
+    a.format = 0;
+    a.fp8 = b;
+    a.x = x;
+    a.x_dtype = x_dtype;
+    a.tokens = tokens;
+    a.top_k = top_k;
+    a.ids = ids;
+    a.ids_dtype = ids_dtype;
+    a.weights = weights;
+    a.weights_dtype = weights_dtype;
+    a.out = out;
+    a.pair_out = pair_out;
+    a.hidden = b.hidden;
+    a.intermediate = b.intermediate;
+    a.slots = b.slots;
+    decode_workspace_layout(tokens, top_k, b.hidden, b.intermediate, sms, 0, static_cast<char*>(base), &a.ws);
+    a.ctas = sms * kDecodeCtasPerSm;
+    const cudaError_t err = decode_launch(a, static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return fail("decode launch failed: %s", cudaGetErrorString(err));
     return 0;
 }
 

@@ -41,6 +41,8 @@ EXPORTS = (
     "drama_b200_fp8_moe_layer",
     "drama_b200_fp8_moe_router",
     "drama_b200_fp8_moe_experts",
+    "drama_b200_static_scratch_bytes",
+    "drama_b200_fp8_decode_static",
 )
 
 c_void_p, c_int, c_int64, c_size_t = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_size_t
@@ -109,6 +111,9 @@ class Library:
         dll.drama_b200_fp8_moe_experts.argtypes = [
             ctypes.POINTER(Fp8Bank), c_void_p, c_void_p, c_int64, c_int, c_void_p, c_void_p, c_size_t,
             c_void_p]
+        dll.drama_b200_static_scratch_bytes.restype = c_size_t
+        dll.drama_b200_fp8_decode_static.argtypes = [ctypes.POINTER(Fp8Bank)] + decode_args[:10] + [c_void_p]
+        dll.drama_b200_fp8_decode_static.restype = c_int
         for name in ("drama_b200_device_check", "drama_b200_route_topk", "drama_b200_permute_routes",
                      "drama_b200_fp8_decode", "drama_b200_int4_decode", "drama_b200_fp8_moe_layer",
                      "drama_b200_fp8_moe_router", "drama_b200_fp8_moe_experts"):

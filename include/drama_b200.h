@@ -199,6 +199,37 @@ DRAMA_B200_API int drama_b200_fp8_moe_experts(const DramaB200Fp8Bank* bank, cons
  * with drama_b200_decode_status_offset() bytes into the workspace. */
 DRAMA_B200_API size_t drama_b200_decode_status_offset(void);
 
+/* ---------------------------------------------------------------------------
+ * FP8 decode without a workspace, for callers that cannot allocate device
+ * memory: a host binding with no device allocator of its own, or a process
+ * whose memory manager has reserved the device and permits no further
+ * allocation (cudaMalloc would also synchronise the device). This entry point
+ * has no counterpart in the reference; the reference always allocates its
+ * outputs and scratch through PyTorch.
+ *
+ * Same arguments and results as drama_b200_fp8_decode minus the workspace.
+ * Its scratch is a static device array of drama_b200_static_scratch_bytes()
+ * (16 MiB) inside the library, held on every GPU that loads the library until
+ * the process exits. A call whose scratch need, drama_b200_decode_workspace_
+ * bytes() for the same sizes, exceeds that fails with a message naming both
+ * sizes; on a 148-SM B200 at top-8 that is above 94 tokens at hidden 2048 /
+ * intermediate 768 and above 43 tokens at hidden 4096 / intermediate 2048.
+ * The call allocates nothing.
+ *
+ * The first call on a device (with that device current) looks up the array's
+ * device address and clears the array on the caller's stream; make that first
+ * call before any stream capture. Every call, from any thread, shares the
+ * one array and leaves it reusable, so calls that can overlap on the GPU
+ * (different streams without ordering between them) race; order them.
+ * ------------------------------------------------------------------------- */
+DRAMA_B200_API size_t drama_b200_static_scratch_bytes(void);
+
+DRAMA_B200_API int drama_b200_fp8_decode_static(const DramaB200Fp8Bank* bank, const void* x,
+                                                int x_dtype, int64_t tokens, int top_k,
+                                                const void* ids, int ids_dtype,
+                                                const void* weights, int weights_dtype,
+                                                void* out, float* pair_out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
