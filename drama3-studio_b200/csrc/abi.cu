@@ -332,7 +332,7 @@ int drama_b200_fp8_moe_layer(const DramaB200Fp8Bank* bank, const void* gate, con
                                      ids_out, weights_out, normed_out, moe_out, workspace, workspace_bytes, &m, &d);
     if (st) return st < 0 ? -1 : 0;
     cudaError_t err;
-    if (routed_layer_supported(tokens, top_k, m.hidden, m.experts)) {
+    if (routed_layer_supported(tokens, top_k, m.hidden, m.intermediate, m.experts)) {
         // one hidden row: router + gate/up and down + combine, two launches
         RoutedLayerArgs r{};
         r.bank = d.fp8;

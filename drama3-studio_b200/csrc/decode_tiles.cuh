@@ -303,6 +303,30 @@ __device__ __forceinline__ void up_issue(uint32_t dst, const DecodeArgs& a, int 
     }
 }
 
+// FP8 gate/up cell with its two 128x128 block scales already in hand (gate
+// rows' scale sg, up rows' scale su): 16 rows x 128 K of each projection
+// against the B fragments xb, block sums scaled and added to tot in fp32.
+__device__ __forceinline__ void up_mma_fp8_scaled(const uint4 (&q)[8], float sg, float su, const uint32_t (&xb)[16],
+                                                  float (&tot)[8]) {
+    float ag[4] = {0.f, 0.f, 0.f, 0.f}, au[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int s = 0; s < 8; ++s) {
+        const int qi = s >> 2, ci = s & 3;
+        uint32_t A[4], B[4];
+        e4m3x4_to_f16x2x2(comp(q[qi], ci), A[0], A[2]);
+        e4m3x4_to_f16x2x2(comp(q[2 + qi], ci), A[1], A[3]);
+        mma_f16_16816(ag, A, xb[2 * s], xb[2 * s + 1]);
+        e4m3x4_to_f16x2x2(comp(q[4 + qi], ci), B[0], B[2]);
+        e4m3x4_to_f16x2x2(comp(q[6 + qi], ci), B[1], B[3]);
+        mma_f16_16816(au, B, xb[2 * s], xb[2 * s + 1]);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        tot[i] = fmaf(ag[i], sg, tot[i]);
+        tot[4 + i] = fmaf(au[i], su, tot[4 + i]);
+    }
+}
+
 template <int FMT>
 __device__ __forceinline__ void up_mma(const uint4 (&q)[UpShape<FMT>::NCH], const DecodeArgs& a, int slot,
                                        const CellIt& it, int g, const uint32_t (&xb)[16], float (&tot)[8]) {
@@ -313,22 +337,7 @@ __device__ __forceinline__ void up_mma(const uint4 (&q)[UpShape<FMT>::NCH], cons
         const float* sp = b.w13_scale + slot * b.w13_scale_slot_stride + it.kb;
         const float sg = __ldg(sp + ((it.jt * 16) >> 7) * b.w13_scale_row_stride);
         const float su = __ldg(sp + ((I + it.jt * 16) >> 7) * b.w13_scale_row_stride);
-#pragma unroll
-        for (int s = 0; s < 8; ++s) {
-            const int qi = s >> 2, ci = s & 3;
-            uint32_t A[4], B[4];
-            e4m3x4_to_f16x2x2(comp(q[qi], ci), A[0], A[2]);
-            e4m3x4_to_f16x2x2(comp(q[2 + qi], ci), A[1], A[3]);
-            mma_f16_16816(ag, A, xb[2 * s], xb[2 * s + 1]);
-            e4m3x4_to_f16x2x2(comp(q[4 + qi], ci), B[0], B[2]);
-            e4m3x4_to_f16x2x2(comp(q[6 + qi], ci), B[1], B[3]);
-            mma_f16_16816(au, B, xb[2 * s], xb[2 * s + 1]);
-        }
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            tot[i] = fmaf(ag[i], sg, tot[i]);
-            tot[4 + i] = fmaf(au[i], su, tot[4 + i]);
-        }
+        up_mma_fp8_scaled(q, sg, su, xb, tot);
     } else {
         const DramaB200Int4Bank& b = a.int4;
         const int rows[4] = {it.jt * 16 + g, it.jt * 16 + g + 8, I + it.jt * 16 + g, I + it.jt * 16 + g + 8};
@@ -504,9 +513,13 @@ __device__ __forceinline__ int dn_fragment(const uint4* hq, uint32_t (&hb)[16]) 
             }
         }
     }
-    float m = 0.0f;
+    // max |v| as a tree (max is exact in any order)
+    float mx[8];
 #pragma unroll
-    for (int j = 0; j < 32; ++j) m = fmaxf(m, fabsf(v[j]));
+    for (int j = 0; j < 8; ++j) mx[j] = fmaxf(fmaxf(fabsf(v[j]), fabsf(v[j + 8])), fmaxf(fabsf(v[j + 16]), fabsf(v[j + 24])));
+#pragma unroll
+    for (int j = 0; j < 4; ++j) mx[j] = fmaxf(mx[j], mx[j + 4]);
+    float m = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
     m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
     m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
     const int e = f16_exponent_for(m);
@@ -523,6 +536,54 @@ __device__ __forceinline__ int dn_fragment(const uint4* hq, uint32_t (&hb)[16]) 
     return e;
 }
 
+// FP8 down-projection block: 16 rows x 128 K against the activation
+// fragments hb, scaled by the weight block scale sb and the activation
+// columns' powers of two s0 / s1, added to tot in fp32. `ad` is zero scratch.
+__device__ __forceinline__ void dn_mma_fp8_block(const uint4* wq, float sb, float s0, float s1,
+                                                 const uint32_t (&hb)[16], float (&ad)[4], float (&tot)[4]) {
+#pragma unroll
+    for (int s = 0; s < 8; ++s) {
+        const int qi = s >> 2, ci = s & 3;
+        uint32_t A[4];
+        e4m3x4_to_f16x2x2(comp(wq[qi], ci), A[0], A[2]);
+        e4m3x4_to_f16x2x2(comp(wq[2 + qi], ci), A[1], A[3]);
+        mma_f16_16816(ad, A, hb[2 * s], hb[2 * s + 1]);
+    }
+    tot[0] = fmaf(ad[0], sb * s0, tot[0]);
+    tot[1] = fmaf(ad[1], sb * s1, tot[1]);
+    tot[2] = fmaf(ad[2], sb * s0, tot[2]);
+    tot[3] = fmaf(ad[3], sb * s1, tot[3]);
+}
+
+// The same block with the 8 MMAs in two independent chains (k steps 0-3 and
+// 4-7, summed before scaling): shorter latency when one warp owns a whole
+// K range.
+__device__ __forceinline__ void dn_mma_fp8_block2(const uint4* wq, float sb, float s0, float s1,
+                                                  const uint32_t (&hb)[16], float (&tot)[4]) {
+    float a0[4] = {0.f, 0.f, 0.f, 0.f}, a1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+        uint32_t A[4], B[4];
+        e4m3x4_to_f16x2x2(comp(wq[0], s), A[0], A[2]);
+        e4m3x4_to_f16x2x2(comp(wq[2], s), A[1], A[3]);
+        mma_f16_16816(a0, A, hb[2 * s], hb[2 * s + 1]);
+        e4m3x4_to_f16x2x2(comp(wq[1], s), B[0], B[2]);
+        e4m3x4_to_f16x2x2(comp(wq[3], s), B[1], B[3]);
+        mma_f16_16816(a1, B, hb[2 * (s + 4)], hb[2 * (s + 4) + 1]);
+    }
+    tot[0] = fmaf(a0[0] + a1[0], sb * s0, tot[0]);
+    tot[1] = fmaf(a0[1] + a1[1], sb * s1, tot[1]);
+    tot[2] = fmaf(a0[2] + a1[2], sb * s0, tot[2]);
+    tot[3] = fmaf(a0[3] + a1[3], sb * s1, tot[3]);
+}
+
+// Power-of-two scales of the activation columns 2t and 2t + 1 (their
+// exponents e are held by lanes 8t and 8t + 4).
+__device__ __forceinline__ void column_scales(int e, int t, float& s0, float& s1) {
+    s0 = ldexpf(1.0f, __shfl_sync(0xffffffffu, e, 8 * t));
+    s1 = ldexpf(1.0f, __shfl_sync(0xffffffffu, e, 8 * t + 4));
+}
+
 template <int FMT>
 __device__ __forceinline__ void dn_mma(const uint4* wq, const DecodeArgs& a, int slot, const CellIt& it, int g, int t,
                                        const uint32_t (&hb)[16], int e, float (&tot)[4]) {
@@ -534,18 +595,7 @@ __device__ __forceinline__ void dn_mma(const uint4* wq, const DecodeArgs& a, int
         const DramaB200Fp8Bank& b = a.fp8;
         const float sb =
             __ldg(b.w2_scale + slot * b.w2_scale_slot_stride + ((it.jt * 16) >> 7) * b.w2_scale_row_stride + it.kb);
-#pragma unroll
-        for (int s = 0; s < 8; ++s) {
-            const int qi = s >> 2, ci = s & 3;
-            uint32_t A[4];
-            e4m3x4_to_f16x2x2(comp(wq[qi], ci), A[0], A[2]);
-            e4m3x4_to_f16x2x2(comp(wq[2 + qi], ci), A[1], A[3]);
-            mma_f16_16816(ad, A, hb[2 * s], hb[2 * s + 1]);
-        }
-        tot[0] = fmaf(ad[0], sb * s0, tot[0]);
-        tot[1] = fmaf(ad[1], sb * s1, tot[1]);
-        tot[2] = fmaf(ad[2], sb * s0, tot[2]);
-        tot[3] = fmaf(ad[3], sb * s1, tot[3]);
+        dn_mma_fp8_block(wq, sb, s0, s1, hb, ad, tot);
     } else {
         const DramaB200Int4Bank& b = a.int4;
         const int rows[2] = {it.jt * 16 + g, it.jt * 16 + g + 8};

@@ -175,7 +175,7 @@ struct RoutedLayerArgs {
     __nv_bfloat16* normed_out;
     __nv_bfloat16* moe_out;
 };
-bool routed_layer_supported(int64_t tokens, int top_k, int hidden, int experts);
+bool routed_layer_supported(int64_t tokens, int top_k, int hidden, int intermediate, int experts);
 cudaError_t routed_layer_launch(const RoutedLayerArgs& a, int sm_count, cudaStream_t s);
 
 }  // namespace drama

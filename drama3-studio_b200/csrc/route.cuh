@@ -6,6 +6,50 @@
 
 namespace drama {
 
+// Sort + renormalise the k candidates that the selection left in s_key /
+// s_idx (gatherTopK order) exactly as torch's CUDA topk(sorted=True) and the
+// renormalisation do. Called by a whole warp; lanes 0..k-1 get the result.
+__device__ __forceinline__ void route_finish(int k, bool renormalize, int lane, const float* s_key, const int* s_idx,
+                                             int& out_idx, float& out_w) {
+    constexpr unsigned kFull = 0xffffffffu;
+    float key = lane < k ? s_key[lane] : 0.0f;
+    int idx = lane < k ? s_idx[lane] : 0;
+    bool valid = lane < k;
+    // 32-slot bitonic network (lane = slot); pair (l, l ^ stride).
+    auto stage = [&](int stride, bool flag) {
+        const float pk = __shfl_xor_sync(kFull, key, stride);
+        const int pi = __shfl_xor_sync(kFull, idx, stride);
+        const bool pv = __shfl_xor_sync(kFull, valid, stride);
+        const bool is_a = (lane & stride) == 0;
+        const float ka = is_a ? key : pk, kb = is_a ? pk : key;
+        const bool va = is_a ? valid : pv, vb = is_a ? pv : valid;
+        const bool swap = ((ka > kb) && va) || !vb;
+        if (swap == flag) {
+            key = pk;
+            idx = pi;
+            valid = pv;
+        }
+    };
+#pragma unroll
+    for (int size = 2; size < 32; size <<= 1) {
+#pragma unroll
+        for (int stride = size >> 1; stride > 0; stride >>= 1)
+            stage(stride, (((lane / (2 * stride)) * stride + (lane % stride)) & (size >> 1)) != 0);
+    }
+#pragma unroll
+    for (int stride = 16; stride > 0; stride >>= 1) stage(stride, false);
+    float w = valid ? key : 0.0f;
+    if (renormalize) {
+        int p2 = 1;
+        while (p2 < k) p2 <<= 1;
+        float tsum = lane < k ? key : 0.0f;
+        for (int off = 1; off < p2; off <<= 1) tsum = tsum + __shfl_down_sync(kFull, tsum, off);
+        w = w / __shfl_sync(kFull, tsum, 0);
+    }
+    out_idx = idx;
+    out_w = w;
+}
+
 // LANES lanes x ITERS values cover next_pow2(E). `load(idx)` returns the fp32
 // logit idx (< E). On return lanes 0..k-1 hold (index, weight) of the k routes
 // in torch's topk order; `s_key`/`s_idx` are 32-entry per-warp scratch.
@@ -88,42 +132,126 @@ __device__ __forceinline__ void route_row(Load load, int E, int k, bool renormal
         base += __popc(b);
     }
     __syncwarp();
-    float key = lane < k ? s_key[lane] : 0.0f;
-    int idx = lane < k ? s_idx[lane] : 0;
-    bool valid = lane < k;
-    // 32-slot bitonic network (lane = slot); pair (l, l ^ stride).
-    auto stage = [&](int stride, bool flag) {
-        const float pk = __shfl_xor_sync(kFull, key, stride);
-        const int pi = __shfl_xor_sync(kFull, idx, stride);
-        const bool pv = __shfl_xor_sync(kFull, valid, stride);
-        const bool is_a = (lane & stride) == 0;
-        const float ka = is_a ? key : pk, kb = is_a ? pk : key;
-        const bool va = is_a ? valid : pv, vb = is_a ? pv : valid;
-        const bool swap = ((ka > kb) && va) || !vb;
-        if (swap == flag) {
-            key = pk;
-            idx = pi;
-            valid = pv;
+    route_finish(k, renormalize, lane, s_key, s_idx, out_idx, out_w);
+}
+
+// Softmax of one row, by one warp, in route_row's arithmetic order; writes
+// p[e] for e < E to `probs` (shared memory).
+template <int LANES, int ITERS, typename Load>
+__device__ __forceinline__ void route_softmax(Load load, int E, int lane, float* probs) {
+    constexpr unsigned kFull = 0xffffffffu;
+    float v[ITERS];
+#pragma unroll
+    for (int i = 0; i < ITERS; ++i) {
+        const int idx = lane + i * LANES;
+        v[i] = (lane < LANES && idx < E) ? load(idx) : -INFINITY;
+    }
+    float m = v[0];
+#pragma unroll
+    for (int i = 1; i < ITERS; ++i) m = fmaxf(m, v[i]);
+#pragma unroll
+    for (int off = LANES / 2; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(kFull, m, off));
+    float sum = 0.0f;
+#pragma unroll
+    for (int i = 0; i < ITERS; ++i) {
+        v[i] = expf(v[i] - m);
+        sum += v[i];
+    }
+#pragma unroll
+    for (int off = LANES / 2; off > 0; off >>= 1) sum = sum + __shfl_xor_sync(kFull, sum, off);
+#pragma unroll
+    for (int i = 0; i < ITERS; ++i) {
+        const int idx = lane + i * LANES;
+        if (lane < LANES && idx < E) probs[idx] = v[i] / sum;
+    }
+}
+
+// Top-k of the probabilities by rank, over all threads of the CTA: element e
+// is chosen when fewer than k elements rank before it (greater, or equal with
+// a smaller index), and the chosen ones are placed in gatherTopK order
+// (greater than the k-th value in index order, then equal ones in index
+// order) in s_key / s_idx[0..k) - the same candidates and slots as
+// route_row's selection rounds. `probs` holds E values >= 0 and has room for
+// E rounded up to 4 (the padding is set to -1 here); s_cnt is scratch for
+// one int per warp plus one float. Contains __syncthreads(): call from every
+// thread of the CTA (blockDim.x a multiple of 32, at most 1024).
+__device__ __forceinline__ void route_select_cta(float* probs, int E, int k, float* s_key, int* s_idx, int* s_cnt) {
+    const int E4 = (E + 3) & ~3;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, warps = blockDim.x >> 5;
+    float* s_kth = reinterpret_cast<float*>(s_cnt + 32);
+    if (tid < E4 - E) probs[E + tid] = -1.0f;
+    __syncthreads();
+    const float4* p4 = reinterpret_cast<const float4*>(probs);
+    // rank of element e: threads 2e' and 2e' + 1 scan the two halves of the
+    // index range and add their counts
+    const int n4 = E4 / 4, h4 = (n4 + 1) / 2;
+    for (int base = 0; base < E; base += static_cast<int>(blockDim.x) / 2) {
+        const int e = base + (tid >> 1), half = tid & 1;
+        const float pe = e < E ? probs[e] : 0.0f;
+        int r = 0;
+        if (e < E) {
+            const int j4_end = half ? n4 : h4;
+#pragma unroll 4
+            for (int j4 = half ? h4 : 0; j4 < j4_end; ++j4) {
+                const float4 q = p4[j4];
+                const int j = 4 * j4;
+                r += (q.x > pe) || (q.x == pe && j < e);
+                r += (q.y > pe) || (q.y == pe && j + 1 < e);
+                r += (q.z > pe) || (q.z == pe && j + 2 < e);
+                r += (q.w > pe) || (q.w == pe && j + 3 < e);
+            }
         }
-    };
-#pragma unroll
-    for (int size = 2; size < 32; size <<= 1) {
-#pragma unroll
-        for (int stride = size >> 1; stride > 0; stride >>= 1)
-            stage(stride, (((lane / (2 * stride)) * stride + (lane % stride)) & (size >> 1)) != 0);
+        r += __shfl_xor_sync(0xffffffffu, r, 1);
+        if (e < E && half == 0 && r == k - 1) *s_kth = pe;
     }
+    __syncthreads();
+    const float kth = *s_kth;
+    // Slots: an exclusive prefix count, in index order, of the elements above
+    // kth and of those equal to it (warp ballots, then the warps' totals).
+    int base_gt = 0, base_eq = 0, total_gt = 0;
+    {
+        // total number of elements above kth (every thread needs it)
+        int c = 0;
+        for (int e = lane; e < E; e += 32) c += probs[e] > kth;
 #pragma unroll
-    for (int stride = 16; stride > 0; stride >>= 1) stage(stride, false);
-    float w = valid ? key : 0.0f;
-    if (renormalize) {
-        int p2 = 1;
-        while (p2 < k) p2 <<= 1;
-        float tsum = lane < k ? key : 0.0f;
-        for (int off = 1; off < p2; off <<= 1) tsum = tsum + __shfl_down_sync(kFull, tsum, off);
-        w = w / __shfl_sync(kFull, tsum, 0);
+        for (int off = 16; off > 0; off >>= 1) c += __shfl_xor_sync(0xffffffffu, c, off);
+        total_gt = c;
     }
-    out_idx = idx;
-    out_w = w;
+    const unsigned below = (1u << lane) - 1u;
+    for (int e0 = 0; e0 < E; e0 += blockDim.x) {
+        const int e = e0 + tid;
+        const float pe = e < E ? probs[e] : -1.0f;
+        const unsigned bg = __ballot_sync(0xffffffffu, pe > kth);
+        const unsigned be = __ballot_sync(0xffffffffu, pe == kth);
+        if (lane == 0) {
+            s_cnt[warp] = __popc(bg);
+            s_cnt[16 + warp] = __popc(be);
+        }
+        __syncthreads();
+        int pre_gt = base_gt, pre_eq = base_eq, all_gt = 0, all_eq = 0;
+        for (int w = 0; w < warps; ++w) {
+            if (w < warp) {
+                pre_gt += s_cnt[w];
+                pre_eq += s_cnt[16 + w];
+            }
+            all_gt += s_cnt[w];
+            all_eq += s_cnt[16 + w];
+        }
+        if (pe > kth) {
+            const int pos = pre_gt + __popc(bg & below);
+            s_key[pos] = pe;
+            s_idx[pos] = e;
+        } else if (pe == kth) {
+            const int pos = total_gt + pre_eq + __popc(be & below);
+            if (pos < k) {
+                s_key[pos] = pe;
+                s_idx[pos] = e;
+            }
+        }
+        base_gt += all_gt;
+        base_eq += all_eq;
+        __syncthreads();
+    }
 }
 
 // Calls f.template operator()<LANES, ITERS>() for next_pow2(experts) <= 1024.
