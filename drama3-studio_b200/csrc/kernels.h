@@ -156,6 +156,23 @@ struct MoeLayerArgs {
 cudaError_t moe_router_launch(const MoeLayerArgs& m, cudaStream_t s);
 
 // ---------------------------------------------------------------------------
+// Prefill (K2, prefill_gemm.cu): permute + grouped tensor-core GEMMs + combine.
+// ---------------------------------------------------------------------------
+struct PrefillWorkspace {
+    int32_t* status;          // [4]: [0] pairs dropped for an out-of-range id
+    int64_t* order;           // [P] pairs sorted by expert (stable)
+    int64_t* counts;          // [E]
+    int64_t* offsets;         // [E + 1]
+    __nv_bfloat16* h;         // [P][I] SwiGLU activations in sorted order
+    __nv_bfloat16* down;      // [P][H] bf16 down projections by pair
+};
+size_t prefill_workspace_layout(int64_t tokens, int top_k, int hidden, int intermediate, int experts, char* base,
+                                PrefillWorkspace* ws);
+cudaError_t prefill_launch(const DramaB200Fp8Bank& bank, const void* x, int64_t tokens, int top_k, const void* ids,
+                           int ids_dtype, const void* weights, int weights_dtype, void* out,
+                           const PrefillWorkspace& ws, int sm_count, cudaStream_t s);
+
+// ---------------------------------------------------------------------------
 // Single-row MoE layer in two launches (routed_layer.cu): router + gate/up in
 // thread-block clusters, then down + combine + residual per hidden tile.
 // ---------------------------------------------------------------------------

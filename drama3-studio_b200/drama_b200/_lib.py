@@ -41,6 +41,9 @@ EXPORTS = (
     "drama_b200_fp8_moe_layer",
     "drama_b200_fp8_moe_router",
     "drama_b200_fp8_moe_experts",
+    "drama_b200_prefill_workspace_bytes",
+    "drama_b200_prefill_status_offset",
+    "drama_b200_fp8_prefill",
     "drama_b200_static_scratch_bytes",
     "drama_b200_fp8_decode_static",
 )
@@ -111,6 +114,12 @@ class Library:
         dll.drama_b200_fp8_moe_experts.argtypes = [
             ctypes.POINTER(Fp8Bank), c_void_p, c_void_p, c_int64, c_int, c_void_p, c_void_p, c_size_t,
             c_void_p]
+        dll.drama_b200_prefill_workspace_bytes.argtypes = [c_int64, c_int, c_int, c_int, c_int]
+        dll.drama_b200_prefill_workspace_bytes.restype = c_size_t
+        dll.drama_b200_prefill_status_offset.restype = c_size_t
+        dll.drama_b200_fp8_prefill.argtypes = [ctypes.POINTER(Fp8Bank), c_void_p, c_int64, c_int, c_void_p, c_int,
+                                               c_void_p, c_int, c_void_p, c_void_p, c_size_t, c_void_p]
+        dll.drama_b200_fp8_prefill.restype = c_int
         dll.drama_b200_static_scratch_bytes.restype = c_size_t
         dll.drama_b200_fp8_decode_static.argtypes = [ctypes.POINTER(Fp8Bank)] + decode_args[:10] + [c_void_p]
         dll.drama_b200_fp8_decode_static.restype = c_int

@@ -29,6 +29,7 @@ from . import _lib
 FP8_DTYPE = torch.float8_e4m3fn
 FLOAT_DTYPES = (torch.float16, torch.bfloat16, torch.float32)
 MAX_DECODE_PAIRS = 4096
+PREFILL_MIN_PAIRS = 512  # below this the decode GEMVs are faster than a tensor-core tile
 
 
 @dataclass(frozen=True)
@@ -76,6 +77,7 @@ class _Workspace:
 
 
 _WORKSPACES = _Workspace()
+_PREFILL_WORKSPACES = _Workspace()
 
 
 def _rows(t: Tensor) -> Tensor:
@@ -239,12 +241,62 @@ class _DecodeBackend:
 
 
 class B200ExpertBackend(_DecodeBackend):
-    """FP8 (E4M3, 128x128 block scales) experts; TorchExpertBackend arithmetic."""
+    """FP8 (E4M3, 128x128 block scales) experts; TorchExpertBackend arithmetic.
+
+    ``forward`` on bf16 rows with at least ``prefill_min_pairs`` (token, slot)
+    pairs runs the grouped tensor-core GEMMs (``fp8_prefill``); smaller calls and
+    ``forward_pairs`` run the decode GEMV kernels.
+    """
 
     entry = "drama_b200_fp8_decode"
 
+    def __init__(self, *, validate_ids: bool = True, prefill_min_pairs: int = PREFILL_MIN_PAIRS) -> None:
+        super().__init__(validate_ids=validate_ids)
+        self.prefill_min_pairs = prefill_min_pairs
+
     def _bank(self, staged, hidden):
         return _fp8_bank(staged, hidden)
+
+    def forward(self, x: Tensor, ids: Tensor, weights: Tensor, staged) -> Tensor:
+        if (x.dtype == torch.bfloat16 and ids.ndim == 2 and ids.shape[0] == x.shape[0] and x.ndim == 2
+                and ids.numel() >= self.prefill_min_pairs and x.shape[1] % 256 == 0
+                and staged.w2_weight.shape[-1] % 128 == 0):
+            if weights.shape != ids.shape:
+                raise ValueError("Routing weights must match IDs and top_k must be positive")
+            return fp8_prefill(x, ids, weights, staged, validate_ids=self.validate_ids)
+        return super().forward(x, ids, weights, staged)
+
+
+def fp8_prefill(x: Tensor, ids: Tensor, weights: Tensor, staged, *, validate_ids: bool = True) -> Tensor:
+    """Many-token FP8 expert forward on the grouped tensor-core GEMMs.
+
+    Same result contract as ``TorchExpertBackend.forward`` (offload.py:202-213):
+    bf16 ``x [T,H]``, local slot ``ids [T,k]``, ``weights [T,k]``; returns bf16
+    ``[T,H]`` with route slots summed in slot order in fp32.
+    """
+    if x.dtype != torch.bfloat16:
+        raise ValueError("fp8_prefill runs on bf16 hidden rows")
+    hidden = x.shape[-1]
+    bank, keep = _fp8_bank(staged, hidden)
+    _check_common(x, ids, weights, bank.slots, hidden, validate_ids)
+    tokens, top_k = ids.shape
+    x = x.contiguous()
+    ids = ids.contiguous()
+    weights = weights.contiguous()
+    if weights.dtype not in FLOAT_DTYPES:
+        weights = weights.float()
+    out = torch.empty_like(x)
+    if tokens == 0:
+        return out
+    lib = _lib.library()
+    nbytes = lib.dll.drama_b200_prefill_workspace_bytes(tokens, top_k, hidden, bank.intermediate, bank.slots)
+    ws = _PREFILL_WORKSPACES.get(x.device, nbytes)
+    lib.check(lib.dll.drama_b200_fp8_prefill(
+        ctypes.byref(bank), x.data_ptr(), tokens, top_k, ids.data_ptr(), _lib.DTYPE_CODES[ids.dtype],
+        weights.data_ptr(), _lib.DTYPE_CODES[weights.dtype], out.data_ptr(), ws.data_ptr(), ws.numel(),
+        _lib.stream_handle(x.device)))
+    del keep
+    return out
 
 
 class QuantizedB200Backend(_DecodeBackend):

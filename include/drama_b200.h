@@ -200,6 +200,30 @@ DRAMA_B200_API int drama_b200_fp8_moe_experts(const DramaB200Fp8Bank* bank, cons
 DRAMA_B200_API size_t drama_b200_decode_status_offset(void);
 
 /* ---------------------------------------------------------------------------
+ * K2 prefill: the same layer math as drama_b200_fp8_decode for many tokens,
+ * as grouped tensor-core GEMMs over experts. Replaces ExpertBackend.forward
+ * (src/drama_low_vram/offload.py:187-196) as TorchExpertBackend computes it
+ * (offload.py:199-244): W = bf16(fp8 * block scale) (offload.py:44-56),
+ *   gu = bf16(x @ W13^T); h = bf16(bf16(silu(gate)) * up);
+ *   down = bf16(h @ W2^T); out[t] = bf16(sum over slots, in slot order, of
+ *   down[t*k+s] * weight[t*k+s])   (fp32 sum).
+ * x, out: bf16 [tokens, H] (must not overlap); ids: [tokens, top_k] I32/I64
+ * local slots; weights: [tokens, top_k] F32/F16/BF16. H % 256 == 0,
+ * I % 128 == 0, slots <= 1024, pairs <= 2^24. A pair whose id is outside
+ * [0, slots) contributes zero and is counted in status word 0
+ * (drama_b200_prefill_status_offset() bytes into the workspace).
+ * ------------------------------------------------------------------------- */
+DRAMA_B200_API size_t drama_b200_prefill_workspace_bytes(int64_t tokens, int top_k, int hidden,
+                                                         int intermediate, int experts);
+
+DRAMA_B200_API size_t drama_b200_prefill_status_offset(void);
+
+DRAMA_B200_API int drama_b200_fp8_prefill(const DramaB200Fp8Bank* bank, const void* x, int64_t tokens,
+                                          int top_k, const void* ids, int ids_dtype,
+                                          const void* weights, int weights_dtype, void* out,
+                                          void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
  * FP8 decode without a workspace, for callers that cannot allocate device
  * memory: a host binding with no device allocator of its own, or a process
  * whose memory manager has reserved the device and permits no further

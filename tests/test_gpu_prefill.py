@@ -1,0 +1,101 @@
+"""K2 prefill grouped tensor-core GEMMs against the dequant-path oracle.
+
+The prefill path computes TorchExpertBackend's W16A16 arithmetic with the
+weights dequantised to bf16 (offload.py:44-56, 199-244), so small cases are
+held to the oracle at the 2e-2 bar; the config-3 shape (4096 tokens, Zipf
+routes) is held to the decode kernels, which compute the same layer with
+exact FP8 values, at the same bar.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from helpers import assert_parity, np_bank, np_f32
+from oracle import restate as R
+
+pytestmark = pytest.mark.gpu
+
+
+class _Staged:
+    def __init__(self, bank):
+        self.w13_weight = bank["w13_weight"]
+        self.w13_scale_inv = bank["w13_scale_inv"]
+        self.w2_weight = bank["w2_weight"]
+        self.w2_scale_inv = bank["w2_scale_inv"]
+
+
+def _case(device, tokens, top_k, experts, hidden, inter, seed, zipf=False):
+    from drama_b200 import synthetic
+
+    bank = synthetic.fp8_bank(experts, hidden, inter, seed, device=device, chunk=experts)
+    routes = synthetic.zipf_routes if zipf else synthetic.uniform_routes
+    ids, w = routes(tokens, top_k, experts, seed + 1, device=device)
+    x = synthetic.hidden_states(tokens, hidden, seed + 2, device=device)
+    return bank, x, ids.to(torch.int64).contiguous(), w.to(torch.bfloat16).contiguous()
+
+
+@pytest.mark.parametrize("tokens,top_k,experts,hidden,inter,zipf",
+                         [(96, 4, 8, 256, 128, False), (300, 8, 16, 512, 256, True), (40, 2, 4, 256, 384, False)])
+def test_prefill_matches_dequant_oracle(cuda_device, tokens, top_k, experts, hidden, inter, zipf):
+    from drama_b200.backend import fp8_prefill
+
+    bank, x, ids, w = _case(cuda_device, tokens, top_k, experts, hidden, inter, seed=tokens, zipf=zipf)
+    out = fp8_prefill(x, ids, w, _Staged(bank))
+    torch.cuda.synchronize()
+    ref = R.fp8_dequant_forward(np_f32(x), ids.cpu().numpy(), np_f32(w), np_bank(bank), "bfloat16")
+    assert_parity(np_f32(out), ref, label=f"prefill T={tokens} k={top_k} E={experts} {hidden}x{inter}")
+    # same inputs, second call on the same workspace: identical bits
+    again = fp8_prefill(x, ids, w, _Staged(bank))
+    torch.cuda.synchronize()
+    assert torch.equal(out.view(torch.int16), again.view(torch.int16))
+
+
+def test_prefill_config3_matches_decode_kernels(cuda_device):
+    """4096 tokens, top-8 of 128 experts, Zipf(1.1): tensor-core path vs GEMV path."""
+    from drama_b200.backend import B200ExpertBackend, fp8_prefill
+
+    bank, x, ids, w = _case(cuda_device, 4096, 8, 128, 2048, 768, seed=7, zipf=True)
+    staged = _Staged(bank)
+    out = fp8_prefill(x, ids, w, staged)
+    gemv = B200ExpertBackend(prefill_min_pairs=1 << 30).forward(x, ids, w, staged)
+    torch.cuda.synchronize()
+    assert_parity(np_f32(out), np_f32(gemv), label="prefill vs decode kernels, config 3")
+    # a few rows against the oracle directly
+    rows = [0, 1, 2047, 4095]
+    ref = R.fp8_dequant_forward(np_f32(x[rows]), ids[rows].cpu().numpy(), np_f32(w[rows]), np_bank(bank), "bfloat16")
+    assert_parity(np_f32(out[rows]), ref, label="prefill config 3, oracle rows")
+
+
+def test_prefill_out_of_range_ids_contribute_zero(cuda_device):
+    from drama_b200 import _lib
+
+    bank, x, ids, w = _case(cuda_device, 64, 4, 8, 256, 128, seed=5)
+    ids_bad = ids.clone()
+    ids_bad[3, 1] = 99
+    ids_bad[10, 0] = -1
+    lib = _lib.library()
+    from drama_b200.backend import _fp8_bank
+
+    fp8, keep = _fp8_bank(_Staged(bank), 256)
+    nbytes = lib.dll.drama_b200_prefill_workspace_bytes(64, 4, 256, 128, 8)
+    ws = torch.zeros(nbytes, dtype=torch.uint8, device=cuda_device)
+    out = torch.empty_like(x)
+    lib.check(lib.dll.drama_b200_fp8_prefill(
+        ctypes.byref(fp8), x.data_ptr(), 64, 4, ids_bad.data_ptr(), _lib.I64, w.data_ptr(), _lib.BF16,
+        out.data_ptr(), ws.data_ptr(), ws.numel(), _lib.stream_handle(x.device)))
+    torch.cuda.synchronize()
+    off = lib.dll.drama_b200_prefill_status_offset()
+    status = ws[off:off + 8].view(torch.int32).cpu().tolist()
+    assert status == [2, 0]
+    w_zeroed = w.clone()
+    w_zeroed[3, 1] = 0
+    w_zeroed[10, 0] = 0
+    ids_ok = ids_bad.clamp(0, 7)
+    ref = R.fp8_dequant_forward(np_f32(x), ids_ok.cpu().numpy(), np_f32(w_zeroed), np_bank(bank), "bfloat16")
+    assert_parity(np_f32(out), ref, label="prefill with dropped pairs")
+    del keep
