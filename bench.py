@@ -44,6 +44,8 @@ def parse_args():
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--layers", type=int, default=48)
     p.add_argument("--decode-steps", type=int, default=512, help="decode tokens per CUDA graph")
+    p.add_argument("--workload", choices=("decode", "prefill"), default="decode",
+                   help="decode: config 1 (the headline); prefill: config 3 (4096 tokens, one layer, Zipf)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
     return p.parse_args()
@@ -53,24 +55,64 @@ def parse_args():
 # clocks sampled during the timed region
 # ---------------------------------------------------------------------------
 class ClockSampler:
+    """SM clocks and throttle reasons sampled while the timed region runs.
+
+    NVML is polled every 2 ms from a thread, so a timed region of a few tens
+    of milliseconds still gets samples; ``nvidia-smi -lms 200`` is the
+    fallback when NVML cannot be loaded. ``__enter__`` returns after the first
+    sample (or 2 s), so the sampler is running when the region starts.
+    """
+
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASON_BITS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+                   ("sw_power_cap", 0x4))
 
     def __init__(self, gpu_id: str):
         self.gpu_id = gpu_id
+        self.samples: list[tuple[float, float, int]] = []   # (sm MHz, max MHz, reason mask)
         self.lines: list[str] = []
         self.proc = None
+        self.thread = None
+        self.stop = threading.Event()
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
-                 "-i", self.gpu_id], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
+            import pynvml
+
+            pynvml.nvmlInit()
+            if self.gpu_id.startswith("GPU-"):
+                handle = pynvml.nvmlDeviceGetHandleByUUID(self.gpu_id)
+            else:
+                handle = pynvml.nvmlDeviceGetHandleByIndex(int(self.gpu_id))
+            max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM))
+
+            def poll():
+                while not self.stop.is_set():
+                    try:
+                        mhz = float(pynvml.nvmlDeviceGetClockInfo(handle, pynvml.NVML_CLOCK_SM))
+                        mask = int(pynvml.nvmlDeviceGetCurrentClocksEventReasons(handle))
+                        self.samples.append((mhz, max_mhz, mask))
+                    except pynvml.NVMLError:
+                        pass
+                    self.stop.wait(0.002)
+
+            self.thread = threading.Thread(target=poll, daemon=True)
             self.thread.start()
-        except (OSError, ValueError):
-            self.proc = None
+        except Exception:  # NVML missing or the device not found: nvidia-smi instead
+            self.thread = None
+            try:
+                self.proc = subprocess.Popen(
+                    ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                     "-i", self.gpu_id], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                self.thread = threading.Thread(target=self._read, daemon=True)
+                self.thread.start()
+            except (OSError, ValueError):
+                self.proc = None
+        deadline = time.monotonic() + 2.0
+        while self.thread is not None and not (self.samples or self.lines) and time.monotonic() < deadline:
+            time.sleep(0.002)
         return self
 
     def _read(self):
@@ -78,17 +120,23 @@ class ClockSampler:
             self.lines.append(line.strip())
 
     def __exit__(self, *exc):
+        self.stop.set()
         if self.proc is not None:
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
+        if self.thread is not None:
             self.thread.join(timeout=2)
 
     def summary(self) -> dict:
         mhz, max_mhz, reasons = [], None, set()
-        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for sm, mx, mask in self.samples:
+            mhz.append(sm)
+            max_mhz = mx
+            reasons.update(name for name, bit in self.REASON_BITS if mask & bit)
+        names = [name for name, _ in self.REASON_BITS]
         for line in self.lines:
             parts = [x.strip() for x in line.split(",")]
             if len(parts) < 9:
@@ -103,7 +151,8 @@ class ClockSampler:
                     reasons.add(name)
         mhz.sort()
         return {"sm_mhz": mhz[len(mhz) // 2] if mhz else None, "sm_max_mhz": max_mhz,
-                "reasons": sorted(reasons), "samples": len(mhz)}
+                "reasons": sorted(reasons), "samples": len(mhz),
+                "source": "nvml 2 ms" if self.samples else "nvidia-smi 200 ms"}
 
 
 def measured_peaks() -> dict:
@@ -330,10 +379,114 @@ def run_ours(args) -> None:
         print(json.dumps(line))
 
 
+def run_prefill(args) -> None:
+    """Config 3: one FP8 MoE layer over 4096 prefill tokens, Zipf(1.1) routes.
+
+    One step = ``fp8_prefill`` on the 4096 rows (permute, two grouped
+    tensor-core GEMMs, combine). ``value`` = tokens/s with inputs resident;
+    the roofline is the bf16 tensor pipe (the dequant path computes in bf16),
+    FLOPs = 2 * pairs * (2I * H + H * I) per step.
+    """
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=device, timeout=timedelta(seconds=300))
+    from drama_b200 import synthetic
+    from drama_b200.backend import fp8_prefill
+
+    tokens = 4096
+    bank = synthetic.fp8_bank(EXPERTS, HIDDEN, INTER, rank, device=device, chunk=EXPERTS)
+
+    class Staged:
+        w13_weight = bank["w13_weight"]
+        w13_scale_inv = bank["w13_scale_inv"]
+        w2_weight = bank["w2_weight"]
+        w2_scale_inv = bank["w2_scale_inv"]
+
+    ids, w = synthetic.zipf_routes(tokens, TOP_K, EXPERTS, 100 + rank, device=device)
+    ids = ids.to(torch.int64).contiguous()
+    w = w.to(torch.bfloat16).contiguous()
+    x = synthetic.hidden_states(tokens, HIDDEN, 200 + rank, device=device)
+    for _ in range(max(3, args.warmup)):
+        fp8_prefill(x, ids, w, Staged, validate_ids=False)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+
+    barrier()
+    props = torch.cuda.get_device_properties(device)
+    gpu_id = f"GPU-{props.uuid}" if getattr(props, "uuid", None) else str(local)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(gpu_id) as clocks:
+        e0.record()
+        for _ in range(args.steps):
+            fp8_prefill(x, ids, w, Staged, validate_ids=False)
+        e1.record()
+        e1.synchronize()
+    barrier()
+    ms = e0.elapsed_time(e1) / args.steps
+    host_x = x.cpu().pin_memory()
+    host_out = torch.empty_like(host_x).pin_memory()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for _ in range(args.steps):
+        x.copy_(host_x, non_blocking=True)
+        out = fp8_prefill(x, ids, w, Staged, validate_ids=False)
+        host_out.copy_(out, non_blocking=True)
+    f1.record()
+    f1.synchronize()
+    e2e_ms = f0.elapsed_time(f1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms, e2e_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e2e_ms = float(t[0]), float(t[1])
+    pairs = tokens * TOP_K
+    flops = 2.0 * pairs * (2 * INTER * HIDDEN + HIDDEN * INTER)
+    peak_path = REPO / "MEASURED_PEAKS.json"
+    peak = json.loads(peak_path.read_text())["bf16_tflops"] if peak_path.is_file() else 1590.0
+    achieved = flops / (ms / 1000.0) / 1e12
+    line = {
+        "metric": "FP8 MoE-layer prefill tokens/s (config 3)", "value": tokens * world / (ms / 1000.0),
+        "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": max(3, args.warmup),
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp8-e4m3 weights dequantised to bf16, bf16 activations, fp32 accumulate",
+        "data": "synthetic (seeded random-init weights, hidden rows, Zipf(1.1) routes)",
+        "config": {"workload": (f"config3: prefill {tokens} tokens through one FP8 MoE layer (hidden {HIDDEN}, "
+                                f"{EXPERTS} experts, top-{TOP_K}, intermediate {INTER}), Zipf(1.1) routing"),
+                   "tokens": tokens, "hidden": HIDDEN, "experts": EXPERTS, "top_k": TOP_K, "intermediate": INTER,
+                   "parallelism": f"replicas{world}" if world > 1 else "single",
+                   "l2": "inputs larger than L2: 604 MB bank, 134 MB of per-pair down rows"},
+        "roofline": {"kernel": "prefill step: permute + gate/up GEMM + down GEMM + combine", "bound": "tensor",
+                     "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                     "peak_source": "measured (MEASURED_PEAKS.json bf16_tflops, cuBLAS bf16 burst)",
+                     "traffic": None, "algorithmic_flops_per_launch": flops},
+        "e2e": {"value": tokens * world / (e2e_ms / 1000.0), "unit": "tokens/s",
+                "h2d_bytes_per_step": x.numel() * 2, "d2h_bytes_per_step": x.numel() * 2},
+        "gpu_launches": args.steps * 4,
+        "clocks": clocks.summary(),
+    }
+    if world > 1:
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line))
+
+
 def main() -> None:
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "prefill":
+        run_prefill(args)
     else:
         run_ours(args)
 
