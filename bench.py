@@ -44,8 +44,12 @@ def parse_args():
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--layers", type=int, default=48)
     p.add_argument("--decode-steps", type=int, default=512, help="decode tokens per CUDA graph")
-    p.add_argument("--workload", choices=("decode", "prefill"), default="decode",
-                   help="decode: config 1 (the headline); prefill: config 3 (4096 tokens, one layer, Zipf)")
+    p.add_argument("--workload", choices=("decode", "prefill", "ep", "offload"), default="decode",
+                   help="decode: config 1 (the headline); prefill: config 3 (4096 tokens, one layer, Zipf); "
+                        "ep: config 4 expert-parallel decode of 256 tokens over the torchrun ranks; "
+                        "offload: config 4's 1-GPU offload variant (32 of 128 experts resident per layer)")
+    p.add_argument("--host-layers", type=int, default=48,
+                   help="offload: distinct pinned host stores (layers beyond reuse them in turn)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
     return p.parse_args()
@@ -481,12 +485,354 @@ def run_prefill(args) -> None:
         print(json.dumps(line))
 
 
+# ---------------------------------------------------------------------------
+# config 4: expert-parallel decode of 256 tokens, and the offload variant
+# ---------------------------------------------------------------------------
+EP_TOKENS = 256
+EP_CHUNK = 16          # experts generated per seed, so every G sees the same banks
+
+
+def _dist_setup():
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=device, timeout=timedelta(seconds=300))
+    props = torch.cuda.get_device_properties(device)
+    gpu_id = f"GPU-{props.uuid}" if getattr(props, "uuid", None) else str(local)
+    return world, rank, device, gpu_id
+
+
+def _max_over_ranks(values, world, device):
+    import torch
+    import torch.distributed as dist
+
+    if world == 1:
+        return values
+    t = torch.tensor(values, device=device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.tolist()
+
+
+def _ep_bank(layer: int, experts: range, device):
+    """This rank's experts of one layer; expert e's bytes do not depend on the shard."""
+    import torch
+
+    from drama_b200 import synthetic
+
+    parts = [synthetic.fp8_bank(EP_CHUNK, HIDDEN, INTER, 90_000 + layer * 100 + c // EP_CHUNK, device=device,
+                                chunk=EP_CHUNK)
+             for c in range(experts.start, experts.stop, EP_CHUNK)]
+    return {n: torch.cat([p[n] for p in parts]) for n in parts[0]}
+
+
+def _ep_routes(layers: int, device):
+    import torch
+
+    from drama_b200 import synthetic
+
+    out = []
+    for l in range(layers):
+        ids, w = synthetic.zipf_routes(EP_TOKENS, TOP_K, EXPERTS, 95_000 + l, device=device)
+        out.append((ids.to(torch.int32).contiguous(), w.to(torch.bfloat16).contiguous()))
+    return out
+
+
+def run_ep(args) -> None:
+    """Config 4: 256 decode tokens through 48 FP8 MoE layers, experts sharded over the ranks.
+
+    Strong scaling: the 256 tokens and 128 experts per layer are split over
+    the G ranks (tokens T/G per rank, experts E/G per rank); one step is one
+    replay of a CUDA graph holding all 48 layers (dispatch, NCCL all-to-alls,
+    grouped GEMMs, combine). ``value`` = 256 tokens / max-over-ranks step time.
+    """
+    import torch
+    import torch.distributed as dist
+
+    from drama_b200 import synthetic
+    from drama_b200.expert_parallel import ExpertParallelMoE, nccl_all_to_all, shard_experts, shard_tokens
+
+    world, rank, device, gpu_id = _dist_setup()
+    t0 = time.perf_counter()
+    experts = shard_experts(EXPERTS, world, rank)
+    rows = shard_tokens(EP_TOKENS, world, rank)
+
+    class Bank:
+        def __init__(self, d):
+            self.__dict__.update(d)
+
+    banks = [Bank(_ep_bank(l, experts, device)) for l in range(args.layers)]
+    routes = _ep_routes(args.layers, device)
+    local_routes = [(i[rows].contiguous(), w[rows].contiguous()) for i, w in routes]
+    h0 = synthetic.hidden_states(EP_TOKENS, HIDDEN, 97_000, device=device)[rows].contiguous()
+    model = ExpertParallelMoE(banks, experts=EXPERTS, top_k=TOP_K, tokens=EP_TOKENS // world, ranks=world,
+                              rank=rank, all_to_all=nccl_all_to_all() if world > 1 else None)
+    x = h0.clone()
+    model.step(x, local_routes)                       # eager pass: checks, lazy init
+    torch.cuda.synchronize(device)
+    dropped = model.dropped()
+    x.copy_(h0)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        model.step(x, local_routes)
+    x.copy_(h0)
+    graph.replay()                                    # one step from h0: the checksum below
+    torch.cuda.synchronize(device)
+    checksum = float(x.double().sum())
+    checksum = _sum_over_ranks(checksum, world, device)
+    build_s = time.perf_counter() - t0
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+
+    for _ in range(max(3, args.warmup)):
+        graph.replay()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(gpu_id) as clocks:
+        e0.record()
+        for _ in range(args.steps):
+            graph.replay()
+        e1.record()
+        e1.synchronize()
+    barrier()
+    ms = e0.elapsed_time(e1) / args.steps
+    host_in = h0.cpu().pin_memory()
+    host_out = torch.empty_like(host_in).pin_memory()
+    barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for _ in range(args.steps):
+        x.copy_(host_in, non_blocking=True)
+        graph.replay()
+        host_out.copy_(x, non_blocking=True)
+    f1.record()
+    f1.synchronize()
+    barrier()
+    e2e_ms = f0.elapsed_time(f1) / args.steps
+    ms, e2e_ms = _max_over_ranks([ms, e2e_ms], world, device)
+
+    # Algorithmic weight bytes: every expert touched on this rank, every layer.
+    nbytes = synthetic.expert_nbytes_fp8(HIDDEN, INTER)
+    touched = 0
+    for ids, _ in routes:
+        u = torch.unique(ids.long())
+        touched += int(((u >= experts.start) & (u < experts.stop)).sum())
+    step_bytes = touched * nbytes + 2 * (EP_TOKENS // world) * HIDDEN * 2 * args.layers
+    peaks = measured_peaks()
+    achieved = step_bytes / (ms / 1000.0) / 1e9
+    link_bytes = 2 * world * model.capacity * HIDDEN * 2 * args.layers if world > 1 else 0
+    line = {
+        "metric": METRIC, "value": EP_TOKENS / (ms / 1000.0), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None,
+        "dtype": "fp8-e4m3 weights dequantised to bf16, bf16 activations, fp32 accumulate",
+        "data": "synthetic (seeded random-init weights and hidden rows, Zipf(1.1) routes per layer)",
+        "config": {"workload": (f"config4: expert-parallel decode of {EP_TOKENS} tokens through {args.layers} FP8 "
+                                f"MoE layers (hidden {HIDDEN}, {EXPERTS} experts, top-{TOP_K}, intermediate {INTER}),"
+                                f" Zipf(1.1) routing, {EXPERTS // world} experts and {EP_TOKENS // world} tokens "
+                                f"per GPU, NCCL all-to-all dispatch/combine, one CUDA graph per step"),
+                   "tokens": EP_TOKENS, "layers": args.layers, "experts_per_gpu": EXPERTS // world,
+                   "parallelism": f"ep{world}", "capacity_rows_per_peer": model.capacity,
+                   "l2": "inputs larger than L2: every step reads the touched experts of 48 layers"},
+        "roofline": {"kernel": "one EP decode step on one rank (dispatch, all-to-alls, grouped GEMMs, combine)",
+                     "bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": achieved / peaks["hbm_gbs"],
+                     "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs)", "traffic": None,
+                     "algorithmic_bytes_per_launch": step_bytes},
+        "nvlink_bytes_per_step_per_gpu": link_bytes,
+        "e2e": {"value": EP_TOKENS / (e2e_ms / 1000.0), "unit": "tokens/s",
+                "h2d_bytes_per_step": h0.numel() * 2 * world, "d2h_bytes_per_step": h0.numel() * 2 * world},
+        "gpu_launches": args.steps * args.layers * model.launches_per_layer(),
+        "clocks": clocks.summary(),
+        "checksum": checksum, "dropped_pairs": list(dropped),
+        "setup_s": round(build_s, 1),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        ref = CpuReference(_ep_bank(0, range(0, EXPERTS), device))
+        ref.layer()
+        cpu = ref.sample(args.cpu_seconds, args.layers)
+        cpu["sample"] += "; one token per step (the workload's 256 tokens would take 256x as long)"
+        line["cpu_baseline"] = cpu
+    del graph
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line))
+
+
+def _sum_over_ranks(value: float, world: int, device) -> float:
+    import torch
+    import torch.distributed as dist
+
+    if world == 1:
+        return value
+    t = torch.tensor([value], device=device, dtype=torch.float64)
+    dist.all_reduce(t)
+    return float(t.item())
+
+
+def _pinned_h2d_gbs(device) -> float:
+    """Pinned host -> HBM copy bandwidth of this box (1 GiB, best of 3, CUDA events)."""
+    import torch
+
+    src = torch.empty(1 << 30, dtype=torch.uint8).pin_memory()
+    dst = torch.empty(1 << 30, dtype=torch.uint8, device=device)
+    best = 0.0
+    for _ in range(3):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        dst.copy_(src, non_blocking=True)
+        b.record()
+        b.synchronize()
+        best = max(best, (1 << 30) / (a.elapsed_time(b) / 1000.0) / 1e9)
+    del src, dst
+    return best
+
+
+def run_offload(args) -> None:
+    """Config 4, offload variant: 1 GPU, 32 of 128 experts resident per layer.
+
+    The resident 32 are each layer's most-routed experts (the ranking the
+    reference's host-budget/hot-cache logic makes from observed routes); the
+    other 96 live in page-locked host memory and the touched ones are staged
+    through ``StagingArena`` on a copy stream every layer, one layer ahead of
+    the compute. One step = 256 decode tokens through every layer.
+    """
+    import torch
+
+    from drama_b200 import synthetic
+    from drama_b200.backend import fp8_prefill
+    from drama_b200.staging import PackedExperts, StagingArena
+
+    world, rank, device, gpu_id = _dist_setup()
+    t0 = time.perf_counter()
+    resident_n = EXPERTS // 4
+    # Layer l is a copy of layer l % host_layers (weights, routes, residency);
+    # at least 3 distinct layers, so no slot set ever holds the ids its next
+    # stage asks for and every layer's cold experts really cross PCIe.
+    host_layers = max(3, min(args.host_layers, args.layers))
+    routes = _ep_routes(host_layers, device)
+    residents, stores, plans = [], [], []
+    for l in range(host_layers):
+        ids = routes[l][0].long()
+        counts = torch.bincount(ids.reshape(-1), minlength=EXPERTS).cpu()
+        order = sorted(range(EXPERTS), key=lambda e: (-int(counts[e]), e))
+        hot = sorted(order[:resident_n])
+        cold = sorted(order[resident_n:])
+        bank = _ep_bank(l, range(0, EXPERTS), device)
+        stores.append(PackedExperts.from_bank({n: t[cold].cpu() for n, t in bank.items()}, pin_memory=True))
+        residents.append(PackedExperts.from_bank({n: t[hot] for n, t in bank.items()}, device=device))
+        del bank
+        touched = sorted(set(torch.unique(ids).tolist()) - set(hot))
+        cold_pos = {e: i for i, e in enumerate(cold)}
+        stage_ids = torch.tensor([cold_pos[e] for e in touched], dtype=torch.int64)
+        local = {e: i for i, e in enumerate(touched)}
+        local.update({e: len(touched) + i for i, e in enumerate(hot)})
+        lut = torch.tensor([local.get(e, -1) for e in range(EXPERTS)], dtype=torch.int32, device=device)
+        plans.append((l, stage_ids, lut[ids].contiguous(), routes[l][1], len(touched)))
+    plans = [plans[l % host_layers] for l in range(args.layers)]
+    arena = StagingArena(EXPERTS, buffers=2)
+    h0 = synthetic.hidden_states(EP_TOKENS, HIDDEN, 97_000, device=device)
+    x = h0.clone()
+    build_s = time.perf_counter() - t0
+    hot_slots = list(range(resident_n))
+
+    def step(x):
+        for src_layer, stage_ids, local_ids, w, n_cold in plans:
+            store = stores[src_layer]
+            with arena.session(store, device):
+                if n_cold:
+                    arena.stage(store, stage_ids)
+                    bank = arena.combine_resident(n_cold, residents[src_layer], hot_slots)
+                else:
+                    bank = residents[src_layer].staged()
+                moe = fp8_prefill(x, local_ids, w, bank, validate_ids=False)
+                torch.add(x, moe, out=x)
+        return x
+
+    for _ in range(max(3, args.warmup)):
+        x.copy_(h0)
+        step(x)
+    torch.cuda.synchronize(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(gpu_id) as clocks:
+        e0.record()
+        for _ in range(args.steps):
+            step(x)
+        e1.record()
+        e1.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    host_in = h0.cpu().pin_memory()
+    host_out = torch.empty_like(host_in).pin_memory()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for _ in range(args.steps):
+        x.copy_(host_in, non_blocking=True)
+        step(x)
+        host_out.copy_(x, non_blocking=True)
+    f1.record()
+    f1.synchronize()
+    e2e_ms = f0.elapsed_time(f1) / args.steps
+    ms, e2e_ms = _max_over_ranks([ms, e2e_ms], world, device)
+    nbytes = synthetic.expert_nbytes_fp8(HIDDEN, INTER)
+    staged_bytes = sum(p[4] for p in plans) * nbytes
+    pcie = _pinned_h2d_gbs(device)
+    achieved = staged_bytes / (ms / 1000.0) / 1e9
+    line = {
+        "metric": METRIC, "value": EP_TOKENS * world / (ms / 1000.0), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp8-e4m3 weights dequantised to bf16, bf16 activations, fp32 accumulate",
+        "data": "synthetic (seeded random-init weights and hidden rows, Zipf(1.1) routes per layer)",
+        "config": {"workload": (f"config4 offload: {EP_TOKENS} decode tokens through {args.layers} FP8 MoE layers "
+                                f"on one GPU, {resident_n} of {EXPERTS} experts resident per layer (the most "
+                                f"routed), the touched others staged from page-locked host memory each layer"),
+                   "tokens": EP_TOKENS, "layers": args.layers, "resident_per_layer": resident_n,
+                   "host_stores": host_layers, "parallelism": f"replicas{world}" if world > 1 else "single",
+                   "staged_experts_per_step": sum(p[4] for p in plans),
+                   "l2": "inputs larger than L2: ~20 GB staged per step"},
+        "roofline": {"kernel": "one offload step (host->HBM staging on a copy stream + grouped GEMMs)",
+                     "bound": "pcie", "achieved": achieved, "peak": pcie, "unit": "GB/s", "frac": achieved / pcie,
+                     "peak_source": "measured in this run: 1 GiB pinned host -> HBM cudaMemcpyAsync, best of 3",
+                     "traffic": None, "algorithmic_bytes_per_launch": staged_bytes},
+        "e2e": {"value": EP_TOKENS * world / (e2e_ms / 1000.0), "unit": "tokens/s",
+                "h2d_bytes_per_step": h0.numel() * 2, "d2h_bytes_per_step": h0.numel() * 2},
+        "gpu_launches": args.steps * args.layers * 4,
+        "clocks": clocks.summary(),
+        "staging": {"h2d_bytes": arena.stats.h2d_bytes, "stage_calls": arena.stats.h2d_copy_calls,
+                    "reuse_hits": arena.stats.expert_cache_hits},
+        "setup_s": round(build_s, 1),
+    }
+    arena.close()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line))
+
+
 def main() -> None:
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
     elif args.workload == "prefill":
         run_prefill(args)
+    elif args.workload == "ep":
+        run_ep(args)
+    elif args.workload == "offload":
+        run_offload(args)
     else:
         run_ours(args)
 

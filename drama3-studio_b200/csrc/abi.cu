@@ -432,6 +432,55 @@ int drama_b200_fp8_prefill(const DramaB200Fp8Bank* bank, const void* x, int64_t 
     return 0;
 }
 
+int drama_b200_ep_dispatch(const void* hidden, int64_t tokens, int hidden_size, const void* ids, int ids_dtype,
+                           int top_k, int experts, int ranks, int64_t capacity, void* send_rows, int32_t* send_ids,
+                           int32_t* pair_rows, int32_t* status, void* stream) {
+    if (!hidden || !ids || !send_rows || !send_ids || !pair_rows)
+        return fail("hidden, ids, send_rows, send_ids and pair_rows are required");
+    if (!index_dtype(ids_dtype)) return fail("expert IDs must be int32 or int64");
+    if (tokens < 0 || top_k < 1 || top_k > 32) return fail("tokens must be >= 0 and top_k in [1, 32]");
+    if (tokens * top_k > (int64_t(1) << 24)) return fail("dispatch supports at most 2^24 (token, slot) pairs");
+    if (hidden_size < 8 || hidden_size % 8) return fail("hidden size must be a positive multiple of 8");
+    if (ranks < 1 || ranks > kMaxEpRanks) return fail("ranks must be in [1, %d]", kMaxEpRanks);
+    if (experts < ranks || experts % ranks || experts > (1 << 20))
+        return fail("experts (%d) must be a multiple of ranks (%d) and at most 2^20", experts, ranks);
+    if (capacity < 1 || capacity * ranks > INT32_MAX) return fail("capacity must be in [1, 2^31 / ranks)");
+    if (!aligned16(hidden) || !aligned16(send_rows)) return fail("hidden rows must start on 16-byte boundaries");
+    const size_t hb = static_cast<size_t>(tokens) * hidden_size * 2;
+    const size_t sb = static_cast<size_t>(capacity) * ranks * hidden_size * 2;
+    if (overlaps(send_rows, sb, hidden, hb)) return fail("send rows must not overlap the hidden states");
+    int sms = 0;
+    if (sm_count_current(&sms)) return -1;
+    const cudaError_t err = ep_dispatch_launch(hidden, tokens, hidden_size, ids, ids_dtype, top_k, experts, ranks,
+                                               capacity, send_rows, send_ids, pair_rows, status, sms,
+                                               static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return fail("dispatch launch failed: %s", cudaGetErrorString(err));
+    return 0;
+}
+
+int drama_b200_ep_combine(const void* rows, int64_t row_count, const int32_t* pair_rows, const void* weights,
+                          int weights_dtype, int64_t tokens, int top_k, int hidden_size, const void* residual,
+                          void* out, void* stream) {
+    if (!rows || !pair_rows || !weights || !out) return fail("rows, pair_rows, weights and out are required");
+    if (row_count < 0) return fail("row_count must be non-negative");
+    if (!float_dtype(weights_dtype)) return fail("routing weights must be floating point");
+    if (tokens < 0 || top_k < 1 || top_k > 32) return fail("tokens must be >= 0 and top_k in [1, 32]");
+    if (hidden_size < 8 || hidden_size % 8) return fail("hidden size must be a positive multiple of 8");
+    if (!aligned16(rows) || !aligned16(out) || (residual && !aligned16(residual)))
+        return fail("rows, residual and out must start on 16-byte boundaries");
+    const size_t ob = static_cast<size_t>(tokens) * hidden_size * 2;
+    if (overlaps(out, ob, rows, static_cast<size_t>(row_count) * hidden_size * 2))
+        return fail("output must not overlap the expert rows");
+    if (residual && residual != out && overlaps(out, ob, residual, ob))
+        return fail("output may be the residual itself but must not partly overlap it");
+    int sms = 0;
+    if (sm_count_current(&sms)) return -1;
+    const cudaError_t err = ep_combine_launch(rows, row_count, pair_rows, weights, weights_dtype, tokens, top_k, hidden_size,
+                                              residual, out, sms, static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return fail("combine launch failed: %s", cudaGetErrorString(err));
+    return 0;
+}
+
 }  // extern "C"
 
 // ---------------------------------------------------------------------------

@@ -150,6 +150,18 @@ __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
     return out;
 }
 
+// Route-slot combine step on 8 bf16 values: acc += fp32(row) * w, the product
+// rounded to fp32 before the add (offload.py:212, 1244: weighted fp32 pair
+// rows summed in slot order), so no FMA contraction.
+__device__ __forceinline__ void combine_accumulate(float (&acc)[8], uint4 q, float w) {
+    const uint32_t v[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+        acc[2 * u] = __fadd_rn(acc[2 * u], __fmul_rn(__uint_as_float(v[u] << 16), w));
+        acc[2 * u + 1] = __fadd_rn(acc[2 * u + 1], __fmul_rn(__uint_as_float(v[u] & 0xffff0000u), w));
+    }
+}
+
 __device__ __forceinline__ float ld_cg_f32(const float* p) { return __ldcg(p); }
 
 // Power-of-two exponent e such that |amax| * 2^-e lies in [2^14, 2^15): the

@@ -166,6 +166,15 @@ struct PrefillWorkspace {
     __nv_bfloat16* h;         // [P][I] SwiGLU activations in sorted order
     __nv_bfloat16* down;      // [P][H] bf16 down projections by pair
 };
+// Expert-parallel exchange (expert_parallel.cu).
+constexpr int kMaxEpRanks = 8;
+cudaError_t ep_dispatch_launch(const void* hidden, int64_t tokens, int H, const void* ids, int ids_dtype, int top_k,
+                               int experts, int ranks, int64_t cap, void* send_rows, int32_t* send_ids,
+                               int32_t* pair_rows, int32_t* status, int sm_count, cudaStream_t s);
+cudaError_t ep_combine_launch(const void* rows, int64_t row_count, const int32_t* pair_rows, const void* weights, int weights_dtype,
+                              int64_t tokens, int top_k, int H, const void* residual, void* out, int sm_count,
+                              cudaStream_t s);
+
 size_t prefill_workspace_layout(int64_t tokens, int top_k, int hidden, int intermediate, int experts, char* base,
                                 PrefillWorkspace* ws);
 cudaError_t prefill_launch(const DramaB200Fp8Bank& bank, const void* x, int64_t tokens, int top_k, const void* ids,

@@ -274,14 +274,8 @@ __global__ void prefill_combine_kernel(const __nv_bfloat16* down, const void* id
             const int64_t p = t * top_k + s;
             const int64_t id = load_index(ids, ids_dtype, p);
             if (id < 0 || id >= experts) continue;  // dropped pair: contributes zero
-            const float wt = load_any(weights, weights_dtype, p);
-            const uint4 q = __ldg(reinterpret_cast<const uint4*>(down + p * H + c));
-            const uint32_t wv[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                acc[2 * u] += __uint_as_float(wv[u] << 16) * wt;
-                acc[2 * u + 1] += __uint_as_float(wv[u] & 0xffff0000u) * wt;
-            }
+            combine_accumulate(acc, __ldg(reinterpret_cast<const uint4*>(down + p * H + c)),
+                               load_any(weights, weights_dtype, p));
         }
         uint32_t o[4];
 #pragma unroll

@@ -1,0 +1,87 @@
+// Host -> HBM expert staging on a copy stream (the transfer half of the
+// reference's _StagingPool.stage, src/drama_low_vram/offload.py:543-651).
+//
+// The reference gathers the requested experts into a pinned host buffer and
+// then issues one H2D copy on the compute stream (offload.py:596-636), so the
+// DMA and the expert kernels serialise. Here the caller's host store is itself
+// page-locked (cudaHostAlloc'd, or cudaHostRegister'ed over an mmap), each
+// expert's bytes go straight from the store into its arena slot, copies that
+// continue one another in both address spaces are merged into one DMA, and
+// everything runs on a caller-chosen copy stream bracketed by events, so the
+// compute stream only waits for the bytes it is about to read.
+//
+// A pageable source would turn cudaMemcpyAsync into a staged, synchronous
+// copy and quietly remove the overlap, so it is rejected instead.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace drama {
+namespace {
+
+int pointer_kind(const void* p, cudaMemoryType* type, int* device) {
+    cudaPointerAttributes attr{};
+    const cudaError_t err = cudaPointerGetAttributes(&attr, p);
+    if (err != cudaSuccess) {
+        cudaGetLastError();
+        return fail("cudaPointerGetAttributes(%p): %s", p, cudaGetErrorString(err));
+    }
+    *type = attr.type;
+    *device = attr.device;
+    return 0;
+}
+
+}  // namespace
+}  // namespace drama
+
+using namespace drama;
+
+extern "C" {
+
+int drama_b200_stage_copies(const void* const* host_src, void* const* dev_dst, const uint64_t* bytes, int count,
+                            void* copy_stream, void* wait_event, void* done_event) {
+    if (count < 0) return fail("copy count must be non-negative, got %d", count);
+    if (count > 0 && (!host_src || !dev_dst || !bytes)) return fail("copy arrays must not be null");
+    int dst_device = -1;
+    for (int i = 0; i < count; ++i) {
+        if (!host_src[i] || !dev_dst[i]) return fail("copy %d has a null pointer", i);
+        if (bytes[i] == 0) return fail("copy %d has zero bytes", i);
+        cudaMemoryType type;
+        int device = -1;
+        if (pointer_kind(host_src[i], &type, &device)) return -1;
+        if (type != cudaMemoryTypeHost)
+            return fail("copy %d: source %p is not page-locked host memory (pin it or cudaHostRegister it)", i,
+                        host_src[i]);
+        if (pointer_kind(dev_dst[i], &type, &device)) return -1;
+        if (type != cudaMemoryTypeDevice) return fail("copy %d: destination %p is not device memory", i, dev_dst[i]);
+        if (dst_device < 0) dst_device = device;
+        if (device != dst_device) return fail("copy %d: destinations span devices %d and %d", i, dst_device, device);
+    }
+    cudaStream_t stream = static_cast<cudaStream_t>(copy_stream);
+    if (wait_event) {
+        const cudaError_t err = cudaStreamWaitEvent(stream, static_cast<cudaEvent_t>(wait_event), 0);
+        if (err != cudaSuccess) return fail("cudaStreamWaitEvent: %s", cudaGetErrorString(err));
+    }
+    int i = 0;
+    while (i < count) {
+        const char* src = static_cast<const char*>(host_src[i]);
+        char* dst = static_cast<char*>(dev_dst[i]);
+        uint64_t run = bytes[i];
+        int j = i + 1;
+        while (j < count && static_cast<const char*>(host_src[j]) == src + run &&
+               static_cast<char*>(dev_dst[j]) == dst + run) {
+            run += bytes[j];
+            ++j;
+        }
+        const cudaError_t err = cudaMemcpyAsync(dst, src, run, cudaMemcpyHostToDevice, stream);
+        if (err != cudaSuccess) return fail("cudaMemcpyAsync of %llu bytes: %s", (unsigned long long)run,
+                                            cudaGetErrorString(err));
+        i = j;
+    }
+    if (done_event) {
+        const cudaError_t err = cudaEventRecord(static_cast<cudaEvent_t>(done_event), stream);
+        if (err != cudaSuccess) return fail("cudaEventRecord: %s", cudaGetErrorString(err));
+    }
+    return 0;
+}
+
+}  // extern "C"

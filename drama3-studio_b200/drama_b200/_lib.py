@@ -46,6 +46,9 @@ EXPORTS = (
     "drama_b200_fp8_prefill",
     "drama_b200_static_scratch_bytes",
     "drama_b200_fp8_decode_static",
+    "drama_b200_ep_dispatch",
+    "drama_b200_ep_combine",
+    "drama_b200_stage_copies",
 )
 
 c_void_p, c_int, c_int64, c_size_t = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_size_t
@@ -123,6 +126,14 @@ class Library:
         dll.drama_b200_static_scratch_bytes.restype = c_size_t
         dll.drama_b200_fp8_decode_static.argtypes = [ctypes.POINTER(Fp8Bank)] + decode_args[:10] + [c_void_p]
         dll.drama_b200_fp8_decode_static.restype = c_int
+        dll.drama_b200_stage_copies.argtypes = [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p]
+        dll.drama_b200_stage_copies.restype = c_int
+        dll.drama_b200_ep_dispatch.argtypes = [c_void_p, c_int64, c_int, c_void_p, c_int, c_int, c_int, c_int,
+                                               c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]
+        dll.drama_b200_ep_dispatch.restype = c_int
+        dll.drama_b200_ep_combine.argtypes = [c_void_p, c_int64, c_void_p, c_void_p, c_int, c_int64, c_int, c_int,
+                                              c_void_p, c_void_p, c_void_p]
+        dll.drama_b200_ep_combine.restype = c_int
         for name in ("drama_b200_device_check", "drama_b200_route_topk", "drama_b200_permute_routes",
                      "drama_b200_fp8_decode", "drama_b200_int4_decode", "drama_b200_fp8_moe_layer",
                      "drama_b200_fp8_moe_router", "drama_b200_fp8_moe_experts"):

@@ -1,0 +1,203 @@
+"""Expert-parallel MoE decode over G GPUs (one process per GPU, NCCL all-to-all).
+
+The reference runs every expert on one GPU (``ExpertOffloadManager``,
+``src/drama_low_vram/offload.py:1016-1276``); here the E experts of each layer
+are split into G contiguous blocks of E/G, rank r holding block r, and each
+rank owns T/G of the T tokens. One layer on rank r:
+
+1. ``drama_b200_ep_dispatch``: every (token, slot) pair's hidden row goes into
+   the send block of the rank that owns its expert, with the receiver-local
+   expert id beside it (fixed ``capacity`` rows per destination, so nothing
+   has to be known on the host and the step can be captured in a CUDA graph).
+2. all-to-all of the rows and of the ids (NCCL over NVLink).
+3. ``drama_b200_fp8_prefill`` with top_k 1 and unit weights on the received
+   rows: each row's bf16 down projection through the grouped GEMMs (unused
+   rows are dropped by their id).
+4. all-to-all of the expert rows back to where they came from.
+5. ``drama_b200_ep_combine``: route-weighted sum in slot order plus residual,
+   ``h' = bf16(h + bf16(sum_s w_s * row_s))``, as one layer of the oracle's
+   ``stack_layer`` with the routes given.
+
+Every pair's arithmetic is the same whatever G is (rows are computed one by
+one by the same kernels and summed in slot order by their owner), so the
+result does not depend on the number of GPUs.
+
+The exchange itself is a pluggable callable, ``all_to_all(out, inp)``; the
+product uses ``torch.distributed.all_to_all_single`` on the process group.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from typing import Callable, Sequence
+
+import torch
+from torch import Tensor
+
+from . import _lib
+from .backend import _fp8_bank
+
+AllToAll = Callable[[Tensor, Tensor], None]
+
+
+def shard_experts(experts: int, ranks: int, rank: int) -> range:
+    """Global expert ids held by ``rank`` (contiguous blocks of E/G)."""
+    if ranks < 1 or experts % ranks:
+        raise ValueError(f"{experts} experts do not split evenly over {ranks} ranks")
+    if not 0 <= rank < ranks:
+        raise ValueError(f"rank {rank} outside [0, {ranks})")
+    per = experts // ranks
+    return range(rank * per, (rank + 1) * per)
+
+
+def shard_tokens(tokens: int, ranks: int, rank: int) -> slice:
+    """The token rows owned by ``rank`` (contiguous blocks of T/G)."""
+    if tokens % ranks:
+        raise ValueError(f"{tokens} tokens do not split evenly over {ranks} ranks")
+    per = tokens // ranks
+    return slice(rank * per, (rank + 1) * per)
+
+
+def nccl_all_to_all(group=None) -> AllToAll:
+    """Equal-split all-to-all on ``group`` (rows travel as int32 words)."""
+    import torch.distributed as dist
+
+    def run(out: Tensor, inp: Tensor) -> None:
+        dist.all_to_all_single(out, inp, group=group)
+
+    return run
+
+
+@dataclass
+class ExchangeBuffers:
+    """Per-rank scratch of one layer, reused by every layer and step."""
+
+    send_rows: Tensor     # [G*cap, H] bf16
+    send_ids: Tensor      # [G*cap] int32
+    pair_rows: Tensor     # [T_l*k] int32
+    recv_rows: Tensor     # [G*cap, H] bf16
+    recv_ids: Tensor      # [G*cap] int32
+    expert_rows: Tensor   # [G*cap, H] bf16
+    back_rows: Tensor     # [G*cap, H] bf16
+    unit: Tensor          # [G*cap, 1] bf16 ones
+    status: Tensor        # [4] int32
+    workspace: Tensor     # prefill workspace
+
+
+class ExpertParallelMoE:
+    """One rank's share of an expert-parallel FP8 MoE layer stack.
+
+    ``banks[l]`` is this rank's slice of layer ``l``: an ``ExpertStore``-shaped
+    FP8 bank (the four role tensors) of the E/G experts ``shard_experts``
+    gives, indexed by local id.
+    """
+
+    def __init__(self, banks: Sequence, *, experts: int, top_k: int, tokens: int, ranks: int = 1, rank: int = 0,
+                 all_to_all: AllToAll | None = None, capacity: int | None = None) -> None:
+        if not banks:
+            raise ValueError("At least one layer bank is required")
+        self.ranks, self.rank = ranks, rank
+        self.experts, self.top_k = experts, top_k
+        self.local_experts = len(shard_experts(experts, ranks, rank))
+        self.tokens = tokens                        # tokens owned by this rank
+        self.capacity = capacity if capacity is not None else tokens * top_k
+        if self.capacity < 1:
+            raise ValueError("Capacity must be positive")
+        if ranks > 1 and all_to_all is None:
+            raise ValueError("More than one rank needs an all_to_all")
+        self.all_to_all = all_to_all
+        first = banks[0]
+        self.hidden = first.w13_weight.shape[-1]
+        self.intermediate = first.w2_weight.shape[-1]
+        self.device = first.w13_weight.device
+        self._banks = []
+        for bank in banks:
+            if bank.w13_weight.shape[0] != self.local_experts:
+                raise ValueError(f"Each bank must hold this rank's {self.local_experts} experts")
+            self._banks.append(_fp8_bank(bank, self.hidden))
+        self.lib = _lib.library()
+        self.buffers = self._allocate()
+
+    def _allocate(self) -> ExchangeBuffers:
+        rows = self.ranks * self.capacity
+        dev, H = self.device, self.hidden
+        ws_bytes = self.lib.dll.drama_b200_prefill_workspace_bytes(rows, 1, H, self.intermediate,
+                                                                   self.local_experts)
+        bf = dict(dtype=torch.bfloat16, device=dev)
+        return ExchangeBuffers(
+            send_rows=torch.zeros(rows, H, **bf), send_ids=torch.empty(rows, dtype=torch.int32, device=dev),
+            pair_rows=torch.empty(self.tokens * self.top_k, dtype=torch.int32, device=dev),
+            recv_rows=torch.zeros(rows, H, **bf), recv_ids=torch.empty(rows, dtype=torch.int32, device=dev),
+            expert_rows=torch.zeros(rows, H, **bf), back_rows=torch.zeros(rows, H, **bf),
+            unit=torch.ones(rows, 1, **bf), status=torch.zeros(4, dtype=torch.int32, device=dev),
+            workspace=torch.zeros(max(ws_bytes, 256), dtype=torch.uint8, device=dev))
+
+    def _check_routes(self, h: Tensor, ids: Tensor, weights: Tensor) -> None:
+        if h.dtype != torch.bfloat16 or tuple(h.shape) != (self.tokens, self.hidden) or not h.is_contiguous():
+            raise ValueError(f"Hidden rows must be contiguous bf16 [{self.tokens}, {self.hidden}]")
+        if tuple(ids.shape) != (self.tokens, self.top_k) or ids.dtype not in (torch.int32, torch.int64):
+            raise ValueError(f"Expert IDs must be integer [{self.tokens}, {self.top_k}]")
+        if tuple(weights.shape) != tuple(ids.shape) or not weights.is_floating_point():
+            raise ValueError("Routing weights must match the expert IDs")
+
+    def layer(self, h: Tensor, ids: Tensor, weights: Tensor, layer: int, out: Tensor | None = None) -> Tensor:
+        """``bf16(h + moe(h))`` for this rank's tokens through layer ``layer``.
+
+        ``ids`` are global expert ids, ``weights`` the route weights, both
+        ``[T_l, k]`` and contiguous. ``out`` may be ``h`` (in place).
+        """
+        self._check_routes(h, ids, weights)
+        out = torch.empty_like(h) if out is None else out
+        b = self.buffers
+        self._dispatch(h, ids)
+        if self.ranks > 1:
+            self.all_to_all(b.recv_rows.view(torch.int32), b.send_rows.view(torch.int32))
+            self.all_to_all(b.recv_ids, b.send_ids)
+            recv_rows, recv_ids = b.recv_rows, b.recv_ids
+        else:
+            recv_rows, recv_ids = b.send_rows, b.send_ids
+        self._run_experts(layer, recv_rows, recv_ids, b.expert_rows)
+        if self.ranks > 1:
+            self.all_to_all(b.back_rows.view(torch.int32), b.expert_rows.view(torch.int32))
+            back = b.back_rows
+        else:
+            back = b.expert_rows
+        self._combine(back, weights, h, out)
+        return out
+
+    # The three device steps (CUDA kernels of this library).
+    def _dispatch(self, h: Tensor, ids: Tensor) -> None:
+        b, lib = self.buffers, self.lib
+        lib.check(lib.dll.drama_b200_ep_dispatch(
+            h.data_ptr(), self.tokens, self.hidden, ids.data_ptr(), _lib.DTYPE_CODES[ids.dtype], self.top_k,
+            self.experts, self.ranks, self.capacity, b.send_rows.data_ptr(), b.send_ids.data_ptr(),
+            b.pair_rows.data_ptr(), b.status.data_ptr(), _lib.stream_handle(h.device)))
+
+    def _run_experts(self, layer: int, rows: Tensor, ids: Tensor, out: Tensor) -> None:
+        b, lib = self.buffers, self.lib
+        bank, _ = self._banks[layer]
+        lib.check(lib.dll.drama_b200_fp8_prefill(
+            ctypes.byref(bank), rows.data_ptr(), rows.shape[0], 1, ids.data_ptr(), _lib.I32, b.unit.data_ptr(),
+            _lib.BF16, out.data_ptr(), b.workspace.data_ptr(), b.workspace.numel(), _lib.stream_handle(rows.device)))
+
+    def _combine(self, back: Tensor, weights: Tensor, h: Tensor, out: Tensor) -> None:
+        b, lib = self.buffers, self.lib
+        lib.check(lib.dll.drama_b200_ep_combine(
+            back.data_ptr(), back.shape[0], b.pair_rows.data_ptr(), weights.data_ptr(), _lib.DTYPE_CODES[weights.dtype],
+            self.tokens, self.top_k, self.hidden, h.data_ptr(), out.data_ptr(), _lib.stream_handle(h.device)))
+
+    def step(self, h: Tensor, routes: Sequence[tuple[Tensor, Tensor]]) -> Tensor:
+        """All layers in order, in place on ``h``; ``routes[l] = (ids, weights)``."""
+        for layer, (ids, weights) in enumerate(routes):
+            self.layer(h, ids, weights, layer, out=h)
+        return h
+
+    def launches_per_layer(self) -> int:
+        """Kernels of this library per layer: plan + pack, permute + 2 GEMMs + combine, EP combine."""
+        return 7
+
+    def dropped(self) -> tuple[int, int]:
+        """(pairs with an out-of-range id, pairs over capacity) of the last layer (synchronises)."""
+        s = self.buffers.status.tolist()
+        return s[0], s[1]

@@ -254,6 +254,66 @@ DRAMA_B200_API int drama_b200_fp8_decode_static(const DramaB200Fp8Bank* bank, co
                                                 const void* weights, int weights_dtype,
                                                 void* out, float* pair_out, void* stream);
 
+/* ---------------------------------------------------------------------------
+ * Expert parallelism over G ranks (experts in contiguous blocks of E/G per
+ * rank). The reference is single-GPU, so the exchange has no counterpart in
+ * it; the two entries split the reference's partitioned expert call
+ * (src/drama_low_vram/offload.py:1206-1276: group the (token, slot) pairs by
+ * expert, run each expert on its rows, sum fp32 weighted rows in slot order at
+ * 1242-1244) across the ranks.
+ *
+ * drama_b200_ep_dispatch: for the local hidden rows [tokens, hidden_size]
+ * (bf16) and their routes ids [tokens, top_k] (global expert ids), writes
+ *   send_rows [ranks, capacity, hidden_size] bf16: the hidden row of every pair
+ *     in the block of the rank owning its expert, pairs in order;
+ *   send_ids [ranks, capacity] int32: the receiver-local expert id of each
+ *     row (id - rank * E/G), or E/G for an unused row;
+ *   pair_rows [tokens * top_k] int32: the row of each pair in send_rows, -1
+ *     for a pair whose id is outside [0, experts) or that did not fit;
+ *   status[0] (int32, may be NULL) = pairs with an out-of-range id, status[1]
+ *     = pairs beyond a destination's capacity (capacity = tokens * top_k
+ *     never overflows).
+ * After an all-to-all of send_rows / send_ids, drama_b200_fp8_prefill with
+ * top_k 1 and unit weights on the received rows gives each row's bf16 down
+ * projection (unused rows are dropped by their id); a second all-to-all
+ * brings them back in the same positions.
+ *
+ * drama_b200_ep_combine: out[t] = bf16(residual[t] + bf16(sum over slots s in
+ * order of rows[pair_rows[t*k+s]] * weights[t*k+s])), fp32 products and sums
+ * (offload.py:212, 1244), over rows [row_count, hidden_size] bf16; a pair whose
+ * row is -1 or outside [0, row_count) contributes zero. residual may be NULL,
+ * or equal to out.
+ * ------------------------------------------------------------------------- */
+DRAMA_B200_API int drama_b200_ep_dispatch(const void* hidden, int64_t tokens, int hidden_size, const void* ids,
+                                          int ids_dtype, int top_k, int experts, int ranks, int64_t capacity,
+                                          void* send_rows, int32_t* send_ids, int32_t* pair_rows,
+                                          int32_t* status, void* stream);
+
+DRAMA_B200_API int drama_b200_ep_combine(const void* rows, int64_t row_count, const int32_t* pair_rows,
+                                         const void* weights, int weights_dtype, int64_t tokens, int top_k,
+                                         int hidden_size, const void* residual, void* out, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * K4 staging: host -> HBM expert copies on a copy stream. Replaces the
+ * transfer half of _StagingPool.stage (src/drama_low_vram/offload.py:543-651:
+ * the host gather at 561-594 and the H2D copy_ on the compute stream at
+ * 596-636) and its _copy_done event (offload.py:637-645).
+ *
+ * Copy i moves bytes[i] from host_src[i] to dev_dst[i]. Sources must be
+ * page-locked host memory (cudaHostAlloc or cudaHostRegister); a pageable
+ * source is rejected because cudaMemcpyAsync would silently run it
+ * synchronously. Destinations must be device memory on one device. Copies
+ * that continue one another in both address spaces are issued as one
+ * cudaMemcpyAsync. Before the first copy copy_stream waits on wait_event
+ * (may be NULL: e.g. the compute event after the last reader of these slots);
+ * after the last copy done_event is recorded on copy_stream (may be NULL).
+ * Both events must already exist (cudaEventCreate). All pointers are checked
+ * before anything is enqueued. count 0 only waits and records.
+ * ------------------------------------------------------------------------- */
+DRAMA_B200_API int drama_b200_stage_copies(const void* const* host_src, void* const* dev_dst,
+                                           const uint64_t* bytes, int count, void* copy_stream,
+                                           void* wait_event, void* done_event);
+
 #ifdef __cplusplus
 }
 #endif

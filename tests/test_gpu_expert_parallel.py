@@ -1,0 +1,255 @@
+"""Expert-parallel kernels and the EP layer stack on the GPU.
+
+* ``drama_b200_ep_dispatch`` / ``drama_b200_ep_combine`` against CPU
+  restatements of their contracts: exact (indices, bytes, and the fp32
+  slot-order sum, which has one rounding order).
+* One rank (G = 1) of ``ExpertParallelMoE`` against ``fp8_prefill`` plus the
+  residual (bit for bit: the same kernels see the same rows) and against the
+  oracle's dequant path (the north_star tolerance).
+* G = 2 and 4 emulated on one GPU (every rank's steps run in turn, the
+  all-to-all done by copying blocks) and, when two GPUs are present, G = 2
+  over NCCL: the result must equal G = 1 bit for bit.
+"""
+
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+from helpers import assert_parity, np_bank, np_f32
+from oracle import restate as R
+
+pytestmark = pytest.mark.gpu
+
+E, H, I, K, T, LAYERS = 16, 512, 256, 4, 32, 2
+
+
+class Bank:
+    def __init__(self, d):
+        self.__dict__.update(d)
+
+
+def _inputs(device):
+    from drama_b200 import synthetic
+
+    banks = [synthetic.fp8_bank(E, H, I, seed=40 + l, device=device, chunk=E) for l in range(LAYERS)]
+    routes = []
+    for l in range(LAYERS):
+        ids, w = synthetic.zipf_routes(T, K, E, seed=50 + l, device=device)
+        routes.append((ids.to(torch.int64).contiguous(), w.to(torch.bfloat16).contiguous()))
+    h = synthetic.hidden_states(T, H, seed=60, device=device)
+    return banks, routes, h
+
+
+def _model(banks, ranks=1, rank=0, tokens=T, all_to_all=None, capacity=None):
+    from drama_b200.expert_parallel import ExpertParallelMoE, shard_experts
+
+    ex = shard_experts(E, ranks, rank)
+    local = [Bank({n: v[ex.start:ex.stop] for n, v in b.items()}) for b in banks]
+    return ExpertParallelMoE(local, experts=E, top_k=K, tokens=tokens, ranks=ranks, rank=rank,
+                             all_to_all=all_to_all or (lambda o, i: None), capacity=capacity)
+
+
+def _dispatch_restated(h, ids, experts, ranks, cap):
+    per = experts // ranks
+    send_ids = np.full(ranks * cap, per, np.int32)
+    pair_rows = np.full(ids.size, -1, np.int32)
+    fill = [0] * ranks
+    dropped = overflow = 0
+    for p, e in enumerate(ids.reshape(-1).tolist()):
+        if not 0 <= e < experts:
+            dropped += 1
+            continue
+        d = e // per
+        if fill[d] >= cap:
+            overflow += 1
+            continue
+        row = d * cap + fill[d]
+        fill[d] += 1
+        send_ids[row] = e - d * per
+        pair_rows[p] = row
+    return send_ids, pair_rows, (dropped, overflow)
+
+
+@pytest.mark.parametrize("ranks,cap", [(1, 37 * 8), (2, 37 * 8), (8, 37 * 8), (4, 20)])
+def test_dispatch_matches_its_restatement(cuda_device, ranks, cap):
+    from drama_b200 import _lib
+
+    lib = _lib.library()
+    gen = torch.Generator().manual_seed(ranks * 100 + cap)
+    tokens, top_k, experts = 37, 8, 128
+    ids = torch.randint(-2, experts + 3, (tokens, top_k), generator=gen)
+    h = torch.randn(tokens, 256, generator=gen).to(torch.bfloat16).to(cuda_device)
+    send_rows = torch.zeros(ranks * cap, 256, dtype=torch.bfloat16, device=cuda_device)
+    send_ids = torch.empty(ranks * cap, dtype=torch.int32, device=cuda_device)
+    pair_rows = torch.empty(tokens * top_k, dtype=torch.int32, device=cuda_device)
+    status = torch.zeros(4, dtype=torch.int32, device=cuda_device)
+    for dtype in (torch.int64, torch.int32):
+        d_ids = ids.to(dtype).to(cuda_device)
+        lib.check(lib.dll.drama_b200_ep_dispatch(
+            h.data_ptr(), tokens, 256, d_ids.data_ptr(), _lib.DTYPE_CODES[dtype], top_k, experts, ranks, cap,
+            send_rows.data_ptr(), send_ids.data_ptr(), pair_rows.data_ptr(), status.data_ptr(),
+            _lib.stream_handle(cuda_device)))
+        torch.cuda.synchronize()
+        want_ids, want_rows, (dropped, overflow) = _dispatch_restated(h, ids.numpy(), experts, ranks, cap)
+        assert np.array_equal(send_ids.cpu().numpy(), want_ids)
+        assert np.array_equal(pair_rows.cpu().numpy(), want_rows)
+        assert status[:2].tolist() == [dropped, overflow]
+        for p, row in enumerate(want_rows.tolist()):
+            if row >= 0:
+                assert torch.equal(send_rows[row], h[p // top_k])
+
+
+@pytest.mark.parametrize("wdtype,residual", [(torch.bfloat16, True), (torch.float32, False)])
+def test_combine_matches_its_restatement(cuda_device, wdtype, residual):
+    from drama_b200 import _lib
+
+    lib = _lib.library()
+    gen = torch.Generator().manual_seed(7)
+    tokens, top_k, hidden, nrows = 19, 8, 512, 200
+    rows = torch.randn(nrows, hidden, generator=gen).to(torch.bfloat16)
+    pair_rows = torch.randint(-1, nrows, (tokens * top_k,), generator=gen, dtype=torch.int32)
+    w = torch.rand(tokens, top_k, generator=gen).to(wdtype)
+    h = torch.randn(tokens, hidden, generator=gen).to(torch.bfloat16)
+    acc = torch.zeros(tokens, hidden)
+    for s in range(top_k):
+        r = pair_rows.view(tokens, top_k)[:, s].long()
+        take = (r >= 0).float()[:, None]
+        prod = rows[r.clamp_min(0)].float() * w[:, s].float()[:, None]
+        acc = acc + prod * take                      # a skipped pair adds +0.0
+    want = acc.to(torch.bfloat16)
+    if residual:
+        want = (h.float() + want.float()).to(torch.bfloat16)
+    d = {n: t.to(cuda_device) for n, t in dict(rows=rows, pair_rows=pair_rows, w=w, h=h).items()}
+    out = torch.empty(tokens, hidden, dtype=torch.bfloat16, device=cuda_device)
+    lib.check(lib.dll.drama_b200_ep_combine(
+        d["rows"].data_ptr(), nrows, d["pair_rows"].data_ptr(), d["w"].data_ptr(), _lib.DTYPE_CODES[wdtype], tokens,
+        top_k, hidden, d["h"].data_ptr() if residual else None, out.data_ptr(), _lib.stream_handle(cuda_device)))
+    torch.cuda.synchronize()
+    assert torch.equal(out.cpu(), want)
+
+
+def _reference_stack(banks, routes, h):
+    from drama_b200.backend import fp8_prefill
+
+    x = h.clone()
+    for bank, (ids, w) in zip(banks, routes):
+        moe = fp8_prefill(x, ids, w, Bank(bank))
+        x = (x.float() + moe.float()).to(torch.bfloat16)
+    return x
+
+
+def test_single_rank_matches_prefill_and_the_oracle(cuda_device):
+    banks, routes, h = _inputs(cuda_device)
+    model = _model(banks)
+    x = h.clone()
+    model.step(x, routes)
+    torch.cuda.synchronize()
+    assert model.dropped() == (0, 0)
+    assert torch.equal(x, _reference_stack(banks, routes, h))
+    y = np_f32(h)
+    for bank, (ids, w) in zip(banks, routes):
+        y = R.round_bf16(y + R.fp8_dequant_forward(y, ids.cpu().numpy(), np_f32(w), np_bank(bank)))
+    assert_parity(np_f32(x), y, label="EP G=1 vs oracle stack")
+
+
+def _emulated(banks, routes, h, ranks):
+    """G ranks on one GPU: each rank's device steps in turn, blocks copied for the all-to-all."""
+    from drama_b200.expert_parallel import shard_tokens
+
+    tl = T // ranks
+    models = [_model(banks, ranks, r, tokens=tl) for r in range(ranks)]
+    cap = models[0].capacity
+    xs = [h[shard_tokens(T, ranks, r)].clone() for r in range(ranks)]
+    for layer, (ids, w) in enumerate(routes):
+        rs = [(ids[shard_tokens(T, ranks, r)].contiguous(), w[shard_tokens(T, ranks, r)].contiguous())
+              for r in range(ranks)]
+        for r, m in enumerate(models):
+            m._dispatch(xs[r], rs[r][0])
+        for r, m in enumerate(models):
+            for s, src in enumerate(models):
+                m.buffers.recv_rows[s * cap:(s + 1) * cap] = src.buffers.send_rows[r * cap:(r + 1) * cap]
+                m.buffers.recv_ids[s * cap:(s + 1) * cap] = src.buffers.send_ids[r * cap:(r + 1) * cap]
+        for m in models:
+            m._run_experts(layer, m.buffers.recv_rows, m.buffers.recv_ids, m.buffers.expert_rows)
+        for r, m in enumerate(models):
+            for s, src in enumerate(models):
+                m.buffers.back_rows[s * cap:(s + 1) * cap] = src.buffers.expert_rows[r * cap:(r + 1) * cap]
+        for r, m in enumerate(models):
+            m._combine(m.buffers.back_rows, rs[r][1], xs[r], xs[r])
+    return torch.cat(xs)
+
+
+@pytest.mark.parametrize("ranks", [2, 4])
+def test_emulated_ranks_equal_one_rank_bit_for_bit(cuda_device, ranks):
+    banks, routes, h = _inputs(cuda_device)
+    single = _model(banks)
+    x = h.clone()
+    single.step(x, routes)
+    got = _emulated(banks, routes, h, ranks)
+    torch.cuda.synchronize()
+    assert torch.equal(got, x)
+
+
+def test_small_capacity_drops_and_counts_overflow(cuda_device):
+    banks, routes, h = _inputs(cuda_device)
+    model = _model(banks, capacity=8)
+    x = h.clone()
+    model.layer(x, routes[0][0], routes[0][1], 0, out=x)
+    torch.cuda.synchronize()
+    dropped, overflow = model.dropped()
+    assert dropped == 0 and overflow == T * K - 8
+
+
+def _nccl_rank(rank, world, port, out_dir):
+    import torch.distributed as dist
+
+    from drama_b200.expert_parallel import nccl_all_to_all, shard_tokens
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    device = torch.device("cuda", rank)
+    from datetime import timedelta
+
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=device, timeout=timedelta(seconds=120))
+    try:
+        banks, routes, h = _inputs(device)
+        rows = shard_tokens(T, world, rank)
+        model = _model(banks, world, rank, tokens=T // world, all_to_all=nccl_all_to_all())
+        local = [(i[rows].contiguous(), w[rows].contiguous()) for i, w in routes]
+        x = h[rows].clone()
+        model.step(x, local)                          # eager
+        g_in = h[rows].clone()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            model.step(g_in, local)
+        g_in.copy_(h[rows])
+        graph.replay()
+        torch.cuda.synchronize()
+        del graph
+        torch.save({"eager": x.cpu(), "graph": g_in.cpu()}, os.path.join(out_dir, f"rank{rank}.pt"))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_gpus_over_nccl_equal_one_rank(cuda_device, tmp_path):
+    import torch.multiprocessing as mp
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    banks, routes, h = _inputs(cuda_device)
+    single = _model(banks)
+    x = h.clone()
+    single.step(x, routes)
+    torch.cuda.synchronize()
+    mp.spawn(_nccl_rank, args=(2, port, str(tmp_path)), nprocs=2, join=True)
+    parts = [torch.load(tmp_path / f"rank{r}.pt") for r in range(2)]
+    assert torch.equal(torch.cat([p["eager"] for p in parts]), x.cpu())
+    assert torch.equal(torch.cat([p["graph"] for p in parts]), x.cpu())
