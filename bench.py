@@ -44,10 +44,11 @@ def parse_args():
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--layers", type=int, default=48)
     p.add_argument("--decode-steps", type=int, default=512, help="decode tokens per CUDA graph")
-    p.add_argument("--workload", choices=("decode", "prefill", "ep", "offload"), default="decode",
+    p.add_argument("--workload", choices=("decode", "prefill", "ep", "offload", "int4"), default="decode",
                    help="decode: config 1 (the headline); prefill: config 3 (4096 tokens, one layer, Zipf); "
                         "ep: config 4 expert-parallel decode of 256 tokens over the torchrun ranks; "
-                        "offload: config 4's 1-GPU offload variant (32 of 128 experts resident per layer)")
+                        "offload: config 4's 1-GPU offload variant (32 of 128 experts resident per layer); "
+                        "int4: config 2 (one W4A16 asymmetric layer, decode batches 1/4/16, uniform routes)")
     p.add_argument("--host-layers", type=int, default=48,
                    help="offload: distinct pinned host stores (layers beyond reuse them in turn)")
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -823,6 +824,116 @@ def run_offload(args) -> None:
         print(json.dumps(line))
 
 
+# ---------------------------------------------------------------------------
+# config 2: one INT4 W4A16 layer, decode batches of 1, 4 and 16 tokens
+# ---------------------------------------------------------------------------
+INT4_CALLS = 64      # calls per CUDA graph, each with its own uniform routes
+
+
+def run_int4(args) -> None:
+    """Config 2: QuantizedB200Backend(0) on an asymmetric W4A16 bank, batches 1/4/16.
+
+    One step = one replay of a CUDA graph holding 64 expert calls, each with
+    its own seeded uniform routes (so consecutive calls read different
+    experts of the 314 MB bank, which is larger than L2). ``value`` is the
+    batch-1 tokens/s; every batch is reported under ``by_batch`` with its
+    algorithmic bytes (the distinct experts of each call) and GB/s.
+    """
+    import torch
+
+    from drama_b200 import QuantizedB200Backend, QuantizedBank, synthetic
+
+    world, rank, device, gpu_id = _dist_setup()
+    bank = synthetic.int4_bank(EXPERTS, HIDDEN, INTER, 2024 + rank, device=device, asymmetric=True)
+    qb = QuantizedBank(**bank)
+    backend = QuantizedB200Backend(0, validate_ids=False)
+    nbytes = synthetic.expert_nbytes_int4(HIDDEN, INTER)
+    peaks = measured_peaks()
+    results = {}
+    clocks_summary = None
+    for batch in (1, 4, 16):
+        routes = [synthetic.uniform_routes(batch, TOP_K, EXPERTS, 300 + 100 * batch + c, device=device)
+                  for c in range(INT4_CALLS)]
+        routes = [(i.to(torch.int32).contiguous(), w.to(torch.bfloat16).contiguous()) for i, w in routes]
+        xs = [synthetic.hidden_states(batch, HIDDEN, 900 + c, device=device) for c in range(INT4_CALLS)]
+        outs = [None] * INT4_CALLS
+        cap_stream = torch.cuda.Stream(device)          # the backend's workspace is per (device, stream)
+        cap_stream.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(cap_stream):
+            for c in range(INT4_CALLS):                 # eager: workspace, checks
+                outs[c] = backend.forward(xs[c], routes[c][0], routes[c][1], qb)
+        torch.cuda.synchronize(device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=cap_stream):
+            for c in range(INT4_CALLS):
+                outs[c] = backend.forward(xs[c], routes[c][0], routes[c][1], qb)
+        for _ in range(max(3, args.warmup)):
+            graph.replay()
+        torch.cuda.synchronize(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(gpu_id) as clocks:
+            e0.record()
+            for _ in range(args.steps):
+                graph.replay()
+            e1.record()
+            e1.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps
+        ms = _max_over_ranks([ms], world, device)[0]
+        unique = sum(int(torch.unique(i).numel()) for i, _ in routes)
+        call_bytes = unique * nbytes / INT4_CALLS + 2 * batch * HIDDEN * 2
+        call_ms = ms / INT4_CALLS
+        results[batch] = {"tokens_per_s": batch * INT4_CALLS * world / (ms / 1000.0), "call_us": call_ms * 1000.0,
+                          "unique_experts_per_call": unique / INT4_CALLS,
+                          "algorithmic_bytes_per_call": call_bytes,
+                          "achieved_gbs": call_bytes / (call_ms / 1000.0) / 1e9}
+        if batch == 1:
+            clocks_summary = clocks.summary()
+            host_x = [x.cpu().pin_memory() for x in xs]
+            host_o = torch.empty(INT4_CALLS, batch, HIDDEN, dtype=torch.bfloat16).pin_memory()
+            f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            f0.record()
+            for _ in range(args.steps):
+                for c in range(INT4_CALLS):
+                    xs[c].copy_(host_x[c], non_blocking=True)
+                graph.replay()
+                for c in range(INT4_CALLS):
+                    host_o[c].copy_(outs[c], non_blocking=True)
+            f1.record()
+            f1.synchronize()
+            e2e_ms = _max_over_ranks([f0.elapsed_time(f1) / args.steps], world, device)[0]
+        del graph
+    b1 = results[1]
+    line = {
+        "metric": METRIC, "value": b1["tokens_per_s"], "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": max(3, args.warmup), "ms_per_step": INT4_CALLS * b1["call_us"] / 1000.0, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None,
+        "dtype": "int4 weights (asymmetric, group 128, bf16 scales, uint4 zero-points), f16 MMA, fp32 accumulate",
+        "data": "synthetic (seeded random-init weights and hidden rows, uniform routes)",
+        "config": {"workload": (f"config2: one W4A16 MoE layer (hidden {HIDDEN}, {EXPERTS} experts, top-{TOP_K}, "
+                                f"intermediate {INTER}), decode batches 1/4/16 (value: batch 1), "
+                                f"{INT4_CALLS} calls per CUDA graph with distinct uniform routes"),
+                   "batches": [1, 4, 16], "calls_per_graph": INT4_CALLS,
+                   "parallelism": f"replicas{world}" if world > 1 else "single",
+                   "l2": "bank of 314 MB (> L2), routes differ call to call"},
+        "roofline": {"kernel": "one W4A16 expert call (prep + up + down kernels), batch 1", "bound": "hbm",
+                     "achieved": b1["achieved_gbs"], "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": b1["achieved_gbs"] / peaks["hbm_gbs"],
+                     "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs)", "traffic": None,
+                     "algorithmic_bytes_per_launch": b1["algorithmic_bytes_per_call"]},
+        "by_batch": results,
+        "e2e": {"value": INT4_CALLS * world / (e2e_ms / 1000.0), "unit": "tokens/s",
+                "h2d_bytes_per_step": INT4_CALLS * HIDDEN * 2, "d2h_bytes_per_step": INT4_CALLS * HIDDEN * 2},
+        "gpu_launches": args.steps * INT4_CALLS * 3,
+        "clocks": clocks_summary,
+    }
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line))
+
+
 def main() -> None:
     args = parse_args()
     if args.impl == "reference":
@@ -833,6 +944,8 @@ def main() -> None:
         run_ep(args)
     elif args.workload == "offload":
         run_offload(args)
+    elif args.workload == "int4":
+        run_int4(args)
     else:
         run_ours(args)
 

@@ -432,6 +432,45 @@ int drama_b200_fp8_prefill(const DramaB200Fp8Bank* bank, const void* x, int64_t 
     return 0;
 }
 
+size_t drama_b200_expert_rows_workspace_bytes(int64_t rows, int hidden, int intermediate, int experts) {
+    return prefill_workspace_layout(rows, 1, hidden, intermediate, experts, nullptr, nullptr);
+}
+
+int drama_b200_fp8_expert_rows(const DramaB200Fp8Bank* bank, const void* x, int64_t rows, const void* ids,
+                               int ids_dtype, void* out, void* workspace, size_t workspace_bytes, void* stream) {
+    if (!bank || !x || !ids || !out) return fail("bank, x, ids and out are required");
+    const DramaB200Fp8Bank& b = *bank;
+    if (!index_dtype(ids_dtype)) return fail("expert IDs must be int32 or int64");
+    if (rows < 0 || rows > (int64_t(1) << 24)) return fail("rows must be in [0, 2^24]");
+    if (b.hidden % 128 || b.hidden < 128 || b.intermediate % 128 || b.intermediate < 128)
+        return fail("hidden and intermediate must be positive multiples of 128");
+    if (b.slots < 1 || b.slots > 1024) return fail("slots must be in [1, 1024]");
+    if (!b.w13 || !b.w13_scale || !b.w2 || !b.w2_scale) return fail("FP8 bank pointers are required");
+    if (!aligned16(b.w13) || !aligned16(b.w2) || !aligned16(x) || !aligned16(out) || b.w13_row_stride % 16 ||
+        b.w2_row_stride % 16 || b.w13_slot_stride % 16 || b.w2_slot_stride % 16)
+        return fail("FP8 weight rows and the hidden rows must start on 16-byte boundaries");
+    if (b.w13_row_stride < b.hidden || b.w2_row_stride < b.intermediate ||
+        b.w13_slot_stride < b.w13_row_stride * 2 * b.intermediate || b.w2_slot_stride < b.w2_row_stride * b.hidden)
+        return fail("FP8 weight strides are smaller than the bank geometry");
+    if (b.w13_scale_row_stride < b.hidden / 128 || b.w2_scale_row_stride < b.intermediate / 128)
+        return fail("FP8 scale strides are smaller than the bank geometry");
+    const size_t xb = static_cast<size_t>(rows) * b.hidden * 2;
+    if (overlaps(out, xb, x, xb)) return fail("output must not overlap the hidden rows");
+    if (rows == 0) return 0;
+    int sms = 0;
+    if (sm_count_current(&sms)) return -1;
+    const size_t need = prefill_workspace_layout(rows, 1, b.hidden, b.intermediate, b.slots, nullptr, nullptr);
+    if (!workspace || workspace_bytes < need)
+        return fail("expert-rows workspace too small: need %zu bytes, got %zu", need, workspace_bytes);
+    if (reinterpret_cast<uintptr_t>(workspace) & 255u) return fail("workspace must be 256-byte aligned");
+    PrefillWorkspace ws;
+    prefill_workspace_layout(rows, 1, b.hidden, b.intermediate, b.slots, static_cast<char*>(workspace), &ws);
+    const cudaError_t err = expert_rows_launch(b, x, rows, ids, ids_dtype, out, ws, sms,
+                                               static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return fail("expert-rows launch failed: %s", cudaGetErrorString(err));
+    return 0;
+}
+
 int drama_b200_ep_dispatch(const void* hidden, int64_t tokens, int hidden_size, const void* ids, int ids_dtype,
                            int top_k, int experts, int ranks, int64_t capacity, void* send_rows, int32_t* send_ids,
                            int32_t* pair_rows, int32_t* status, void* stream) {

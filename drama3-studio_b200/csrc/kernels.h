@@ -166,6 +166,11 @@ struct PrefillWorkspace {
     __nv_bfloat16* h;         // [P][I] SwiGLU activations in sorted order
     __nv_bfloat16* down;      // [P][H] bf16 down projections by pair
 };
+// Per-row bf16 down projections on the swap-AB grouped GEMMs (expert_rows.cu);
+// scratch is a PrefillWorkspace laid out for (rows, top_k 1).
+cudaError_t expert_rows_launch(const DramaB200Fp8Bank& bank, const void* x, int64_t rows, const void* ids,
+                               int ids_dtype, void* out, const PrefillWorkspace& ws, int sm_count, cudaStream_t s);
+
 // Expert-parallel exchange (expert_parallel.cu).
 constexpr int kMaxEpRanks = 8;
 cudaError_t ep_dispatch_launch(const void* hidden, int64_t tokens, int H, const void* ids, int ids_dtype, int top_k,

@@ -21,6 +21,7 @@
 // instruction on the GPU before its first MMA commit, cause not found.)
 #include "common.cuh"
 #include "decode_tiles.cuh"
+#include "grouped.cuh"
 #include "kernels.h"
 
 namespace drama {
@@ -55,39 +56,6 @@ __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r
                  : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
                  : "r"(addr));
 }
-__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-// FP8 E4M3 x4 -> 4 fp32 (exact): bytes 0, 1 -> lo halves; 2, 3 -> hi.
-__device__ __forceinline__ void fp8x4_to_f32(uint32_t w, float (&o)[4]) {
-    uint32_t lo, hi;
-    e4m3x4_to_f16x2x2(w, lo, hi);
-    o[0] = __half2float(__ushort_as_half(static_cast<unsigned short>(lo & 0xffffu)));
-    o[1] = __half2float(__ushort_as_half(static_cast<unsigned short>(lo >> 16)));
-    o[2] = __half2float(__ushort_as_half(static_cast<unsigned short>(hi & 0xffffu)));
-    o[3] = __half2float(__ushort_as_half(static_cast<unsigned short>(hi >> 16)));
-}
-
-// Tile t of the flattened list (expert, m block, n block); prefix[e] = tiles
-// of experts < e.
-__device__ __forceinline__ void decode_tile(int t, const int* prefix, int E, int nblocks, int& e, int& mb, int& nb) {
-    int lo = 0, hi = E;  // largest e with prefix[e] <= t
-    while (hi - lo > 1) {
-        const int mid = (lo + hi) >> 1;
-        if (prefix[mid] <= t) lo = mid;
-        else hi = mid;
-    }
-    e = lo;
-    const int local = t - prefix[lo];
-    mb = local / nblocks;
-    nb = local % nblocks;
-}
-
 template <int MODE>
 __global__ void __launch_bounds__(kPfThreads, 1) prefill_gemm_kernel(PrefillArgs a) {
     extern __shared__ __align__(16) uint8_t smem_pf[];
@@ -238,10 +206,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_gemm_kernel(PrefillArgs
                         float hv[2];
 #pragma unroll
                         for (int q = 0; q < 2; ++q) {
-                            const float gate = __bfloat162float(__float2bfloat16_rn(acc[mt][j][2 * r + q]));
-                            const float up = __bfloat162float(__float2bfloat16_rn(acc[mt][j + 4][2 * r + q]));
-                            const float act = __bfloat162float(__float2bfloat16_rn(gate / (1.0f + expf(-gate))));
-                            hv[q] = act * up;
+                            hv[q] = swiglu_rounded(acc[mt][j][2 * r + q], acc[mt][j + 4][2 * r + q]);
                         }
                         *reinterpret_cast<__nv_bfloat162*>(hrow + 8 * j) = __floats2bfloat162_rn(hv[0], hv[1]);
                     }

@@ -46,6 +46,8 @@ EXPORTS = (
     "drama_b200_fp8_prefill",
     "drama_b200_static_scratch_bytes",
     "drama_b200_fp8_decode_static",
+    "drama_b200_expert_rows_workspace_bytes",
+    "drama_b200_fp8_expert_rows",
     "drama_b200_ep_dispatch",
     "drama_b200_ep_combine",
     "drama_b200_stage_copies",
@@ -128,6 +130,11 @@ class Library:
         dll.drama_b200_fp8_decode_static.restype = c_int
         dll.drama_b200_stage_copies.argtypes = [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p]
         dll.drama_b200_stage_copies.restype = c_int
+        dll.drama_b200_expert_rows_workspace_bytes.argtypes = [c_int64, c_int, c_int, c_int]
+        dll.drama_b200_expert_rows_workspace_bytes.restype = c_size_t
+        dll.drama_b200_fp8_expert_rows.argtypes = [ctypes.POINTER(Fp8Bank), c_void_p, c_int64, c_void_p, c_int,
+                                                   c_void_p, c_void_p, c_size_t, c_void_p]
+        dll.drama_b200_fp8_expert_rows.restype = c_int
         dll.drama_b200_ep_dispatch.argtypes = [c_void_p, c_int64, c_int, c_void_p, c_int, c_int, c_int, c_int,
                                                c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]
         dll.drama_b200_ep_dispatch.restype = c_int

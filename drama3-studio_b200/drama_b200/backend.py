@@ -299,6 +299,36 @@ def fp8_prefill(x: Tensor, ids: Tensor, weights: Tensor, staged, *, validate_ids
     return out
 
 
+def fp8_expert_rows(x: Tensor, ids: Tensor, staged) -> Tensor:
+    """Per-row bf16 down projections ``[rows, H]`` of ``x [rows, H]`` through expert ``ids[rows]``.
+
+    ``TorchExpertBackend.forward_pairs`` (offload.py:215-244) before the route
+    weight, on the swap-AB grouped GEMMs: each row's result is independent of
+    the other rows. Rows whose id is outside the bank are left as zeros.
+    """
+    if x.dtype != torch.bfloat16 or x.ndim != 2:
+        raise ValueError("fp8_expert_rows runs on bf16 rows [N, H]")
+    hidden = x.shape[-1]
+    bank, keep = _fp8_bank(staged, hidden)
+    if ids.shape != (x.shape[0],) and ids.shape != (x.shape[0], 1):
+        raise ValueError("fp8_expert_rows takes one expert id per row")
+    if ids.dtype not in (torch.int32, torch.int64) or ids.device != x.device:
+        raise ValueError("Expert IDs must be integer tensors on the rows' device")
+    x = x.contiguous()
+    ids = ids.reshape(-1).contiguous()
+    out = torch.zeros_like(x)
+    if x.shape[0] == 0:
+        return out
+    lib = _lib.library()
+    nbytes = lib.dll.drama_b200_expert_rows_workspace_bytes(x.shape[0], hidden, bank.intermediate, bank.slots)
+    ws = _PREFILL_WORKSPACES.get(x.device, nbytes)
+    lib.check(lib.dll.drama_b200_fp8_expert_rows(
+        ctypes.byref(bank), x.data_ptr(), x.shape[0], ids.data_ptr(), _lib.DTYPE_CODES[ids.dtype], out.data_ptr(),
+        ws.data_ptr(), ws.numel(), _lib.stream_handle(x.device)))
+    del keep
+    return out
+
+
 class QuantizedB200Backend(_DecodeBackend):
     """GPTQ W4A16 (mode 0) experts, symmetric or with uint4 zero-points."""
 

@@ -10,9 +10,9 @@ rank owns T/G of the T tokens. One layer on rank r:
    expert id beside it (fixed ``capacity`` rows per destination, so nothing
    has to be known on the host and the step can be captured in a CUDA graph).
 2. all-to-all of the rows and of the ids (NCCL over NVLink).
-3. ``drama_b200_fp8_prefill`` with top_k 1 and unit weights on the received
-   rows: each row's bf16 down projection through the grouped GEMMs (unused
-   rows are dropped by their id).
+3. ``drama_b200_fp8_expert_rows`` on the received rows: each row's bf16 down
+   projection through the swap-AB grouped GEMMs, built for the few rows per
+   expert of a decode batch (unused rows are dropped by their id).
 4. all-to-all of the expert rows back to where they came from.
 5. ``drama_b200_ep_combine``: route-weighted sum in slot order plus residual,
    ``h' = bf16(h + bf16(sum_s w_s * row_s))``, as one layer of the oracle's
@@ -80,9 +80,8 @@ class ExchangeBuffers:
     recv_ids: Tensor      # [G*cap] int32
     expert_rows: Tensor   # [G*cap, H] bf16
     back_rows: Tensor     # [G*cap, H] bf16
-    unit: Tensor          # [G*cap, 1] bf16 ones
     status: Tensor        # [4] int32
-    workspace: Tensor     # prefill workspace
+    workspace: Tensor     # expert-rows workspace
 
 
 class ExpertParallelMoE:
@@ -122,15 +121,15 @@ class ExpertParallelMoE:
     def _allocate(self) -> ExchangeBuffers:
         rows = self.ranks * self.capacity
         dev, H = self.device, self.hidden
-        ws_bytes = self.lib.dll.drama_b200_prefill_workspace_bytes(rows, 1, H, self.intermediate,
-                                                                   self.local_experts)
+        ws_bytes = self.lib.dll.drama_b200_expert_rows_workspace_bytes(rows, H, self.intermediate,
+                                                                       self.local_experts)
         bf = dict(dtype=torch.bfloat16, device=dev)
         return ExchangeBuffers(
             send_rows=torch.zeros(rows, H, **bf), send_ids=torch.empty(rows, dtype=torch.int32, device=dev),
             pair_rows=torch.empty(self.tokens * self.top_k, dtype=torch.int32, device=dev),
             recv_rows=torch.zeros(rows, H, **bf), recv_ids=torch.empty(rows, dtype=torch.int32, device=dev),
             expert_rows=torch.zeros(rows, H, **bf), back_rows=torch.zeros(rows, H, **bf),
-            unit=torch.ones(rows, 1, **bf), status=torch.zeros(4, dtype=torch.int32, device=dev),
+            status=torch.zeros(4, dtype=torch.int32, device=dev),
             workspace=torch.zeros(max(ws_bytes, 256), dtype=torch.uint8, device=dev))
 
     def _check_routes(self, h: Tensor, ids: Tensor, weights: Tensor) -> None:
@@ -177,9 +176,9 @@ class ExpertParallelMoE:
     def _run_experts(self, layer: int, rows: Tensor, ids: Tensor, out: Tensor) -> None:
         b, lib = self.buffers, self.lib
         bank, _ = self._banks[layer]
-        lib.check(lib.dll.drama_b200_fp8_prefill(
-            ctypes.byref(bank), rows.data_ptr(), rows.shape[0], 1, ids.data_ptr(), _lib.I32, b.unit.data_ptr(),
-            _lib.BF16, out.data_ptr(), b.workspace.data_ptr(), b.workspace.numel(), _lib.stream_handle(rows.device)))
+        lib.check(lib.dll.drama_b200_fp8_expert_rows(
+            ctypes.byref(bank), rows.data_ptr(), rows.shape[0], ids.data_ptr(), _lib.I32, out.data_ptr(),
+            b.workspace.data_ptr(), b.workspace.numel(), _lib.stream_handle(rows.device)))
 
     def _combine(self, back: Tensor, weights: Tensor, h: Tensor, out: Tensor) -> None:
         b, lib = self.buffers, self.lib
@@ -194,8 +193,8 @@ class ExpertParallelMoE:
         return h
 
     def launches_per_layer(self) -> int:
-        """Kernels of this library per layer: plan + pack, permute + 2 GEMMs + combine, EP combine."""
-        return 7
+        """Kernels of this library per layer: plan + pack, permute + 2 GEMMs, EP combine."""
+        return 6
 
     def dropped(self) -> tuple[int, int]:
         """(pairs with an out-of-range id, pairs over capacity) of the last layer (synchronises)."""

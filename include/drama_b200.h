@@ -255,6 +255,25 @@ DRAMA_B200_API int drama_b200_fp8_decode_static(const DramaB200Fp8Bank* bank, co
                                                 void* out, float* pair_out, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Per-row expert projections for few rows per expert (decode batches, the
+ * rows an expert-parallel rank receives, staged offload). Replaces
+ * TorchExpertBackend.forward_pairs (src/drama_low_vram/offload.py:215-244)
+ * before its route weighting: row r of out [rows, hidden] (bf16) =
+ * bf16(bf16(bf16(silu(g)) * u) @ W2^T) with g, u = bf16(x[r] @ W13^T) and
+ * W = bf16(fp8 * block scale), for the expert ids[r] (I32/I64). Rows whose id
+ * is outside [0, slots) are not written (status[0] counts them, at
+ * drama_b200_prefill_status_offset() in the workspace). x: [rows, hidden]
+ * bf16; hidden and intermediate multiples of 128; rows <= 2^24. Each row's
+ * result is independent of the other rows in the call.
+ * ------------------------------------------------------------------------- */
+DRAMA_B200_API size_t drama_b200_expert_rows_workspace_bytes(int64_t rows, int hidden, int intermediate,
+                                                             int experts);
+
+DRAMA_B200_API int drama_b200_fp8_expert_rows(const DramaB200Fp8Bank* bank, const void* x, int64_t rows,
+                                              const void* ids, int ids_dtype, void* out, void* workspace,
+                                              size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Expert parallelism over G ranks (experts in contiguous blocks of E/G per
  * rank). The reference is single-GPU, so the exchange has no counterpart in
  * it; the two entries split the reference's partitioned expert call

@@ -3,9 +3,10 @@
 * ``drama_b200_ep_dispatch`` / ``drama_b200_ep_combine`` against CPU
   restatements of their contracts: exact (indices, bytes, and the fp32
   slot-order sum, which has one rounding order).
-* One rank (G = 1) of ``ExpertParallelMoE`` against ``fp8_prefill`` plus the
-  residual (bit for bit: the same kernels see the same rows) and against the
-  oracle's dequant path (the north_star tolerance).
+* One rank (G = 1) of ``ExpertParallelMoE`` against ``fp8_expert_rows`` per
+  (token, slot) row with the combine restated in torch (bit for bit: the same
+  kernel sees the same rows) and against the oracle's dequant path (the
+  north_star tolerance).
 * G = 2 and 4 emulated on one GPU (every rank's steps run in turn, the
   all-to-all done by copying blocks) and, when two GPUs are present, G = 2
   over NCCL: the result must equal G = 1 bit for bit.
@@ -134,16 +135,20 @@ def test_combine_matches_its_restatement(cuda_device, wdtype, residual):
 
 
 def _reference_stack(banks, routes, h):
-    from drama_b200.backend import fp8_prefill
+    """fp8_expert_rows per (token, slot) row, then the slot-order fp32 combine and residual in torch."""
+    from drama_b200.backend import fp8_expert_rows
 
     x = h.clone()
     for bank, (ids, w) in zip(banks, routes):
-        moe = fp8_prefill(x, ids, w, Bank(bank))
-        x = (x.float() + moe.float()).to(torch.bfloat16)
+        rows = fp8_expert_rows(x.repeat_interleave(K, dim=0), ids.reshape(-1), Bank(bank)).float()
+        acc = torch.zeros(T, H, device=x.device)
+        for s in range(K):
+            acc = acc + rows[s::K] * w[:, s].float()[:, None]
+        x = (x.float() + acc.to(torch.bfloat16).float()).to(torch.bfloat16)
     return x
 
 
-def test_single_rank_matches_prefill_and_the_oracle(cuda_device):
+def test_single_rank_matches_expert_rows_and_the_oracle(cuda_device):
     banks, routes, h = _inputs(cuda_device)
     model = _model(banks)
     x = h.clone()
