@@ -433,7 +433,7 @@ int drama_b200_fp8_prefill(const DramaB200Fp8Bank* bank, const void* x, int64_t 
 }
 
 size_t drama_b200_expert_rows_workspace_bytes(int64_t rows, int hidden, int intermediate, int experts) {
-    return prefill_workspace_layout(rows, 1, hidden, intermediate, experts, nullptr, nullptr);
+    return expert_rows_workspace_layout(rows, hidden, intermediate, experts, nullptr, nullptr);
 }
 
 int drama_b200_fp8_expert_rows(const DramaB200Fp8Bank* bank, const void* x, int64_t rows, const void* ids,
@@ -459,12 +459,12 @@ int drama_b200_fp8_expert_rows(const DramaB200Fp8Bank* bank, const void* x, int6
     if (rows == 0) return 0;
     int sms = 0;
     if (sm_count_current(&sms)) return -1;
-    const size_t need = prefill_workspace_layout(rows, 1, b.hidden, b.intermediate, b.slots, nullptr, nullptr);
+    const size_t need = expert_rows_workspace_layout(rows, b.hidden, b.intermediate, b.slots, nullptr, nullptr);
     if (!workspace || workspace_bytes < need)
         return fail("expert-rows workspace too small: need %zu bytes, got %zu", need, workspace_bytes);
     if (reinterpret_cast<uintptr_t>(workspace) & 255u) return fail("workspace must be 256-byte aligned");
-    PrefillWorkspace ws;
-    prefill_workspace_layout(rows, 1, b.hidden, b.intermediate, b.slots, static_cast<char*>(workspace), &ws);
+    RowsWorkspace ws;
+    expert_rows_workspace_layout(rows, b.hidden, b.intermediate, b.slots, static_cast<char*>(workspace), &ws);
     const cudaError_t err = expert_rows_launch(b, x, rows, ids, ids_dtype, out, ws, sms,
                                                static_cast<cudaStream_t>(stream));
     if (err != cudaSuccess) return fail("expert-rows launch failed: %s", cudaGetErrorString(err));

@@ -166,10 +166,21 @@ struct PrefillWorkspace {
     __nv_bfloat16* h;         // [P][I] SwiGLU activations in sorted order
     __nv_bfloat16* down;      // [P][H] bf16 down projections by pair
 };
-// Per-row bf16 down projections on the swap-AB grouped GEMMs (expert_rows.cu);
-// scratch is a PrefillWorkspace laid out for (rows, top_k 1).
+// Per-row bf16 down projections on the swap-AB grouped GEMMs (expert_rows.cu).
+struct RowsWorkspace {
+    int32_t* status;          // [4]: [0] rows dropped for an out-of-range id
+    int64_t* order;           // [rows] sorted by expert (stable)
+    int64_t* counts;          // [E]
+    int64_t* offsets;         // [E + 1]
+    __half* xh;               // [rows][H] f16 copies scaled per 64 columns
+    float* xs;                // [rows][H / 64] their scales (powers of two)
+    __half* h;                // [rows][I] SwiGLU activations, sorted, f16 scaled per 64 columns
+    float* hs;                // [rows][I / 64]
+};
+size_t expert_rows_workspace_layout(int64_t rows, int hidden, int intermediate, int experts, char* base,
+                                    RowsWorkspace* ws);
 cudaError_t expert_rows_launch(const DramaB200Fp8Bank& bank, const void* x, int64_t rows, const void* ids,
-                               int ids_dtype, void* out, const PrefillWorkspace& ws, int sm_count, cudaStream_t s);
+                               int ids_dtype, void* out, const RowsWorkspace& ws, int sm_count, cudaStream_t s);
 
 // Expert-parallel exchange (expert_parallel.cu).
 constexpr int kMaxEpRanks = 8;

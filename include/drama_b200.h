@@ -259,8 +259,10 @@ DRAMA_B200_API int drama_b200_fp8_decode_static(const DramaB200Fp8Bank* bank, co
  * rows an expert-parallel rank receives, staged offload). Replaces
  * TorchExpertBackend.forward_pairs (src/drama_low_vram/offload.py:215-244)
  * before its route weighting: row r of out [rows, hidden] (bf16) =
- * bf16(bf16(bf16(silu(g)) * u) @ W2^T) with g, u = bf16(x[r] @ W13^T) and
- * W = bf16(fp8 * block scale), for the expert ids[r] (I32/I64). Rows whose id
+ * bf16(bf16(bf16(silu(g)) * u) @ W2^T) with g, u = bf16(x[r] @ W13^T), for the
+ * expert ids[r] (I32/I64), computed as the decode kernels compute it: exact
+ * f16 expansion of the E4M3 weights, block scales applied to fp32 partial
+ * sums, activations as f16 with a power-of-two scale per 64 values. Rows whose id
  * is outside [0, slots) are not written (status[0] counts them, at
  * drama_b200_prefill_status_offset() in the workspace). x: [rows, hidden]
  * bf16; hidden and intermediate multiples of 128; rows <= 2^24. Each row's
