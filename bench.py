@@ -534,6 +534,15 @@ def _ep_bank(layer: int, experts: range, device):
     return {n: torch.cat([p[n] for p in parts]) for n in parts[0]}
 
 
+def _ep_bank_of(layer: int, experts: list[int], device):
+    """The listed experts of one layer, in that order (same bytes as ``_ep_bank`` gives them)."""
+    import torch
+
+    chunks = sorted({e // EP_CHUNK for e in experts})
+    full = {c: _ep_bank(layer, range(c * EP_CHUNK, (c + 1) * EP_CHUNK), device) for c in chunks}
+    return {n: torch.stack([full[e // EP_CHUNK][n][e % EP_CHUNK] for e in experts]) for n in full[chunks[0]]}
+
+
 def _ep_routes(layers: int, device):
     import torch
 
@@ -558,23 +567,29 @@ def run_ep(args) -> None:
     import torch.distributed as dist
 
     from drama_b200 import synthetic
-    from drama_b200.expert_parallel import ExpertParallelMoE, nccl_all_to_all, shard_experts, shard_tokens
+    from drama_b200.expert_parallel import (ExpertParallelMoE, balanced_placement, experts_of_rank, nccl_all_to_all,
+                                            shard_tokens)
 
     world, rank, device, gpu_id = _dist_setup()
     t0 = time.perf_counter()
-    experts = shard_experts(EXPERTS, world, rank)
     rows = shard_tokens(EP_TOKENS, world, rank)
 
     class Bank:
         def __init__(self, d):
             self.__dict__.update(d)
 
-    banks = [Bank(_ep_bank(l, experts, device)) for l in range(args.layers)]
     routes = _ep_routes(args.layers, device)
+    # experts placed on ranks by their observed route counts (balanced rows per rank)
+    placements, banks = [], []
+    for l in range(args.layers):
+        counts = torch.bincount(routes[l][0].reshape(-1).long(), minlength=EXPERTS).tolist()
+        placement = balanced_placement(counts, world) if world > 1 else list(range(EXPERTS))
+        placements.append(torch.tensor(placement, dtype=torch.int32, device=device) if world > 1 else None)
+        banks.append(Bank(_ep_bank_of(l, experts_of_rank(placement, world, rank), device)))
     local_routes = [(i[rows].contiguous(), w[rows].contiguous()) for i, w in routes]
     h0 = synthetic.hidden_states(EP_TOKENS, HIDDEN, 97_000, device=device)[rows].contiguous()
     model = ExpertParallelMoE(banks, experts=EXPERTS, top_k=TOP_K, tokens=EP_TOKENS // world, ranks=world,
-                              rank=rank, all_to_all=nccl_all_to_all() if world > 1 else None)
+                              rank=rank, all_to_all=nccl_all_to_all() if world > 1 else None, placements=placements)
     x = h0.clone()
     model.step(x, local_routes)                       # eager pass: checks, lazy init
     torch.cuda.synchronize(device)
@@ -625,9 +640,9 @@ def run_ep(args) -> None:
     # Algorithmic weight bytes: every expert touched on this rank, every layer.
     nbytes = synthetic.expert_nbytes_fp8(HIDDEN, INTER)
     touched = 0
-    for ids, _ in routes:
-        u = torch.unique(ids.long())
-        touched += int(((u >= experts.start) & (u < experts.stop)).sum())
+    for l, (ids, _) in enumerate(routes):
+        held = set(experts_of_rank(placements[l].tolist(), world, rank)) if world > 1 else set(range(EXPERTS))
+        touched += len(set(torch.unique(ids.long()).tolist()) & held)
     step_bytes = touched * nbytes + 2 * (EP_TOKENS // world) * HIDDEN * 2 * args.layers
     peaks = measured_peaks()
     achieved = step_bytes / (ms / 1000.0) / 1e9
@@ -644,6 +659,7 @@ def run_ep(args) -> None:
                                 f"per GPU, NCCL all-to-all dispatch/combine, one CUDA graph per step"),
                    "tokens": EP_TOKENS, "layers": args.layers, "experts_per_gpu": EXPERTS // world,
                    "parallelism": f"ep{world}", "capacity_rows_per_peer": model.capacity,
+                   "placement": "by observed route counts (balanced rows per rank)" if world > 1 else "all local",
                    "l2": "inputs larger than L2: every step reads the touched experts of 48 layers"},
         "roofline": {"kernel": "one EP decode step on one rank (dispatch, all-to-alls, grouped GEMMs, combine)",
                      "bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",

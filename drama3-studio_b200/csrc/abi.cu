@@ -436,11 +436,14 @@ size_t drama_b200_expert_rows_workspace_bytes(int64_t rows, int hidden, int inte
     return expert_rows_workspace_layout(rows, hidden, intermediate, experts, nullptr, nullptr);
 }
 
-int drama_b200_fp8_expert_rows(const DramaB200Fp8Bank* bank, const void* x, int64_t rows, const void* ids,
-                               int ids_dtype, void* out, void* workspace, size_t workspace_bytes, void* stream) {
-    if (!bank || !x || !ids || !out) return fail("bank, x, ids and out are required");
+int drama_b200_fp8_expert_rows(const DramaB200Fp8Bank* bank, const void* x, int64_t x_row_stride, int64_t rows,
+                               const void* ids, int ids_dtype, void* out, void* workspace, size_t workspace_bytes,
+                               void* stream) {
+    if (!bank || !x || !out) return fail("bank, x and out are required");
     const DramaB200Fp8Bank& b = *bank;
-    if (!index_dtype(ids_dtype)) return fail("expert IDs must be int32 or int64");
+    if (ids && !index_dtype(ids_dtype)) return fail("expert IDs must be int32 or int64");
+    if (x_row_stride % 8 || x_row_stride < b.hidden || (!ids && x_row_stride < b.hidden + 8))
+        return fail("x_row_stride must be a multiple of 8, at least hidden (hidden + 8 for tagged rows)");
     if (rows < 0 || rows > (int64_t(1) << 24)) return fail("rows must be in [0, 2^24]");
     if (b.hidden % 128 || b.hidden < 128 || b.intermediate % 128 || b.intermediate < 128)
         return fail("hidden and intermediate must be positive multiples of 128");
@@ -454,8 +457,8 @@ int drama_b200_fp8_expert_rows(const DramaB200Fp8Bank* bank, const void* x, int6
         return fail("FP8 weight strides are smaller than the bank geometry");
     if (b.w13_scale_row_stride < b.hidden / 128 || b.w2_scale_row_stride < b.intermediate / 128)
         return fail("FP8 scale strides are smaller than the bank geometry");
-    const size_t xb = static_cast<size_t>(rows) * b.hidden * 2;
-    if (overlaps(out, xb, x, xb)) return fail("output must not overlap the hidden rows");
+    const size_t xb = static_cast<size_t>(rows) * x_row_stride * 2, ob = static_cast<size_t>(rows) * b.hidden * 2;
+    if (overlaps(out, ob, x, xb)) return fail("output must not overlap the hidden rows");
     if (rows == 0) return 0;
     int sms = 0;
     if (sm_count_current(&sms)) return -1;
@@ -465,17 +468,19 @@ int drama_b200_fp8_expert_rows(const DramaB200Fp8Bank* bank, const void* x, int6
     if (reinterpret_cast<uintptr_t>(workspace) & 255u) return fail("workspace must be 256-byte aligned");
     RowsWorkspace ws;
     expert_rows_workspace_layout(rows, b.hidden, b.intermediate, b.slots, static_cast<char*>(workspace), &ws);
-    const cudaError_t err = expert_rows_launch(b, x, rows, ids, ids_dtype, out, ws, sms,
+    const cudaError_t err = expert_rows_launch(b, x, x_row_stride, rows, ids, ids_dtype, out, ws, sms,
                                                static_cast<cudaStream_t>(stream));
     if (err != cudaSuccess) return fail("expert-rows launch failed: %s", cudaGetErrorString(err));
     return 0;
 }
 
 int drama_b200_ep_dispatch(const void* hidden, int64_t tokens, int hidden_size, const void* ids, int ids_dtype,
-                           int top_k, int experts, int ranks, int64_t capacity, void* send_rows, int32_t* send_ids,
-                           int32_t* pair_rows, int32_t* status, void* stream) {
-    if (!hidden || !ids || !send_rows || !send_ids || !pair_rows)
-        return fail("hidden, ids, send_rows, send_ids and pair_rows are required");
+                           int top_k, int experts, int ranks, const int32_t* placement, int64_t capacity,
+                           void* send_rows, int64_t send_row_stride, int32_t* send_ids, int32_t* pair_rows,
+                           int32_t* status, void* stream) {
+    if (!hidden || !ids || !send_rows || !pair_rows) return fail("hidden, ids, send_rows and pair_rows are required");
+    if (send_row_stride % 8 || send_row_stride < hidden_size || (!send_ids && send_row_stride < hidden_size + 8))
+        return fail("send_row_stride must be a multiple of 8, at least hidden (hidden + 8 without send_ids)");
     if (!index_dtype(ids_dtype)) return fail("expert IDs must be int32 or int64");
     if (tokens < 0 || top_k < 1 || top_k > 32) return fail("tokens must be >= 0 and top_k in [1, 32]");
     if (tokens * top_k > (int64_t(1) << 24)) return fail("dispatch supports at most 2^24 (token, slot) pairs");
@@ -486,13 +491,13 @@ int drama_b200_ep_dispatch(const void* hidden, int64_t tokens, int hidden_size, 
     if (capacity < 1 || capacity * ranks > INT32_MAX) return fail("capacity must be in [1, 2^31 / ranks)");
     if (!aligned16(hidden) || !aligned16(send_rows)) return fail("hidden rows must start on 16-byte boundaries");
     const size_t hb = static_cast<size_t>(tokens) * hidden_size * 2;
-    const size_t sb = static_cast<size_t>(capacity) * ranks * hidden_size * 2;
+    const size_t sb = static_cast<size_t>(capacity) * ranks * send_row_stride * 2;
     if (overlaps(send_rows, sb, hidden, hb)) return fail("send rows must not overlap the hidden states");
     int sms = 0;
     if (sm_count_current(&sms)) return -1;
     const cudaError_t err = ep_dispatch_launch(hidden, tokens, hidden_size, ids, ids_dtype, top_k, experts, ranks,
-                                               capacity, send_rows, send_ids, pair_rows, status, sms,
-                                               static_cast<cudaStream_t>(stream));
+                                               placement, capacity, send_rows, send_row_stride, send_ids, pair_rows,
+                                               status, sms, static_cast<cudaStream_t>(stream));
     if (err != cudaSuccess) return fail("dispatch launch failed: %s", cudaGetErrorString(err));
     return 0;
 }

@@ -1,6 +1,8 @@
 // Expert-parallel dispatch and combine around the grouped expert GEMMs.
 //
-// Experts are sharded in contiguous blocks of E/G over G ranks. Each rank owns
+// Experts are sharded in blocks of E/G over G ranks: contiguous by id, or by a
+// placement table (rank-major position of every expert, e.g. chosen from
+// observed route counts so that the ranks receive similar numbers of rows). Each rank owns
 // a slice of the tokens; every (token, slot) pair whose expert lives on rank d
 // sends the token's hidden row to d, d runs its experts on what it received,
 // and the bf16 down rows travel back to the owner, which sums them in route
@@ -23,20 +25,36 @@ namespace drama {
 namespace {
 
 constexpr int kPlanThreads = 1024;
+
+// Rank-major position of pair p's expert: placement[id] (a permutation of
+// [0, experts) giving each expert's rank * E/G + local id), or id itself when
+// placement is null; -1 for an id or a placement entry outside [0, experts).
+__device__ __forceinline__ int64_t ep_position(const void* ids, int ids_dtype, int64_t p, int experts,
+                                               const int32_t* placement) {
+    const int64_t id = load_index(ids, ids_dtype, p);
+    if (id < 0 || id >= experts) return -1;
+    const int64_t pos = placement ? static_cast<int64_t>(__ldg(placement + id)) : id;
+    return pos >= 0 && pos < experts ? pos : -1;
+}
 constexpr int kPlanWarps = kPlanThreads / 32;
 
 // One CTA: destination rank of every pair, its row in the send buffer (pairs
 // keep their order inside a destination), and the receiver-local expert id of
 // every send row. Deterministic: the same ids always give the same rows.
 __global__ void __launch_bounds__(kPlanThreads)
-ep_plan_kernel(const void* ids, int ids_dtype, int64_t pairs, int experts, int ranks, int64_t cap,
-               int32_t* send_ids, int32_t* pair_rows, int32_t* status) {
+ep_plan_kernel(const void* ids, int ids_dtype, int64_t pairs, int experts, int ranks, const int32_t* placement,
+               int64_t cap, __nv_bfloat16* send_rows, int64_t row_stride, int H, int32_t* send_ids,
+               int32_t* pair_rows, int32_t* status) {
     __shared__ int warp_tot[kMaxEpRanks][kPlanWarps];
     __shared__ int dropped, overflow;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int per_rank = experts / ranks;
     if (tid == 0) dropped = overflow = 0;
-    for (int64_t i = tid; i < ranks * cap; i += kPlanThreads) send_ids[i] = per_rank;
+    // the receiver-local id of every send row: in send_ids, or in the row's tail
+    auto id_slot = [&](int64_t row) -> int32_t* {
+        return send_ids ? send_ids + row : reinterpret_cast<int32_t*>(send_rows + row * row_stride + H);
+    };
+    for (int64_t i = tid; i < ranks * cap; i += kPlanThreads) *id_slot(i) = per_rank;
     const int64_t chunk = (pairs + kPlanThreads - 1) / kPlanThreads;
     const int64_t p0 = min(pairs, tid * chunk), p1 = min(pairs, p0 + chunk);
     int count[kMaxEpRanks];
@@ -44,9 +62,9 @@ ep_plan_kernel(const void* ids, int ids_dtype, int64_t pairs, int experts, int r
     for (int d = 0; d < kMaxEpRanks; ++d) count[d] = 0;
     int bad = 0;
     for (int64_t p = p0; p < p1; ++p) {
-        const int64_t id = load_index(ids, ids_dtype, p);
-        if (id < 0 || id >= experts) { ++bad; continue; }
-        const int d = static_cast<int>(id / per_rank);
+        const int64_t pos = ep_position(ids, ids_dtype, p, experts, placement);
+        if (pos < 0) { ++bad; continue; }
+        const int d = static_cast<int>(pos / per_rank);
 #pragma unroll
         for (int r = 0; r < kMaxEpRanks; ++r) count[r] += (r == d);
     }
@@ -78,17 +96,17 @@ ep_plan_kernel(const void* ids, int ids_dtype, int64_t pairs, int experts, int r
     for (int d = 0; d < kMaxEpRanks; ++d) base[d] += warp_tot[d][warp];
     int over = 0;
     for (int64_t p = p0; p < p1; ++p) {
-        const int64_t id = load_index(ids, ids_dtype, p);
+        const int64_t pos = ep_position(ids, ids_dtype, p, experts, placement);
         int32_t row = -1;
-        if (id >= 0 && id < experts) {
-            const int d = static_cast<int>(id / per_rank);
+        if (pos >= 0) {
+            const int d = static_cast<int>(pos / per_rank);
             int slot = 0;
 #pragma unroll
             for (int r = 0; r < kMaxEpRanks; ++r)
                 if (r == d) slot = base[r]++;
             if (slot < cap) {
                 row = static_cast<int32_t>(d * cap + slot);
-                send_ids[row] = static_cast<int32_t>(id - static_cast<int64_t>(d) * per_rank);
+                *id_slot(row) = static_cast<int32_t>(pos - static_cast<int64_t>(d) * per_rank);
             } else {
                 ++over;
             }
@@ -106,7 +124,7 @@ ep_plan_kernel(const void* ids, int ids_dtype, int64_t pairs, int experts, int r
 
 // send_rows[pair_rows[p]] = hidden[p / top_k], 16 bytes per thread step.
 __global__ void ep_pack_kernel(const __nv_bfloat16* hidden, int64_t pairs, int top_k, int H,
-                               const int32_t* pair_rows, __nv_bfloat16* send_rows) {
+                               const int32_t* pair_rows, __nv_bfloat16* send_rows, int64_t row_stride) {
     const int vec = H / 8;
     const int64_t n = pairs * vec;
     for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
@@ -116,7 +134,7 @@ __global__ void ep_pack_kernel(const __nv_bfloat16* hidden, int64_t pairs, int t
         const int32_t row = __ldg(pair_rows + p);
         if (row < 0) continue;
         const uint4 q = __ldg(reinterpret_cast<const uint4*>(hidden + (p / top_k) * H + c));
-        *reinterpret_cast<uint4*>(send_rows + static_cast<int64_t>(row) * H + c) = q;
+        *reinterpret_cast<uint4*>(send_rows + static_cast<int64_t>(row) * row_stride + c) = q;
     }
 }
 
@@ -173,15 +191,17 @@ int grid_for(int64_t work, int sm_count) {
 }  // namespace
 
 cudaError_t ep_dispatch_launch(const void* hidden, int64_t tokens, int H, const void* ids, int ids_dtype, int top_k,
-                               int experts, int ranks, int64_t cap, void* send_rows, int32_t* send_ids,
-                               int32_t* pair_rows, int32_t* status, int sm_count, cudaStream_t s) {
+                               int experts, int ranks, const int32_t* placement, int64_t cap, void* send_rows,
+                               int64_t row_stride, int32_t* send_ids, int32_t* pair_rows, int32_t* status,
+                               int sm_count, cudaStream_t s) {
     const int64_t pairs = tokens * top_k;
-    ep_plan_kernel<<<1, kPlanThreads, 0, s>>>(ids, ids_dtype, pairs, experts, ranks, cap, send_ids, pair_rows,
-                                              status);
+    ep_plan_kernel<<<1, kPlanThreads, 0, s>>>(ids, ids_dtype, pairs, experts, ranks, placement, cap,
+                                              static_cast<__nv_bfloat16*>(send_rows), row_stride, H, send_ids,
+                                              pair_rows, status);
     if (pairs > 0)
         ep_pack_kernel<<<grid_for(pairs * (H / 8), sm_count), 256, 0, s>>>(
             static_cast<const __nv_bfloat16*>(hidden), pairs, top_k, H, pair_rows,
-            static_cast<__nv_bfloat16*>(send_rows));
+            static_cast<__nv_bfloat16*>(send_rows), row_stride);
     return cudaGetLastError();
 }
 

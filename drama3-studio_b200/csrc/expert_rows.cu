@@ -73,15 +73,20 @@ __device__ __forceinline__ uint4 pack_f16x8(const float (&v)[8], float inv) {
     return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
-// bf16 rows [rows, H] -> f16 rows scaled by 2^-e per 64-wide block, and 2^e.
-// Eight threads per block (16 bytes each); the block maximum by shuffles.
-__global__ void rows_to_f16_kernel(const __nv_bfloat16* x, int64_t rows, int H, __half* xh, float* xs) {
+// bf16 rows (row r at x + r * x_stride) -> f16 rows [rows, H] scaled by 2^-e
+// per 64-wide block, and 2^e. Eight threads per block (16 bytes each); the
+// block maximum by shuffles. With `ids` set, the int32 at element H of each
+// row (a tagged row) is copied to ids[r].
+__global__ void rows_to_f16_kernel(const __nv_bfloat16* x, int64_t x_stride, int64_t rows, int H, __half* xh,
+                                   float* xs, int32_t* ids) {
     const int64_t n = rows * (H / 8);
     const int64_t n_pad = (n + 31) & ~int64_t(31);   // whole warps iterate together (the shuffles)
     for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n_pad;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
         const bool ok = i < n;
-        const uint4 q = ok ? __ldg(reinterpret_cast<const uint4*>(x) + i) : make_uint4(0u, 0u, 0u, 0u);
+        const int64_t r = i / (H / 8), c = i - r * (H / 8);
+        const uint4 q = ok ? __ldg(reinterpret_cast<const uint4*>(x + r * x_stride) + c) : make_uint4(0u, 0u, 0u, 0u);
+        if (ok && ids && c == 0) ids[r] = *reinterpret_cast<const int32_t*>(x + r * x_stride + H);
         const uint32_t w[4] = {q.x, q.y, q.z, q.w};
         float v[8];
         float m = 0.0f;
@@ -354,12 +359,14 @@ size_t expert_rows_workspace_layout(int64_t rows, int hidden, int intermediate, 
     w.xs = reinterpret_cast<float*>(take(static_cast<size_t>(rows) * (hidden / 64) * 4));
     w.h = reinterpret_cast<__half*>(take(static_cast<size_t>(rows) * intermediate * 2));
     w.hs = reinterpret_cast<float*>(take(static_cast<size_t>(rows) * (intermediate / 64) * 4));
+    w.ids = reinterpret_cast<int32_t*>(take(static_cast<size_t>(rows) * 4));
     if (ws) *ws = w;
     return off;
 }
 
-cudaError_t expert_rows_launch(const DramaB200Fp8Bank& bank, const void* x, int64_t rows, const void* ids,
-                               int ids_dtype, void* out, const RowsWorkspace& ws, int sm_count, cudaStream_t s) {
+cudaError_t expert_rows_launch(const DramaB200Fp8Bank& bank, const void* x, int64_t x_stride, int64_t rows,
+                               const void* ids, int ids_dtype, void* out, const RowsWorkspace& ws, int sm_count,
+                               cudaStream_t s) {
     static bool configured = false;  // benign race: identical values
     if (!configured) {
         cudaError_t err = cudaFuncSetAttribute(swap_gemm_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -369,12 +376,13 @@ cudaError_t expert_rows_launch(const DramaB200Fp8Bank& bank, const void* x, int6
         if (err != cudaSuccess) return err;
         configured = true;
     }
-    PermuteArgs pa{ids, ids_dtype, rows, bank.slots, ws.order, ws.counts, ws.offsets, ws.status};
-    cudaError_t err = permute_routes(pa, s);
-    if (err != cudaSuccess) return err;
     rows_to_f16_kernel<<<grid_for(rows * (bank.hidden / 8), sm_count), 256, 0, s>>>(
-        static_cast<const __nv_bfloat16*>(x), rows, bank.hidden, ws.xh, ws.xs);
-    err = cudaGetLastError();
+        static_cast<const __nv_bfloat16*>(x), x_stride, rows, bank.hidden, ws.xh, ws.xs, ids ? nullptr : ws.ids);
+    cudaError_t err = cudaGetLastError();
+    if (err != cudaSuccess) return err;
+    PermuteArgs pa{ids ? ids : ws.ids, ids ? ids_dtype : DRAMA_B200_I32, rows, bank.slots, ws.order, ws.counts,
+                   ws.offsets, ws.status};
+    err = permute_routes(pa, s);
     if (err != cudaSuccess) return err;
     SwapArgs a{};
     a.bank = bank;

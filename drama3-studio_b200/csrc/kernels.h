@@ -176,17 +176,20 @@ struct RowsWorkspace {
     float* xs;                // [rows][H / 64] their scales (powers of two)
     __half* h;                // [rows][I] SwiGLU activations, sorted, f16 scaled per 64 columns
     float* hs;                // [rows][I / 64]
+    int32_t* ids;             // [rows] expert ids taken from tagged rows
 };
 size_t expert_rows_workspace_layout(int64_t rows, int hidden, int intermediate, int experts, char* base,
                                     RowsWorkspace* ws);
-cudaError_t expert_rows_launch(const DramaB200Fp8Bank& bank, const void* x, int64_t rows, const void* ids,
-                               int ids_dtype, void* out, const RowsWorkspace& ws, int sm_count, cudaStream_t s);
+cudaError_t expert_rows_launch(const DramaB200Fp8Bank& bank, const void* x, int64_t x_stride, int64_t rows,
+                               const void* ids, int ids_dtype, void* out, const RowsWorkspace& ws, int sm_count,
+                               cudaStream_t s);
 
 // Expert-parallel exchange (expert_parallel.cu).
 constexpr int kMaxEpRanks = 8;
 cudaError_t ep_dispatch_launch(const void* hidden, int64_t tokens, int H, const void* ids, int ids_dtype, int top_k,
-                               int experts, int ranks, int64_t cap, void* send_rows, int32_t* send_ids,
-                               int32_t* pair_rows, int32_t* status, int sm_count, cudaStream_t s);
+                               int experts, int ranks, const int32_t* placement, int64_t cap, void* send_rows,
+                               int64_t row_stride, int32_t* send_ids, int32_t* pair_rows, int32_t* status,
+                               int sm_count, cudaStream_t s);
 cudaError_t ep_combine_launch(const void* rows, int64_t row_count, const int32_t* pair_rows, const void* weights, int weights_dtype,
                               int64_t tokens, int top_k, int H, const void* residual, void* out, int sm_count,
                               cudaStream_t s);

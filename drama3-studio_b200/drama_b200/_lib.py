@@ -132,11 +132,12 @@ class Library:
         dll.drama_b200_stage_copies.restype = c_int
         dll.drama_b200_expert_rows_workspace_bytes.argtypes = [c_int64, c_int, c_int, c_int]
         dll.drama_b200_expert_rows_workspace_bytes.restype = c_size_t
-        dll.drama_b200_fp8_expert_rows.argtypes = [ctypes.POINTER(Fp8Bank), c_void_p, c_int64, c_void_p, c_int,
-                                                   c_void_p, c_void_p, c_size_t, c_void_p]
+        dll.drama_b200_fp8_expert_rows.argtypes = [ctypes.POINTER(Fp8Bank), c_void_p, c_int64, c_int64, c_void_p,
+                                                   c_int, c_void_p, c_void_p, c_size_t, c_void_p]
         dll.drama_b200_fp8_expert_rows.restype = c_int
         dll.drama_b200_ep_dispatch.argtypes = [c_void_p, c_int64, c_int, c_void_p, c_int, c_int, c_int, c_int,
-                                               c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]
+                                               c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_void_p,
+                                               c_void_p]
         dll.drama_b200_ep_dispatch.restype = c_int
         dll.drama_b200_ep_combine.argtypes = [c_void_p, c_int64, c_void_p, c_void_p, c_int, c_int64, c_int, c_int,
                                               c_void_p, c_void_p, c_void_p]

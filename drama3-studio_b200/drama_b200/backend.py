@@ -323,8 +323,8 @@ def fp8_expert_rows(x: Tensor, ids: Tensor, staged) -> Tensor:
     nbytes = lib.dll.drama_b200_expert_rows_workspace_bytes(x.shape[0], hidden, bank.intermediate, bank.slots)
     ws = _PREFILL_WORKSPACES.get(x.device, nbytes)
     lib.check(lib.dll.drama_b200_fp8_expert_rows(
-        ctypes.byref(bank), x.data_ptr(), x.shape[0], ids.data_ptr(), _lib.DTYPE_CODES[ids.dtype], out.data_ptr(),
-        ws.data_ptr(), ws.numel(), _lib.stream_handle(x.device)))
+        ctypes.byref(bank), x.data_ptr(), hidden, x.shape[0], ids.data_ptr(), _lib.DTYPE_CODES[ids.dtype],
+        out.data_ptr(), ws.data_ptr(), ws.numel(), _lib.stream_handle(x.device)))
     del keep
     return out
 

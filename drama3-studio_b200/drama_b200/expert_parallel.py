@@ -6,10 +6,11 @@ are split into G contiguous blocks of E/G, rank r holding block r, and each
 rank owns T/G of the T tokens. One layer on rank r:
 
 1. ``drama_b200_ep_dispatch``: every (token, slot) pair's hidden row goes into
-   the send block of the rank that owns its expert, with the receiver-local
-   expert id beside it (fixed ``capacity`` rows per destination, so nothing
-   has to be known on the host and the step can be captured in a CUDA graph).
-2. all-to-all of the rows and of the ids (NCCL over NVLink).
+   the send block of the rank that owns its expert, tagged with the
+   receiver-local expert id in its last 16 bytes (fixed ``capacity`` rows per
+   destination, so nothing has to be known on the host and the step can be
+   captured in a CUDA graph).
+2. one all-to-all of the tagged rows (NCCL over NVLink).
 3. ``drama_b200_fp8_expert_rows`` on the received rows: each row's bf16 down
    projection through the swap-AB grouped GEMMs, built for the few rows per
    expert of a decode batch (unused rows are dropped by their id).
@@ -39,6 +40,7 @@ from . import _lib
 from .backend import _fp8_bank
 
 AllToAll = Callable[[Tensor, Tensor], None]
+TAG = 8   # bf16 elements after each exchanged hidden row: the int32 local expert id and padding to 16 bytes
 
 
 def shard_experts(experts: int, ranks: int, rank: int) -> range:
@@ -59,6 +61,37 @@ def shard_tokens(tokens: int, ranks: int, rank: int) -> slice:
     return slice(rank * per, (rank + 1) * per)
 
 
+def balanced_placement(counts: Sequence[int], ranks: int) -> list[int]:
+    """Rank-major positions that even out the rows each rank receives.
+
+    ``counts[e]`` is how many (token, slot) pairs expert e got (observed
+    routes, as the reference's host-budget / hot-cache logic counts them).
+    Experts are taken in decreasing count (ties by id) and each goes to the
+    rank with the fewest rows so far that still has a free slot; its local id
+    is its arrival order on that rank. Returns ``placement`` with
+    ``placement[e] = rank * E/G + local``.
+    """
+    experts = len(counts)
+    per = len(shard_experts(experts, ranks, 0))
+    load = [0] * ranks
+    fill = [0] * ranks
+    placement = [0] * experts
+    for e in sorted(range(experts), key=lambda x: (-int(counts[x]), x)):
+        r = min((r for r in range(ranks) if fill[r] < per), key=lambda r: (load[r], r))
+        placement[e] = r * per + fill[r]
+        fill[r] += 1
+        load[r] += int(counts[e])
+    return placement
+
+
+def experts_of_rank(placement: Sequence[int], ranks: int, rank: int) -> list[int]:
+    """Global ids of the experts ``rank`` holds, in local-id order."""
+    experts = len(placement)
+    per = len(shard_experts(experts, ranks, rank))
+    local = {p - rank * per: e for e, p in enumerate(placement) if p // per == rank}
+    return [local[i] for i in range(per)]
+
+
 def nccl_all_to_all(group=None) -> AllToAll:
     """Equal-split all-to-all on ``group`` (rows travel as int32 words)."""
     import torch.distributed as dist
@@ -73,11 +106,9 @@ def nccl_all_to_all(group=None) -> AllToAll:
 class ExchangeBuffers:
     """Per-rank scratch of one layer, reused by every layer and step."""
 
-    send_rows: Tensor     # [G*cap, H] bf16
-    send_ids: Tensor      # [G*cap] int32
+    send_rows: Tensor     # [G*cap, H + 8] bf16: hidden row, then the local expert id (int32) and padding
     pair_rows: Tensor     # [T_l*k] int32
-    recv_rows: Tensor     # [G*cap, H] bf16
-    recv_ids: Tensor      # [G*cap] int32
+    recv_rows: Tensor     # [G*cap, H + 8] bf16
     expert_rows: Tensor   # [G*cap, H] bf16
     back_rows: Tensor     # [G*cap, H] bf16
     status: Tensor        # [4] int32
@@ -88,12 +119,15 @@ class ExpertParallelMoE:
     """One rank's share of an expert-parallel FP8 MoE layer stack.
 
     ``banks[l]`` is this rank's slice of layer ``l``: an ``ExpertStore``-shaped
-    FP8 bank (the four role tensors) of the E/G experts ``shard_experts``
-    gives, indexed by local id.
+    FP8 bank (the four role tensors) of its E/G experts, indexed by local id:
+    those ``shard_experts`` gives, or with ``placements[l]`` (int32 device
+    tensor of rank-major positions, see ``balanced_placement``) those
+    ``experts_of_rank`` gives.
     """
 
     def __init__(self, banks: Sequence, *, experts: int, top_k: int, tokens: int, ranks: int = 1, rank: int = 0,
-                 all_to_all: AllToAll | None = None, capacity: int | None = None) -> None:
+                 all_to_all: AllToAll | None = None, capacity: int | None = None,
+                 placements: Sequence[Tensor | None] | None = None) -> None:
         if not banks:
             raise ValueError("At least one layer bank is required")
         self.ranks, self.rank = ranks, rank
@@ -115,6 +149,12 @@ class ExpertParallelMoE:
             if bank.w13_weight.shape[0] != self.local_experts:
                 raise ValueError(f"Each bank must hold this rank's {self.local_experts} experts")
             self._banks.append(_fp8_bank(bank, self.hidden))
+        if placements is not None and len(placements) != len(banks):
+            raise ValueError("One placement (or None) per layer bank")
+        self.placements = list(placements) if placements is not None else [None] * len(banks)
+        for pl in self.placements:
+            if pl is not None and (pl.dtype != torch.int32 or tuple(pl.shape) != (experts,)):
+                raise ValueError(f"A placement is an int32 tensor of {experts} rank-major positions")
         self.lib = _lib.library()
         self.buffers = self._allocate()
 
@@ -125,9 +165,9 @@ class ExpertParallelMoE:
                                                                        self.local_experts)
         bf = dict(dtype=torch.bfloat16, device=dev)
         return ExchangeBuffers(
-            send_rows=torch.zeros(rows, H, **bf), send_ids=torch.empty(rows, dtype=torch.int32, device=dev),
+            send_rows=torch.zeros(rows, H + TAG, **bf),
             pair_rows=torch.empty(self.tokens * self.top_k, dtype=torch.int32, device=dev),
-            recv_rows=torch.zeros(rows, H, **bf), recv_ids=torch.empty(rows, dtype=torch.int32, device=dev),
+            recv_rows=torch.zeros(rows, H + TAG, **bf),
             expert_rows=torch.zeros(rows, H, **bf), back_rows=torch.zeros(rows, H, **bf),
             status=torch.zeros(4, dtype=torch.int32, device=dev),
             workspace=torch.zeros(max(ws_bytes, 256), dtype=torch.uint8, device=dev))
@@ -149,14 +189,13 @@ class ExpertParallelMoE:
         self._check_routes(h, ids, weights)
         out = torch.empty_like(h) if out is None else out
         b = self.buffers
-        self._dispatch(h, ids)
+        self._dispatch(h, ids, self.placements[layer])
         if self.ranks > 1:
             self.all_to_all(b.recv_rows.view(torch.int32), b.send_rows.view(torch.int32))
-            self.all_to_all(b.recv_ids, b.send_ids)
-            recv_rows, recv_ids = b.recv_rows, b.recv_ids
+            recv_rows = b.recv_rows
         else:
-            recv_rows, recv_ids = b.send_rows, b.send_ids
-        self._run_experts(layer, recv_rows, recv_ids, b.expert_rows)
+            recv_rows = b.send_rows
+        self._run_experts(layer, recv_rows, b.expert_rows)
         if self.ranks > 1:
             self.all_to_all(b.back_rows.view(torch.int32), b.expert_rows.view(torch.int32))
             back = b.back_rows
@@ -166,18 +205,19 @@ class ExpertParallelMoE:
         return out
 
     # The three device steps (CUDA kernels of this library).
-    def _dispatch(self, h: Tensor, ids: Tensor) -> None:
+    def _dispatch(self, h: Tensor, ids: Tensor, placement: Tensor | None = None) -> None:
         b, lib = self.buffers, self.lib
         lib.check(lib.dll.drama_b200_ep_dispatch(
             h.data_ptr(), self.tokens, self.hidden, ids.data_ptr(), _lib.DTYPE_CODES[ids.dtype], self.top_k,
-            self.experts, self.ranks, self.capacity, b.send_rows.data_ptr(), b.send_ids.data_ptr(),
-            b.pair_rows.data_ptr(), b.status.data_ptr(), _lib.stream_handle(h.device)))
+            self.experts, self.ranks, _lib.ptr(placement), self.capacity, b.send_rows.data_ptr(),
+            self.hidden + TAG, None, b.pair_rows.data_ptr(), b.status.data_ptr(), _lib.stream_handle(h.device)))
 
-    def _run_experts(self, layer: int, rows: Tensor, ids: Tensor, out: Tensor) -> None:
+    def _run_experts(self, layer: int, rows: Tensor, out: Tensor) -> None:
+        """Down projections of the tagged ``rows`` (hidden values, then the local expert id)."""
         b, lib = self.buffers, self.lib
         bank, _ = self._banks[layer]
         lib.check(lib.dll.drama_b200_fp8_expert_rows(
-            ctypes.byref(bank), rows.data_ptr(), rows.shape[0], ids.data_ptr(), _lib.I32, out.data_ptr(),
+            ctypes.byref(bank), rows.data_ptr(), self.hidden + TAG, rows.shape[0], None, _lib.I32, out.data_ptr(),
             b.workspace.data_ptr(), b.workspace.numel(), _lib.stream_handle(rows.device)))
 
     def _combine(self, back: Tensor, weights: Tensor, h: Tensor, out: Tensor) -> None:
@@ -193,8 +233,8 @@ class ExpertParallelMoE:
         return h
 
     def launches_per_layer(self) -> int:
-        """Kernels of this library per layer: plan + pack, permute + 2 GEMMs, EP combine."""
-        return 6
+        """Kernels of this library per layer: plan + pack, row prep + permute + 2 GEMMs, EP combine."""
+        return 7
 
     def dropped(self) -> tuple[int, int]:
         """(pairs with an out-of-range id, pairs over capacity) of the last layer (synchronises)."""

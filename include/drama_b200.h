@@ -264,20 +264,22 @@ DRAMA_B200_API int drama_b200_fp8_decode_static(const DramaB200Fp8Bank* bank, co
  * f16 expansion of the E4M3 weights, block scales applied to fp32 partial
  * sums, activations as f16 with a power-of-two scale per 64 values. Rows whose id
  * is outside [0, slots) are not written (status[0] counts them, at
- * drama_b200_prefill_status_offset() in the workspace). x: [rows, hidden]
- * bf16; hidden and intermediate multiples of 128; rows <= 2^24. Each row's
- * result is independent of the other rows in the call.
+ * drama_b200_prefill_status_offset() in the workspace). x: rows of hidden
+ * bf16 values, row r at x + r * x_row_stride (elements, a multiple of 8);
+ * with ids == NULL each row is tagged: its expert id is the int32 at element
+ * `hidden` of the row (x_row_stride >= hidden + 8), as drama_b200_ep_dispatch
+ * writes them. hidden and intermediate multiples of 128; rows <= 2^24. Each
+ * row's result is independent of the other rows in the call.
  * ------------------------------------------------------------------------- */
 DRAMA_B200_API size_t drama_b200_expert_rows_workspace_bytes(int64_t rows, int hidden, int intermediate,
                                                              int experts);
 
-DRAMA_B200_API int drama_b200_fp8_expert_rows(const DramaB200Fp8Bank* bank, const void* x, int64_t rows,
-                                              const void* ids, int ids_dtype, void* out, void* workspace,
-                                              size_t workspace_bytes, void* stream);
+DRAMA_B200_API int drama_b200_fp8_expert_rows(const DramaB200Fp8Bank* bank, const void* x, int64_t x_row_stride,
+                                              int64_t rows, const void* ids, int ids_dtype, void* out,
+                                              void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------
- * Expert parallelism over G ranks (experts in contiguous blocks of E/G per
- * rank). The reference is single-GPU, so the exchange has no counterpart in
+ * Expert parallelism over G ranks (E/G experts per rank). The reference is single-GPU, so the exchange has no counterpart in
  * it; the two entries split the reference's partitioned expert call
  * (src/drama_low_vram/offload.py:1206-1276: group the (token, slot) pairs by
  * expert, run each expert on its rows, sum fp32 weighted rows in slot order at
@@ -285,19 +287,26 @@ DRAMA_B200_API int drama_b200_fp8_expert_rows(const DramaB200Fp8Bank* bank, cons
  *
  * drama_b200_ep_dispatch: for the local hidden rows [tokens, hidden_size]
  * (bf16) and their routes ids [tokens, top_k] (global expert ids), writes
- *   send_rows [ranks, capacity, hidden_size] bf16: the hidden row of every pair
- *     in the block of the rank owning its expert, pairs in order;
- *   send_ids [ranks, capacity] int32: the receiver-local expert id of each
- *     row (id - rank * E/G), or E/G for an unused row;
+ * the following. placement (int32 [experts], may be NULL) gives each expert's
+ * rank-major position, a permutation of [0, experts): expert e lives on rank
+ * placement[e] / (experts / ranks) as local id placement[e] % (experts /
+ * ranks); NULL means placement[e] = e (contiguous blocks).
+ *   send_rows [ranks, capacity] rows of send_row_stride bf16 elements (a
+ *     multiple of 8, >= hidden_size): the hidden row of every pair in the
+ *     block of the rank owning its expert, pairs in order;
+ *   the receiver-local expert id of each row, or E/G for an unused row: in
+ *     send_ids [ranks, capacity] int32, or when send_ids is NULL as the int32
+ *     at element hidden_size of the row itself (send_row_stride >=
+ *     hidden_size + 8), so that one all-to-all carries rows and ids;
  *   pair_rows [tokens * top_k] int32: the row of each pair in send_rows, -1
  *     for a pair whose id is outside [0, experts) or that did not fit;
  *   status[0] (int32, may be NULL) = pairs with an out-of-range id, status[1]
  *     = pairs beyond a destination's capacity (capacity = tokens * top_k
  *     never overflows).
- * After an all-to-all of send_rows / send_ids, drama_b200_fp8_prefill with
- * top_k 1 and unit weights on the received rows gives each row's bf16 down
- * projection (unused rows are dropped by their id); a second all-to-all
- * brings them back in the same positions.
+ * After an all-to-all of the tagged send rows, drama_b200_fp8_expert_rows
+ * (ids NULL) on the received rows gives each row's bf16 down projection
+ * (unused rows are dropped by their id); a second all-to-all brings them back
+ * in the same positions.
  *
  * drama_b200_ep_combine: out[t] = bf16(residual[t] + bf16(sum over slots s in
  * order of rows[pair_rows[t*k+s]] * weights[t*k+s])), fp32 products and sums
@@ -306,8 +315,9 @@ DRAMA_B200_API int drama_b200_fp8_expert_rows(const DramaB200Fp8Bank* bank, cons
  * or equal to out.
  * ------------------------------------------------------------------------- */
 DRAMA_B200_API int drama_b200_ep_dispatch(const void* hidden, int64_t tokens, int hidden_size, const void* ids,
-                                          int ids_dtype, int top_k, int experts, int ranks, int64_t capacity,
-                                          void* send_rows, int32_t* send_ids, int32_t* pair_rows,
+                                          int ids_dtype, int top_k, int experts, int ranks,
+                                          const int32_t* placement, int64_t capacity, void* send_rows,
+                                          int64_t send_row_stride, int32_t* send_ids, int32_t* pair_rows,
                                           int32_t* status, void* stream);
 
 DRAMA_B200_API int drama_b200_ep_combine(const void* rows, int64_t row_count, const int32_t* pair_rows,

@@ -56,25 +56,29 @@ def _cpu_model_class():
             super().__init__(banks, **kw)
             self.np_banks = [np_bank(vars(b)) for b in banks]
 
-        def _dispatch(self, h, ids):
+        def _dispatch(self, h, ids, placement=None):
             b, G, cap = self.buffers, self.ranks, self.capacity
             per = self.experts // G
-            b.send_ids.fill_(per)
+            pos = placement.tolist() if placement is not None else list(range(self.experts))
+            tags = b.send_rows.view(torch.int32)[:, self.hidden // 2]   # the int32 after each hidden row
+            tags.fill_(per)
             b.pair_rows.fill_(-1)
             fill = [0] * G
             for p, e in enumerate(ids.reshape(-1).tolist()):
                 if not 0 <= e < self.experts:
                     continue
-                d = e // per
+                d = pos[e] // per
                 if fill[d] >= cap:
                     continue
                 row = d * cap + fill[d]
                 fill[d] += 1
-                b.send_rows[row] = h[p // self.top_k]
-                b.send_ids[row] = e - d * per
+                b.send_rows[row, :self.hidden] = h[p // self.top_k]
+                tags[row] = pos[e] - d * per
                 b.pair_rows[p] = row
 
-        def _run_experts(self, layer, rows, ids, out):
+        def _run_experts(self, layer, rows, out):
+            ids = rows.view(torch.int32)[:, self.hidden // 2].clone()
+            rows = rows[:, :self.hidden]
             out.zero_()
             valid = [i for i, e in enumerate(ids.tolist()) if 0 <= e < self.local_experts]
             if valid:
@@ -95,17 +99,31 @@ def _cpu_model_class():
     return CpuExpertParallel
 
 
-def _rank_main(rank: int, world: int, port: int, out_dir: str) -> None:
+def _placements(routes, world):
+    from drama_b200.expert_parallel import balanced_placement
+
+    out = []
+    for ids, _ in routes:
+        counts = torch.bincount(ids.reshape(-1), minlength=E).tolist()
+        out.append(torch.tensor(balanced_placement(counts, world), dtype=torch.int32))
+    return out
+
+
+def _rank_main(rank: int, world: int, port: int, out_dir: str, balanced: bool) -> None:
     import torch.distributed as dist
 
-    from drama_b200.expert_parallel import nccl_all_to_all, shard_experts, shard_tokens
+    from drama_b200.expert_parallel import experts_of_rank, nccl_all_to_all, shard_experts, shard_tokens
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         banks, routes, h = _inputs()
-        experts = shard_experts(E, world, rank)
-        local = [{n: v[experts.start:experts.stop] for n, v in b.items()} for b in banks]
+        placements = _placements(routes, world) if balanced else None
+        local = []
+        for l, b in enumerate(banks):
+            held = experts_of_rank(placements[l].tolist(), world, rank) if balanced else \
+                list(shard_experts(E, world, rank))
+            local.append({n: v[held] for n, v in b.items()})
         rows = shard_tokens(T, world, rank)
 
         class Bank:
@@ -113,7 +131,7 @@ def _rank_main(rank: int, world: int, port: int, out_dir: str) -> None:
                 self.__dict__.update(d)
 
         model = _cpu_model_class()([Bank(b) for b in local], experts=E, top_k=K, tokens=T // world, ranks=world,
-                                   rank=rank, all_to_all=nccl_all_to_all())
+                                   rank=rank, all_to_all=nccl_all_to_all(), placements=placements)
         x = h[rows].contiguous()
         model.step(x, [(ids[rows].contiguous(), w[rows].contiguous()) for ids, w in routes])
         torch.save(x, os.path.join(out_dir, f"rank{rank}.pt"))
@@ -127,11 +145,12 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def test_two_gloo_ranks_match_the_single_process_oracle(tmp_path):
+@pytest.mark.parametrize("balanced", [False, True])
+def test_two_gloo_ranks_match_the_single_process_oracle(tmp_path, balanced):
     import torch.multiprocessing as mp
 
     world = 2
-    mp.spawn(_rank_main, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    mp.spawn(_rank_main, args=(world, _free_port(), str(tmp_path), balanced), nprocs=world, join=True)
     banks, routes, h = _inputs()
     expected = _oracle_stack(banks, routes, h)
     got = np.concatenate([np_f32(torch.load(tmp_path / f"rank{r}.pt")) for r in range(world)])
@@ -149,6 +168,19 @@ def test_single_rank_needs_no_exchange():
     x = h.clone()
     model.step(x, routes)
     assert np.array_equal(np_f32(x), _oracle_stack(banks, routes, h))
+
+
+def test_balanced_placement_evens_out_the_rows():
+    from drama_b200.expert_parallel import balanced_placement, experts_of_rank
+
+    counts = [100, 90, 10, 10, 5, 5, 1, 1]
+    placement = balanced_placement(counts, 2)
+    assert sorted(placement) == list(range(8))
+    loads = [sum(counts[e] for e in experts_of_rank(placement, 2, r)) for r in range(2)]
+    assert loads == [112, 110]                 # greedy by count, four experts per rank
+    assert experts_of_rank(placement, 2, 0)[0] == 0 and experts_of_rank(placement, 2, 1)[0] == 1
+    # contiguous blocks are the identity placement
+    assert experts_of_rank(list(range(8)), 4, 2) == [4, 5]
 
 
 def test_shard_helpers_and_argument_checks():

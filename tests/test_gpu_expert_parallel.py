@@ -46,17 +46,28 @@ def _inputs(device):
     return banks, routes, h
 
 
-def _model(banks, ranks=1, rank=0, tokens=T, all_to_all=None, capacity=None):
-    from drama_b200.expert_parallel import ExpertParallelMoE, shard_experts
+def _placements(routes, ranks, device):
+    from drama_b200.expert_parallel import balanced_placement
 
-    ex = shard_experts(E, ranks, rank)
-    local = [Bank({n: v[ex.start:ex.stop] for n, v in b.items()}) for b in banks]
+    return [torch.tensor(balanced_placement(torch.bincount(ids.reshape(-1).cpu(), minlength=E).tolist(), ranks),
+                         dtype=torch.int32, device=device) for ids, _ in routes]
+
+
+def _model(banks, ranks=1, rank=0, tokens=T, all_to_all=None, capacity=None, placements=None):
+    from drama_b200.expert_parallel import ExpertParallelMoE, experts_of_rank, shard_experts
+
+    local = []
+    for l, b in enumerate(banks):
+        held = experts_of_rank(placements[l].tolist(), ranks, rank) if placements is not None else \
+            list(shard_experts(E, ranks, rank))
+        local.append(Bank({n: v[held] for n, v in b.items()}))
     return ExpertParallelMoE(local, experts=E, top_k=K, tokens=tokens, ranks=ranks, rank=rank,
-                             all_to_all=all_to_all or (lambda o, i: None), capacity=capacity)
+                             all_to_all=all_to_all or (lambda o, i: None), capacity=capacity, placements=placements)
 
 
-def _dispatch_restated(h, ids, experts, ranks, cap):
+def _dispatch_restated(h, ids, experts, ranks, cap, placement=None):
     per = experts // ranks
+    pos = list(range(experts)) if placement is None else placement
     send_ids = np.full(ranks * cap, per, np.int32)
     pair_rows = np.full(ids.size, -1, np.int32)
     fill = [0] * ranks
@@ -65,19 +76,21 @@ def _dispatch_restated(h, ids, experts, ranks, cap):
         if not 0 <= e < experts:
             dropped += 1
             continue
-        d = e // per
+        d = pos[e] // per
         if fill[d] >= cap:
             overflow += 1
             continue
         row = d * cap + fill[d]
         fill[d] += 1
-        send_ids[row] = e - d * per
+        send_ids[row] = pos[e] - d * per
         pair_rows[p] = row
     return send_ids, pair_rows, (dropped, overflow)
 
 
-@pytest.mark.parametrize("ranks,cap", [(1, 37 * 8), (2, 37 * 8), (8, 37 * 8), (4, 20)])
-def test_dispatch_matches_its_restatement(cuda_device, ranks, cap):
+@pytest.mark.parametrize("ranks,cap,permuted,tagged", [(1, 37 * 8, False, False), (2, 37 * 8, False, True),
+                                                       (8, 37 * 8, False, False), (4, 20, False, True),
+                                                       (4, 37 * 8, True, True)])
+def test_dispatch_matches_its_restatement(cuda_device, ranks, cap, permuted, tagged):
     from drama_b200 import _lib
 
     lib = _lib.library()
@@ -85,24 +98,30 @@ def test_dispatch_matches_its_restatement(cuda_device, ranks, cap):
     tokens, top_k, experts = 37, 8, 128
     ids = torch.randint(-2, experts + 3, (tokens, top_k), generator=gen)
     h = torch.randn(tokens, 256, generator=gen).to(torch.bfloat16).to(cuda_device)
-    send_rows = torch.zeros(ranks * cap, 256, dtype=torch.bfloat16, device=cuda_device)
+    stride = 256 + 8 if tagged else 256
+    send_rows = torch.zeros(ranks * cap, stride, dtype=torch.bfloat16, device=cuda_device)
     send_ids = torch.empty(ranks * cap, dtype=torch.int32, device=cuda_device)
     pair_rows = torch.empty(tokens * top_k, dtype=torch.int32, device=cuda_device)
     status = torch.zeros(4, dtype=torch.int32, device=cuda_device)
+    placement = torch.randperm(experts, generator=gen).to(torch.int32) if permuted else None
+    d_place = placement.to(cuda_device) if permuted else None
     for dtype in (torch.int64, torch.int32):
         d_ids = ids.to(dtype).to(cuda_device)
         lib.check(lib.dll.drama_b200_ep_dispatch(
-            h.data_ptr(), tokens, 256, d_ids.data_ptr(), _lib.DTYPE_CODES[dtype], top_k, experts, ranks, cap,
-            send_rows.data_ptr(), send_ids.data_ptr(), pair_rows.data_ptr(), status.data_ptr(),
+            h.data_ptr(), tokens, 256, d_ids.data_ptr(), _lib.DTYPE_CODES[dtype], top_k, experts, ranks,
+            _lib.ptr(d_place), cap, send_rows.data_ptr(), stride, None if tagged else send_ids.data_ptr(),
+            pair_rows.data_ptr(), status.data_ptr(),
             _lib.stream_handle(cuda_device)))
         torch.cuda.synchronize()
-        want_ids, want_rows, (dropped, overflow) = _dispatch_restated(h, ids.numpy(), experts, ranks, cap)
-        assert np.array_equal(send_ids.cpu().numpy(), want_ids)
+        want_ids, want_rows, (dropped, overflow) = _dispatch_restated(
+            h, ids.numpy(), experts, ranks, cap, placement.tolist() if permuted else None)
+        got_ids = send_rows.view(torch.int32)[:, 128] if tagged else send_ids
+        assert np.array_equal(got_ids.cpu().numpy(), want_ids)
         assert np.array_equal(pair_rows.cpu().numpy(), want_rows)
         assert status[:2].tolist() == [dropped, overflow]
         for p, row in enumerate(want_rows.tolist()):
             if row >= 0:
-                assert torch.equal(send_rows[row], h[p // top_k])
+                assert torch.equal(send_rows[row, :256], h[p // top_k])
 
 
 @pytest.mark.parametrize("wdtype,residual", [(torch.bfloat16, True), (torch.float32, False)])
@@ -162,25 +181,24 @@ def test_single_rank_matches_expert_rows_and_the_oracle(cuda_device):
     assert_parity(np_f32(x), y, label="EP G=1 vs oracle stack")
 
 
-def _emulated(banks, routes, h, ranks):
+def _emulated(banks, routes, h, ranks, placements=None):
     """G ranks on one GPU: each rank's device steps in turn, blocks copied for the all-to-all."""
     from drama_b200.expert_parallel import shard_tokens
 
     tl = T // ranks
-    models = [_model(banks, ranks, r, tokens=tl) for r in range(ranks)]
+    models = [_model(banks, ranks, r, tokens=tl, placements=placements) for r in range(ranks)]
     cap = models[0].capacity
     xs = [h[shard_tokens(T, ranks, r)].clone() for r in range(ranks)]
     for layer, (ids, w) in enumerate(routes):
         rs = [(ids[shard_tokens(T, ranks, r)].contiguous(), w[shard_tokens(T, ranks, r)].contiguous())
               for r in range(ranks)]
         for r, m in enumerate(models):
-            m._dispatch(xs[r], rs[r][0])
+            m._dispatch(xs[r], rs[r][0], m.placements[layer])
         for r, m in enumerate(models):
             for s, src in enumerate(models):
                 m.buffers.recv_rows[s * cap:(s + 1) * cap] = src.buffers.send_rows[r * cap:(r + 1) * cap]
-                m.buffers.recv_ids[s * cap:(s + 1) * cap] = src.buffers.send_ids[r * cap:(r + 1) * cap]
         for m in models:
-            m._run_experts(layer, m.buffers.recv_rows, m.buffers.recv_ids, m.buffers.expert_rows)
+            m._run_experts(layer, m.buffers.recv_rows, m.buffers.expert_rows)
         for r, m in enumerate(models):
             for s, src in enumerate(models):
                 m.buffers.back_rows[s * cap:(s + 1) * cap] = src.buffers.expert_rows[r * cap:(r + 1) * cap]
@@ -189,13 +207,13 @@ def _emulated(banks, routes, h, ranks):
     return torch.cat(xs)
 
 
-@pytest.mark.parametrize("ranks", [2, 4])
-def test_emulated_ranks_equal_one_rank_bit_for_bit(cuda_device, ranks):
+@pytest.mark.parametrize("ranks,balanced", [(2, False), (4, False), (4, True)])
+def test_emulated_ranks_equal_one_rank_bit_for_bit(cuda_device, ranks, balanced):
     banks, routes, h = _inputs(cuda_device)
     single = _model(banks)
     x = h.clone()
     single.step(x, routes)
-    got = _emulated(banks, routes, h, ranks)
+    got = _emulated(banks, routes, h, ranks, _placements(routes, ranks, cuda_device) if balanced else None)
     torch.cuda.synchronize()
     assert torch.equal(got, x)
 

@@ -82,3 +82,28 @@ def test_against_the_tile_gemm(cuda_device):
     same = int((rows == tile).all(dim=1).sum())
     print(f"expert rows vs tile GEMM: {same} of 200 rows bit-identical")
     assert_parity(np_f32(rows), np_f32(tile), label="expert rows vs tile GEMM")
+
+
+def test_tagged_rows_equal_rows_with_an_id_array(cuda_device):
+    """Rows carrying their expert id after the hidden values (the exchanged layout)."""
+    import ctypes
+
+    from drama_b200 import _lib
+    from drama_b200.backend import _fp8_bank, fp8_expert_rows
+
+    bank, ids, x = _case(cuda_device, 16, 1024, 256, 90, seed=12, bad=4, hot=40)
+    want = fp8_expert_rows(x, ids, Bank(bank))
+    tagged = torch.zeros(90, 1024 + 8, dtype=torch.bfloat16, device=cuda_device)
+    tagged[:, :1024] = x
+    tagged.view(torch.int32)[:, 512] = ids.to(torch.int32)
+    lib = _lib.library()
+    fb, keep = _fp8_bank(Bank(bank), 1024)
+    ws = torch.zeros(lib.dll.drama_b200_expert_rows_workspace_bytes(90, 1024, 256, 16), dtype=torch.uint8,
+                     device=cuda_device)
+    out = torch.zeros(90, 1024, dtype=torch.bfloat16, device=cuda_device)
+    lib.check(lib.dll.drama_b200_fp8_expert_rows(ctypes.byref(fb), tagged.data_ptr(), 1024 + 8, 90, None, _lib.I32,
+                                                 out.data_ptr(), ws.data_ptr(), ws.numel(),
+                                                 _lib.stream_handle(cuda_device)))
+    torch.cuda.synchronize()
+    assert torch.equal(out, want)
+    del keep
