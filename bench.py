@@ -49,6 +49,8 @@ def parse_args():
                         "ep: config 4 expert-parallel decode of 256 tokens over the torchrun ranks; "
                         "offload: config 4's 1-GPU offload variant (32 of 128 experts resident per layer); "
                         "int4: config 2 (one W4A16 asymmetric layer, decode batches 1/4/16, uniform routes)")
+    p.add_argument("--exchange", choices=("p2p", "nccl"), default="p2p",
+                   help="ep: NVLink peer-memory exchange (default) or NCCL all-to-alls")
     p.add_argument("--host-layers", type=int, default=48,
                    help="offload: distinct pinned host stores (layers beyond reuse them in turn)")
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -589,11 +591,13 @@ def run_ep(args) -> None:
     local_routes = [(i[rows].contiguous(), w[rows].contiguous()) for i, w in routes]
     h0 = synthetic.hidden_states(EP_TOKENS, HIDDEN, 97_000, device=device)[rows].contiguous()
     model = ExpertParallelMoE(banks, experts=EXPERTS, top_k=TOP_K, tokens=EP_TOKENS // world, ranks=world,
-                              rank=rank, all_to_all=nccl_all_to_all() if world > 1 else None, placements=placements)
+                              rank=rank, all_to_all=nccl_all_to_all() if world > 1 else None, placements=placements,
+                              exchange=args.exchange if world > 1 else "nccl")   # one GPU: no exchange at all
     x = h0.clone()
     model.step(x, local_routes)                       # eager pass: checks, lazy init
     torch.cuda.synchronize(device)
     dropped = model.dropped()
+    timed_out = model.timed_out() if model.exchange == "p2p" else False
     x.copy_(h0)
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph):
@@ -646,7 +650,12 @@ def run_ep(args) -> None:
     step_bytes = touched * nbytes + 2 * (EP_TOKENS // world) * HIDDEN * 2 * args.layers
     peaks = measured_peaks()
     achieved = step_bytes / (ms / 1000.0) / 1e9
-    link_bytes = 2 * world * model.capacity * HIDDEN * 2 * args.layers if world > 1 else 0
+    if world == 1:
+        link_bytes = 0
+    elif args.exchange == "nccl":
+        link_bytes = 2 * world * model.capacity * HIDDEN * 2 * args.layers
+    else:   # the real rows only, each way
+        link_bytes = 2 * (EP_TOKENS // world) * TOP_K * HIDDEN * 2 * args.layers
     line = {
         "metric": METRIC, "value": EP_TOKENS / (ms / 1000.0), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": ms, "higher_is_better": True,
@@ -656,9 +665,12 @@ def run_ep(args) -> None:
         "config": {"workload": (f"config4: expert-parallel decode of {EP_TOKENS} tokens through {args.layers} FP8 "
                                 f"MoE layers (hidden {HIDDEN}, {EXPERTS} experts, top-{TOP_K}, intermediate {INTER}),"
                                 f" Zipf(1.1) routing, {EXPERTS // world} experts and {EP_TOKENS // world} tokens "
-                                f"per GPU, NCCL all-to-all dispatch/combine, one CUDA graph per step"),
+                                f"per GPU, " + ("no exchange" if world == 1 else "NVLink peer-memory dispatch/combine"
+                                                if args.exchange == "p2p" else "NCCL all-to-all dispatch/combine")
+                                + ", one CUDA graph per step"),
                    "tokens": EP_TOKENS, "layers": args.layers, "experts_per_gpu": EXPERTS // world,
                    "parallelism": f"ep{world}", "capacity_rows_per_peer": model.capacity,
+                   "exchange": model.exchange if world > 1 else "none",
                    "placement": "by observed route counts (balanced rows per rank)" if world > 1 else "all local",
                    "l2": "inputs larger than L2: every step reads the touched experts of 48 layers"},
         "roofline": {"kernel": "one EP decode step on one rank (dispatch, all-to-alls, grouped GEMMs, combine)",
@@ -671,7 +683,7 @@ def run_ep(args) -> None:
                 "h2d_bytes_per_step": h0.numel() * 2 * world, "d2h_bytes_per_step": h0.numel() * 2 * world},
         "gpu_launches": args.steps * args.layers * model.launches_per_layer(),
         "clocks": clocks.summary(),
-        "checksum": checksum, "dropped_pairs": list(dropped),
+        "checksum": checksum, "dropped_pairs": list(dropped), "peer_wait_timed_out": timed_out,
         "setup_s": round(build_s, 1),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -681,6 +693,7 @@ def run_ep(args) -> None:
         cpu["sample"] += "; one token per step (the workload's 256 tokens would take 256x as long)"
         line["cpu_baseline"] = cpu
     del graph
+    model.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -502,6 +502,163 @@ int drama_b200_ep_dispatch(const void* hidden, int64_t tokens, int hidden_size, 
     return 0;
 }
 
+int drama_b200_ep_buffers_alloc(int ranks, int64_t capacity, int hidden, void** recv, void** back,
+                                int32_t** signals, int32_t** counters) {
+    if (!recv || !back || !signals || !counters) return fail("output pointers are required");
+    if (ranks < 1 || ranks > kMaxEpRanks || capacity < 1 || hidden < 8 || hidden % 8)
+        return fail("ranks in [1, %d], capacity >= 1 and hidden a positive multiple of 8", kMaxEpRanks);
+    *recv = *back = nullptr;
+    *signals = *counters = nullptr;
+    const size_t rows = static_cast<size_t>(ranks) * capacity;
+    cudaError_t err = cudaMalloc(recv, rows * (hidden + 8) * 2);
+    if (err == cudaSuccess) err = cudaMalloc(back, rows * hidden * 2);
+    if (err == cudaSuccess) err = cudaMalloc(reinterpret_cast<void**>(signals), 256);
+    if (err == cudaSuccess) err = cudaMalloc(reinterpret_cast<void**>(counters), 256);
+    if (err == cudaSuccess) err = cudaMemset(*signals, 0, 256);
+    if (err == cudaSuccess) err = cudaMemset(*counters, 0, 256);
+    if (err == cudaSuccess) err = cudaMemset(*recv, 0, rows * (hidden + 8) * 2);
+    if (err != cudaSuccess) {
+        cudaFree(*recv);
+        cudaFree(*back);
+        cudaFree(*signals);
+        cudaFree(*counters);
+        *recv = *back = nullptr;
+        *signals = *counters = nullptr;
+        return fail("allocating the exchange buffers: %s", cudaGetErrorString(err));
+    }
+    return 0;
+}
+
+int drama_b200_ep_buffers_free(void* recv, void* back, int32_t* signals, int32_t* counters) {
+    cudaFree(recv);
+    cudaFree(back);
+    cudaFree(signals);
+    cudaFree(counters);
+    const cudaError_t err = cudaGetLastError();
+    if (err != cudaSuccess) return fail("freeing the exchange buffers: %s", cudaGetErrorString(err));
+    return 0;
+}
+
+int drama_b200_ipc_handle(const void* device_ptr, void* handle_out) {
+    if (!device_ptr || !handle_out) return fail("device_ptr and handle_out are required");
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "CUDA IPC handles are 64 bytes");
+    cudaIpcMemHandle_t h;
+    const cudaError_t err = cudaIpcGetMemHandle(&h, const_cast<void*>(device_ptr));
+    if (err != cudaSuccess) return fail("cudaIpcGetMemHandle: %s", cudaGetErrorString(err));
+    memcpy(handle_out, &h, sizeof(h));
+    return 0;
+}
+
+int drama_b200_ipc_open(const void* handle, void** device_ptr) {
+    if (!handle || !device_ptr) return fail("handle and device_ptr are required");
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    const cudaError_t err = cudaIpcOpenMemHandle(device_ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    if (err != cudaSuccess) return fail("cudaIpcOpenMemHandle: %s", cudaGetErrorString(err));
+    return 0;
+}
+
+int drama_b200_ipc_close(void* device_ptr) {
+    const cudaError_t err = cudaIpcCloseMemHandle(device_ptr);
+    if (err != cudaSuccess) return fail("cudaIpcCloseMemHandle: %s", cudaGetErrorString(err));
+    return 0;
+}
+
+namespace {
+int check_peers(const DramaB200EpPeers* peers) {
+    if (!peers) return fail("peers are required");
+    const DramaB200EpPeers& q = *peers;
+    if (q.ranks < 1 || q.ranks > kMaxEpRanks || q.rank < 0 || q.rank >= q.ranks)
+        return fail("ranks must be in [1, %d] and rank in [0, ranks)", kMaxEpRanks);
+    if (q.capacity < 1 || q.capacity * q.ranks > INT32_MAX) return fail("capacity must be in [1, 2^31 / ranks)");
+    if (q.hidden < 8 || q.hidden % 8) return fail("hidden must be a positive multiple of 8");
+    if (q.experts < q.ranks || q.experts % q.ranks) return fail("experts must be a multiple of ranks");
+    for (int r = 0; r < q.ranks; ++r)
+        if (!q.recv[r] || !q.back[r] || !q.signals[r]) return fail("rank %d's exchange buffers are missing", r);
+    if (!q.epoch || !q.done) return fail("epoch and done counters are required");
+    return 0;
+}
+}  // namespace
+
+int drama_b200_ep_p2p_dispatch(const DramaB200EpPeers* peers, const void* hidden, int64_t tokens, const void* ids,
+                               int ids_dtype, int top_k, const int32_t* placement, int32_t* pair_rows,
+                               int32_t* scratch, int32_t* status, void* stream) {
+    if (check_peers(peers)) return -1;
+    if (!hidden || !ids || !pair_rows || !scratch) return fail("hidden, ids, pair_rows and scratch are required");
+    if (!index_dtype(ids_dtype)) return fail("expert IDs must be int32 or int64");
+    if (tokens < 0 || top_k < 1 || top_k > 32) return fail("tokens must be >= 0 and top_k in [1, 32]");
+    if (tokens * top_k > peers->capacity) return fail("capacity must be at least tokens * top_k");
+    if (!aligned16(hidden)) return fail("hidden rows must start on 16-byte boundaries");
+    int sms = 0;
+    if (sm_count_current(&sms)) return -1;
+    const cudaError_t err = ep_p2p_dispatch_launch(*peers, hidden, tokens, ids, ids_dtype, top_k, placement,
+                                                   pair_rows, scratch, status, sms, static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return fail("peer dispatch launch failed: %s", cudaGetErrorString(err));
+    return 0;
+}
+
+int drama_b200_ep_p2p_receive(const DramaB200EpPeers* peers, int32_t* status, void* stream) {
+    if (check_peers(peers)) return -1;
+    const cudaError_t err = ep_p2p_receive_launch(*peers, status, static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return fail("peer receive launch failed: %s", cudaGetErrorString(err));
+    return 0;
+}
+
+int drama_b200_fp8_expert_rows_p2p(const DramaB200Fp8Bank* bank, const DramaB200EpPeers* peers, void* workspace,
+                                   size_t workspace_bytes, void* stream) {
+    if (check_peers(peers)) return -1;
+    if (!bank) return fail("bank is required");
+    const DramaB200Fp8Bank& b = *bank;
+    if (b.hidden != peers->hidden) return fail("bank hidden size %d differs from the exchange's %d", b.hidden,
+                                               peers->hidden);
+    if (b.slots != peers->experts / peers->ranks) return fail("the bank must hold experts / ranks slots");
+    if (b.hidden % 128 || b.intermediate % 128 || b.intermediate < 128)
+        return fail("hidden and intermediate must be positive multiples of 128");
+    if (!b.w13 || !b.w13_scale || !b.w2 || !b.w2_scale) return fail("FP8 bank pointers are required");
+    if (!aligned16(b.w13) || !aligned16(b.w2) || b.w13_row_stride % 16 || b.w2_row_stride % 16 ||
+        b.w13_slot_stride % 16 || b.w2_slot_stride % 16)
+        return fail("FP8 weight rows must start on 16-byte boundaries");
+    const int64_t rows = peers->capacity * peers->ranks;
+    int sms = 0;
+    if (sm_count_current(&sms)) return -1;
+    const size_t need = expert_rows_workspace_layout(rows, b.hidden, b.intermediate, b.slots, nullptr, nullptr);
+    if (!workspace || workspace_bytes < need)
+        return fail("expert-rows workspace too small: need %zu bytes, got %zu", need, workspace_bytes);
+    if (reinterpret_cast<uintptr_t>(workspace) & 255u) return fail("workspace must be 256-byte aligned");
+    RowsWorkspace ws;
+    expert_rows_workspace_layout(rows, b.hidden, b.intermediate, b.slots, static_cast<char*>(workspace), &ws);
+    RowsScatter sc;
+    sc.ranks = peers->ranks;
+    sc.rank = peers->rank;
+    sc.cap = peers->capacity;
+    for (int r = 0; r < peers->ranks; ++r) sc.dst[r] = static_cast<__nv_bfloat16*>(peers->back[r]);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t err = expert_rows_launch(b, peers->recv[peers->rank], b.hidden + 8, rows, nullptr, DRAMA_B200_I32,
+                                         nullptr, ws, sms, s, &sc);
+    if (err == cudaSuccess) err = ep_p2p_signal_back_launch(*peers, s);
+    if (err != cudaSuccess) return fail("peer expert-rows launch failed: %s", cudaGetErrorString(err));
+    return 0;
+}
+
+int drama_b200_ep_p2p_combine(const DramaB200EpPeers* peers, const int32_t* pair_rows, const void* weights,
+                              int weights_dtype, int64_t tokens, int top_k, const void* residual, void* out,
+                              int32_t* status, void* stream) {
+    if (check_peers(peers)) return -1;
+    if (!pair_rows || !weights || !out) return fail("pair_rows, weights and out are required");
+    if (!float_dtype(weights_dtype)) return fail("routing weights must be floating point");
+    if (tokens < 0 || top_k < 1 || top_k > 32) return fail("tokens must be >= 0 and top_k in [1, 32]");
+    if (!aligned16(out) || (residual && !aligned16(residual))) return fail("out and residual must be 16-byte aligned");
+    int sms = 0;
+    if (sm_count_current(&sms)) return -1;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t err = ep_p2p_wait_back_launch(*peers, status, s);
+    if (err == cudaSuccess)
+        err = ep_combine_launch(peers->back[peers->rank], peers->capacity * peers->ranks, pair_rows, weights,
+                                weights_dtype, tokens, top_k, peers->hidden, residual, out, sms, s);
+    if (err != cudaSuccess) return fail("peer combine launch failed: %s", cudaGetErrorString(err));
+    return 0;
+}
+
 int drama_b200_ep_combine(const void* rows, int64_t row_count, const int32_t* pair_rows, const void* weights,
                           int weights_dtype, int64_t tokens, int top_k, int hidden_size, const void* residual,
                           void* out, void* stream) {

@@ -52,6 +52,7 @@ struct SwapArgs {
     __half* h;                   // GEMM 0 out: f16 h [P, I] sorted, scaled per 64 columns
     float* hs;                   // GEMM 0 out: [P, I / 64] scales of h
     __nv_bfloat16* out;          // GEMM 1 out: down [*, H] by order[s]
+    RowsScatter scatter;         // GEMM 1 out to peers instead (ranks > 0)
     int top_k, E, H, I;
 };
 
@@ -326,13 +327,23 @@ __global__ void __launch_bounds__(kSwThreads, 2) swap_gemm_kernel(SwapArgs a) {
                 const int q = tid + 256 * i, tok = q >> 4, c8 = q & 15;
                 if (tok < live) {
                     const int64_t row = a.order[off + tok0 + tok];
-                    *reinterpret_cast<uint4*>(a.out + row * H + kSwRows * rb + 8 * c8) =
+                    __nv_bfloat16* dst;
+                    if (a.scatter.ranks > 0) {
+                        // received row r came from rank r / cap as its row r % cap: straight back into
+                        // that rank's return buffer, block of this rank
+                        const int64_t src = row / a.scatter.cap, j = row - src * a.scatter.cap;
+                        dst = a.scatter.dst[src] + (a.scatter.rank * a.scatter.cap + j) * H;
+                    } else {
+                        dst = a.out + row * H;
+                    }
+                    *reinterpret_cast<uint4*>(dst + kSwRows * rb + 8 * c8) =
                         *reinterpret_cast<const uint4*>(s_d + tok * kSwRows + 8 * c8);
                 }
             }
         }
         __syncthreads();   // the next item's loads reuse the ring
     }
+    if (MODE == 1 && a.scatter.ranks > 0) __threadfence_system();  // peer stores visible before the signal kernel
 }
 
 int grid_for(int64_t work, int sm_count) {
@@ -366,7 +377,7 @@ size_t expert_rows_workspace_layout(int64_t rows, int hidden, int intermediate, 
 
 cudaError_t expert_rows_launch(const DramaB200Fp8Bank& bank, const void* x, int64_t x_stride, int64_t rows,
                                const void* ids, int ids_dtype, void* out, const RowsWorkspace& ws, int sm_count,
-                               cudaStream_t s) {
+                               cudaStream_t s, const RowsScatter* scatter) {
     static bool configured = false;  // benign race: identical values
     if (!configured) {
         cudaError_t err = cudaFuncSetAttribute(swap_gemm_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -402,6 +413,7 @@ cudaError_t expert_rows_launch(const DramaB200Fp8Bank& bank, const void* x, int6
     a.x = ws.h;
     a.xs = ws.hs;
     a.out = static_cast<__nv_bfloat16*>(out);
+    if (scatter) a.scatter = *scatter;
     swap_gemm_kernel<1><<<2 * sm_count, kSwThreads, kSwSmem, s>>>(a);
     return cudaGetLastError();
 }

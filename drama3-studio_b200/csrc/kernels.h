@@ -180,9 +180,17 @@ struct RowsWorkspace {
 };
 size_t expert_rows_workspace_layout(int64_t rows, int hidden, int intermediate, int experts, char* base,
                                     RowsWorkspace* ws);
+// GEMM 1 rows written to other ranks: received row r (from rank r / cap) goes
+// to dst[r / cap] + (rank * cap + r % cap) * H.
+struct RowsScatter {
+    int ranks = 0;            // 0: no scatter
+    int rank = 0;
+    int64_t cap = 0;
+    __nv_bfloat16* dst[8] = {};
+};
 cudaError_t expert_rows_launch(const DramaB200Fp8Bank& bank, const void* x, int64_t x_stride, int64_t rows,
                                const void* ids, int ids_dtype, void* out, const RowsWorkspace& ws, int sm_count,
-                               cudaStream_t s);
+                               cudaStream_t s, const RowsScatter* scatter = nullptr);
 
 // Expert-parallel exchange (expert_parallel.cu).
 constexpr int kMaxEpRanks = 8;
@@ -193,6 +201,15 @@ cudaError_t ep_dispatch_launch(const void* hidden, int64_t tokens, int H, const 
 cudaError_t ep_combine_launch(const void* rows, int64_t row_count, const int32_t* pair_rows, const void* weights, int weights_dtype,
                               int64_t tokens, int top_k, int H, const void* residual, void* out, int sm_count,
                               cudaStream_t s);
+
+// Expert-parallel exchange over peer memory (ep_p2p.cu).
+cudaError_t ep_p2p_dispatch_launch(const DramaB200EpPeers& peers, const void* hidden, int64_t tokens,
+                                   const void* ids, int ids_dtype, int top_k, const int32_t* placement,
+                                   int32_t* pair_rows, int32_t* scratch, int32_t* status, int sm_count,
+                                   cudaStream_t s);
+cudaError_t ep_p2p_receive_launch(const DramaB200EpPeers& peers, int32_t* status, cudaStream_t s);
+cudaError_t ep_p2p_signal_back_launch(const DramaB200EpPeers& peers, cudaStream_t s);
+cudaError_t ep_p2p_wait_back_launch(const DramaB200EpPeers& peers, int32_t* status, cudaStream_t s);
 
 size_t prefill_workspace_layout(int64_t tokens, int top_k, int hidden, int intermediate, int experts, char* base,
                                 PrefillWorkspace* ws);

@@ -50,6 +50,15 @@ EXPORTS = (
     "drama_b200_fp8_expert_rows",
     "drama_b200_ep_dispatch",
     "drama_b200_ep_combine",
+    "drama_b200_ep_buffers_alloc",
+    "drama_b200_ep_buffers_free",
+    "drama_b200_ipc_handle",
+    "drama_b200_ipc_open",
+    "drama_b200_ipc_close",
+    "drama_b200_ep_p2p_dispatch",
+    "drama_b200_ep_p2p_receive",
+    "drama_b200_fp8_expert_rows_p2p",
+    "drama_b200_ep_p2p_combine",
     "drama_b200_stage_copies",
 )
 
@@ -80,6 +89,15 @@ class Int4Bank(ctypes.Structure):
         ("w2_zeros_slot_stride", c_int64), ("w2_zeros_row_stride", c_int64),
         ("scale_dtype", ctypes.c_int32), ("slots", ctypes.c_int32),
         ("hidden", ctypes.c_int32), ("intermediate", ctypes.c_int32),
+    ]
+
+
+class EpPeers(ctypes.Structure):
+    _fields_ = [
+        ("ranks", ctypes.c_int32), ("rank", ctypes.c_int32), ("capacity", c_int64),
+        ("hidden", ctypes.c_int32), ("experts", ctypes.c_int32),
+        ("recv", c_void_p * 8), ("back", c_void_p * 8), ("signals", c_void_p * 8),
+        ("epoch", c_void_p), ("done", c_void_p),
     ]
 
 
@@ -142,6 +160,23 @@ class Library:
         dll.drama_b200_ep_combine.argtypes = [c_void_p, c_int64, c_void_p, c_void_p, c_int, c_int64, c_int, c_int,
                                               c_void_p, c_void_p, c_void_p]
         dll.drama_b200_ep_combine.restype = c_int
+        vpp = ctypes.POINTER(c_void_p)
+        dll.drama_b200_ep_buffers_alloc.argtypes = [c_int, c_int64, c_int, vpp, vpp, vpp, vpp]
+        dll.drama_b200_ep_buffers_free.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p]
+        dll.drama_b200_ipc_handle.argtypes = [c_void_p, c_void_p]
+        dll.drama_b200_ipc_open.argtypes = [c_void_p, vpp]
+        dll.drama_b200_ipc_close.argtypes = [c_void_p]
+        peers = ctypes.POINTER(EpPeers)
+        dll.drama_b200_ep_p2p_dispatch.argtypes = [peers, c_void_p, c_int64, c_void_p, c_int, c_int, c_void_p,
+                                                   c_void_p, c_void_p, c_void_p, c_void_p]
+        dll.drama_b200_ep_p2p_receive.argtypes = [peers, c_void_p, c_void_p]
+        dll.drama_b200_fp8_expert_rows_p2p.argtypes = [ctypes.POINTER(Fp8Bank), peers, c_void_p, c_size_t, c_void_p]
+        dll.drama_b200_ep_p2p_combine.argtypes = [peers, c_void_p, c_void_p, c_int, c_int64, c_int, c_void_p,
+                                                  c_void_p, c_void_p, c_void_p]
+        for name in ("drama_b200_ep_buffers_alloc", "drama_b200_ep_buffers_free", "drama_b200_ipc_handle",
+                     "drama_b200_ipc_open", "drama_b200_ipc_close", "drama_b200_ep_p2p_dispatch",
+                     "drama_b200_ep_p2p_receive", "drama_b200_fp8_expert_rows_p2p", "drama_b200_ep_p2p_combine"):
+            getattr(dll, name).restype = c_int
         for name in ("drama_b200_device_check", "drama_b200_route_topk", "drama_b200_permute_routes",
                      "drama_b200_fp8_decode", "drama_b200_int4_decode", "drama_b200_fp8_moe_layer",
                      "drama_b200_fp8_moe_router", "drama_b200_fp8_moe_experts"):

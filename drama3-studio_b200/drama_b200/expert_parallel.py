@@ -23,8 +23,17 @@ Every pair's arithmetic is the same whatever G is (rows are computed one by
 one by the same kernels and summed in slot order by their owner), so the
 result does not depend on the number of GPUs.
 
-The exchange itself is a pluggable callable, ``all_to_all(out, inp)``; the
-product uses ``torch.distributed.all_to_all_single`` on the process group.
+Two exchanges:
+
+* ``exchange="p2p"`` (``PeerExchange``): the ranks map each other's receive and
+  return buffers (CUDA IPC over NVLink). The dispatch kernel stores only the
+  real rows straight into the owners' receive buffers; the second expert
+  GEMM stores each result straight into the source's return buffer; epoch
+  flags with bounded waits order the steps. No NCCL on the data path and no
+  padding on the wire.
+* ``exchange="nccl"``: fixed-capacity blocks through
+  ``torch.distributed.all_to_all_single`` (a pluggable ``all_to_all(out, inp)``
+  callable, which the CPU tests replace by gloo).
 """
 
 from __future__ import annotations
@@ -92,6 +101,74 @@ def experts_of_rank(placement: Sequence[int], ranks: int, rank: int) -> list[int
     return [local[i] for i in range(per)]
 
 
+class PeerExchange:
+    """This rank's exchange buffers and the mapped buffers of every other rank.
+
+    Created collectively (every rank of ``group`` at once): each rank
+    allocates its receive / return / signal buffers in the library, the CUDA
+    IPC handles go round with ``all_gather``, and each rank opens the others'.
+    ``close`` (also collective) unmaps and frees them.
+    """
+
+    def __init__(self, *, ranks: int, rank: int, capacity: int, hidden: int, experts: int, device,
+                 group=None) -> None:
+        import torch.distributed as dist
+
+        self.lib = lib = _lib.library()
+        self.ranks, self.rank, self.group, self.device = ranks, rank, group, torch.device(device)
+        ptrs = [ctypes.c_void_p() for _ in range(4)]
+        with torch.cuda.device(self.device):
+            lib.check(lib.dll.drama_b200_ep_buffers_alloc(ranks, capacity, hidden, *[ctypes.byref(q) for q in ptrs]))
+        self._own = [q.value for q in ptrs]
+        recv, back, sig, counters = self._own
+        handles = (ctypes.c_ubyte * 192)()
+        for i, ptr in enumerate((recv, back, sig)):
+            lib.check(lib.dll.drama_b200_ipc_handle(ptr, ctypes.addressof(handles) + 64 * i))
+        mine = torch.tensor(list(bytes(handles)), dtype=torch.uint8, device=self.device)
+        if ranks > 1:
+            every = [torch.empty_like(mine) for _ in range(ranks)]
+            dist.all_gather(every, mine, group=group)
+            every = [bytes(t.cpu().tolist()) for t in every]
+        else:
+            every = [bytes(handles)]
+        peers = _lib.EpPeers()
+        peers.ranks, peers.rank, peers.capacity = ranks, rank, capacity
+        peers.hidden, peers.experts = hidden, experts
+        self._opened = []
+        for r in range(ranks):
+            if r == rank:
+                peers.recv[r], peers.back[r], peers.signals[r] = recv, back, sig
+                continue
+            got = []
+            for i in range(3):
+                buf = (ctypes.c_ubyte * 64).from_buffer_copy(every[r][64 * i:64 * i + 64])
+                q = ctypes.c_void_p()
+                with torch.cuda.device(self.device):
+                    lib.check(lib.dll.drama_b200_ipc_open(buf, ctypes.byref(q)))
+                got.append(q.value)
+                self._opened.append(q.value)
+            peers.recv[r], peers.back[r], peers.signals[r] = got
+        peers.epoch, peers.done = counters, counters + 64
+        self.peers = peers
+
+    def close(self) -> None:
+        import torch.distributed as dist
+
+        if self._own is None:
+            return
+        torch.cuda.synchronize(self.device)
+        if self.ranks > 1:
+            dist.barrier(group=self.group)      # no rank reads or writes a peer's buffers any more
+        with torch.cuda.device(self.device):
+            for ptr in self._opened:
+                self.lib.dll.drama_b200_ipc_close(ptr)
+            if self.ranks > 1:
+                dist.barrier(group=self.group)  # every mapping of this rank's buffers is gone
+            self.lib.check(self.lib.dll.drama_b200_ep_buffers_free(*self._own))
+        self._own = None
+        self._opened = []
+
+
 def nccl_all_to_all(group=None) -> AllToAll:
     """Equal-split all-to-all on ``group`` (rows travel as int32 words)."""
     import torch.distributed as dist
@@ -127,7 +204,7 @@ class ExpertParallelMoE:
 
     def __init__(self, banks: Sequence, *, experts: int, top_k: int, tokens: int, ranks: int = 1, rank: int = 0,
                  all_to_all: AllToAll | None = None, capacity: int | None = None,
-                 placements: Sequence[Tensor | None] | None = None) -> None:
+                 placements: Sequence[Tensor | None] | None = None, exchange: str = "nccl", group=None) -> None:
         if not banks:
             raise ValueError("At least one layer bank is required")
         self.ranks, self.rank = ranks, rank
@@ -137,7 +214,10 @@ class ExpertParallelMoE:
         self.capacity = capacity if capacity is not None else tokens * top_k
         if self.capacity < 1:
             raise ValueError("Capacity must be positive")
-        if ranks > 1 and all_to_all is None:
+        if exchange not in ("nccl", "p2p"):
+            raise ValueError("exchange must be 'nccl' or 'p2p'")
+        self.exchange = exchange
+        if exchange == "nccl" and ranks > 1 and all_to_all is None:
             raise ValueError("More than one rank needs an all_to_all")
         self.all_to_all = all_to_all
         first = banks[0]
@@ -157,6 +237,11 @@ class ExpertParallelMoE:
                 raise ValueError(f"A placement is an int32 tensor of {experts} rank-major positions")
         self.lib = _lib.library()
         self.buffers = self._allocate()
+        self.peer_exchange = None
+        if exchange == "p2p":
+            self.peer_exchange = PeerExchange(ranks=ranks, rank=rank, capacity=self.capacity, hidden=self.hidden,
+                                              experts=experts, device=self.device, group=group)
+            self.scratch = torch.zeros(self.tokens * self.top_k + 8, dtype=torch.int32, device=self.device)
 
     def _allocate(self) -> ExchangeBuffers:
         rows = self.ranks * self.capacity
@@ -188,6 +273,8 @@ class ExpertParallelMoE:
         """
         self._check_routes(h, ids, weights)
         out = torch.empty_like(h) if out is None else out
+        if self.exchange == "p2p":
+            return self._layer_p2p(h, ids, weights, layer, out)
         b = self.buffers
         self._dispatch(h, ids, self.placements[layer])
         if self.ranks > 1:
@@ -203,6 +290,32 @@ class ExpertParallelMoE:
             back = b.expert_rows
         self._combine(back, weights, h, out)
         return out
+
+    def _layer_p2p(self, h: Tensor, ids: Tensor, weights: Tensor, layer: int, out: Tensor) -> Tensor:
+        b, lib, peers = self.buffers, self.lib, ctypes.byref(self.peer_exchange.peers)
+        stream = _lib.stream_handle(h.device)
+        bank, _ = self._banks[layer]
+        lib.check(lib.dll.drama_b200_ep_p2p_dispatch(
+            peers, h.data_ptr(), self.tokens, ids.data_ptr(), _lib.DTYPE_CODES[ids.dtype], self.top_k,
+            _lib.ptr(self.placements[layer]), b.pair_rows.data_ptr(), self.scratch.data_ptr(), b.status.data_ptr(),
+            stream))
+        lib.check(lib.dll.drama_b200_ep_p2p_receive(peers, b.status.data_ptr(), stream))
+        lib.check(lib.dll.drama_b200_fp8_expert_rows_p2p(ctypes.byref(bank), peers, b.workspace.data_ptr(),
+                                                         b.workspace.numel(), stream))
+        lib.check(lib.dll.drama_b200_ep_p2p_combine(
+            peers, b.pair_rows.data_ptr(), weights.data_ptr(), _lib.DTYPE_CODES[weights.dtype], self.tokens,
+            self.top_k, h.data_ptr(), out.data_ptr(), b.status.data_ptr(), stream))
+        return out
+
+    def close(self) -> None:
+        """Release the peer exchange (collective across the ranks)."""
+        if self.peer_exchange is not None:
+            self.peer_exchange.close()
+            self.peer_exchange = None
+
+    def timed_out(self) -> bool:
+        """Whether a peer wait of the last layers gave up (synchronises)."""
+        return bool(self.buffers.status[2].item())
 
     # The three device steps (CUDA kernels of this library).
     def _dispatch(self, h: Tensor, ids: Tensor, placement: Tensor | None = None) -> None:
@@ -233,8 +346,9 @@ class ExpertParallelMoE:
         return h
 
     def launches_per_layer(self) -> int:
-        """Kernels of this library per layer: plan + pack, row prep + permute + 2 GEMMs, EP combine."""
-        return 7
+        """Kernels of this library per layer."""
+        # nccl: plan + pack, row prep + permute + 2 GEMMs, combine; p2p adds the receive, signal and wait kernels
+        return 10 if self.exchange == "p2p" else 7
 
     def dropped(self) -> tuple[int, int]:
         """(pairs with an out-of-range id, pairs over capacity) of the last layer (synchronises)."""

@@ -325,6 +325,64 @@ DRAMA_B200_API int drama_b200_ep_combine(const void* rows, int64_t row_count, co
                                          int hidden_size, const void* residual, void* out, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Expert-parallel exchange over NVLink peer memory (no counterpart in the
+ * reference; an alternative to the all-to-alls around drama_b200_ep_dispatch).
+ * Each rank allocates three buffers with drama_b200_ep_buffers_alloc, shares
+ * them with drama_b200_ipc_handle / drama_b200_ipc_open, and fills a
+ * DramaB200EpPeers with every rank's pointers (its own for its own rank):
+ *   recv    [ranks][capacity][hidden + 8] bf16: block s written by rank s;
+ *           row = hidden values, then the receiver-local expert id (int32);
+ *   back    [ranks][capacity][hidden] bf16: block d written by rank d;
+ *   signals [3 * ranks] int32 (zeroed): dispatch flags, row counts, return
+ *           flags; epoch and done are this rank's own counters (zeroed).
+ * A layer is, in stream order on every rank:
+ *   drama_b200_ep_p2p_dispatch   (rows into the owners' recv, then flags)
+ *   drama_b200_ep_p2p_receive    (wait for every source, mark unused rows)
+ *   drama_b200_fp8_expert_rows_p2p (GEMMs; results into the sources' back)
+ *   drama_b200_ep_p2p_combine    (wait for every expert rank, slot-order sum)
+ * Every rank must issue the same sequence of layers. Waits give up after 2 s
+ * and set status[2]; the result of that step is then invalid.
+ * ------------------------------------------------------------------------- */
+typedef struct DramaB200EpPeers {
+    int32_t ranks, rank;
+    int64_t capacity;           /* rows per (source, destination) block: tokens * top_k */
+    int32_t hidden, experts;
+    void* recv[8];
+    void* back[8];
+    int32_t* signals[8];
+    int32_t* epoch;             /* this rank's step counter */
+    int32_t* done;              /* this rank's arrival counter of the dispatch kernel */
+} DramaB200EpPeers;
+
+DRAMA_B200_API int drama_b200_ep_buffers_alloc(int ranks, int64_t capacity, int hidden, void** recv, void** back,
+                                               int32_t** signals, int32_t** counters);
+
+DRAMA_B200_API int drama_b200_ep_buffers_free(void* recv, void* back, int32_t* signals, int32_t* counters);
+
+/* CUDA IPC of a buffer from drama_b200_ep_buffers_alloc (64-byte handles). */
+DRAMA_B200_API int drama_b200_ipc_handle(const void* device_ptr, void* handle_out);
+
+DRAMA_B200_API int drama_b200_ipc_open(const void* handle, void** device_ptr);
+
+DRAMA_B200_API int drama_b200_ipc_close(void* device_ptr);
+
+/* scratch: int32 [tokens * top_k + ranks]; pair_rows as drama_b200_ep_dispatch. */
+DRAMA_B200_API int drama_b200_ep_p2p_dispatch(const DramaB200EpPeers* peers, const void* hidden, int64_t tokens,
+                                              const void* ids, int ids_dtype, int top_k,
+                                              const int32_t* placement, int32_t* pair_rows, int32_t* scratch,
+                                              int32_t* status, void* stream);
+
+DRAMA_B200_API int drama_b200_ep_p2p_receive(const DramaB200EpPeers* peers, int32_t* status, void* stream);
+
+/* workspace: drama_b200_expert_rows_workspace_bytes(ranks * capacity, ...). */
+DRAMA_B200_API int drama_b200_fp8_expert_rows_p2p(const DramaB200Fp8Bank* bank, const DramaB200EpPeers* peers,
+                                                  void* workspace, size_t workspace_bytes, void* stream);
+
+DRAMA_B200_API int drama_b200_ep_p2p_combine(const DramaB200EpPeers* peers, const int32_t* pair_rows,
+                                             const void* weights, int weights_dtype, int64_t tokens, int top_k,
+                                             const void* residual, void* out, int32_t* status, void* stream);
+
+/* ---------------------------------------------------------------------------
  * K4 staging: host -> HBM expert copies on a copy stream. Replaces the
  * transfer half of _StagingPool.stage (src/drama_low_vram/offload.py:543-651:
  * the host gather at 561-594 and the H2D copy_ on the compute stream at

@@ -53,7 +53,7 @@ def _placements(routes, ranks, device):
                          dtype=torch.int32, device=device) for ids, _ in routes]
 
 
-def _model(banks, ranks=1, rank=0, tokens=T, all_to_all=None, capacity=None, placements=None):
+def _model(banks, ranks=1, rank=0, tokens=T, all_to_all=None, capacity=None, placements=None, exchange="nccl"):
     from drama_b200.expert_parallel import ExpertParallelMoE, experts_of_rank, shard_experts
 
     local = []
@@ -62,7 +62,8 @@ def _model(banks, ranks=1, rank=0, tokens=T, all_to_all=None, capacity=None, pla
             list(shard_experts(E, ranks, rank))
         local.append(Bank({n: v[held] for n, v in b.items()}))
     return ExpertParallelMoE(local, experts=E, top_k=K, tokens=tokens, ranks=ranks, rank=rank,
-                             all_to_all=all_to_all or (lambda o, i: None), capacity=capacity, placements=placements)
+                             all_to_all=all_to_all or (lambda o, i: None), capacity=capacity, placements=placements,
+                             exchange=exchange)
 
 
 def _dispatch_restated(h, ids, experts, ranks, cap, placement=None):
@@ -218,6 +219,28 @@ def test_emulated_ranks_equal_one_rank_bit_for_bit(cuda_device, ranks, balanced)
     assert torch.equal(got, x)
 
 
+def test_peer_exchange_on_one_rank_equals_the_nccl_path(cuda_device):
+    """The NVLink exchange (here a rank writing to itself) leaves every bit as it was."""
+    banks, routes, h = _inputs(cuda_device)
+    ref = _model(banks)
+    x = h.clone()
+    ref.step(x, routes)
+    p2p = _model(banks, exchange="p2p")
+    y = h.clone()
+    p2p.step(y, routes)
+    g_in = h.clone()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        p2p.step(g_in, routes)
+    g_in.copy_(h)
+    graph.replay()
+    torch.cuda.synchronize()
+    assert not p2p.timed_out()
+    assert torch.equal(y, x) and torch.equal(g_in, x)
+    del graph
+    p2p.close()
+
+
 def test_small_capacity_drops_and_counts_overflow(cuda_device):
     banks, routes, h = _inputs(cuda_device)
     model = _model(banks, capacity=8)
@@ -242,19 +265,28 @@ def _nccl_rank(rank, world, port, out_dir):
     try:
         banks, routes, h = _inputs(device)
         rows = shard_tokens(T, world, rank)
-        model = _model(banks, world, rank, tokens=T // world, all_to_all=nccl_all_to_all())
         local = [(i[rows].contiguous(), w[rows].contiguous()) for i, w in routes]
-        x = h[rows].clone()
-        model.step(x, local)                          # eager
-        g_in = h[rows].clone()
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            model.step(g_in, local)
-        g_in.copy_(h[rows])
-        graph.replay()
-        torch.cuda.synchronize()
-        del graph
-        torch.save({"eager": x.cpu(), "graph": g_in.cpu()}, os.path.join(out_dir, f"rank{rank}.pt"))
+        placements = _placements(routes, world, device)
+        result = {}
+        for exchange in ("nccl", "p2p"):
+            model = _model(banks, world, rank, tokens=T // world, all_to_all=nccl_all_to_all(),
+                           placements=placements, exchange=exchange)
+            x = h[rows].clone()
+            model.step(x, local)                          # eager
+            g_in = h[rows].clone()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                model.step(g_in, local)
+            for _ in range(2):                            # replays: the epochs keep moving in lockstep
+                g_in.copy_(h[rows])
+                graph.replay()
+            torch.cuda.synchronize()
+            del graph
+            if exchange == "p2p":
+                assert not model.timed_out()
+            model.close()
+            result[exchange] = {"eager": x.cpu(), "graph": g_in.cpu()}
+        torch.save(result, os.path.join(out_dir, f"rank{rank}.pt"))
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -274,5 +306,6 @@ def test_two_gpus_over_nccl_equal_one_rank(cuda_device, tmp_path):
     torch.cuda.synchronize()
     mp.spawn(_nccl_rank, args=(2, port, str(tmp_path)), nprocs=2, join=True)
     parts = [torch.load(tmp_path / f"rank{r}.pt") for r in range(2)]
-    assert torch.equal(torch.cat([p["eager"] for p in parts]), x.cpu())
-    assert torch.equal(torch.cat([p["graph"] for p in parts]), x.cpu())
+    for exchange in ("nccl", "p2p"):
+        assert torch.equal(torch.cat([p[exchange]["eager"] for p in parts]), x.cpu()), exchange
+        assert torch.equal(torch.cat([p[exchange]["graph"] for p in parts]), x.cpu()), exchange
