@@ -582,30 +582,24 @@ int check_peers(const DramaB200EpPeers* peers) {
 
 int drama_b200_ep_p2p_dispatch(const DramaB200EpPeers* peers, const void* hidden, int64_t tokens, const void* ids,
                                int ids_dtype, int top_k, const int32_t* placement, int32_t* pair_rows,
-                               int32_t* scratch, int32_t* status, void* stream) {
+                               int32_t* status, void* stream) {
     if (check_peers(peers)) return -1;
-    if (!hidden || !ids || !pair_rows || !scratch) return fail("hidden, ids, pair_rows and scratch are required");
+    if (!hidden || !ids || !pair_rows) return fail("hidden, ids and pair_rows are required");
     if (!index_dtype(ids_dtype)) return fail("expert IDs must be int32 or int64");
     if (tokens < 0 || top_k < 1 || top_k > 32) return fail("tokens must be >= 0 and top_k in [1, 32]");
     if (tokens * top_k > peers->capacity) return fail("capacity must be at least tokens * top_k");
+    if (tokens * top_k > kP2pMaxPairs) return fail("the peer dispatch handles at most %d pairs per rank", kP2pMaxPairs);
     if (!aligned16(hidden)) return fail("hidden rows must start on 16-byte boundaries");
     int sms = 0;
     if (sm_count_current(&sms)) return -1;
     const cudaError_t err = ep_p2p_dispatch_launch(*peers, hidden, tokens, ids, ids_dtype, top_k, placement,
-                                                   pair_rows, scratch, status, sms, static_cast<cudaStream_t>(stream));
+                                                   pair_rows, status, sms, static_cast<cudaStream_t>(stream));
     if (err != cudaSuccess) return fail("peer dispatch launch failed: %s", cudaGetErrorString(err));
     return 0;
 }
 
-int drama_b200_ep_p2p_receive(const DramaB200EpPeers* peers, int32_t* status, void* stream) {
-    if (check_peers(peers)) return -1;
-    const cudaError_t err = ep_p2p_receive_launch(*peers, status, static_cast<cudaStream_t>(stream));
-    if (err != cudaSuccess) return fail("peer receive launch failed: %s", cudaGetErrorString(err));
-    return 0;
-}
-
 int drama_b200_fp8_expert_rows_p2p(const DramaB200Fp8Bank* bank, const DramaB200EpPeers* peers, void* workspace,
-                                   size_t workspace_bytes, void* stream) {
+                                   size_t workspace_bytes, int32_t* status, void* stream) {
     if (check_peers(peers)) return -1;
     if (!bank) return fail("bank is required");
     const DramaB200Fp8Bank& b = *bank;
@@ -627,15 +621,26 @@ int drama_b200_fp8_expert_rows_p2p(const DramaB200Fp8Bank* bank, const DramaB200
     if (reinterpret_cast<uintptr_t>(workspace) & 255u) return fail("workspace must be 256-byte aligned");
     RowsWorkspace ws;
     expert_rows_workspace_layout(rows, b.hidden, b.intermediate, b.slots, static_cast<char*>(workspace), &ws);
+    const int me = peers->rank;
+    RowsReceive rc;
+    rc.signals = peers->signals[me];
+    rc.epoch = peers->epoch;
+    rc.ranks = peers->ranks;
+    rc.cap = peers->capacity;
+    rc.unused = b.slots;
+    rc.status = status;
     RowsScatter sc;
     sc.ranks = peers->ranks;
-    sc.rank = peers->rank;
+    sc.rank = me;
     sc.cap = peers->capacity;
-    for (int r = 0; r < peers->ranks; ++r) sc.dst[r] = static_cast<__nv_bfloat16*>(peers->back[r]);
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    cudaError_t err = expert_rows_launch(b, peers->recv[peers->rank], b.hidden + 8, rows, nullptr, DRAMA_B200_I32,
-                                         nullptr, ws, sms, s, &sc);
-    if (err == cudaSuccess) err = ep_p2p_signal_back_launch(*peers, s);
+    for (int r = 0; r < peers->ranks; ++r) {
+        sc.dst[r] = static_cast<__nv_bfloat16*>(peers->back[r]);
+        sc.signals[r] = peers->signals[r];
+    }
+    sc.done = peers->done + 16;   // the GEMM's own arrival counter, 64 bytes after the dispatch's
+    sc.epoch = peers->epoch;
+    const cudaError_t err = expert_rows_launch(b, peers->recv[me], b.hidden + 8, rows, nullptr, DRAMA_B200_I32,
+                                               nullptr, ws, sms, static_cast<cudaStream_t>(stream), &sc, &rc);
     if (err != cudaSuccess) return fail("peer expert-rows launch failed: %s", cudaGetErrorString(err));
     return 0;
 }
@@ -650,11 +655,11 @@ int drama_b200_ep_p2p_combine(const DramaB200EpPeers* peers, const int32_t* pair
     if (!aligned16(out) || (residual && !aligned16(residual))) return fail("out and residual must be 16-byte aligned");
     int sms = 0;
     if (sm_count_current(&sms)) return -1;
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    cudaError_t err = ep_p2p_wait_back_launch(*peers, status, s);
-    if (err == cudaSuccess)
-        err = ep_combine_launch(peers->back[peers->rank], peers->capacity * peers->ranks, pair_rows, weights,
-                                weights_dtype, tokens, top_k, peers->hidden, residual, out, sms, s);
+    const int me = peers->rank;
+    const cudaError_t err = ep_combine_launch(peers->back[me], peers->capacity * peers->ranks, pair_rows, weights,
+                                              weights_dtype, tokens, top_k, peers->hidden, residual, out, sms,
+                                              static_cast<cudaStream_t>(stream), peers->signals[me] + 2 * peers->ranks,
+                                              peers->epoch, peers->ranks, status);
     if (err != cudaSuccess) return fail("peer combine launch failed: %s", cudaGetErrorString(err));
     return 0;
 }

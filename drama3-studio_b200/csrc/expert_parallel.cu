@@ -20,6 +20,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "peer.cuh"
 
 namespace drama {
 namespace {
@@ -145,7 +146,9 @@ __global__ void ep_pack_kernel(const __nv_bfloat16* hidden, int64_t pairs, int t
 __global__ void ep_combine_kernel(const __nv_bfloat16* rows, int64_t row_count, const int32_t* pair_rows,
                                   const void* weights,
                                   int weights_dtype, int64_t tokens, int top_k, int H,
-                                  const __nv_bfloat16* residual, __nv_bfloat16* out) {
+                                  const __nv_bfloat16* residual, __nv_bfloat16* out, PeerWait wait) {
+    peer_wait_cta(wait);  // rows written by other ranks (peer exchange): their return flags first
+    const bool peer = wait.flags != nullptr;
     const int vec = H / 8;
     const int64_t n = tokens * vec;
     for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
@@ -157,8 +160,8 @@ __global__ void ep_combine_kernel(const __nv_bfloat16* rows, int64_t row_count, 
             const int64_t p = t * top_k + s;
             const int32_t row = __ldg(pair_rows + p);
             if (row < 0 || row >= row_count) continue;
-            combine_accumulate(acc, __ldg(reinterpret_cast<const uint4*>(rows + static_cast<int64_t>(row) * H + c)),
-                               load_any(weights, weights_dtype, p));
+            const uint4* src = reinterpret_cast<const uint4*>(rows + static_cast<int64_t>(row) * H + c);
+            combine_accumulate(acc, peer ? __ldcg(src) : __ldg(src), load_any(weights, weights_dtype, p));
         }
         uint32_t o[4];
         if (residual) {
@@ -205,13 +208,20 @@ cudaError_t ep_dispatch_launch(const void* hidden, int64_t tokens, int H, const 
     return cudaGetLastError();
 }
 
-cudaError_t ep_combine_launch(const void* rows, int64_t row_count, const int32_t* pair_rows, const void* weights, int weights_dtype,
-                              int64_t tokens, int top_k, int H, const void* residual, void* out, int sm_count,
-                              cudaStream_t s) {
-    if (tokens > 0)
+cudaError_t ep_combine_launch(const void* rows, int64_t row_count, const int32_t* pair_rows, const void* weights,
+                              int weights_dtype, int64_t tokens, int top_k, int H, const void* residual, void* out,
+                              int sm_count, cudaStream_t s, const int32_t* wait_flags, const int32_t* wait_epoch,
+                              int wait_ranks, int32_t* status) {
+    PeerWait w;
+    w.flags = wait_flags;
+    w.epoch = wait_epoch;
+    w.ranks = wait_ranks;
+    w.bit = 2;
+    w.status = status;
+    if (tokens > 0 || wait_flags)
         ep_combine_kernel<<<grid_for(tokens * (H / 8), sm_count), 256, 0, s>>>(
             static_cast<const __nv_bfloat16*>(rows), row_count, pair_rows, weights, weights_dtype, tokens, top_k, H,
-            static_cast<const __nv_bfloat16*>(residual), static_cast<__nv_bfloat16*>(out));
+            static_cast<const __nv_bfloat16*>(residual), static_cast<__nv_bfloat16*>(out), w);
     return cudaGetLastError();
 }
 

@@ -27,6 +27,7 @@
 #include "decode_tiles.cuh"
 #include "grouped.cuh"
 #include "kernels.h"
+#include "peer.cuh"
 
 namespace drama {
 
@@ -79,15 +80,42 @@ __device__ __forceinline__ uint4 pack_f16x8(const float (&v)[8], float inv) {
 // block maximum by shuffles. With `ids` set, the int32 at element H of each
 // row (a tagged row) is copied to ids[r].
 __global__ void rows_to_f16_kernel(const __nv_bfloat16* x, int64_t x_stride, int64_t rows, int H, __half* xh,
-                                   float* xs, int32_t* ids) {
+                                   float* xs, int32_t* ids, RowsReceive recv) {
+    // Rows written by other ranks: wait for their flags, then treat the rows of
+    // block s past count[s] as unused (id recv.unused, nothing converted).
+    __shared__ int s_count[8];
+    PeerWait pw;
+    pw.flags = recv.signals;
+    pw.epoch = recv.epoch;
+    pw.ranks = recv.ranks;
+    pw.bit = 1;
+    pw.status = recv.status;
+    peer_wait_cta(pw);
+    if (recv.signals) {
+        if (static_cast<int>(threadIdx.x) < recv.ranks)
+            s_count[threadIdx.x] = ld_acquire_sys(recv.signals + recv.ranks + threadIdx.x);
+        __syncthreads();
+    }
     const int64_t n = rows * (H / 8);
     const int64_t n_pad = (n + 31) & ~int64_t(31);   // whole warps iterate together (the shuffles)
     for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n_pad;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const bool ok = i < n;
         const int64_t r = i / (H / 8), c = i - r * (H / 8);
-        const uint4 q = ok ? __ldg(reinterpret_cast<const uint4*>(x + r * x_stride) + c) : make_uint4(0u, 0u, 0u, 0u);
-        if (ok && ids && c == 0) ids[r] = *reinterpret_cast<const int32_t*>(x + r * x_stride + H);
+        bool ok = i < n;
+        if (ok && recv.signals) {
+            const int64_t src = r / recv.cap;
+            if (r - src * recv.cap >= s_count[src]) {
+                ok = false;
+                if (c == 0) ids[r] = recv.unused;
+            }
+        }
+        // peer-written rows are read through L2 (never from a stale L1 line)
+        const uint4 q = ok ? (recv.signals ? __ldcg(reinterpret_cast<const uint4*>(x + r * x_stride) + c)
+                                           : __ldg(reinterpret_cast<const uint4*>(x + r * x_stride) + c))
+                           : make_uint4(0u, 0u, 0u, 0u);
+        if (ok && ids && c == 0)
+            ids[r] = recv.signals ? __ldcg(reinterpret_cast<const int32_t*>(x + r * x_stride + H))
+                                  : *reinterpret_cast<const int32_t*>(x + r * x_stride + H);
         const uint32_t w[4] = {q.x, q.y, q.z, q.w};
         float v[8];
         float m = 0.0f;
@@ -343,7 +371,18 @@ __global__ void __launch_bounds__(kSwThreads, 2) swap_gemm_kernel(SwapArgs a) {
         }
         __syncthreads();   // the next item's loads reuse the ring
     }
-    if (MODE == 1 && a.scatter.ranks > 0) __threadfence_system();  // peer stores visible before the signal kernel
+    if (MODE == 1 && a.scatter.ranks > 0) {
+        // every CTA's peer stores fenced; the last CTA to finish publishes the return flags
+        __threadfence_system();
+        __syncthreads();
+        if (tid == 0 && atomicAdd(a.scatter.done, 1) == static_cast<int>(gridDim.x) - 1) {
+            __threadfence_system();
+            const int e = *a.scatter.epoch;
+            for (int d = 0; d < a.scatter.ranks; ++d)
+                st_release_sys(a.scatter.signals[d] + 2 * a.scatter.ranks + a.scatter.rank, e);
+            *a.scatter.done = 0;
+        }
+    }
 }
 
 int grid_for(int64_t work, int sm_count) {
@@ -377,7 +416,7 @@ size_t expert_rows_workspace_layout(int64_t rows, int hidden, int intermediate, 
 
 cudaError_t expert_rows_launch(const DramaB200Fp8Bank& bank, const void* x, int64_t x_stride, int64_t rows,
                                const void* ids, int ids_dtype, void* out, const RowsWorkspace& ws, int sm_count,
-                               cudaStream_t s, const RowsScatter* scatter) {
+                               cudaStream_t s, const RowsScatter* scatter, const RowsReceive* receive) {
     static bool configured = false;  // benign race: identical values
     if (!configured) {
         cudaError_t err = cudaFuncSetAttribute(swap_gemm_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -388,7 +427,8 @@ cudaError_t expert_rows_launch(const DramaB200Fp8Bank& bank, const void* x, int6
         configured = true;
     }
     rows_to_f16_kernel<<<grid_for(rows * (bank.hidden / 8), sm_count), 256, 0, s>>>(
-        static_cast<const __nv_bfloat16*>(x), x_stride, rows, bank.hidden, ws.xh, ws.xs, ids ? nullptr : ws.ids);
+        static_cast<const __nv_bfloat16*>(x), x_stride, rows, bank.hidden, ws.xh, ws.xs, ids ? nullptr : ws.ids,
+        receive ? *receive : RowsReceive{});
     cudaError_t err = cudaGetLastError();
     if (err != cudaSuccess) return err;
     PermuteArgs pa{ids ? ids : ws.ids, ids ? ids_dtype : DRAMA_B200_I32, rows, bank.slots, ws.order, ws.counts,

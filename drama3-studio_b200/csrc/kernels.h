@@ -182,15 +182,30 @@ size_t expert_rows_workspace_layout(int64_t rows, int hidden, int intermediate, 
                                     RowsWorkspace* ws);
 // GEMM 1 rows written to other ranks: received row r (from rank r / cap) goes
 // to dst[r / cap] + (rank * cap + r % cap) * H.
+// After the last CTA of GEMM 1: signals[d][2 * ranks + rank] = *epoch for every d.
 struct RowsScatter {
     int ranks = 0;            // 0: no scatter
     int rank = 0;
     int64_t cap = 0;
     __nv_bfloat16* dst[8] = {};
+    int32_t* signals[8] = {};
+    int32_t* done = nullptr;
+    const int32_t* epoch = nullptr;
+};
+// Rows written by other ranks into blocks of `cap`: wait for signals[0, ranks)
+// == *epoch; rows of block s past signals[ranks + s] get id `unused`.
+struct RowsReceive {
+    const int32_t* signals = nullptr;  // null: plain rows
+    const int32_t* epoch = nullptr;
+    int ranks = 0;
+    int64_t cap = 0;
+    int unused = 0;
+    int32_t* status = nullptr;
 };
 cudaError_t expert_rows_launch(const DramaB200Fp8Bank& bank, const void* x, int64_t x_stride, int64_t rows,
                                const void* ids, int ids_dtype, void* out, const RowsWorkspace& ws, int sm_count,
-                               cudaStream_t s, const RowsScatter* scatter = nullptr);
+                               cudaStream_t s, const RowsScatter* scatter = nullptr,
+                               const RowsReceive* receive = nullptr);
 
 // Expert-parallel exchange (expert_parallel.cu).
 constexpr int kMaxEpRanks = 8;
@@ -198,18 +213,16 @@ cudaError_t ep_dispatch_launch(const void* hidden, int64_t tokens, int H, const 
                                int experts, int ranks, const int32_t* placement, int64_t cap, void* send_rows,
                                int64_t row_stride, int32_t* send_ids, int32_t* pair_rows, int32_t* status,
                                int sm_count, cudaStream_t s);
-cudaError_t ep_combine_launch(const void* rows, int64_t row_count, const int32_t* pair_rows, const void* weights, int weights_dtype,
-                              int64_t tokens, int top_k, int H, const void* residual, void* out, int sm_count,
-                              cudaStream_t s);
+cudaError_t ep_combine_launch(const void* rows, int64_t row_count, const int32_t* pair_rows, const void* weights,
+                              int weights_dtype, int64_t tokens, int top_k, int H, const void* residual, void* out,
+                              int sm_count, cudaStream_t s, const int32_t* wait_flags = nullptr,
+                              const int32_t* wait_epoch = nullptr, int wait_ranks = 0, int32_t* status = nullptr);
 
 // Expert-parallel exchange over peer memory (ep_p2p.cu).
+constexpr int kP2pMaxPairs = 4096;  // (token, slot) pairs per rank and layer of the fused peer dispatch
 cudaError_t ep_p2p_dispatch_launch(const DramaB200EpPeers& peers, const void* hidden, int64_t tokens,
                                    const void* ids, int ids_dtype, int top_k, const int32_t* placement,
-                                   int32_t* pair_rows, int32_t* scratch, int32_t* status, int sm_count,
-                                   cudaStream_t s);
-cudaError_t ep_p2p_receive_launch(const DramaB200EpPeers& peers, int32_t* status, cudaStream_t s);
-cudaError_t ep_p2p_signal_back_launch(const DramaB200EpPeers& peers, cudaStream_t s);
-cudaError_t ep_p2p_wait_back_launch(const DramaB200EpPeers& peers, int32_t* status, cudaStream_t s);
+                                   int32_t* pair_rows, int32_t* status, int sm_count, cudaStream_t s);
 
 size_t prefill_workspace_layout(int64_t tokens, int top_k, int hidden, int intermediate, int experts, char* base,
                                 PrefillWorkspace* ws);

@@ -56,7 +56,6 @@ EXPORTS = (
     "drama_b200_ipc_open",
     "drama_b200_ipc_close",
     "drama_b200_ep_p2p_dispatch",
-    "drama_b200_ep_p2p_receive",
     "drama_b200_fp8_expert_rows_p2p",
     "drama_b200_ep_p2p_combine",
     "drama_b200_stage_copies",
@@ -168,14 +167,14 @@ class Library:
         dll.drama_b200_ipc_close.argtypes = [c_void_p]
         peers = ctypes.POINTER(EpPeers)
         dll.drama_b200_ep_p2p_dispatch.argtypes = [peers, c_void_p, c_int64, c_void_p, c_int, c_int, c_void_p,
-                                                   c_void_p, c_void_p, c_void_p, c_void_p]
-        dll.drama_b200_ep_p2p_receive.argtypes = [peers, c_void_p, c_void_p]
-        dll.drama_b200_fp8_expert_rows_p2p.argtypes = [ctypes.POINTER(Fp8Bank), peers, c_void_p, c_size_t, c_void_p]
+                                                   c_void_p, c_void_p, c_void_p]
+        dll.drama_b200_fp8_expert_rows_p2p.argtypes = [ctypes.POINTER(Fp8Bank), peers, c_void_p, c_size_t, c_void_p,
+                                                       c_void_p]
         dll.drama_b200_ep_p2p_combine.argtypes = [peers, c_void_p, c_void_p, c_int, c_int64, c_int, c_void_p,
                                                   c_void_p, c_void_p, c_void_p]
         for name in ("drama_b200_ep_buffers_alloc", "drama_b200_ep_buffers_free", "drama_b200_ipc_handle",
                      "drama_b200_ipc_open", "drama_b200_ipc_close", "drama_b200_ep_p2p_dispatch",
-                     "drama_b200_ep_p2p_receive", "drama_b200_fp8_expert_rows_p2p", "drama_b200_ep_p2p_combine"):
+                     "drama_b200_fp8_expert_rows_p2p", "drama_b200_ep_p2p_combine"):
             getattr(dll, name).restype = c_int
         for name in ("drama_b200_device_check", "drama_b200_route_topk", "drama_b200_permute_routes",
                      "drama_b200_fp8_decode", "drama_b200_int4_decode", "drama_b200_fp8_moe_layer",

@@ -241,7 +241,6 @@ class ExpertParallelMoE:
         if exchange == "p2p":
             self.peer_exchange = PeerExchange(ranks=ranks, rank=rank, capacity=self.capacity, hidden=self.hidden,
                                               experts=experts, device=self.device, group=group)
-            self.scratch = torch.zeros(self.tokens * self.top_k + 8, dtype=torch.int32, device=self.device)
 
     def _allocate(self) -> ExchangeBuffers:
         rows = self.ranks * self.capacity
@@ -297,11 +296,9 @@ class ExpertParallelMoE:
         bank, _ = self._banks[layer]
         lib.check(lib.dll.drama_b200_ep_p2p_dispatch(
             peers, h.data_ptr(), self.tokens, ids.data_ptr(), _lib.DTYPE_CODES[ids.dtype], self.top_k,
-            _lib.ptr(self.placements[layer]), b.pair_rows.data_ptr(), self.scratch.data_ptr(), b.status.data_ptr(),
-            stream))
-        lib.check(lib.dll.drama_b200_ep_p2p_receive(peers, b.status.data_ptr(), stream))
+            _lib.ptr(self.placements[layer]), b.pair_rows.data_ptr(), b.status.data_ptr(), stream))
         lib.check(lib.dll.drama_b200_fp8_expert_rows_p2p(ctypes.byref(bank), peers, b.workspace.data_ptr(),
-                                                         b.workspace.numel(), stream))
+                                                         b.workspace.numel(), b.status.data_ptr(), stream))
         lib.check(lib.dll.drama_b200_ep_p2p_combine(
             peers, b.pair_rows.data_ptr(), weights.data_ptr(), _lib.DTYPE_CODES[weights.dtype], self.tokens,
             self.top_k, h.data_ptr(), out.data_ptr(), b.status.data_ptr(), stream))
@@ -347,8 +344,9 @@ class ExpertParallelMoE:
 
     def launches_per_layer(self) -> int:
         """Kernels of this library per layer."""
-        # nccl: plan + pack, row prep + permute + 2 GEMMs, combine; p2p adds the receive, signal and wait kernels
-        return 10 if self.exchange == "p2p" else 7
+        # nccl: plan + pack, row prep + permute + 2 GEMMs, combine; p2p: dispatch, row prep + permute + 2 GEMMs,
+        # combine
+        return 6 if self.exchange == "p2p" else 7
 
     def dropped(self) -> tuple[int, int]:
         """(pairs with an out-of-range id, pairs over capacity) of the last layer (synchronises)."""

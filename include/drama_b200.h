@@ -336,12 +336,13 @@ DRAMA_B200_API int drama_b200_ep_combine(const void* rows, int64_t row_count, co
  *   signals [3 * ranks] int32 (zeroed): dispatch flags, row counts, return
  *           flags; epoch and done are this rank's own counters (zeroed).
  * A layer is, in stream order on every rank:
- *   drama_b200_ep_p2p_dispatch   (rows into the owners' recv, then flags)
- *   drama_b200_ep_p2p_receive    (wait for every source, mark unused rows)
- *   drama_b200_fp8_expert_rows_p2p (GEMMs; results into the sources' back)
- *   drama_b200_ep_p2p_combine    (wait for every expert rank, slot-order sum)
+ *   drama_b200_ep_p2p_dispatch     (rows into the owners' recv, then flags)
+ *   drama_b200_fp8_expert_rows_p2p (waits for every source; results into
+ *                                   the sources' back, then return flags)
+ *   drama_b200_ep_p2p_combine      (waits for every expert rank; slot sum)
  * Every rank must issue the same sequence of layers. Waits give up after 2 s
- * and set status[2]; the result of that step is then invalid.
+ * and set status[2]; the result of that step is then invalid. The counters
+ * block (epoch, dispatch and GEMM arrival counts) is 256 zeroed bytes.
  * ------------------------------------------------------------------------- */
 typedef struct DramaB200EpPeers {
     int32_t ranks, rank;
@@ -351,7 +352,7 @@ typedef struct DramaB200EpPeers {
     void* back[8];
     int32_t* signals[8];
     int32_t* epoch;             /* this rank's step counter */
-    int32_t* done;              /* this rank's arrival counter of the dispatch kernel */
+    int32_t* done;              /* this rank's arrival counters (32 int32, zeroed) */
 } DramaB200EpPeers;
 
 DRAMA_B200_API int drama_b200_ep_buffers_alloc(int ranks, int64_t capacity, int hidden, void** recv, void** back,
@@ -366,17 +367,16 @@ DRAMA_B200_API int drama_b200_ipc_open(const void* handle, void** device_ptr);
 
 DRAMA_B200_API int drama_b200_ipc_close(void* device_ptr);
 
-/* scratch: int32 [tokens * top_k + ranks]; pair_rows as drama_b200_ep_dispatch. */
+/* pair_rows as drama_b200_ep_dispatch; tokens * top_k <= 4096. */
 DRAMA_B200_API int drama_b200_ep_p2p_dispatch(const DramaB200EpPeers* peers, const void* hidden, int64_t tokens,
                                               const void* ids, int ids_dtype, int top_k,
-                                              const int32_t* placement, int32_t* pair_rows, int32_t* scratch,
-                                              int32_t* status, void* stream);
-
-DRAMA_B200_API int drama_b200_ep_p2p_receive(const DramaB200EpPeers* peers, int32_t* status, void* stream);
+                                              const int32_t* placement, int32_t* pair_rows, int32_t* status,
+                                              void* stream);
 
 /* workspace: drama_b200_expert_rows_workspace_bytes(ranks * capacity, ...). */
 DRAMA_B200_API int drama_b200_fp8_expert_rows_p2p(const DramaB200Fp8Bank* bank, const DramaB200EpPeers* peers,
-                                                  void* workspace, size_t workspace_bytes, void* stream);
+                                                  void* workspace, size_t workspace_bytes, int32_t* status,
+                                                  void* stream);
 
 DRAMA_B200_API int drama_b200_ep_p2p_combine(const DramaB200EpPeers* peers, const int32_t* pair_rows,
                                              const void* weights, int weights_dtype, int64_t tokens, int top_k,
