@@ -12,6 +12,8 @@
 //
 // A pageable source would turn cudaMemcpyAsync into a staged, synchronous
 // copy and quietly remove the overlap, so it is rejected instead.
+#include <unistd.h>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -80,6 +82,45 @@ int drama_b200_stage_copies(const void* const* host_src, void* const* dev_dst, c
     if (done_event) {
         const cudaError_t err = cudaEventRecord(static_cast<cudaEvent_t>(done_event), stream);
         if (err != cudaSuccess) return fail("cudaEventRecord: %s", cudaGetErrorString(err));
+    }
+    return 0;
+}
+
+int drama_b200_host_register(void* host_ptr, uint64_t bytes, int read_only, void** registered_base,
+                              uint64_t* registered_bytes) {
+    if (!host_ptr || bytes == 0) return fail("host_ptr and a non-zero byte count are required");
+    if (!registered_base || !registered_bytes) return fail("registered_base and registered_bytes are required");
+    const long page = sysconf(_SC_PAGESIZE);
+    if (page <= 0) return fail("sysconf(_SC_PAGESIZE) failed");
+    const uintptr_t p = reinterpret_cast<uintptr_t>(host_ptr);
+    const uintptr_t start = p / page * page;
+    const uintptr_t end = (p + bytes + page - 1) / page * page;
+    unsigned flags = cudaHostRegisterPortable;
+    if (read_only) {
+        int dev = 0, supported = 0;
+        cudaError_t err = cudaGetDevice(&dev);
+        if (err == cudaSuccess) err = cudaDeviceGetAttribute(&supported, cudaDevAttrHostRegisterReadOnlySupported, dev);
+        if (err != cudaSuccess) return fail("querying read-only host registration: %s", cudaGetErrorString(err));
+        if (!supported) return fail("device %d cannot register read-only host memory", dev);
+        flags |= cudaHostRegisterReadOnly;
+    }
+    const cudaError_t err = cudaHostRegister(reinterpret_cast<void*>(start), end - start, flags);
+    if (err != cudaSuccess) {
+        cudaGetLastError();
+        return fail("cudaHostRegister of %llu bytes at %p: %s", (unsigned long long)(end - start),
+                    reinterpret_cast<void*>(start), cudaGetErrorString(err));
+    }
+    *registered_base = reinterpret_cast<void*>(start);
+    *registered_bytes = end - start;
+    return 0;
+}
+
+int drama_b200_host_unregister(void* registered_base) {
+    if (!registered_base) return fail("registered_base is required");
+    const cudaError_t err = cudaHostUnregister(registered_base);
+    if (err != cudaSuccess) {
+        cudaGetLastError();
+        return fail("cudaHostUnregister(%p): %s", registered_base, cudaGetErrorString(err));
     }
     return 0;
 }

@@ -59,6 +59,8 @@ EXPORTS = (
     "drama_b200_fp8_expert_rows_p2p",
     "drama_b200_ep_p2p_combine",
     "drama_b200_stage_copies",
+    "drama_b200_host_register",
+    "drama_b200_host_unregister",
 )
 
 c_void_p, c_int, c_int64, c_size_t = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_size_t
@@ -147,6 +149,9 @@ class Library:
         dll.drama_b200_fp8_decode_static.restype = c_int
         dll.drama_b200_stage_copies.argtypes = [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p]
         dll.drama_b200_stage_copies.restype = c_int
+        dll.drama_b200_host_register.argtypes = [c_void_p, ctypes.c_uint64, c_int, ctypes.POINTER(c_void_p),
+                                                 ctypes.POINTER(ctypes.c_uint64)]
+        dll.drama_b200_host_unregister.argtypes = [c_void_p]
         dll.drama_b200_expert_rows_workspace_bytes.argtypes = [c_int64, c_int, c_int, c_int]
         dll.drama_b200_expert_rows_workspace_bytes.restype = c_size_t
         dll.drama_b200_fp8_expert_rows.argtypes = [ctypes.POINTER(Fp8Bank), c_void_p, c_int64, c_int64, c_void_p,

@@ -1,0 +1,315 @@
+"""Expert cache files as a staging source: read-only mmap, page-locked in place.
+
+On-disk format (kept identical so caches move between the two implementations):
+the reference's ``"drama3-official-fp8-experts"`` version 1
+(src/drama_low_vram/expert_cache_file.py:28-33 names, 113-153 layout, 378-395
+manifest, 426-471 reader checks). ``experts.bin`` holds, for layer 0, 1, ...
+in turn, the four role tensors of ``ExpertStore`` back to back with no padding:
+
+    w13_weight    [E, 2I, H]          float8_e4m3fn  (gate rows, then up rows)
+    w13_scale_inv [E, 2I/128, H/128]  float32
+    w2_weight     [E, H, I]           float8_e4m3fn
+    w2_scale_inv  [E, H/128, I/128]   float32
+
+``manifest.json`` records the model geometry, every buffer's shape, dtype,
+byte offset and size, the data file's size and SHA-256, and a model
+fingerprint.
+
+What this module adds for the B200 path is ``ExpertCacheFile.register``: it
+page-locks a layer window of the read-only mapping where it lies
+(``drama_b200_host_register`` with ``cudaHostRegisterReadOnly``), after which
+the layer's role views are page-locked tensors and ``StagingArena`` copies each
+requested expert straight from the page cache into its HBM slot (four DMAs per
+expert, one per role, merged where experts are adjacent). The reference reads
+the same mapping through a host gather into a pinned bounce buffer before every
+copy (offload.py:561-594); an unregistered cache still takes that route
+through the arena's bounce path.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import hashlib
+import json
+import math
+import mmap
+import re
+import sys
+import warnings
+from pathlib import Path
+from typing import Any
+
+import torch
+from torch import Tensor
+
+from . import _lib
+from .staging import EXPERT_BUFFER_NAMES, StagedExperts
+
+CACHE_FORMAT = "drama3-official-fp8-experts"
+CACHE_FORMAT_VERSION = 1
+MANIFEST_NAME = "manifest.json"
+DATA_NAME = "experts.bin"
+BLOCK = 128
+_CHUNK = 1 << 20
+_SHA256 = re.compile(r"[a-f0-9]{64}")
+# role -> (torch dtype, manifest dtype name, element size)
+ROLE_DTYPES = {
+    "w13_weight": (torch.float8_e4m3fn, "float8_e4m3fn", 1),
+    "w13_scale_inv": (torch.float32, "float32", 4),
+    "w2_weight": (torch.float8_e4m3fn, "float8_e4m3fn", 1),
+    "w2_scale_inv": (torch.float32, "float32", 4),
+}
+
+
+def _int_field(value: Any, label: str, minimum: int = 0) -> int:
+    if isinstance(value, bool) or not isinstance(value, int) or value < minimum:
+        raise ValueError(f"{label} must be an integer >= {minimum}")
+    return value
+
+
+def role_shapes(num_experts: int, hidden: int, intermediate: int) -> dict[str, tuple[int, int, int]]:
+    return {
+        "w13_weight": (num_experts, 2 * intermediate, hidden),
+        "w13_scale_inv": (num_experts, 2 * intermediate // BLOCK, hidden // BLOCK),
+        "w2_weight": (num_experts, hidden, intermediate),
+        "w2_scale_inv": (num_experts, hidden // BLOCK, intermediate // BLOCK),
+    }
+
+
+def cache_layout(num_layers: int, num_experts: int, hidden: int,
+                 intermediate: int) -> tuple[list[dict[str, Any]], int]:
+    """Per-layer buffer records of the manifest and the data file's size."""
+    for label, value in (("num_layers", num_layers), ("num_experts", num_experts), ("hidden", hidden),
+                         ("intermediate", intermediate)):
+        _int_field(value, label, 1)
+    if hidden % BLOCK or intermediate % BLOCK:
+        raise ValueError("Expert dimensions must be divisible by the FP8 block size")
+    shapes = role_shapes(num_experts, hidden, intermediate)
+    layers, offset = [], 0
+    for index in range(num_layers):
+        buffers = {}
+        for name in EXPERT_BUFFER_NAMES:
+            _, dtype_name, size = ROLE_DTYPES[name]
+            nbytes = math.prod(shapes[name]) * size
+            buffers[name] = {"shape": list(shapes[name]), "dtype": dtype_name, "offset": offset, "nbytes": nbytes}
+            offset += nbytes
+        layers.append({"index": index, "buffers": buffers})
+    return layers, offset
+
+
+def write_expert_cache(cache_dir: str | Path, layers: list[dict[str, Tensor]], *,
+                       model_fingerprint: str | None = None, source: dict[str, Any] | None = None) -> Path:
+    """Write ``layers`` (one ``ExpertStore``-shaped dict per layer) as a cache directory.
+
+    The reference builds caches from a safetensors checkpoint
+    (``build_expert_cache``); this writes banks already in memory, in the same
+    format. ``model_fingerprint`` defaults to the SHA-256 of the geometry.
+    """
+    if not layers:
+        raise ValueError("An expert cache needs at least one layer")
+    experts, gate_up, hidden = layers[0]["w13_weight"].shape
+    inter = gate_up // 2
+    records, total = cache_layout(len(layers), experts, hidden, inter)
+    cache_dir = Path(cache_dir)
+    cache_dir.mkdir(parents=True, exist_ok=True)
+    digest = hashlib.sha256()
+    written = 0
+    with (cache_dir / DATA_NAME).open("wb") as handle:
+        for index, bank in enumerate(layers):
+            for name in EXPERT_BUFFER_NAMES:
+                spec = records[index]["buffers"][name]
+                t = bank[name]
+                if list(t.shape) != spec["shape"] or t.dtype != ROLE_DTYPES[name][0]:
+                    raise ValueError(f"layer {index} {name}: shape/dtype mismatch")
+                raw = t.detach().cpu().contiguous().view(torch.uint8).numpy().tobytes()
+                handle.write(raw)
+                digest.update(raw)
+                written += len(raw)
+    if written != total:
+        raise ValueError(f"Expert cache byte count mismatch: {written} != {total}")
+    model = {"model_type": "fish_omni", "num_layers": len(layers), "num_experts": experts, "hidden": hidden,
+             "intermediate": inter, "block_size": BLOCK}
+    if model_fingerprint is None:
+        model_fingerprint = hashlib.sha256(json.dumps(model, sort_keys=True).encode()).hexdigest()
+    manifest = {
+        "format": CACHE_FORMAT,
+        "format_version": CACHE_FORMAT_VERSION,
+        "byte_order": "little",
+        "model_fingerprint": model_fingerprint,
+        "model": model,
+        "source": source if source is not None else {},
+        "data": {"name": DATA_NAME, "size": total, "sha256": digest.hexdigest()},
+        "layers": records,
+    }
+    with (cache_dir / MANIFEST_NAME).open("w", encoding="utf-8", newline="\n") as handle:
+        json.dump(manifest, handle, indent=2, sort_keys=True)
+        handle.write("\n")
+    return cache_dir
+
+
+class ExpertCacheFile:
+    """A validated expert cache: read-only mapping, zero-copy role views, page locking."""
+
+    def __init__(self, cache_dir: Path, manifest: dict[str, Any]) -> None:
+        self.cache_dir = Path(cache_dir)
+        self.manifest = manifest
+        if manifest.get("format") != CACHE_FORMAT:
+            raise ValueError("Unsupported expert cache format")
+        if manifest.get("format_version") != CACHE_FORMAT_VERSION:
+            raise ValueError("Unsupported expert cache version")
+        if manifest.get("byte_order") != "little" or sys.byteorder != "little":
+            raise ValueError("Expert cache requires little-endian byte order")
+        model = manifest.get("model")
+        if not isinstance(model, dict) or model.get("model_type") != "fish_omni":
+            raise ValueError("Expert cache is not a Fish Omni model")
+        if model.get("block_size") != BLOCK:
+            raise ValueError("Unsupported expert block size")
+        self.num_layers = _int_field(model.get("num_layers"), "num_layers", 1)
+        self.num_experts = _int_field(model.get("num_experts"), "num_experts", 1)
+        self.hidden = _int_field(model.get("hidden"), "hidden", 1)
+        self.intermediate = _int_field(model.get("intermediate"), "intermediate", 1)
+        self._layers, self.nbytes = cache_layout(self.num_layers, self.num_experts, self.hidden, self.intermediate)
+        if manifest.get("layers") != self._layers:
+            raise ValueError("Expert cache buffer layout mismatch")
+        data = manifest.get("data")
+        if not isinstance(data, dict) or data.get("name") != DATA_NAME:
+            raise ValueError("Invalid expert cache data filename")
+        if _int_field(data.get("size"), "data size", 1) != self.nbytes:
+            raise ValueError("Expert cache data size mismatch")
+        if not isinstance(data.get("sha256"), str) or not _SHA256.fullmatch(data["sha256"]):
+            raise ValueError("Invalid expert cache data SHA256")
+        fingerprint = manifest.get("model_fingerprint")
+        if not isinstance(fingerprint, str) or not _SHA256.fullmatch(fingerprint):
+            raise ValueError("Invalid expert cache model fingerprint")
+        self.model_fingerprint = fingerprint
+        self._data_path = self.cache_dir / DATA_NAME
+        if not self._data_path.is_file() or self._data_path.stat().st_size != self.nbytes:
+            raise ValueError("Expert cache file is truncated or has extra data")
+        self._mmap: mmap.mmap | None = None
+        self._mapping: Tensor | None = None
+        self._stores: dict[int, StagedExperts] = {}
+        self._registered: list[tuple[int, int, int, int]] = []  # (base, bytes, first layer, end layer)
+        self._closed = False
+
+    @classmethod
+    def open(cls, cache_dir: str | Path, *, verify_data: bool = False) -> "ExpertCacheFile":
+        cache_dir = Path(cache_dir).resolve()
+        raw = (cache_dir / MANIFEST_NAME).read_bytes()
+        try:
+            manifest = json.loads(raw)
+        except (UnicodeDecodeError, json.JSONDecodeError) as exc:
+            raise ValueError(f"Invalid JSON file: {cache_dir / MANIFEST_NAME}") from exc
+        if not isinstance(manifest, dict):
+            raise ValueError(f"Expected a JSON object: {cache_dir / MANIFEST_NAME}")
+        cache = cls(cache_dir, manifest)
+        if verify_data:
+            cache.verify_data()
+        return cache
+
+    def verify_data(self) -> None:
+        digest = hashlib.sha256()
+        with self._data_path.open("rb") as handle:
+            while chunk := handle.read(_CHUNK):
+                digest.update(chunk)
+        if digest.hexdigest() != self.manifest["data"]["sha256"]:
+            raise ValueError("Expert cache data checksum mismatch")
+
+    # -- mapping and views ---------------------------------------------------
+    def _map(self) -> Tensor:
+        if self._closed:
+            raise RuntimeError("Expert cache is closed")
+        if self._mapping is None:
+            with self._data_path.open("rb") as handle:
+                self._mmap = mmap.mmap(handle.fileno(), self.nbytes, access=mmap.ACCESS_READ)
+            with warnings.catch_warnings():
+                warnings.filterwarnings("ignore", message="The given buffer is not writable", category=UserWarning)
+                self._mapping = torch.frombuffer(self._mmap, dtype=torch.uint8, count=self.nbytes)
+        return self._mapping
+
+    def _check_layer(self, layer: int) -> None:
+        if not isinstance(layer, int) or isinstance(layer, bool) or not 0 <= layer < self.num_layers:
+            raise IndexError(f"Invalid expert cache layer index: {layer}")
+
+    def layer_span(self, layer: int) -> tuple[int, int]:
+        """(byte offset, byte count) of one layer in the data file."""
+        self._check_layer(layer)
+        buffers = self._layers[layer]["buffers"]
+        start = buffers[EXPERT_BUFFER_NAMES[0]]["offset"]
+        last = buffers[EXPERT_BUFFER_NAMES[-1]]
+        return start, last["offset"] + last["nbytes"] - start
+
+    def layer_buffers(self, layer: int) -> dict[str, Tensor]:
+        """Zero-copy, read-only role views of one layer (must not be written)."""
+        self._check_layer(layer)
+        mapping = self._map()
+        out = {}
+        for name in EXPERT_BUFFER_NAMES:
+            spec = self._layers[layer]["buffers"][name]
+            out[name] = mapping.narrow(0, spec["offset"], spec["nbytes"]).view(ROLE_DTYPES[name][0]).view(spec["shape"])
+        return out
+
+    def layer_store(self, layer: int) -> StagedExperts:
+        """The layer as a ``StagingArena`` store; the same object for every call, so
+        the arena's reuse rule (same ids from the same store) applies."""
+        store = self._stores.get(layer)
+        if store is None:
+            store = StagedExperts(**self.layer_buffers(layer))
+            self._stores[layer] = store
+        return store
+
+    # -- page locking ----------------------------------------------------------
+    def register(self, first: int = 0, count: int | None = None) -> int:
+        """Page-lock layers ``[first, first + count)`` (default: all) in place.
+
+        Returns the number of bytes locked (the window widened to whole pages).
+        A window may not overlap one already registered.
+        """
+        count = self.num_layers - first if count is None else count
+        self._check_layer(first)
+        if count < 1 or first + count > self.num_layers:
+            raise IndexError("Layer window outside the expert cache")
+        for _, _, a, b in self._registered:
+            if first < b + 1 and a < first + count + 1:  # page widening can make neighbours touch
+                raise ValueError(f"Layers [{first}, {first + count}) overlap or adjoin registered layers [{a}, {b})")
+        start = self.layer_span(first)[0]
+        end_off, end_len = self.layer_span(first + count - 1)
+        mapping = self._map()
+        base, size = ctypes.c_void_p(), ctypes.c_uint64()
+        lib = _lib.library()
+        lib.check(lib.dll.drama_b200_host_register(mapping.data_ptr() + start, end_off + end_len - start, 1,
+                                                   ctypes.byref(base), ctypes.byref(size)))
+        self._registered.append((base.value, size.value, first, first + count))
+        return size.value
+
+    @property
+    def registered_layers(self) -> list[tuple[int, int]]:
+        return [(a, b) for _, _, a, b in self._registered]
+
+    def unregister(self) -> None:
+        """Release every page-locked window. Copies reading them must be complete."""
+        if not self._registered:
+            return
+        if torch.cuda.is_initialized():
+            torch.cuda.synchronize()
+        lib = _lib.library()
+        while self._registered:
+            base, _, _, _ = self._registered.pop()
+            lib.check(lib.dll.drama_b200_host_unregister(base))
+
+    def close(self) -> None:
+        """Unregister and drop this object's views; tensors already handed out keep the mapping alive."""
+        self.unregister()
+        self._stores.clear()
+        self._mapping = None
+        self._mmap = None
+        self._closed = True
+
+    def __enter__(self) -> "ExpertCacheFile":
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self.close()
+
+
+__all__ = ["CACHE_FORMAT", "CACHE_FORMAT_VERSION", "DATA_NAME", "MANIFEST_NAME", "ExpertCacheFile",
+           "cache_layout", "write_expert_cache"]

@@ -403,6 +403,27 @@ DRAMA_B200_API int drama_b200_stage_copies(const void* const* host_src, void* co
                                            const uint64_t* bytes, int count, void* copy_stream,
                                            void* wait_event, void* done_event);
 
+/* ---------------------------------------------------------------------------
+ * Host byte sources for staging: page-lock an existing host range, e.g. a
+ * read-only mmap of an expert cache file (experts.bin, manifest format
+ * "drama3-official-fp8-experts" v1, src/drama_low_vram/expert_cache_file.py:
+ * 28-33, 112-153, 526-556), so that drama_b200_stage_copies can DMA expert
+ * rows straight out of the mapping. The reference instead gathers those rows
+ * into a pinned bounce buffer on the host (offload.py:561-594, native
+ * drama_gather_rows, native/include/drama_native.h:28) before each copy.
+ *
+ * [host_ptr, host_ptr + bytes) is widened to whole pages and registered with
+ * cudaHostRegisterPortable, plus cudaHostRegisterReadOnly when read_only is
+ * non-zero (required for a PROT_READ mapping; refused when the device cannot
+ * do it). The widened range is returned in registered_base/registered_bytes;
+ * pass registered_base to drama_b200_host_unregister. Ranges that share a page
+ * cannot both be registered.
+ * ------------------------------------------------------------------------- */
+DRAMA_B200_API int drama_b200_host_register(void* host_ptr, uint64_t bytes, int read_only,
+                                            void** registered_base, uint64_t* registered_bytes);
+
+DRAMA_B200_API int drama_b200_host_unregister(void* registered_base);
+
 #ifdef __cplusplus
 }
 #endif
