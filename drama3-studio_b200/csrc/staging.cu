@@ -49,10 +49,14 @@ int drama_b200_stage_copies(const void* const* host_src, void* const* dev_dst, c
         if (bytes[i] == 0) return fail("copy %d has zero bytes", i);
         cudaMemoryType type;
         int device = -1;
-        if (pointer_kind(host_src[i], &type, &device)) return -1;
-        if (type != cudaMemoryTypeHost)
-            return fail("copy %d: source %p is not page-locked host memory (pin it or cudaHostRegister it)", i,
-                        host_src[i]);
+        // both ends: a registered range may cover the start of a source but not its end
+        const void* last = static_cast<const char*>(host_src[i]) + (bytes[i] - 1);
+        for (const void* q : {host_src[i], last}) {
+            if (pointer_kind(q, &type, &device)) return -1;
+            if (type != cudaMemoryTypeHost)
+                return fail("copy %d: source byte %p is not page-locked host memory (pin it or cudaHostRegister it)",
+                            i, q);
+        }
         if (pointer_kind(dev_dst[i], &type, &device)) return -1;
         if (type != cudaMemoryTypeDevice) return fail("copy %d: destination %p is not device memory", i, dev_dst[i]);
         if (dst_device < 0) dst_device = device;
@@ -112,6 +116,23 @@ int drama_b200_host_register(void* host_ptr, uint64_t bytes, int read_only, void
     }
     *registered_base = reinterpret_cast<void*>(start);
     *registered_bytes = end - start;
+    return 0;
+}
+
+int drama_b200_host_locked(const void* host_ptr, uint64_t bytes, int* locked) {
+    if (!locked) return fail("locked is required");
+    *locked = 0;
+    if (!host_ptr || bytes == 0) return fail("host_ptr and a non-zero byte count are required");
+    const void* last = static_cast<const char*>(host_ptr) + (bytes - 1);
+    for (const void* q : {host_ptr, last}) {
+        cudaPointerAttributes attr{};
+        if (cudaPointerGetAttributes(&attr, q) != cudaSuccess) {
+            cudaGetLastError();
+            return 0;
+        }
+        if (attr.type != cudaMemoryTypeHost) return 0;
+    }
+    *locked = 1;
     return 0;
 }
 

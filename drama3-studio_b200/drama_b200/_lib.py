@@ -61,6 +61,7 @@ EXPORTS = (
     "drama_b200_stage_copies",
     "drama_b200_host_register",
     "drama_b200_host_unregister",
+    "drama_b200_host_locked",
 )
 
 c_void_p, c_int, c_int64, c_size_t = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_size_t
@@ -152,6 +153,7 @@ class Library:
         dll.drama_b200_host_register.argtypes = [c_void_p, ctypes.c_uint64, c_int, ctypes.POINTER(c_void_p),
                                                  ctypes.POINTER(ctypes.c_uint64)]
         dll.drama_b200_host_unregister.argtypes = [c_void_p]
+        dll.drama_b200_host_locked.argtypes = [c_void_p, ctypes.c_uint64, ctypes.POINTER(c_int)]
         dll.drama_b200_expert_rows_workspace_bytes.argtypes = [c_int64, c_int, c_int, c_int]
         dll.drama_b200_expert_rows_workspace_bytes.restype = c_size_t
         dll.drama_b200_fp8_expert_rows.argtypes = [ctypes.POINTER(Fp8Bank), c_void_p, c_int64, c_int64, c_void_p,
@@ -192,6 +194,12 @@ class Library:
         if status:
             message = self.dll.drama_b200_error()
             raise RuntimeError(message.decode("utf-8", errors="replace") if message else "drama_b200 error")
+
+    def host_locked(self, ptr: int, nbytes: int) -> bool:
+        """Whether both ends of a host byte range are page-locked (pinned or registered)."""
+        locked = c_int(0)
+        self.check(self.dll.drama_b200_host_locked(ptr, nbytes, ctypes.byref(locked)))
+        return bool(locked.value)
 
     def device_check(self, device: int) -> int:
         count = c_int(0)

@@ -16,14 +16,22 @@ byte offset and size, the data file's size and SHA-256, and a model
 fingerprint.
 
 What this module adds for the B200 path is ``ExpertCacheFile.register``: it
-page-locks a layer window of the read-only mapping where it lies
-(``drama_b200_host_register`` with ``cudaHostRegisterReadOnly``), after which
-the layer's role views are page-locked tensors and ``StagingArena`` copies each
-requested expert straight from the page cache into its HBM slot (four DMAs per
-expert, one per role, merged where experts are adjacent). The reference reads
-the same mapping through a host gather into a pinned bounce buffer before every
-copy (offload.py:561-594); an unregistered cache still takes that route
-through the arena's bounce path.
+page-locks a layer window of the mapping where it lies (``drama_b200_host_register``
+with ``cudaHostRegisterReadOnly``), after which the layer's role views are
+page-locked tensors and ``StagingArena`` copies each requested expert straight
+from the page cache into its HBM slot (four DMAs per expert, one per role,
+merged where experts are adjacent). The reference reads the same mapping
+through a host gather into a pinned bounce buffer before every copy
+(offload.py:561-594); an unregistered cache still takes that route through the
+arena's bounce path.
+
+The file is mapped private (``MAP_PRIVATE``, copy-on-write; nothing ever
+reaches the file) rather than ``PROT_READ``-only as the reference maps it:
+on B200 hosts with driver 580 ``cudaHostRegister`` refuses ``PROT_READ``
+mappings with or without the read-only flag, and accepts a private mapping
+with it. A read-only registration pins the page-cache pages themselves (no
+copy-on-write copies), so registering costs no extra RAM. The views must still
+only be read.
 """
 
 from __future__ import annotations
@@ -35,7 +43,6 @@ import math
 import mmap
 import re
 import sys
-import warnings
 from pathlib import Path
 from typing import Any
 
@@ -148,7 +155,7 @@ def write_expert_cache(cache_dir: str | Path, layers: list[dict[str, Tensor]], *
 
 
 class ExpertCacheFile:
-    """A validated expert cache: read-only mapping, zero-copy role views, page locking."""
+    """A validated expert cache: private mapping, zero-copy role views, page locking."""
 
     def __init__(self, cache_dir: Path, manifest: dict[str, Any]) -> None:
         self.cache_dir = Path(cache_dir)
@@ -220,10 +227,8 @@ class ExpertCacheFile:
             raise RuntimeError("Expert cache is closed")
         if self._mapping is None:
             with self._data_path.open("rb") as handle:
-                self._mmap = mmap.mmap(handle.fileno(), self.nbytes, access=mmap.ACCESS_READ)
-            with warnings.catch_warnings():
-                warnings.filterwarnings("ignore", message="The given buffer is not writable", category=UserWarning)
-                self._mapping = torch.frombuffer(self._mmap, dtype=torch.uint8, count=self.nbytes)
+                self._mmap = mmap.mmap(handle.fileno(), self.nbytes, access=mmap.ACCESS_COPY)
+            self._mapping = torch.frombuffer(self._mmap, dtype=torch.uint8, count=self.nbytes)
         return self._mapping
 
     def _check_layer(self, layer: int) -> None:

@@ -36,6 +36,7 @@ from torch import Tensor, nn
 from . import _lib
 from .backend import (FLOAT_DTYPES, FP8_DTYPE, MAX_DECODE_PAIRS, _PREFILL_WORKSPACES, _WORKSPACES,
                       B200ExpertBackend, QuantizedB200Backend)
+from .staging import host_locked
 
 EXPERT_BUFFER_NAMES = ("w13_weight", "w13_scale_inv", "w2_weight", "w2_scale_inv")
 FP8_BLOCK = 128
@@ -126,7 +127,7 @@ class _ResidentBank:
         self.nbytes = 0
         with torch.cuda.stream(stream):
             for name, t in tensors.items():
-                src = t if t.is_pinned() else t.pin_memory()
+                src = t if host_locked(t) else t.pin_memory()
                 dev = torch.empty(t.shape, dtype=t.dtype, device=device)
                 dev.copy_(src, non_blocking=True)
                 setattr(self, name, dev)

@@ -43,6 +43,17 @@ FP8_DTYPE = torch.float8_e4m3fn
 BLOCK = 128
 
 
+def host_locked(t: Tensor) -> bool:
+    """A host tensor whose own byte range is page-locked (torch's ``is_pinned``
+    looks only at the start of the whole storage, which misleads for views into
+    a partly registered mapping)."""
+    if t.device.type != "cpu" or t.numel() == 0:
+        return False
+    if not torch.cuda.is_available():
+        return t.is_pinned()
+    return _lib.library().host_locked(t.data_ptr(), t.numel() * t.element_size())
+
+
 def role_layout(hidden: int, intermediate: int) -> list[tuple[str, torch.dtype, tuple[int, ...], int, int]]:
     """(name, dtype, per-expert shape, byte offset, bytes) of each role in a packed slot."""
     roles = [
@@ -127,7 +138,7 @@ class PackedExperts:
         return packed
 
     def is_pinned(self) -> bool:
-        return self.raw.device.type == "cpu" and self.raw.is_pinned()
+        return host_locked(self.raw)
 
     def staged(self, count: int | None = None, start: int = 0) -> StagedExperts:
         stop = self.num_experts if count is None else start + count
@@ -331,7 +342,7 @@ class StagingArena:
             base_src, base_dst, row = packed.raw.data_ptr(), arena.raw.data_ptr(), arena.expert_bytes
             return ([base_src + e * row for e in ids], [base_dst + i * row for i in range(len(ids))],
                     [row] * len(ids))
-        if packed is None and all(getattr(store, n).is_pinned() for n in EXPERT_BUFFER_NAMES):
+        if packed is None and all(host_locked(getattr(store, n)) for n in EXPERT_BUFFER_NAMES):
             src, dst, nbytes = [], [], []
             for name, _, _, offset, size in role_layout(arena.hidden, arena.intermediate):
                 role = getattr(store, name)

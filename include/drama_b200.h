@@ -405,7 +405,7 @@ DRAMA_B200_API int drama_b200_stage_copies(const void* const* host_src, void* co
 
 /* ---------------------------------------------------------------------------
  * Host byte sources for staging: page-lock an existing host range, e.g. a
- * read-only mmap of an expert cache file (experts.bin, manifest format
+ * private mmap of an expert cache file (experts.bin, manifest format
  * "drama3-official-fp8-experts" v1, src/drama_low_vram/expert_cache_file.py:
  * 28-33, 112-153, 526-556), so that drama_b200_stage_copies can DMA expert
  * rows straight out of the mapping. The reference instead gathers those rows
@@ -414,8 +414,11 @@ DRAMA_B200_API int drama_b200_stage_copies(const void* const* host_src, void* co
  *
  * [host_ptr, host_ptr + bytes) is widened to whole pages and registered with
  * cudaHostRegisterPortable, plus cudaHostRegisterReadOnly when read_only is
- * non-zero (required for a PROT_READ mapping; refused when the device cannot
- * do it). The widened range is returned in registered_base/registered_bytes;
+ * non-zero (refused when the device cannot do it). Read-only registration of a
+ * MAP_PRIVATE file mapping pins the page-cache pages themselves, with no
+ * copy-on-write copies; the driver refuses PROT_READ-only file mappings and
+ * shared writable mappings of disk files, with or without the flag.
+ * The widened range is returned in registered_base/registered_bytes;
  * pass registered_base to drama_b200_host_unregister. Ranges that share a page
  * cannot both be registered.
  * ------------------------------------------------------------------------- */
@@ -423,6 +426,12 @@ DRAMA_B200_API int drama_b200_host_register(void* host_ptr, uint64_t bytes, int 
                                             void** registered_base, uint64_t* registered_bytes);
 
 DRAMA_B200_API int drama_b200_host_unregister(void* registered_base);
+
+/* *locked = 1 when the first and the last byte of [host_ptr, host_ptr + bytes)
+ * are page-locked host memory, else 0. Unlike torch's Tensor.is_pinned, which
+ * looks at the start of the whole storage, this looks at the range itself: a
+ * view into a partly registered mapping reads as locked only where it is. */
+DRAMA_B200_API int drama_b200_host_locked(const void* host_ptr, uint64_t bytes, int* locked);
 
 #ifdef __cplusplus
 }

@@ -8,6 +8,8 @@ expert outputs as the resident bank.
 
 from __future__ import annotations
 
+import ctypes
+
 import pytest
 import torch
 
@@ -25,7 +27,7 @@ def _forward(staged, x, ids, w):
 def test_registered_cache_stages_without_bounce(cuda_device, tmp_path):
     from drama_b200 import synthetic
     from drama_b200.expert_cache import ExpertCacheFile, write_expert_cache
-    from drama_b200.staging import StagedExperts, StagingArena
+    from drama_b200.staging import StagedExperts, StagingArena, host_locked
 
     banks = [synthetic.fp8_bank(E, H, I, 300 + layer) for layer in range(3)]
     write_expert_cache(tmp_path / "cache", banks)
@@ -36,8 +38,24 @@ def test_registered_cache_stages_without_bounce(cuda_device, tmp_path):
     assert locked >= off + size - start and cache.registered_layers == [(0, 2)]
     with pytest.raises(ValueError, match="overlap or adjoin"):
         cache.register(2, 1)  # its first page is the last page of layer 1
-    assert all(t.is_pinned() for t in cache.layer_buffers(1).values())
-    assert not cache.layer_buffers(2)["w13_weight"].is_pinned()
+    assert all(host_locked(t) for t in cache.layer_buffers(1).values())
+    # layer 2 starts inside the last registered page: its roles are not page-locked
+    # (torch's is_pinned looks at the storage start and says they are)
+    assert not any(host_locked(t) for t in cache.layer_buffers(2).values())
+    assert cache.layer_buffers(2)["w13_weight"].is_pinned()
+    # a copy that starts in the registered page but runs past it is refused before anything moves
+    from drama_b200 import _lib
+
+    lib = _lib.library()
+    first = cache.layer_buffers(2)["w13_weight"][0]
+    assert lib.host_locked(first.data_ptr(), 1)
+    dev = torch.empty(first.numel(), dtype=torch.uint8, device=cuda_device)
+    src = (ctypes.c_void_p * 1)(first.data_ptr())
+    dst = (ctypes.c_void_p * 1)(dev.data_ptr())
+    n = (ctypes.c_uint64 * 1)(first.numel())
+    stream = torch.cuda.current_stream(cuda_device).cuda_stream
+    assert lib.dll.drama_b200_stage_copies(src, dst, n, 1, stream, None, None) == -1
+    assert b"not page-locked" in lib.dll.drama_b200_error()
 
     arena = StagingArena(6)
     x = synthetic.hidden_states(5, H, 1, device=cuda_device)
