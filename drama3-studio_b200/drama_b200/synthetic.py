@@ -11,6 +11,11 @@ value distributions of the benchmark configurations:
   (``src/drama_low_vram/quantized_model.py:26-68``): ``[E, N, K/8]`` int32 with
   nibble ``k % 8`` at bit ``4*(k % 8)``, group 128 along K, plus (asymmetric)
   ``[E, N/8, K/128]`` int32 zero-points, nibble ``n % 8`` at bit ``4*(n % 8)``.
+* W8A8 modes 1-3 (INT8-ConvRot, W6A8, W4A8 codebook): the ``QuantizedStore``
+  layouts of ``quantized_model.py:45-68, 114-151`` with the value ranges of the
+  reference's own kernel test (``tests/test_quantized_kernels.py:47-69``):
+  uniform int8 / 6-bit / 4-bit codes, FP8 relative scales in [1, 2), fp32
+  channel scales sized so a projection's outputs are O(1).
 * Activations bf16 N(0, 1); router weight bf16 N(0, 0.02); RMSNorm gamma
   1 + N(0, 0.01).
 
@@ -22,6 +27,7 @@ from __future__ import annotations
 
 import math
 
+import numpy as np
 import torch
 
 FP8 = torch.float8_e4m3fn
@@ -185,3 +191,47 @@ def expert_nbytes_int4(hidden: int, intermediate: int) -> int:
     scales = 2 * (n13 * hidden // BLOCK + n2 * intermediate // BLOCK)
     zeros = 4 * (n13 // 8 * hidden // BLOCK + n2 // 8 * math.ceil(intermediate / BLOCK))
     return words + scales + zeros
+
+
+def w8a8_bank(mode: int, experts: int, hidden: int, intermediate: int, seed: int) -> dict[str, torch.Tensor]:
+    """A ``QuantizedStore``-shaped CPU bank for W8A8 mode 1, 2 or 3 (numpy PCG64 stream).
+
+    mode 1: ``[E, N, K]`` int8 weights, ``[E, N, 1]`` fp32 channel scales.
+    mode 2: ``[E, N, 3K/4]`` int8 (K/2 bytes of low nibbles, column 2j in the
+            low nibble of byte j; then K/4 bytes of top-two bits, column 4j+i
+            at bits 2i of byte j); ``[E, N, K/16 + 4]`` uint8 scales (FP8
+            relative scale per 16 columns, then the fp32 channel scale).
+    mode 3: ``[E, N, K/2]`` int8 4-bit codes; ``[E, N, K/16 + 8]`` uint8 (as
+            mode 2, plus one fp32 codebook entry in bytes K/16+4.. of rows 0-15).
+    """
+    if mode not in (1, 2, 3):
+        raise ValueError("W8A8 banks are modes 1, 2 and 3")
+    rng = np.random.default_rng(seed)
+    typical = {1: 64.0, 2: 24.0, 3: 10.0}[mode]  # mean |grid value| of the mode
+    bank = {}
+    for name, n, k in (("w13", 2 * intermediate, hidden), ("w2", hidden, intermediate)):
+        channel = (rng.random((experts, n, 1)) / (typical * math.sqrt(k))).astype(np.float32)
+        if mode == 1:
+            bank[f"{name}_weight"] = torch.from_numpy(rng.integers(-127, 128, (experts, n, k), dtype=np.int8))
+            bank[f"{name}_scale_inv"] = torch.from_numpy(channel)
+            continue
+        codes = rng.integers(0, 64 if mode == 2 else 16, (experts, n, k))
+        low = (codes[..., 0::2] & 15) | ((codes[..., 1::2] & 15) << 4)
+        if mode == 2:
+            high = np.zeros((experts, n, k // 4), dtype=np.int64)
+            for i in range(4):
+                high |= ((codes[..., i::4] >> 4) & 3) << (2 * i)
+            raw = np.concatenate((low, high), axis=-1)
+        else:
+            raw = low
+        relative = torch.from_numpy((rng.random((experts, n, k // 16)) + 1.0).astype(np.float32)).to(FP8)
+        aux = torch.zeros((experts, n, k // 16 + (8 if mode == 3 else 4)), dtype=torch.uint8)
+        aux[..., :k // 16] = relative.view(torch.uint8)
+        aux[..., k // 16:k // 16 + 4] = torch.from_numpy(channel).view(torch.uint8)
+        if mode == 3:
+            table = np.linspace(-12.0, 13.0, 16) + rng.normal(0.0, 0.25, (experts, 16))
+            aux[:, :16, k // 16 + 4:] = torch.from_numpy(table.astype(np.float32)).view(torch.uint8).reshape(
+                experts, 16, 4)
+        bank[f"{name}_weight"] = torch.from_numpy(raw.astype(np.uint8)).view(torch.int8)
+        bank[f"{name}_scale_inv"] = aux
+    return bank

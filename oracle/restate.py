@@ -600,3 +600,150 @@ def stack_layer(hidden, gamma, gate_weight, bank, top_k: int = 8, eps: float = 1
     ids, weights, _ = route_topk(logits, top_k, True, "bfloat16")
     moe = fp8_dequant_forward(normed, ids, weights, bank, "bfloat16")
     return round_bf16(h + moe), normed, ids, weights
+
+
+# --------------------------------------------------------------------------
+# W8A8 modes 1-3 (quantized_kernels.py:15-45, 115-189, 217-248)
+# --------------------------------------------------------------------------
+
+# The regular H4 basis whose 4-fold Kronecker power, divided by 16, rotates
+# each 256-column group of the activations (quantized_kernels.py:30-45). It is
+# symmetric, so x @ M equals M @ x.
+H4 = np.array([[1, 1, 1, -1], [1, 1, -1, 1], [1, -1, 1, 1], [-1, 1, 1, 1]], dtype=np.float64)
+CONVROT_GROUP = 256
+
+
+def round_from_f64(values, dtype: str) -> np.ndarray:
+    """One round-to-nearest-even from float64 to ``dtype`` (returned as float32)."""
+    v = np.asarray(values, dtype=np.float64)
+    if dtype == "float32":
+        return v.astype(F32)
+    digits, min_exp = {"bfloat16": (8, -133), "float16": (11, -24)}[dtype]
+    _, exp = np.frexp(v)
+    ulp = np.ldexp(1.0, np.maximum(exp - digits, min_exp))
+    return (np.round(v / ulp) * ulp).astype(F32)
+
+
+def convrot_rotate(x, dtype: str = "bfloat16") -> np.ndarray:
+    """``x.reshape(-1, 256) @ H`` rounded to ``dtype`` (quantized_kernels.py:40, 65).
+
+    Computed as four radix-4 stages in float64 (stage s transforms base-4 digit
+    s, least significant first; each output adds its four inputs in digit
+    order), then divided by 16 and rounded once. For bf16/f16 inputs the sums
+    are exact whenever a row's magnitudes span fewer than ~2^37, so this is the
+    correctly rounded product; the reference's bf16 matmul accumulates in fp32
+    and differs only where that accumulation rounds across a bf16 boundary.
+    The sm_100a kernel runs the same stages in the same order.
+    """
+    x = np.asarray(x, dtype=np.float64)
+    rows, k = x.shape
+    if k % CONVROT_GROUP:
+        raise ValueError("ConvRot rows need a multiple of 256 columns")
+    y = x.reshape(rows, k // CONVROT_GROUP, 4, 4, 4, 4)  # digits 3, 2, 1, 0
+    for axis in (5, 4, 3, 2):  # digit 0 first
+        moved = np.moveaxis(y, axis, -1)
+        out = np.empty_like(moved)
+        for d in range(4):
+            acc = moved[..., 0] * H4[0, d]
+            for i in range(1, 4):
+                acc = acc + moved[..., i] * H4[i, d]
+            out[..., d] = acc
+        y = np.moveaxis(out, -1, axis)
+    return round_from_f64(y.reshape(rows, k) / 16.0, dtype)
+
+
+def quantize_rows_int8(rotated):
+    """Per-row symmetric INT8 (``_row_quant``, quantized_kernels.py:15-23;
+    ``projection_torch`` 66-67): scale = max(amax, 1e-12) / 127, q = rint(x / scale)
+    clamped to +-127, all in IEEE fp32. Returns (q int8 [R,K], scale fp32 [R])."""
+    r = np.asarray(rotated, dtype=F32)
+    amax = np.abs(r).max(axis=1)
+    scale = (np.maximum(amax, F32(1e-12)) / F32(127.0)).astype(F32)
+    q = np.rint((r / scale[:, None]).astype(F32))
+    return np.clip(q, -127, 127).astype(np.int8), scale
+
+
+def w8a8_grid(weight, scales, mode: int, k: int):
+    """One expert's int8 weight grid [N, K] and per-row channel scale [N]
+    (``_quant_gemm`` MODE 1-3, quantized_kernels.py:139-170; layouts of
+    quantized_model.py:45-68, 114-151).
+
+    mode 1: int8 weights, fp32 scale [N, 1].
+    mode 2: K/2 bytes of low nibbles (column 2j in the low nibble of byte j),
+            then K/4 bytes of top-two bits (column 4j+i at bits 2i of byte j);
+            level = code - 32.
+    mode 3: K/2 bytes of 4-bit codes; level = codebook[code], the 16 fp32
+            codebook entries stored in bytes K/16+4..K/16+8 of rows 0..15.
+    modes 2/3: per-16-column FP8 E4M3 relative scales in scale bytes [0, K/16),
+            the fp32 channel scale in bytes [K/16, K/16+4);
+            grid = clamp(rint(level * relative), +-127) in fp32.
+    """
+    w = np.asarray(weight)
+    s = np.asarray(scales)
+    if mode == 1:
+        return w.astype(np.int8), s.reshape(-1).astype(F32)
+    raw = w.view(np.uint8).astype(np.int64)
+    n = raw.shape[0]
+    low = raw[:, :k // 2]
+    code = np.stack((low & 15, low >> 4), axis=-1).reshape(n, k)
+    aux = s.view(np.uint8)
+    if mode == 2:
+        high = raw[:, k // 2:k // 2 + k // 4]
+        top = (high[..., None] >> (np.arange(4) * 2)) & 3
+        code = code | (top.reshape(n, k) << 4)
+        level = (code - 32).astype(F32)
+    elif mode == 3:
+        table = np.ascontiguousarray(aux[:16, k // 16 + 4:k // 16 + 8]).view(F32).reshape(16)
+        level = table[code]
+    else:
+        raise ValueError(f"unsupported W8A8 mode {mode}")
+    relative = decode_fp8(aux[:, :k // 16]).astype(F32)
+    grid = np.rint((level * np.repeat(relative, 16, axis=1)).astype(F32))
+    channel = np.ascontiguousarray(aux[:, k // 16:k // 16 + 4]).view(F32).reshape(n)
+    return np.clip(grid, -127, 127).astype(np.int8), channel
+
+
+def w8a8_projection(q, q_scale, grid, channel) -> np.ndarray:
+    """``(float(int32 acc) * activation scale) * channel scale`` per output
+    (quantized_kernels.py:172-179), fp32; the caller rounds to bf16."""
+    acc = q.astype(np.int64) @ grid.astype(np.int64).T
+    return ((acc.astype(F32) * np.asarray(q_scale, F32)[:, None]).astype(F32)
+            * np.asarray(channel, F32)[None, :]).astype(F32)
+
+
+def w8a8_pairs(x, ids, weights, bank, mode: int, dtype: str = "bfloat16"):
+    """``QuantizedExpertBackend(mode)._pairs`` (quantized_kernels.py:230-245) on
+    the GPU kernel's semantics: weighted fp32 partials [P, H].
+
+    up = bf16(projection(rotate_quantize(x), W13)); act = bf16(bf16(silu(gate)) * up);
+    down = bf16(projection(rotate_quantize(act), W2)) * weight.
+    """
+    x = np.asarray(x, dtype=F32)
+    ids = np.asarray(ids, dtype=np.int64).reshape(-1)
+    weights = np.asarray(weights, dtype=F32).reshape(-1)
+    hidden = x.shape[1]
+    inter = bank["w13_weight"].shape[1] // 2
+    qx, sx = quantize_rows_int8(convrot_rotate(x, dtype))
+    out = np.zeros((ids.size, hidden), dtype=F32)
+    grids: dict[int, tuple] = {}
+    for row, slot in enumerate(ids.tolist()):
+        if slot not in grids:
+            grids[slot] = (w8a8_grid(bank["w13_weight"][slot], bank["w13_scale_inv"][slot], mode, hidden),
+                           w8a8_grid(bank["w2_weight"][slot], bank["w2_scale_inv"][slot], mode, inter))
+        (g13, c13), (g2, c2) = grids[slot]
+        gu = round_to(w8a8_projection(qx[row:row + 1], sx[row:row + 1], g13, c13)[0], dtype)
+        act = round_to(round_to(silu(gu[:inter]), dtype) * gu[inter:], dtype)
+        qh, sh = quantize_rows_int8(convrot_rotate(act[None, :], dtype))
+        down = round_to(w8a8_projection(qh, sh, g2, c2)[0], dtype)
+        out[row] = (down * weights[row]).astype(F32)
+    return out
+
+
+def w8a8_forward(x, ids, weights, bank, mode: int, dtype: str = "bfloat16"):
+    """``QuantizedExpertBackend(mode).forward`` (quantized_kernels.py:222-229):
+    per-token rows repeated over the route slots, partials summed in slot order."""
+    x = np.asarray(x, dtype=F32)
+    tokens, top_k = np.asarray(ids).shape
+    pairs = w8a8_pairs(np.repeat(x, top_k, axis=0), np.asarray(ids).reshape(-1),
+                       np.asarray(weights).reshape(-1), bank, mode, dtype)
+    return combine_slots(pairs, tokens, top_k, dtype)
