@@ -248,6 +248,57 @@ int drama_b200_int4_decode(const DramaB200Int4Bank* bank, const void* x, int x_d
     return finish_decode(a, workspace, workspace_bytes, stream);
 }
 
+size_t drama_b200_w8a8_workspace_bytes(int64_t tokens, int top_k, int hidden, int intermediate) {
+    return w8a8_workspace_layout(tokens, top_k, hidden, intermediate, nullptr, nullptr);
+}
+
+int drama_b200_w8a8_decode(const DramaB200W8a8Bank* bank, const void* x, int x_dtype, int64_t tokens, int top_k,
+                           const void* ids, int ids_dtype, const void* weights, int weights_dtype, void* out,
+                           float* pair_out, void* workspace, size_t workspace_bytes, void* stream) {
+    if (!bank) return fail("bank is required");
+    const DramaB200W8a8Bank& b = *bank;
+    if (validate_decode_common(x, x_dtype, tokens, top_k, ids, ids_dtype, weights, weights_dtype, out, pair_out,
+                               b.hidden, b.intermediate, b.slots))
+        return -1;
+    if (x_dtype != DRAMA_B200_BF16) return fail("W8A8 hidden rows must be bfloat16");
+    if (b.mode < 1 || b.mode > 3) return fail("W8A8 mode must be 1, 2 or 3; got %d", b.mode);
+    if (b.hidden % 256 || b.intermediate % 256)
+        return fail("W8A8 needs hidden and intermediate sizes that are multiples of 256 (ConvRot groups)");
+    if (!b.w13 || !b.w13_scale || !b.w2 || !b.w2_scale) return fail("W8A8 bank pointers are required");
+    const int H = b.hidden, I = b.intermediate;
+    struct RoleCheck { const char* name; const void* w; const void* sc; int64_t ws, wr, ss, sr; int n, k; };
+    const RoleCheck roles[2] = {
+        {"w13", b.w13, b.w13_scale, b.w13_slot_stride, b.w13_row_stride, b.w13_scale_slot_stride,
+         b.w13_scale_row_stride, 2 * I, H},
+        {"w2", b.w2, b.w2_scale, b.w2_slot_stride, b.w2_row_stride, b.w2_scale_slot_stride, b.w2_scale_row_stride, H,
+         I}};
+    for (const RoleCheck& r : roles) {
+        const int64_t row_bytes = b.mode == 1 ? r.k : b.mode == 2 ? 3 * static_cast<int64_t>(r.k) / 4 : r.k / 2;
+        const int64_t scale_bytes = b.mode == 1 ? 4 : r.k / 16 + (b.mode == 3 ? 8 : 4);
+        const int64_t align = b.mode == 1 ? 16 : 8;  // 16-byte rows (mode 1) / 8-byte nibble loads
+        if (reinterpret_cast<uintptr_t>(r.w) % align || r.wr % align || r.ws % align)
+            return fail("%s weight rows must start on %lld-byte boundaries", r.name, static_cast<long long>(align));
+        if (reinterpret_cast<uintptr_t>(r.sc) % 4 || r.sr % 4 || r.ss % 4)
+            return fail("%s scale rows must start on 4-byte boundaries", r.name);
+        if (r.wr < row_bytes || r.ws < r.wr * r.n || r.sr < scale_bytes || r.ss < r.sr * r.n)
+            return fail("%s strides are smaller than the mode-%d bank geometry", r.name, b.mode);
+        if (b.mode == 3 && r.n < 16) return fail("%s: the W4A8 codebook needs at least 16 rows", r.name);
+    }
+    if (tokens == 0) return 0;
+    int sms = 0;
+    if (sm_count_current(&sms)) return -1;
+    const size_t need = w8a8_workspace_layout(tokens, top_k, H, I, nullptr, nullptr);
+    if (!workspace || workspace_bytes < need)
+        return fail("W8A8 workspace too small: need %zu bytes, got %zu", need, workspace_bytes);
+    if (reinterpret_cast<uintptr_t>(workspace) & 255u) return fail("workspace must be 256-byte aligned");
+    W8a8Workspace ws{};
+    w8a8_workspace_layout(tokens, top_k, H, I, static_cast<char*>(workspace), &ws);
+    const cudaError_t err = w8a8_decode_launch(b, x, tokens, top_k, ids, ids_dtype, weights, weights_dtype, out,
+                                               x_dtype, pair_out, ws, sms, static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return fail("W8A8 launch failed: %s", cudaGetErrorString(err));
+    return 0;
+}
+
 size_t drama_b200_moe_layer_workspace_bytes(int64_t tokens, int top_k, int hidden, int intermediate,
                                              int experts) {
     int sms = 0;

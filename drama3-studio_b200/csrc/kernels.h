@@ -224,6 +224,28 @@ cudaError_t ep_p2p_dispatch_launch(const DramaB200EpPeers& peers, const void* hi
                                    const void* ids, int ids_dtype, int top_k, const int32_t* placement,
                                    int32_t* pair_rows, int32_t* status, int sm_count, cudaStream_t s);
 
+// W8A8 modes 1-3 (w8a8_decode.cu): ConvRot-rotated INT8 activations times
+// INT8 / 6-bit / 4-bit-codebook weights on int8 tensor cores.
+struct W8a8Workspace {
+    int32_t* status;          // [4]: [0] pairs dropped for an out-of-range slot
+    int32_t* num_groups;      // [1]
+    int32_t* order;           // [P] pairs sorted by slot (stable)
+    int4* g_rec;              // [P][2] group records (write_group layout)
+    int8_t* xq;               // [T][H] rotated, quantised token rows
+    float* xs;                // [T]
+    __nv_bfloat16* up;        // [P][2I] gate/up projections (bf16)
+    int8_t* hq;               // [P][I] rotated, quantised SwiGLU rows
+    float* hs;                // [P]
+    float* wts;               // [P] route weights as fp32
+    float* pair_out;          // [P][H] weighted fp32 partials
+};
+size_t w8a8_workspace_layout(int64_t tokens, int top_k, int hidden, int intermediate, char* base,
+                             W8a8Workspace* ws);
+cudaError_t w8a8_decode_launch(const DramaB200W8a8Bank& bank, const void* x, int64_t tokens, int top_k,
+                               const void* ids, int ids_dtype, const void* weights, int weights_dtype, void* out,
+                               int out_dtype, float* pair_out, const W8a8Workspace& ws, int sm_count,
+                               cudaStream_t s);
+
 size_t prefill_workspace_layout(int64_t tokens, int top_k, int hidden, int intermediate, int experts, char* base,
                                 PrefillWorkspace* ws);
 cudaError_t prefill_launch(const DramaB200Fp8Bank& bank, const void* x, int64_t tokens, int top_k, const void* ids,

@@ -37,6 +37,8 @@ EXPORTS = (
     "drama_b200_decode_status_offset",
     "drama_b200_fp8_decode",
     "drama_b200_int4_decode",
+    "drama_b200_w8a8_workspace_bytes",
+    "drama_b200_w8a8_decode",
     "drama_b200_moe_layer_workspace_bytes",
     "drama_b200_fp8_moe_layer",
     "drama_b200_fp8_moe_router",
@@ -94,6 +96,18 @@ class Int4Bank(ctypes.Structure):
     ]
 
 
+class W8a8Bank(ctypes.Structure):
+    _fields_ = [
+        ("mode", ctypes.c_int32),
+        ("w13", c_void_p), ("w13_scale", c_void_p), ("w2", c_void_p), ("w2_scale", c_void_p),
+        ("w13_slot_stride", c_int64), ("w13_row_stride", c_int64),
+        ("w13_scale_slot_stride", c_int64), ("w13_scale_row_stride", c_int64),
+        ("w2_slot_stride", c_int64), ("w2_row_stride", c_int64),
+        ("w2_scale_slot_stride", c_int64), ("w2_scale_row_stride", c_int64),
+        ("slots", ctypes.c_int32), ("hidden", ctypes.c_int32), ("intermediate", ctypes.c_int32),
+    ]
+
+
 class EpPeers(ctypes.Structure):
     _fields_ = [
         ("ranks", ctypes.c_int32), ("rank", ctypes.c_int32), ("capacity", c_int64),
@@ -128,6 +142,10 @@ class Library:
                        c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]
         dll.drama_b200_fp8_decode.argtypes = [ctypes.POINTER(Fp8Bank)] + decode_args
         dll.drama_b200_int4_decode.argtypes = [ctypes.POINTER(Int4Bank)] + decode_args
+        dll.drama_b200_w8a8_decode.argtypes = [ctypes.POINTER(W8a8Bank)] + decode_args
+        dll.drama_b200_w8a8_decode.restype = c_int
+        dll.drama_b200_w8a8_workspace_bytes.argtypes = [c_int64, c_int, c_int, c_int]
+        dll.drama_b200_w8a8_workspace_bytes.restype = c_size_t
         dll.drama_b200_moe_layer_workspace_bytes.argtypes = [c_int64, c_int, c_int, c_int, c_int]
         dll.drama_b200_moe_layer_workspace_bytes.restype = c_size_t
         dll.drama_b200_fp8_moe_layer.argtypes = [

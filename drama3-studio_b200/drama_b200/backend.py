@@ -5,9 +5,10 @@
 with the arithmetic of ``TorchExpertBackend`` (``offload.py:199-244``, the
 PyTorch W16A16 dequant path), plus ``forward_decode_pairs``
 (``offload.py:346-356``) which the manager calls for batch-1 partitions.
-``QuantizedB200Backend(0)`` replaces ``QuantizedExpertBackend(0)``
-(``src/drama_low_vram/quantized_kernels.py:217-248``) for GPTQ W4A16 banks and
-additionally accepts asymmetric uint4 zero-points.
+``QuantizedB200Backend(mode)`` replaces ``QuantizedExpertBackend(mode)``
+(``src/drama_low_vram/quantized_kernels.py:217-248``): GPTQ W4A16 banks (mode
+0, additionally with asymmetric uint4 zero-points) and the W8A8 INT8-ConvRot,
+W6A8 and W4A8-codebook banks (modes 1-3).
 
 Both are drop-ins: ``install_expert_offload(backbone, backend=B200ExpertBackend())``
 (``offload.py:1534-1569``) needs no other change. Every call enqueues work on
@@ -183,6 +184,9 @@ class _DecodeBackend:
     def _bank(self, staged, hidden):  # pragma: no cover - overridden
         raise NotImplementedError
 
+    def _workspace_bytes(self, lib, tokens, top_k, hidden, intermediate) -> int:
+        return lib.dll.drama_b200_decode_workspace_bytes(tokens, top_k, hidden, intermediate)
+
     def _run(self, x: Tensor, ids: Tensor, weights: Tensor, staged, *, combine: bool) -> Tensor:
         hidden = x.shape[-1]
         bank, keep = self._bank(staged, hidden)
@@ -200,7 +204,7 @@ class _DecodeBackend:
             out, pair_out = torch.empty_like(x), None
         else:
             out, pair_out = None, torch.empty((tokens * top_k, hidden), device=x.device, dtype=torch.float32)
-        nbytes = lib.dll.drama_b200_decode_workspace_bytes(tokens, top_k, hidden, bank.intermediate)
+        nbytes = self._workspace_bytes(lib, tokens, top_k, hidden, bank.intermediate)
         ws = _WORKSPACES.get(x.device, nbytes)
         fn = getattr(lib.dll, self.entry)
         lib.check(fn(ctypes.byref(bank), x.data_ptr(), _lib.DTYPE_CODES[x.dtype], tokens, top_k,
@@ -329,17 +333,77 @@ def fp8_expert_rows(x: Tensor, ids: Tensor, staged) -> Tensor:
     return out
 
 
+QUANTIZED_MODES = {0: "W4A16-GPTQ", 1: "INT8-ConvRot", 2: "W6A8", 3: "W4A8"}
+
+
 class QuantizedB200Backend(_DecodeBackend):
-    """GPTQ W4A16 (mode 0) experts, symmetric or with uint4 zero-points."""
+    """``QuantizedExpertBackend(mode)`` (quantized_kernels.py:217-248) on sm_100a.
+
+    mode 0: GPTQ W4A16, symmetric or with uint4 zero-points (f16 MMAs).
+    modes 1-3: INT8-ConvRot, W6A8 and W4A8-codebook banks with ConvRot-rotated
+    int8 activations on int8 tensor cores (``drama_b200_w8a8_decode``); bf16
+    hidden rows, H and I multiples of 256.
+    """
 
     entry = "drama_b200_int4_decode"
 
     def __init__(self, mode: int = 0, *, validate_ids: bool = True) -> None:
-        if mode != 0:
-            raise ValueError("QuantizedB200Backend implements GPTQ W4A16 (mode 0)")
+        if mode not in QUANTIZED_MODES:
+            raise ValueError("Unknown quantized bank format")
         super().__init__(validate_ids=validate_ids)
         self.mode = mode
-        self.quantized_mode = "W4A16-GPTQ"
+        self.quantized_mode = QUANTIZED_MODES[mode]
+        if mode:
+            self.entry = "drama_b200_w8a8_decode"
 
     def _bank(self, staged, hidden):
-        return _int4_bank(staged, hidden)
+        return _int4_bank(staged, hidden) if self.mode == 0 else _w8a8_bank(staged, hidden, self.mode)
+
+    def _workspace_bytes(self, lib, tokens, top_k, hidden, intermediate) -> int:
+        if self.mode == 0:
+            return super()._workspace_bytes(lib, tokens, top_k, hidden, intermediate)
+        return lib.dll.drama_b200_w8a8_workspace_bytes(tokens, top_k, hidden, intermediate)
+
+    def _run(self, x: Tensor, ids: Tensor, weights: Tensor, staged, *, combine: bool) -> Tensor:
+        if self.mode and x.dtype != torch.bfloat16:
+            raise ValueError(f"{self.quantized_mode} experts run on bfloat16 hidden rows")
+        return super()._run(x, ids, weights, staged, combine=combine)
+
+
+def _w8a8_bank(staged, hidden: int, mode: int) -> tuple[_lib.W8a8Bank, tuple]:
+    """Bank descriptor for ``QuantizedStore`` modes 1-3 (quantized_model.py:45-68)."""
+    w13 = _rows(staged.w13_weight)
+    w2 = _rows(staged.w2_weight)
+    s13 = _rows(staged.w13_scale_inv)
+    s2 = _rows(staged.w2_scale_inv)
+    if w13.dtype != torch.int8 or w2.dtype != torch.int8:
+        raise ValueError("Quantized weight dtype mismatch")
+    scale_dtype = torch.float32 if mode == 1 else torch.uint8
+    if s13.dtype != scale_dtype or s2.dtype != scale_dtype:
+        raise ValueError("Quantized scale dtype mismatch")
+    slots, gate_up = w13.shape[0], w13.shape[1]
+    inter = gate_up // 2
+
+    def columns(k):
+        return k if mode == 1 else k * 3 // 4 if mode == 2 else k // 2
+
+    def scale_columns(k):
+        return 1 if mode == 1 else k // 16 + (8 if mode == 3 else 4)
+
+    if tuple(w13.shape) != (slots, gate_up, columns(hidden)) or tuple(w2.shape) != (slots, hidden, columns(inter)):
+        raise ValueError("Quantized weight/scale geometry mismatch")
+    if tuple(s13.shape) != (slots, gate_up, scale_columns(hidden)) or \
+            tuple(s2.shape) != (slots, hidden, scale_columns(inter)):
+        raise ValueError("Quantized weight/scale geometry mismatch")
+    align = 16 if mode == 1 else 8
+    if w13.stride(1) % align or w13.stride(0) % align or w13.data_ptr() % align:
+        w13 = w13.contiguous()
+    if w2.stride(1) % align or w2.stride(0) % align or w2.data_ptr() % align:
+        w2 = w2.contiguous()
+    es = s13.element_size()
+    bank = _lib.W8a8Bank(
+        mode, w13.data_ptr(), s13.data_ptr(), w2.data_ptr(), s2.data_ptr(),
+        w13.stride(0), w13.stride(1), s13.stride(0) * es, s13.stride(1) * es,
+        w2.stride(0), w2.stride(1), s2.stride(0) * es, s2.stride(1) * es,
+        slots, hidden, inter)
+    return bank, (w13, w2, s13, s2)

@@ -97,9 +97,9 @@ def _fp8_store(module: nn.Module) -> dict[str, Tensor]:
 
 
 def _quantized_store(store) -> dict[str, Tensor]:
-    """GPTQ W4A16 bank (``QuantizedStore`` mode 0, quantized_model.py:27-75)."""
-    if getattr(store, "mode", None) != 0:
-        raise ValueError("The resident path runs FP8 banks and quantized mode 0 (GPTQ W4A16)")
+    """A ``QuantizedStore`` bank (modes 0-3, quantized_model.py:27-75)."""
+    if getattr(store, "mode", None) not in (0, 1, 2, 3):
+        raise ValueError("Unknown quantized bank format")
     if hasattr(store, "validate"):
         store.validate()
     out = {name: getattr(store, name) for name in EXPERT_BUFFER_NAMES}
@@ -115,7 +115,7 @@ def _quantized_store(store) -> dict[str, Tensor]:
 def _module_store(module: nn.Module) -> tuple[str, dict[str, Tensor]]:
     quantized = getattr(module, "_drama_quant_store", None)
     if quantized is not None:
-        return "int4", _quantized_store(quantized)
+        return f"q{quantized.mode}", _quantized_store(quantized)
     return "fp8", _fp8_store(module)
 
 
@@ -144,7 +144,7 @@ class ResidentExpertManager:
     """``ExpertOffloadManager`` for banks that stay in HBM; capturable forward.
 
     ``backend`` defaults to ``B200ExpertBackend`` for FP8 modules and
-    ``QuantizedB200Backend(0)`` for GPTQ modules. Banks are copied to
+    ``QuantizedB200Backend(mode)`` for quantized modules (modes 0-3). Banks are copied to
     ``device`` once, at attach time, on a side stream that the caller's current
     stream then waits on.
     """
@@ -159,7 +159,7 @@ class ResidentExpertManager:
         self.validate_ids = validate_ids
         self._backend = backend
         self._fp8 = B200ExpertBackend(validate_ids=False)
-        self._int4 = QuantizedB200Backend(0, validate_ids=False)
+        self._quantized = {mode: QuantizedB200Backend(mode, validate_ids=False) for mode in range(4)}
         self.modules: dict[str, nn.Module] = {}
         self._banks: dict[int, _ResidentBank] = {}
         self._names: dict[int, str] = {}
@@ -215,7 +215,7 @@ class ResidentExpertManager:
     def _backend_for(self, bank: _ResidentBank):
         if self._backend is not None:
             return self._backend
-        return self._int4 if bank.kind == "int4" else self._fp8
+        return self._fp8 if bank.kind == "fp8" else self._quantized[int(bank.kind[1:])]
 
     # -- forward -----------------------------------------------------------
     @torch.no_grad()
@@ -265,7 +265,7 @@ class ResidentExpertManager:
         rows = max(1, min(tokens, MAX_DECODE_PAIRS // max(1, top_k)))
         with ctx:
             for bank in self._banks.values():
-                nbytes = lib.dll.drama_b200_decode_workspace_bytes(rows, top_k, bank.hidden, bank.intermediate)
+                nbytes = self._backend_for(bank)._workspace_bytes(lib, rows, top_k, bank.hidden, bank.intermediate)
                 _WORKSPACES.get(self.device, nbytes)
                 if bank.kind == "fp8":
                     nbytes = lib.dll.drama_b200_prefill_workspace_bytes(tokens, top_k, bank.hidden,

@@ -152,6 +152,55 @@ DRAMA_B200_API int drama_b200_int4_decode(const DramaB200Int4Bank* bank, const v
                                           void* stream);
 
 /* ---------------------------------------------------------------------------
+ * W8A8 expert banks, modes 1-3 of QuantizedExpertBackend(mode)
+ * (src/drama_low_vram/quantized_kernels.py:115-189 _quant_gemm, 217-248 the
+ * backend; layouts of quantized_model.py:45-68, 114-151):
+ *   mode 1 INT8-ConvRot: w [slots, N, K] int8, scale [slots, N, 1] fp32.
+ *   mode 2 W6A8: w [slots, N, 3K/4]: K/2 bytes of low nibbles (column 2j in
+ *          the low nibble of byte j) then K/4 bytes of top-two bits (column
+ *          4j+i at bits 2i of byte j), level = code - 32; scale [slots, N,
+ *          K/16 + 4] uint8: an FP8 E4M3 relative scale per 16 columns, then the
+ *          fp32 channel scale.
+ *   mode 3 W4A8: w [slots, N, K/2] 4-bit codes, level = codebook[code];
+ *          scale [slots, N, K/16 + 8]: as mode 2 plus one fp32 codebook entry
+ *          in bytes K/16+4..K/16+8 of rows 0..15.
+ * Weight grid (modes 2/3) = clamp(rint(level * relative), +-127) in fp32.
+ * Strides are in BYTES. W13 rows: N = 2I, K = H; W2 rows: N = H, K = I.
+ * ------------------------------------------------------------------------- */
+typedef struct DramaB200W8a8Bank {
+    int32_t mode;              /* 1, 2 or 3 */
+    const void* w13;
+    const void* w13_scale;
+    const void* w2;
+    const void* w2_scale;
+    int64_t w13_slot_stride, w13_row_stride;
+    int64_t w13_scale_slot_stride, w13_scale_row_stride;
+    int64_t w2_slot_stride, w2_row_stride;
+    int64_t w2_scale_slot_stride, w2_scale_row_stride;
+    int32_t slots, hidden, intermediate;
+} DramaB200W8a8Bank;
+
+/* The W8A8 expert FFN, QuantizedExpertBackend(mode).forward / forward_pairs:
+ *   r = bf16(x_row @ kron(H4,H4,H4,H4)/16 per 256 columns)   (ConvRot)
+ *   q = clamp(rint(r / s), +-127), s = max(amax(r), 1e-12) / 127  (per row)
+ *   proj = bf16((float(int32 sum q * grid) * s) * channel)
+ *   gate, up = proj(x, W13); h = bf16(bf16(silu(gate)) * up)
+ *   partial[p] = float(proj(h, W2)) * weight[p]   (fp32)
+ *   out[t] = sum over route slots, in slot order, of partial[t*top_k + s]
+ * x: [tokens, H] bfloat16 (the reference's compute dtype on sm_80+); out the
+ * same; ids/weights [tokens, top_k]; pair_out as in drama_b200_fp8_decode.
+ * The rotation is computed as four radix-4 stages in float64 and rounded once;
+ * the integer sums are exact. H and I must be multiples of 256;
+ * pairs <= 4096, slots <= 1024. Ids outside [0, slots) contribute zero and are
+ * counted in the workspace status word. */
+DRAMA_B200_API size_t drama_b200_w8a8_workspace_bytes(int64_t tokens, int top_k, int hidden, int intermediate);
+
+DRAMA_B200_API int drama_b200_w8a8_decode(const DramaB200W8a8Bank* bank, const void* x, int x_dtype,
+                                          int64_t tokens, int top_k, const void* ids, int ids_dtype,
+                                          const void* weights, int weights_dtype, void* out, float* pair_out,
+                                          void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
  * One decode MoE layer, fully on the device (graph-capturable):
  *   normed = bf16(x * 1/sqrt(mean(x^2) + eps) * gamma)      (fixed fp32 order)
  *   logits = bf16(normed @ gate^T)                           (fixed fp32 order)

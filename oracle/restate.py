@@ -28,6 +28,11 @@ Drama3-Studio source tree):
                           - ``src/drama_low_vram/quantized_kernels.py:48-112, 217-248``
                             (mode 0 GPTQ W4A16), extended with explicit uint4
                             zero-points (``zp = 8`` reproduces the reference).
+* ``convrot_rotate`` / ``quantize_rows_int8`` / ``convrot_grid`` /
+  ``convrot_pairs`` / ``convrot_forward``
+                          - ``src/drama_low_vram/quantized_kernels.py:15-45, 115-189,
+                            217-248`` (W8A8 modes 1-3: INT8-ConvRot, W6A8, W4A8
+                            codebook; layouts of ``quantized_model.py:45-68, 114-151``).
 * ``rms_norm`` / ``stack_layer`` - the decode layer of
                             ``src/drama_low_vram/backbone_graph.py:306-337`` without
                             the mixer and the shared expert.
@@ -663,7 +668,7 @@ def quantize_rows_int8(rotated):
     return np.clip(q, -127, 127).astype(np.int8), scale
 
 
-def w8a8_grid(weight, scales, mode: int, k: int):
+def convrot_grid(weight, scales, mode: int, k: int):
     """One expert's int8 weight grid [N, K] and per-row channel scale [N]
     (``_quant_gemm`` MODE 1-3, quantized_kernels.py:139-170; layouts of
     quantized_model.py:45-68, 114-151).
@@ -703,7 +708,7 @@ def w8a8_grid(weight, scales, mode: int, k: int):
     return np.clip(grid, -127, 127).astype(np.int8), channel
 
 
-def w8a8_projection(q, q_scale, grid, channel) -> np.ndarray:
+def convrot_projection(q, q_scale, grid, channel) -> np.ndarray:
     """``(float(int32 acc) * activation scale) * channel scale`` per output
     (quantized_kernels.py:172-179), fp32; the caller rounds to bf16."""
     acc = q.astype(np.int64) @ grid.astype(np.int64).T
@@ -711,7 +716,7 @@ def w8a8_projection(q, q_scale, grid, channel) -> np.ndarray:
             * np.asarray(channel, F32)[None, :]).astype(F32)
 
 
-def w8a8_pairs(x, ids, weights, bank, mode: int, dtype: str = "bfloat16"):
+def convrot_pairs(x, ids, weights, bank, mode: int, dtype: str = "bfloat16"):
     """``QuantizedExpertBackend(mode)._pairs`` (quantized_kernels.py:230-245) on
     the GPU kernel's semantics: weighted fp32 partials [P, H].
 
@@ -728,22 +733,22 @@ def w8a8_pairs(x, ids, weights, bank, mode: int, dtype: str = "bfloat16"):
     grids: dict[int, tuple] = {}
     for row, slot in enumerate(ids.tolist()):
         if slot not in grids:
-            grids[slot] = (w8a8_grid(bank["w13_weight"][slot], bank["w13_scale_inv"][slot], mode, hidden),
-                           w8a8_grid(bank["w2_weight"][slot], bank["w2_scale_inv"][slot], mode, inter))
+            grids[slot] = (convrot_grid(bank["w13_weight"][slot], bank["w13_scale_inv"][slot], mode, hidden),
+                           convrot_grid(bank["w2_weight"][slot], bank["w2_scale_inv"][slot], mode, inter))
         (g13, c13), (g2, c2) = grids[slot]
-        gu = round_to(w8a8_projection(qx[row:row + 1], sx[row:row + 1], g13, c13)[0], dtype)
+        gu = round_to(convrot_projection(qx[row:row + 1], sx[row:row + 1], g13, c13)[0], dtype)
         act = round_to(round_to(silu(gu[:inter]), dtype) * gu[inter:], dtype)
         qh, sh = quantize_rows_int8(convrot_rotate(act[None, :], dtype))
-        down = round_to(w8a8_projection(qh, sh, g2, c2)[0], dtype)
+        down = round_to(convrot_projection(qh, sh, g2, c2)[0], dtype)
         out[row] = (down * weights[row]).astype(F32)
     return out
 
 
-def w8a8_forward(x, ids, weights, bank, mode: int, dtype: str = "bfloat16"):
+def convrot_forward(x, ids, weights, bank, mode: int, dtype: str = "bfloat16"):
     """``QuantizedExpertBackend(mode).forward`` (quantized_kernels.py:222-229):
     per-token rows repeated over the route slots, partials summed in slot order."""
     x = np.asarray(x, dtype=F32)
     tokens, top_k = np.asarray(ids).shape
-    pairs = w8a8_pairs(np.repeat(x, top_k, axis=0), np.asarray(ids).reshape(-1),
+    pairs = convrot_pairs(np.repeat(x, top_k, axis=0), np.asarray(ids).reshape(-1),
                        np.asarray(weights).reshape(-1), bank, mode, dtype)
     return combine_slots(pairs, tokens, top_k, dtype)

@@ -30,7 +30,7 @@ def _case(mode):
 def test_weight_grids_match_the_reference_reconstruction(mode):
     bank, *_ = _case(mode)
     for name, k in (("13", HIDDEN), ("2", INTER)):
-        grids = np.stack([R.w8a8_grid(bank[f"w{name}_weight"][e], bank[f"w{name}_scale_inv"][e], mode, k)[0]
+        grids = np.stack([R.convrot_grid(bank[f"w{name}_weight"][e], bank[f"w{name}_scale_inv"][e], mode, k)[0]
                           for e in range(bank[f"w{name}_weight"].shape[0])])
         assert hashlib.sha256(grids.tobytes()).hexdigest() == bytes(GOLDEN[f"grid{name}_{mode}"]).decode()
 
@@ -45,10 +45,10 @@ def test_rotated_int8_activations_match_the_reference(mode):
 @pytest.mark.parametrize("mode", [1, 2, 3])
 def test_forward_and_pairs_match_the_reference(mode):
     bank, x, ids, w = _case(mode)
-    out = R.w8a8_forward(x, ids, w, bank, mode)
+    out = R.convrot_forward(x, ids, w, bank, mode)
     assert_parity(out, GOLDEN[f"forward{mode}"], label=f"W8A8 mode {mode} forward")
     assert (out == GOLDEN[f"forward{mode}"]).mean() >= 0.95
-    pairs = R.w8a8_pairs(np.repeat(x, ids.shape[1], 0), ids.reshape(-1), w.reshape(-1), bank, mode)
+    pairs = R.convrot_pairs(np.repeat(x, ids.shape[1], 0), ids.reshape(-1), w.reshape(-1), bank, mode)
     assert_parity(pairs, GOLDEN[f"pairs{mode}"], label=f"W8A8 mode {mode} pairs")
 
 

@@ -64,14 +64,14 @@ def test_dense_bank_rejected():
         install_resident_experts(Backbone([Experts(_bank(), fp8=False)]))
 
 
-def test_quantized_modes_other_than_gptq_rejected():
+def test_unknown_quantized_mode_rejected():
     module = Experts(_bank())
 
     class Store:
-        mode = 2
+        mode = 7
 
     module._drama_quant_store = Store()
-    with pytest.raises(ValueError, match="quantized mode 0"):
+    with pytest.raises(ValueError, match="Unknown quantized bank format"):
         install_resident_experts(Backbone([module]))
 
 
