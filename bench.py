@@ -44,11 +44,14 @@ def parse_args():
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--layers", type=int, default=48)
     p.add_argument("--decode-steps", type=int, default=512, help="decode tokens per CUDA graph")
-    p.add_argument("--workload", choices=("decode", "prefill", "ep", "offload", "int4"), default="decode",
+    p.add_argument("--workload", choices=("decode", "prefill", "ep", "offload", "int4", "w8a8"), default="decode",
                    help="decode: config 1 (the headline); prefill: config 3 (4096 tokens, one layer, Zipf); "
                         "ep: config 4 expert-parallel decode of 256 tokens over the torchrun ranks; "
                         "offload: config 4's 1-GPU offload variant (32 of 128 experts resident per layer); "
-                        "int4: config 2 (one W4A16 asymmetric layer, decode batches 1/4/16, uniform routes)")
+                        "int4: config 2 (one W4A16 asymmetric layer, decode batches 1/4/16, uniform routes); "
+                        "w8a8: config 2's measurement on a W8A8 bank of --mode 1, 2 or 3")
+    p.add_argument("--mode", type=int, choices=(1, 2, 3), default=1,
+                   help="w8a8: 1 INT8-ConvRot, 2 W6A8, 3 W4A8 codebook")
     p.add_argument("--exchange", choices=("p2p", "nccl"), default="p2p",
                    help="ep: NVLink peer-memory exchange (default) or NCCL all-to-alls")
     p.add_argument("--host-layers", type=int, default=48,
@@ -859,24 +862,55 @@ def run_offload(args) -> None:
 INT4_CALLS = 64      # calls per CUDA graph, each with its own uniform routes
 
 
-def run_int4(args) -> None:
-    """Config 2: QuantizedB200Backend(0) on an asymmetric W4A16 bank, batches 1/4/16.
+W8A8_NAMES = {1: "INT8-ConvRot", 2: "W6A8", 3: "W4A8 codebook"}
 
-    One step = one replay of a CUDA graph holding 64 expert calls, each with
-    its own seeded uniform routes (so consecutive calls read different
-    experts of the 314 MB bank, which is larger than L2). ``value`` is the
-    batch-1 tokens/s; every batch is reported under ``by_batch`` with its
-    algorithmic bytes (the distinct experts of each call) and GB/s.
+
+def w8a8_expert_nbytes(mode: int, hidden: int, inter: int) -> int:
+    """Bytes of one W8A8 expert: weights plus scale rows (quantized_model.py:45-68)."""
+    total = 0
+    for n, k in ((2 * inter, hidden), (hidden, inter)):
+        cols = k if mode == 1 else k * 3 // 4 if mode == 2 else k // 2
+        scale = 4 if mode == 1 else k // 16 + (8 if mode == 3 else 4)
+        total += n * (cols + scale)
+    return total
+
+
+def _w8a8_device_bank(mode: int, device, seed: int):
+    """The 128-expert W8A8 bank on the device, generated 16 experts at a time."""
+    import torch
+
+    from drama_b200 import synthetic
+
+    parts = [synthetic.w8a8_bank(mode, 16, HIDDEN, INTER, seed + c) for c in range(0, EXPERTS, 16)]
+    return {k: torch.cat([p[k] for p in parts]).to(device) for k in parts[0]}
+
+
+def run_int4(args, mode: int = 0) -> None:
+    """Config 2: QuantizedB200Backend(mode) on a quantized bank, batches 1/4/16.
+
+    mode 0 is config 2 itself (asymmetric W4A16); modes 1-3 run the same
+    measurement on a W8A8 bank (INT8-ConvRot, W6A8, W4A8 codebook). One step =
+    one replay of a CUDA graph holding 64 expert calls, each with its own
+    seeded uniform routes (so consecutive calls read different experts of a
+    bank larger than L2). ``value`` is the batch-1 tokens/s; every batch is
+    reported under ``by_batch`` with its algorithmic bytes (the distinct
+    experts of each call) and GB/s.
     """
     import torch
 
     from drama_b200 import QuantizedB200Backend, QuantizedBank, synthetic
 
     world, rank, device, gpu_id = _dist_setup()
-    bank = synthetic.int4_bank(EXPERTS, HIDDEN, INTER, 2024 + rank, device=device, asymmetric=True)
-    qb = QuantizedBank(**bank)
-    backend = QuantizedB200Backend(0, validate_ids=False)
-    nbytes = synthetic.expert_nbytes_int4(HIDDEN, INTER)
+    if mode == 0:
+        bank = synthetic.int4_bank(EXPERTS, HIDDEN, INTER, 2024 + rank, device=device, asymmetric=True)
+        qb = QuantizedBank(**bank)
+        nbytes = synthetic.expert_nbytes_int4(HIDDEN, INTER)
+    else:
+        from types import SimpleNamespace
+
+        qb = SimpleNamespace(**_w8a8_device_bank(mode, device, 3000 + 1000 * mode + rank))
+        nbytes = w8a8_expert_nbytes(mode, HIDDEN, INTER)
+    backend = QuantizedB200Backend(mode, validate_ids=False)
     peaks = measured_peaks()
     results = {}
     clocks_summary = None
@@ -932,19 +966,32 @@ def run_int4(args) -> None:
             e2e_ms = _max_over_ranks([f0.elapsed_time(f1) / args.steps], world, device)[0]
         del graph
     b1 = results[1]
+    if mode == 0:
+        dtype = "int4 weights (asymmetric, group 128, bf16 scales, uint4 zero-points), f16 MMA, fp32 accumulate"
+        layer = "W4A16"
+        kernel = "one W4A16 expert call (prep + up + down kernels), batch 1"
+        launches = 3
+    else:
+        dtype = (f"{W8A8_NAMES[mode]} weights, ConvRot-rotated int8 activations, s8 MMA, int32 accumulate, "
+                 "bf16 projections")
+        layer = f"W8A8 mode {mode} ({W8A8_NAMES[mode]})"
+        kernel = (f"one {W8A8_NAMES[mode]} expert call (prep, rotate, up GEMV, rotate, down GEMV, combine), "
+                  "batch 1")
+        launches = 6
     line = {
         "metric": METRIC, "value": b1["tokens_per_s"], "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": max(3, args.warmup), "ms_per_step": INT4_CALLS * b1["call_us"] / 1000.0, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None,
-        "dtype": "int4 weights (asymmetric, group 128, bf16 scales, uint4 zero-points), f16 MMA, fp32 accumulate",
+        "dtype": dtype,
         "data": "synthetic (seeded random-init weights and hidden rows, uniform routes)",
-        "config": {"workload": (f"config2: one W4A16 MoE layer (hidden {HIDDEN}, {EXPERTS} experts, top-{TOP_K}, "
+        "config": {"workload": ((f"config2: one {layer} MoE layer" if mode == 0 else f"one {layer} MoE layer")
+                                + f" (hidden {HIDDEN}, {EXPERTS} experts, top-{TOP_K}, "
                                 f"intermediate {INTER}), decode batches 1/4/16 (value: batch 1), "
                                 f"{INT4_CALLS} calls per CUDA graph with distinct uniform routes"),
                    "batches": [1, 4, 16], "calls_per_graph": INT4_CALLS,
                    "parallelism": f"replicas{world}" if world > 1 else "single",
-                   "l2": "bank of 314 MB (> L2), routes differ call to call"},
-        "roofline": {"kernel": "one W4A16 expert call (prep + up + down kernels), batch 1", "bound": "hbm",
+                   "l2": f"bank of {EXPERTS * nbytes / 1e6:.0f} MB (> L2), routes differ call to call"},
+        "roofline": {"kernel": kernel, "bound": "hbm",
                      "achieved": b1["achieved_gbs"], "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": b1["achieved_gbs"] / peaks["hbm_gbs"],
                      "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs)", "traffic": None,
@@ -952,7 +999,7 @@ def run_int4(args) -> None:
         "by_batch": results,
         "e2e": {"value": INT4_CALLS * world / (e2e_ms / 1000.0), "unit": "tokens/s",
                 "h2d_bytes_per_step": INT4_CALLS * HIDDEN * 2, "d2h_bytes_per_step": INT4_CALLS * HIDDEN * 2},
-        "gpu_launches": args.steps * INT4_CALLS * 3,
+        "gpu_launches": args.steps * INT4_CALLS * launches,
         "clocks": clocks_summary,
     }
     if world > 1:
@@ -975,6 +1022,8 @@ def main() -> None:
         run_offload(args)
     elif args.workload == "int4":
         run_int4(args)
+    elif args.workload == "w8a8":
+        run_int4(args, mode=args.mode)
     else:
         run_ours(args)
 

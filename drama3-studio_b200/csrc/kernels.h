@@ -238,6 +238,10 @@ struct W8a8Workspace {
     float* hs;                // [P]
     float* wts;               // [P] route weights as fp32
     float* pair_out;          // [P][H] weighted fp32 partials
+    int32_t* up_cnt;          // [cells] split-K arrivals per gate/up cell (zeroed by prep)
+    int32_t* dn_cnt;          // [cells] split-K arrivals per down cell (zeroed by prep)
+    int32_t* cmb_cnt;         // [H/16] finished down cells per row tile (zeroed by prep)
+    int4* part;               // [tasks][32] int32 partial sums of split-K warps
 };
 size_t w8a8_workspace_layout(int64_t tokens, int top_k, int hidden, int intermediate, char* base,
                              W8a8Workspace* ws);

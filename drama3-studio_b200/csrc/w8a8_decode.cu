@@ -15,16 +15,23 @@
 // which equals the correctly rounded product for all practical inputs.
 //
 // Launches (one stream, in order):
-//   prep   : stable bucket of route slots into expert groups of <= 8 pairs;
-//   rotate : token rows -> int8 + scale (one CTA per row);
-//   gemv   : gate/up projections; every warp owns cells (group, 16-row tile)
-//            and streams the tile's weights for the whole K with 16-byte
-//            loads, dequantising in registers into mma.m16n8k32 s8 fragments
-//            whose N dimension holds the group's tokens (weights read once
-//            per group);
+//   prep   : CTA 0 groups the route slots into expert groups of <= 8 pairs
+//            (one warp with match_any for <= 32 pairs, else a stable bucket;
+//            a column's result does not depend on its group, so any grouping
+//            gives the same bits); CTAs 1..T rotate and quantise one token row
+//            each;
+//   gemv   : gate/up projections. A task is (group, 16-row tile, K part):
+//            the warp streams that part of the tile's weights with 16-byte
+//            loads, dequantises them in registers into mma.m16n8k32 s8
+//            fragments whose N dimension holds the group's tokens (weights
+//            read once per group), and, when K is split, leaves its int32
+//            partial sums for the last-arriving warp of the tile, which adds
+//            them (exactly, in any order) and applies the epilogue. K is split
+//            only when there are too few tiles to occupy the GPU (batch 1);
 //   rotate : SwiGLU rows (bf16(bf16(silu(gate)) * up)) -> int8 + scale;
-//   gemv   : down projections, rounded to bf16 and weighted in fp32;
-//   combine: route slots summed in slot order in fp32.
+//   gemv   : down projections, rounded to bf16 and weighted in fp32; the
+//            warp that finishes the last cell of a 16-row tile of H sums the
+//            route slots of those rows in slot order in fp32 (the combine).
 //
 // K permutation: within each 64-column span, thread t of a quad takes the 16
 // consecutive columns 16t..16t+15 of both its weight rows and its token row,
@@ -37,10 +44,12 @@
 namespace drama {
 namespace {
 
-constexpr int kW8GemvThreads = 256;
-constexpr int kW8Unroll = 4;  // 64-column spans per register batch (K is a multiple of 256)
-constexpr int kRotThreads = 256;
+constexpr int kW8GemvThreads = 128;
+constexpr int kW8Unroll = 4;  // split-K granule: 64-column spans per register batch (K % 256 == 0)
 constexpr int kW8Group = 8;
+constexpr int kW8TargetWarps = 4736;  // 148 SMs x 32 warps: the split-K target
+
+__device__ __forceinline__ void w8_fence() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
 
 __device__ __forceinline__ void mma_s8_16832(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
     asm volatile(
@@ -72,36 +81,206 @@ __device__ __forceinline__ float fp8_to_float(uint32_t byte) {
     return __half2float(__ushort_as_half(static_cast<unsigned short>(h2 & 0xffffu)));
 }
 
-// clamp(rint(level * rel), +-127) as a two's-complement byte (fp32, like the reference).
+// Packed-half helpers (round-to-nearest, never contracted into an FMA).
+__device__ __forceinline__ uint32_t h2_sub(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+__device__ __forceinline__ uint32_t h2_mul(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+__device__ __forceinline__ uint32_t h2_add(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("add.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+__device__ __forceinline__ uint32_t h2_clamp127(uint32_t a) {
+    uint32_t d;
+    asm("max.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(0xD7F0D7F0u));  // -127
+    asm("min.f16x2 %0, %1, %2;" : "=r"(d) : "r"(d), "r"(0x57F057F0u));  // +127
+    return d;
+}
+
+// clamp(rint(level * rel), +-127) (fp32 product, like the reference) in the
+// low byte: the lower clamp first (-127 is an integer, so the order does not
+// matter), then one round-to-nearest-even conversion that saturates at 127.
 __device__ __forceinline__ uint32_t grid_byte(float level, float rel) {
-    float v = rintf(__fmul_rn(level, rel));
-    v = fminf(fmaxf(v, -127.0f), 127.0f);
-    return static_cast<uint32_t>(static_cast<int>(v)) & 0xffu;
+    const float v = fmaxf(__fmul_rn(level, rel), -127.0f);
+    uint32_t q;
+    asm("cvt.rni.sat.s8.f32 %0, %1;" : "=r"(q) : "f"(v));
+    return q;
 }
 
 // ---------------------------------------------------------------------------
-// prep: groups of <= 8 pairs per slot (same records as the FP8/INT4 decode)
+// ConvRot rotation + per-row int8 quantisation of one row, by a whole CTA
+// (blockDim a multiple of 256; chunks of 256 columns in passes)
+// ---------------------------------------------------------------------------
+__constant__ double kH4[4][4] = {{1, 1, 1, -1}, {1, 1, -1, 1}, {1, -1, 1, 1}, {-1, 1, 1, 1}};
+
+// ACT = false: row = bf16 [K]; ACT = true: row = bf16 gate/up [2K] and the
+// rotated row is bf16(bf16(silu(gate)) * up). s_v: blockDim doubles; s_row: K floats.
+template <bool ACT>
+__device__ void rotate_row(const __nv_bfloat16* row, int K, int8_t* q, float* qs, double* s_v, float* s_row) {
+    __shared__ float s_red[32];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nthr = blockDim.x;
+    const int j = tid & 255;
+    double* v = s_v + (tid - j);  // this thread's 256-value chunk buffer
+    float amax = 0.0f;
+    for (int c0 = 0; c0 < K; c0 += nthr) {
+        const int col = c0 + tid;
+        const bool live = col < K;  // K and nthr are multiples of 256: whole chunks are live or idle
+        if (live) {
+            float x;
+            if (ACT) {
+                const float g = __bfloat162float(row[col]);
+                const float u = __bfloat162float(row[K + col]);
+                const float act = __bfloat162float(__float2bfloat16_rn(g / (1.0f + expf(-g))));
+                x = __bfloat162float(__float2bfloat16_rn(act * u));
+            } else {
+                x = __bfloat162float(row[col]);
+            }
+            v[j] = static_cast<double>(x);
+        }
+        __syncthreads();
+#pragma unroll
+        for (int st = 0; st < 4; ++st) {  // base-4 digit st, least significant first
+            const int stride = 1 << (2 * st);
+            const int d = (j >> (2 * st)) & 3;
+            const int base = j - d * stride;
+            double acc = 0.0;
+            if (live) {
+                acc = kH4[0][d] * v[base];
+                acc = acc + kH4[1][d] * v[base + stride];
+                acc = acc + kH4[2][d] * v[base + 2 * stride];
+                acc = acc + kH4[3][d] * v[base + 3 * stride];
+            }
+            __syncthreads();
+            if (live) v[j] = acc;
+            __syncthreads();
+        }
+        if (live) {
+            const float rv = __bfloat162float(__double2bfloat16(v[j] * 0.0625));
+            s_row[col] = rv;
+            amax = fmaxf(amax, fabsf(rv));
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if (lane == 0) s_red[warp] = amax;
+    __syncthreads();
+    float m = s_red[0];
+    for (int w = 1; w < nthr / 32; ++w) m = fmaxf(m, s_red[w]);
+    const float scale = __fdiv_rn(fmaxf(m, 1e-12f), 127.0f);
+    for (int col = tid; col < K; col += nthr) {
+        float r = rintf(__fdiv_rn(s_row[col], scale));
+        r = fminf(fmaxf(r, -127.0f), 127.0f);
+        q[col] = static_cast<int8_t>(r);
+    }
+    if (tid == 0) *qs = scale;
+}
+
+// ---------------------------------------------------------------------------
+// prep (CTA 0): groups of <= 8 pairs per slot (the FP8/INT4 decode's records)
+// and the split-K counters; CTAs 1..T: token rows -> int8
 // ---------------------------------------------------------------------------
 struct W8PrepArgs {
     const void* ids;
     int ids_dtype;
     const void* weights;
     int weights_dtype;
+    const __nv_bfloat16* x;
     int64_t pairs;
-    int slots, hidden;
+    int slots, hidden, intermediate;
     float* pair_out;  // zeroed rows for dropped pairs
     W8a8Workspace ws;
 };
 
+// The rest of CTA 0's work once the groups exist: counts, counters, weights,
+// zero partials for pairs whose slot is out of range.
+__device__ void w8a8_prep_tail(const W8PrepArgs& a, int groups, int dropped) {
+    const int tid = threadIdx.x;
+    if (tid == 0) {
+        a.ws.num_groups[0] = groups;
+        a.ws.status[0] = dropped;
+    }
+    const int up_cells = groups * (2 * a.intermediate / 16), dn_cells = groups * (a.hidden / 16);
+    for (int i = tid; i < up_cells; i += blockDim.x) a.ws.up_cnt[i] = 0;
+    for (int i = tid; i < dn_cells; i += blockDim.x) a.ws.dn_cnt[i] = 0;
+    for (int i = tid; i < a.hidden / 16; i += blockDim.x) a.ws.cmb_cnt[i] = 0;
+    for (int64_t p = tid; p < a.pairs; p += blockDim.x) a.ws.wts[p] = load_any(a.weights, a.weights_dtype, p);
+    if (dropped) {
+        for (int64_t p = 0; p < a.pairs; ++p) {
+            const int64_t id = load_index(a.ids, a.ids_dtype, p);
+            if (id < 0 || id >= a.slots)
+                for (int n = tid; n < a.hidden; n += blockDim.x) a.pair_out[p * a.hidden + n] = 0.0f;
+        }
+    }
+}
+
 __global__ void __launch_bounds__(1024) w8a8_prep_kernel(W8PrepArgs a) {
-    extern __shared__ int smem_w8prep[];
-    int* smem = smem_w8prep;
+    extern __shared__ __align__(16) unsigned char smem_w8prep[];
+    if (blockIdx.x > 0) {  // rotate token row blockIdx.x - 1
+        double* s_v = reinterpret_cast<double*>(smem_w8prep);
+        float* s_row = reinterpret_cast<float*>(s_v + blockDim.x);
+        const int64_t t = blockIdx.x - 1;
+        rotate_row<false>(a.x + t * a.hidden, a.hidden, a.ws.xq + t * a.hidden, a.ws.xs + t, s_v, s_row);
+        return;
+    }
+    int* smem = reinterpret_cast<int*>(smem_w8prep);
     __shared__ int dropped;
     __shared__ int warp_tot[32];
+    __shared__ int s_groups;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int S = a.slots;
     if (tid == 0) dropped = 0;
     __syncthreads();
+    if (a.pairs <= 32) {
+        // one warp: lanes are pairs; equal ids form groups of <= 8 in lane order
+        if (warp == 0) {
+            const int64_t id = lane < a.pairs ? load_index(a.ids, a.ids_dtype, lane) : -2;
+            const bool valid = id >= 0 && id < S;
+            const int key = valid ? static_cast<int>(id) : -2 - lane;  // invalid lanes stay alone
+            const unsigned mask = __match_any_sync(0xffffffffu, key);
+            const bool leader = valid && lane == __ffs(mask) - 1;
+            const int ng = leader ? (__popc(mask) + kW8Group - 1) / kW8Group : 0;
+            int base = ng;
+#pragma unroll
+            for (int off = 1; off < 32; off <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, base, off);
+                if (lane >= off) base += y;
+            }
+            const int total = __shfl_sync(0xffffffffu, base, 31);
+            base -= ng;
+            if (leader) {
+                unsigned rest = mask;
+                for (int j = 0; j < ng; ++j) {
+                    uint32_t packed[4] = {0u, 0u, 0u, 0u};
+                    int cnt = 0;
+                    while (rest && cnt < kW8Group) {
+                        const int member = __ffs(rest) - 1;
+                        rest &= rest - 1;
+                        packed[cnt >> 1] |= static_cast<uint32_t>(member) << (16 * (cnt & 1));
+                        ++cnt;
+                    }
+                    a.ws.g_rec[2 * (base + j)] = make_int4(static_cast<int>(id), 0, cnt, 0);
+                    a.ws.g_rec[2 * (base + j) + 1] = make_int4(static_cast<int>(packed[0]), static_cast<int>(packed[1]),
+                                                               static_cast<int>(packed[2]), static_cast<int>(packed[3]));
+                }
+            }
+            const unsigned bad = __ballot_sync(0xffffffffu, lane < a.pairs && !valid);
+            if (lane == 0) {
+                s_groups = total;
+                dropped = __popc(bad);
+            }
+        }
+        __syncthreads();
+        w8a8_prep_tail(a, s_groups, dropped);
+        return;
+    }
     stable_bucket(a.ids, a.ids_dtype, a.pairs, S, smem, nullptr, a.ws.order, &dropped);
     const int* counts = smem;
     const int* ends = smem + S;
@@ -133,92 +312,27 @@ __global__ void __launch_bounds__(1024) w8a8_prep_kernel(W8PrepArgs a) {
             const int cnt = min(kW8Group, c - j * kW8Group);
             uint32_t packed[4] = {0u, 0u, 0u, 0u};
             for (int q = 0; q < cnt; ++q)
-                packed[q >> 1] |= static_cast<uint32_t>(a.ws.order[start + j * kW8Group + q] & 0xffff) << (16 * (q & 1));
+                packed[q >> 1] |= static_cast<uint32_t>(a.ws.order[start + j * kW8Group + q] & 0xffff)
+                                  << (16 * (q & 1));
             a.ws.g_rec[2 * (gbase + j)] = make_int4(tid, start + j * kW8Group, cnt, 0);
             a.ws.g_rec[2 * (gbase + j) + 1] = make_int4(static_cast<int>(packed[0]), static_cast<int>(packed[1]),
                                                         static_cast<int>(packed[2]), static_cast<int>(packed[3]));
         }
     }
-    if (tid == 0) {
-        a.ws.num_groups[0] = warp_tot[31];
-        a.ws.status[0] = dropped;
-    }
-    for (int64_t p = tid; p < a.pairs; p += blockDim.x) a.ws.wts[p] = load_any(a.weights, a.weights_dtype, p);
-    if (dropped) {
-        for (int64_t p = 0; p < a.pairs; ++p) {
-            const int64_t id = load_index(a.ids, a.ids_dtype, p);
-            if (id < 0 || id >= S)
-                for (int n = tid; n < a.hidden; n += blockDim.x) a.pair_out[p * a.hidden + n] = 0.0f;
-        }
-    }
+    w8a8_prep_tail(a, warp_tot[31], dropped);
+}
+
+// SwiGLU rows -> int8 (one CTA per pair)
+__global__ void __launch_bounds__(1024) w8a8_act_kernel(const __nv_bfloat16* up, int I, int8_t* hq, float* hs) {
+    extern __shared__ __align__(16) unsigned char smem_w8act[];
+    double* s_v = reinterpret_cast<double*>(smem_w8act);
+    float* s_row = reinterpret_cast<float*>(s_v + blockDim.x);
+    const int64_t p = blockIdx.x;
+    rotate_row<true>(up + p * 2 * I, I, hq + p * I, hs + p, s_v, s_row);
 }
 
 // ---------------------------------------------------------------------------
-// rotate: one row per CTA -> int8 row + fp32 scale
-// ---------------------------------------------------------------------------
-__constant__ double kH4[4][4] = {{1, 1, 1, -1}, {1, 1, -1, 1}, {1, -1, 1, 1}, {-1, 1, 1, 1}};
-
-// ACT = false: src = bf16 rows [rows][K]; ACT = true: src = bf16 gate/up rows
-// [rows][2K] and the row is bf16(bf16(silu(gate)) * up).
-template <bool ACT>
-__global__ void __launch_bounds__(kRotThreads) w8a8_rotate_kernel(const __nv_bfloat16* src, int K, int8_t* q,
-                                                                   float* qs) {
-    extern __shared__ float s_row[];  // [K] rotated, rounded values
-    __shared__ double s_v[kRotThreads];
-    __shared__ float s_red[kRotThreads / 32];
-    const int j = threadIdx.x, lane = j & 31, warp = j >> 5;
-    const int64_t r = blockIdx.x;
-    const __nv_bfloat16* row = src + r * (ACT ? 2 * K : K);
-    float amax = 0.0f;
-    for (int c = 0; c < K / 256; ++c) {
-        const int col = c * 256 + j;
-        float v;
-        if (ACT) {
-            const float g = __bfloat162float(row[col]);
-            const float u = __bfloat162float(row[K + col]);
-            const float act = __bfloat162float(__float2bfloat16_rn(g / (1.0f + expf(-g))));
-            v = __bfloat162float(__float2bfloat16_rn(act * u));
-        } else {
-            v = __bfloat162float(row[col]);
-        }
-        s_v[j] = static_cast<double>(v);
-        __syncthreads();
-#pragma unroll
-        for (int st = 0; st < 4; ++st) {  // base-4 digit st, least significant first
-            const int stride = 1 << (2 * st);
-            const int d = (j >> (2 * st)) & 3;
-            const int base = j - d * stride;
-            double acc = kH4[0][d] * s_v[base];
-            acc = acc + kH4[1][d] * s_v[base + stride];
-            acc = acc + kH4[2][d] * s_v[base + 2 * stride];
-            acc = acc + kH4[3][d] * s_v[base + 3 * stride];
-            __syncthreads();
-            s_v[j] = acc;
-            __syncthreads();
-        }
-        const float rv = __bfloat162float(__double2bfloat16(s_v[j] * 0.0625));
-        s_row[col] = rv;
-        amax = fmaxf(amax, fabsf(rv));
-        __syncthreads();
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    if (lane == 0) s_red[warp] = amax;
-    __syncthreads();
-    float m = s_red[0];
-#pragma unroll
-    for (int w = 1; w < kRotThreads / 32; ++w) m = fmaxf(m, s_red[w]);
-    const float scale = __fdiv_rn(fmaxf(m, 1e-12f), 127.0f);
-    for (int col = j; col < K; col += kRotThreads) {
-        float v = rintf(__fdiv_rn(s_row[col], scale));
-        v = fminf(fmaxf(v, -127.0f), 127.0f);
-        q[r * K + col] = static_cast<int8_t>(v);
-    }
-    if (j == 0) qs[r] = scale;
-}
-
-// ---------------------------------------------------------------------------
-// gemv: cells (group, 16-row tile), full K per warp
+// gemv: tasks (group, 16-row tile, K part)
 // ---------------------------------------------------------------------------
 struct W8Role {
     const uint8_t* w;
@@ -234,9 +348,16 @@ struct W8GemvArgs {
     const int8_t* act;        // [rows][k]
     const float* act_scale;   // [rows]
     int top_k;                // up: activation row = pair / top_k; down: row = pair
+    int ksplit;               // K parts per tile (spans divisible by ksplit * kW8Unroll)
+    int32_t* cnt;             // [cells] arrivals (ksplit > 1)
+    int4* part;               // [tasks][32] partial sums (ksplit > 1)
     __nv_bfloat16* up_out;    // up: [P][n]
     float* pair_out;          // down: [P][n]
     const float* wts;         // down: [P]
+    int32_t* cmb_cnt;         // down: [n/16] finished cells per row tile
+    void* out;                // down: [T][n] combined rows (NULL: pairs only)
+    int out_dtype;
+    int64_t tokens;
 };
 
 // Raw weight bytes of one span for one row, by mode.
@@ -259,6 +380,14 @@ __device__ __forceinline__ void load_span(SpanRaw<MODE>& raw, const uint8_t* wro
 }
 
 // 16 int8 grid values of one row's span slice, as four words (byte j = column 16t + j).
+//
+// Mode 2 runs two columns per instruction in f16x2, exactly: (1024 + code) is
+// built by OR-ing the 6-bit code into 0x6400, minus 1056 gives code - 32; the
+// product with the FP8 relative scale has at most 10 significant bits and lies
+// in [2^-9, 14336], so it is exact in f16 as in the reference's fp32; clamping
+// to +-127 before rounding equals rounding before clamping (the bounds are
+// integers); adding 1536 rounds to the nearest even integer (the f16 spacing
+// in [1024, 2048) is 1), and the low byte of 0x6400 + 512 + v is v mod 256.
 template <int MODE>
 __device__ __forceinline__ void dequant_span(const SpanRaw<MODE>& raw, float cb, uint32_t (&o)[4]) {
     if constexpr (MODE == 1) {
@@ -266,26 +395,33 @@ __device__ __forceinline__ void dequant_span(const SpanRaw<MODE>& raw, float cb,
         o[1] = raw.v.y;
         o[2] = raw.v.z;
         o[3] = raw.v.w;
+    } else if constexpr (MODE == 2) {
+        const uint32_t rel2 = e4m3x2_to_f16x2(raw.rel | (raw.rel << 8));
+        uint32_t r[8];
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {  // columns 2m, 2m + 1
+            const uint32_t L = m < 4 ? raw.lo.x : raw.lo.y;
+            const int b = m & 3;
+            const uint32_t P = __byte_perm(L, 0u, 0x4040u | b | (b << 8));  // [byte b, 0, byte b, 0]
+            const uint32_t Hs = raw.hi >> (4 * m);                          // top bits of 2m (0-1), 2m+1 (2-3)
+            const uint32_t codes = (P & 0x0000000Fu) | ((P >> 4) & 0x000F0000u) | ((Hs & 3u) << 4) |
+                                   ((Hs & 0xCu) << 18) | 0x64006400u;
+            r[m] = h2_add(h2_clamp127(h2_mul(h2_sub(codes, 0x64206420u), rel2)), 0x66006600u);
+        }
+#pragma unroll
+        for (int w = 0; w < 4; ++w) o[w] = __byte_perm(r[2 * w], r[2 * w + 1], 0x6420u);
     } else {
         const float rel = fp8_to_float(raw.rel);
         const uint64_t lo = (static_cast<uint64_t>(raw.lo.y) << 32) | raw.lo.x;
 #pragma unroll
         for (int w = 0; w < 4; ++w) {
-            uint32_t word = 0u;
+            uint32_t q[4];
 #pragma unroll
             for (int b = 0; b < 4; ++b) {
-                const int j = 4 * w + b;
-                int code = static_cast<int>((lo >> (4 * j)) & 15u);
-                float level;
-                if constexpr (MODE == 2) {
-                    code |= static_cast<int>((raw.hi >> (2 * j)) & 3u) << 4;
-                    level = static_cast<float>(code - 32);
-                } else {
-                    level = __shfl_sync(0xffffffffu, cb, code);
-                }
-                word |= grid_byte(level, rel) << (8 * b);
+                const int code = static_cast<int>((lo >> (4 * (4 * w + b))) & 15u);
+                q[b] = grid_byte(__shfl_sync(0xffffffffu, cb, code), rel);
             }
-            o[w] = word;
+            o[w] = __byte_perm(__byte_perm(q[0], q[1], 0x0040u), __byte_perm(q[2], q[3], 0x0040u), 0x5410u);
         }
     }
 }
@@ -301,16 +437,19 @@ __device__ __forceinline__ float channel_scale(const W8Role& r, int slot, int ro
     return __ldg(reinterpret_cast<const float*>(p));
 }
 
-template <int MODE, bool DOWN>
+// U: spans whose loads are all issued before the first MMA (4, or 8 when a
+// task's span count allows, so a batch-1 task is a single round trip).
+template <int MODE, bool DOWN, int U>
 __global__ void __launch_bounds__(kW8GemvThreads) w8a8_gemv_kernel(W8GemvArgs a) {
     const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const int warps_total = gridDim.x * (kW8GemvThreads / 32);
     const int groups = __ldg(a.num_groups);
     const W8Role& role = a.role;
-    const int tiles = role.n / 16, spans = role.k / 64;
+    const int tiles = role.n / 16, spans_per = role.k / 64 / a.ksplit;
+    const int tasks = groups * tiles * a.ksplit;
     const uint64_t pol = policy_evict_first();
-    for (int cell = blockIdx.x * (kW8GemvThreads / 32) + (threadIdx.x >> 5); cell < groups * tiles;
-         cell += warps_total) {
+    for (int task = blockIdx.x * (kW8GemvThreads / 32) + (threadIdx.x >> 5); task < tasks; task += warps_total) {
+        const int cell = task / a.ksplit, kpart = task - cell * a.ksplit;
         const int grp = cell / tiles, tile = cell - grp * tiles;
         const int4 head = __ldg(a.g_rec + 2 * grp);
         const int4 ids4 = __ldg(a.g_rec + 2 * grp + 1);
@@ -328,18 +467,19 @@ __global__ void __launch_bounds__(kW8GemvThreads) w8a8_gemv_kernel(W8GemvArgs a)
             cb = __ldg(reinterpret_cast<const float*>(role.s + slot * role.s_slot + (lane & 15) * role.s_row +
                                                       role.k / 16 + 4));
         int acc[4] = {0, 0, 0, 0};
-        for (int sp = 0; sp < spans; sp += kW8Unroll) {
-            SpanRaw<MODE> raw0[kW8Unroll], raw1[kW8Unroll];
-            uint4 xb[kW8Unroll];
+        const int sp_end = (kpart + 1) * spans_per;
+        for (int sp = kpart * spans_per; sp < sp_end; sp += U) {
+            SpanRaw<MODE> raw0[U], raw1[U];
+            uint4 xb[U];
 #pragma unroll
-            for (int u = 0; u < kW8Unroll; ++u) {
+            for (int u = 0; u < U; ++u) {
                 load_span<MODE>(raw0[u], w0, s0, sp + u, t, role.k, pol);
                 load_span<MODE>(raw1[u], w1, s1, sp + u, t, role.k, pol);
                 xb[u] = arow ? __ldg(reinterpret_cast<const uint4*>(arow + (sp + u) * 64 + 16 * t))
                              : make_uint4(0u, 0u, 0u, 0u);
             }
 #pragma unroll
-            for (int u = 0; u < kW8Unroll; ++u) {
+            for (int u = 0; u < U; ++u) {
                 uint32_t A0[4], A1[4];
                 dequant_span<MODE>(raw0[u], cb, A0);
                 dequant_span<MODE>(raw1[u], cb, A1);
@@ -347,6 +487,27 @@ __global__ void __launch_bounds__(kW8GemvThreads) w8a8_gemv_kernel(W8GemvArgs a)
                 const uint32_t a2[4] = {A0[2], A1[2], A0[3], A1[3]};
                 mma_s8_16832(acc, a1, xb[u].x, xb[u].y);
                 mma_s8_16832(acc, a2, xb[u].z, xb[u].w);
+            }
+        }
+        if (a.ksplit > 1) {
+            // leave the partial sums; the last-arriving part of the tile adds them all
+            __stcg(a.part + static_cast<int64_t>(task) * 32 + lane, make_int4(acc[0], acc[1], acc[2], acc[3]));
+            __syncwarp();
+            int old = 0;
+            if (lane == 0) {
+                w8_fence();
+                old = atomicAdd(a.cnt + cell, 1);
+            }
+            old = __shfl_sync(0xffffffffu, old, 0);
+            if (old != a.ksplit - 1) continue;
+            w8_fence();
+            acc[0] = acc[1] = acc[2] = acc[3] = 0;
+            for (int q = 0; q < a.ksplit; ++q) {
+                const int4 v = __ldcg(a.part + (static_cast<int64_t>(cell) * a.ksplit + q) * 32 + lane);
+                acc[0] += v.x;
+                acc[1] += v.y;
+                acc[2] += v.z;
+                acc[3] += v.w;
             }
         }
         // epilogue: acc[0..1] row r0, token columns 2t, 2t+1; acc[2..3] row r0 + 8
@@ -369,37 +530,53 @@ __global__ void __launch_bounds__(kW8GemvThreads) w8a8_gemv_kernel(W8GemvArgs a)
                 }
             }
         }
+        if constexpr (DOWN) {
+            if (!a.out) continue;
+            // the last cell of this row tile sums its rows' route slots in slot order
+            __syncwarp();
+            int old = 0;
+            if (lane == 0) {
+                w8_fence();
+                old = atomicAdd(a.cmb_cnt + tile, 1);
+            }
+            old = __shfl_sync(0xffffffffu, old, 0);
+            if (old != groups - 1) continue;
+            w8_fence();
+            const int n = role.n;
+            for (int i = lane; i < a.tokens * 16; i += 32) {
+                const int64_t tok = i >> 4;
+                const int row = tile * 16 + (i & 15);
+                float sum = 0.0f;
+                for (int sl = 0; sl < a.top_k; ++sl)
+                    sum = __fadd_rn(sum, __ldcg(a.pair_out + (tok * a.top_k + sl) * n + row));
+                store_any(a.out, a.out_dtype, tok * n + row, sum);
+            }
+        }
     }
 }
 
-// out[t] = sum over slots, in order, of pair_out[t*k + s] (slots with an
-// out-of-range id hold zeros), rounded to the output dtype.
-__global__ void w8a8_combine_kernel(const float* pair_out, int64_t tokens, int top_k, int H, void* out,
-                                    int out_dtype) {
-    const int64_t n = tokens * H;
-    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int64_t tok = i / H, col = i - tok * H;
-        float acc = 0.0f;
-        for (int s = 0; s < top_k; ++s) acc = __fadd_rn(acc, pair_out[(tok * top_k + s) * H + col]);
-        store_any(out, out_dtype, i, acc);
-    }
+// Upper bound of expert groups: every group holds >= 1 pair.
+int64_t max_groups(int64_t pairs) { return pairs; }
+
+// K parts per tile: split only while the tiles alone leave the GPU idle.
+int split_for(int64_t cells, int spans) {
+    for (int ks = 4; ks > 1; --ks)
+        if (cells * ks <= kW8TargetWarps && spans % (ks * kW8Unroll) == 0) return ks;
+    return 1;
 }
+
+int rot_threads(int K) { return K < 1024 ? K : 1024; }
+size_t rot_smem(int K) { return static_cast<size_t>(rot_threads(K)) * sizeof(double) + K * sizeof(float); }
 
 template <int MODE>
-cudaError_t launch_mode(const DramaB200W8a8Bank& b, const void* x, int64_t tokens, int top_k, void* out,
-                        int out_dtype, float* pair_out, const W8a8Workspace& ws, int sm_count, cudaStream_t s) {
+cudaError_t launch_mode(const DramaB200W8a8Bank& b, int64_t tokens, int top_k, void* out, int out_dtype,
+                        float* pair_out, const W8a8Workspace& ws, int sm_count, cudaStream_t s) {
     const int64_t P = tokens * top_k;
     const int H = b.hidden, I = b.intermediate;
-    w8a8_rotate_kernel<false><<<static_cast<unsigned>(tokens), kRotThreads, H * sizeof(float), s>>>(
-        static_cast<const __nv_bfloat16*>(x), H, ws.xq, ws.xs);
-    cudaError_t err = cudaGetLastError();
-    if (err != cudaSuccess) return err;
-    const int max_groups = static_cast<int>(P < b.slots ? P : b.slots) + static_cast<int>(P / kW8Group);
-    auto grid_for = [&](int n) {
-        const int64_t cells = static_cast<int64_t>(max_groups) * (n / 16);
-        int64_t ctas = (cells + kW8GemvThreads / 32 - 1) / (kW8GemvThreads / 32);
-        const int64_t cap = static_cast<int64_t>(sm_count) * 8;
+    const int64_t gmax = max_groups(P);
+    auto grid_for = [&](int64_t tasks) {
+        int64_t ctas = (tasks + kW8GemvThreads / 32 - 1) / (kW8GemvThreads / 32);
+        const int64_t cap = static_cast<int64_t>(sm_count) * 16;
         return static_cast<unsigned>(ctas < 1 ? 1 : (ctas > cap ? cap : ctas));
     };
     W8GemvArgs up{};
@@ -410,12 +587,17 @@ cudaError_t launch_mode(const DramaB200W8a8Bank& b, const void* x, int64_t token
     up.act = ws.xq;
     up.act_scale = ws.xs;
     up.top_k = top_k;
+    up.ksplit = split_for(gmax * (2 * I / 16), H / 64);
+    up.cnt = ws.up_cnt;
+    up.part = ws.part;
     up.up_out = ws.up;
-    w8a8_gemv_kernel<MODE, false><<<grid_for(2 * I), kW8GemvThreads, 0, s>>>(up);
-    err = cudaGetLastError();
+    if ((H / 64 / up.ksplit) % 8 == 0)
+        w8a8_gemv_kernel<MODE, false, 8><<<grid_for(gmax * (2 * I / 16) * up.ksplit), kW8GemvThreads, 0, s>>>(up);
+    else
+        w8a8_gemv_kernel<MODE, false, 4><<<grid_for(gmax * (2 * I / 16) * up.ksplit), kW8GemvThreads, 0, s>>>(up);
+    cudaError_t err = cudaGetLastError();
     if (err != cudaSuccess) return err;
-    w8a8_rotate_kernel<true><<<static_cast<unsigned>(P), kRotThreads, I * sizeof(float), s>>>(ws.up, I, ws.hq,
-                                                                                              ws.hs);
+    w8a8_act_kernel<<<static_cast<unsigned>(P), rot_threads(I), rot_smem(I), s>>>(ws.up, I, ws.hq, ws.hs);
     err = cudaGetLastError();
     if (err != cudaSuccess) return err;
     W8GemvArgs dn{};
@@ -426,14 +608,19 @@ cudaError_t launch_mode(const DramaB200W8a8Bank& b, const void* x, int64_t token
     dn.act = ws.hq;
     dn.act_scale = ws.hs;
     dn.top_k = top_k;
+    dn.ksplit = split_for(gmax * (H / 16), I / 64);
+    dn.cnt = ws.dn_cnt;
+    dn.part = ws.part;
     dn.pair_out = pair_out;
     dn.wts = ws.wts;
-    w8a8_gemv_kernel<MODE, true><<<grid_for(H), kW8GemvThreads, 0, s>>>(dn);
-    err = cudaGetLastError();
-    if (err != cudaSuccess || !out) return err;
-    const int64_t n = tokens * H;
-    const int blocks = static_cast<int>((n + 255) / 256 < sm_count * 4 ? (n + 255) / 256 : sm_count * 4);
-    w8a8_combine_kernel<<<blocks, 256, 0, s>>>(pair_out, tokens, top_k, H, out, out_dtype);
+    dn.cmb_cnt = ws.cmb_cnt;
+    dn.out = out;
+    dn.out_dtype = out_dtype;
+    dn.tokens = tokens;
+    if ((I / 64 / dn.ksplit) % 8 == 0)
+        w8a8_gemv_kernel<MODE, true, 8><<<grid_for(gmax * (H / 16) * dn.ksplit), kW8GemvThreads, 0, s>>>(dn);
+    else
+        w8a8_gemv_kernel<MODE, true, 4><<<grid_for(gmax * (H / 16) * dn.ksplit), kW8GemvThreads, 0, s>>>(dn);
     return cudaGetLastError();
 }
 
@@ -442,6 +629,12 @@ cudaError_t launch_mode(const DramaB200W8a8Bank& b, const void* x, int64_t token
 size_t w8a8_workspace_layout(int64_t tokens, int top_k, int hidden, int intermediate, char* base,
                              W8a8Workspace* ws) {
     const int64_t P = tokens * top_k;
+    const int64_t gmax = max_groups(P);
+    const int64_t up_cells = gmax * (2 * intermediate / 16), dn_cells = gmax * (hidden / 16);
+    const int64_t up_parts = split_for(up_cells, hidden / 64), dn_parts = split_for(dn_cells, intermediate / 64);
+    const int64_t up_tasks = up_parts > 1 ? up_cells * up_parts : 0;
+    const int64_t dn_tasks = dn_parts > 1 ? dn_cells * dn_parts : 0;
+    const int64_t part_tasks = up_tasks > dn_tasks ? up_tasks : dn_tasks;  // up and down share the scratch
     size_t off = 0;
     auto take = [&](size_t bytes) -> char* {
         char* p = base ? base + off : nullptr;
@@ -460,6 +653,10 @@ size_t w8a8_workspace_layout(int64_t tokens, int top_k, int hidden, int intermed
     w.hs = reinterpret_cast<float*>(take(P * 4));
     w.wts = reinterpret_cast<float*>(take(P * 4));
     w.pair_out = reinterpret_cast<float*>(take(static_cast<size_t>(P) * hidden * 4));
+    w.up_cnt = reinterpret_cast<int32_t*>(take(up_cells * 4));
+    w.dn_cnt = reinterpret_cast<int32_t*>(take(dn_cells * 4));
+    w.cmb_cnt = reinterpret_cast<int32_t*>(take(static_cast<size_t>(hidden / 16) * 4));
+    w.part = reinterpret_cast<int4*>(take(static_cast<size_t>(part_tasks) * 32 * sizeof(int4)));
     if (ws) *ws = w;
     return off;
 }
@@ -468,24 +665,29 @@ cudaError_t w8a8_decode_launch(const DramaB200W8a8Bank& bank, const void* x, int
                                const void* ids, int ids_dtype, const void* weights, int weights_dtype, void* out,
                                int out_dtype, float* pair_out, const W8a8Workspace& ws, int sm_count,
                                cudaStream_t s) {
-    W8PrepArgs pa{ids, ids_dtype, weights, weights_dtype, tokens * top_k, bank.slots, bank.hidden,
-                  pair_out ? pair_out : ws.pair_out, ws};
-    const size_t smem = static_cast<size_t>(34) * bank.slots * sizeof(int);
+    float* po = pair_out ? pair_out : ws.pair_out;
+    W8PrepArgs pa{ids, ids_dtype, weights, weights_dtype, static_cast<const __nv_bfloat16*>(x), tokens * top_k,
+                  bank.slots, bank.hidden, bank.intermediate, po, ws};
+    // CTA 0 buckets (34 ints per slot); CTAs 1..T rotate a token row with all 1024 threads
+    const size_t bucket_smem = static_cast<size_t>(34) * bank.slots * sizeof(int);
+    const size_t rot = 1024 * sizeof(double) + static_cast<size_t>(bank.hidden) * sizeof(float);
+    const size_t smem = bucket_smem > rot ? bucket_smem : rot;
     static bool configured = false;  // benign race: identical values
     if (!configured) {
-        const cudaError_t err =
-            cudaFuncSetAttribute(w8a8_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 34 * kMaxSlots * 4);
+        cudaError_t err = cudaFuncSetAttribute(w8a8_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               200 * 1024);
+        if (err == cudaSuccess)
+            err = cudaFuncSetAttribute(w8a8_act_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
         if (err != cudaSuccess) return err;
         configured = true;
     }
-    w8a8_prep_kernel<<<1, 1024, smem, s>>>(pa);
+    w8a8_prep_kernel<<<static_cast<unsigned>(1 + tokens), 1024, smem, s>>>(pa);
     cudaError_t err = cudaGetLastError();
     if (err != cudaSuccess) return err;
-    float* po = pair_out ? pair_out : ws.pair_out;
     switch (bank.mode) {
-        case 1: return launch_mode<1>(bank, x, tokens, top_k, out, out_dtype, po, ws, sm_count, s);
-        case 2: return launch_mode<2>(bank, x, tokens, top_k, out, out_dtype, po, ws, sm_count, s);
-        default: return launch_mode<3>(bank, x, tokens, top_k, out, out_dtype, po, ws, sm_count, s);
+        case 1: return launch_mode<1>(bank, tokens, top_k, out, out_dtype, po, ws, sm_count, s);
+        case 2: return launch_mode<2>(bank, tokens, top_k, out, out_dtype, po, ws, sm_count, s);
+        default: return launch_mode<3>(bank, tokens, top_k, out, out_dtype, po, ws, sm_count, s);
     }
 }
 
