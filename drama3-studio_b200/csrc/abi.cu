@@ -299,6 +299,46 @@ int drama_b200_w8a8_decode(const DramaB200W8a8Bank* bank, const void* x, int x_d
     return 0;
 }
 
+size_t drama_b200_shared_expert_workspace_bytes(int64_t tokens, int hidden, int intermediate) {
+    return shared_expert_workspace_layout(tokens, hidden, intermediate, nullptr, nullptr);
+}
+
+int drama_b200_shared_expert(const DramaB200SharedExpert* mlp, const void* x, int64_t tokens, const void* routed,
+                             const void* residual, void* out, void* workspace, size_t workspace_bytes, void* stream) {
+    if (!mlp) return fail("mlp is required");
+    const DramaB200SharedExpert& m = *mlp;
+    if (!m.gate_proj || !m.up_proj || !m.down_proj || !m.gate_weight) return fail("shared expert weights are required");
+    if (!x || !out) return fail("x and out are required");
+    if (tokens < 0) return fail("tokens must be >= 0");
+    if (m.hidden < 128 || m.hidden % 128 || m.intermediate < 128 || m.intermediate % 128)
+        return fail("hidden and intermediate must be positive multiples of 128");
+    const void* rows[3] = {m.gate_proj, m.up_proj, m.down_proj};
+    const int64_t strides[3] = {m.gate_row_stride, m.up_row_stride, m.down_row_stride};
+    const int64_t widths[3] = {m.hidden, m.hidden, m.intermediate};
+    for (int i = 0; i < 3; ++i) {
+        if (!aligned16(rows[i]) || strides[i] % 8) return fail("weight rows must start on 16-byte boundaries");
+        if (strides[i] < widths[i]) return fail("a weight row stride is smaller than its row");
+    }
+    const void* acts[4] = {x, routed, residual, out};
+    for (const void* p : acts)
+        if (p && !aligned16(p)) return fail("activation rows must be 16-byte aligned");
+    const size_t xb = static_cast<size_t>(tokens) * m.hidden * 2;
+    if (overlaps(out, xb, x, xb)) return fail("output must not overlap x");
+    if (tokens == 0) return 0;
+    int sms = 0;
+    if (sm_count_current(&sms)) return -1;
+    const size_t need = shared_expert_workspace_layout(tokens, m.hidden, m.intermediate, nullptr, nullptr);
+    if (!workspace || workspace_bytes < need)
+        return fail("shared expert workspace too small: need %zu bytes, got %zu", need, workspace_bytes);
+    if (reinterpret_cast<uintptr_t>(workspace) & 255u) return fail("workspace must be 256-byte aligned");
+    SharedWorkspace ws{};
+    shared_expert_workspace_layout(tokens, m.hidden, m.intermediate, static_cast<char*>(workspace), &ws);
+    const cudaError_t err = shared_expert_launch(m, x, tokens, routed, residual, out, ws, sms,
+                                                 static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return fail("shared expert launch failed: %s", cudaGetErrorString(err));
+    return 0;
+}
+
 size_t drama_b200_moe_layer_workspace_bytes(int64_t tokens, int top_k, int hidden, int intermediate,
                                              int experts) {
     int sms = 0;

@@ -250,6 +250,19 @@ cudaError_t w8a8_decode_launch(const DramaB200W8a8Bank& bank, const void* x, int
                                int out_dtype, float* pair_out, const W8a8Workspace& ws, int sm_count,
                                cudaStream_t s);
 
+// Shared expert + gate fused with the routed combine (shared_expert.cu).
+struct SharedWorkspace {
+    __nv_bfloat16* gu;        // [T][2I] gate/up projections
+    __nv_bfloat16* h;         // [T][I] SwiGLU rows
+    float* gate_s;            // [T] bf16-rounded sigmoid gate
+    int32_t* cnt;             // split-K arrivals (reset by the last arriver)
+    float4* part;             // [tasks][32] fp32 partial sums
+};
+size_t shared_expert_workspace_layout(int64_t tokens, int hidden, int inter, char* base, SharedWorkspace* ws);
+cudaError_t shared_expert_launch(const DramaB200SharedExpert& m, const void* x, int64_t tokens, const void* routed,
+                                 const void* residual, void* out, const SharedWorkspace& ws, int sm_count,
+                                 cudaStream_t s);
+
 size_t prefill_workspace_layout(int64_t tokens, int top_k, int hidden, int intermediate, int experts, char* base,
                                 PrefillWorkspace* ws);
 cudaError_t prefill_launch(const DramaB200Fp8Bank& bank, const void* x, int64_t tokens, int top_k, const void* ids,

@@ -1,0 +1,244 @@
+// Shared expert + sigmoid gate, fused with the routed combine and the residual
+// (src/drama_low_vram/backbone_graph.py:327-337):
+//   shared = sigmoid(x @ g^T) * shared_expert(x)          (_shared_impl)
+//   out    = after_mixer + (routed + shared)               (_post_impl)
+// with the rounding points of the reference's bf16 torch modules:
+//   gate, up = bf16(x @ Wg^T), bf16(x @ Wu^T);  h = bf16(bf16(silu(gate)) * up)
+//   d = bf16(h @ Wd^T);  s = bf16(sigmoid(bf16(x @ g^T)));  shared = bf16(s * d)
+//   t = bf16(routed + shared);  out = bf16(after_mixer + t)
+// (routed and after_mixer are optional; without them out = shared or t.)
+//
+// Launches: gate/up GEMV -> per-token SwiGLU and gate scalar -> down GEMV whose
+// epilogue applies the gate, the routed sum and the residual. The GEMVs stream
+// the dense bf16 weights once per group of <= 8 tokens through
+// mma.m16n8k16 bf16 fragments (tokens as N), split K across warps when the
+// tiles alone would leave the GPU idle (batch 1), and add the fp32 partials in
+// part order in the last-arriving warp, so results do not depend on timing.
+#include "common.cuh"
+#include "grouped.cuh"
+#include "kernels.h"
+
+namespace drama {
+namespace {
+
+constexpr int kShThreads = 128;
+constexpr int kShTarget = 4736;  // 148 SMs x 32 warps: the split-K target
+constexpr int kShTok = 8;        // tokens per MMA N tile
+
+__device__ __forceinline__ void sh_fence() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+
+struct ShGemvArgs {
+    const __nv_bfloat16* w0;  // rows [0, n0) (gate_proj, or down_proj)
+    const __nv_bfloat16* w1;  // rows [n0, 2 n0) (up_proj), or NULL
+    int64_t w0_row, w1_row;   // elements
+    int n, k;                 // output rows (2 Is for gate/up, H for down), contraction length
+    int n0;
+    const __nv_bfloat16* act; // [T][k]
+    int64_t tokens;
+    int ksplit;
+    int32_t* cnt;             // [cells]
+    float4* part;             // [tasks][32]
+    // epilogue
+    __nv_bfloat16* gu;        // gate/up: [T][2 Is] bf16
+    const float* gate_s;      // down: [T] bf16-rounded sigmoid gate
+    const __nv_bfloat16* routed;    // down: [T][H] or NULL
+    const __nv_bfloat16* residual;  // down: [T][H] or NULL
+    __nv_bfloat16* out;       // down: [T][H]
+};
+
+template <bool DOWN>
+__global__ void __launch_bounds__(kShThreads) shared_gemv_kernel(ShGemvArgs a) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const int warps_total = gridDim.x * (kShThreads / 32);
+    const int tiles = a.n / 16;
+    const int tgroups = static_cast<int>((a.tokens + kShTok - 1) / kShTok);
+    const int spans_per = a.k / 32 / a.ksplit;  // 32-column spans
+    const int tasks = tgroups * tiles * a.ksplit;
+    const uint64_t pol = policy_evict_first();
+    for (int task = blockIdx.x * (kShThreads / 32) + (threadIdx.x >> 5); task < tasks; task += warps_total) {
+        const int cell = task / a.ksplit, kpart = task - cell * a.ksplit;
+        const int tg = cell / tiles, tile = cell - tg * tiles;
+        const int64_t tok = static_cast<int64_t>(tg) * kShTok + g;
+        const __nv_bfloat16* xrow = tok < a.tokens ? a.act + tok * a.k : nullptr;
+        const int r0 = tile * 16 + g, r1 = r0 + 8;
+        const __nv_bfloat16* w0 = r0 < a.n0 ? a.w0 + r0 * a.w0_row : a.w1 + (r0 - a.n0) * a.w1_row;
+        const __nv_bfloat16* w1 = r1 < a.n0 ? a.w0 + r1 * a.w0_row : a.w1 + (r1 - a.n0) * a.w1_row;
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        const int sp0 = kpart * spans_per;
+        for (int sp = sp0; sp < sp0 + spans_per; sp += 4) {
+            uint4 q0[4], q1[4], xb[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int col = (sp + u) * 32 + 8 * t;
+                q0[u] = ld_stream_v4(w0 + col, pol);
+                q1[u] = ld_stream_v4(w1 + col, pol);
+                xb[u] = xrow ? __ldg(reinterpret_cast<const uint4*>(xrow + col)) : make_uint4(0u, 0u, 0u, 0u);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                // columns 8t..8t+7 of the span: (0,1)+(2,3) feed the first k16 MMA, (4,5)+(6,7) the second
+                const uint32_t a1[4] = {q0[u].x, q1[u].x, q0[u].y, q1[u].y};
+                const uint32_t a2[4] = {q0[u].z, q1[u].z, q0[u].w, q1[u].w};
+                mma_bf16_16816(acc, a1, xb[u].x, xb[u].y);
+                mma_bf16_16816(acc, a2, xb[u].z, xb[u].w);
+            }
+        }
+        if (a.ksplit > 1) {
+            __stcg(a.part + static_cast<int64_t>(task) * 32 + lane, make_float4(acc[0], acc[1], acc[2], acc[3]));
+            __syncwarp();
+            int old = 0;
+            if (lane == 0) {
+                sh_fence();
+                old = atomicAdd(a.cnt + cell, 1);
+            }
+            old = __shfl_sync(0xffffffffu, old, 0);
+            if (old != a.ksplit - 1) continue;
+            if (lane == 0) a.cnt[cell] = 0;  // ready for the next call
+            sh_fence();
+            acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+            for (int q = 0; q < a.ksplit; ++q) {  // part order: the sum does not depend on arrival order
+                const float4 v = __ldcg(a.part + (static_cast<int64_t>(cell) * a.ksplit + q) * 32 + lane);
+                acc[0] += v.x;
+                acc[1] += v.y;
+                acc[2] += v.z;
+                acc[3] += v.w;
+            }
+        }
+        // acc[0..1]: row r0, tokens 2t, 2t+1 of the group; acc[2..3]: row r1
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+            const int64_t tk = static_cast<int64_t>(tg) * kShTok + 2 * t + c;
+            if (tk >= a.tokens) continue;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int row = h ? r1 : r0;
+                const float v = __bfloat162float(__float2bfloat16_rn(acc[2 * h + c]));  // F.linear in bf16
+                if constexpr (DOWN) {
+                    const int64_t o = tk * a.n + row;
+                    float y = __bfloat162float(__float2bfloat16_rn(a.gate_s[tk] * v));  // shared_gate * shared
+                    if (a.routed) y = __bfloat162float(__float2bfloat16_rn(__bfloat162float(a.routed[o]) + y));
+                    if (a.residual) y = __bfloat162float(a.residual[o]) + y;
+                    a.out[o] = __float2bfloat16_rn(y);
+                } else {
+                    a.gu[tk * a.n + row] = __float2bfloat16_rn(v);
+                }
+            }
+        }
+    }
+}
+
+// Per token: h = bf16(bf16(silu(gate)) * up) and s = bf16(sigmoid(bf16(x . g))).
+__global__ void __launch_bounds__(256) shared_act_kernel(const __nv_bfloat16* x, const __nv_bfloat16* gate_w, int H,
+                                                          const __nv_bfloat16* gu, int I, __nv_bfloat16* h,
+                                                          float* gate_s) {
+    __shared__ float s_red[8];
+    const int64_t tok = blockIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    float dot = 0.f;
+    for (int c = tid; c < H; c += blockDim.x)
+        dot = fmaf(__bfloat162float(x[tok * H + c]), __bfloat162float(gate_w[c]), dot);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+    if (lane == 0) s_red[warp] = dot;
+    __syncthreads();
+    if (tid == 0) {
+        float sum = 0.f;
+        for (int w = 0; w < 8; ++w) sum += s_red[w];
+        const float logit = __bfloat162float(__float2bfloat16_rn(sum));
+        gate_s[tok] = __bfloat162float(__float2bfloat16_rn(1.0f / (1.0f + expf(-logit))));
+    }
+    for (int j = tid; j < I; j += blockDim.x) {
+        const float gt = __bfloat162float(gu[tok * 2 * I + j]);
+        const float up = __bfloat162float(gu[tok * 2 * I + I + j]);
+        const float act = __bfloat162float(__float2bfloat16_rn(gt / (1.0f + expf(-gt))));
+        h[tok * I + j] = __float2bfloat16_rn(act * up);
+    }
+}
+
+int sh_split(int64_t cells, int spans) {
+    for (int ks = 4; ks > 1; --ks)
+        if (cells * ks <= kShTarget && spans % (ks * 4) == 0) return ks;
+    return 1;
+}
+
+}  // namespace
+
+size_t shared_expert_workspace_layout(int64_t tokens, int hidden, int inter, char* base, SharedWorkspace* ws) {
+    const int64_t tg = (tokens + kShTok - 1) / kShTok;
+    const int64_t up_cells = tg * (2 * inter / 16), dn_cells = tg * (hidden / 16);
+    const int up_ks = sh_split(up_cells, hidden / 32), dn_ks = sh_split(dn_cells, inter / 32);
+    const int64_t up_tasks = up_ks > 1 ? up_cells * up_ks : 0, dn_tasks = dn_ks > 1 ? dn_cells * dn_ks : 0;
+    size_t off = 0;
+    auto take = [&](size_t bytes) -> char* {
+        char* p = base ? base + off : nullptr;
+        off += (bytes + 255) & ~static_cast<size_t>(255);
+        return p;
+    };
+    SharedWorkspace w{};
+    w.gu = reinterpret_cast<__nv_bfloat16*>(take(static_cast<size_t>(tokens) * 2 * inter * 2));
+    w.h = reinterpret_cast<__nv_bfloat16*>(take(static_cast<size_t>(tokens) * inter * 2));
+    w.gate_s = reinterpret_cast<float*>(take(tokens * 4));
+    w.cnt = reinterpret_cast<int32_t*>(take((up_cells > dn_cells ? up_cells : dn_cells) * 4));
+    w.part = reinterpret_cast<float4*>(take(static_cast<size_t>(up_tasks > dn_tasks ? up_tasks : dn_tasks) * 32 * 16));
+    if (ws) *ws = w;
+    return off;
+}
+
+cudaError_t shared_expert_launch(const DramaB200SharedExpert& m, const void* x, int64_t tokens, const void* routed,
+                                 const void* residual, void* out, const SharedWorkspace& ws, int sm_count,
+                                 cudaStream_t s) {
+    const int H = m.hidden, I = m.intermediate;
+    const int64_t tg = (tokens + kShTok - 1) / kShTok;
+    auto grid_for = [&](int64_t tasks) {
+        const int64_t ctas = (tasks + kShThreads / 32 - 1) / (kShThreads / 32);
+        const int64_t cap = static_cast<int64_t>(sm_count) * 16;
+        return static_cast<unsigned>(ctas < 1 ? 1 : (ctas > cap ? cap : ctas));
+    };
+    // the split-K counters: zeroed per call (the scratch may have held another shape's layout); the gate/up
+    // kernel's last arrivers reset the cells they used, so the down kernel finds them zero as well
+    const int64_t cells = tg * (2 * I > H ? 2 * I : H) / 16;
+    cudaError_t err = cudaMemsetAsync(ws.cnt, 0, static_cast<size_t>(cells) * sizeof(int32_t), s);
+    if (err != cudaSuccess) return err;
+    ShGemvArgs up{};
+    up.w0 = static_cast<const __nv_bfloat16*>(m.gate_proj);
+    up.w1 = static_cast<const __nv_bfloat16*>(m.up_proj);
+    up.w0_row = m.gate_row_stride;
+    up.w1_row = m.up_row_stride;
+    up.n = 2 * I;
+    up.n0 = I;
+    up.k = H;
+    up.act = static_cast<const __nv_bfloat16*>(x);
+    up.tokens = tokens;
+    up.ksplit = sh_split(tg * (2 * I / 16), H / 32);
+    up.cnt = ws.cnt;
+    up.part = ws.part;
+    up.gu = ws.gu;
+    shared_gemv_kernel<false><<<grid_for(tg * (2 * I / 16) * up.ksplit), kShThreads, 0, s>>>(up);
+    err = cudaGetLastError();
+    if (err != cudaSuccess) return err;
+    shared_act_kernel<<<static_cast<unsigned>(tokens), 256, 0, s>>>(
+        static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(m.gate_weight), H, ws.gu, I, ws.h,
+        ws.gate_s);
+    err = cudaGetLastError();
+    if (err != cudaSuccess) return err;
+    ShGemvArgs dn{};
+    dn.w0 = static_cast<const __nv_bfloat16*>(m.down_proj);
+    dn.w1 = nullptr;
+    dn.w0_row = m.down_row_stride;
+    dn.n = H;
+    dn.n0 = H;
+    dn.k = I;
+    dn.act = ws.h;
+    dn.tokens = tokens;
+    dn.ksplit = sh_split(tg * (H / 16), I / 32);
+    dn.cnt = ws.cnt;
+    dn.part = ws.part;
+    dn.gate_s = ws.gate_s;
+    dn.routed = static_cast<const __nv_bfloat16*>(routed);
+    dn.residual = static_cast<const __nv_bfloat16*>(residual);
+    dn.out = static_cast<__nv_bfloat16*>(out);
+    shared_gemv_kernel<true><<<grid_for(tg * (H / 16) * dn.ksplit), kShThreads, 0, s>>>(dn);
+    return cudaGetLastError();
+}
+
+}  // namespace drama

@@ -39,6 +39,8 @@ EXPORTS = (
     "drama_b200_int4_decode",
     "drama_b200_w8a8_workspace_bytes",
     "drama_b200_w8a8_decode",
+    "drama_b200_shared_expert_workspace_bytes",
+    "drama_b200_shared_expert",
     "drama_b200_moe_layer_workspace_bytes",
     "drama_b200_fp8_moe_layer",
     "drama_b200_fp8_moe_router",
@@ -108,6 +110,14 @@ class W8a8Bank(ctypes.Structure):
     ]
 
 
+class SharedExpert(ctypes.Structure):
+    _fields_ = [
+        ("gate_proj", c_void_p), ("up_proj", c_void_p), ("down_proj", c_void_p), ("gate_weight", c_void_p),
+        ("gate_row_stride", c_int64), ("up_row_stride", c_int64), ("down_row_stride", c_int64),
+        ("hidden", ctypes.c_int32), ("intermediate", ctypes.c_int32),
+    ]
+
+
 class EpPeers(ctypes.Structure):
     _fields_ = [
         ("ranks", ctypes.c_int32), ("rank", ctypes.c_int32), ("capacity", c_int64),
@@ -146,6 +156,11 @@ class Library:
         dll.drama_b200_w8a8_decode.restype = c_int
         dll.drama_b200_w8a8_workspace_bytes.argtypes = [c_int64, c_int, c_int, c_int]
         dll.drama_b200_w8a8_workspace_bytes.restype = c_size_t
+        dll.drama_b200_shared_expert_workspace_bytes.argtypes = [c_int64, c_int, c_int]
+        dll.drama_b200_shared_expert_workspace_bytes.restype = c_size_t
+        dll.drama_b200_shared_expert.argtypes = [ctypes.POINTER(SharedExpert), c_void_p, c_int64, c_void_p, c_void_p,
+                                                 c_void_p, c_void_p, c_size_t, c_void_p]
+        dll.drama_b200_shared_expert.restype = c_int
         dll.drama_b200_moe_layer_workspace_bytes.argtypes = [c_int64, c_int, c_int, c_int, c_int]
         dll.drama_b200_moe_layer_workspace_bytes.restype = c_size_t
         dll.drama_b200_fp8_moe_layer.argtypes = [

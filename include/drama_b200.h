@@ -201,6 +201,36 @@ DRAMA_B200_API int drama_b200_w8a8_decode(const DramaB200W8a8Bank* bank, const v
                                           void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Shared expert + sigmoid gate fused with the routed combine and the residual:
+ * BackboneDecodeGraph._shared_impl and _post_impl
+ * (src/drama_low_vram/backbone_graph.py:327-337) with the rounding points of
+ * the bf16 torch modules they call:
+ *   gate, up = bf16(x @ gate_proj^T), bf16(x @ up_proj^T)
+ *   h = bf16(bf16(silu(gate)) * up);  d = bf16(h @ down_proj^T)
+ *   s = bf16(sigmoid(bf16(x . gate_weight)));  shared = bf16(s * d)
+ *   t = routed ? bf16(routed + shared) : shared
+ *   out = residual ? bf16(residual + t) : t
+ * x, routed, residual, out: [tokens, H] bfloat16 (row stride H); weights bf16
+ * row-major with row strides in elements (multiples of 8, 16-byte aligned).
+ * H and I multiples of 128. out may alias routed or residual (each element is
+ * read before it is written, by the same thread).
+ * ------------------------------------------------------------------------- */
+typedef struct DramaB200SharedExpert {
+    const void* gate_proj;     /* [I, H] */
+    const void* up_proj;       /* [I, H] */
+    const void* down_proj;     /* [H, I] */
+    const void* gate_weight;   /* [H]: shared_expert_gate (a Linear to one output, no bias) */
+    int64_t gate_row_stride, up_row_stride, down_row_stride;
+    int32_t hidden, intermediate;
+} DramaB200SharedExpert;
+
+DRAMA_B200_API size_t drama_b200_shared_expert_workspace_bytes(int64_t tokens, int hidden, int intermediate);
+
+DRAMA_B200_API int drama_b200_shared_expert(const DramaB200SharedExpert* mlp, const void* x, int64_t tokens,
+                                            const void* routed, const void* residual, void* out, void* workspace,
+                                            size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
  * One decode MoE layer, fully on the device (graph-capturable):
  *   normed = bf16(x * 1/sqrt(mean(x^2) + eps) * gamma)      (fixed fp32 order)
  *   logits = bf16(normed @ gate^T)                           (fixed fp32 order)

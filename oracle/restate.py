@@ -33,6 +33,9 @@ Drama3-Studio source tree):
                           - ``src/drama_low_vram/quantized_kernels.py:15-45, 115-189,
                             217-248`` (W8A8 modes 1-3: INT8-ConvRot, W6A8, W4A8
                             codebook; layouts of ``quantized_model.py:45-68, 114-151``).
+* ``shared_expert`` / ``post_moe``
+                          - ``src/drama_low_vram/backbone_graph.py:327-337`` (shared
+                            expert, sigmoid gate, ``after_mixer + (experts + shared)``).
 * ``rms_norm`` / ``stack_layer`` - the decode layer of
                             ``src/drama_low_vram/backbone_graph.py:306-337`` without
                             the mixer and the shared expert.
@@ -752,3 +755,28 @@ def convrot_forward(x, ids, weights, bank, mode: int, dtype: str = "bfloat16"):
     pairs = convrot_pairs(np.repeat(x, top_k, axis=0), np.asarray(ids).reshape(-1),
                        np.asarray(weights).reshape(-1), bank, mode, dtype)
     return combine_slots(pairs, tokens, top_k, dtype)
+
+
+# --------------------------------------------------------------------------
+# Shared expert + gate and the post-MoE sum (backbone_graph.py:327-337)
+# --------------------------------------------------------------------------
+
+
+def shared_expert(x, gate_proj, up_proj, down_proj, gate_weight):
+    """``sigmoid(shared_expert_gate(x)) * shared_expert(x)`` with bf16 modules:
+    each Linear rounds to bf16, silu and the products round to bf16."""
+    x = np.asarray(x, dtype=F32)
+    gate = round_bf16(x @ np.asarray(gate_proj, F32).T)
+    up = round_bf16(x @ np.asarray(up_proj, F32).T)
+    h = round_bf16(round_bf16(silu(gate)) * up)
+    d = round_bf16(h @ np.asarray(down_proj, F32).T)
+    logit = round_bf16(x @ np.asarray(gate_weight, F32).reshape(-1, 1))
+    with np.errstate(over="ignore"):
+        s = round_bf16((F32(1.0) / (F32(1.0) + np.exp(-logit).astype(F32))).astype(F32))
+    return round_bf16(s * d)
+
+
+def post_moe(after_mixer, expert_output, shared):
+    """``after_mixer + (expert_output + shared)`` in bf16 (``_post_impl``)."""
+    t = round_bf16(np.asarray(expert_output, F32) + np.asarray(shared, F32))
+    return round_bf16(np.asarray(after_mixer, F32) + t)

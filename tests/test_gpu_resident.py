@@ -187,3 +187,37 @@ def test_resident_gptq_bank_matches_oracle(cuda_device):
         assert_parity(np_f32(out), ref, label="resident GPTQ")
     finally:
         manager.close()
+
+
+@pytest.mark.parametrize("kind", ["fp8", "gptq", "w8a8"])
+def test_batched_verification_rows_equal_per_row_calls(cuda_device, kind):
+    """``backbone_block(..., batch_experts=True)`` sends 1, 2 or 4 rows through one expert call
+    (src/drama_low_vram/verification.py:71-80); each row's result must not depend on the others."""
+    from drama_b200 import synthetic
+    from drama_b200.resident import install_resident_experts
+
+    if kind == "fp8":
+        module = Experts(synthetic.fp8_bank(E, H, I, 91))
+    else:
+        module = Experts(synthetic.fp8_bank(1, 256, 128, 0))
+        if kind == "gptq":
+            bank = synthetic.int4_bank(E, H, I, 92, asymmetric=False, scale_dtype=torch.float16)
+            module._drama_quant_store = _GptqStore(bank["w13_weight"], bank["w13_scale_inv"], bank["w2_weight"],
+                                                   bank["w2_scale_inv"], H, I)
+        else:
+            bank = synthetic.w8a8_bank(2, E, H, I, 93)
+            module._drama_quant_store = _GptqStore(bank["w13_weight"], bank["w13_scale_inv"], bank["w2_weight"],
+                                                   bank["w2_scale_inv"], H, I, mode=2)
+            module._drama_quant_store.validate = lambda: None
+    manager = install_resident_experts(nn.ModuleList([module]), device=cuda_device)
+    try:
+        for count in (1, 2, 4):
+            x = synthetic.hidden_states(count, H, 100 + count, device=cuda_device)
+            ids, w = synthetic.uniform_routes(count, K, E, 200 + count, device=cuda_device)
+            w = w.to(torch.bfloat16)
+            batched = module(x, ids, w)
+            rows = torch.cat([module(x[r:r + 1], ids[r:r + 1], w[r:r + 1]) for r in range(count)])
+            torch.cuda.synchronize()
+            assert torch.equal(batched.view(torch.int16), rows.view(torch.int16)), f"{kind}, {count} rows"
+    finally:
+        manager.close()
