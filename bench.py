@@ -44,12 +44,16 @@ def parse_args():
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--layers", type=int, default=48)
     p.add_argument("--decode-steps", type=int, default=512, help="decode tokens per CUDA graph")
-    p.add_argument("--workload", choices=("decode", "prefill", "ep", "offload", "int4", "w8a8"), default="decode",
+    p.add_argument("--workload", choices=("decode", "prefill", "ep", "offload", "int4", "w8a8", "shared"),
+                   default="decode",
                    help="decode: config 1 (the headline); prefill: config 3 (4096 tokens, one layer, Zipf); "
                         "ep: config 4 expert-parallel decode of 256 tokens over the torchrun ranks; "
                         "offload: config 4's 1-GPU offload variant (32 of 128 experts resident per layer); "
                         "int4: config 2 (one W4A16 asymmetric layer, decode batches 1/4/16, uniform routes); "
-                        "w8a8: config 2's measurement on a W8A8 bank of --mode 1, 2 or 3")
+                        "w8a8: config 2's measurement on a W8A8 bank of --mode 1, 2 or 3; "
+                        "shared: the shared expert + gate fused with the routed sum and residual, 48 layers")
+    p.add_argument("--shared-inter", type=int, default=768,
+                   help="shared: shared_expert_intermediate_size (the checkpoint's value is not available here)")
     p.add_argument("--mode", type=int, choices=(1, 2, 3), default=1,
                    help="w8a8: 1 INT8-ConvRot, 2 W6A8, 3 W4A8 codebook")
     p.add_argument("--exchange", choices=("p2p", "nccl"), default="p2p",
@@ -1010,6 +1014,111 @@ def run_int4(args, mode: int = 0) -> None:
         print(json.dumps(line))
 
 
+def run_shared(args) -> None:
+    """Shared expert + sigmoid gate fused with the routed sum and the residual
+    (``_shared_impl`` + ``_post_impl``, backbone_graph.py:327-337), batches 1/4/16.
+
+    One step = one replay of a CUDA graph holding one call per layer of a
+    48-layer stack of distinct bf16 shared experts (48 x 3 x H x I x 2 bytes,
+    larger than L2). ``value`` is the batch-1 tokens/s of the 48-layer pass.
+    """
+    import torch
+
+    from drama_b200 import synthetic
+    from drama_b200.shared import SharedExpertB200
+
+    world, rank, device, gpu_id = _dist_setup()
+    inter, layers = args.shared_inter, args.layers
+    gen = torch.Generator(device=device)
+    gen.manual_seed(4000 + rank)
+
+    def w(*shape):
+        return (torch.randn(*shape, generator=gen, device=device) * 0.03).to(torch.bfloat16)
+
+    mods = [SharedExpertB200(w(inter, HIDDEN), w(inter, HIDDEN), w(HIDDEN, inter), w(1, HIDDEN))
+            for _ in range(layers)]
+    layer_bytes = 3 * HIDDEN * inter * 2 + HIDDEN * 2
+    peaks = measured_peaks()
+    results = {}
+    clocks_summary = e2e_ms = None
+    for batch in (1, 4, 16):
+        x = synthetic.hidden_states(batch, HIDDEN, 50 + batch, device=device)
+        routed = synthetic.hidden_states(batch, HIDDEN, 60 + batch, device=device) * 0.1
+        hid = [synthetic.hidden_states(batch, HIDDEN, 70 + batch, device=device)]
+        cap = torch.cuda.Stream(device)
+        cap.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(cap):
+            h = hid[0]
+            for m in mods:
+                h = m.post(h, routed, x)
+        torch.cuda.synchronize(device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=cap):
+            h = hid[0]
+            for m in mods:
+                h = m.post(h, routed, x)
+            final = h
+        for _ in range(max(3, args.warmup)):
+            graph.replay()
+        torch.cuda.synchronize(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(gpu_id) as clocks:
+            e0.record()
+            for _ in range(args.steps):
+                graph.replay()
+            e1.record()
+            e1.synchronize()
+        ms = _max_over_ranks([e0.elapsed_time(e1) / args.steps], world, device)[0]
+        call_us = ms * 1000.0 / layers
+        step_bytes = layers * (layer_bytes + 4 * batch * HIDDEN * 2)
+        results[batch] = {"tokens_per_s": batch * world / (ms / 1000.0), "layer_us": call_us,
+                          "algorithmic_bytes_per_layer": layer_bytes + 4 * batch * HIDDEN * 2,
+                          "achieved_gbs": step_bytes / (ms / 1000.0) / 1e9}
+        if batch == 1:
+            clocks_summary = clocks.summary()
+            host_in = hid[0].cpu().pin_memory()
+            host_out = torch.empty_like(host_in).pin_memory()
+            f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            f0.record()
+            for _ in range(args.steps):
+                hid[0].copy_(host_in, non_blocking=True)
+                graph.replay()
+                host_out.copy_(final, non_blocking=True)
+            f1.record()
+            f1.synchronize()
+            e2e_ms = _max_over_ranks([f0.elapsed_time(f1) / args.steps], world, device)[0]
+        del graph
+    b1 = results[1]
+    line = {
+        "metric": METRIC, "value": b1["tokens_per_s"], "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": max(3, args.warmup), "ms_per_step": layers * b1["layer_us"] / 1000.0, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16 weights and activations, bf16 MMA, fp32 accumulate",
+        "data": "synthetic (seeded random-init weights and hidden rows)",
+        "config": {"workload": (f"shared expert + gate fused with the routed sum and residual, {layers} layers "
+                                f"(hidden {HIDDEN}, shared intermediate {inter} assumed), batches 1/4/16 "
+                                "(value: batch 1), one CUDA graph per batch"),
+                   "batches": [1, 4, 16], "parallelism": f"replicas{world}" if world > 1 else "single",
+                   "l2": f"{layers} distinct experts, {layers * layer_bytes / 1e6:.0f} MB (> L2)"},
+        "roofline": {"kernel": "one layer's shared expert (gate/up GEMV, SwiGLU, down GEMV + fused sum), batch 1",
+                     "bound": "hbm", "achieved": b1["achieved_gbs"], "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": b1["achieved_gbs"] / peaks["hbm_gbs"],
+                     "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs)", "traffic": None,
+                     "algorithmic_bytes_per_launch": b1["algorithmic_bytes_per_layer"]},
+        "by_batch": results,
+        "e2e": {"value": world / (e2e_ms / 1000.0), "unit": "tokens/s",
+                "h2d_bytes_per_step": HIDDEN * 2, "d2h_bytes_per_step": HIDDEN * 2},
+        "gpu_launches": args.steps * layers * 3,
+        "clocks": clocks_summary,
+    }
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line))
+
+
 def main() -> None:
     args = parse_args()
     if args.impl == "reference":
@@ -1024,6 +1133,8 @@ def main() -> None:
         run_int4(args)
     elif args.workload == "w8a8":
         run_int4(args, mode=args.mode)
+    elif args.workload == "shared":
+        run_shared(args)
     else:
         run_ours(args)
 

@@ -309,7 +309,7 @@ int drama_b200_shared_expert(const DramaB200SharedExpert* mlp, const void* x, in
     const DramaB200SharedExpert& m = *mlp;
     if (!m.gate_proj || !m.up_proj || !m.down_proj || !m.gate_weight) return fail("shared expert weights are required");
     if (!x || !out) return fail("x and out are required");
-    if (tokens < 0) return fail("tokens must be >= 0");
+    if (tokens < 0 || tokens > kMaxSharedTokens) return fail("tokens must be in [0, %d]", kMaxSharedTokens);
     if (m.hidden < 128 || m.hidden % 128 || m.intermediate < 128 || m.intermediate % 128)
         return fail("hidden and intermediate must be positive multiples of 128");
     const void* rows[3] = {m.gate_proj, m.up_proj, m.down_proj};

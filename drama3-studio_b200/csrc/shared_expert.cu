@@ -135,8 +135,16 @@ __global__ void __launch_bounds__(256) shared_act_kernel(const __nv_bfloat16* x,
     const int64_t tok = blockIdx.x;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     float dot = 0.f;
-    for (int c = tid; c < H; c += blockDim.x)
-        dot = fmaf(__bfloat162float(x[tok * H + c]), __bfloat162float(gate_w[c]), dot);
+    for (int c = tid * 8; c < H; c += blockDim.x * 8) {  // 8 columns per 16-byte load
+        const uint4 xv = __ldg(reinterpret_cast<const uint4*>(x + tok * H + c));
+        const uint4 gv = __ldg(reinterpret_cast<const uint4*>(gate_w + c));
+        const uint32_t xs[4] = {xv.x, xv.y, xv.z, xv.w}, gs[4] = {gv.x, gv.y, gv.z, gv.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            dot = fmaf(__uint_as_float(xs[i] << 16), __uint_as_float(gs[i] << 16), dot);
+            dot = fmaf(__uint_as_float(xs[i] & 0xffff0000u), __uint_as_float(gs[i] & 0xffff0000u), dot);
+        }
+    }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
     if (lane == 0) s_red[warp] = dot;
@@ -147,6 +155,7 @@ __global__ void __launch_bounds__(256) shared_act_kernel(const __nv_bfloat16* x,
         const float logit = __bfloat162float(__float2bfloat16_rn(sum));
         gate_s[tok] = __bfloat162float(__float2bfloat16_rn(1.0f / (1.0f + expf(-logit))));
     }
+#pragma unroll 4
     for (int j = tid; j < I; j += blockDim.x) {
         const float gt = __bfloat162float(gu[tok * 2 * I + j]);
         const float up = __bfloat162float(gu[tok * 2 * I + I + j]);
@@ -155,8 +164,10 @@ __global__ void __launch_bounds__(256) shared_act_kernel(const __nv_bfloat16* x,
     }
 }
 
+// K parts per tile: as many as keep the warps within the target, each part a
+// whole number of 4-span load batches (one round trip per batch).
 int sh_split(int64_t cells, int spans) {
-    for (int ks = 4; ks > 1; --ks)
+    for (int ks = spans / 4; ks > 1; --ks)
         if (cells * ks <= kShTarget && spans % (ks * 4) == 0) return ks;
     return 1;
 }
@@ -175,10 +186,13 @@ size_t shared_expert_workspace_layout(int64_t tokens, int hidden, int inter, cha
         return p;
     };
     SharedWorkspace w{};
+    // Split-K counters first, sized for the largest call, so that their place does not move with the
+    // shape: zero-filled once with the workspace, every cell is reset by its last arriver.
+    const int64_t max_tg = (kMaxSharedTokens + kShTok - 1) / kShTok;
+    w.cnt = reinterpret_cast<int32_t*>(take(max_tg * ((2 * inter > hidden ? 2 * inter : hidden) / 16) * 4));
     w.gu = reinterpret_cast<__nv_bfloat16*>(take(static_cast<size_t>(tokens) * 2 * inter * 2));
     w.h = reinterpret_cast<__nv_bfloat16*>(take(static_cast<size_t>(tokens) * inter * 2));
     w.gate_s = reinterpret_cast<float*>(take(tokens * 4));
-    w.cnt = reinterpret_cast<int32_t*>(take((up_cells > dn_cells ? up_cells : dn_cells) * 4));
     w.part = reinterpret_cast<float4*>(take(static_cast<size_t>(up_tasks > dn_tasks ? up_tasks : dn_tasks) * 32 * 16));
     if (ws) *ws = w;
     return off;
@@ -194,11 +208,6 @@ cudaError_t shared_expert_launch(const DramaB200SharedExpert& m, const void* x, 
         const int64_t cap = static_cast<int64_t>(sm_count) * 16;
         return static_cast<unsigned>(ctas < 1 ? 1 : (ctas > cap ? cap : ctas));
     };
-    // the split-K counters: zeroed per call (the scratch may have held another shape's layout); the gate/up
-    // kernel's last arrivers reset the cells they used, so the down kernel finds them zero as well
-    const int64_t cells = tg * (2 * I > H ? 2 * I : H) / 16;
-    cudaError_t err = cudaMemsetAsync(ws.cnt, 0, static_cast<size_t>(cells) * sizeof(int32_t), s);
-    if (err != cudaSuccess) return err;
     ShGemvArgs up{};
     up.w0 = static_cast<const __nv_bfloat16*>(m.gate_proj);
     up.w1 = static_cast<const __nv_bfloat16*>(m.up_proj);
@@ -214,7 +223,7 @@ cudaError_t shared_expert_launch(const DramaB200SharedExpert& m, const void* x, 
     up.part = ws.part;
     up.gu = ws.gu;
     shared_gemv_kernel<false><<<grid_for(tg * (2 * I / 16) * up.ksplit), kShThreads, 0, s>>>(up);
-    err = cudaGetLastError();
+    cudaError_t err = cudaGetLastError();
     if (err != cudaSuccess) return err;
     shared_act_kernel<<<static_cast<unsigned>(tokens), 256, 0, s>>>(
         static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(m.gate_weight), H, ws.gu, I, ws.h,

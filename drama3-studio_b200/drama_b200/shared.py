@@ -22,6 +22,7 @@ from . import _lib
 from .backend import _Workspace
 
 _SHARED_WORKSPACES = _Workspace()
+MAX_TOKENS = 4096  # rows per library call
 
 
 def _rowmajor(t: Tensor, name: str, shape: tuple[int, int]) -> Tensor:
@@ -85,6 +86,12 @@ class SharedExpertB200:
         elif out.shape != x.shape or out.dtype != torch.bfloat16 or not out.is_contiguous():
             raise ValueError("out must be a contiguous bfloat16 tensor shaped like the hidden rows")
         if tokens == 0:
+            return out
+        if tokens > MAX_TOKENS:  # rows are independent: run in chunks
+            for a in range(0, tokens, MAX_TOKENS):
+                b = min(tokens, a + MAX_TOKENS)
+                self._run(x[a:b], None if routed is None else routed[a:b],
+                          None if residual is None else residual[a:b], out[a:b])
             return out
         lib = _lib.library()
         nbytes = lib.dll.drama_b200_shared_expert_workspace_bytes(tokens, self.hidden, self.intermediate)
