@@ -169,7 +169,10 @@ int drama_b200_permute_routes(const void* ids, int ids_dtype, int64_t pairs, int
 size_t drama_b200_decode_workspace_bytes(int64_t tokens, int top_k, int hidden, int intermediate) {
     int sms = 0;
     if (sm_count_current(&sms)) sms = 148;
-    return decode_workspace_layout(tokens, top_k, hidden, intermediate, sms, 0, nullptr, nullptr);
+    const size_t decode = decode_workspace_layout(tokens, top_k, hidden, intermediate, sms, 0, nullptr, nullptr);
+    // the bf16 INT4 path runs on the W8A8 schedule and its scratch
+    const size_t rows = w8a8_workspace_layout(tokens, top_k, hidden, intermediate, nullptr, nullptr);
+    return decode > rows ? decode : rows;
 }
 
 size_t drama_b200_decode_status_offset(void) { return 0; }
@@ -229,6 +232,22 @@ int drama_b200_int4_decode(const DramaB200Int4Bank* bank, const void* x, int x_d
         b.w13_slot_stride < b.w13_row_stride * 2 * b.intermediate ||
         b.w2_slot_stride < b.w2_row_stride * b.hidden)
         return fail("INT4 weight strides are smaller than the bank geometry");
+    if (x_dtype == DRAMA_B200_BF16 && b.hidden % 256 == 0 && b.intermediate % 256 == 0) {
+        // bf16 rows: grouping + split-K GEMVs with the reference's per-element bf16 weights
+        if (tokens == 0) return 0;
+        int sms = 0;
+        if (sm_count_current(&sms)) return -1;
+        const size_t need = w8a8_workspace_layout(tokens, top_k, b.hidden, b.intermediate, nullptr, nullptr);
+        if (!workspace || workspace_bytes < need)
+            return fail("decode workspace too small: need %zu bytes, got %zu", need, workspace_bytes);
+        if (reinterpret_cast<uintptr_t>(workspace) & 255u) return fail("workspace must be 256-byte aligned");
+        W8a8Workspace ws{};
+        w8a8_workspace_layout(tokens, top_k, b.hidden, b.intermediate, static_cast<char*>(workspace), &ws);
+        const cudaError_t err = int4_rows_launch(b, x, tokens, top_k, ids, ids_dtype, weights, weights_dtype, out,
+                                                 x_dtype, pair_out, ws, sms, static_cast<cudaStream_t>(stream));
+        if (err != cudaSuccess) return fail("INT4 launch failed: %s", cudaGetErrorString(err));
+        return 0;
+    }
     DecodeArgs a{};
     a.format = 1;
     a.int4 = b;

@@ -245,6 +245,10 @@ struct W8a8Workspace {
 };
 size_t w8a8_workspace_layout(int64_t tokens, int top_k, int hidden, int intermediate, char* base,
                              W8a8Workspace* ws);
+// GPTQ W4A16 on the same schedule (bf16 hidden rows; scratch from w8a8_workspace_layout).
+cudaError_t int4_rows_launch(const DramaB200Int4Bank& bank, const void* x, int64_t tokens, int top_k,
+                             const void* ids, int ids_dtype, const void* weights, int weights_dtype, void* out,
+                             int out_dtype, float* pair_out, const W8a8Workspace& ws, int sm_count, cudaStream_t s);
 cudaError_t w8a8_decode_launch(const DramaB200W8a8Bank& bank, const void* x, int64_t tokens, int top_k,
                                const void* ids, int ids_dtype, const void* weights, int weights_dtype, void* out,
                                int out_dtype, float* pair_out, const W8a8Workspace& ws, int sm_count,

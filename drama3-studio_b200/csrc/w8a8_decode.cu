@@ -38,6 +38,7 @@
 // and feeds bytes 0-7 to the first k32 MMA and bytes 8-15 to the second. A and
 // B use the same permutation, so every product still pairs equal columns.
 #include "common.cuh"
+#include "grouped.cuh"
 #include "kernels.h"
 #include "bucket.cuh"
 
@@ -624,6 +625,280 @@ cudaError_t launch_mode(const DramaB200W8a8Bank& b, int64_t tokens, int top_k, v
     return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------------------
+// GPTQ W4A16 (mode 0) on the same schedule: grouping, split-K GEMVs with tokens
+// as the MMA N dimension, SwiGLU, down GEMV with the fused slot combine.
+// Weights are dequantised the way the reference's kernel does it
+// (quantized_kernels.py:139-147): w = bf16((code - zp) * scale) per element,
+// then bf16 MMAs with fp32 accumulation.
+//
+// Per 128-column block (one scale group) thread t of a quad takes the 32
+// columns 32t..32t+31 of its two weight rows (four int32 words) and of its
+// token row. A word's nibbles i and i + 4 become one bf16x2 pair (one shift and
+// one LOP3 with the 128.0 bias 0x4300 per pair, then code - zp exactly and one
+// rounding of the product with the scale); the token row is paired the same
+// way with byte permutes, so each product still joins equal columns.
+// ---------------------------------------------------------------------------
+struct I4Role {
+    const int32_t* w;       // [slots][n][k/8]
+    const void* s;          // [slots][n][k/128] bf16 or f16
+    const int32_t* z;       // [slots][n/8][k/128] or NULL (8)
+    int64_t w_slot, w_row, s_slot, s_row, z_slot, z_row;  // elements
+    int s_dtype;
+    int n, k;
+};
+
+struct I4GemvArgs {
+    I4Role role;
+    const int4* g_rec;
+    const int32_t* num_groups;
+    const __nv_bfloat16* act;  // up: x [T][k]; down: SwiGLU rows in gu [P][2I] (row stride act_stride)
+    int64_t act_stride;
+    int top_k;
+    int ksplit;
+    int32_t* cnt;
+    float4* part;
+    __nv_bfloat16* gu;         // up: [P][2I]
+    float* pair_out;           // down
+    const float* wts;
+    int32_t* cmb_cnt;
+    void* out;
+    int out_dtype;
+    int64_t tokens;
+};
+
+__device__ __forceinline__ float i4_scale(const void* p, int dtype, int64_t i) {
+    return dtype == DRAMA_B200_BF16 ? __bfloat162float(__ldg(static_cast<const __nv_bfloat16*>(p) + i))
+                                    : __half2float(__ldg(static_cast<const __half*>(p) + i));
+}
+
+__device__ __forceinline__ uint32_t bf2_sub(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+__device__ __forceinline__ uint32_t bf2_mul(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
+// bf16x2 (w_i, w_{i+4}) of nibbles i and i + 4 of word W: bf16((code - zp) * scale).
+// zb = bf16x2 (128 + zp) twice; BF16: sc2 = bf16x2 scale twice; else scf = the fp32 scale.
+template <bool BF16>
+__device__ __forceinline__ uint32_t int4_pair(uint32_t W, int i, uint32_t zb, uint32_t sc2, float scf) {
+    const uint32_t biased = ((W >> (4 * i)) & 0x000F000Fu) | 0x43004300u;  // 128 + code, exact in bf16
+    const uint32_t level = bf2_sub(biased, zb);                             // code - zp, exact
+    if constexpr (BF16) {
+        return bf2_mul(level, sc2);  // exact product rounded once, as in fp32 then .to(bf16)
+    } else {
+        const float lo = __fmul_rn(__uint_as_float(level << 16), scf);
+        const float hi = __fmul_rn(__uint_as_float(level & 0xffff0000u), scf);
+        const __nv_bfloat162 p = __floats2bfloat162_rn(lo, hi);
+        return *reinterpret_cast<const uint32_t*>(&p);
+    }
+}
+
+template <bool DOWN, bool BF16>
+__global__ void __launch_bounds__(kW8GemvThreads) int4_gemv_kernel(I4GemvArgs a) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const int warps_total = gridDim.x * (kW8GemvThreads / 32);
+    const int groups = __ldg(a.num_groups);
+    const I4Role& role = a.role;
+    const int tiles = role.n / 16, blocks_per = role.k / 128 / a.ksplit;
+    const int tasks = groups * tiles * a.ksplit;
+    const uint64_t pol = policy_evict_first();
+    for (int task = blockIdx.x * (kW8GemvThreads / 32) + (threadIdx.x >> 5); task < tasks; task += warps_total) {
+        const int cell = task / a.ksplit, kpart = task - cell * a.ksplit;
+        const int grp = cell / tiles, tile = cell - grp * tiles;
+        const int4 head = __ldg(a.g_rec + 2 * grp);
+        const int4 ids4 = __ldg(a.g_rec + 2 * grp + 1);
+        const int slot = head.x, count = head.z;
+        const int my_pair = g < count ? group_pair(ids4, g) : -1;
+        const __nv_bfloat16* arow =
+            my_pair >= 0 ? a.act + static_cast<int64_t>(DOWN ? my_pair : my_pair / a.top_k) * a.act_stride
+                         : nullptr;
+        const int r0 = tile * 16 + g, r1 = r0 + 8;
+        const int32_t* w0 = role.w + slot * role.w_slot + static_cast<int64_t>(r0) * role.w_row;
+        const int32_t* w1 = w0 + 8 * role.w_row;
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        const int b0 = kpart * blocks_per;
+        for (int kb = b0; kb < b0 + blocks_per; kb += 2) {  // two 128-column blocks per load batch
+            uint4 q0[2], q1[2], xr[2][4];
+            float s0[2], s1[2];
+            uint32_t z0[2], z1[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const int blk = kb + u;
+                q0[u] = ld_stream_v4(w0 + blk * 16 + 4 * t, pol);
+                q1[u] = ld_stream_v4(w1 + blk * 16 + 4 * t, pol);
+#pragma unroll
+                for (int v = 0; v < 4; ++v)
+                    xr[u][v] = arow ? __ldg(reinterpret_cast<const uint4*>(arow + blk * 128 + 32 * t) + v)
+                                    : make_uint4(0u, 0u, 0u, 0u);
+                const int64_t so = slot * role.s_slot + blk;
+                s0[u] = i4_scale(role.s, role.s_dtype, so + static_cast<int64_t>(r0) * role.s_row);
+                s1[u] = i4_scale(role.s, role.s_dtype, so + static_cast<int64_t>(r1) * role.s_row);
+                z0[u] = z1[u] = 8u;
+                if (role.z) {
+                    const int32_t* zp = role.z + slot * role.z_slot + blk;
+                    z0[u] = (static_cast<uint32_t>(__ldg(zp + (r0 >> 3) * role.z_row)) >> (4 * (r0 & 7))) & 15u;
+                    z1[u] = (static_cast<uint32_t>(__ldg(zp + (r1 >> 3) * role.z_row)) >> (4 * (r1 & 7))) & 15u;
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const uint32_t zb0 = (0x4300u + z0[u]) * 0x10001u, zb1 = (0x4300u + z1[u]) * 0x10001u;
+                const __nv_bfloat162 sp0 = __floats2bfloat162_rn(s0[u], s0[u]);
+                const __nv_bfloat162 sp1 = __floats2bfloat162_rn(s1[u], s1[u]);
+                const uint32_t sc0 = *reinterpret_cast<const uint32_t*>(&sp0);
+                const uint32_t sc1 = *reinterpret_cast<const uint32_t*>(&sp1);
+                const uint32_t W0[4] = {q0[u].x, q0[u].y, q0[u].z, q0[u].w};
+                const uint32_t W1[4] = {q1[u].x, q1[u].y, q1[u].z, q1[u].w};
+                const uint32_t X[16] = {xr[u][0].x, xr[u][0].y, xr[u][0].z, xr[u][0].w, xr[u][1].x, xr[u][1].y,
+                                        xr[u][1].z, xr[u][1].w, xr[u][2].x, xr[u][2].y, xr[u][2].z, xr[u][2].w,
+                                        xr[u][3].x, xr[u][3].y, xr[u][3].z, xr[u][3].w};
+#pragma unroll
+                for (int w = 0; w < 4; ++w) {  // word w: columns 8w..8w+7 of this thread's 32
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {  // pairs (2h, 2h+4) and (2h+1, 2h+5)
+                        const uint32_t A[4] = {int4_pair<BF16>(W0[w], 2 * h, zb0, sc0, s0[u]),
+                                               int4_pair<BF16>(W1[w], 2 * h, zb1, sc1, s1[u]),
+                                               int4_pair<BF16>(W0[w], 2 * h + 1, zb0, sc0, s0[u]),
+                                               int4_pair<BF16>(W1[w], 2 * h + 1, zb1, sc1, s1[u])};
+                        // token columns (2h, 2h+4) and (2h+1, 2h+5): low or high halves of x words 4w+h, 4w+h+2
+                        const uint32_t xa = X[4 * w + h], xb = X[4 * w + h + 2];
+                        mma_bf16_16816(acc, A, __byte_perm(xa, xb, 0x5410u), __byte_perm(xa, xb, 0x7632u));
+                    }
+                }
+            }
+        }
+        if (a.ksplit > 1) {
+            __stcg(a.part + static_cast<int64_t>(task) * 32 + lane, make_float4(acc[0], acc[1], acc[2], acc[3]));
+            __syncwarp();
+            int old = 0;
+            if (lane == 0) {
+                w8_fence();
+                old = atomicAdd(a.cnt + cell, 1);
+            }
+            old = __shfl_sync(0xffffffffu, old, 0);
+            if (old != a.ksplit - 1) continue;
+            w8_fence();
+            acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+            for (int q = 0; q < a.ksplit; ++q) {  // part order: independent of arrival order
+                const float4 v = __ldcg(a.part + (static_cast<int64_t>(cell) * a.ksplit + q) * 32 + lane);
+                acc[0] += v.x;
+                acc[1] += v.y;
+                acc[2] += v.z;
+                acc[3] += v.w;
+            }
+        }
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+            const int col = 2 * t + c;
+            if (col >= count) continue;
+            const int pair = group_pair(ids4, col);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int row = h ? r1 : r0;
+                const float v = __bfloat162float(__float2bfloat16_rn(acc[2 * h + c]));  // projection in bf16
+                if constexpr (DOWN)
+                    a.pair_out[static_cast<int64_t>(pair) * role.n + row] = __fmul_rn(v, __ldg(a.wts + pair));
+                else
+                    a.gu[static_cast<int64_t>(pair) * role.n + row] = __float2bfloat16_rn(v);
+            }
+        }
+        if constexpr (DOWN) {
+            if (!a.out) continue;
+            __syncwarp();
+            int old = 0;
+            if (lane == 0) {
+                w8_fence();
+                old = atomicAdd(a.cmb_cnt + tile, 1);
+            }
+            old = __shfl_sync(0xffffffffu, old, 0);
+            if (old != groups - 1) continue;
+            w8_fence();
+            const int n = role.n;
+            for (int i = lane; i < a.tokens * 16; i += 32) {
+                const int64_t tok = i >> 4;
+                const int row = tile * 16 + (i & 15);
+                float sum = 0.0f;
+                for (int sl = 0; sl < a.top_k; ++sl)
+                    sum = __fadd_rn(sum, __ldcg(a.pair_out + (tok * a.top_k + sl) * n + row));
+                store_any(a.out, a.out_dtype, tok * n + row, sum);
+            }
+        }
+    }
+}
+
+// SwiGLU in place: gate half of each gu row <- bf16(bf16(silu(gate)) * up).
+__global__ void __launch_bounds__(256) int4_act_kernel(__nv_bfloat16* gu, int I) {
+    __nv_bfloat16* row = gu + static_cast<int64_t>(blockIdx.x) * 2 * I;
+    for (int j = threadIdx.x; j < I; j += blockDim.x) {
+        const float gt = __bfloat162float(row[j]);
+        const float up = __bfloat162float(row[I + j]);
+        const float act = __bfloat162float(__float2bfloat16_rn(gt / (1.0f + expf(-gt))));
+        row[j] = __float2bfloat16_rn(act * up);
+    }
+}
+
+int split_blocks(int64_t cells, int blocks) {
+    for (int ks = blocks / 2; ks > 1; --ks)
+        if (cells * ks <= kW8TargetWarps && blocks % (ks * 2) == 0) return ks;
+    return 1;
+}
+
+template <bool BF16>
+cudaError_t int4_launch_fmt(const DramaB200Int4Bank& b, const void* x, int64_t tokens, int top_k, void* out,
+                            int out_dtype, float* pair_out, const W8a8Workspace& ws, int sm_count, cudaStream_t s) {
+    const int64_t P = tokens * top_k;
+    const int H = b.hidden, I = b.intermediate;
+    const int64_t gmax = max_groups(P);
+    auto grid_for = [&](int64_t tasks) {
+        const int64_t ctas = (tasks + kW8GemvThreads / 32 - 1) / (kW8GemvThreads / 32);
+        const int64_t cap = static_cast<int64_t>(sm_count) * 16;
+        return static_cast<unsigned>(ctas < 1 ? 1 : (ctas > cap ? cap : ctas));
+    };
+    I4GemvArgs up{};
+    up.role = I4Role{b.w13, b.w13_scale, b.w13_zeros, b.w13_slot_stride, b.w13_row_stride, b.w13_scale_slot_stride,
+                     b.w13_scale_row_stride, b.w13_zeros_slot_stride, b.w13_zeros_row_stride, b.scale_dtype, 2 * I, H};
+    up.g_rec = ws.g_rec;
+    up.num_groups = ws.num_groups;
+    up.act = static_cast<const __nv_bfloat16*>(x);
+    up.act_stride = H;
+    up.top_k = top_k;
+    up.ksplit = split_blocks(gmax * (2 * I / 16), H / 128);
+    up.cnt = ws.up_cnt;
+    up.part = reinterpret_cast<float4*>(ws.part);
+    up.gu = ws.up;
+    int4_gemv_kernel<false, BF16><<<grid_for(gmax * (2 * I / 16) * up.ksplit), kW8GemvThreads, 0, s>>>(up);
+    cudaError_t err = cudaGetLastError();
+    if (err != cudaSuccess) return err;
+    int4_act_kernel<<<static_cast<unsigned>(P), 256, 0, s>>>(ws.up, I);
+    err = cudaGetLastError();
+    if (err != cudaSuccess) return err;
+    I4GemvArgs dn{};
+    dn.role = I4Role{b.w2, b.w2_scale, b.w2_zeros, b.w2_slot_stride, b.w2_row_stride, b.w2_scale_slot_stride,
+                     b.w2_scale_row_stride, b.w2_zeros_slot_stride, b.w2_zeros_row_stride, b.scale_dtype, H, I};
+    dn.g_rec = ws.g_rec;
+    dn.num_groups = ws.num_groups;
+    dn.act = ws.up;
+    dn.act_stride = 2 * I;
+    dn.top_k = top_k;
+    dn.ksplit = split_blocks(gmax * (H / 16), I / 128);
+    dn.cnt = ws.dn_cnt;
+    dn.part = reinterpret_cast<float4*>(ws.part);
+    dn.pair_out = pair_out;
+    dn.wts = ws.wts;
+    dn.cmb_cnt = ws.cmb_cnt;
+    dn.out = out;
+    dn.out_dtype = out_dtype;
+    dn.tokens = tokens;
+    int4_gemv_kernel<true, BF16><<<grid_for(gmax * (H / 16) * dn.ksplit), kW8GemvThreads, 0, s>>>(dn);
+    return cudaGetLastError();
+}
+
 }  // namespace
 
 size_t w8a8_workspace_layout(int64_t tokens, int top_k, int hidden, int intermediate, char* base,
@@ -689,6 +964,28 @@ cudaError_t w8a8_decode_launch(const DramaB200W8a8Bank& bank, const void* x, int
         case 2: return launch_mode<2>(bank, tokens, top_k, out, out_dtype, po, ws, sm_count, s);
         default: return launch_mode<3>(bank, tokens, top_k, out, out_dtype, po, ws, sm_count, s);
     }
+}
+
+cudaError_t int4_rows_launch(const DramaB200Int4Bank& bank, const void* x, int64_t tokens, int top_k,
+                             const void* ids, int ids_dtype, const void* weights, int weights_dtype, void* out,
+                             int out_dtype, float* pair_out, const W8a8Workspace& ws, int sm_count, cudaStream_t s) {
+    float* po = pair_out ? pair_out : ws.pair_out;
+    W8PrepArgs pa{ids, ids_dtype, weights, weights_dtype, static_cast<const __nv_bfloat16*>(x), tokens * top_k,
+                  bank.slots, bank.hidden, bank.intermediate, po, ws};
+    static bool configured = false;  // benign race: identical values
+    if (!configured) {
+        const cudaError_t err = cudaFuncSetAttribute(w8a8_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                     200 * 1024);
+        if (err != cudaSuccess) return err;
+        configured = true;
+    }
+    // CTA 0 alone: the grouping (W4A16 keeps the activations in bf16)
+    w8a8_prep_kernel<<<1, 1024, static_cast<size_t>(34) * bank.slots * sizeof(int), s>>>(pa);
+    cudaError_t err = cudaGetLastError();
+    if (err != cudaSuccess) return err;
+    return bank.scale_dtype == DRAMA_B200_BF16
+               ? int4_launch_fmt<true>(bank, x, tokens, top_k, out, out_dtype, po, ws, sm_count, s)
+               : int4_launch_fmt<false>(bank, x, tokens, top_k, out, out_dtype, po, ws, sm_count, s);
 }
 
 }  // namespace drama
