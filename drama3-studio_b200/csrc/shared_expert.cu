@@ -8,7 +8,8 @@
 //   t = bf16(routed + shared);  out = bf16(after_mixer + t)
 // (routed and after_mixer are optional; without them out = shared or t.)
 //
-// Launches: gate/up GEMV -> per-token SwiGLU and gate scalar -> down GEMV whose
+// Launches (chained by programmatic dependent launch): gate/up GEMV -> per-token
+// SwiGLU and gate scalar -> down GEMV whose
 // epilogue applies the gate, the routed sum and the residual. The GEMVs stream
 // the dense bf16 weights once per group of <= 8 tokens through
 // mma.m16n8k16 bf16 fragments (tokens as N), split K across warps when the
@@ -48,6 +49,8 @@ struct ShGemvArgs {
 
 template <bool DOWN>
 __global__ void __launch_bounds__(kShThreads) shared_gemv_kernel(ShGemvArgs a) {
+    grid_launch_dependents();  // programmatic dependent launch
+    grid_dependency_wait();
     const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const int warps_total = gridDim.x * (kShThreads / 32);
     const int tiles = a.n / 16;
@@ -131,6 +134,8 @@ __global__ void __launch_bounds__(kShThreads) shared_gemv_kernel(ShGemvArgs a) {
 __global__ void __launch_bounds__(256) shared_act_kernel(const __nv_bfloat16* x, const __nv_bfloat16* gate_w, int H,
                                                           const __nv_bfloat16* gu, int I, __nv_bfloat16* h,
                                                           float* gate_s) {
+    grid_launch_dependents();  // programmatic dependent launch
+    grid_dependency_wait();
     __shared__ float s_red[8];
     const int64_t tok = blockIdx.x;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -222,13 +227,12 @@ cudaError_t shared_expert_launch(const DramaB200SharedExpert& m, const void* x, 
     up.cnt = ws.cnt;
     up.part = ws.part;
     up.gu = ws.gu;
-    shared_gemv_kernel<false><<<grid_for(tg * (2 * I / 16) * up.ksplit), kShThreads, 0, s>>>(up);
-    cudaError_t err = cudaGetLastError();
+    cudaError_t err = launch_pdl(shared_gemv_kernel<false>, dim3(grid_for(tg * (2 * I / 16) * up.ksplit)),
+                                 dim3(kShThreads), 0, s, up);
     if (err != cudaSuccess) return err;
-    shared_act_kernel<<<static_cast<unsigned>(tokens), 256, 0, s>>>(
-        static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(m.gate_weight), H, ws.gu, I, ws.h,
-        ws.gate_s);
-    err = cudaGetLastError();
+    err = launch_pdl(shared_act_kernel, dim3(static_cast<unsigned>(tokens)), dim3(256), 0, s,
+                     static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(m.gate_weight), H,
+                     static_cast<const __nv_bfloat16*>(ws.gu), I, ws.h, ws.gate_s);
     if (err != cudaSuccess) return err;
     ShGemvArgs dn{};
     dn.w0 = static_cast<const __nv_bfloat16*>(m.down_proj);
@@ -246,8 +250,8 @@ cudaError_t shared_expert_launch(const DramaB200SharedExpert& m, const void* x, 
     dn.routed = static_cast<const __nv_bfloat16*>(routed);
     dn.residual = static_cast<const __nv_bfloat16*>(residual);
     dn.out = static_cast<__nv_bfloat16*>(out);
-    shared_gemv_kernel<true><<<grid_for(tg * (H / 16) * dn.ksplit), kShThreads, 0, s>>>(dn);
-    return cudaGetLastError();
+    return launch_pdl(shared_gemv_kernel<true>, dim3(grid_for(tg * (H / 16) * dn.ksplit)), dim3(kShThreads), 0, s,
+                      dn);
 }
 
 }  // namespace drama

@@ -14,7 +14,7 @@
 // The rotation runs as four radix-4 stages in float64 and is rounded once,
 // which equals the correctly rounded product for all practical inputs.
 //
-// Launches (one stream, in order):
+// Launches (one stream, in order, chained by programmatic dependent launch):
 //   prep   : CTA 0 groups the route slots into expert groups of <= 8 pairs
 //            (one warp with match_any for <= 32 pairs, else a stable bucket;
 //            a column's result does not depend on its group, so any grouping
@@ -223,6 +223,8 @@ __device__ void w8a8_prep_tail(const W8PrepArgs& a, int groups, int dropped) {
 }
 
 __global__ void __launch_bounds__(1024) w8a8_prep_kernel(W8PrepArgs a) {
+    grid_launch_dependents();  // programmatic dependent launch: the next kernel may start its launch
+    grid_dependency_wait();    // the previous kernel's results are visible from here
     extern __shared__ __align__(16) unsigned char smem_w8prep[];
     if (blockIdx.x > 0) {  // rotate token row blockIdx.x - 1
         double* s_v = reinterpret_cast<double*>(smem_w8prep);
@@ -325,6 +327,8 @@ __global__ void __launch_bounds__(1024) w8a8_prep_kernel(W8PrepArgs a) {
 
 // SwiGLU rows -> int8 (one CTA per pair)
 __global__ void __launch_bounds__(1024) w8a8_act_kernel(const __nv_bfloat16* up, int I, int8_t* hq, float* hs) {
+    grid_launch_dependents();  // programmatic dependent launch: the next kernel may start its launch
+    grid_dependency_wait();    // the previous kernel's results are visible from here
     extern __shared__ __align__(16) unsigned char smem_w8act[];
     double* s_v = reinterpret_cast<double*>(smem_w8act);
     float* s_row = reinterpret_cast<float*>(s_v + blockDim.x);
@@ -442,6 +446,8 @@ __device__ __forceinline__ float channel_scale(const W8Role& r, int slot, int ro
 // task's span count allows, so a batch-1 task is a single round trip).
 template <int MODE, bool DOWN, int U>
 __global__ void __launch_bounds__(kW8GemvThreads) w8a8_gemv_kernel(W8GemvArgs a) {
+    grid_launch_dependents();  // programmatic dependent launch: the next kernel may start its launch
+    grid_dependency_wait();    // the previous kernel's results are visible from here
     const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const int warps_total = gridDim.x * (kW8GemvThreads / 32);
     const int groups = __ldg(a.num_groups);
@@ -592,14 +598,13 @@ cudaError_t launch_mode(const DramaB200W8a8Bank& b, int64_t tokens, int top_k, v
     up.cnt = ws.up_cnt;
     up.part = ws.part;
     up.up_out = ws.up;
-    if ((H / 64 / up.ksplit) % 8 == 0)
-        w8a8_gemv_kernel<MODE, false, 8><<<grid_for(gmax * (2 * I / 16) * up.ksplit), kW8GemvThreads, 0, s>>>(up);
-    else
-        w8a8_gemv_kernel<MODE, false, 4><<<grid_for(gmax * (2 * I / 16) * up.ksplit), kW8GemvThreads, 0, s>>>(up);
-    cudaError_t err = cudaGetLastError();
+    const dim3 up_grid(grid_for(gmax * (2 * I / 16) * up.ksplit));
+    cudaError_t err = (H / 64 / up.ksplit) % 8 == 0
+                          ? launch_pdl(w8a8_gemv_kernel<MODE, false, 8>, up_grid, dim3(kW8GemvThreads), 0, s, up)
+                          : launch_pdl(w8a8_gemv_kernel<MODE, false, 4>, up_grid, dim3(kW8GemvThreads), 0, s, up);
     if (err != cudaSuccess) return err;
-    w8a8_act_kernel<<<static_cast<unsigned>(P), rot_threads(I), rot_smem(I), s>>>(ws.up, I, ws.hq, ws.hs);
-    err = cudaGetLastError();
+    err = launch_pdl(w8a8_act_kernel, dim3(static_cast<unsigned>(P)), dim3(rot_threads(I)), rot_smem(I), s, ws.up, I,
+                     ws.hq, ws.hs);
     if (err != cudaSuccess) return err;
     W8GemvArgs dn{};
     dn.role = W8Role{static_cast<const uint8_t*>(b.w2), static_cast<const uint8_t*>(b.w2_scale), b.w2_slot_stride,
@@ -618,11 +623,10 @@ cudaError_t launch_mode(const DramaB200W8a8Bank& b, int64_t tokens, int top_k, v
     dn.out = out;
     dn.out_dtype = out_dtype;
     dn.tokens = tokens;
-    if ((I / 64 / dn.ksplit) % 8 == 0)
-        w8a8_gemv_kernel<MODE, true, 8><<<grid_for(gmax * (H / 16) * dn.ksplit), kW8GemvThreads, 0, s>>>(dn);
-    else
-        w8a8_gemv_kernel<MODE, true, 4><<<grid_for(gmax * (H / 16) * dn.ksplit), kW8GemvThreads, 0, s>>>(dn);
-    return cudaGetLastError();
+    const dim3 dn_grid(grid_for(gmax * (H / 16) * dn.ksplit));
+    return (I / 64 / dn.ksplit) % 8 == 0
+               ? launch_pdl(w8a8_gemv_kernel<MODE, true, 8>, dn_grid, dim3(kW8GemvThreads), 0, s, dn)
+               : launch_pdl(w8a8_gemv_kernel<MODE, true, 4>, dn_grid, dim3(kW8GemvThreads), 0, s, dn);
 }
 
 // ---------------------------------------------------------------------------
@@ -701,6 +705,8 @@ __device__ __forceinline__ uint32_t int4_pair(uint32_t W, int i, uint32_t zb, ui
 
 template <bool DOWN, bool BF16>
 __global__ void __launch_bounds__(kW8GemvThreads) int4_gemv_kernel(I4GemvArgs a) {
+    grid_launch_dependents();  // programmatic dependent launch: the next kernel may start its launch
+    grid_dependency_wait();    // the previous kernel's results are visible from here
     const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const int warps_total = gridDim.x * (kW8GemvThreads / 32);
     const int groups = __ldg(a.num_groups);
@@ -834,6 +840,8 @@ __global__ void __launch_bounds__(kW8GemvThreads) int4_gemv_kernel(I4GemvArgs a)
 
 // SwiGLU in place: gate half of each gu row <- bf16(bf16(silu(gate)) * up).
 __global__ void __launch_bounds__(256) int4_act_kernel(__nv_bfloat16* gu, int I) {
+    grid_launch_dependents();  // programmatic dependent launch: the next kernel may start its launch
+    grid_dependency_wait();    // the previous kernel's results are visible from here
     __nv_bfloat16* row = gu + static_cast<int64_t>(blockIdx.x) * 2 * I;
     for (int j = threadIdx.x; j < I; j += blockDim.x) {
         const float gt = __bfloat162float(row[j]);
@@ -872,11 +880,10 @@ cudaError_t int4_launch_fmt(const DramaB200Int4Bank& b, const void* x, int64_t t
     up.cnt = ws.up_cnt;
     up.part = reinterpret_cast<float4*>(ws.part);
     up.gu = ws.up;
-    int4_gemv_kernel<false, BF16><<<grid_for(gmax * (2 * I / 16) * up.ksplit), kW8GemvThreads, 0, s>>>(up);
-    cudaError_t err = cudaGetLastError();
+    cudaError_t err = launch_pdl(int4_gemv_kernel<false, BF16>, dim3(grid_for(gmax * (2 * I / 16) * up.ksplit)),
+                                 dim3(kW8GemvThreads), 0, s, up);
     if (err != cudaSuccess) return err;
-    int4_act_kernel<<<static_cast<unsigned>(P), 256, 0, s>>>(ws.up, I);
-    err = cudaGetLastError();
+    err = launch_pdl(int4_act_kernel, dim3(static_cast<unsigned>(P)), dim3(256), 0, s, ws.up, I);
     if (err != cudaSuccess) return err;
     I4GemvArgs dn{};
     dn.role = I4Role{b.w2, b.w2_scale, b.w2_zeros, b.w2_slot_stride, b.w2_row_stride, b.w2_scale_slot_stride,
@@ -895,8 +902,8 @@ cudaError_t int4_launch_fmt(const DramaB200Int4Bank& b, const void* x, int64_t t
     dn.out = out;
     dn.out_dtype = out_dtype;
     dn.tokens = tokens;
-    int4_gemv_kernel<true, BF16><<<grid_for(gmax * (H / 16) * dn.ksplit), kW8GemvThreads, 0, s>>>(dn);
-    return cudaGetLastError();
+    return launch_pdl(int4_gemv_kernel<true, BF16>, dim3(grid_for(gmax * (H / 16) * dn.ksplit)), dim3(kW8GemvThreads),
+                      0, s, dn);
 }
 
 }  // namespace
@@ -956,8 +963,7 @@ cudaError_t w8a8_decode_launch(const DramaB200W8a8Bank& bank, const void* x, int
         if (err != cudaSuccess) return err;
         configured = true;
     }
-    w8a8_prep_kernel<<<static_cast<unsigned>(1 + tokens), 1024, smem, s>>>(pa);
-    cudaError_t err = cudaGetLastError();
+    cudaError_t err = launch_pdl(w8a8_prep_kernel, dim3(static_cast<unsigned>(1 + tokens)), dim3(1024), smem, s, pa);
     if (err != cudaSuccess) return err;
     switch (bank.mode) {
         case 1: return launch_mode<1>(bank, tokens, top_k, out, out_dtype, po, ws, sm_count, s);
@@ -980,8 +986,8 @@ cudaError_t int4_rows_launch(const DramaB200Int4Bank& bank, const void* x, int64
         configured = true;
     }
     // CTA 0 alone: the grouping (W4A16 keeps the activations in bf16)
-    w8a8_prep_kernel<<<1, 1024, static_cast<size_t>(34) * bank.slots * sizeof(int), s>>>(pa);
-    cudaError_t err = cudaGetLastError();
+    cudaError_t err = launch_pdl(w8a8_prep_kernel, dim3(1), dim3(1024), static_cast<size_t>(34) * bank.slots * sizeof(int),
+                                 s, pa);
     if (err != cudaSuccess) return err;
     return bank.scale_dtype == DRAMA_B200_BF16
                ? int4_launch_fmt<true>(bank, x, tokens, top_k, out, out_dtype, po, ws, sm_count, s)
