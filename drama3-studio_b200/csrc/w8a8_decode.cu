@@ -659,9 +659,7 @@ struct I4GemvArgs {
     const __nv_bfloat16* act;  // up: x [T][k]; down: SwiGLU rows in gu [P][2I] (row stride act_stride)
     int64_t act_stride;
     int top_k;
-    int ksplit;
-    int32_t* cnt;
-    float4* part;
+    int ksplit;                // warps per team (K shares per tile)
     __nv_bfloat16* gu;         // up: [P][2I]
     float* pair_out;           // down
     const float* wts;
@@ -703,19 +701,186 @@ __device__ __forceinline__ uint32_t int4_pair(uint32_t W, int i, uint32_t zb, ui
     }
 }
 
+// One 128-column block of one warp: the raw loads, issued one block ahead of
+// the MMAs that consume them.
+struct I4Block {
+    uint4 q0, q1;    // the two weight rows' 32 nibbles
+    uint4 x[4];      // the token row's 32 bf16
+    float s0, s1;    // scales
+    uint32_t z0, z1; // zero points
+};
+
+__device__ __forceinline__ void i4_load(I4Block& b, const I4Role& role, const int32_t* w0, const int32_t* w1,
+                                        const __nv_bfloat16* arow, int slot, int r0, int r1, int blk, int t,
+                                        uint64_t pol) {
+    b.q0 = ld_stream_v4(w0 + blk * 16 + 4 * t, pol);
+    b.q1 = ld_stream_v4(w1 + blk * 16 + 4 * t, pol);
+#pragma unroll
+    for (int v = 0; v < 4; ++v)
+        b.x[v] = arow ? __ldg(reinterpret_cast<const uint4*>(arow + blk * 128 + 32 * t) + v) : make_uint4(0u, 0u, 0u, 0u);
+    const int64_t so = slot * role.s_slot + blk;
+    b.s0 = i4_scale(role.s, role.s_dtype, so + static_cast<int64_t>(r0) * role.s_row);
+    b.s1 = i4_scale(role.s, role.s_dtype, so + static_cast<int64_t>(r1) * role.s_row);
+    b.z0 = b.z1 = 8u;
+    if (role.z) {
+        const int32_t* zp = role.z + slot * role.z_slot + blk;
+        b.z0 = (static_cast<uint32_t>(__ldg(zp + (r0 >> 3) * role.z_row)) >> (4 * (r0 & 7))) & 15u;
+        b.z1 = (static_cast<uint32_t>(__ldg(zp + (r1 >> 3) * role.z_row)) >> (4 * (r1 & 7))) & 15u;
+    }
+}
+
+template <bool BF16>
+__device__ __forceinline__ void i4_mma(const I4Block& b, float (&acc)[4]) {
+    const uint32_t zb0 = (0x4300u + b.z0) * 0x10001u, zb1 = (0x4300u + b.z1) * 0x10001u;
+    const __nv_bfloat162 sp0 = __floats2bfloat162_rn(b.s0, b.s0);
+    const __nv_bfloat162 sp1 = __floats2bfloat162_rn(b.s1, b.s1);
+    const uint32_t sc0 = *reinterpret_cast<const uint32_t*>(&sp0);
+    const uint32_t sc1 = *reinterpret_cast<const uint32_t*>(&sp1);
+    const uint32_t W0[4] = {b.q0.x, b.q0.y, b.q0.z, b.q0.w};
+    const uint32_t W1[4] = {b.q1.x, b.q1.y, b.q1.z, b.q1.w};
+    const uint32_t X[16] = {b.x[0].x, b.x[0].y, b.x[0].z, b.x[0].w, b.x[1].x, b.x[1].y, b.x[1].z, b.x[1].w,
+                            b.x[2].x, b.x[2].y, b.x[2].z, b.x[2].w, b.x[3].x, b.x[3].y, b.x[3].z, b.x[3].w};
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {  // word w: columns 8w..8w+7 of this thread's 32
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {  // pairs (2h, 2h+4) and (2h+1, 2h+5)
+            const uint32_t A[4] = {int4_pair<BF16>(W0[w], 2 * h, zb0, sc0, b.s0),
+                                   int4_pair<BF16>(W1[w], 2 * h, zb1, sc1, b.s1),
+                                   int4_pair<BF16>(W0[w], 2 * h + 1, zb0, sc0, b.s0),
+                                   int4_pair<BF16>(W1[w], 2 * h + 1, zb1, sc1, b.s1)};
+            // token columns (2h, 2h+4) and (2h+1, 2h+5): low or high halves of x words 4w+h, 4w+h+2
+            const uint32_t xa = X[4 * w + h], xb = X[4 * w + h + 2];
+            mma_bf16_16816(acc, A, __byte_perm(xa, xb, 0x5410u), __byte_perm(xa, xb, 0x7632u));
+        }
+    }
+}
+
+// Epilogue of one cell (one warp): bf16 projections to gu (up) or weighted
+// fp32 partials (down), then, for the last cell of a row tile, the slot sum.
+template <bool DOWN>
+__device__ __forceinline__ void i4_epilogue(const I4GemvArgs& a, const float (&acc)[4], const int4& ids4, int count,
+                                            int tile, int r0, int r1, int groups, int lane, int t) {
+    const I4Role& role = a.role;
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+        const int col = 2 * t + c;
+        if (col >= count) continue;
+        const int pair = group_pair(ids4, col);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int row = h ? r1 : r0;
+            const float v = __bfloat162float(__float2bfloat16_rn(acc[2 * h + c]));  // projection in bf16
+            if constexpr (DOWN)
+                a.pair_out[static_cast<int64_t>(pair) * role.n + row] = __fmul_rn(v, __ldg(a.wts + pair));
+            else
+                a.gu[static_cast<int64_t>(pair) * role.n + row] = __float2bfloat16_rn(v);
+        }
+    }
+    if constexpr (DOWN) {
+        if (a.out) {
+            // the last cell of this row tile sums its rows' route slots in slot order
+            __syncwarp();
+            int old = 0;
+            if (lane == 0) {
+                w8_fence();
+                old = atomicAdd(a.cmb_cnt + tile, 1);
+            }
+            old = __shfl_sync(0xffffffffu, old, 0);
+            if (old == groups - 1) {
+                w8_fence();
+                const int n = role.n;
+                for (int i = lane; i < a.tokens * 16; i += 32) {
+                    const int64_t tok = i >> 4;
+                    const int row = tile * 16 + (i & 15);
+                    float sum = 0.0f;
+                    for (int sl = 0; sl < a.top_k; ++sl)
+                        sum = __fadd_rn(sum, __ldcg(a.pair_out + (tok * a.top_k + sl) * n + row));
+                    store_any(a.out, a.out_dtype, tok * n + row, sum);
+                }
+            }
+        }
+    }
+}
+
+// The warps of a CTA form teams of KS (a.ksplit) warps; a team owns one cell
+// (group, 16-row tile) at a time and warp q of the team takes the q-th
+// contiguous share of the K blocks, streaming it with the next block's loads in
+// flight while the current one is multiplied. The shares are added in warp
+// order through shared memory, so no global fence or atomic reduces a tile.
+// Used when there are few cells (batch 1): one team of up to 8 warps per CTA.
 template <bool DOWN, bool BF16>
-__global__ void __launch_bounds__(kW8GemvThreads) int4_gemv_kernel(I4GemvArgs a) {
+__global__ void __launch_bounds__(256) int4_gemv_kernel(I4GemvArgs a) {
+    grid_launch_dependents();  // programmatic dependent launch: the next kernel may start its launch
+    grid_dependency_wait();    // the previous kernel's results are visible from here
+    __shared__ float4 s_part[8][32];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const int KS = a.ksplit, teams = (blockDim.x >> 5) / KS, team = warp / KS, q = warp - team * KS;
+    const int groups = __ldg(a.num_groups);
+    const I4Role& role = a.role;
+    const int tiles = role.n / 16, blocks = role.k / 128;
+    const int per = blocks / KS, b_lo = q * per, b_hi = b_lo + per;
+    const uint64_t pol = policy_evict_first();
+    const int total = groups * tiles;
+    // every warp runs the same number of rounds, so the barriers below are uniform
+    for (int base = blockIdx.x * teams; base < total; base += gridDim.x * teams) {
+        const int cell = base + team;
+        const bool live = cell < total;
+        const int grp = live ? cell / tiles : 0, tile = live ? cell - grp * tiles : 0;
+        const int4 head = __ldg(a.g_rec + 2 * grp);
+        const int4 ids4 = __ldg(a.g_rec + 2 * grp + 1);
+        const int slot = head.x, count = live ? head.z : 0;
+        const int my_pair = g < count ? group_pair(ids4, g) : -1;
+        const __nv_bfloat16* arow =
+            my_pair >= 0 ? a.act + static_cast<int64_t>(DOWN ? my_pair : my_pair / a.top_k) * a.act_stride
+                         : nullptr;
+        const int r0 = tile * 16 + g, r1 = r0 + 8;
+        const int32_t* w0 = role.w + slot * role.w_slot + static_cast<int64_t>(r0) * role.w_row;
+        const int32_t* w1 = w0 + 8 * role.w_row;
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        if (live) {
+            I4Block cur, nxt;
+            i4_load(cur, role, w0, w1, arow, slot, r0, r1, b_lo, t, pol);
+            for (int blk = b_lo; blk < b_hi; blk += 2) {
+                if (blk + 1 < b_hi) i4_load(nxt, role, w0, w1, arow, slot, r0, r1, blk + 1, t, pol);
+                i4_mma<BF16>(cur, acc);
+                if (blk + 1 >= b_hi) break;
+                if (blk + 2 < b_hi) i4_load(cur, role, w0, w1, arow, slot, r0, r1, blk + 2, t, pol);
+                i4_mma<BF16>(nxt, acc);
+            }
+        }
+        if (KS > 1) {
+            s_part[warp][lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+            __syncthreads();
+            if (q == 0) {
+                acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+                for (int p = 0; p < KS; ++p) {  // warp (= K) order
+                    const float4 v = s_part[warp + p][lane];
+                    acc[0] += v.x;
+                    acc[1] += v.y;
+                    acc[2] += v.z;
+                    acc[3] += v.w;
+                }
+            }
+        }
+        if (q == 0 && live) i4_epilogue<DOWN>(a, acc, ids4, count, tile, r0, r1, groups, lane, t);
+        if (KS > 1) __syncthreads();  // s_part is reused by the next cell
+    }
+}
+
+// Larger batches (many cells): every warp owns whole cells and loads two K
+// blocks per round trip.
+template <bool DOWN, bool BF16>
+__global__ void __launch_bounds__(kW8GemvThreads) int4_gemv_wide_kernel(I4GemvArgs a) {
     grid_launch_dependents();  // programmatic dependent launch: the next kernel may start its launch
     grid_dependency_wait();    // the previous kernel's results are visible from here
     const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const int warps_total = gridDim.x * (kW8GemvThreads / 32);
     const int groups = __ldg(a.num_groups);
     const I4Role& role = a.role;
-    const int tiles = role.n / 16, blocks_per = role.k / 128 / a.ksplit;
-    const int tasks = groups * tiles * a.ksplit;
+    const int tiles = role.n / 16, blocks = role.k / 128;
     const uint64_t pol = policy_evict_first();
-    for (int task = blockIdx.x * (kW8GemvThreads / 32) + (threadIdx.x >> 5); task < tasks; task += warps_total) {
-        const int cell = task / a.ksplit, kpart = task - cell * a.ksplit;
+    for (int cell = blockIdx.x * (kW8GemvThreads / 32) + (threadIdx.x >> 5); cell < groups * tiles;
+         cell += warps_total) {
         const int grp = cell / tiles, tile = cell - grp * tiles;
         const int4 head = __ldg(a.g_rec + 2 * grp);
         const int4 ids4 = __ldg(a.g_rec + 2 * grp + 1);
@@ -728,113 +893,14 @@ __global__ void __launch_bounds__(kW8GemvThreads) int4_gemv_kernel(I4GemvArgs a)
         const int32_t* w0 = role.w + slot * role.w_slot + static_cast<int64_t>(r0) * role.w_row;
         const int32_t* w1 = w0 + 8 * role.w_row;
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
-        const int b0 = kpart * blocks_per;
-        for (int kb = b0; kb < b0 + blocks_per; kb += 2) {  // two 128-column blocks per load batch
-            uint4 q0[2], q1[2], xr[2][4];
-            float s0[2], s1[2];
-            uint32_t z0[2], z1[2];
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-                const int blk = kb + u;
-                q0[u] = ld_stream_v4(w0 + blk * 16 + 4 * t, pol);
-                q1[u] = ld_stream_v4(w1 + blk * 16 + 4 * t, pol);
-#pragma unroll
-                for (int v = 0; v < 4; ++v)
-                    xr[u][v] = arow ? __ldg(reinterpret_cast<const uint4*>(arow + blk * 128 + 32 * t) + v)
-                                    : make_uint4(0u, 0u, 0u, 0u);
-                const int64_t so = slot * role.s_slot + blk;
-                s0[u] = i4_scale(role.s, role.s_dtype, so + static_cast<int64_t>(r0) * role.s_row);
-                s1[u] = i4_scale(role.s, role.s_dtype, so + static_cast<int64_t>(r1) * role.s_row);
-                z0[u] = z1[u] = 8u;
-                if (role.z) {
-                    const int32_t* zp = role.z + slot * role.z_slot + blk;
-                    z0[u] = (static_cast<uint32_t>(__ldg(zp + (r0 >> 3) * role.z_row)) >> (4 * (r0 & 7))) & 15u;
-                    z1[u] = (static_cast<uint32_t>(__ldg(zp + (r1 >> 3) * role.z_row)) >> (4 * (r1 & 7))) & 15u;
-                }
-            }
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-                const uint32_t zb0 = (0x4300u + z0[u]) * 0x10001u, zb1 = (0x4300u + z1[u]) * 0x10001u;
-                const __nv_bfloat162 sp0 = __floats2bfloat162_rn(s0[u], s0[u]);
-                const __nv_bfloat162 sp1 = __floats2bfloat162_rn(s1[u], s1[u]);
-                const uint32_t sc0 = *reinterpret_cast<const uint32_t*>(&sp0);
-                const uint32_t sc1 = *reinterpret_cast<const uint32_t*>(&sp1);
-                const uint32_t W0[4] = {q0[u].x, q0[u].y, q0[u].z, q0[u].w};
-                const uint32_t W1[4] = {q1[u].x, q1[u].y, q1[u].z, q1[u].w};
-                const uint32_t X[16] = {xr[u][0].x, xr[u][0].y, xr[u][0].z, xr[u][0].w, xr[u][1].x, xr[u][1].y,
-                                        xr[u][1].z, xr[u][1].w, xr[u][2].x, xr[u][2].y, xr[u][2].z, xr[u][2].w,
-                                        xr[u][3].x, xr[u][3].y, xr[u][3].z, xr[u][3].w};
-#pragma unroll
-                for (int w = 0; w < 4; ++w) {  // word w: columns 8w..8w+7 of this thread's 32
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {  // pairs (2h, 2h+4) and (2h+1, 2h+5)
-                        const uint32_t A[4] = {int4_pair<BF16>(W0[w], 2 * h, zb0, sc0, s0[u]),
-                                               int4_pair<BF16>(W1[w], 2 * h, zb1, sc1, s1[u]),
-                                               int4_pair<BF16>(W0[w], 2 * h + 1, zb0, sc0, s0[u]),
-                                               int4_pair<BF16>(W1[w], 2 * h + 1, zb1, sc1, s1[u])};
-                        // token columns (2h, 2h+4) and (2h+1, 2h+5): low or high halves of x words 4w+h, 4w+h+2
-                        const uint32_t xa = X[4 * w + h], xb = X[4 * w + h + 2];
-                        mma_bf16_16816(acc, A, __byte_perm(xa, xb, 0x5410u), __byte_perm(xa, xb, 0x7632u));
-                    }
-                }
-            }
+        for (int blk = 0; blk < blocks; blk += 2) {  // blocks is even (K % 256 == 0)
+            I4Block b0, b1;
+            i4_load(b0, role, w0, w1, arow, slot, r0, r1, blk, t, pol);
+            i4_load(b1, role, w0, w1, arow, slot, r0, r1, blk + 1, t, pol);
+            i4_mma<BF16>(b0, acc);
+            i4_mma<BF16>(b1, acc);
         }
-        if (a.ksplit > 1) {
-            __stcg(a.part + static_cast<int64_t>(task) * 32 + lane, make_float4(acc[0], acc[1], acc[2], acc[3]));
-            __syncwarp();
-            int old = 0;
-            if (lane == 0) {
-                w8_fence();
-                old = atomicAdd(a.cnt + cell, 1);
-            }
-            old = __shfl_sync(0xffffffffu, old, 0);
-            if (old != a.ksplit - 1) continue;
-            w8_fence();
-            acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
-            for (int q = 0; q < a.ksplit; ++q) {  // part order: independent of arrival order
-                const float4 v = __ldcg(a.part + (static_cast<int64_t>(cell) * a.ksplit + q) * 32 + lane);
-                acc[0] += v.x;
-                acc[1] += v.y;
-                acc[2] += v.z;
-                acc[3] += v.w;
-            }
-        }
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-            const int col = 2 * t + c;
-            if (col >= count) continue;
-            const int pair = group_pair(ids4, col);
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const int row = h ? r1 : r0;
-                const float v = __bfloat162float(__float2bfloat16_rn(acc[2 * h + c]));  // projection in bf16
-                if constexpr (DOWN)
-                    a.pair_out[static_cast<int64_t>(pair) * role.n + row] = __fmul_rn(v, __ldg(a.wts + pair));
-                else
-                    a.gu[static_cast<int64_t>(pair) * role.n + row] = __float2bfloat16_rn(v);
-            }
-        }
-        if constexpr (DOWN) {
-            if (!a.out) continue;
-            __syncwarp();
-            int old = 0;
-            if (lane == 0) {
-                w8_fence();
-                old = atomicAdd(a.cmb_cnt + tile, 1);
-            }
-            old = __shfl_sync(0xffffffffu, old, 0);
-            if (old != groups - 1) continue;
-            w8_fence();
-            const int n = role.n;
-            for (int i = lane; i < a.tokens * 16; i += 32) {
-                const int64_t tok = i >> 4;
-                const int row = tile * 16 + (i & 15);
-                float sum = 0.0f;
-                for (int sl = 0; sl < a.top_k; ++sl)
-                    sum = __fadd_rn(sum, __ldcg(a.pair_out + (tok * a.top_k + sl) * n + row));
-                store_any(a.out, a.out_dtype, tok * n + row, sum);
-            }
-        }
+        i4_epilogue<DOWN>(a, acc, ids4, count, tile, r0, r1, groups, lane, t);
     }
 }
 
@@ -851,9 +917,11 @@ __global__ void __launch_bounds__(256) int4_act_kernel(__nv_bfloat16* gu, int I)
     }
 }
 
-int split_blocks(int64_t cells, int blocks) {
-    for (int ks = blocks / 2; ks > 1; --ks)
-        if (cells * ks <= kW8TargetWarps && blocks % (ks * 2) == 0) return ks;
+// Warps per CTA (= K shares per tile): the most that keep the warps within the
+// target and divide the blocks, at most 8.
+int int4_warps(int64_t cells, int blocks) {
+    for (int ks = 8; ks > 1; --ks)
+        if (cells * ks <= kW8TargetWarps && blocks % ks == 0) return ks;
     return 1;
 }
 
@@ -863,9 +931,17 @@ cudaError_t int4_launch_fmt(const DramaB200Int4Bank& b, const void* x, int64_t t
     const int64_t P = tokens * top_k;
     const int H = b.hidden, I = b.intermediate;
     const int64_t gmax = max_groups(P);
-    auto grid_for = [&](int64_t tasks) {
-        const int64_t ctas = (tasks + kW8GemvThreads / 32 - 1) / (kW8GemvThreads / 32);
+    auto grid_wide = [&](int64_t cells) {
+        const int64_t ctas = (cells + kW8GemvThreads / 32 - 1) / (kW8GemvThreads / 32);
         const int64_t cap = static_cast<int64_t>(sm_count) * 16;
+        return static_cast<unsigned>(ctas < 1 ? 1 : (ctas > cap ? cap : ctas));
+    };
+    // a CTA is one team of ks warps (ks > 1) or four single-warp teams
+    auto team_threads = [](int ks) { return 32 * (ks > 1 ? ks : 4); };
+    auto grid_cells = [&](int64_t cells, int ks) {
+        const int teams = ks > 1 ? 1 : 4;
+        const int64_t ctas = (cells + teams - 1) / teams;
+        const int64_t cap = static_cast<int64_t>(sm_count) * (ks > 1 ? 4 : 8);
         return static_cast<unsigned>(ctas < 1 ? 1 : (ctas > cap ? cap : ctas));
     };
     I4GemvArgs up{};
@@ -876,12 +952,14 @@ cudaError_t int4_launch_fmt(const DramaB200Int4Bank& b, const void* x, int64_t t
     up.act = static_cast<const __nv_bfloat16*>(x);
     up.act_stride = H;
     up.top_k = top_k;
-    up.ksplit = split_blocks(gmax * (2 * I / 16), H / 128);
-    up.cnt = ws.up_cnt;
-    up.part = reinterpret_cast<float4*>(ws.part);
     up.gu = ws.up;
-    cudaError_t err = launch_pdl(int4_gemv_kernel<false, BF16>, dim3(grid_for(gmax * (2 * I / 16) * up.ksplit)),
-                                 dim3(kW8GemvThreads), 0, s, up);
+    const int64_t up_cells = gmax * (2 * I / 16);
+    up.ksplit = int4_warps(up_cells, H / 128);
+    cudaError_t err =
+        up.ksplit > 1
+            ? launch_pdl(int4_gemv_kernel<false, BF16>, dim3(grid_cells(up_cells, up.ksplit)),
+                         dim3(team_threads(up.ksplit)), 0, s, up)
+            : launch_pdl(int4_gemv_wide_kernel<false, BF16>, dim3(grid_wide(up_cells)), dim3(kW8GemvThreads), 0, s, up);
     if (err != cudaSuccess) return err;
     err = launch_pdl(int4_act_kernel, dim3(static_cast<unsigned>(P)), dim3(256), 0, s, ws.up, I);
     if (err != cudaSuccess) return err;
@@ -893,17 +971,19 @@ cudaError_t int4_launch_fmt(const DramaB200Int4Bank& b, const void* x, int64_t t
     dn.act = ws.up;
     dn.act_stride = 2 * I;
     dn.top_k = top_k;
-    dn.ksplit = split_blocks(gmax * (H / 16), I / 128);
-    dn.cnt = ws.dn_cnt;
-    dn.part = reinterpret_cast<float4*>(ws.part);
     dn.pair_out = pair_out;
     dn.wts = ws.wts;
     dn.cmb_cnt = ws.cmb_cnt;
     dn.out = out;
     dn.out_dtype = out_dtype;
     dn.tokens = tokens;
-    return launch_pdl(int4_gemv_kernel<true, BF16>, dim3(grid_for(gmax * (H / 16) * dn.ksplit)), dim3(kW8GemvThreads),
-                      0, s, dn);
+    const int64_t dn_cells = gmax * (H / 16);
+    dn.ksplit = int4_warps(dn_cells, I / 128);
+    return dn.ksplit > 1
+               ? launch_pdl(int4_gemv_kernel<true, BF16>, dim3(grid_cells(dn_cells, dn.ksplit)),
+                            dim3(team_threads(dn.ksplit)), 0, s, dn)
+               : launch_pdl(int4_gemv_wide_kernel<true, BF16>, dim3(grid_wide(dn_cells)), dim3(kW8GemvThreads), 0, s,
+                            dn);
 }
 
 }  // namespace
