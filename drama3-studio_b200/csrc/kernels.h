@@ -238,10 +238,7 @@ struct W8a8Workspace {
     float* hs;                // [P]
     float* wts;               // [P] route weights as fp32
     float* pair_out;          // [P][H] weighted fp32 partials
-    int32_t* up_cnt;          // [cells] split-K arrivals per gate/up cell (zeroed by prep)
-    int32_t* dn_cnt;          // [cells] split-K arrivals per down cell (zeroed by prep)
     int32_t* cmb_cnt;         // [H/16] finished down cells per row tile (zeroed by prep)
-    int4* part;               // [tasks][32] int32 partial sums of split-K warps
 };
 size_t w8a8_workspace_layout(int64_t tokens, int top_k, int hidden, int intermediate, char* base,
                              W8a8Workspace* ws);
@@ -260,8 +257,6 @@ struct SharedWorkspace {
     __nv_bfloat16* gu;        // [T][2I] gate/up projections
     __nv_bfloat16* h;         // [T][I] SwiGLU rows
     float* gate_s;            // [T] bf16-rounded sigmoid gate
-    int32_t* cnt;             // split-K arrivals (reset by the last arriver)
-    float4* part;             // [tasks][32] fp32 partial sums
 };
 size_t shared_expert_workspace_layout(int64_t tokens, int hidden, int inter, char* base, SharedWorkspace* ws);
 cudaError_t shared_expert_launch(const DramaB200SharedExpert& m, const void* x, int64_t tokens, const void* routed,

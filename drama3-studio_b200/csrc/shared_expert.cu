@@ -12,9 +12,10 @@
 // SwiGLU and gate scalar -> down GEMV whose
 // epilogue applies the gate, the routed sum and the residual. The GEMVs stream
 // the dense bf16 weights once per group of <= 8 tokens through
-// mma.m16n8k16 bf16 fragments (tokens as N), split K across warps when the
-// tiles alone would leave the GPU idle (batch 1), and add the fp32 partials in
-// part order in the last-arriving warp, so results do not depend on timing.
+// mma.m16n8k16 bf16 fragments (tokens as N). When the tiles alone would leave
+// the GPU idle (batch 1) a CTA of up to 16 warps shares one tile, each warp a
+// part of K, and warp 0 adds the fp32 parts in warp order from shared memory,
+// so results do not depend on timing.
 #include "common.cuh"
 #include "grouped.cuh"
 #include "kernels.h"
@@ -26,8 +27,6 @@ constexpr int kShThreads = 128;
 constexpr int kShTarget = 4736;  // 148 SMs x 32 warps: the split-K target
 constexpr int kShTok = 8;        // tokens per MMA N tile
 
-__device__ __forceinline__ void sh_fence() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
-
 struct ShGemvArgs {
     const __nv_bfloat16* w0;  // rows [0, n0) (gate_proj, or down_proj)
     const __nv_bfloat16* w1;  // rows [n0, 2 n0) (up_proj), or NULL
@@ -36,9 +35,7 @@ struct ShGemvArgs {
     int n0;
     const __nv_bfloat16* act; // [T][k]
     int64_t tokens;
-    int ksplit;
-    int32_t* cnt;             // [cells]
-    float4* part;             // [tasks][32]
+    int ksplit;               // warps per CTA sharing one cell (K parts), 1: one cell per warp
     // epilogue
     __nv_bfloat16* gu;        // gate/up: [T][2 Is] bf16
     const float* gate_s;      // down: [T] bf16-rounded sigmoid gate
@@ -48,18 +45,22 @@ struct ShGemvArgs {
 };
 
 template <bool DOWN>
-__global__ void __launch_bounds__(kShThreads) shared_gemv_kernel(ShGemvArgs a) {
+__global__ void __launch_bounds__(512) shared_gemv_kernel(ShGemvArgs a) {
     grid_launch_dependents();  // programmatic dependent launch
     grid_dependency_wait();
-    const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    const int warps_total = gridDim.x * (kShThreads / 32);
+    __shared__ float4 s_part[16][32];
+    const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3, warp = threadIdx.x >> 5;
     const int tiles = a.n / 16;
     const int tgroups = static_cast<int>((a.tokens + kShTok - 1) / kShTok);
     const int spans_per = a.k / 32 / a.ksplit;  // 32-column spans
-    const int tasks = tgroups * tiles * a.ksplit;
     const uint64_t pol = policy_evict_first();
-    for (int task = blockIdx.x * (kShThreads / 32) + (threadIdx.x >> 5); task < tasks; task += warps_total) {
-        const int cell = task / a.ksplit, kpart = task - cell * a.ksplit;
+    // a.ksplit > 1: the CTA's a.ksplit warps share one cell (warp = K part) and add their fp32 sums in warp
+    // order through shared memory; a.ksplit == 1: every warp owns whole cells
+    const bool team = a.ksplit > 1;
+    const int first = team ? blockIdx.x : blockIdx.x * (blockDim.x >> 5) + warp;
+    const int step = team ? gridDim.x : gridDim.x * (blockDim.x >> 5);
+    for (int cell = first; cell < tgroups * tiles; cell += step) {
+        const int kpart = team ? warp : 0;
         const int tg = cell / tiles, tile = cell - tg * tiles;
         const int64_t tok = static_cast<int64_t>(tg) * kShTok + g;
         const __nv_bfloat16* xrow = tok < a.tokens ? a.act + tok * a.k : nullptr;
@@ -86,27 +87,21 @@ __global__ void __launch_bounds__(kShThreads) shared_gemv_kernel(ShGemvArgs a) {
                 mma_bf16_16816(acc, a2, xb[u].z, xb[u].w);
             }
         }
-        if (a.ksplit > 1) {
-            __stcg(a.part + static_cast<int64_t>(task) * 32 + lane, make_float4(acc[0], acc[1], acc[2], acc[3]));
-            __syncwarp();
-            int old = 0;
-            if (lane == 0) {
-                sh_fence();
-                old = atomicAdd(a.cnt + cell, 1);
-            }
-            old = __shfl_sync(0xffffffffu, old, 0);
-            if (old != a.ksplit - 1) continue;
-            if (lane == 0) a.cnt[cell] = 0;  // ready for the next call
-            sh_fence();
-            acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
-            for (int q = 0; q < a.ksplit; ++q) {  // part order: the sum does not depend on arrival order
-                const float4 v = __ldcg(a.part + (static_cast<int64_t>(cell) * a.ksplit + q) * 32 + lane);
-                acc[0] += v.x;
-                acc[1] += v.y;
-                acc[2] += v.z;
-                acc[3] += v.w;
+        if (team) {
+            s_part[warp][lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+            __syncthreads();
+            if (warp == 0) {
+                acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+                for (int q = 0; q < a.ksplit; ++q) {  // warp (= K) order: the sum does not depend on timing
+                    const float4 v = s_part[q][lane];
+                    acc[0] += v.x;
+                    acc[1] += v.y;
+                    acc[2] += v.z;
+                    acc[3] += v.w;
+                }
             }
         }
+        if (!team || warp == 0) {
         // acc[0..1]: row r0, tokens 2t, 2t+1 of the group; acc[2..3]: row r1
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
@@ -127,6 +122,8 @@ __global__ void __launch_bounds__(kShThreads) shared_gemv_kernel(ShGemvArgs a) {
                 }
             }
         }
+        }
+        if (team) __syncthreads();  // s_part is reused by the next cell
     }
 }
 
@@ -172,7 +169,7 @@ __global__ void __launch_bounds__(256) shared_act_kernel(const __nv_bfloat16* x,
 // K parts per tile: as many as keep the warps within the target, each part a
 // whole number of 4-span load batches (one round trip per batch).
 int sh_split(int64_t cells, int spans) {
-    for (int ks = spans / 4; ks > 1; --ks)
+    for (int ks = spans / 4 < 16 ? spans / 4 : 16; ks > 1; --ks)
         if (cells * ks <= kShTarget && spans % (ks * 4) == 0) return ks;
     return 1;
 }
@@ -180,10 +177,6 @@ int sh_split(int64_t cells, int spans) {
 }  // namespace
 
 size_t shared_expert_workspace_layout(int64_t tokens, int hidden, int inter, char* base, SharedWorkspace* ws) {
-    const int64_t tg = (tokens + kShTok - 1) / kShTok;
-    const int64_t up_cells = tg * (2 * inter / 16), dn_cells = tg * (hidden / 16);
-    const int up_ks = sh_split(up_cells, hidden / 32), dn_ks = sh_split(dn_cells, inter / 32);
-    const int64_t up_tasks = up_ks > 1 ? up_cells * up_ks : 0, dn_tasks = dn_ks > 1 ? dn_cells * dn_ks : 0;
     size_t off = 0;
     auto take = [&](size_t bytes) -> char* {
         char* p = base ? base + off : nullptr;
@@ -191,14 +184,9 @@ size_t shared_expert_workspace_layout(int64_t tokens, int hidden, int inter, cha
         return p;
     };
     SharedWorkspace w{};
-    // Split-K counters first, sized for the largest call, so that their place does not move with the
-    // shape: zero-filled once with the workspace, every cell is reset by its last arriver.
-    const int64_t max_tg = (kMaxSharedTokens + kShTok - 1) / kShTok;
-    w.cnt = reinterpret_cast<int32_t*>(take(max_tg * ((2 * inter > hidden ? 2 * inter : hidden) / 16) * 4));
     w.gu = reinterpret_cast<__nv_bfloat16*>(take(static_cast<size_t>(tokens) * 2 * inter * 2));
     w.h = reinterpret_cast<__nv_bfloat16*>(take(static_cast<size_t>(tokens) * inter * 2));
     w.gate_s = reinterpret_cast<float*>(take(tokens * 4));
-    w.part = reinterpret_cast<float4*>(take(static_cast<size_t>(up_tasks > dn_tasks ? up_tasks : dn_tasks) * 32 * 16));
     if (ws) *ws = w;
     return off;
 }
@@ -208,9 +196,12 @@ cudaError_t shared_expert_launch(const DramaB200SharedExpert& m, const void* x, 
                                  cudaStream_t s) {
     const int H = m.hidden, I = m.intermediate;
     const int64_t tg = (tokens + kShTok - 1) / kShTok;
-    auto grid_for = [&](int64_t tasks) {
-        const int64_t ctas = (tasks + kShThreads / 32 - 1) / (kShThreads / 32);
-        const int64_t cap = static_cast<int64_t>(sm_count) * 16;
+    // split tiles: one CTA of ks warps per cell; otherwise four single-warp cells per CTA
+    auto cta_threads = [](int ks) { return ks > 1 ? 32 * ks : kShThreads; };
+    auto grid_cells = [&](int64_t cells, int ks) {
+        const int per_cta = ks > 1 ? 1 : kShThreads / 32;
+        const int64_t ctas = (cells + per_cta - 1) / per_cta;
+        const int64_t cap = static_cast<int64_t>(sm_count) * (ks > 1 ? (32 + ks - 1) / ks : 16);
         return static_cast<unsigned>(ctas < 1 ? 1 : (ctas > cap ? cap : ctas));
     };
     ShGemvArgs up{};
@@ -224,11 +215,9 @@ cudaError_t shared_expert_launch(const DramaB200SharedExpert& m, const void* x, 
     up.act = static_cast<const __nv_bfloat16*>(x);
     up.tokens = tokens;
     up.ksplit = sh_split(tg * (2 * I / 16), H / 32);
-    up.cnt = ws.cnt;
-    up.part = ws.part;
     up.gu = ws.gu;
-    cudaError_t err = launch_pdl(shared_gemv_kernel<false>, dim3(grid_for(tg * (2 * I / 16) * up.ksplit)),
-                                 dim3(kShThreads), 0, s, up);
+    cudaError_t err = launch_pdl(shared_gemv_kernel<false>, dim3(grid_cells(tg * (2 * I / 16), up.ksplit)),
+                                 dim3(cta_threads(up.ksplit)), 0, s, up);
     if (err != cudaSuccess) return err;
     err = launch_pdl(shared_act_kernel, dim3(static_cast<unsigned>(tokens)), dim3(256), 0, s,
                      static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(m.gate_weight), H,
@@ -244,14 +233,12 @@ cudaError_t shared_expert_launch(const DramaB200SharedExpert& m, const void* x, 
     dn.act = ws.h;
     dn.tokens = tokens;
     dn.ksplit = sh_split(tg * (H / 16), I / 32);
-    dn.cnt = ws.cnt;
-    dn.part = ws.part;
     dn.gate_s = ws.gate_s;
     dn.routed = static_cast<const __nv_bfloat16*>(routed);
     dn.residual = static_cast<const __nv_bfloat16*>(residual);
     dn.out = static_cast<__nv_bfloat16*>(out);
-    return launch_pdl(shared_gemv_kernel<true>, dim3(grid_for(tg * (H / 16) * dn.ksplit)), dim3(kShThreads), 0, s,
-                      dn);
+    return launch_pdl(shared_gemv_kernel<true>, dim3(grid_cells(tg * (H / 16), dn.ksplit)),
+                      dim3(cta_threads(dn.ksplit)), 0, s, dn);
 }
 
 }  // namespace drama

@@ -20,14 +20,14 @@
 //            a column's result does not depend on its group, so any grouping
 //            gives the same bits); CTAs 1..T rotate and quantise one token row
 //            each;
-//   gemv   : gate/up projections. A task is (group, 16-row tile, K part):
-//            the warp streams that part of the tile's weights with 16-byte
-//            loads, dequantises them in registers into mma.m16n8k32 s8
-//            fragments whose N dimension holds the group's tokens (weights
-//            read once per group), and, when K is split, leaves its int32
-//            partial sums for the last-arriving warp of the tile, which adds
-//            them (exactly, in any order) and applies the epilogue. K is split
-//            only when there are too few tiles to occupy the GPU (batch 1);
+//   gemv   : gate/up projections. A cell is (group, 16-row tile): a warp
+//            streams the tile's weights with 16-byte loads, dequantises them
+//            in registers into mma.m16n8k32 s8 fragments whose N dimension
+//            holds the group's tokens (weights read once per group). When
+//            there are too few cells to occupy the GPU (batch 1), a CTA of up
+//            to 8 warps shares one cell, each warp a contiguous part of K, and
+//            warp 0 adds the int32 sums from shared memory (exact in any
+//            order) and applies the epilogue;
 //   rotate : SwiGLU rows (bf16(bf16(silu(gate)) * up)) -> int8 + scale;
 //   gemv   : down projections, rounded to bf16 and weighted in fp32; the
 //            warp that finishes the last cell of a 16-row tile of H sums the
@@ -208,9 +208,6 @@ __device__ void w8a8_prep_tail(const W8PrepArgs& a, int groups, int dropped) {
         a.ws.num_groups[0] = groups;
         a.ws.status[0] = dropped;
     }
-    const int up_cells = groups * (2 * a.intermediate / 16), dn_cells = groups * (a.hidden / 16);
-    for (int i = tid; i < up_cells; i += blockDim.x) a.ws.up_cnt[i] = 0;
-    for (int i = tid; i < dn_cells; i += blockDim.x) a.ws.dn_cnt[i] = 0;
     for (int i = tid; i < a.hidden / 16; i += blockDim.x) a.ws.cmb_cnt[i] = 0;
     for (int64_t p = tid; p < a.pairs; p += blockDim.x) a.ws.wts[p] = load_any(a.weights, a.weights_dtype, p);
     if (dropped) {
@@ -353,9 +350,7 @@ struct W8GemvArgs {
     const int8_t* act;        // [rows][k]
     const float* act_scale;   // [rows]
     int top_k;                // up: activation row = pair / top_k; down: row = pair
-    int ksplit;               // K parts per tile (spans divisible by ksplit * kW8Unroll)
-    int32_t* cnt;             // [cells] arrivals (ksplit > 1)
-    int4* part;               // [tasks][32] partial sums (ksplit > 1)
+    int ksplit;               // K parts per tile = warps per CTA when > 1 (spans divisible by ksplit * kW8Unroll)
     __nv_bfloat16* up_out;    // up: [P][n]
     float* pair_out;          // down: [P][n]
     const float* wts;         // down: [P]
@@ -445,18 +440,22 @@ __device__ __forceinline__ float channel_scale(const W8Role& r, int slot, int ro
 // U: spans whose loads are all issued before the first MMA (4, or 8 when a
 // task's span count allows, so a batch-1 task is a single round trip).
 template <int MODE, bool DOWN, int U>
-__global__ void __launch_bounds__(kW8GemvThreads) w8a8_gemv_kernel(W8GemvArgs a) {
+__global__ void __launch_bounds__(256) w8a8_gemv_kernel(W8GemvArgs a) {
     grid_launch_dependents();  // programmatic dependent launch: the next kernel may start its launch
     grid_dependency_wait();    // the previous kernel's results are visible from here
-    const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    const int warps_total = gridDim.x * (kW8GemvThreads / 32);
+    __shared__ int4 s_part[8][32];
+    const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3, warp = threadIdx.x >> 5;
     const int groups = __ldg(a.num_groups);
     const W8Role& role = a.role;
     const int tiles = role.n / 16, spans_per = role.k / 64 / a.ksplit;
-    const int tasks = groups * tiles * a.ksplit;
     const uint64_t pol = policy_evict_first();
-    for (int task = blockIdx.x * (kW8GemvThreads / 32) + (threadIdx.x >> 5); task < tasks; task += warps_total) {
-        const int cell = task / a.ksplit, kpart = task - cell * a.ksplit;
+    // a.ksplit > 1: the CTA's a.ksplit warps share one cell (warp = K part) and add their int32 sums in
+    // shared memory; a.ksplit == 1: every warp owns whole cells
+    const bool team = a.ksplit > 1;
+    const int first = team ? blockIdx.x : blockIdx.x * (blockDim.x >> 5) + warp;
+    const int step = team ? gridDim.x : gridDim.x * (blockDim.x >> 5);
+    for (int cell = first; cell < groups * tiles; cell += step) {
+        const int kpart = team ? warp : 0;
         const int grp = cell / tiles, tile = cell - grp * tiles;
         const int4 head = __ldg(a.g_rec + 2 * grp);
         const int4 ids4 = __ldg(a.g_rec + 2 * grp + 1);
@@ -496,69 +495,66 @@ __global__ void __launch_bounds__(kW8GemvThreads) w8a8_gemv_kernel(W8GemvArgs a)
                 mma_s8_16832(acc, a2, xb[u].z, xb[u].w);
             }
         }
-        if (a.ksplit > 1) {
-            // leave the partial sums; the last-arriving part of the tile adds them all
-            __stcg(a.part + static_cast<int64_t>(task) * 32 + lane, make_int4(acc[0], acc[1], acc[2], acc[3]));
-            __syncwarp();
-            int old = 0;
-            if (lane == 0) {
-                w8_fence();
-                old = atomicAdd(a.cnt + cell, 1);
-            }
-            old = __shfl_sync(0xffffffffu, old, 0);
-            if (old != a.ksplit - 1) continue;
-            w8_fence();
-            acc[0] = acc[1] = acc[2] = acc[3] = 0;
-            for (int q = 0; q < a.ksplit; ++q) {
-                const int4 v = __ldcg(a.part + (static_cast<int64_t>(cell) * a.ksplit + q) * 32 + lane);
-                acc[0] += v.x;
-                acc[1] += v.y;
-                acc[2] += v.z;
-                acc[3] += v.w;
-            }
+        if (team) {
+            s_part[warp][lane] = make_int4(acc[0], acc[1], acc[2], acc[3]);
+            __syncthreads();
+            if (warp == 0)
+                for (int q = 1; q < a.ksplit; ++q) {  // exact integer sums: any order gives the same bits
+                    const int4 v = s_part[q][lane];
+                    acc[0] += v.x;
+                    acc[1] += v.y;
+                    acc[2] += v.z;
+                    acc[3] += v.w;
+                }
         }
-        // epilogue: acc[0..1] row r0, token columns 2t, 2t+1; acc[2..3] row r0 + 8
-        const float sb0 = channel_scale<MODE>(role, slot, r0), sb1 = channel_scale<MODE>(role, slot, r0 + 8);
+        if (!team || warp == 0) {
+            // epilogue: acc[0..1] row r0, token columns 2t, 2t+1; acc[2..3] row r0 + 8
+            const float sb0 = channel_scale<MODE>(role, slot, r0), sb1 = channel_scale<MODE>(role, slot, r0 + 8);
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-            const int col = 2 * t + c;
-            if (col >= count) continue;
-            const int pair = group_pair(ids4, col);
-            const float sa = __ldg(a.act_scale + (DOWN ? pair : pair / a.top_k));
+            for (int c = 0; c < 2; ++c) {
+                const int col = 2 * t + c;
+                if (col >= count) continue;
+                const int pair = group_pair(ids4, col);
+                const float sa = __ldg(a.act_scale + (DOWN ? pair : pair / a.top_k));
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const int row = r0 + 8 * h;
-                const float v = __fmul_rn(__fmul_rn(__int2float_rn(acc[2 * h + c]), sa), h ? sb1 : sb0);
-                if constexpr (DOWN) {
-                    const float rounded = __bfloat162float(__float2bfloat16_rn(v));
-                    a.pair_out[static_cast<int64_t>(pair) * role.n + row] = __fmul_rn(rounded, __ldg(a.wts + pair));
-                } else {
-                    a.up_out[static_cast<int64_t>(pair) * role.n + row] = __float2bfloat16_rn(v);
+                for (int h = 0; h < 2; ++h) {
+                    const int row = r0 + 8 * h;
+                    const float v = __fmul_rn(__fmul_rn(__int2float_rn(acc[2 * h + c]), sa), h ? sb1 : sb0);
+                    if constexpr (DOWN) {
+                        const float rounded = __bfloat162float(__float2bfloat16_rn(v));
+                        a.pair_out[static_cast<int64_t>(pair) * role.n + row] =
+                            __fmul_rn(rounded, __ldg(a.wts + pair));
+                    } else {
+                        a.up_out[static_cast<int64_t>(pair) * role.n + row] = __float2bfloat16_rn(v);
+                    }
+                }
+            }
+            if constexpr (DOWN) {
+                // the last cell of this row tile sums its rows' route slots in slot order
+                int old = -1;
+                if (a.out) {
+                    __syncwarp();
+                    if (lane == 0) {
+                        w8_fence();
+                        old = atomicAdd(a.cmb_cnt + tile, 1);
+                    }
+                    old = __shfl_sync(0xffffffffu, old, 0);
+                }
+                if (old == groups - 1) {
+                    w8_fence();
+                    const int n = role.n;
+                    for (int i = lane; i < a.tokens * 16; i += 32) {
+                        const int64_t tok = i >> 4;
+                        const int row = tile * 16 + (i & 15);
+                        float sum = 0.0f;
+                        for (int sl = 0; sl < a.top_k; ++sl)
+                            sum = __fadd_rn(sum, __ldcg(a.pair_out + (tok * a.top_k + sl) * n + row));
+                        store_any(a.out, a.out_dtype, tok * n + row, sum);
+                    }
                 }
             }
         }
-        if constexpr (DOWN) {
-            if (!a.out) continue;
-            // the last cell of this row tile sums its rows' route slots in slot order
-            __syncwarp();
-            int old = 0;
-            if (lane == 0) {
-                w8_fence();
-                old = atomicAdd(a.cmb_cnt + tile, 1);
-            }
-            old = __shfl_sync(0xffffffffu, old, 0);
-            if (old != groups - 1) continue;
-            w8_fence();
-            const int n = role.n;
-            for (int i = lane; i < a.tokens * 16; i += 32) {
-                const int64_t tok = i >> 4;
-                const int row = tile * 16 + (i & 15);
-                float sum = 0.0f;
-                for (int sl = 0; sl < a.top_k; ++sl)
-                    sum = __fadd_rn(sum, __ldcg(a.pair_out + (tok * a.top_k + sl) * n + row));
-                store_any(a.out, a.out_dtype, tok * n + row, sum);
-            }
-        }
+        if (team) __syncthreads();  // s_part is reused by the next cell
     }
 }
 
@@ -567,7 +563,7 @@ int64_t max_groups(int64_t pairs) { return pairs; }
 
 // K parts per tile: split only while the tiles alone leave the GPU idle.
 int split_for(int64_t cells, int spans) {
-    for (int ks = 4; ks > 1; --ks)
+    for (int ks = 8; ks > 1; --ks)
         if (cells * ks <= kW8TargetWarps && spans % (ks * kW8Unroll) == 0) return ks;
     return 1;
 }
@@ -581,9 +577,12 @@ cudaError_t launch_mode(const DramaB200W8a8Bank& b, int64_t tokens, int top_k, v
     const int64_t P = tokens * top_k;
     const int H = b.hidden, I = b.intermediate;
     const int64_t gmax = max_groups(P);
-    auto grid_for = [&](int64_t tasks) {
-        int64_t ctas = (tasks + kW8GemvThreads / 32 - 1) / (kW8GemvThreads / 32);
-        const int64_t cap = static_cast<int64_t>(sm_count) * 16;
+    // split tiles: one CTA of ks warps per cell; otherwise four single-warp cells per CTA
+    auto cta_threads = [](int ks) { return ks > 1 ? 32 * ks : kW8GemvThreads; };
+    auto grid_cells = [&](int64_t cells, int ks) {
+        const int per_cta = ks > 1 ? 1 : kW8GemvThreads / 32;
+        const int64_t ctas = (cells + per_cta - 1) / per_cta;
+        const int64_t cap = static_cast<int64_t>(sm_count) * (ks > 1 ? 32 / ks : 16);
         return static_cast<unsigned>(ctas < 1 ? 1 : (ctas > cap ? cap : ctas));
     };
     W8GemvArgs up{};
@@ -595,13 +594,11 @@ cudaError_t launch_mode(const DramaB200W8a8Bank& b, int64_t tokens, int top_k, v
     up.act_scale = ws.xs;
     up.top_k = top_k;
     up.ksplit = split_for(gmax * (2 * I / 16), H / 64);
-    up.cnt = ws.up_cnt;
-    up.part = ws.part;
     up.up_out = ws.up;
-    const dim3 up_grid(grid_for(gmax * (2 * I / 16) * up.ksplit));
+    const dim3 up_grid(grid_cells(gmax * (2 * I / 16), up.ksplit)), up_block(cta_threads(up.ksplit));
     cudaError_t err = (H / 64 / up.ksplit) % 8 == 0
-                          ? launch_pdl(w8a8_gemv_kernel<MODE, false, 8>, up_grid, dim3(kW8GemvThreads), 0, s, up)
-                          : launch_pdl(w8a8_gemv_kernel<MODE, false, 4>, up_grid, dim3(kW8GemvThreads), 0, s, up);
+                          ? launch_pdl(w8a8_gemv_kernel<MODE, false, 8>, up_grid, up_block, 0, s, up)
+                          : launch_pdl(w8a8_gemv_kernel<MODE, false, 4>, up_grid, up_block, 0, s, up);
     if (err != cudaSuccess) return err;
     err = launch_pdl(w8a8_act_kernel, dim3(static_cast<unsigned>(P)), dim3(rot_threads(I)), rot_smem(I), s, ws.up, I,
                      ws.hq, ws.hs);
@@ -615,18 +612,16 @@ cudaError_t launch_mode(const DramaB200W8a8Bank& b, int64_t tokens, int top_k, v
     dn.act_scale = ws.hs;
     dn.top_k = top_k;
     dn.ksplit = split_for(gmax * (H / 16), I / 64);
-    dn.cnt = ws.dn_cnt;
-    dn.part = ws.part;
     dn.pair_out = pair_out;
     dn.wts = ws.wts;
     dn.cmb_cnt = ws.cmb_cnt;
     dn.out = out;
     dn.out_dtype = out_dtype;
     dn.tokens = tokens;
-    const dim3 dn_grid(grid_for(gmax * (H / 16) * dn.ksplit));
+    const dim3 dn_grid(grid_cells(gmax * (H / 16), dn.ksplit)), dn_block(cta_threads(dn.ksplit));
     return (I / 64 / dn.ksplit) % 8 == 0
-               ? launch_pdl(w8a8_gemv_kernel<MODE, true, 8>, dn_grid, dim3(kW8GemvThreads), 0, s, dn)
-               : launch_pdl(w8a8_gemv_kernel<MODE, true, 4>, dn_grid, dim3(kW8GemvThreads), 0, s, dn);
+               ? launch_pdl(w8a8_gemv_kernel<MODE, true, 8>, dn_grid, dn_block, 0, s, dn)
+               : launch_pdl(w8a8_gemv_kernel<MODE, true, 4>, dn_grid, dn_block, 0, s, dn);
 }
 
 // ---------------------------------------------------------------------------
@@ -991,12 +986,6 @@ cudaError_t int4_launch_fmt(const DramaB200Int4Bank& b, const void* x, int64_t t
 size_t w8a8_workspace_layout(int64_t tokens, int top_k, int hidden, int intermediate, char* base,
                              W8a8Workspace* ws) {
     const int64_t P = tokens * top_k;
-    const int64_t gmax = max_groups(P);
-    const int64_t up_cells = gmax * (2 * intermediate / 16), dn_cells = gmax * (hidden / 16);
-    const int64_t up_parts = split_for(up_cells, hidden / 64), dn_parts = split_for(dn_cells, intermediate / 64);
-    const int64_t up_tasks = up_parts > 1 ? up_cells * up_parts : 0;
-    const int64_t dn_tasks = dn_parts > 1 ? dn_cells * dn_parts : 0;
-    const int64_t part_tasks = up_tasks > dn_tasks ? up_tasks : dn_tasks;  // up and down share the scratch
     size_t off = 0;
     auto take = [&](size_t bytes) -> char* {
         char* p = base ? base + off : nullptr;
@@ -1015,10 +1004,7 @@ size_t w8a8_workspace_layout(int64_t tokens, int top_k, int hidden, int intermed
     w.hs = reinterpret_cast<float*>(take(P * 4));
     w.wts = reinterpret_cast<float*>(take(P * 4));
     w.pair_out = reinterpret_cast<float*>(take(static_cast<size_t>(P) * hidden * 4));
-    w.up_cnt = reinterpret_cast<int32_t*>(take(up_cells * 4));
-    w.dn_cnt = reinterpret_cast<int32_t*>(take(dn_cells * 4));
     w.cmb_cnt = reinterpret_cast<int32_t*>(take(static_cast<size_t>(hidden / 16) * 4));
-    w.part = reinterpret_cast<int4*>(take(static_cast<size_t>(part_tasks) * 32 * sizeof(int4)));
     if (ws) *ws = w;
     return off;
 }

@@ -213,9 +213,7 @@ DRAMA_B200_API int drama_b200_w8a8_decode(const DramaB200W8a8Bank* bank, const v
  * x, routed, residual, out: [tokens, H] bfloat16 (row stride H); weights bf16
  * row-major with row strides in elements (multiples of 8, 16-byte aligned).
  * H and I multiples of 128, tokens <= 4096. out may alias routed or residual
- * (each element is read before it is written, by the same thread). The
- * workspace is zero-filled once and then used only by this entry point: its
- * split-K counters sit at its start and every call leaves them zero.
+ * (each element is read before it is written, by the same thread).
  * ------------------------------------------------------------------------- */
 typedef struct DramaB200SharedExpert {
     const void* gate_proj;     /* [I, H] */
