@@ -973,15 +973,15 @@ def run_int4(args, mode: int = 0) -> None:
     if mode == 0:
         dtype = "int4 weights (asymmetric, group 128, bf16 scales, uint4 zero-points), f16 MMA, fp32 accumulate"
         layer = "W4A16"
-        kernel = "one W4A16 expert call (prep + up + down kernels), batch 1"
+        kernel = "one W4A16 expert call (grouping, gate/up GEMV with SwiGLU, down GEMV with the fused combine), batch 1"
         launches = 3
     else:
         dtype = (f"{W8A8_NAMES[mode]} weights, ConvRot-rotated int8 activations, s8 MMA, int32 accumulate, "
                  "bf16 projections")
         layer = f"W8A8 mode {mode} ({W8A8_NAMES[mode]})"
-        kernel = (f"one {W8A8_NAMES[mode]} expert call (prep, rotate, up GEMV, rotate, down GEMV, combine), "
-                  "batch 1")
-        launches = 6
+        kernel = (f"one {W8A8_NAMES[mode]} expert call (grouping + token rotation, up GEMV, SwiGLU rotation, "
+                  "down GEMV with the fused combine), batch 1")
+        launches = 4
     line = {
         "metric": METRIC, "value": b1["tokens_per_s"], "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": max(3, args.warmup), "ms_per_step": INT4_CALLS * b1["call_us"] / 1000.0, "higher_is_better": True,

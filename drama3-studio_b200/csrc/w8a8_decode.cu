@@ -696,23 +696,22 @@ __device__ __forceinline__ uint32_t int4_pair(uint32_t W, int i, uint32_t zb, ui
     }
 }
 
-// One 128-column block of one warp: the raw loads, issued one block ahead of
-// the MMAs that consume them.
-struct I4Block {
+// One 128-column block of one warp: the raw loads of a row pair (rows g and
+// g + 8 of a tile) and of the token row, issued one block ahead of the MMAs
+// that consume them.
+struct I4Rows {
     uint4 q0, q1;    // the two weight rows' 32 nibbles
-    uint4 x[4];      // the token row's 32 bf16
     float s0, s1;    // scales
     uint32_t z0, z1; // zero points
 };
+struct I4X {
+    uint4 x[4];      // the token row's 32 bf16
+};
 
-__device__ __forceinline__ void i4_load(I4Block& b, const I4Role& role, const int32_t* w0, const int32_t* w1,
-                                        const __nv_bfloat16* arow, int slot, int r0, int r1, int blk, int t,
-                                        uint64_t pol) {
+__device__ __forceinline__ void i4_load_rows(I4Rows& b, const I4Role& role, const int32_t* w0, const int32_t* w1,
+                                             int slot, int r0, int r1, int blk, int t, uint64_t pol) {
     b.q0 = ld_stream_v4(w0 + blk * 16 + 4 * t, pol);
     b.q1 = ld_stream_v4(w1 + blk * 16 + 4 * t, pol);
-#pragma unroll
-    for (int v = 0; v < 4; ++v)
-        b.x[v] = arow ? __ldg(reinterpret_cast<const uint4*>(arow + blk * 128 + 32 * t) + v) : make_uint4(0u, 0u, 0u, 0u);
     const int64_t so = slot * role.s_slot + blk;
     b.s0 = i4_scale(role.s, role.s_dtype, so + static_cast<int64_t>(r0) * role.s_row);
     b.s1 = i4_scale(role.s, role.s_dtype, so + static_cast<int64_t>(r1) * role.s_row);
@@ -724,8 +723,14 @@ __device__ __forceinline__ void i4_load(I4Block& b, const I4Role& role, const in
     }
 }
 
+__device__ __forceinline__ void i4_load_x(I4X& b, const __nv_bfloat16* arow, int blk, int t) {
+#pragma unroll
+    for (int v = 0; v < 4; ++v)
+        b.x[v] = arow ? __ldg(reinterpret_cast<const uint4*>(arow + blk * 128 + 32 * t) + v) : make_uint4(0u, 0u, 0u, 0u);
+}
+
 template <bool BF16>
-__device__ __forceinline__ void i4_mma(const I4Block& b, float (&acc)[4]) {
+__device__ __forceinline__ void i4_mma(const I4Rows& b, const I4X& xb, float (&acc)[4]) {
     const uint32_t zb0 = (0x4300u + b.z0) * 0x10001u, zb1 = (0x4300u + b.z1) * 0x10001u;
     const __nv_bfloat162 sp0 = __floats2bfloat162_rn(b.s0, b.s0);
     const __nv_bfloat162 sp1 = __floats2bfloat162_rn(b.s1, b.s1);
@@ -733,8 +738,8 @@ __device__ __forceinline__ void i4_mma(const I4Block& b, float (&acc)[4]) {
     const uint32_t sc1 = *reinterpret_cast<const uint32_t*>(&sp1);
     const uint32_t W0[4] = {b.q0.x, b.q0.y, b.q0.z, b.q0.w};
     const uint32_t W1[4] = {b.q1.x, b.q1.y, b.q1.z, b.q1.w};
-    const uint32_t X[16] = {b.x[0].x, b.x[0].y, b.x[0].z, b.x[0].w, b.x[1].x, b.x[1].y, b.x[1].z, b.x[1].w,
-                            b.x[2].x, b.x[2].y, b.x[2].z, b.x[2].w, b.x[3].x, b.x[3].y, b.x[3].z, b.x[3].w};
+    const uint32_t X[16] = {xb.x[0].x, xb.x[0].y, xb.x[0].z, xb.x[0].w, xb.x[1].x, xb.x[1].y, xb.x[1].z, xb.x[1].w,
+                            xb.x[2].x, xb.x[2].y, xb.x[2].z, xb.x[2].w, xb.x[3].x, xb.x[3].y, xb.x[3].z, xb.x[3].w};
 #pragma unroll
     for (int w = 0; w < 4; ++w) {  // word w: columns 8w..8w+7 of this thread's 32
 #pragma unroll
@@ -744,17 +749,43 @@ __device__ __forceinline__ void i4_mma(const I4Block& b, float (&acc)[4]) {
                                    int4_pair<BF16>(W0[w], 2 * h + 1, zb0, sc0, b.s0),
                                    int4_pair<BF16>(W1[w], 2 * h + 1, zb1, sc1, b.s1)};
             // token columns (2h, 2h+4) and (2h+1, 2h+5): low or high halves of x words 4w+h, 4w+h+2
-            const uint32_t xa = X[4 * w + h], xb = X[4 * w + h + 2];
-            mma_bf16_16816(acc, A, __byte_perm(xa, xb, 0x5410u), __byte_perm(xa, xb, 0x7632u));
+            const uint32_t xa = X[4 * w + h], xc = X[4 * w + h + 2];
+            mma_bf16_16816(acc, A, __byte_perm(xa, xc, 0x5410u), __byte_perm(xa, xc, 0x7632u));
         }
     }
 }
 
-// Epilogue of one cell (one warp): bf16 projections to gu (up) or weighted
-// fp32 partials (down), then, for the last cell of a row tile, the slot sum.
-template <bool DOWN>
-__device__ __forceinline__ void i4_epilogue(const I4GemvArgs& a, const float (&acc)[4], const int4& ids4, int count,
-                                            int tile, int r0, int r1, int groups, int lane, int t) {
+// The row pairs a warp multiplies: one pair for the down projection; for the
+// gate/up projection (GLU) the gate rows g, g + 8 of tile j and the up rows
+// I + g, I + g + 8 of the same j, so that SiLU(gate) * up is formed in the
+// epilogue and no separate SwiGLU pass is needed.
+template <bool GLU>
+struct I4Stage {
+    I4Rows r[GLU ? 2 : 1];
+    I4X x;
+};
+
+struct I4RowPtrs {
+    const int32_t* w0[2];
+    const int32_t* w1[2];
+    int r0[2], r1[2];
+};
+
+template <bool GLU>
+__device__ __forceinline__ void i4_load_stage(I4Stage<GLU>& st, const I4Role& role, const I4RowPtrs& rp,
+                                              const __nv_bfloat16* arow, int slot, int blk, int t, uint64_t pol) {
+#pragma unroll
+    for (int i = 0; i < (GLU ? 2 : 1); ++i)
+        i4_load_rows(st.r[i], role, rp.w0[i], rp.w1[i], slot, rp.r0[i], rp.r1[i], blk, t, pol);
+    i4_load_x(st.x, arow, blk, t);
+}
+
+// Epilogue of one cell (one warp): gate/up -> bf16(bf16(silu(gate)) * up) into
+// the gate half of gu (GLU), or down -> weighted fp32 partials followed, for
+// the last cell of a row tile, by the slot sum.
+template <bool DOWN, bool GLU>
+__device__ __forceinline__ void i4_epilogue(const I4GemvArgs& a, const float (&acc)[2][4], const int4& ids4,
+                                            int count, int tile, const I4RowPtrs& rp, int groups, int lane, int t) {
     const I4Role& role = a.role;
 #pragma unroll
     for (int c = 0; c < 2; ++c) {
@@ -763,12 +794,17 @@ __device__ __forceinline__ void i4_epilogue(const I4GemvArgs& a, const float (&a
         const int pair = group_pair(ids4, col);
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-            const int row = h ? r1 : r0;
-            const float v = __bfloat162float(__float2bfloat16_rn(acc[2 * h + c]));  // projection in bf16
-            if constexpr (DOWN)
+            const int row = h ? rp.r1[0] : rp.r0[0];
+            const float v = __bfloat162float(__float2bfloat16_rn(acc[0][2 * h + c]));  // projection in bf16
+            if constexpr (DOWN) {
                 a.pair_out[static_cast<int64_t>(pair) * role.n + row] = __fmul_rn(v, __ldg(a.wts + pair));
-            else
+            } else if constexpr (GLU) {
+                const float up = __bfloat162float(__float2bfloat16_rn(acc[1][2 * h + c]));
+                const float act = __bfloat162float(__float2bfloat16_rn(v / (1.0f + expf(-v))));
+                a.gu[static_cast<int64_t>(pair) * role.n + row] = __float2bfloat16_rn(act * up);
+            } else {
                 a.gu[static_cast<int64_t>(pair) * role.n + row] = __float2bfloat16_rn(v);
+            }
         }
     }
     if constexpr (DOWN) {
@@ -797,6 +833,20 @@ __device__ __forceinline__ void i4_epilogue(const I4GemvArgs& a, const float (&a
     }
 }
 
+// Row pointers of a cell: tile j of the down rows, or gate tile j plus up tile j.
+template <bool GLU>
+__device__ __forceinline__ I4RowPtrs i4_rows(const I4Role& role, int slot, int tile, int g) {
+    I4RowPtrs rp{};
+#pragma unroll
+    for (int i = 0; i < (GLU ? 2 : 1); ++i) {
+        rp.r0[i] = (i ? role.n / 2 : 0) + tile * 16 + g;
+        rp.r1[i] = rp.r0[i] + 8;
+        rp.w0[i] = role.w + slot * role.w_slot + static_cast<int64_t>(rp.r0[i]) * role.w_row;
+        rp.w1[i] = rp.w0[i] + 8 * role.w_row;
+    }
+    return rp;
+}
+
 // The warps of a CTA form teams of KS (a.ksplit) warps; a team owns one cell
 // (group, 16-row tile) at a time and warp q of the team takes the q-th
 // contiguous share of the K blocks, streaming it with the next block's loads in
@@ -805,14 +855,15 @@ __device__ __forceinline__ void i4_epilogue(const I4GemvArgs& a, const float (&a
 // Used when there are few cells (batch 1): one team of up to 8 warps per CTA.
 template <bool DOWN, bool BF16>
 __global__ void __launch_bounds__(256) int4_gemv_kernel(I4GemvArgs a) {
+    constexpr bool GLU = !DOWN;
     grid_launch_dependents();  // programmatic dependent launch: the next kernel may start its launch
     grid_dependency_wait();    // the previous kernel's results are visible from here
-    __shared__ float4 s_part[8][32];
+    __shared__ float4 s_part[GLU ? 2 : 1][8][32];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const int KS = a.ksplit, teams = (blockDim.x >> 5) / KS, team = warp / KS, q = warp - team * KS;
     const int groups = __ldg(a.num_groups);
     const I4Role& role = a.role;
-    const int tiles = role.n / 16, blocks = role.k / 128;
+    const int tiles = role.n / (GLU ? 32 : 16), blocks = role.k / 128;
     const int per = blocks / KS, b_lo = q * per, b_hi = b_lo + per;
     const uint64_t pol = policy_evict_first();
     const int total = groups * tiles;
@@ -828,36 +879,41 @@ __global__ void __launch_bounds__(256) int4_gemv_kernel(I4GemvArgs a) {
         const __nv_bfloat16* arow =
             my_pair >= 0 ? a.act + static_cast<int64_t>(DOWN ? my_pair : my_pair / a.top_k) * a.act_stride
                          : nullptr;
-        const int r0 = tile * 16 + g, r1 = r0 + 8;
-        const int32_t* w0 = role.w + slot * role.w_slot + static_cast<int64_t>(r0) * role.w_row;
-        const int32_t* w1 = w0 + 8 * role.w_row;
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        const I4RowPtrs rp = i4_rows<GLU>(role, slot, tile, g);
+        float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
         if (live) {
-            I4Block cur, nxt;
-            i4_load(cur, role, w0, w1, arow, slot, r0, r1, b_lo, t, pol);
+            I4Stage<GLU> cur, nxt;
+            i4_load_stage<GLU>(cur, role, rp, arow, slot, b_lo, t, pol);
             for (int blk = b_lo; blk < b_hi; blk += 2) {
-                if (blk + 1 < b_hi) i4_load(nxt, role, w0, w1, arow, slot, r0, r1, blk + 1, t, pol);
-                i4_mma<BF16>(cur, acc);
+                if (blk + 1 < b_hi) i4_load_stage<GLU>(nxt, role, rp, arow, slot, blk + 1, t, pol);
+#pragma unroll
+                for (int i = 0; i < (GLU ? 2 : 1); ++i) i4_mma<BF16>(cur.r[i], cur.x, acc[i]);
                 if (blk + 1 >= b_hi) break;
-                if (blk + 2 < b_hi) i4_load(cur, role, w0, w1, arow, slot, r0, r1, blk + 2, t, pol);
-                i4_mma<BF16>(nxt, acc);
+                if (blk + 2 < b_hi) i4_load_stage<GLU>(cur, role, rp, arow, slot, blk + 2, t, pol);
+#pragma unroll
+                for (int i = 0; i < (GLU ? 2 : 1); ++i) i4_mma<BF16>(nxt.r[i], nxt.x, acc[i]);
             }
         }
         if (KS > 1) {
-            s_part[warp][lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+#pragma unroll
+            for (int i = 0; i < (GLU ? 2 : 1); ++i)
+                s_part[i][warp][lane] = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
             __syncthreads();
             if (q == 0) {
-                acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
-                for (int p = 0; p < KS; ++p) {  // warp (= K) order
-                    const float4 v = s_part[warp + p][lane];
-                    acc[0] += v.x;
-                    acc[1] += v.y;
-                    acc[2] += v.z;
-                    acc[3] += v.w;
+#pragma unroll
+                for (int i = 0; i < (GLU ? 2 : 1); ++i) {
+                    acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+                    for (int p = 0; p < KS; ++p) {  // warp (= K) order
+                        const float4 v = s_part[i][warp + p][lane];
+                        acc[i][0] += v.x;
+                        acc[i][1] += v.y;
+                        acc[i][2] += v.z;
+                        acc[i][3] += v.w;
+                    }
                 }
             }
         }
-        if (q == 0 && live) i4_epilogue<DOWN>(a, acc, ids4, count, tile, r0, r1, groups, lane, t);
+        if (q == 0 && live) i4_epilogue<DOWN, GLU>(a, acc, ids4, count, tile, rp, groups, lane, t);
         if (KS > 1) __syncthreads();  // s_part is reused by the next cell
     }
 }
@@ -866,13 +922,14 @@ __global__ void __launch_bounds__(256) int4_gemv_kernel(I4GemvArgs a) {
 // blocks per round trip.
 template <bool DOWN, bool BF16>
 __global__ void __launch_bounds__(kW8GemvThreads) int4_gemv_wide_kernel(I4GemvArgs a) {
+    constexpr bool GLU = !DOWN;
     grid_launch_dependents();  // programmatic dependent launch: the next kernel may start its launch
     grid_dependency_wait();    // the previous kernel's results are visible from here
     const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const int warps_total = gridDim.x * (kW8GemvThreads / 32);
     const int groups = __ldg(a.num_groups);
     const I4Role& role = a.role;
-    const int tiles = role.n / 16, blocks = role.k / 128;
+    const int tiles = role.n / (GLU ? 32 : 16), blocks = role.k / 128;
     const uint64_t pol = policy_evict_first();
     for (int cell = blockIdx.x * (kW8GemvThreads / 32) + (threadIdx.x >> 5); cell < groups * tiles;
          cell += warps_total) {
@@ -884,38 +941,26 @@ __global__ void __launch_bounds__(kW8GemvThreads) int4_gemv_wide_kernel(I4GemvAr
         const __nv_bfloat16* arow =
             my_pair >= 0 ? a.act + static_cast<int64_t>(DOWN ? my_pair : my_pair / a.top_k) * a.act_stride
                          : nullptr;
-        const int r0 = tile * 16 + g, r1 = r0 + 8;
-        const int32_t* w0 = role.w + slot * role.w_slot + static_cast<int64_t>(r0) * role.w_row;
-        const int32_t* w1 = w0 + 8 * role.w_row;
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        const I4RowPtrs rp = i4_rows<GLU>(role, slot, tile, g);
+        float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
         for (int blk = 0; blk < blocks; blk += 2) {  // blocks is even (K % 256 == 0)
-            I4Block b0, b1;
-            i4_load(b0, role, w0, w1, arow, slot, r0, r1, blk, t, pol);
-            i4_load(b1, role, w0, w1, arow, slot, r0, r1, blk + 1, t, pol);
-            i4_mma<BF16>(b0, acc);
-            i4_mma<BF16>(b1, acc);
+            I4Stage<GLU> s0, s1;
+            i4_load_stage<GLU>(s0, role, rp, arow, slot, blk, t, pol);
+            i4_load_stage<GLU>(s1, role, rp, arow, slot, blk + 1, t, pol);
+#pragma unroll
+            for (int i = 0; i < (GLU ? 2 : 1); ++i) {
+                i4_mma<BF16>(s0.r[i], s0.x, acc[i]);
+                i4_mma<BF16>(s1.r[i], s1.x, acc[i]);
+            }
         }
-        i4_epilogue<DOWN>(a, acc, ids4, count, tile, r0, r1, groups, lane, t);
-    }
-}
-
-// SwiGLU in place: gate half of each gu row <- bf16(bf16(silu(gate)) * up).
-__global__ void __launch_bounds__(256) int4_act_kernel(__nv_bfloat16* gu, int I) {
-    grid_launch_dependents();  // programmatic dependent launch: the next kernel may start its launch
-    grid_dependency_wait();    // the previous kernel's results are visible from here
-    __nv_bfloat16* row = gu + static_cast<int64_t>(blockIdx.x) * 2 * I;
-    for (int j = threadIdx.x; j < I; j += blockDim.x) {
-        const float gt = __bfloat162float(row[j]);
-        const float up = __bfloat162float(row[I + j]);
-        const float act = __bfloat162float(__float2bfloat16_rn(gt / (1.0f + expf(-gt))));
-        row[j] = __float2bfloat16_rn(act * up);
+        i4_epilogue<DOWN, GLU>(a, acc, ids4, count, tile, rp, groups, lane, t);
     }
 }
 
 // Warps per CTA (= K shares per tile): the most that keep the warps within the
 // target and divide the blocks, at most 8.
-int int4_warps(int64_t cells, int blocks) {
-    for (int ks = 8; ks > 1; --ks)
+int int4_warps(int64_t cells, int blocks, int max_ks = 8) {
+    for (int ks = max_ks; ks > 1; --ks)
         if (cells * ks <= kW8TargetWarps && blocks % ks == 0) return ks;
     return 1;
 }
@@ -948,15 +993,14 @@ cudaError_t int4_launch_fmt(const DramaB200Int4Bank& b, const void* x, int64_t t
     up.act_stride = H;
     up.top_k = top_k;
     up.gu = ws.up;
-    const int64_t up_cells = gmax * (2 * I / 16);
-    up.ksplit = int4_warps(up_cells, H / 128);
+    const int64_t up_cells = gmax * (I / 16);  // a cell is gate tile j with up tile j
+    // two row pairs per warp: teams of at most 4 warps (one wave), and only while the cells alone are few
+    up.ksplit = up_cells * 8 <= kW8TargetWarps ? int4_warps(up_cells, H / 128, 4) : 1;
     cudaError_t err =
         up.ksplit > 1
             ? launch_pdl(int4_gemv_kernel<false, BF16>, dim3(grid_cells(up_cells, up.ksplit)),
                          dim3(team_threads(up.ksplit)), 0, s, up)
             : launch_pdl(int4_gemv_wide_kernel<false, BF16>, dim3(grid_wide(up_cells)), dim3(kW8GemvThreads), 0, s, up);
-    if (err != cudaSuccess) return err;
-    err = launch_pdl(int4_act_kernel, dim3(static_cast<unsigned>(P)), dim3(256), 0, s, ws.up, I);
     if (err != cudaSuccess) return err;
     I4GemvArgs dn{};
     dn.role = I4Role{b.w2, b.w2_scale, b.w2_zeros, b.w2_slot_stride, b.w2_row_stride, b.w2_scale_slot_stride,
