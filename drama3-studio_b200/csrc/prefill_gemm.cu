@@ -56,8 +56,10 @@ __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r
                  : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
                  : "r"(addr));
 }
+// The down GEMM (MODE 1) fits two CTAs per SM (registers and shared memory), so
+// it runs twice as many warps to hide the ldmatrix / cp.async latency.
 template <int MODE>
-__global__ void __launch_bounds__(kPfThreads, 1) prefill_gemm_kernel(PrefillArgs a) {
+__global__ void __launch_bounds__(kPfThreads, MODE == 1 ? 2 : 1) prefill_gemm_kernel(PrefillArgs a) {
     extern __shared__ __align__(16) uint8_t smem_pf[];
     __shared__ int s_prefix[1025];
     constexpr int NT = MODE == 0 ? 8 : 4;        // n8 tiles per warp (gate 4 + up 4, or 4)
@@ -305,7 +307,7 @@ cudaError_t prefill_launch(const DramaB200Fp8Bank& bank, const void* x, int64_t 
     if (err != cudaSuccess) return err;
     a.x = ws.h;
     a.out = ws.down;
-    prefill_gemm_kernel<1><<<sm_count, kPfThreads, kPfSmem, s>>>(a);
+    prefill_gemm_kernel<1><<<2 * sm_count, kPfThreads, kPfSmem, s>>>(a);
     err = cudaGetLastError();
     if (err != cudaSuccess) return err;
     const int64_t chunks = tokens * (bank.hidden / 8);
