@@ -254,7 +254,6 @@ cudaError_t w8a8_decode_launch(const DramaB200W8a8Bank& bank, const void* x, int
 // Shared expert + gate fused with the routed combine (shared_expert.cu).
 constexpr int kMaxSharedTokens = 4096;
 struct SharedWorkspace {
-    __nv_bfloat16* gu;        // [T][2I] gate/up projections
     __nv_bfloat16* h;         // [T][I] SwiGLU rows
     float* gate_s;            // [T] bf16-rounded sigmoid gate
 };

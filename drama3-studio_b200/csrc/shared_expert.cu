@@ -8,9 +8,10 @@
 //   t = bf16(routed + shared);  out = bf16(after_mixer + t)
 // (routed and after_mixer are optional; without them out = shared or t.)
 //
-// Launches (chained by programmatic dependent launch): gate/up GEMV -> per-token
-// SwiGLU and gate scalar -> down GEMV whose
-// epilogue applies the gate, the routed sum and the residual. The GEMVs stream
+// Launches (chained by programmatic dependent launch): the gate/up GEMV, whose
+// epilogue forms the SwiGLU rows and (one extra cell per token group) the
+// sigmoid gate scalars, then the down GEMV, whose epilogue applies the gate,
+// the routed sum and the residual. The GEMVs stream
 // the dense bf16 weights once per group of <= 8 tokens through
 // mma.m16n8k16 bf16 fragments (tokens as N). When the tiles alone would leave
 // the GPU idle (batch 1) a CTA of up to 16 warps shares one tile, each warp a
@@ -28,29 +29,36 @@ constexpr int kShTarget = 4736;  // 148 SMs x 32 warps: the split-K target
 constexpr int kShTok = 8;        // tokens per MMA N tile
 
 struct ShGemvArgs {
-    const __nv_bfloat16* w0;  // rows [0, n0) (gate_proj, or down_proj)
-    const __nv_bfloat16* w1;  // rows [n0, 2 n0) (up_proj), or NULL
+    const __nv_bfloat16* w0;  // gate_proj [I][H] (up) or down_proj [H][I] (down)
+    const __nv_bfloat16* w1;  // up_proj [I][H] (up) or NULL
+    const __nv_bfloat16* gate_weight;  // up: the [H] shared_expert_gate row
     int64_t w0_row, w1_row;   // elements
-    int n, k;                 // output rows (2 Is for gate/up, H for down), contraction length
-    int n0;
+    int n, k;                 // output rows (I for up: SwiGLU rows; H for down), contraction length
     const __nv_bfloat16* act; // [T][k]
     int64_t tokens;
     int ksplit;               // warps per CTA sharing one cell (K parts), 1: one cell per warp
     // epilogue
-    __nv_bfloat16* gu;        // gate/up: [T][2 Is] bf16
-    const float* gate_s;      // down: [T] bf16-rounded sigmoid gate
+    __nv_bfloat16* h;         // up: [T][I] SwiGLU rows
+    float* gate_s;            // up writes, down reads: [T] bf16-rounded sigmoid gate
     const __nv_bfloat16* routed;    // down: [T][H] or NULL
     const __nv_bfloat16* residual;  // down: [T][H] or NULL
     __nv_bfloat16* out;       // down: [T][H]
 };
 
+// Up (GLU): a cell's 16 MMA rows are gate rows 8j..8j+7 and up rows 8j..8j+7,
+// so a thread holds gate and up of the same row and the epilogue forms
+// bf16(bf16(silu(gate)) * up) itself; one extra cell per token group (tile
+// I/8) multiplies the gate vector and writes the sigmoid gate scalars.
+// Down: a cell is one 16-row tile of H; its epilogue applies the gate, the
+// routed sum and the residual.
 template <bool DOWN>
 __global__ void __launch_bounds__(512) shared_gemv_kernel(ShGemvArgs a) {
+    constexpr bool GLU = !DOWN;
     grid_launch_dependents();  // programmatic dependent launch
     grid_dependency_wait();
     __shared__ float4 s_part[16][32];
     const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3, warp = threadIdx.x >> 5;
-    const int tiles = a.n / 16;
+    const int tiles = GLU ? a.n / 8 + 1 : a.n / 16;
     const int tgroups = static_cast<int>((a.tokens + kShTok - 1) / kShTok);
     const int spans_per = a.k / 32 / a.ksplit;  // 32-column spans
     const uint64_t pol = policy_evict_first();
@@ -62,11 +70,13 @@ __global__ void __launch_bounds__(512) shared_gemv_kernel(ShGemvArgs a) {
     for (int cell = first; cell < tgroups * tiles; cell += step) {
         const int kpart = team ? warp : 0;
         const int tg = cell / tiles, tile = cell - tg * tiles;
+        const bool gate_cell = GLU && tile == a.n / 8;
         const int64_t tok = static_cast<int64_t>(tg) * kShTok + g;
         const __nv_bfloat16* xrow = tok < a.tokens ? a.act + tok * a.k : nullptr;
-        const int r0 = tile * 16 + g, r1 = r0 + 8;
-        const __nv_bfloat16* w0 = r0 < a.n0 ? a.w0 + r0 * a.w0_row : a.w1 + (r0 - a.n0) * a.w1_row;
-        const __nv_bfloat16* w1 = r1 < a.n0 ? a.w0 + r1 * a.w0_row : a.w1 + (r1 - a.n0) * a.w1_row;
+        // MMA rows g and g + 8 of this thread
+        const int row = GLU ? tile * 8 + g : tile * 16 + g;
+        const __nv_bfloat16* w0 = gate_cell ? a.gate_weight : a.w0 + row * a.w0_row;
+        const __nv_bfloat16* w1 = gate_cell ? a.gate_weight : GLU ? a.w1 + row * a.w1_row : a.w0 + (row + 8) * a.w0_row;
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
         const int sp0 = kpart * spans_per;
         for (int sp = sp0; sp < sp0 + spans_per; sp += 4) {
@@ -102,67 +112,33 @@ __global__ void __launch_bounds__(512) shared_gemv_kernel(ShGemvArgs a) {
             }
         }
         if (!team || warp == 0) {
-        // acc[0..1]: row r0, tokens 2t, 2t+1 of the group; acc[2..3]: row r1
+            // acc[0..1]: MMA row g, tokens 2t, 2t+1 of the group; acc[2..3]: MMA row g + 8
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-            const int64_t tk = static_cast<int64_t>(tg) * kShTok + 2 * t + c;
-            if (tk >= a.tokens) continue;
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const int row = h ? r1 : r0;
-                const float v = __bfloat162float(__float2bfloat16_rn(acc[2 * h + c]));  // F.linear in bf16
-                if constexpr (DOWN) {
-                    const int64_t o = tk * a.n + row;
-                    float y = __bfloat162float(__float2bfloat16_rn(a.gate_s[tk] * v));  // shared_gate * shared
-                    if (a.routed) y = __bfloat162float(__float2bfloat16_rn(__bfloat162float(a.routed[o]) + y));
-                    if (a.residual) y = __bfloat162float(a.residual[o]) + y;
-                    a.out[o] = __float2bfloat16_rn(y);
+            for (int c = 0; c < 2; ++c) {
+                const int64_t tk = static_cast<int64_t>(tg) * kShTok + 2 * t + c;
+                if (tk >= a.tokens) continue;
+                const float v0 = __bfloat162float(__float2bfloat16_rn(acc[c]));      // F.linear in bf16
+                const float v1 = __bfloat162float(__float2bfloat16_rn(acc[2 + c]));
+                if constexpr (GLU) {
+                    if (gate_cell) {  // every MMA row holds x . g; row 0 writes the gate scalars
+                        if (g == 0) a.gate_s[tk] = __bfloat162float(__float2bfloat16_rn(1.0f / (1.0f + expf(-v0))));
+                    } else {          // gate row `row` and up row `row`
+                        const float act = __bfloat162float(__float2bfloat16_rn(v0 / (1.0f + expf(-v0))));
+                        a.h[tk * a.n + row] = __float2bfloat16_rn(act * v1);
+                    }
                 } else {
-                    a.gu[tk * a.n + row] = __float2bfloat16_rn(v);
+#pragma unroll
+                    for (int hh = 0; hh < 2; ++hh) {
+                        const int64_t o = tk * a.n + row + 8 * hh;
+                        float y = __bfloat162float(__float2bfloat16_rn(a.gate_s[tk] * (hh ? v1 : v0)));
+                        if (a.routed) y = __bfloat162float(__float2bfloat16_rn(__bfloat162float(a.routed[o]) + y));
+                        if (a.residual) y = __bfloat162float(a.residual[o]) + y;
+                        a.out[o] = __float2bfloat16_rn(y);
+                    }
                 }
             }
         }
-        }
         if (team) __syncthreads();  // s_part is reused by the next cell
-    }
-}
-
-// Per token: h = bf16(bf16(silu(gate)) * up) and s = bf16(sigmoid(bf16(x . g))).
-__global__ void __launch_bounds__(256) shared_act_kernel(const __nv_bfloat16* x, const __nv_bfloat16* gate_w, int H,
-                                                          const __nv_bfloat16* gu, int I, __nv_bfloat16* h,
-                                                          float* gate_s) {
-    grid_launch_dependents();  // programmatic dependent launch
-    grid_dependency_wait();
-    __shared__ float s_red[8];
-    const int64_t tok = blockIdx.x;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    float dot = 0.f;
-    for (int c = tid * 8; c < H; c += blockDim.x * 8) {  // 8 columns per 16-byte load
-        const uint4 xv = __ldg(reinterpret_cast<const uint4*>(x + tok * H + c));
-        const uint4 gv = __ldg(reinterpret_cast<const uint4*>(gate_w + c));
-        const uint32_t xs[4] = {xv.x, xv.y, xv.z, xv.w}, gs[4] = {gv.x, gv.y, gv.z, gv.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            dot = fmaf(__uint_as_float(xs[i] << 16), __uint_as_float(gs[i] << 16), dot);
-            dot = fmaf(__uint_as_float(xs[i] & 0xffff0000u), __uint_as_float(gs[i] & 0xffff0000u), dot);
-        }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-    if (lane == 0) s_red[warp] = dot;
-    __syncthreads();
-    if (tid == 0) {
-        float sum = 0.f;
-        for (int w = 0; w < 8; ++w) sum += s_red[w];
-        const float logit = __bfloat162float(__float2bfloat16_rn(sum));
-        gate_s[tok] = __bfloat162float(__float2bfloat16_rn(1.0f / (1.0f + expf(-logit))));
-    }
-#pragma unroll 4
-    for (int j = tid; j < I; j += blockDim.x) {
-        const float gt = __bfloat162float(gu[tok * 2 * I + j]);
-        const float up = __bfloat162float(gu[tok * 2 * I + I + j]);
-        const float act = __bfloat162float(__float2bfloat16_rn(gt / (1.0f + expf(-gt))));
-        h[tok * I + j] = __float2bfloat16_rn(act * up);
     }
 }
 
@@ -184,7 +160,6 @@ size_t shared_expert_workspace_layout(int64_t tokens, int hidden, int inter, cha
         return p;
     };
     SharedWorkspace w{};
-    w.gu = reinterpret_cast<__nv_bfloat16*>(take(static_cast<size_t>(tokens) * 2 * inter * 2));
     w.h = reinterpret_cast<__nv_bfloat16*>(take(static_cast<size_t>(tokens) * inter * 2));
     w.gate_s = reinterpret_cast<float*>(take(tokens * 4));
     if (ws) *ws = w;
@@ -207,28 +182,25 @@ cudaError_t shared_expert_launch(const DramaB200SharedExpert& m, const void* x, 
     ShGemvArgs up{};
     up.w0 = static_cast<const __nv_bfloat16*>(m.gate_proj);
     up.w1 = static_cast<const __nv_bfloat16*>(m.up_proj);
+    up.gate_weight = static_cast<const __nv_bfloat16*>(m.gate_weight);
     up.w0_row = m.gate_row_stride;
     up.w1_row = m.up_row_stride;
-    up.n = 2 * I;
-    up.n0 = I;
+    up.n = I;
     up.k = H;
     up.act = static_cast<const __nv_bfloat16*>(x);
     up.tokens = tokens;
-    up.ksplit = sh_split(tg * (2 * I / 16), H / 32);
-    up.gu = ws.gu;
-    cudaError_t err = launch_pdl(shared_gemv_kernel<false>, dim3(grid_cells(tg * (2 * I / 16), up.ksplit)),
+    const int64_t up_cells = tg * (I / 8 + 1);  // + the gate-scalar cell of each token group
+    up.ksplit = sh_split(up_cells, H / 32);
+    up.h = ws.h;
+    up.gate_s = ws.gate_s;
+    cudaError_t err = launch_pdl(shared_gemv_kernel<false>, dim3(grid_cells(up_cells, up.ksplit)),
                                  dim3(cta_threads(up.ksplit)), 0, s, up);
-    if (err != cudaSuccess) return err;
-    err = launch_pdl(shared_act_kernel, dim3(static_cast<unsigned>(tokens)), dim3(256), 0, s,
-                     static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(m.gate_weight), H,
-                     static_cast<const __nv_bfloat16*>(ws.gu), I, ws.h, ws.gate_s);
     if (err != cudaSuccess) return err;
     ShGemvArgs dn{};
     dn.w0 = static_cast<const __nv_bfloat16*>(m.down_proj);
     dn.w1 = nullptr;
     dn.w0_row = m.down_row_stride;
     dn.n = H;
-    dn.n0 = H;
     dn.k = I;
     dn.act = ws.h;
     dn.tokens = tokens;
