@@ -4,7 +4,7 @@
 (src/drama_low_vram/backbone_graph.py:327-337) compute, per layer,
 ``shared = sigmoid(shared_expert_gate(x)) * shared_expert(x)`` with bf16 torch
 modules and then ``after_mixer + (expert_output + shared)``. ``SharedExpertB200``
-does both in three launches on the sm_100a kernels of ``shared_expert.cu``
+does both in two launches on the sm_100a kernels of ``shared_expert.cu``
 (``drama_b200_shared_expert``): the dense bf16 weights are streamed once per
 group of up to 8 tokens, and the down projection's epilogue applies the gate,
 adds the routed output and the residual, so no intermediate [T, H] tensor is
