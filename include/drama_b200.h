@@ -133,6 +133,11 @@ typedef struct DramaB200Int4Bank {
  * pair_out [tokens, H] fp32 receives the weighted partials. Either output may
  * be NULL but not both. Weight bytes are read once per (slot, <=8 tokens).
  * pairs = tokens*top_k <= 4096, slots <= 1024.
+ * drama_b200_int4_decode with bfloat16 rows and H, I multiples of 256 runs the
+ * grouped schedule of the W8A8 entry below, with the weights dequantised per
+ * element to bf16 as the reference's kernel does (quantized_kernels.py:139-147:
+ * bf16((code - zp) * scale)) and bf16 MMAs; other rows take the f16 path with
+ * exact levels and per-block scales.
  * ------------------------------------------------------------------------- */
 DRAMA_B200_API size_t drama_b200_decode_workspace_bytes(int64_t tokens, int top_k, int hidden,
                                                         int intermediate);
