@@ -981,7 +981,7 @@ cudaError_t int4_launch_fmt(const DramaB200Int4Bank& b, const void* x, int64_t t
     auto grid_cells = [&](int64_t cells, int ks) {
         const int teams = ks > 1 ? 1 : 4;
         const int64_t ctas = (cells + teams - 1) / teams;
-        const int64_t cap = static_cast<int64_t>(sm_count) * (ks > 1 ? 4 : 8);
+        const int64_t cap = static_cast<int64_t>(sm_count) * (ks > 1 ? 32 / ks : 8);  // up to 32 warps per SM
         return static_cast<unsigned>(ctas < 1 ? 1 : (ctas > cap ? cap : ctas));
     };
     I4GemvArgs up{};
