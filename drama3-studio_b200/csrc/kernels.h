@@ -233,7 +233,7 @@ struct W8a8Workspace {
     int4* g_rec;              // [P][2] group records (write_group layout)
     int8_t* xq;               // [T][H] rotated, quantised token rows
     float* xs;                // [T]
-    __nv_bfloat16* up;        // [P][2I] gate/up projections (bf16)
+    __nv_bfloat16* up;        // [P][I] SwiGLU rows (bf16); INT4 decode: [P][2I] gate/up
     int8_t* hq;               // [P][I] rotated, quantised SwiGLU rows
     float* hs;                // [P]
     float* wts;               // [P] route weights as fp32

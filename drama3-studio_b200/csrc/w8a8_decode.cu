@@ -20,15 +20,17 @@
 //            a column's result does not depend on its group, so any grouping
 //            gives the same bits); CTAs 1..T rotate and quantise one token row
 //            each;
-//   gemv   : gate/up projections. A cell is (group, 16-row tile): a warp
+//   gemv   : gate/up projections. A cell is (group, 8 gate rows j..j+7 in
+//            MMA rows 0-7 and their 8 up rows in MMA rows 8-15): a warp
 //            streams the tile's weights with 16-byte loads, dequantises them
 //            in registers into mma.m16n8k32 s8 fragments whose N dimension
 //            holds the group's tokens (weights read once per group). When
 //            there are too few cells to occupy the GPU (batch 1), a CTA of up
 //            to 8 warps shares one cell, each warp a contiguous part of K, and
 //            warp 0 adds the int32 sums from shared memory (exact in any
-//            order) and applies the epilogue;
-//   rotate : SwiGLU rows (bf16(bf16(silu(gate)) * up)) -> int8 + scale;
+//            order) and applies the epilogue, which writes the SwiGLU rows
+//            bf16(bf16(silu(gate)) * up) [P][I];
+//   rotate : SwiGLU rows -> int8 + scale;
 //   gemv   : down projections, rounded to bf16 and weighted in fp32; the
 //            warp that finishes the last cell of a 16-row tile of H sums the
 //            route slots of those rows in slot order in fp32 (the combine).
@@ -121,9 +123,7 @@ __device__ __forceinline__ uint32_t grid_byte(float level, float rel) {
 // ---------------------------------------------------------------------------
 __constant__ double kH4[4][4] = {{1, 1, 1, -1}, {1, 1, -1, 1}, {1, -1, 1, 1}, {-1, 1, 1, 1}};
 
-// ACT = false: row = bf16 [K]; ACT = true: row = bf16 gate/up [2K] and the
-// rotated row is bf16(bf16(silu(gate)) * up). s_v: blockDim doubles; s_row: K floats.
-template <bool ACT>
+// row = bf16 [K]. s_v: blockDim doubles; s_row: K floats.
 __device__ void rotate_row(const __nv_bfloat16* row, int K, int8_t* q, float* qs, double* s_v, float* s_row) {
     __shared__ float s_red[32];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nthr = blockDim.x;
@@ -134,16 +134,7 @@ __device__ void rotate_row(const __nv_bfloat16* row, int K, int8_t* q, float* qs
         const int col = c0 + tid;
         const bool live = col < K;  // K and nthr are multiples of 256: whole chunks are live or idle
         if (live) {
-            float x;
-            if (ACT) {
-                const float g = __bfloat162float(row[col]);
-                const float u = __bfloat162float(row[K + col]);
-                const float act = __bfloat162float(__float2bfloat16_rn(g / (1.0f + expf(-g))));
-                x = __bfloat162float(__float2bfloat16_rn(act * u));
-            } else {
-                x = __bfloat162float(row[col]);
-            }
-            v[j] = static_cast<double>(x);
+            v[j] = static_cast<double>(__bfloat162float(row[col]));
         }
         __syncthreads();
 #pragma unroll
@@ -227,7 +218,7 @@ __global__ void __launch_bounds__(1024) w8a8_prep_kernel(W8PrepArgs a) {
         double* s_v = reinterpret_cast<double*>(smem_w8prep);
         float* s_row = reinterpret_cast<float*>(s_v + blockDim.x);
         const int64_t t = blockIdx.x - 1;
-        rotate_row<false>(a.x + t * a.hidden, a.hidden, a.ws.xq + t * a.hidden, a.ws.xs + t, s_v, s_row);
+        rotate_row(a.x + t * a.hidden, a.hidden, a.ws.xq + t * a.hidden, a.ws.xs + t, s_v, s_row);
         return;
     }
     int* smem = reinterpret_cast<int*>(smem_w8prep);
@@ -330,7 +321,7 @@ __global__ void __launch_bounds__(1024) w8a8_act_kernel(const __nv_bfloat16* up,
     double* s_v = reinterpret_cast<double*>(smem_w8act);
     float* s_row = reinterpret_cast<float*>(s_v + blockDim.x);
     const int64_t p = blockIdx.x;
-    rotate_row<true>(up + p * 2 * I, I, hq + p * I, hs + p, s_v, s_row);
+    rotate_row(up + p * I, I, hq + p * I, hs + p, s_v, s_row);
 }
 
 // ---------------------------------------------------------------------------
@@ -351,7 +342,7 @@ struct W8GemvArgs {
     const float* act_scale;   // [rows]
     int top_k;                // up: activation row = pair / top_k; down: row = pair
     int ksplit;               // K parts per tile = warps per CTA when > 1 (spans divisible by ksplit * kW8Unroll)
-    __nv_bfloat16* up_out;    // up: [P][n]
+    __nv_bfloat16* up_out;    // up: [P][n / 2] SwiGLU rows
     float* pair_out;          // down: [P][n]
     const float* wts;         // down: [P]
     int32_t* cmb_cnt;         // down: [n/16] finished cells per row tile
@@ -447,6 +438,9 @@ __global__ void __launch_bounds__(256) w8a8_gemv_kernel(W8GemvArgs a) {
     const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3, warp = threadIdx.x >> 5;
     const int groups = __ldg(a.num_groups);
     const W8Role& role = a.role;
+    // up: cell j's MMA rows g are gate rows 8j + g and rows g + 8 the up rows of the same j, so the epilogue
+    // forms the SwiGLU rows; down: cell j is rows 16j..16j+15. Either way 16 weight rows per cell.
+    constexpr bool GLU = !DOWN;
     const int tiles = role.n / 16, spans_per = role.k / 64 / a.ksplit;
     const uint64_t pol = policy_evict_first();
     // a.ksplit > 1: the CTA's a.ksplit warps share one cell (warp = K part) and add their int32 sums in
@@ -463,11 +457,12 @@ __global__ void __launch_bounds__(256) w8a8_gemv_kernel(W8GemvArgs a) {
         const int my_pair = g < count ? group_pair(ids4, g) : -1;
         const int8_t* arow =
             my_pair >= 0 ? a.act + static_cast<int64_t>(DOWN ? my_pair : my_pair / a.top_k) * role.k : nullptr;
-        const int r0 = tile * 16 + g;
+        const int r0 = GLU ? tile * 8 + g : tile * 16 + g;
+        const int r1 = GLU ? role.n / 2 + r0 : r0 + 8;
         const uint8_t* w0 = role.w + slot * role.w_slot + static_cast<int64_t>(r0) * role.w_row;
-        const uint8_t* w1 = w0 + 8 * role.w_row;
+        const uint8_t* w1 = role.w + slot * role.w_slot + static_cast<int64_t>(r1) * role.w_row;
         const uint8_t* s0 = role.s + slot * role.s_slot + static_cast<int64_t>(r0) * role.s_row;
-        const uint8_t* s1 = s0 + 8 * role.s_row;
+        const uint8_t* s1 = role.s + slot * role.s_slot + static_cast<int64_t>(r1) * role.s_row;
         float cb = 0.0f;
         if constexpr (MODE == 3)
             cb = __ldg(reinterpret_cast<const float*>(role.s + slot * role.s_slot + (lane & 15) * role.s_row +
@@ -508,25 +503,26 @@ __global__ void __launch_bounds__(256) w8a8_gemv_kernel(W8GemvArgs a) {
                 }
         }
         if (!team || warp == 0) {
-            // epilogue: acc[0..1] row r0, token columns 2t, 2t+1; acc[2..3] row r0 + 8
-            const float sb0 = channel_scale<MODE>(role, slot, r0), sb1 = channel_scale<MODE>(role, slot, r0 + 8);
+            // epilogue: acc[0..1] row r0, token columns 2t, 2t+1; acc[2..3] row r1
+            const float sb0 = channel_scale<MODE>(role, slot, r0), sb1 = channel_scale<MODE>(role, slot, r1);
 #pragma unroll
             for (int c = 0; c < 2; ++c) {
                 const int col = 2 * t + c;
                 if (col >= count) continue;
                 const int pair = group_pair(ids4, col);
                 const float sa = __ldg(a.act_scale + (DOWN ? pair : pair / a.top_k));
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int row = r0 + 8 * h;
-                    const float v = __fmul_rn(__fmul_rn(__int2float_rn(acc[2 * h + c]), sa), h ? sb1 : sb0);
-                    if constexpr (DOWN) {
-                        const float rounded = __bfloat162float(__float2bfloat16_rn(v));
-                        a.pair_out[static_cast<int64_t>(pair) * role.n + row] =
-                            __fmul_rn(rounded, __ldg(a.wts + pair));
-                    } else {
-                        a.up_out[static_cast<int64_t>(pair) * role.n + row] = __float2bfloat16_rn(v);
-                    }
+                // projections rounded to bf16 (the reference kernel's output type)
+                const float v0 = __bfloat162float(
+                    __float2bfloat16_rn(__fmul_rn(__fmul_rn(__int2float_rn(acc[c]), sa), sb0)));
+                const float v1 = __bfloat162float(
+                    __float2bfloat16_rn(__fmul_rn(__fmul_rn(__int2float_rn(acc[2 + c]), sa), sb1)));
+                if constexpr (DOWN) {
+                    const float w = __ldg(a.wts + pair);
+                    a.pair_out[static_cast<int64_t>(pair) * role.n + r0] = __fmul_rn(v0, w);
+                    a.pair_out[static_cast<int64_t>(pair) * role.n + r1] = __fmul_rn(v1, w);
+                } else {  // bf16(bf16(silu(gate)) * up) of row r0
+                    const float act = __bfloat162float(__float2bfloat16_rn(v0 / (1.0f + expf(-v0))));
+                    a.up_out[static_cast<int64_t>(pair) * (role.n / 2) + r0] = __float2bfloat16_rn(act * v1);
                 }
             }
             if constexpr (DOWN) {
@@ -593,7 +589,7 @@ cudaError_t launch_mode(const DramaB200W8a8Bank& b, int64_t tokens, int top_k, v
     up.act = ws.xq;
     up.act_scale = ws.xs;
     up.top_k = top_k;
-    up.ksplit = split_for(gmax * (2 * I / 16), H / 64);
+    up.ksplit = split_for(gmax * (2 * I / 16), H / 64);  // a cell: 8 gate rows and their 8 up rows
     up.up_out = ws.up;
     const dim3 up_grid(grid_cells(gmax * (2 * I / 16), up.ksplit)), up_block(cta_threads(up.ksplit));
     cudaError_t err = (H / 64 / up.ksplit) % 8 == 0
