@@ -379,8 +379,14 @@ __device__ __forceinline__ void load_span(SpanRaw<MODE>& raw, const uint8_t* wro
 // to +-127 before rounding equals rounding before clamping (the bounds are
 // integers); adding 1536 rounds to the nearest even integer (the f16 spacing
 // in [1024, 2048) is 1), and the low byte of 0x6400 + 512 + v is v mod 256.
+//
+// Mode 3 looks the grid values up in a table of the slot's codebook: row r (an
+// FP8 relative-scale byte) holds grid_byte(codebook[c], rel(r)) for the codes
+// c = 0..15, built with the same grid_byte, so the lookup is exact. Four
+// columns take three byte permutes: the low three code bits select from codes
+// 0-7 and from codes 8-15, bit 3 picks between the two.
 template <int MODE>
-__device__ __forceinline__ void dequant_span(const SpanRaw<MODE>& raw, float cb, uint32_t (&o)[4]) {
+__device__ __forceinline__ void dequant_span(const SpanRaw<MODE>& raw, const uint4* tab, uint32_t (&o)[4]) {
     if constexpr (MODE == 1) {
         o[0] = raw.v.x;
         o[1] = raw.v.y;
@@ -402,19 +408,24 @@ __device__ __forceinline__ void dequant_span(const SpanRaw<MODE>& raw, float cb,
 #pragma unroll
         for (int w = 0; w < 4; ++w) o[w] = __byte_perm(r[2 * w], r[2 * w + 1], 0x6420u);
     } else {
-        const float rel = fp8_to_float(raw.rel);
-        const uint64_t lo = (static_cast<uint64_t>(raw.lo.y) << 32) | raw.lo.x;
+        const uint4 T = tab[raw.rel];  // grid bytes of codes 0-15 at this relative scale
 #pragma unroll
-        for (int w = 0; w < 4; ++w) {
-            uint32_t q[4];
-#pragma unroll
-            for (int b = 0; b < 4; ++b) {
-                const int code = static_cast<int>((lo >> (4 * (4 * w + b))) & 15u);
-                q[b] = grid_byte(__shfl_sync(0xffffffffu, cb, code), rel);
-            }
-            o[w] = __byte_perm(__byte_perm(q[0], q[1], 0x0040u), __byte_perm(q[2], q[3], 0x0040u), 0x5410u);
+        for (int h = 0; h < 2; ++h) {
+            const uint32_t word = h ? raw.lo.y : raw.lo.x;  // columns 8h..8h+7, nibble j = column 8h + j
+            const uint32_t idx = word & 0x77777777u;
+            const uint32_t pick = ((word >> 1) & 0x44444444u) | 0x32103210u;  // selector + 4 where code >= 8
+            o[2 * h] = __byte_perm(__byte_perm(T.x, T.y, idx), __byte_perm(T.z, T.w, idx), pick);
+            o[2 * h + 1] =
+                __byte_perm(__byte_perm(T.x, T.y, idx >> 16), __byte_perm(T.z, T.w, idx >> 16), pick >> 16);
         }
     }
+}
+
+// Mode 3: the grid table of one slot (256 relative-scale bytes x 16 codes), entries
+// e = first, first + n, ... written by threads whose code (e & 15) matches their
+// codebook value cb (n and first are such that e & 15 == lane & 15).
+__device__ __forceinline__ void build_grid_table(uint8_t* tab, float cb, int first, int n) {
+    for (int e = first; e < 4096; e += n) tab[e] = static_cast<uint8_t>(grid_byte(cb, fp8_to_float(e >> 4)));
 }
 
 __device__ __forceinline__ int group_pair(const int4& ids4, int c) {
@@ -435,6 +446,8 @@ __global__ void __launch_bounds__(256) w8a8_gemv_kernel(W8GemvArgs a) {
     grid_launch_dependents();  // programmatic dependent launch: the next kernel may start its launch
     grid_dependency_wait();    // the previous kernel's results are visible from here
     __shared__ int4 s_part[8][32];
+    extern __shared__ uint4 s_tab[];  // mode 3: grid tables (w8_table_smem bytes)
+    int tab_slot = -1;
     const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3, warp = threadIdx.x >> 5;
     const int groups = __ldg(a.num_groups);
     const W8Role& role = a.role;
@@ -463,10 +476,26 @@ __global__ void __launch_bounds__(256) w8a8_gemv_kernel(W8GemvArgs a) {
         const uint8_t* w1 = role.w + slot * role.w_slot + static_cast<int64_t>(r1) * role.w_row;
         const uint8_t* s0 = role.s + slot * role.s_slot + static_cast<int64_t>(r0) * role.s_row;
         const uint8_t* s1 = role.s + slot * role.s_slot + static_cast<int64_t>(r1) * role.s_row;
-        float cb = 0.0f;
-        if constexpr (MODE == 3)
-            cb = __ldg(reinterpret_cast<const float*>(role.s + slot * role.s_slot + (lane & 15) * role.s_row +
-                                                      role.k / 16 + 4));
+        const uint4* tab = nullptr;
+        if constexpr (MODE == 3) {
+            // the slot's grid table: one per CTA when the warps share a cell, else one per warp
+            uint4* mine = s_tab + (team ? 0 : warp * 256);
+            tab = mine;
+            if (slot != tab_slot) {  // uniform over the threads that share the table
+                tab_slot = slot;
+                const float cb = __ldg(reinterpret_cast<const float*>(
+                    role.s + slot * role.s_slot + (lane & 15) * role.s_row + role.k / 16 + 4));
+                if (team) {
+                    __syncthreads();  // the previous table's readers are done
+                    build_grid_table(reinterpret_cast<uint8_t*>(mine), cb, threadIdx.x, blockDim.x);
+                    __syncthreads();
+                } else {
+                    __syncwarp();
+                    build_grid_table(reinterpret_cast<uint8_t*>(mine), cb, lane, 32);
+                    __syncwarp();
+                }
+            }
+        }
         int acc[4] = {0, 0, 0, 0};
         const int sp_end = (kpart + 1) * spans_per;
         for (int sp = kpart * spans_per; sp < sp_end; sp += U) {
@@ -482,8 +511,8 @@ __global__ void __launch_bounds__(256) w8a8_gemv_kernel(W8GemvArgs a) {
 #pragma unroll
             for (int u = 0; u < U; ++u) {
                 uint32_t A0[4], A1[4];
-                dequant_span<MODE>(raw0[u], cb, A0);
-                dequant_span<MODE>(raw1[u], cb, A1);
+                dequant_span<MODE>(raw0[u], tab, A0);
+                dequant_span<MODE>(raw1[u], tab, A1);
                 const uint32_t a1[4] = {A0[0], A1[0], A0[1], A1[1]};
                 const uint32_t a2[4] = {A0[2], A1[2], A0[3], A1[3]};
                 mma_s8_16832(acc, a1, xb[u].x, xb[u].y);
@@ -564,6 +593,10 @@ int split_for(int64_t cells, int spans) {
     return 1;
 }
 
+// Dynamic shared memory of a W8A8 GEMV launch: mode 3 keeps a 4 KB grid table
+// per CTA (warps sharing a cell) or per warp.
+size_t w8_table_smem(int mode, int ks) { return mode == 3 ? 4096u * (ks > 1 ? 1 : kW8GemvThreads / 32) : 0; }
+
 int rot_threads(int K) { return K < 1024 ? K : 1024; }
 size_t rot_smem(int K) { return static_cast<size_t>(rot_threads(K)) * sizeof(double) + K * sizeof(float); }
 
@@ -593,8 +626,10 @@ cudaError_t launch_mode(const DramaB200W8a8Bank& b, int64_t tokens, int top_k, v
     up.up_out = ws.up;
     const dim3 up_grid(grid_cells(gmax * (2 * I / 16), up.ksplit)), up_block(cta_threads(up.ksplit));
     cudaError_t err = (H / 64 / up.ksplit) % 8 == 0
-                          ? launch_pdl(w8a8_gemv_kernel<MODE, false, 8>, up_grid, up_block, 0, s, up)
-                          : launch_pdl(w8a8_gemv_kernel<MODE, false, 4>, up_grid, up_block, 0, s, up);
+                          ? launch_pdl(w8a8_gemv_kernel<MODE, false, 8>, up_grid, up_block,
+                                       w8_table_smem(MODE, up.ksplit), s, up)
+                          : launch_pdl(w8a8_gemv_kernel<MODE, false, 4>, up_grid, up_block,
+                                       w8_table_smem(MODE, up.ksplit), s, up);
     if (err != cudaSuccess) return err;
     err = launch_pdl(w8a8_act_kernel, dim3(static_cast<unsigned>(P)), dim3(rot_threads(I)), rot_smem(I), s, ws.up, I,
                      ws.hq, ws.hs);
@@ -616,8 +651,10 @@ cudaError_t launch_mode(const DramaB200W8a8Bank& b, int64_t tokens, int top_k, v
     dn.tokens = tokens;
     const dim3 dn_grid(grid_cells(gmax * (H / 16), dn.ksplit)), dn_block(cta_threads(dn.ksplit));
     return (I / 64 / dn.ksplit) % 8 == 0
-               ? launch_pdl(w8a8_gemv_kernel<MODE, true, 8>, dn_grid, dn_block, 0, s, dn)
-               : launch_pdl(w8a8_gemv_kernel<MODE, true, 4>, dn_grid, dn_block, 0, s, dn);
+               ? launch_pdl(w8a8_gemv_kernel<MODE, true, 8>, dn_grid, dn_block, w8_table_smem(MODE, dn.ksplit), s,
+                            dn)
+               : launch_pdl(w8a8_gemv_kernel<MODE, true, 4>, dn_grid, dn_block, w8_table_smem(MODE, dn.ksplit), s,
+                            dn);
 }
 
 // ---------------------------------------------------------------------------
