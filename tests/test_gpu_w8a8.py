@@ -96,3 +96,34 @@ def test_out_of_range_ids_contribute_zero_and_graph_replays_bitwise(cuda_device)
         graph.replay()
         torch.cuda.synchronize()
         assert torch.equal(static.view(torch.int16), eager.view(torch.int16))
+
+
+@pytest.mark.parametrize("mode", [2, 3])
+def test_every_relative_scale_byte(cuda_device, mode):
+    """Every non-NaN FP8 E4M3 relative-scale byte (zero, subnormals, negatives, and values whose grid saturates at
+    +-127) through the W6A8 f16x2 dequantisation and the W4A8 grid table (one table row per byte). The channel
+    scales are powers of two that keep the projections O(1); the integer sums are exact, so a wrong grid value
+    shows up as a changed output, not only as a larger error."""
+    from drama_b200 import synthetic
+    from drama_b200.backend import QuantizedB200Backend
+
+    hidden, inter, experts, tokens, top_k = 512, 256, 4, 3, 2
+    bank = synthetic.w8a8_bank(mode, experts, hidden, inter, seed=80 + mode)
+    usable = np.array([b for b in range(256) if b & 0x7F != 0x7F], dtype=np.uint8)  # 0x7F / 0xFF are NaN
+    for name, k, channel in (("w13", hidden, 2.0 ** -11), ("w2", inter, 2.0 ** -11)):
+        aux = bank[f"{name}_scale_inv"].numpy()  # shares memory with the tensor
+        e, n = aux.shape[:2]
+        cells = np.arange(e * n * (k // 16)).reshape(e, n, k // 16)
+        aux[..., :k // 16] = usable[(cells * 37 + cells // usable.size) % usable.size]
+        aux[..., k // 16:k // 16 + 4] = np.frombuffer(np.float32(channel).tobytes(), dtype=np.uint8)
+    assert all(np.isin(usable, bank[f"{name}_scale_inv"].numpy()[..., :k // 16]).all()
+               for name, k in (("w13", hidden), ("w2", inter)))
+    x = synthetic.hidden_states(tokens, hidden, 81, device=cuda_device)
+    ids, w = synthetic.uniform_routes(tokens, top_k, experts, 82, device=cuda_device)
+    w = w.to(torch.bfloat16)
+    out = QuantizedB200Backend(mode).forward(x, ids, w, _device_bank(bank, cuda_device))
+    torch.cuda.synchronize()
+    ref = R.convrot_forward(np_f32(x), ids.cpu().numpy(), np_f32(w), _np(bank), mode)
+    assert np.isfinite(ref).all() and 0.05 < np.abs(ref).max() < 64
+    assert_parity(np_f32(out), ref, label=f"mode {mode} every relative-scale byte")
+    assert (np_f32(out) == ref).mean() >= 0.9
