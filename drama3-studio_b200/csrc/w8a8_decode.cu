@@ -84,26 +84,22 @@ __device__ __forceinline__ float fp8_to_float(uint32_t byte) {
     return __half2float(__ushort_as_half(static_cast<unsigned short>(h2 & 0xffffu)));
 }
 
-// Packed-half helpers (round-to-nearest, never contracted into an FMA).
+// Packed-half helpers (round-to-nearest; each is one explicit instruction, never contracted).
 __device__ __forceinline__ uint32_t h2_sub(uint32_t a, uint32_t b) {
     uint32_t d;
     asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
     return d;
 }
-__device__ __forceinline__ uint32_t h2_mul(uint32_t a, uint32_t b) {
+__device__ __forceinline__ uint32_t h2_fma(uint32_t a, uint32_t b, uint32_t c) {
     uint32_t d;
-    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
     return d;
 }
-__device__ __forceinline__ uint32_t h2_add(uint32_t a, uint32_t b) {
+// clamp to [1536 - 127, 1536 + 127] = [1409, 1663]
+__device__ __forceinline__ uint32_t h2_clamp_grid(uint32_t a) {
     uint32_t d;
-    asm("add.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-    return d;
-}
-__device__ __forceinline__ uint32_t h2_clamp127(uint32_t a) {
-    uint32_t d;
-    asm("max.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(0xD7F0D7F0u));  // -127
-    asm("min.f16x2 %0, %1, %2;" : "=r"(d) : "r"(d), "r"(0x57F057F0u));  // +127
+    asm("max.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(0x65816581u));  // 1409
+    asm("min.f16x2 %0, %1, %2;" : "=r"(d) : "r"(d), "r"(0x667F667Fu));  // 1663
     return d;
 }
 
@@ -372,13 +368,16 @@ __device__ __forceinline__ void load_span(SpanRaw<MODE>& raw, const uint8_t* wro
 
 // 16 int8 grid values of one row's span slice, as four words (byte j = column 16t + j).
 //
-// Mode 2 runs two columns per instruction in f16x2, exactly: (1024 + code) is
-// built by OR-ing the 6-bit code into 0x6400, minus 1056 gives code - 32; the
-// product with the FP8 relative scale has at most 10 significant bits and lies
-// in [2^-9, 14336], so it is exact in f16 as in the reference's fp32; clamping
-// to +-127 before rounding equals rounding before clamping (the bounds are
-// integers); adding 1536 rounds to the nearest even integer (the f16 spacing
-// in [1024, 2048) is 1), and the low byte of 0x6400 + 512 + v is v mod 256.
+// Mode 2 runs two columns per instruction in f16x2, exactly. The 6-bit codes of
+// a word's 8 columns are assembled bytewise (low nibbles from the code bytes,
+// top bits from the matching nibble of the top-bit word, which one byte permute
+// lines up); (1024 + code) is the code OR-ed into 0x6400, minus 1056 gives
+// level = code - 32. One fused multiply-add level * rel + 1536 rounds the exact
+// value once: where it lies in [1024, 2048) (f16 spacing 1) that is
+// 1536 + rint(level * rel), round half to even as the reference's rint of its
+// (exact) fp32 product. Rounding is monotone, so clamping the sum to
+// [1409, 1663] afterwards equals clamping rint(level * rel) to +-127, and the
+// low byte of 0x6400 + 512 + v is v mod 256.
 //
 // Mode 3 looks the grid values up in a table of the slot's codebook: row r (an
 // FP8 relative-scale byte) holds grid_byte(codebook[c], rel(r)) for the codes
@@ -394,16 +393,21 @@ __device__ __forceinline__ void dequant_span(const SpanRaw<MODE>& raw, const uin
         o[3] = raw.v.w;
     } else if constexpr (MODE == 2) {
         const uint32_t rel2 = e4m3x2_to_f16x2(raw.rel | (raw.rel << 8));
+        const uint32_t hi4 = raw.hi >> 4;
         uint32_t r[8];
 #pragma unroll
-        for (int m = 0; m < 8; ++m) {  // columns 2m, 2m + 1
-            const uint32_t L = m < 4 ? raw.lo.x : raw.lo.y;
-            const int b = m & 3;
-            const uint32_t P = __byte_perm(L, 0u, 0x4040u | b | (b << 8));  // [byte b, 0, byte b, 0]
-            const uint32_t Hs = raw.hi >> (4 * m);                          // top bits of 2m (0-1), 2m+1 (2-3)
-            const uint32_t codes = (P & 0x0000000Fu) | ((P >> 4) & 0x000F0000u) | ((Hs & 3u) << 4) |
-                                   ((Hs & 0xCu) << 18) | 0x64006400u;
-            r[m] = h2_add(h2_clamp127(h2_mul(h2_sub(codes, 0x64206420u), rel2)), 0x66006600u);
+        for (int h = 0; h < 2; ++h) {  // columns 8h..8h+7: pairs m = 4h + b are columns 2m, 2m + 1
+            const uint32_t L = h ? raw.lo.y : raw.lo.x;  // byte b: column 2m low nibble, 2m + 1 high nibble
+            // byte b of X: nibble m of the top-bit word in its low nibble (bits 0-1: column 2m, 2-3: 2m + 1)
+            const uint32_t X = __byte_perm(raw.hi, hi4, h ? 0x7362u : 0x5140u);
+            const uint32_t ce = (L & 0x0F0F0F0Fu) | ((X << 4) & 0x30303030u);         // byte b: code of 2m
+            const uint32_t co = ((L >> 4) & 0x0F0F0F0Fu) | ((X << 2) & 0x30303030u);  // byte b: code of 2m + 1
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+                const uint32_t pair = __byte_perm(ce, co, b | (b << 4) | ((4 + b) << 8) | ((4 + b) << 12));
+                const uint32_t codes = (pair & 0x00FF00FFu) | 0x64006400u;  // f16x2 1024 + code
+                r[4 * h + b] = h2_clamp_grid(h2_fma(h2_sub(codes, 0x64206420u), rel2, 0x66006600u));
+            }
         }
 #pragma unroll
         for (int w = 0; w < 4; ++w) o[w] = __byte_perm(r[2 * w], r[2 * w + 1], 0x6420u);
