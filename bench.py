@@ -370,14 +370,16 @@ def run_ours(args) -> None:
         "data": "synthetic (seeded random-init weights and hidden rows)", "config": config_dict(args, world),
         "hbm_gbs_per_gpu": layer_bytes * args.layers * value / world / 1e9,
         "roofline": {
-            "kernel": "one MoE layer: routed_up_kernel (router + gate/up) + routed_down_kernel (down + combine)",
+            "kernel": ("one MoE layer: decode_layer_kernel (RMSNorm, router, gate/up, down and slot combine in "
+                       "one launch)" if st.launches_per_layer() == 1 else
+                       "one MoE layer: routed_up_kernel (router + gate/up) + routed_down_kernel (down + combine)"),
             "bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
             "frac": achieved / peaks["hbm_gbs"], "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs)",
             "traffic": traffic, "algorithmic_bytes_per_launch": layer_bytes, "launch_ms": layer_ms,
         },
         "e2e": {"value": tokens / (e2e_ms / 1000.0), "unit": "tokens/s",
                 "h2d_bytes_per_step": inputs.numel() * 2, "d2h_bytes_per_step": outputs.numel() * 2},
-        "gpu_launches": args.steps * steps_per_graph * args.layers * 2,
+        "gpu_launches": args.steps * steps_per_graph * args.layers * st.launches_per_layer(),
         "clocks": clocks.summary(),
         "setup_s": {"build": round(build_s, 1), "capture": round(capture_s, 1)},
     }

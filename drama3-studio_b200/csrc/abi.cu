@@ -1,6 +1,8 @@
 // extern "C" entry points: validation first, then launches on the caller's
 // stream. Status/error conventions follow the reference's native ABI v1
 // (native/src/runtime.cpp:278-290: status 0/-1 plus a thread-local message).
+#include <cuda.h>
+
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -99,11 +101,57 @@ int validate_decode_common(const void* x, int x_dtype, int64_t tokens, int top_k
     return 0;
 }
 
+// Validation and argument block of the FP8 decode entry points (with a
+// workspace or with the library's static scratch).
+int prepare_fp8_decode(const DramaB200Fp8Bank* bank, const void* x, int x_dtype, int64_t tokens, int top_k,
+                       const void* ids, int ids_dtype, const void* weights, int weights_dtype, void* out,
+                       float* pair_out, DecodeArgs* out_args) {
+    if (!bank) return fail("bank is required");
+    const DramaB200Fp8Bank& b = *bank;
+    if (validate_decode_common(x, x_dtype, tokens, top_k, ids, ids_dtype, weights, weights_dtype, out, pair_out,
+                               b.hidden, b.intermediate, b.slots))
+        return -1;
+    if (!b.w13 || !b.w13_scale || !b.w2 || !b.w2_scale) return fail("FP8 bank pointers are required");
+    if (!aligned16(b.w13) || !aligned16(b.w2) || b.w13_row_stride % 16 || b.w2_row_stride % 16 ||
+        b.w13_slot_stride % 16 || b.w2_slot_stride % 16)
+        return fail("FP8 weight rows must start on 16-byte boundaries");
+    if (b.w13_row_stride < b.hidden || b.w2_row_stride < b.intermediate ||
+        b.w13_slot_stride < b.w13_row_stride * 2 * b.intermediate ||
+        b.w2_slot_stride < b.w2_row_stride * b.hidden)
+        return fail("FP8 weight strides are smaller than the bank geometry");
+    if (b.w13_scale_row_stride < b.hidden / 128 || b.w2_scale_row_stride < b.intermediate / 128)
+        return fail("FP8 scale strides are smaller than the bank geometry");
+    DecodeArgs& a = *out_args;
+    a = DecodeArgs{};
+    a.format = 0;
+    a.fp8 = b;
+    a.x = x;
+    a.x_dtype = x_dtype;
+    a.tokens = tokens;
+    a.top_k = top_k;
+    a.ids = ids;
+    a.ids_dtype = ids_dtype;
+    a.weights = weights;
+    a.weights_dtype = weights_dtype;
+    a.out = out;
+    a.pair_out = pair_out;
+    a.hidden = b.hidden;
+    a.intermediate = b.intermediate;
+    a.slots = b.slots;
+    return 0;
+}
+
+// Scratch need of a decode call on the current device (0 on failure, with the error set).
+size_t decode_scratch_need(const DecodeArgs& a, int* sms) {
+    if (sm_count_current(sms)) return 0;
+    return decode_workspace_layout(a.tokens, a.top_k, a.hidden, a.intermediate, *sms, 0, nullptr, nullptr);
+}
+
 int finish_decode(DecodeArgs& a, void* workspace, size_t workspace_bytes, void* stream) {
     if (a.tokens == 0) return 0;
     int sms = 0;
-    if (sm_count_current(&sms)) return -1;
-    const size_t need = decode_workspace_layout(a.tokens, a.top_k, a.hidden, a.intermediate, sms, 0, nullptr, nullptr);
+    const size_t need = decode_scratch_need(a, &sms);
+    if (!need) return -1;
     if (!workspace || workspace_bytes < need)
         return fail("decode workspace too small: need %zu bytes, got %zu", need, workspace_bytes);
     if (reinterpret_cast<uintptr_t>(workspace) & 255u) return fail("workspace must be 256-byte aligned");
@@ -180,37 +228,10 @@ size_t drama_b200_decode_status_offset(void) { return 0; }
 int drama_b200_fp8_decode(const DramaB200Fp8Bank* bank, const void* x, int x_dtype, int64_t tokens,
                           int top_k, const void* ids, int ids_dtype, const void* weights, int weights_dtype,
                           void* out, float* pair_out, void* workspace, size_t workspace_bytes, void* stream) {
-    if (!bank) return fail("bank is required");
-    const DramaB200Fp8Bank& b = *bank;
-    if (validate_decode_common(x, x_dtype, tokens, top_k, ids, ids_dtype, weights, weights_dtype, out, pair_out,
-                               b.hidden, b.intermediate, b.slots))
-        return -1;
-    if (!b.w13 || !b.w13_scale || !b.w2 || !b.w2_scale) return fail("FP8 bank pointers are required");
-    if (!aligned16(b.w13) || !aligned16(b.w2) || b.w13_row_stride % 16 || b.w2_row_stride % 16 ||
-        b.w13_slot_stride % 16 || b.w2_slot_stride % 16)
-        return fail("FP8 weight rows must start on 16-byte boundaries");
-    if (b.w13_row_stride < b.hidden || b.w2_row_stride < b.intermediate ||
-        b.w13_slot_stride < b.w13_row_stride * 2 * b.intermediate ||
-        b.w2_slot_stride < b.w2_row_stride * b.hidden)
-        return fail("FP8 weight strides are smaller than the bank geometry");
-    if (b.w13_scale_row_stride < b.hidden / 128 || b.w2_scale_row_stride < b.intermediate / 128)
-        return fail("FP8 scale strides are smaller than the bank geometry");
     DecodeArgs a{};
-    a.format = 0;
-    a.fp8 = b;
-    a.x = x;
-    a.x_dtype = x_dtype;
-    a.tokens = tokens;
-    a.top_k = top_k;
-    a.ids = ids;
-    a.ids_dtype = ids_dtype;
-    a.weights = weights;
-    a.weights_dtype = weights_dtype;
-    a.out = out;
-    a.pair_out = pair_out;
-    a.hidden = b.hidden;
-    a.intermediate = b.intermediate;
-    a.slots = b.slots;
+    if (prepare_fp8_decode(bank, x, x_dtype, tokens, top_k, ids, ids_dtype, weights, weights_dtype, out, pair_out,
+                           &a))
+        return -1;
     return finish_decode(a, workspace, workspace_bytes, stream);
 }
 
@@ -431,6 +452,34 @@ int prepare_moe_layer(const DramaB200Fp8Bank* bank, const void* gate, const void
 }
 }  // namespace
 
+namespace {
+DecodeLayerArgs one_launch_layer(const MoeLayerArgs& m, const DecodeArgs& d, void* moe_out, const void* normed_in,
+                                 const void* logits_in) {
+    DecodeLayerArgs a{};
+    RoutedLayerArgs& r = a.layer;
+    r.bank = d.fp8;
+    r.hidden_in = m.hidden_in;
+    r.hidden_out = m.hidden_out;
+    r.gamma = m.gamma;
+    r.gate = m.gate;
+    r.eps = m.eps;
+    r.E = m.experts;
+    r.k = m.top_k;
+    r.H = m.hidden;
+    r.I = m.intermediate;
+    r.ws = d.ws;
+    r.ids_out = m.ids_out;
+    r.weights_out = m.weights_out;
+    r.normed_out = m.normed_out;
+    r.moe_out = static_cast<__nv_bfloat16*>(moe_out);
+    a.normed_in = static_cast<const __nv_bfloat16*>(normed_in);
+    a.logits_in = static_cast<const __nv_bfloat16*>(logits_in);
+    a.part = d.ws.layer_part;
+    a.tickets = d.ws.layer_tickets;
+    return a;
+}
+}  // namespace
+
 int drama_b200_fp8_moe_layer(const DramaB200Fp8Bank* bank, const void* gate, const void* next_gate,
                              const float* gamma, float eps, const void* hidden_in, void* hidden_out,
                              int64_t tokens, int top_k, int64_t* ids_out, void* weights_out,
@@ -442,7 +491,10 @@ int drama_b200_fp8_moe_layer(const DramaB200Fp8Bank* bank, const void* gate, con
                                      ids_out, weights_out, normed_out, moe_out, workspace, workspace_bytes, &m, &d);
     if (st) return st < 0 ? -1 : 0;
     cudaError_t err;
-    if (routed_layer_supported(tokens, top_k, m.hidden, m.intermediate, m.experts)) {
+    if (decode_layer_supported(tokens, top_k, m.hidden, m.intermediate, m.experts)) {
+        // one hidden row: the whole layer in one launch
+        err = decode_layer_launch(one_launch_layer(m, d, moe_out, nullptr, nullptr), static_cast<cudaStream_t>(stream));
+    } else if (routed_layer_supported(tokens, top_k, m.hidden, m.intermediate, m.experts)) {
         // one hidden row: router + gate/up and down + combine, two launches
         RoutedLayerArgs r{};
         r.bank = d.fp8;
@@ -465,6 +517,38 @@ int drama_b200_fp8_moe_layer(const DramaB200Fp8Bank* bank, const void* gate, con
         err = moe_router_launch(m, static_cast<cudaStream_t>(stream));
         if (err == cudaSuccess) err = decode_experts_launch(d, static_cast<cudaStream_t>(stream));
     }
+    if (err != cudaSuccess) return fail("MoE layer launch failed: %s", cudaGetErrorString(err));
+    return 0;
+}
+
+int drama_b200_moe_layer_launches(int64_t tokens, int top_k, int hidden, int intermediate, int experts) {
+    if (decode_layer_supported(tokens, top_k, hidden, intermediate, experts)) return 1;
+    if (routed_layer_supported(tokens, top_k, hidden, intermediate, experts)) return 2;
+    return 3;
+}
+
+int drama_b200_fp8_moe_layer_logits(const DramaB200Fp8Bank* bank, const void* normed, const void* logits,
+                                    const void* hidden_in, void* hidden_out, int64_t tokens, int top_k,
+                                    int64_t* ids_out, void* weights_out, void* moe_out, void* workspace,
+                                    size_t workspace_bytes, void* stream) {
+    if (!normed || !logits) return fail("normed row and router logits are required");
+    if (!aligned16(normed) || !aligned16(logits)) return fail("normed row and logits must be 16-byte aligned");
+    if (tokens != 1) return fail("the logits-driven layer runs one decode row (tokens == 1), got %lld",
+                                 static_cast<long long>(tokens));
+    MoeLayerArgs m;
+    DecodeArgs d;
+    // The router weight and gamma are not read; the normalised row stands in for both pointers.
+    const float one = 1.0f;
+    const int st = prepare_moe_layer(bank, normed, nullptr, &one, 1e-6f, hidden_in, hidden_out, tokens, top_k,
+                                     ids_out, weights_out, nullptr, moe_out, workspace, workspace_bytes, &m, &d);
+    if (st) return st < 0 ? -1 : 0;
+    if (!decode_layer_supported(tokens, top_k, m.hidden, m.intermediate, m.experts))
+        return fail("the logits-driven layer supports hidden %% 512 == 0 up to 2048, intermediate %% 16 == 0, "
+                    "top_k <= 16 (got hidden %d, intermediate %d, top_k %d)", m.hidden, m.intermediate, top_k);
+    m.gamma = nullptr;
+    m.gate = nullptr;
+    const cudaError_t err =
+        decode_layer_launch(one_launch_layer(m, d, moe_out, normed, logits), static_cast<cudaStream_t>(stream));
     if (err != cudaSuccess) return fail("MoE layer launch failed: %s", cudaGetErrorString(err));
     return 0;
 }
@@ -818,23 +902,52 @@ static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBy
 namespace drama {
 namespace {
 std::mutex g_static_mutex;
-void* g_static_base[64] = {nullptr};
+struct StaticBase {
+    CUcontext ctx;
+    void* ptr;
+};
+StaticBase g_static_base[64] = {};
 
-// Set-up on the first call per device (with that device current): the
-// array's device address, and one clear of the array on the caller's stream
-// (the decode scratch contract: zero before first use; every call then
-// leaves it reusable).
-int static_scratch(int dev, cudaStream_t stream, void** out) {
-    std::lock_guard<std::mutex> lock(g_static_mutex);
-    if (!g_static_base[dev]) {
-        void* ptr = nullptr;
-        cudaError_t err = cudaGetSymbolAddress(&ptr, g_static_scratch);
-        if (err != cudaSuccess) return fail("cudaGetSymbolAddress(static scratch): %s", cudaGetErrorString(err));
-        err = cudaMemsetAsync(ptr, 0, kStaticScratchBytes, stream);
-        if (err != cudaSuccess) return fail("clearing the static scratch: %s", cudaGetErrorString(err));
-        g_static_base[dev] = ptr;
+// The context current on this thread (null when none is), through the
+// driver entry point the runtime exposes.
+int current_context(CUcontext* ctx) {
+    using GetCurrent = CUresult (*)(CUcontext*);
+    static GetCurrent fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult found{};
+        const cudaError_t err = cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &found);
+        if (err != cudaSuccess || found != cudaDriverEntryPointSuccess || !p)
+            return fail("cuCtxGetCurrent is not available from the driver");
+        fn = reinterpret_cast<GetCurrent>(p);
     }
-    *out = g_static_base[dev];
+    if (fn(ctx) != CUDA_SUCCESS) return fail("cuCtxGetCurrent failed");
+    return 0;
+}
+
+// The array's device address in the current context. It is looked up on
+// the first call in each context (cudaGetSymbolAddress) and kept per
+// context, so a device reset or another context on the same device gets its
+// own address. No clear is needed: every decode call rewrites the status
+// words and zeroes its split-K and combine counters before the expert kernels
+// read them (decode_prep_kernel), so the array's previous contents are never
+// read.
+int static_scratch(void** out) {
+    int dev = 0;
+    const cudaError_t derr = cudaGetDevice(&dev);
+    if (derr != cudaSuccess) return fail("cudaGetDevice: %s", cudaGetErrorString(derr));
+    if (dev < 0 || dev >= 64) return fail("device ordinal %d out of range", dev);
+    CUcontext ctx = nullptr;
+    if (current_context(&ctx)) return -1;
+    std::lock_guard<std::mutex> lock(g_static_mutex);
+    if (!ctx || !g_static_base[dev].ptr || g_static_base[dev].ctx != ctx) {
+        void* ptr = nullptr;
+        const cudaError_t err = cudaGetSymbolAddress(&ptr, g_static_scratch);
+        if (err != cudaSuccess) return fail("cudaGetSymbolAddress(static scratch): %s", cudaGetErrorString(err));
+        if (current_context(&ctx)) return -1;  // the lookup binds the device's primary context if none was current
+        g_static_base[dev] = {ctx, ptr};
+    }
+    *out = g_static_base[dev].ptr;
     return 0;
 }
 }  // namespace
@@ -847,56 +960,21 @@ size_t drama_b200_static_scratch_bytes(void) { return kStaticScratchBytes; }
 int drama_b200_fp8_decode_static(const DramaB200Fp8Bank* bank, const void* x, int x_dtype, int64_t tokens,
                                  int top_k, const void* ids, int ids_dtype, const void* weights,
                                  int weights_dtype, void* out, float* pair_out, void* stream) {
-    if (!bank) return fail("bank is required");
-    const DramaB200Fp8Bank& b = *bank;
-    if (validate_decode_common(x, x_dtype, tokens, top_k, ids, ids_dtype, weights, weights_dtype, out, pair_out,
-                               b.hidden, b.intermediate, b.slots))
+    DecodeArgs a{};
+    if (prepare_fp8_decode(bank, x, x_dtype, tokens, top_k, ids, ids_dtype, weights, weights_dtype, out, pair_out,
+                           &a))
         return -1;
-    if (!b.w13 || !b.w13_scale || !b.w2 || !b.w2_scale) return fail("FP8 bank pointers are required");
-    if (!aligned16(b.w13) || !aligned16(b.w2) || b.w13_row_stride % 16 || b.w2_row_stride % 16 ||
-        b.w13_slot_stride % 16 || b.w2_slot_stride % 16)
-        return fail("FP8 weight rows must start on 16-byte boundaries");
-    if (b.w13_row_stride < b.hidden || b.w2_row_stride < b.intermediate ||
-        b.w13_slot_stride < b.w13_row_stride * 2 * b.intermediate ||
-        b.w2_slot_stride < b.w2_row_stride * b.hidden)
-        return fail("FP8 weight strides are smaller than the bank geometry");
-    if (b.w13_scale_row_stride < b.hidden / 128 || b.w2_scale_row_stride < b.intermediate / 128)
-        return fail("FP8 scale strides are smaller than the bank geometry");
     if (tokens == 0) return 0;
     int sms = 0;
-    if (sm_count_current(&sms)) return -1;
-    const size_t need = decode_workspace_layout(tokens, top_k, b.hidden, b.intermediate, sms, 0, nullptr, nullptr);
+    const size_t need = decode_scratch_need(a, &sms);
+    if (!need) return -1;
     if (need > kStaticScratchBytes)
         return fail("decode of %lld tokens x top-%d at hidden %d, intermediate %d needs %zu bytes of scratch; "
                     "the library's static scratch holds %zu (use drama_b200_fp8_decode with a workspace)",
-                    static_cast<long long>(tokens), top_k, b.hidden, b.intermediate, need, kStaticScratchBytes);
-    int dev = 0;
-    const cudaError_t derr = cudaGetDevice(&dev);
-    if (derr != cudaSuccess) return fail("cudaGetDevice: %s", cudaGetErrorString(derr));
-    if (dev < 0 || dev >= 64) return fail("device ordinal %d out of range", dev);
+                    static_cast<long long>(tokens), top_k, a.hidden, a.intermediate, need, kStaticScratchBytes);
     void* base = nullptr;
-    if (static_scratch(dev, static_cast<cudaStream_t>(stream), &base)) return -1;
-    DecodeArgs a{};
-    a.format = 0;
-    a.fp8 = b;
-    a.x = x;
-    a.x_dtype = x_dtype;
-    a.tokens = tokens;
-    a.top_k = top_k;
-    a.ids = ids;
-    a.ids_dtype = ids_dtype;
-    a.weights = weights;
-    a.weights_dtype = weights_dtype;
-    a.out = out;
-    a.pair_out = pair_out;
-    a.hidden = b.hidden;
-    a.intermediate = b.intermediate;
-    a.slots = b.slots;
-    decode_workspace_layout(tokens, top_k, b.hidden, b.intermediate, sms, 0, static_cast<char*>(base), &a.ws);
-    a.ctas = sms * kDecodeCtasPerSm;
-    const cudaError_t err = decode_launch(a, static_cast<cudaStream_t>(stream));
-    if (err != cudaSuccess) return fail("decode launch failed: %s", cudaGetErrorString(err));
-    return 0;
+    if (static_scratch(&base)) return -1;
+    return finish_decode(a, base, kStaticScratchBytes, stream);
 }
 
 }  // extern "C"

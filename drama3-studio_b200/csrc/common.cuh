@@ -137,7 +137,7 @@ __device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t pair) {
 // D = A(16x16 f16, row) * B(16x8 f16, col) + C, fp32 accumulate.
 __device__ __forceinline__ void mma_f16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
                                               uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
         "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])

@@ -390,6 +390,8 @@ size_t decode_workspace_layout(int64_t tokens, int top_k, int hidden, int interm
     if (experts > 0) {
         w.logits = reinterpret_cast<float*>(take(tokens * experts * 4));
         w.router_cnt = reinterpret_cast<int32_t*>(take(4));
+        w.layer_part = reinterpret_cast<float*>(take(static_cast<size_t>(sm_count) * hidden * 4));
+        w.layer_tickets = reinterpret_cast<int32_t*>(take(64));
     }
     if (ws) *ws = w;
     return off;

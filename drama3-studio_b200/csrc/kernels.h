@@ -1,6 +1,7 @@
 // Internal kernel entry points and argument blocks (host side of the ABI).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -82,6 +83,8 @@ struct DecodeWorkspace {
     int32_t* cmb_cnt;     // [H/16]
     float* logits;        // [T][E] router logits (MoE layer entry point only)
     int32_t* router_cnt;  // [1]
+    float* layer_part;    // [SMs][H] partial down projections of the one-launch layer (MoE layer only)
+    int32_t* layer_tickets;  // [16] its arrival tickets, reset by the last arriver
 };
 
 // The split-K and combine counters of one call: zeroed by whichever kernel
@@ -290,5 +293,24 @@ struct RoutedLayerArgs {
 };
 bool routed_layer_supported(int64_t tokens, int top_k, int hidden, int intermediate, int experts);
 cudaError_t routed_layer_launch(const RoutedLayerArgs& a, int sm_count, cudaStream_t s);
+
+// ---------------------------------------------------------------------------
+// Single-row MoE layer in ONE launch (decode_layer.cu): 4-CTA clusters, each
+// owning a run of one routed expert's intermediate tiles; gate/up rows by
+// bulk copies into a shared-memory ring, the down projection per run, and
+// the slot-ordered combine by the last CTA to arrive.
+// ---------------------------------------------------------------------------
+struct DecodeLayerArgs {
+    CUtensorMap w13_map;                 // the bank's gate/up rows as [slot][gate|up][row][K block][128 B]
+    CUtensorMap w2_map;                  // the bank's down rows as [slot][row][I bytes]
+    RoutedLayerArgs layer;               // uses ws.status[3] (a bounded wait timed out)
+    const __nv_bfloat16* normed_in;      // with logits_in: the caller's normalised row, bf16 [H]
+    const __nv_bfloat16* logits_in;      // null: RMSNorm and router GEMV inside the kernel
+    float* part;                         // [units][H] fp32 partial down projections
+    int32_t* tickets;                    // [4] arrival tickets, reset by the last arriver
+    int parts, nkt, stages;              // set by decode_layer_launch (with w13_map)
+};
+bool decode_layer_supported(int64_t tokens, int top_k, int hidden, int intermediate, int experts);
+cudaError_t decode_layer_launch(DecodeLayerArgs a, cudaStream_t s);
 
 }  // namespace drama

@@ -43,6 +43,8 @@ EXPORTS = (
     "drama_b200_shared_expert",
     "drama_b200_moe_layer_workspace_bytes",
     "drama_b200_fp8_moe_layer",
+    "drama_b200_fp8_moe_layer_logits",
+    "drama_b200_moe_layer_launches",
     "drama_b200_fp8_moe_router",
     "drama_b200_fp8_moe_experts",
     "drama_b200_prefill_workspace_bytes",
@@ -166,6 +168,11 @@ class Library:
         dll.drama_b200_fp8_moe_layer.argtypes = [
             ctypes.POINTER(Fp8Bank), c_void_p, c_void_p, c_void_p, ctypes.c_float, c_void_p, c_void_p,
             c_int64, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]
+        dll.drama_b200_moe_layer_launches.argtypes = [c_int64, c_int, c_int, c_int, c_int]
+        dll.drama_b200_moe_layer_launches.restype = c_int
+        dll.drama_b200_fp8_moe_layer_logits.argtypes = [
+            ctypes.POINTER(Fp8Bank), c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_void_p, c_void_p,
+            c_void_p, c_void_p, c_size_t, c_void_p]
         dll.drama_b200_fp8_moe_router.argtypes = [
             ctypes.POINTER(Fp8Bank), c_void_p, c_void_p, c_void_p, ctypes.c_float, c_void_p,
             c_int64, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]

@@ -15,6 +15,7 @@ import ctypes
 from dataclasses import dataclass, field
 
 import torch
+import torch.nn.functional as F
 from torch import Tensor
 
 from . import _lib
@@ -60,20 +61,43 @@ def moe_layer_workspace(tokens: int, top_k: int, hidden: int, intermediate: int,
     return torch.zeros(nbytes, dtype=torch.uint8, device=device)
 
 
+def torch_router_inputs(hidden_in: Tensor, layer: MoELayer, eps: float) -> tuple[Tensor, Tensor]:
+    """The reference decode graph's RMSNorm and router logits, in torch ops.
+
+    ``BackboneDecodeGraph._route_impl`` (``src/drama_low_vram/backbone_graph.py:
+    316-319``): the RMSNorm in fp32 math cast to bf16, then ``moe.gate`` as a
+    bf16 ``F.linear``. Returns ``(normed, logits)``, both bf16.
+    """
+    x = hidden_in.float()
+    normed = (x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps) * layer.gamma).to(torch.bfloat16)
+    return normed, F.linear(normed, layer.gate)
+
+
 def moe_layer(hidden_in: Tensor, layer: MoELayer, out: Tensor, workspace: Tensor, *, top_k: int = 8,
               eps: float = 1e-6, next_gate: Tensor | None = None, trace: LayerTrace | None = None,
-              layer_events: tuple | None = None) -> Tensor:
+              layer_events: tuple | None = None, router: str = "fused") -> Tensor:
     """Enqueue one fused MoE layer on the current stream; returns ``out``.
 
-    One hidden row runs as two launches (router + gate/up in thread-block
-    clusters, then down + combine + residual); more rows run the router,
+    One hidden row runs as one launch (thread-block clusters, each streaming a
+    run of one routed expert's gate/up and down rows; the last CTA to finish
+    combines the slots and adds the residual); more rows run the router,
     expert-group and K1 kernels. ``layer_events=(start, end)`` records CUDA
     events around the layer's launches.
+
+    ``router="fused"`` computes RMSNorm and the router GEMV inside the layer in
+    a fixed fp32 order; ``router="torch"`` takes them from torch ops
+    (``torch_router_inputs``), so the routes are those of the reference's
+    decode graph bit for bit, at the cost of the extra launches.
     """
     if hidden_in.dtype != torch.bfloat16 or out.dtype != torch.bfloat16:
         raise ValueError("The fused MoE layer runs on bf16 hidden states")
     if not hidden_in.is_contiguous() or not out.is_contiguous() or hidden_in.shape != out.shape:
         raise ValueError("hidden_in and out must be contiguous and of equal shape")
+    if router not in ("fused", "torch"):
+        raise ValueError("router must be 'fused' or 'torch'")
+    if router == "torch":
+        return _moe_layer_torch_router(hidden_in, layer, out, workspace, top_k=top_k, eps=eps, trace=trace,
+                                       layer_events=layer_events)
     bank, keep = layer.bank()
     tokens = hidden_in.shape[0]
     lib = _lib.library()
@@ -92,16 +116,38 @@ def moe_layer(hidden_in: Tensor, layer: MoELayer, out: Tensor, workspace: Tensor
     return out
 
 
+def _moe_layer_torch_router(hidden_in, layer, out, workspace, *, top_k, eps, trace, layer_events):
+    if hidden_in.shape[0] != 1:
+        raise ValueError("router='torch' runs one decode row per call")
+    bank, keep = layer.bank()
+    lib = _lib.library()
+    stream = _lib.stream_handle(hidden_in.device)
+    if layer_events is not None:
+        layer_events[0].record()
+    normed, logits = torch_router_inputs(hidden_in, layer, eps)
+    lib.check(lib.dll.drama_b200_fp8_moe_layer_logits(
+        ctypes.byref(bank), normed.data_ptr(), logits.data_ptr(), hidden_in.data_ptr(), out.data_ptr(), 1, top_k,
+        _lib.ptr(trace.ids if trace else None), _lib.ptr(trace.weights if trace else None),
+        _lib.ptr(trace.moe if trace else None), workspace.data_ptr(), workspace.numel(), stream))
+    if layer_events is not None:
+        layer_events[1].record()
+    if trace is not None:
+        trace.normed.copy_(normed)
+    return out
+
+
 class DecodeStack:
     """``layers`` MoE layers applied to ``tokens`` hidden rows per decode step."""
 
-    def __init__(self, layers: list[MoELayer], *, tokens: int = 1, top_k: int = 8, eps: float = 1e-6):
+    def __init__(self, layers: list[MoELayer], *, tokens: int = 1, top_k: int = 8, eps: float = 1e-6,
+                 router: str = "fused"):
         if not layers:
             raise ValueError("DecodeStack needs at least one layer")
         self.layers = layers
         self.tokens = tokens
         self.top_k = top_k
         self.eps = eps
+        self.router = router
         first = layers[0]
         self.device = first.gate.device
         self.experts, self.hidden = first.gate.shape
@@ -122,7 +168,7 @@ class DecodeStack:
             nxt = self.layers[i + 1].gate if i + 1 < n else None
             moe_layer(src, layer, dst, self.workspace, top_k=self.top_k, eps=self.eps, next_gate=nxt,
                       trace=None if traces is None else traces[i],
-                      layer_events=None if layer_events is None else layer_events[i])
+                      layer_events=None if layer_events is None else layer_events[i], router=self.router)
             src = dst
         return out
 
@@ -151,6 +197,12 @@ class DecodeStack:
                           layer_events=self.layer_events[s] if s < timed_steps else None)
         self.graph = graph
         return graph
+
+    def launches_per_layer(self) -> int:
+        """Library kernel launches per layer (torch's RMSNorm and GEMV launches not counted)."""
+        lib = _lib.library()
+        return lib.dll.drama_b200_moe_layer_launches(self.tokens, self.top_k, self.hidden, self.intermediate,
+                                                     self.experts)
 
     def layer_time_ms(self) -> float:
         """Mean duration of one layer's launches in the last replay."""

@@ -262,6 +262,29 @@ DRAMA_B200_API int drama_b200_fp8_moe_layer(const DramaB200Fp8Bank* bank, const 
                                             void* weights_out, void* normed_out, void* moe_out,
                                             void* workspace, size_t workspace_bytes, void* stream);
 
+/* Kernel launches one drama_b200_fp8_moe_layer call makes for these sizes on
+ * the current device (1: the one-launch single-row layer; 2: the two-launch
+ * single-row layer; 3: router, gate/up and down launches for several rows). */
+DRAMA_B200_API int drama_b200_moe_layer_launches(int64_t tokens, int top_k, int hidden, int intermediate,
+                                                 int experts);
+
+/* The same decode layer driven by the caller's router inputs: `normed` is the
+ * bf16 [H] row after the RMSNorm and `logits` the bf16 [experts] router
+ * logits, both as the reference's decode graph computes them
+ * (BackboneDecodeGraph._route_impl, src/drama_low_vram/backbone_graph.py:
+ * 316-319: post_attention_layernorm, then moe.gate as a bf16 F.linear). The
+ * layer applies softmax(logits.float()) -> topk -> renormalise -> bf16 (lines
+ * 320-323, torch's order), the experts on `normed`, and the residual
+ * (hidden_out = bf16(hidden_in + experts)), so its routes are the reference's
+ * bit for bit whatever RMSNorm and GEMV order produced the inputs.
+ * tokens == 1; hidden % 512 == 0 up to 2048; intermediate % 16 == 0;
+ * top_k <= 16. Workspace: drama_b200_moe_layer_workspace_bytes. */
+DRAMA_B200_API int drama_b200_fp8_moe_layer_logits(const DramaB200Fp8Bank* bank, const void* normed,
+                                                   const void* logits, const void* hidden_in, void* hidden_out,
+                                                   int64_t tokens, int top_k, int64_t* ids_out,
+                                                   void* weights_out, void* moe_out, void* workspace,
+                                                   size_t workspace_bytes, void* stream);
+
 /* The two halves of drama_b200_fp8_moe_layer, for callers that time or
  * interleave them: the router (RMSNorm, router GEMV, top-k, expert groups,
  * written into the workspace) and the expert GEMVs with combine + residual
@@ -324,11 +347,14 @@ DRAMA_B200_API int drama_b200_fp8_prefill(const DramaB200Fp8Bank* bank, const vo
  * intermediate 768 and above 43 tokens at hidden 4096 / intermediate 2048.
  * The call allocates nothing.
  *
- * The first call on a device (with that device current) looks up the array's
- * device address and clears the array on the caller's stream; make that first
- * call before any stream capture. Every call, from any thread, shares the
- * one array and leaves it reusable, so calls that can overlap on the GPU
- * (different streams without ordering between them) race; order them.
+ * The first call in each device context (with that device current) looks up
+ * the array's device address with cudaGetSymbolAddress and keeps it for that
+ * context; make that first call before any stream capture. The array needs
+ * no clearing: every call rewrites its status words and zeroes its counters
+ * before the expert kernels read them, and keeps the last call's other
+ * contents. Every call, from any thread, shares the one array, so calls that
+ * can overlap on the GPU (different streams without ordering between them)
+ * race; order them.
  * ------------------------------------------------------------------------- */
 DRAMA_B200_API size_t drama_b200_static_scratch_bytes(void);
 
