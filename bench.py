@@ -237,6 +237,60 @@ class CpuReference:
         }
 
 
+class TorchDequantReference:
+    """The reference's PyTorch dequant path on the host: TorchExpertBackend.forward.
+
+    ``src/drama_low_vram/offload.py:199-244`` run unmodified from the copy that
+    build() places under oracle/_ref, on CPU tensors, one config-0 token-layer
+    per call (the 8 routed experts dequantised to bf16, F.linear, weighted slot
+    sum), with the oracle's RMSNorm and router in front as in CpuReference.
+    """
+
+    def __init__(self, bank):
+        import torch
+
+        sys.path.insert(0, str(REPO / "oracle" / "_ref"))
+        from drama_low_vram.offload import StagedExperts, TorchExpertBackend
+
+        from drama_b200 import synthetic
+
+        self.torch = torch
+        self.threads = torch.get_num_threads()
+        self.staged = StagedExperts(**{k: v.detach().cpu().contiguous() for k, v in bank.items()})
+        self.backend = TorchExpertBackend()
+        self.gate = synthetic.gate_weight(EXPERTS, HIDDEN, 500).float().numpy()
+        self.gamma = synthetic.norm_gamma(HIDDEN, 700).numpy()
+        self.x = synthetic.hidden_states(1, HIDDEN, 11).float().numpy()
+
+    def layer(self) -> None:
+        from oracle import restate as R
+
+        torch = self.torch
+        normed = R.rms_norm(self.x, self.gamma)
+        logits = R.gate_logits(normed, self.gate)
+        ids, w, _ = R.route_topk(logits, TOP_K, True, "bfloat16")
+        x = torch.from_numpy(normed).to(torch.bfloat16)
+        moe = self.backend.forward(x, torch.from_numpy(ids), torch.from_numpy(w).to(torch.bfloat16), self.staged)
+        self.x = R.round_bf16(self.x + moe.float().numpy())
+
+    def sample(self, seconds: float, layers: int) -> dict:
+        done, start = 0, time.perf_counter()
+        while True:
+            self.layer()
+            done += 1
+            elapsed = time.perf_counter() - start
+            if elapsed >= seconds:
+                break
+        per_layer = elapsed / done
+        return {
+            "value": 1.0 / (per_layer * layers), "unit": "tokens/s", "cores": self.threads, "kind": "reference",
+            "sample": (f"{done} token-layers in {elapsed:.1f}s: the reference's TorchExpertBackend.forward "
+                       f"(offload.py:199-244, W16A16 dequant path, torch on {self.threads} threads) for the 8 "
+                       f"routed experts plus the oracle's RMSNorm/router; value = 1 / ({layers} x mean "
+                       f"token-layer time)"),
+        }
+
+
 def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -388,6 +442,12 @@ def run_ours(args) -> None:
                             "w2_weight": layers[0].w2_weight, "w2_scale_inv": layers[0].w2_scale_inv})
         ref.layer()
         line["cpu_baseline"] = ref.sample(args.cpu_seconds, args.layers)
+        if (REPO / "oracle" / "_ref" / "drama_low_vram").is_dir():
+            bank = {"w13_weight": layers[0].w13_weight, "w13_scale_inv": layers[0].w13_scale_inv,
+                    "w2_weight": layers[0].w2_weight, "w2_scale_inv": layers[0].w2_scale_inv}
+            torch_ref = TorchDequantReference(bank)
+            torch_ref.layer()
+            line["cpu_baseline"]["torch_dequant"] = torch_ref.sample(args.cpu_seconds / 2, args.layers)
     del graph
     if world > 1:
         dist.destroy_process_group()

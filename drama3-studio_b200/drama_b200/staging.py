@@ -193,6 +193,11 @@ class StagingArena:
         self._turn = -1
         self._active: _SlotSet | None = None
         self._slot_index: dict[tuple[int, ...], Tensor] = {}
+        # Set by the reference manager's configure_host_residency
+        # (offload.py:1344-1345): a RAM tier that decides where each expert's
+        # host bytes come from, and the layer of each store.
+        self.host_residency = None
+        self.host_store_layers: dict[tuple[int, ...], int] = {}
 
     # -- allocation -------------------------------------------------------
     def _allocate(self, hidden: int, intermediate: int, device: torch.device) -> None:
@@ -335,6 +340,8 @@ class StagingArena:
         raw = store.raw if isinstance(store, PackedExperts) else store.w13_weight
         if raw.device.type != "cpu":
             raise ValueError("The staging store must live in host memory")
+        if self.host_residency is not None and self.host_residency.enabled:
+            return self._bounce(store, expert_ids, slot_set, residency=True)
         ids = expert_ids.tolist()
         arena = slot_set.arena
         packed = store if isinstance(store, PackedExperts) else getattr(store, "packed", None)
@@ -357,8 +364,10 @@ class StagingArena:
                 return src, dst, nbytes
         return self._bounce(store, expert_ids, slot_set)
 
-    def _bounce(self, store, expert_ids: Tensor, slot_set: _SlotSet):
-        """Pageable store: gather into a pinned bounce buffer first (``offload.py:561-594``)."""
+    def _bounce(self, store, expert_ids: Tensor, slot_set: _SlotSet, *, residency: bool = False):
+        """Gather into a pinned bounce buffer first (``offload.py:561-594``): the
+        host-residency tier's own gather when one is configured, else
+        ``index_select`` from a pageable store."""
         arena = slot_set.arena
         if slot_set.bounce is None:
             slot_set.bounce = PackedExperts.allocate(self.capacity, arena.hidden, arena.intermediate,
@@ -367,7 +376,15 @@ class StagingArena:
         if slot_set.copy_pending:
             slot_set.copy_done.synchronize()     # the bounce rows are still being read by the last DMA
         count = expert_ids.numel()
-        if isinstance(store, PackedExperts):
+        if residency:
+            key = tuple(id(getattr(store, name)) for name in EXPERT_BUFFER_NAMES)
+            layer = self.host_store_layers.get(key)
+            if layer is None:
+                raise RuntimeError("Expert buffers changed; reconfigure host residency")
+            self.host_residency.copy_to(layer, expert_ids,
+                                        {name: getattr(slot_set.bounce, name) for name in EXPERT_BUFFER_NAMES},
+                                        observe=False)
+        elif isinstance(store, PackedExperts):
             torch.index_select(store.raw, 0, expert_ids, out=slot_set.bounce.raw[:count])
         else:
             for name in EXPERT_BUFFER_NAMES:

@@ -172,7 +172,7 @@ def make_permute() -> dict:
 
 def main() -> None:
     parser = argparse.ArgumentParser()
-    parser.add_argument("--reference", default="/root/reference/src")
+    parser.add_argument("--reference", default=str(Path(__file__).resolve().parents[3] / "reference" / "src"))
     args = parser.parse_args()
     sys.path.insert(0, args.reference)
     torch.manual_seed(0)

@@ -65,10 +65,17 @@ def test_prefill_config3_matches_decode_kernels(cuda_device):
     gemv = B200ExpertBackend(prefill_min_pairs=1 << 30).forward(x, ids, w, staged)
     torch.cuda.synchronize()
     assert_parity(np_f32(out), np_f32(gemv), label="prefill vs decode kernels, config 3")
-    # a few rows against the oracle directly
-    rows = [0, 1, 2047, 4095]
-    ref = R.fp8_dequant_forward(np_f32(x[rows]), ids[rows].cpu().numpy(), np_f32(w[rows]), np_bank(bank), "bfloat16")
-    assert_parity(np_f32(out[rows]), ref, label="prefill config 3, oracle rows")
+    # 256 rows against the oracle directly: 128 routed to the most-loaded
+    # (Zipf head) expert, 128 seeded others
+    flat = ids.cpu().numpy()
+    head = np.bincount(flat.reshape(-1), minlength=128).argmax()
+    on_head = np.flatnonzero((flat == head).any(axis=1))
+    rng = np.random.default_rng(7)
+    rows = np.concatenate([rng.choice(on_head, 128, replace=False),
+                           rng.choice(np.setdiff1d(np.arange(4096), on_head), 128, replace=False)])
+    rows.sort()
+    ref = R.fp8_dequant_forward(np_f32(x[rows]), flat[rows], np_f32(w[rows]), np_bank(bank), "bfloat16")
+    assert_parity(np_f32(out[rows]), ref, label=f"prefill config 3, 256 oracle rows (head expert {head})")
 
 
 def test_prefill_out_of_range_ids_contribute_zero(cuda_device):

@@ -8,6 +8,10 @@ workspace. These tests call both entry points through the C ABI on the same
 inputs and hold the static one to the parity bar of the other GPU tests, on
 two calls in a row (the second call reuses what the first left in the array).
 
+Both entry points run the same kernels on the same inputs, so the outputs are
+compared bit for bit. The device's free memory (cudaMemGetInfo) is read around
+the second static call, after the first call's set-up: it must not shrink.
+
 The file name makes pytest collect it last, after every other test file.
 """
 
@@ -72,10 +76,16 @@ def test_static_scratch_decode_matches_workspace_decode(cuda_device, tokens, top
     torch.cuda.synchronize()
     for call in range(2):
         out = torch.full_like(x, float("nan"))
+        torch.cuda.synchronize()
+        free_before = torch.cuda.mem_get_info(cuda_device)[0]
         lib.check(_static_call(lib, fp8, x, ids, w, top_k, out))
         torch.cuda.synchronize()
+        free_after = torch.cuda.mem_get_info(cuda_device)[0]
+        if call == 1:
+            assert free_after >= free_before, f"static-scratch call allocated {free_before - free_after} bytes"
         assert_parity(np_f32(out), np_f32(expected), max_abs=MAX_ABS_TOL, rel=REL_TOL,
                       label=f"static-scratch decode, call {call + 1}")
+        assert torch.equal(out.view(torch.int16), expected.view(torch.int16)), f"call {call + 1} differs in bits"
     del ws, keep
 
 
