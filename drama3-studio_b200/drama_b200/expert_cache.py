@@ -68,12 +68,6 @@ ROLE_DTYPES = {
 }
 
 
-def _int_field(value: Any, label: str, minimum: int = 0) -> int:
-    if isinstance(value, bool) or not isinstance(value, int) or value < minimum:
-        raise ValueError(f"{label} must be an integer >= {minimum}")
-    return value
-
-
 def role_shapes(num_experts: int, hidden: int, intermediate: int) -> dict[str, tuple[int, int, int]]:
     return {
         "w13_weight": (num_experts, 2 * intermediate, hidden),
@@ -88,7 +82,8 @@ def cache_layout(num_layers: int, num_experts: int, hidden: int,
     """Per-layer buffer records of the manifest and the data file's size."""
     for label, value in (("num_layers", num_layers), ("num_experts", num_experts), ("hidden", hidden),
                          ("intermediate", intermediate)):
-        _int_field(value, label, 1)
+        if type(value) is not int or value < 1:
+            raise ValueError(f"{label} must be a positive integer")
     if hidden % BLOCK or intermediate % BLOCK:
         raise ValueError("Expert dimensions must be divisible by the FP8 block size")
     shapes = role_shapes(num_experts, hidden, intermediate)
@@ -154,44 +149,95 @@ def write_expert_cache(cache_dir: str | Path, layers: list[dict[str, Tensor]], *
     return cache_dir
 
 
+# ---------------------------------------------------------------------------
+# Manifest validation: a declarative schema (field -> rule) walked by one
+# generic checker, then the checks that relate fields to each other and to
+# the data file.
+# ---------------------------------------------------------------------------
+_MISSING = object()
+
+
+class _Rule:
+    """One manifest value: ``accepts(value)`` and a description for errors."""
+
+    def __init__(self, describe: str, accepts) -> None:
+        self.describe = describe
+        self.accepts = accepts
+
+
+def _exactly(expected: Any) -> _Rule:
+    return _Rule(repr(expected), lambda v: v == expected and type(v) is type(expected))
+
+
+def _count(minimum: int) -> _Rule:
+    return _Rule(f"an integer >= {minimum}", lambda v: type(v) is int and v >= minimum)
+
+
+_HEX_DIGEST = _Rule("64 lowercase hex digits", lambda v: isinstance(v, str) and _SHA256.fullmatch(v) is not None)
+
+MANIFEST_SCHEMA: dict[str, Any] = {
+    "format": _exactly(CACHE_FORMAT),
+    "format_version": _exactly(CACHE_FORMAT_VERSION),
+    "byte_order": _exactly("little"),
+    "model_fingerprint": _HEX_DIGEST,
+    "model": {
+        "model_type": _exactly("fish_omni"),
+        "block_size": _exactly(BLOCK),
+        "num_layers": _count(1),
+        "num_experts": _count(1),
+        "hidden": _count(1),
+        "intermediate": _count(1),
+    },
+    "data": {"name": _exactly(DATA_NAME), "size": _count(1), "sha256": _HEX_DIGEST},
+}
+
+
+def check_manifest(schema: dict[str, Any], manifest: Any, path: str = "") -> dict[str, Any]:
+    """Validate ``manifest`` against ``schema``; returns the checked values by dotted path.
+
+    Raises ``ValueError("expert cache manifest: <path> ...")`` for the first
+    field that is missing or breaks its rule.
+    """
+    where = path or "the manifest"
+    if not isinstance(manifest, dict):
+        raise ValueError(f"expert cache manifest: {where} must be a JSON object")
+    values: dict[str, Any] = {}
+    for key, rule in schema.items():
+        field = f"{path}.{key}" if path else key
+        value = manifest.get(key, _MISSING)
+        if isinstance(rule, dict):
+            values.update(check_manifest(rule, value if value is not _MISSING else None, field))
+        elif value is _MISSING or not rule.accepts(value):
+            found = "missing" if value is _MISSING else f"found {value!r}"
+            raise ValueError(f"expert cache manifest: {field} must be {rule.describe} ({found})")
+        else:
+            values[field] = value
+    return values
+
+
 class ExpertCacheFile:
     """A validated expert cache: private mapping, zero-copy role views, page locking."""
 
     def __init__(self, cache_dir: Path, manifest: dict[str, Any]) -> None:
         self.cache_dir = Path(cache_dir)
         self.manifest = manifest
-        if manifest.get("format") != CACHE_FORMAT:
-            raise ValueError("Unsupported expert cache format")
-        if manifest.get("format_version") != CACHE_FORMAT_VERSION:
-            raise ValueError("Unsupported expert cache version")
-        if manifest.get("byte_order") != "little" or sys.byteorder != "little":
-            raise ValueError("Expert cache requires little-endian byte order")
-        model = manifest.get("model")
-        if not isinstance(model, dict) or model.get("model_type") != "fish_omni":
-            raise ValueError("Expert cache is not a Fish Omni model")
-        if model.get("block_size") != BLOCK:
-            raise ValueError("Unsupported expert block size")
-        self.num_layers = _int_field(model.get("num_layers"), "num_layers", 1)
-        self.num_experts = _int_field(model.get("num_experts"), "num_experts", 1)
-        self.hidden = _int_field(model.get("hidden"), "hidden", 1)
-        self.intermediate = _int_field(model.get("intermediate"), "intermediate", 1)
+        if sys.byteorder != "little":
+            raise ValueError("expert cache files are little-endian; this host is not")
+        fields = check_manifest(MANIFEST_SCHEMA, manifest)
+        self.num_layers = fields["model.num_layers"]
+        self.num_experts = fields["model.num_experts"]
+        self.hidden = fields["model.hidden"]
+        self.intermediate = fields["model.intermediate"]
+        self.model_fingerprint = fields["model_fingerprint"]
+        # the buffer records follow from the geometry; the manifest must repeat them exactly
         self._layers, self.nbytes = cache_layout(self.num_layers, self.num_experts, self.hidden, self.intermediate)
         if manifest.get("layers") != self._layers:
-            raise ValueError("Expert cache buffer layout mismatch")
-        data = manifest.get("data")
-        if not isinstance(data, dict) or data.get("name") != DATA_NAME:
-            raise ValueError("Invalid expert cache data filename")
-        if _int_field(data.get("size"), "data size", 1) != self.nbytes:
-            raise ValueError("Expert cache data size mismatch")
-        if not isinstance(data.get("sha256"), str) or not _SHA256.fullmatch(data["sha256"]):
-            raise ValueError("Invalid expert cache data SHA256")
-        fingerprint = manifest.get("model_fingerprint")
-        if not isinstance(fingerprint, str) or not _SHA256.fullmatch(fingerprint):
-            raise ValueError("Invalid expert cache model fingerprint")
-        self.model_fingerprint = fingerprint
+            raise ValueError("expert cache manifest: layers do not match the layout of the model geometry")
+        if fields["data.size"] != self.nbytes:
+            raise ValueError(f"expert cache manifest: data.size is {fields['data.size']}, the layout needs {self.nbytes}")
         self._data_path = self.cache_dir / DATA_NAME
         if not self._data_path.is_file() or self._data_path.stat().st_size != self.nbytes:
-            raise ValueError("Expert cache file is truncated or has extra data")
+            raise ValueError(f"expert cache data file {self._data_path} is truncated or has extra data")
         self._mmap: mmap.mmap | None = None
         self._mapping: Tensor | None = None
         self._stores: dict[int, StagedExperts] = {}
@@ -201,25 +247,23 @@ class ExpertCacheFile:
     @classmethod
     def open(cls, cache_dir: str | Path, *, verify_data: bool = False) -> "ExpertCacheFile":
         cache_dir = Path(cache_dir).resolve()
-        raw = (cache_dir / MANIFEST_NAME).read_bytes()
         try:
-            manifest = json.loads(raw)
+            manifest = json.loads((cache_dir / MANIFEST_NAME).read_bytes())
         except (UnicodeDecodeError, json.JSONDecodeError) as exc:
-            raise ValueError(f"Invalid JSON file: {cache_dir / MANIFEST_NAME}") from exc
-        if not isinstance(manifest, dict):
-            raise ValueError(f"Expected a JSON object: {cache_dir / MANIFEST_NAME}")
+            raise ValueError(f"expert cache manifest {cache_dir / MANIFEST_NAME} is not valid JSON") from exc
         cache = cls(cache_dir, manifest)
         if verify_data:
             cache.verify_data()
         return cache
 
     def verify_data(self) -> None:
+        """Hash the whole data file and compare with the manifest's data.sha256."""
         digest = hashlib.sha256()
         with self._data_path.open("rb") as handle:
             while chunk := handle.read(_CHUNK):
                 digest.update(chunk)
         if digest.hexdigest() != self.manifest["data"]["sha256"]:
-            raise ValueError("Expert cache data checksum mismatch")
+            raise ValueError("expert cache data checksum mismatch (data.sha256)")
 
     # -- mapping and views ---------------------------------------------------
     def _map(self) -> Tensor:
@@ -316,5 +360,5 @@ class ExpertCacheFile:
         self.close()
 
 
-__all__ = ["CACHE_FORMAT", "CACHE_FORMAT_VERSION", "DATA_NAME", "MANIFEST_NAME", "ExpertCacheFile",
-           "cache_layout", "write_expert_cache"]
+__all__ = ["CACHE_FORMAT", "CACHE_FORMAT_VERSION", "DATA_NAME", "MANIFEST_NAME", "MANIFEST_SCHEMA",
+           "ExpertCacheFile", "cache_layout", "check_manifest", "write_expert_cache"]

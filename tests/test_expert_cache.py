@@ -64,13 +64,17 @@ def _tampered(tmp_path, edit):
 
 
 @pytest.mark.parametrize("edit,error,message", [
-    (lambda m, d: m.update(format="other"), ValueError, "Unsupported expert cache format"),
-    (lambda m, d: m.update(format_version=2), ValueError, "Unsupported expert cache version"),
-    (lambda m, d: m.update(byte_order="big"), ValueError, "little-endian"),
-    (lambda m, d: m["model"].update(block_size=64), ValueError, "block size"),
-    (lambda m, d: m["layers"][1]["buffers"]["w2_weight"].update(offset=0), ValueError, "layout mismatch"),
-    (lambda m, d: m["data"].update(sha256="xyz"), ValueError, "Invalid expert cache data SHA256"),
-    (lambda m, d: m.update(model_fingerprint=None), ValueError, "fingerprint"),
+    (lambda m, d: m.update(format="other"), ValueError, "manifest: format must be"),
+    (lambda m, d: m.update(format_version=2), ValueError, "manifest: format_version must be"),
+    (lambda m, d: m.update(format_version=True), ValueError, "manifest: format_version must be"),
+    (lambda m, d: m.update(byte_order="big"), ValueError, "manifest: byte_order must be"),
+    (lambda m, d: m["model"].update(block_size=64), ValueError, "manifest: model.block_size must be"),
+    (lambda m, d: m["model"].pop("hidden"), ValueError, r"model.hidden must be an integer >= 1 \(missing\)"),
+    (lambda m, d: m.update(model="fish_omni"), ValueError, "manifest: model must be a JSON object"),
+    (lambda m, d: m["layers"][1]["buffers"]["w2_weight"].update(offset=0), ValueError, "layers do not match"),
+    (lambda m, d: m["data"].update(size=m["data"]["size"] + 1), ValueError, "data.size is"),
+    (lambda m, d: m["data"].update(sha256="xyz"), ValueError, "manifest: data.sha256 must be 64 lowercase hex"),
+    (lambda m, d: m.update(model_fingerprint=None), ValueError, "manifest: model_fingerprint must be"),
     (lambda m, d: (d / DATA_NAME).write_bytes((d / DATA_NAME).read_bytes()[:-4]), ValueError, "truncated"),
 ])
 def test_manifest_rejections(tmp_path, edit, error, message):
