@@ -215,60 +215,28 @@ def check_manifest(schema: dict[str, Any], manifest: Any, path: str = "") -> dic
     return values
 
 
-class ExpertCacheFile:
-    """A validated expert cache: private mapping, zero-copy role views, page locking."""
+class MappedExperts:
+    """Expert banks laid out in one file, mapped private and viewed in place.
 
-    def __init__(self, cache_dir: Path, manifest: dict[str, Any]) -> None:
-        self.cache_dir = Path(cache_dir)
-        self.manifest = manifest
-        if sys.byteorder != "little":
-            raise ValueError("expert cache files are little-endian; this host is not")
-        fields = check_manifest(MANIFEST_SCHEMA, manifest)
-        self.num_layers = fields["model.num_layers"]
-        self.num_experts = fields["model.num_experts"]
-        self.hidden = fields["model.hidden"]
-        self.intermediate = fields["model.intermediate"]
-        self.model_fingerprint = fields["model_fingerprint"]
-        # the buffer records follow from the geometry; the manifest must repeat them exactly
-        self._layers, self.nbytes = cache_layout(self.num_layers, self.num_experts, self.hidden, self.intermediate)
-        if manifest.get("layers") != self._layers:
-            raise ValueError("expert cache manifest: layers do not match the layout of the model geometry")
-        if fields["data.size"] != self.nbytes:
-            raise ValueError(f"expert cache manifest: data.size is {fields['data.size']}, the layout needs {self.nbytes}")
-        self._data_path = self.cache_dir / DATA_NAME
-        if not self._data_path.is_file() or self._data_path.stat().st_size != self.nbytes:
-            raise ValueError(f"expert cache data file {self._data_path} is truncated or has extra data")
+    A subclass sets ``_data_path``, ``nbytes``, ``num_layers`` and
+    ``_role_records(layer)`` (role name -> (byte offset, byte count, shape));
+    this class provides the mapping, zero-copy role views, the per-layer
+    staging store and page locking of layer windows.
+    """
+
+    def _init_mapping(self) -> None:
         self._mmap: mmap.mmap | None = None
         self._mapping: Tensor | None = None
         self._stores: dict[int, StagedExperts] = {}
         self._registered: list[tuple[int, int, int, int]] = []  # (base, bytes, first layer, end layer)
         self._closed = False
 
-    @classmethod
-    def open(cls, cache_dir: str | Path, *, verify_data: bool = False) -> "ExpertCacheFile":
-        cache_dir = Path(cache_dir).resolve()
-        try:
-            manifest = json.loads((cache_dir / MANIFEST_NAME).read_bytes())
-        except (UnicodeDecodeError, json.JSONDecodeError) as exc:
-            raise ValueError(f"expert cache manifest {cache_dir / MANIFEST_NAME} is not valid JSON") from exc
-        cache = cls(cache_dir, manifest)
-        if verify_data:
-            cache.verify_data()
-        return cache
+    def _role_records(self, layer: int) -> dict[str, tuple[int, int, tuple[int, ...]]]:
+        raise NotImplementedError
 
-    def verify_data(self) -> None:
-        """Hash the whole data file and compare with the manifest's data.sha256."""
-        digest = hashlib.sha256()
-        with self._data_path.open("rb") as handle:
-            while chunk := handle.read(_CHUNK):
-                digest.update(chunk)
-        if digest.hexdigest() != self.manifest["data"]["sha256"]:
-            raise ValueError("expert cache data checksum mismatch (data.sha256)")
-
-    # -- mapping and views ---------------------------------------------------
     def _map(self) -> Tensor:
         if self._closed:
-            raise RuntimeError("Expert cache is closed")
+            raise RuntimeError("Expert source is closed")
         if self._mapping is None:
             with self._data_path.open("rb") as handle:
                 self._mmap = mmap.mmap(handle.fileno(), self.nbytes, access=mmap.ACCESS_COPY)
@@ -277,25 +245,22 @@ class ExpertCacheFile:
 
     def _check_layer(self, layer: int) -> None:
         if not isinstance(layer, int) or isinstance(layer, bool) or not 0 <= layer < self.num_layers:
-            raise IndexError(f"Invalid expert cache layer index: {layer}")
+            raise IndexError(f"Invalid expert layer index: {layer}")
 
     def layer_span(self, layer: int) -> tuple[int, int]:
-        """(byte offset, byte count) of one layer in the data file."""
+        """(byte offset, byte count) of the smallest range holding one layer's four roles."""
         self._check_layer(layer)
-        buffers = self._layers[layer]["buffers"]
-        start = buffers[EXPERT_BUFFER_NAMES[0]]["offset"]
-        last = buffers[EXPERT_BUFFER_NAMES[-1]]
-        return start, last["offset"] + last["nbytes"] - start
+        records = self._role_records(layer).values()
+        start = min(offset for offset, _, _ in records)
+        end = max(offset + size for offset, size, _ in records)
+        return start, end - start
 
     def layer_buffers(self, layer: int) -> dict[str, Tensor]:
         """Zero-copy, read-only role views of one layer (must not be written)."""
         self._check_layer(layer)
         mapping = self._map()
-        out = {}
-        for name in EXPERT_BUFFER_NAMES:
-            spec = self._layers[layer]["buffers"][name]
-            out[name] = mapping.narrow(0, spec["offset"], spec["nbytes"]).view(ROLE_DTYPES[name][0]).view(spec["shape"])
-        return out
+        return {name: mapping.narrow(0, offset, size).view(ROLE_DTYPES[name][0]).view(shape)
+                for name, (offset, size, shape) in self._role_records(layer).items()}
 
     def layer_store(self, layer: int) -> StagedExperts:
         """The layer as a ``StagingArena`` store; the same object for every call, so
@@ -306,26 +271,26 @@ class ExpertCacheFile:
             self._stores[layer] = store
         return store
 
-    # -- page locking ----------------------------------------------------------
     def register(self, first: int = 0, count: int | None = None) -> int:
-        """Page-lock layers ``[first, first + count)`` (default: all) in place.
+        """Page-lock the bytes of layers ``[first, first + count)`` (default: all) in place.
 
         Returns the number of bytes locked (the window widened to whole pages).
-        A window may not overlap one already registered.
+        A window may not overlap or adjoin one already registered.
         """
         count = self.num_layers - first if count is None else count
         self._check_layer(first)
         if count < 1 or first + count > self.num_layers:
-            raise IndexError("Layer window outside the expert cache")
+            raise IndexError("Layer window outside the expert source")
         for _, _, a, b in self._registered:
             if first < b + 1 and a < first + count + 1:  # page widening can make neighbours touch
                 raise ValueError(f"Layers [{first}, {first + count}) overlap or adjoin registered layers [{a}, {b})")
-        start = self.layer_span(first)[0]
-        end_off, end_len = self.layer_span(first + count - 1)
+        spans = [self.layer_span(layer) for layer in range(first, first + count)]
+        start = min(offset for offset, _ in spans)
+        end = max(offset + size for offset, size in spans)
         mapping = self._map()
         base, size = ctypes.c_void_p(), ctypes.c_uint64()
         lib = _lib.library()
-        lib.check(lib.dll.drama_b200_host_register(mapping.data_ptr() + start, end_off + end_len - start, 1,
+        lib.check(lib.dll.drama_b200_host_register(mapping.data_ptr() + start, end - start, 1,
                                                    ctypes.byref(base), ctypes.byref(size)))
         self._registered.append((base.value, size.value, first, first + count))
         return size.value
@@ -353,12 +318,64 @@ class ExpertCacheFile:
         self._mmap = None
         self._closed = True
 
-    def __enter__(self) -> "ExpertCacheFile":
+    def __enter__(self):
         return self
 
     def __exit__(self, *exc) -> None:
         self.close()
 
 
+class ExpertCacheFile(MappedExperts):
+    """A validated expert cache: private mapping, zero-copy role views, page locking."""
+
+    def __init__(self, cache_dir: Path, manifest: dict[str, Any]) -> None:
+        self.cache_dir = Path(cache_dir)
+        self.manifest = manifest
+        if sys.byteorder != "little":
+            raise ValueError("expert cache files are little-endian; this host is not")
+        fields = check_manifest(MANIFEST_SCHEMA, manifest)
+        self.num_layers = fields["model.num_layers"]
+        self.num_experts = fields["model.num_experts"]
+        self.hidden = fields["model.hidden"]
+        self.intermediate = fields["model.intermediate"]
+        self.model_fingerprint = fields["model_fingerprint"]
+        # the buffer records follow from the geometry; the manifest must repeat them exactly
+        self._layers, self.nbytes = cache_layout(self.num_layers, self.num_experts, self.hidden, self.intermediate)
+        if manifest.get("layers") != self._layers:
+            raise ValueError("expert cache manifest: layers do not match the layout of the model geometry")
+        if fields["data.size"] != self.nbytes:
+            raise ValueError(f"expert cache manifest: data.size is {fields['data.size']}, the layout needs {self.nbytes}")
+        self._data_path = self.cache_dir / DATA_NAME
+        if not self._data_path.is_file() or self._data_path.stat().st_size != self.nbytes:
+            raise ValueError(f"expert cache data file {self._data_path} is truncated or has extra data")
+        self._init_mapping()
+
+    @classmethod
+    def open(cls, cache_dir: str | Path, *, verify_data: bool = False) -> "ExpertCacheFile":
+        cache_dir = Path(cache_dir).resolve()
+        try:
+            manifest = json.loads((cache_dir / MANIFEST_NAME).read_bytes())
+        except (UnicodeDecodeError, json.JSONDecodeError) as exc:
+            raise ValueError(f"expert cache manifest {cache_dir / MANIFEST_NAME} is not valid JSON") from exc
+        cache = cls(cache_dir, manifest)
+        if verify_data:
+            cache.verify_data()
+        return cache
+
+    def verify_data(self) -> None:
+        """Hash the whole data file and compare with the manifest's data.sha256."""
+        digest = hashlib.sha256()
+        with self._data_path.open("rb") as handle:
+            while chunk := handle.read(_CHUNK):
+                digest.update(chunk)
+        if digest.hexdigest() != self.manifest["data"]["sha256"]:
+            raise ValueError("expert cache data checksum mismatch (data.sha256)")
+
+    def _role_records(self, layer: int) -> dict[str, tuple[int, int, tuple[int, ...]]]:
+        buffers = self._layers[layer]["buffers"]
+        return {name: (buffers[name]["offset"], buffers[name]["nbytes"], tuple(buffers[name]["shape"]))
+                for name in EXPERT_BUFFER_NAMES}
+
+
 __all__ = ["CACHE_FORMAT", "CACHE_FORMAT_VERSION", "DATA_NAME", "MANIFEST_NAME", "MANIFEST_SCHEMA",
-           "ExpertCacheFile", "cache_layout", "check_manifest", "write_expert_cache"]
+           "ExpertCacheFile", "MappedExperts", "cache_layout", "check_manifest", "write_expert_cache"]

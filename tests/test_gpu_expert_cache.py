@@ -82,3 +82,31 @@ def test_registered_cache_stages_without_bounce(cuda_device, tmp_path):
     arena.close()
     cache.close()
     assert cache.registered_layers == []
+
+
+def test_packed_checkpoint_stages_from_the_page_locked_file(cuda_device, tmp_path):
+    """The packed safetensors checkpoint (shared_checkpoint.py's source) as an arena store."""
+    from drama_b200 import synthetic
+    from drama_b200.packed_checkpoint import PackedCheckpointExperts
+    from drama_b200.staging import StagedExperts, StagingArena, host_locked
+    from test_packed_checkpoint import write_packed
+
+    banks = [synthetic.fp8_bank(E, H, I, 500 + layer) for layer in range(2)]
+    packed = PackedCheckpointExperts.open(write_packed(tmp_path / "ckpt", banks))
+    packed.register(0, 2)
+    assert all(host_locked(t) for layer in range(2) for t in packed.layer_buffers(layer).values())
+    arena = StagingArena(4)
+    x = synthetic.hidden_states(3, H, 2, device=cuda_device)
+    for layer, chosen in ((0, [2, 7, 11]), (1, [0, 15])):
+        store = packed.layer_store(layer)
+        ids_host = torch.tensor(chosen, dtype=torch.int64)
+        local, w = synthetic.uniform_routes(3, 2, len(chosen), seed=layer, device=cuda_device)
+        with arena.session(store, cuda_device):
+            got = _forward(arena.stage(store, ids_host), x, local, w)
+        resident = StagedExperts(**{n: t[ids_host].to(cuda_device) for n, t in banks[layer].items()})
+        want = _forward(resident, x, local, w)
+        torch.cuda.synchronize()
+        assert torch.equal(got, want), layer
+    assert arena.stats.bounce_gathers == 0
+    arena.close()
+    packed.close()
