@@ -11,14 +11,35 @@
 // compute stream only waits for the bytes it is about to read.
 //
 // A pageable source would turn cudaMemcpyAsync into a staged, synchronous
-// copy and quietly remove the overlap, so it is rejected instead.
+// copy and quietly remove the overlap, so it is rejected instead; so is a
+// source that starts in a window registered here and runs past its end, and
+// no merged DMA crosses from one registered window into another.
 #include <unistd.h>
+
+#include <map>
+#include <mutex>
 
 #include "common.cuh"
 #include "kernels.h"
 
 namespace drama {
 namespace {
+
+// Windows page-locked through drama_b200_host_register: [start, end).
+std::mutex g_windows_mutex;
+std::map<uintptr_t, uintptr_t> g_windows;
+
+// The registered window holding byte p, or {0, 0} when p lies in none of them
+// (memory page-locked by its allocator, e.g. cudaHostAlloc).
+std::pair<uintptr_t, uintptr_t> window_of(const void* p) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    std::lock_guard<std::mutex> lock(g_windows_mutex);
+    auto it = g_windows.upper_bound(a);
+    if (it == g_windows.begin()) return {0, 0};
+    --it;
+    if (a < it->second) return {it->first, it->second};
+    return {0, 0};
+}
 
 int pointer_kind(const void* p, cudaMemoryType* type, int* device) {
     cudaPointerAttributes attr{};
@@ -57,6 +78,12 @@ int drama_b200_stage_copies(const void* const* host_src, void* const* dev_dst, c
                 return fail("copy %d: source byte %p is not page-locked host memory (pin it or cudaHostRegister it)",
                             i, q);
         }
+        // a source that starts in a registered window must end in it: the bytes
+        // after it may belong to another registration or none, and a DMA across
+        // the boundary would turn into a staged, synchronous copy
+        const auto window = window_of(host_src[i]);
+        if (window.second && reinterpret_cast<uintptr_t>(last) >= window.second)
+            return fail("copy %d: source runs past the end of its registered host window", i);
         if (pointer_kind(dev_dst[i], &type, &device)) return -1;
         if (type != cudaMemoryTypeDevice) return fail("copy %d: destination %p is not device memory", i, dev_dst[i]);
         if (dst_device < 0) dst_device = device;
@@ -73,8 +100,11 @@ int drama_b200_stage_copies(const void* const* host_src, void* const* dev_dst, c
         char* dst = static_cast<char*>(dev_dst[i]);
         uint64_t run = bytes[i];
         int j = i + 1;
+        // merge copies that continue one another in both address spaces and
+        // lie in the same registered window (or both in allocator-pinned memory)
+        const auto window = window_of(src);
         while (j < count && static_cast<const char*>(host_src[j]) == src + run &&
-               static_cast<char*>(dev_dst[j]) == dst + run) {
+               static_cast<char*>(dev_dst[j]) == dst + run && window_of(host_src[j]) == window) {
             run += bytes[j];
             ++j;
         }
@@ -114,6 +144,10 @@ int drama_b200_host_register(void* host_ptr, uint64_t bytes, int read_only, void
         return fail("cudaHostRegister of %llu bytes at %p: %s", (unsigned long long)(end - start),
                     reinterpret_cast<void*>(start), cudaGetErrorString(err));
     }
+    {
+        std::lock_guard<std::mutex> lock(g_windows_mutex);
+        g_windows[start] = end;
+    }
     *registered_base = reinterpret_cast<void*>(start);
     *registered_bytes = end - start;
     return 0;
@@ -143,6 +177,8 @@ int drama_b200_host_unregister(void* registered_base) {
         cudaGetLastError();
         return fail("cudaHostUnregister(%p): %s", registered_base, cudaGetErrorString(err));
     }
+    std::lock_guard<std::mutex> lock(g_windows_mutex);
+    g_windows.erase(reinterpret_cast<uintptr_t>(registered_base));
     return 0;
 }
 

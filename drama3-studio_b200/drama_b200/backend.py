@@ -60,6 +60,9 @@ class _Workspace:
 
     def __init__(self) -> None:
         self._buffers: dict[tuple[int, int], Tensor] = {}
+        # Buffers outgrown by a later call stay alive: a CUDA graph captured
+        # while one was current keeps writing to it on every replay.
+        self._retired: list[Tensor] = []
         self._lock = threading.Lock()
 
     def get(self, device: torch.device, nbytes: int) -> Tensor:
@@ -72,6 +75,8 @@ class _Workspace:
                     raise RuntimeError(
                         "drama_b200 workspace must be allocated before CUDA graph capture; "
                         "run one eager call of the same size first")
+                if buf is not None:
+                    self._retired.append(buf)
                 buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
                 self._buffers[key] = buf
             return buf
