@@ -235,6 +235,37 @@ int drama_b200_fp8_decode(const DramaB200Fp8Bank* bank, const void* x, int x_dty
     return finish_decode(a, workspace, workspace_bytes, stream);
 }
 
+size_t drama_b200_fp8_w8a8_workspace_bytes(int64_t tokens, int top_k, int hidden, int intermediate) {
+    return fp8_w8a8_workspace_layout(tokens, top_k, hidden, intermediate, nullptr, nullptr);
+}
+
+int drama_b200_fp8_w8a8_decode(const DramaB200Fp8Bank* bank, const void* x, int64_t tokens, int top_k,
+                               const void* ids, int ids_dtype, const void* weights, int weights_dtype, void* out,
+                               float* pair_out, void* x_fp8_out, float* x_scale_out, void* workspace,
+                               size_t workspace_bytes, void* stream) {
+    DecodeArgs a{};
+    if (prepare_fp8_decode(bank, x, DRAMA_B200_BF16, tokens, top_k, ids, ids_dtype, weights, weights_dtype, out,
+                           pair_out, &a))
+        return -1;
+    if (tokens == 0) return 0;
+    const size_t need = fp8_w8a8_workspace_layout(tokens, top_k, a.hidden, a.intermediate, nullptr, nullptr);
+    if (!workspace || workspace_bytes < need)
+        return fail("W8A8 workspace too small: need %zu bytes, got %zu", need, workspace_bytes);
+    if (reinterpret_cast<uintptr_t>(workspace) & 255u) return fail("workspace must be 256-byte aligned");
+    Fp8W8a8Workspace ws;
+    fp8_w8a8_workspace_layout(tokens, top_k, a.hidden, a.intermediate, static_cast<char*>(workspace), &ws);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t err = fp8_w8a8_launch(a.fp8, x, tokens, top_k, ids, ids_dtype, weights, weights_dtype, out, pair_out,
+                                      ws, s);
+    if (err == cudaSuccess && x_fp8_out)
+        err = cudaMemcpyAsync(x_fp8_out, ws.xq, static_cast<size_t>(tokens) * a.hidden, cudaMemcpyDeviceToDevice, s);
+    if (err == cudaSuccess && x_scale_out)
+        err = cudaMemcpyAsync(x_scale_out, ws.xs, static_cast<size_t>(tokens) * (a.hidden / 128) * 4,
+                              cudaMemcpyDeviceToDevice, s);
+    if (err != cudaSuccess) return fail("W8A8 decode launch failed: %s", cudaGetErrorString(err));
+    return 0;
+}
+
 int drama_b200_int4_decode(const DramaB200Int4Bank* bank, const void* x, int x_dtype, int64_t tokens,
                            int top_k, const void* ids, int ids_dtype, const void* weights, int weights_dtype,
                            void* out, float* pair_out, void* workspace, size_t workspace_bytes, void* stream) {

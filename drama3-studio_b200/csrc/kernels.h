@@ -254,6 +254,23 @@ cudaError_t w8a8_decode_launch(const DramaB200W8a8Bank& bank, const void* x, int
                                int out_dtype, float* pair_out, const W8a8Workspace& ws, int sm_count,
                                cudaStream_t s);
 
+// The official FP8 W8A8 contract (fp8_w8a8.cu): 1x128 E4M3 activations,
+// E4M3 tensor-core block dots, bf16 gate/up, requantised SwiGLU rows.
+struct Fp8W8a8Workspace {
+    int32_t* status;    // [4]: [0] pairs with an out-of-range id
+    uint8_t* xq;        // [T][H] E4M3 token rows
+    float* xs;          // [T][H/128]
+    float* h;           // [P][I] SwiGLU rows (fp32)
+    uint8_t* hq;        // [P][I] E4M3
+    float* hs;          // [P][I/128]
+    float* pair_out;    // [P][H] weighted fp32 partials
+};
+size_t fp8_w8a8_workspace_layout(int64_t tokens, int top_k, int hidden, int intermediate, char* base,
+                                 Fp8W8a8Workspace* ws);
+cudaError_t fp8_w8a8_launch(const DramaB200Fp8Bank& bank, const void* x, int64_t tokens, int top_k, const void* ids,
+                            int ids_dtype, const void* weights, int weights_dtype, void* out, float* pair_out,
+                            const Fp8W8a8Workspace& ws, cudaStream_t s);
+
 // Shared expert + gate fused with the routed combine (shared_expert.cu).
 constexpr int kMaxSharedTokens = 4096;
 struct SharedWorkspace {

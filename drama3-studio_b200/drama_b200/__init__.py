@@ -7,12 +7,13 @@ Compute runs only in ``lib/libdrama_b200.so`` (hand-written CUDA for sm_100a,
 C ABI in ``include/drama_b200.h``); there is no CPU fallback.
 """
 
-from .backend import B200ExpertBackend, QuantizedB200Backend, QuantizedBank  # noqa: F401
+from .backend import B200ExpertBackend, Fp8W8a8B200Backend, QuantizedB200Backend, QuantizedBank  # noqa: F401
 from .resident import ResidentExpertManager, install_resident_experts  # noqa: F401
 from .router import permute_routes, route_topk  # noqa: F401
 
 __all__ = [
     "B200ExpertBackend",
+    "Fp8W8a8B200Backend",
     "QuantizedB200Backend",
     "QuantizedBank",
     "ResidentExpertManager",

@@ -37,6 +37,8 @@ EXPORTS = (
     "drama_b200_decode_status_offset",
     "drama_b200_fp8_decode",
     "drama_b200_int4_decode",
+    "drama_b200_fp8_w8a8_workspace_bytes",
+    "drama_b200_fp8_w8a8_decode",
     "drama_b200_w8a8_workspace_bytes",
     "drama_b200_w8a8_decode",
     "drama_b200_shared_expert_workspace_bytes",
@@ -154,6 +156,11 @@ class Library:
                        c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]
         dll.drama_b200_fp8_decode.argtypes = [ctypes.POINTER(Fp8Bank)] + decode_args
         dll.drama_b200_int4_decode.argtypes = [ctypes.POINTER(Int4Bank)] + decode_args
+        dll.drama_b200_fp8_w8a8_workspace_bytes.argtypes = [c_int64, c_int, c_int, c_int]
+        dll.drama_b200_fp8_w8a8_workspace_bytes.restype = c_size_t
+        dll.drama_b200_fp8_w8a8_decode.argtypes = [
+            ctypes.POINTER(Fp8Bank), c_void_p, c_int64, c_int, c_void_p, c_int, c_void_p, c_int, c_void_p,
+            c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]
         dll.drama_b200_w8a8_decode.argtypes = [ctypes.POINTER(W8a8Bank)] + decode_args
         dll.drama_b200_w8a8_decode.restype = c_int
         dll.drama_b200_w8a8_workspace_bytes.argtypes = [c_int64, c_int, c_int, c_int]

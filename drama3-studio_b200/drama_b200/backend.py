@@ -276,6 +276,54 @@ class B200ExpertBackend(_DecodeBackend):
         return super().forward(x, ids, weights, staged)
 
 
+class Fp8W8a8B200Backend(_DecodeBackend):
+    """FP8 experts with the official W8A8 arithmetic of ``TritonExpertBackend``.
+
+    The reference's production GPU backend (``offload.py:247-356``) runs the
+    upstream FP8 MoE kernels: token rows and SwiGLU rows quantised to E4M3 in
+    1x128 blocks, E4M3 x E4M3 block dots promoted with both block scales
+    (``fp8_decode.py:114-147``; CPU statement ``native/src/runtime.cpp:
+    162-237``). This backend computes that contract on the same staged banks
+    as ``B200ExpertBackend`` (whose arithmetic is the W16A16 dequant path of
+    ``TorchExpertBackend``); rows must be bfloat16.
+    """
+
+    entry = "drama_b200_fp8_w8a8_decode"
+
+    def _bank(self, staged, hidden):
+        return _fp8_bank(staged, hidden)
+
+    def _workspace_bytes(self, lib, tokens, top_k, hidden, intermediate) -> int:
+        return lib.dll.drama_b200_fp8_w8a8_workspace_bytes(tokens, top_k, hidden, intermediate)
+
+    def _run(self, x: Tensor, ids: Tensor, weights: Tensor, staged, *, combine: bool,
+             x_fp8: Tensor | None = None, x_scale: Tensor | None = None) -> Tensor:
+        if x.dtype != torch.bfloat16:
+            raise ValueError("The FP8 W8A8 backend quantises bfloat16 hidden rows")
+        hidden = x.shape[-1]
+        bank, keep = self._bank(staged, hidden)
+        _check_common(x, ids, weights, bank.slots, hidden, self.validate_ids)
+        tokens, top_k = ids.shape
+        if tokens * top_k > MAX_DECODE_PAIRS:
+            return self._chunked(x, ids, weights, staged, combine=combine)
+        x, ids, weights = x.contiguous(), ids.contiguous(), weights.contiguous()
+        if weights.dtype not in FLOAT_DTYPES:
+            weights = weights.float()
+        lib = _lib.library()
+        if combine:
+            out, pair_out = torch.empty_like(x), None
+        else:
+            out, pair_out = None, torch.empty((tokens * top_k, hidden), device=x.device, dtype=torch.float32)
+        nbytes = self._workspace_bytes(lib, tokens, top_k, hidden, bank.intermediate)
+        ws = _WORKSPACES.get(x.device, nbytes)
+        lib.check(lib.dll.drama_b200_fp8_w8a8_decode(
+            ctypes.byref(bank), x.data_ptr(), tokens, top_k, ids.data_ptr(), _lib.DTYPE_CODES[ids.dtype],
+            weights.data_ptr(), _lib.DTYPE_CODES[weights.dtype], _lib.ptr(out), _lib.ptr(pair_out),
+            _lib.ptr(x_fp8), _lib.ptr(x_scale), ws.data_ptr(), ws.numel(), _lib.stream_handle(x.device)))
+        del keep
+        return out if combine else pair_out
+
+
 def fp8_prefill(x: Tensor, ids: Tensor, weights: Tensor, staged, *, validate_ids: bool = True) -> Tensor:
     """Many-token FP8 expert forward on the grouped tensor-core GEMMs.
 

@@ -149,6 +149,31 @@ DRAMA_B200_API int drama_b200_fp8_decode(const DramaB200Fp8Bank* bank, const voi
                                          void* workspace, size_t workspace_bytes,
                                          void* stream);
 
+/* ---------------------------------------------------------------------------
+ * The official FP8 W8A8 decode contract of the reference's production GPU
+ * backend (TritonExpertBackend / fp8_decode.forward and quantized_pairs,
+ * src/drama_low_vram/fp8_decode.py:114-147, decode_gemm 24-58; CPU statement
+ * native/src/runtime.cpp:162-237, fp8_cpu_reference.py:14-52) on the same
+ * FP8 bank as drama_b200_fp8_decode:
+ *   x -> 1x128 E4M3 blocks, scale = max(amax, 1e-10) * (1/448);
+ *   gu = sum over blocks of fma(dot(W13, q) * scale, block scale, acc);
+ *   h = (bf16(gate) / (1 + exp(-bf16(gate)))) * bf16(up) -> 1x128 E4M3;
+ *   down likewise; partial = down * weight (fp32); out = bf16(slot-order sum).
+ * x: bf16 [tokens, H]; out (bf16 [tokens, H]) and/or pair_out (fp32
+ * [tokens*top_k, H], forward_pairs) ; x_fp8_out (uint8 [tokens, H]) and
+ * x_scale_out (fp32 [tokens, H/128]), when given, receive the quantised token
+ * rows. Ids outside [0, slots) contribute zero and are counted in workspace
+ * status word 0. H, I multiples of 128; pairs <= 4096.
+ * ------------------------------------------------------------------------- */
+DRAMA_B200_API size_t drama_b200_fp8_w8a8_workspace_bytes(int64_t tokens, int top_k, int hidden,
+                                                          int intermediate);
+
+DRAMA_B200_API int drama_b200_fp8_w8a8_decode(const DramaB200Fp8Bank* bank, const void* x, int64_t tokens,
+                                              int top_k, const void* ids, int ids_dtype, const void* weights,
+                                              int weights_dtype, void* out, float* pair_out, void* x_fp8_out,
+                                              float* x_scale_out, void* workspace, size_t workspace_bytes,
+                                              void* stream);
+
 DRAMA_B200_API int drama_b200_int4_decode(const DramaB200Int4Bank* bank, const void* x,
                                           int x_dtype, int64_t tokens, int top_k,
                                           const void* ids, int ids_dtype, const void* weights,
