@@ -61,6 +61,10 @@ def parse_args():
     p.add_argument("--host-layers", type=int, default=48,
                    help="offload: distinct pinned host stores (layers beyond reuse them in turn)")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--router", choices=("fused", "torch"), default="fused",
+                   help="decode: router in the fused layer kernel, or torch's RMSNorm/linear in front (bit-exact ids)")
+    p.add_argument("--no-ep", action="store_true",
+                   help="decode: skip the config-4 expert-parallel sub-record (\"ep\") of the headline line")
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
     return p.parse_args()
 
@@ -327,7 +331,7 @@ def config_dict(args, world: int) -> dict:
                      f"intermediate {INTER}, E4M3 128x128 block scales), decode batch 1, "
                      f"{args.decode_steps} steps per CUDA graph, all experts resident"),
         "layers": args.layers, "hidden": HIDDEN, "experts": EXPERTS, "top_k": TOP_K, "intermediate": INTER,
-        "batch": 1, "decode_steps_per_graph": args.decode_steps,
+        "batch": 1, "decode_steps_per_graph": args.decode_steps, "router": getattr(args, "router", "fused"),
         "parallelism": f"replicas{world}" if world > 1 else "single",
         "l2": "inputs larger than L2: 29 GB of resident banks, ~1.84 GB of routed weights per token",
     }
@@ -355,7 +359,7 @@ def run_ours(args) -> None:
     t0 = time.perf_counter()
     layers = stack.synthetic_stack(args.layers, experts=EXPERTS, hidden=HIDDEN, intermediate=INTER,
                                    seed=rank, device=device)
-    st = stack.DecodeStack(layers, tokens=1, top_k=TOP_K)
+    st = stack.DecodeStack(layers, tokens=1, top_k=TOP_K, router=args.router)
     steps_per_graph = args.decode_steps
     inputs = torch.stack([synthetic.hidden_states(1, HIDDEN, 10_000 + s, device=device)
                           for s in range(steps_per_graph)])
@@ -449,7 +453,20 @@ def run_ours(args) -> None:
             torch_ref.layer()
             line["cpu_baseline"]["torch_dequant"] = torch_ref.sample(args.cpu_seconds / 2, args.layers)
     del graph
+    if not args.no_ep:
+        # config 4 at the same N: the driver's 1 -> 8 runs then also time expert parallelism
+        del st, layers, inputs, outputs
+        torch.cuda.empty_cache()
+        ep_line, model, ep_graph = measure_ep(args, world, rank, device, gpu_id)
+        line["ep"] = {k: ep_line[k] for k in ("metric", "value", "unit", "n_gpus", "ms_per_step", "scaling",
+                                                 "roofline", "e2e", "gpu_launches", "checksum", "clocks")}
+        line["ep"]["workload"] = ep_line["config"]["workload"]
+        line["ep"]["exchange"] = ep_line["config"]["exchange"]
+        line["ep"]["peer_wait_timed_out"] = ep_line["peer_wait_timed_out"]
+        del ep_graph
+        model.close()
     if world > 1:
+        dist.barrier()
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(line))
@@ -634,6 +651,27 @@ def run_ep(args) -> None:
     replay of a CUDA graph holding all 48 layers (dispatch, NCCL all-to-alls,
     grouped GEMMs, combine). ``value`` = 256 tokens / max-over-ranks step time.
     """
+    import torch.distributed as dist
+
+    world, rank, device, gpu_id = _dist_setup()
+    line, model, graph = measure_ep(args, world, rank, device, gpu_id)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        ref = CpuReference(_ep_bank(0, range(0, EXPERTS), device))
+        ref.layer()
+        cpu = ref.sample(args.cpu_seconds, args.layers)
+        cpu["sample"] += "; one token per step (the workload's 256 tokens would take 256x as long)"
+        line["cpu_baseline"] = cpu
+    del graph
+    model.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line))
+
+
+def measure_ep(args, world: int, rank: int, device, gpu_id: str):
+    """Build, capture and time the config-4 EP step on this rank; returns (line, model, graph)."""
     import torch
     import torch.distributed as dist
 
@@ -641,7 +679,6 @@ def run_ep(args) -> None:
     from drama_b200.expert_parallel import (ExpertParallelMoE, balanced_placement, experts_of_rank, nccl_all_to_all,
                                             shard_tokens)
 
-    world, rank, device, gpu_id = _dist_setup()
     t0 = time.perf_counter()
     rows = shard_tokens(EP_TOKENS, world, rank)
 
@@ -755,19 +792,7 @@ def run_ep(args) -> None:
         "checksum": checksum, "dropped_pairs": list(dropped), "peer_wait_timed_out": timed_out,
         "setup_s": round(build_s, 1),
     }
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        ref = CpuReference(_ep_bank(0, range(0, EXPERTS), device))
-        ref.layer()
-        cpu = ref.sample(args.cpu_seconds, args.layers)
-        cpu["sample"] += "; one token per step (the workload's 256 tokens would take 256x as long)"
-        line["cpu_baseline"] = cpu
-    del graph
-    model.close()
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
-    if rank == 0:
-        print(json.dumps(line))
+    return line, model, graph
 
 
 def _sum_over_ranks(value: float, world: int, device) -> float:

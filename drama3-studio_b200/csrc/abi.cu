@@ -790,6 +790,8 @@ int drama_b200_ipc_close(void* device_ptr) {
 }
 
 namespace {
+constexpr long long kMaxPeerWaitNs = 60'000'000'000LL;  // one minute
+
 int check_peers(const DramaB200EpPeers* peers) {
     if (!peers) return fail("peers are required");
     const DramaB200EpPeers& q = *peers;
@@ -801,6 +803,7 @@ int check_peers(const DramaB200EpPeers* peers) {
     for (int r = 0; r < q.ranks; ++r)
         if (!q.recv[r] || !q.back[r] || !q.signals[r]) return fail("rank %d's exchange buffers are missing", r);
     if (!q.epoch || !q.done) return fail("epoch and done counters are required");
+    if (q.wait_ns < 0 || q.wait_ns > kMaxPeerWaitNs) return fail("wait_ns must be in [0, %lld]", kMaxPeerWaitNs);
     return 0;
 }
 }  // namespace
@@ -854,6 +857,7 @@ int drama_b200_fp8_expert_rows_p2p(const DramaB200Fp8Bank* bank, const DramaB200
     rc.cap = peers->capacity;
     rc.unused = b.slots;
     rc.status = status;
+    rc.wait_ns = peers->wait_ns;
     RowsScatter sc;
     sc.ranks = peers->ranks;
     sc.rank = me;
@@ -884,7 +888,7 @@ int drama_b200_ep_p2p_combine(const DramaB200EpPeers* peers, const int32_t* pair
     const cudaError_t err = ep_combine_launch(peers->back[me], peers->capacity * peers->ranks, pair_rows, weights,
                                               weights_dtype, tokens, top_k, peers->hidden, residual, out, sms,
                                               static_cast<cudaStream_t>(stream), peers->signals[me] + 2 * peers->ranks,
-                                              peers->epoch, peers->ranks, status);
+                                              peers->epoch, peers->ranks, status, peers->wait_ns);
     if (err != cudaSuccess) return fail("peer combine launch failed: %s", cudaGetErrorString(err));
     return 0;
 }

@@ -23,8 +23,9 @@
 //     last CTA publishes the return flags;
 //   combine (expert_parallel.cu): waits for every return flag, then sums the
 //   route slots from the local back buffer.
-// Every wait gives up after 2 s of global time and records status[2]; the
-// step's result is then invalid but no kernel hangs. Waits are on flags
+// Every wait gives up after the descriptor's wait_ns (2 s when 0) of global
+// time and records status[2]; the step's result is then invalid but no kernel
+// hangs. Waits are on flags
 // written by other GPUs (never by another launch on the same GPU).
 //
 // Reuse is safe without further flags: rank A writes rank B's recv block of

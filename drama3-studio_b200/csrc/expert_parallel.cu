@@ -211,13 +211,14 @@ cudaError_t ep_dispatch_launch(const void* hidden, int64_t tokens, int H, const 
 cudaError_t ep_combine_launch(const void* rows, int64_t row_count, const int32_t* pair_rows, const void* weights,
                               int weights_dtype, int64_t tokens, int top_k, int H, const void* residual, void* out,
                               int sm_count, cudaStream_t s, const int32_t* wait_flags, const int32_t* wait_epoch,
-                              int wait_ranks, int32_t* status) {
+                              int wait_ranks, int32_t* status, int64_t wait_ns) {
     PeerWait w;
     w.flags = wait_flags;
     w.epoch = wait_epoch;
     w.ranks = wait_ranks;
     w.bit = 2;
     w.status = status;
+    w.limit_ns = peer_wait_limit(wait_ns);
     if (tokens > 0 || wait_flags)
         ep_combine_kernel<<<grid_for(tokens * (H / 8), sm_count), 256, 0, s>>>(
             static_cast<const __nv_bfloat16*>(rows), row_count, pair_rows, weights, weights_dtype, tokens, top_k, H,

@@ -90,6 +90,7 @@ __global__ void rows_to_f16_kernel(const __nv_bfloat16* x, int64_t x_stride, int
     pw.ranks = recv.ranks;
     pw.bit = 1;
     pw.status = recv.status;
+    pw.limit_ns = peer_wait_limit(recv.wait_ns);
     peer_wait_cta(pw);
     if (recv.signals) {
         if (static_cast<int>(threadIdx.x) < recv.ranks)

@@ -204,6 +204,7 @@ struct RowsReceive {
     int64_t cap = 0;
     int unused = 0;
     int32_t* status = nullptr;
+    int64_t wait_ns = 0;               // limit of the flag wait; 0: the default (2 s)
 };
 cudaError_t expert_rows_launch(const DramaB200Fp8Bank& bank, const void* x, int64_t x_stride, int64_t rows,
                                const void* ids, int ids_dtype, void* out, const RowsWorkspace& ws, int sm_count,
@@ -219,7 +220,8 @@ cudaError_t ep_dispatch_launch(const void* hidden, int64_t tokens, int H, const 
 cudaError_t ep_combine_launch(const void* rows, int64_t row_count, const int32_t* pair_rows, const void* weights,
                               int weights_dtype, int64_t tokens, int top_k, int H, const void* residual, void* out,
                               int sm_count, cudaStream_t s, const int32_t* wait_flags = nullptr,
-                              const int32_t* wait_epoch = nullptr, int wait_ranks = 0, int32_t* status = nullptr);
+                              const int32_t* wait_epoch = nullptr, int wait_ranks = 0, int32_t* status = nullptr,
+                              int64_t wait_ns = 0);
 
 // Expert-parallel exchange over peer memory (ep_p2p.cu).
 constexpr int kP2pMaxPairs = 4096;  // (token, slot) pairs per rank and layer of the fused peer dispatch

@@ -127,7 +127,7 @@ class EpPeers(ctypes.Structure):
         ("ranks", ctypes.c_int32), ("rank", ctypes.c_int32), ("capacity", c_int64),
         ("hidden", ctypes.c_int32), ("experts", ctypes.c_int32),
         ("recv", c_void_p * 8), ("back", c_void_p * 8), ("signals", c_void_p * 8),
-        ("epoch", c_void_p), ("done", c_void_p),
+        ("epoch", c_void_p), ("done", c_void_p), ("wait_ns", c_int64),
     ]
 
 

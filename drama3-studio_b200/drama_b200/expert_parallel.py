@@ -107,11 +107,13 @@ class PeerExchange:
     Created collectively (every rank of ``group`` at once): each rank
     allocates its receive / return / signal buffers in the library, the CUDA
     IPC handles go round with ``all_gather``, and each rank opens the others'.
-    ``close`` (also collective) unmaps and frees them.
+    ``close`` (also collective) unmaps and frees them. Every flag wait of the
+    exchange gives up after ``wait_ns`` nanoseconds (0: 2 s) and records it in
+    the layer's status word 2.
     """
 
     def __init__(self, *, ranks: int, rank: int, capacity: int, hidden: int, experts: int, device,
-                 group=None) -> None:
+                 group=None, wait_ns: int = 0) -> None:
         import torch.distributed as dist
 
         self.lib = lib = _lib.library()
@@ -134,6 +136,7 @@ class PeerExchange:
         peers = _lib.EpPeers()
         peers.ranks, peers.rank, peers.capacity = ranks, rank, capacity
         peers.hidden, peers.experts = hidden, experts
+        peers.wait_ns = wait_ns
         self._opened = []
         for r in range(ranks):
             if r == rank:
@@ -204,7 +207,8 @@ class ExpertParallelMoE:
 
     def __init__(self, banks: Sequence, *, experts: int, top_k: int, tokens: int, ranks: int = 1, rank: int = 0,
                  all_to_all: AllToAll | None = None, capacity: int | None = None,
-                 placements: Sequence[Tensor | None] | None = None, exchange: str = "nccl", group=None) -> None:
+                 placements: Sequence[Tensor | None] | None = None, exchange: str = "nccl", group=None,
+                 peer_wait_ns: int = 0, peer_exchange: PeerExchange | None = None) -> None:
         if not banks:
             raise ValueError("At least one layer bank is required")
         self.ranks, self.rank = ranks, rank
@@ -238,9 +242,16 @@ class ExpertParallelMoE:
         self.lib = _lib.library()
         self.buffers = self._allocate()
         self.peer_exchange = None
-        if exchange == "p2p":
+        if exchange == "p2p" and peer_exchange is not None:
+            # built by the caller (anything with a matching ``peers`` descriptor and ``close``)
+            q = peer_exchange.peers
+            if (q.ranks, q.rank, q.capacity, q.hidden, q.experts) != (ranks, rank, self.capacity, self.hidden, experts):
+                raise ValueError("The peer exchange does not match this layer stack's ranks, capacity or shapes")
+            self.peer_exchange = peer_exchange
+        elif exchange == "p2p":
             self.peer_exchange = PeerExchange(ranks=ranks, rank=rank, capacity=self.capacity, hidden=self.hidden,
-                                              experts=experts, device=self.device, group=group)
+                                              experts=experts, device=self.device, group=group,
+                                              wait_ns=peer_wait_ns)
 
     def _allocate(self) -> ExchangeBuffers:
         rows = self.ranks * self.capacity
@@ -311,7 +322,7 @@ class ExpertParallelMoE:
             self.peer_exchange = None
 
     def timed_out(self) -> bool:
-        """Whether a peer wait of the last layers gave up (synchronises)."""
+        """Whether a peer wait of the layers so far gave up (synchronises)."""
         return bool(self.buffers.status[2].item())
 
     # The three device steps (CUDA kernels of this library).

@@ -475,9 +475,11 @@ DRAMA_B200_API int drama_b200_ep_combine(const void* rows, int64_t row_count, co
  *   drama_b200_fp8_expert_rows_p2p (waits for every source; results into
  *                                   the sources' back, then return flags)
  *   drama_b200_ep_p2p_combine      (waits for every expert rank; slot sum)
- * Every rank must issue the same sequence of layers. Waits give up after 2 s
- * and set status[2]; the result of that step is then invalid. The counters
- * block (epoch, dispatch and GEMM arrival counts) is 256 zeroed bytes.
+ * Every rank must issue the same sequence of layers. Waits give up after
+ * wait_ns nanoseconds of global time (0: 2 s; at most 60 s) and set status[2]
+ * (bit 1: the row prep's wait for a source, bit 2: the combine's wait for an
+ * expert rank); the result of that step is then invalid. The counters block
+ * (epoch, dispatch and GEMM arrival counts) is 256 zeroed bytes.
  * ------------------------------------------------------------------------- */
 typedef struct DramaB200EpPeers {
     int32_t ranks, rank;
@@ -488,6 +490,7 @@ typedef struct DramaB200EpPeers {
     int32_t* signals[8];
     int32_t* epoch;             /* this rank's step counter */
     int32_t* done;              /* this rank's arrival counters (32 int32, zeroed) */
+    int64_t wait_ns;            /* limit of every peer wait; 0: 2 s */
 } DramaB200EpPeers;
 
 DRAMA_B200_API int drama_b200_ep_buffers_alloc(int ranks, int64_t capacity, int hidden, void** recv, void** back,

@@ -10,6 +10,9 @@
 * G = 2 and 4 emulated on one GPU (every rank's steps run in turn, the
   all-to-all done by copying blocks) and, when two GPUs are present, G = 2
   over NCCL: the result must equal G = 1 bit for bit.
+* The peer exchange's bounded waits: a rank that never publishes its flags
+  makes the other rank's waits give up after the limit it set, with the
+  timeout recorded in the status word and no fault.
 """
 
 from __future__ import annotations
@@ -53,7 +56,8 @@ def _placements(routes, ranks, device):
                          dtype=torch.int32, device=device) for ids, _ in routes]
 
 
-def _model(banks, ranks=1, rank=0, tokens=T, all_to_all=None, capacity=None, placements=None, exchange="nccl"):
+def _model(banks, ranks=1, rank=0, tokens=T, all_to_all=None, capacity=None, placements=None, exchange="nccl",
+           peer_exchange=None):
     from drama_b200.expert_parallel import ExpertParallelMoE, experts_of_rank, shard_experts
 
     local = []
@@ -63,7 +67,7 @@ def _model(banks, ranks=1, rank=0, tokens=T, all_to_all=None, capacity=None, pla
         local.append(Bank({n: v[held] for n, v in b.items()}))
     return ExpertParallelMoE(local, experts=E, top_k=K, tokens=tokens, ranks=ranks, rank=rank,
                              all_to_all=all_to_all or (lambda o, i: None), capacity=capacity, placements=placements,
-                             exchange=exchange)
+                             exchange=exchange, peer_exchange=peer_exchange)
 
 
 def _dispatch_restated(h, ids, experts, ranks, cap, placement=None):
@@ -239,6 +243,81 @@ def test_peer_exchange_on_one_rank_equals_the_nccl_path(cuda_device):
     assert torch.equal(y, x) and torch.equal(g_in, x)
     del graph
     p2p.close()
+
+
+class _LoopbackExchange:
+    """Every rank's exchange buffers allocated by this process on one GPU, driven as rank ``rank`` alone."""
+
+    def __init__(self, ranks, rank, capacity, device, wait_ns):
+        import ctypes
+
+        from drama_b200 import _lib
+
+        self.lib = lib = _lib.library()
+        self.device = device
+        peers = _lib.EpPeers()
+        peers.ranks, peers.rank, peers.capacity, peers.hidden, peers.experts = ranks, rank, capacity, H, E
+        self.sets = []
+        with torch.cuda.device(device):
+            for r in range(ranks):
+                ptrs = [ctypes.c_void_p() for _ in range(4)]
+                lib.check(lib.dll.drama_b200_ep_buffers_alloc(ranks, capacity, H, *[ctypes.byref(q) for q in ptrs]))
+                self.sets.append([q.value for q in ptrs])
+                peers.recv[r], peers.back[r], peers.signals[r] = self.sets[-1][:3]
+        peers.epoch, peers.done = self.sets[rank][3], self.sets[rank][3] + 64
+        peers.wait_ns = wait_ns
+        self.peers = peers
+
+    def close(self):
+        torch.cuda.synchronize(self.device)
+        with torch.cuda.device(self.device):
+            for bufs in self.sets:
+                self.lib.check(self.lib.dll.drama_b200_ep_buffers_free(*bufs))
+        self.sets = []
+
+
+def test_peer_waits_run_out_when_a_rank_never_publishes(cuda_device):
+    """Rank 1 of two never runs: rank 0's row prep waits for rank 1's dispatch
+    flag and its combine for rank 1's return flag, flags that nothing sets.
+    Both waits give up after the 20 ms asked for, the kernels return, status
+    word 2 records both (bit 1: row prep, bit 2: combine) and the GPU goes on
+    working: the same layer on one rank afterwards gives its usual bits."""
+    import ctypes
+    import time
+
+    from drama_b200 import _lib
+
+    banks, routes, h = _inputs(cuda_device)
+    tl = T // 2
+    ids, w = routes[0][0][:tl].contiguous(), routes[0][1][:tl].contiguous()
+    single = _model(banks)
+    expected = h.clone()
+    single.layer(expected, routes[0][0], routes[0][1], 0, out=expected)
+
+    exchange = _LoopbackExchange(2, 0, tl * K, cuda_device, wait_ns=20_000_000)
+    model = _model(banks, ranks=2, rank=0, tokens=tl, exchange="p2p", peer_exchange=exchange)
+    x = h[:tl].clone()
+    torch.cuda.synchronize()
+    start = time.monotonic()
+    model.layer(x, ids, w, 0, out=x)
+    torch.cuda.synchronize()
+    elapsed = time.monotonic() - start
+    assert model.timed_out()
+    assert int(model.buffers.status[2].item()) == 1 | 2
+    assert elapsed < 1.5, f"the waits took {elapsed:.2f} s; the limit asked for was 20 ms (default 2 s each)"
+
+    lib = _lib.library()
+    exchange.peers.wait_ns = -1
+    bad = lib.dll.drama_b200_ep_p2p_combine(
+        ctypes.byref(exchange.peers), model.buffers.pair_rows.data_ptr(), w.data_ptr(), _lib.BF16, tl, K,
+        x.data_ptr(), x.data_ptr(), model.buffers.status.data_ptr(), _lib.stream_handle(cuda_device))
+    assert bad == -1 and "wait_ns" in lib.dll.drama_b200_error().decode()
+    model.close()
+
+    again = h.clone()
+    single.layer(again, routes[0][0], routes[0][1], 0, out=again)
+    torch.cuda.synchronize()
+    assert torch.equal(again, expected)
 
 
 def test_small_capacity_drops_and_counts_overflow(cuda_device):

@@ -16,7 +16,9 @@ manager keeps its own host routing, grouping and residency logic:
 
 The same manager with the reference's ``TorchExpertBackend`` (its W16A16
 dequant path) is the expected value; this repository's ``B200ExpertBackend``
-must agree within the 2e-2 bar. A second test replaces the manager's
+must agree within the 2e-2 bar. GPTQ W4A16 banks (mode 0) run the same way:
+``QuantizedB200Backend(0)`` under the manager against the manager running the
+reference's ``QuantizedExpertBackend(0)`` and against the oracle. A second test replaces the manager's
 ``_StagingPool`` with ``StagingArena`` and configures the reference's
 ``HostResidency`` RAM tier (``host_residency.py:53-358``) through the
 manager's own ``configure_host_residency``: the residency logic decides where
@@ -114,6 +116,99 @@ def test_reference_manager_with_b200_backend(cuda_device, config):
     assert mine.stats.forward_calls == len(calls)
     if config.get("cache_experts"):
         assert mine.stats.expert_cache_hits + mine.stats.expert_loads > 0
+    mine.close()
+    ref.close()
+
+
+class Int4Store:
+    """A GPTQ W4A16 bank as the reference's ``QuantizedStore`` holds it (mode 0,
+    ``quantized_model.py:27-68``): int32 nibble words [E, N, K/8], fp16 group
+    scales [E, N, K/128], symmetric codes. ``quantized_model.py`` itself imports
+    the full TTS stack, so the store is restated here with the members the
+    manager reads (``num_experts``, ``hidden``, ``intermediate``, ``nbytes``,
+    ``validate``)."""
+
+    mode = 0
+
+    def __init__(self, bank, hidden, inter):
+        for name in ("w13_weight", "w13_scale_inv", "w2_weight", "w2_scale_inv"):
+            setattr(self, name, bank[name].contiguous())
+        self.hidden, self.intermediate = hidden, inter
+
+    @property
+    def num_experts(self):
+        return self.w13_weight.shape[0]
+
+    @property
+    def nbytes(self):
+        return sum(getattr(self, n).numel() * getattr(self, n).element_size()
+                   for n in ("w13_weight", "w13_scale_inv", "w2_weight", "w2_scale_inv"))
+
+    def validate(self):
+        for bank, scales, n, k in ((self.w13_weight, self.w13_scale_inv, 2 * self.intermediate, self.hidden),
+                                   (self.w2_weight, self.w2_scale_inv, self.hidden, self.intermediate)):
+            assert bank.device.type == "cpu" and bank.dtype == torch.int32 and bank.shape[1:] == (n, k // 8)
+            assert scales.dtype == torch.float16 and scales.shape[1:] == (n, k // 128)
+
+
+class Int4Layer(nn.Module):
+    """A routed-expert module bound to a quantized store, as ``quantized_model._bind`` leaves it."""
+
+    def __init__(self, store):
+        super().__init__()
+        for name in ("w13_weight", "w13_scale_inv", "w2_weight", "w2_scale_inv"):
+            self._buffers[name] = getattr(store, name)
+        self._drama_quant_store = store
+
+    def forward(self, x, ids, weights):  # replaced by the manager
+        raise AssertionError("the offload manager must replace the expert forward")
+
+
+def _int4_backbone(layers, seed):
+    from drama_b200 import synthetic
+
+    backbone = nn.Module()
+    backbone.layers = nn.ModuleList(
+        Int4Layer(Int4Store(synthetic.int4_bank(EXPERTS, HIDDEN, INTER, seed + i, asymmetric=False,
+                                                scale_dtype=torch.float16), HIDDEN, INTER))
+        for i in range(layers))
+    return backbone
+
+
+@pytest.mark.parametrize("config", [
+    {"max_staged_experts": 8, "max_pair_rows": 64},
+    {"max_staged_experts": 4, "max_pair_rows": 8},
+])
+def test_reference_manager_with_quantized_b200_backend(cuda_device, config):
+    """QuantizedB200Backend(0) under the reference's manager against the same
+    manager running the reference's QuantizedExpertBackend(0)
+    (``quantized_kernels.py:217-248``, default tiles) and against the oracle."""
+    off = _reference()
+    import numpy as np
+
+    from drama_low_vram.quantized_kernels import QuantizedExpertBackend
+    from oracle import restate as R
+
+    from drama_b200 import QuantizedB200Backend
+
+    theirs_backend = QuantizedExpertBackend(0)
+    theirs_backend.tuned_tiles = False
+    ours, theirs = _int4_backbone(2, seed=90), _int4_backbone(2, seed=90)
+    mine = off.install_expert_offload(ours, backend=QuantizedB200Backend(0), **config)
+    ref = off.install_expert_offload(theirs, backend=theirs_backend, **config)
+    calls = _calls(cuda_device)
+    got, want = _run(ours, calls), _run(theirs, calls)
+    for (layer, (x, ids, w)), a, b in zip(calls, got, want):
+        label = f"int4 {config} layer {layer} tokens {x.shape[0]}"
+        assert a.dtype == x.dtype and a.shape == x.shape
+        assert_parity(np_f32(a), np_f32(b), label=label + " vs QuantizedExpertBackend")
+        store = ours.layers[layer]._drama_quant_store
+        bank = {n: getattr(store, n).float().numpy() if n.endswith("scale_inv") else getattr(store, n).numpy()
+                for n in ("w13_weight", "w13_scale_inv", "w2_weight", "w2_scale_inv")}
+        bank.update(w13_qzeros=None, w2_qzeros=None)
+        expected = R.int4_forward(np_f32(x), ids.cpu().numpy(), np_f32(w), bank)
+        assert_parity(np_f32(a), np.asarray(expected, dtype=np.float32), label=label + " vs oracle")
+    assert mine.stats.forward_calls == len(calls)
     mine.close()
     ref.close()
 
