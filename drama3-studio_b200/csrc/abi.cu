@@ -81,15 +81,16 @@ namespace {
 
 int validate_decode_common(const void* x, int x_dtype, int64_t tokens, int top_k, const void* ids,
                            int ids_dtype, const void* weights, int weights_dtype, const void* out,
-                           const float* pair_out, int hidden, int intermediate, int slots) {
+                           const float* pair_out, int hidden, int intermediate, int slots,
+                           int64_t max_pairs = kMaxDecodePairs, const char* path = "decode") {
     if (!x || !ids || !weights) return fail("x, ids and weights are required");
     if (!out && !pair_out) return fail("either out or pair_out is required");
     if (!float_dtype(x_dtype)) return fail("x must be float32, float16 or bfloat16");
     if (!float_dtype(weights_dtype)) return fail("routing weights must be floating point");
     if (!index_dtype(ids_dtype)) return fail("expert IDs must be int32 or int64");
     if (tokens < 0 || top_k < 1) return fail("tokens must be >= 0 and top_k >= 1");
-    if (tokens * top_k > kMaxDecodePairs)
-        return fail("decode supports at most %d (token, slot) pairs; got %lld", kMaxDecodePairs,
+    if (tokens * top_k > max_pairs)
+        return fail("%s supports at most %lld (token, slot) pairs; got %lld", path, static_cast<long long>(max_pairs),
                     static_cast<long long>(tokens * top_k));
     if (hidden < 128 || hidden % 128 || intermediate < 128 || intermediate % 128)
         return fail("hidden and intermediate must be positive multiples of 128");
@@ -105,11 +106,12 @@ int validate_decode_common(const void* x, int x_dtype, int64_t tokens, int top_k
 // workspace or with the library's static scratch).
 int prepare_fp8_decode(const DramaB200Fp8Bank* bank, const void* x, int x_dtype, int64_t tokens, int top_k,
                        const void* ids, int ids_dtype, const void* weights, int weights_dtype, void* out,
-                       float* pair_out, DecodeArgs* out_args) {
+                       float* pair_out, DecodeArgs* out_args, int64_t max_pairs = kMaxDecodePairs,
+                       const char* path = "decode") {
     if (!bank) return fail("bank is required");
     const DramaB200Fp8Bank& b = *bank;
     if (validate_decode_common(x, x_dtype, tokens, top_k, ids, ids_dtype, weights, weights_dtype, out, pair_out,
-                               b.hidden, b.intermediate, b.slots))
+                               b.hidden, b.intermediate, b.slots, max_pairs, path))
         return -1;
     if (!b.w13 || !b.w13_scale || !b.w2 || !b.w2_scale) return fail("FP8 bank pointers are required");
     if (!aligned16(b.w13) || !aligned16(b.w2) || b.w13_row_stride % 16 || b.w2_row_stride % 16 ||
@@ -263,6 +265,45 @@ int drama_b200_fp8_w8a8_decode(const DramaB200Fp8Bank* bank, const void* x, int6
         err = cudaMemcpyAsync(x_scale_out, ws.xs, static_cast<size_t>(tokens) * (a.hidden / 128) * 4,
                               cudaMemcpyDeviceToDevice, s);
     if (err != cudaSuccess) return fail("W8A8 decode launch failed: %s", cudaGetErrorString(err));
+    return 0;
+}
+
+int drama_b200_fp8_w8a8_prefill_supported(int hidden, int intermediate, int experts) {
+    return fp8_prefill_tc_supported(hidden, intermediate, experts) ? 1 : 0;
+}
+
+size_t drama_b200_fp8_w8a8_prefill_workspace_bytes(int64_t tokens, int top_k, int hidden, int intermediate,
+                                                   int experts) {
+    return fp8_prefill_tc_workspace_layout(tokens, top_k, hidden, intermediate, experts, nullptr, nullptr) + 1024;
+}
+
+int drama_b200_fp8_w8a8_prefill(const DramaB200Fp8Bank* bank, const void* x, int64_t tokens, int top_k,
+                                const void* ids, int ids_dtype, const void* weights, int weights_dtype, void* out,
+                                float* pair_out, void* workspace, size_t workspace_bytes, void* stream) {
+    DecodeArgs a{};
+    if (prepare_fp8_decode(bank, x, DRAMA_B200_BF16, tokens, top_k, ids, ids_dtype, weights, weights_dtype, out,
+                           pair_out, &a, kMaxPrefillPairs, "the W8A8 prefill"))
+        return -1;
+    if (!fp8_prefill_tc_supported(a.hidden, a.intermediate, a.slots))
+        return fail("the tcgen05 prefill needs hidden a multiple of 256, hidden and intermediate <= 2048, "
+                    "intermediate a multiple of 128 and at most 512 experts");
+    if (tokens == 0) return 0;
+    // the buffers start on 1024-byte boundaries: up to 1023 bytes of the workspace lead in
+    const size_t need = fp8_prefill_tc_workspace_layout(tokens, top_k, a.hidden, a.intermediate, a.slots, nullptr,
+                                                        nullptr) + 1024;
+    if (!workspace || workspace_bytes < need)
+        return fail("W8A8 prefill workspace too small: need %zu bytes, got %zu", need, workspace_bytes);
+    if (reinterpret_cast<uintptr_t>(workspace) & 255u) return fail("workspace must be 256-byte aligned");
+    char* base = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(workspace) + 1023) & ~uintptr_t(1023));
+    if (pair_out && !aligned16(pair_out)) return fail("pair_out must be 16-byte aligned");
+    if (!aligned16(x)) return fail("hidden rows must start on 16-byte boundaries");
+    int sms = 0;
+    if (sm_count_current(&sms)) return -1;
+    Fp8PrefillWorkspace ws;
+    fp8_prefill_tc_workspace_layout(tokens, top_k, a.hidden, a.intermediate, a.slots, base, &ws);
+    const cudaError_t err = fp8_prefill_tc_launch(a.fp8, x, tokens, top_k, ids, ids_dtype, weights, weights_dtype,
+                                                  out, pair_out, ws, sms, static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return fail("W8A8 prefill launch failed: %s", cudaGetErrorString(err));
     return 0;
 }
 

@@ -712,9 +712,7 @@ DlPlan dl_plan(int H, int I, int E, int k, int clusters) {
     return p;
 }
 
-using TensorMapEncode = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                     const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                     CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+}  // namespace
 
 TensorMapEncode tensor_map_encoder() {
     static TensorMapEncode fn = nullptr;
@@ -729,8 +727,6 @@ TensorMapEncode tensor_map_encoder() {
     }
     return fn;
 }
-
-}  // namespace
 
 int decode_layer_clusters() {
     static int cached[64] = {};

@@ -1,0 +1,646 @@
+// K2 prefill on tcgen05: the FP8 W8A8 expert contract as two grouped GEMMs on
+// the 5th-generation tensor cores, accumulators in tensor memory.
+//
+// Contract: the reference's production GPU backend for many rows
+// (TritonExpertBackend.forward_pairs, src/drama_low_vram/offload.py:289-341:
+// 1x128 activation quantisation, the grouped FP8 GEMM with 128x128 weight
+// block scales, SiLU * up requantised 1x128, the down GEMM times the route
+// weight in fp32), with the arithmetic of fp8_decode.py:114-147 and its CPU
+// statement native/src/runtime.cpp:162-237:
+//   x row -> 1x128 blocks: scale = max(amax, 1e-10) * (1/448), q = e4m3(x / scale)
+//   gu[n] = sum over K blocks b of dot_b(W13[n], q) * (xs_b * S13[n/128][b])
+//   gate, up = bf16(gu); h = (gate / (1 + exp(-gate))) * up  (fp32), requantised 1x128
+//   down[n] = sum over I blocks of dot_b(W2[n], hq) * (hs_b * S2[n/128][b])
+//   pair_out = down * route weight (fp32); out[t] = bf16(slot-ordered sum)
+// dot_b (128 E4M3 products) runs as four K = 32 tcgen05 MMAs; the addition
+// order inside the tensor core is the hardware's.
+//
+// Launches, one stream, each after the previous by programmatic dependent
+// launch: permute (pairs bucketed by expert, stable; router.cu) -> quantise
+// the sorted pair rows -> gate/up GEMM -> down GEMM -> slot combine.
+//
+// GEMM CTA (one per SM, persistent, tiles taken with a static stride):
+//   tile = (expert, 128 sorted pair rows, 256 output columns); the gate/up
+//          tile's columns are 128 gate rows and the matching 128 up rows of
+//          W13, the down tile's are 256 rows of W2;
+//   warp 0 loads each K block of 128 bytes (A 128 rows, B 256 rows) with
+//          SWIZZLE_128B tensor-map copies (no multicast) into a 4-stage ring,
+//          and stages the tile's activation and weight scales into shared
+//          memory with cp.async;
+//   warp 1 owns 512 TMEM columns (two fp32 accumulators of 256 columns) and
+//          issues, per K block, four MMAs into one of them;
+//   warps 2-9 load that accumulator (warp w reads lanes 32 (w % 4) ..: the
+//          tile row is the TMEM lane), release it, and promote it into
+//          register accumulators with the two block scales; after the last
+//          K block they run the tile's epilogue.
+// Every wait is bounded: on a timeout the CTA sets status[1], stops issuing,
+// waits (bounded) for its copies and MMAs in flight and frees its TMEM.
+#include <utility>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "tma.cuh"
+#include "umma.cuh"
+
+namespace drama {
+namespace {
+
+constexpr int kTcThreads = 320;
+constexpr int kTcStages = 4;
+constexpr int kTcM = 128;                     // sorted pair rows per tile
+constexpr int kTcN = 256;                     // output columns per tile
+constexpr uint32_t kTcA = kTcM * 128;         // A bytes per stage
+constexpr uint32_t kTcB = kTcN * 128;         // B bytes per stage
+constexpr uint32_t kTcStage = kTcA + kTcB;
+constexpr int kTcMaxKb = 16;                  // K blocks of 128 (H, I <= 2048)
+constexpr int kTcMaxExperts = 512;
+constexpr uint32_t kTmemCols = 512;
+constexpr int kTcEpiThreads = 256;
+
+// Shared memory (offsets from the 1024-aligned base).
+constexpr uint32_t kOffStages = 0;
+constexpr uint32_t kScaleSlot = (kTcMaxKb * kTcM + 2 * kTcMaxKb) * 4;      // activation [kb][row] + 2 weight rows
+constexpr uint32_t kOffScales = kOffStages + kTcStages * kTcStage;
+constexpr uint32_t kOffAmax = kOffScales + 2 * kScaleSlot;                 // [2 tiles][2 halves][128]
+constexpr uint32_t kOffTiles = kOffAmax + 2 * 2 * kTcM * 4;                // first M tile of each expert [E + 1]
+constexpr uint32_t kOffRows = kOffTiles + (kTcMaxExperts + 1) * 4;         // first sorted row of each expert [E + 1]
+constexpr uint32_t kOffBars = (kOffRows + (kTcMaxExperts + 1) * 4 + 15) & ~15u;
+constexpr int kBarFull = 0, kBarEmpty = kTcStages, kBarTFull = 2 * kTcStages, kBarTEmpty = kBarTFull + 2,
+              kBarSFull = kBarTEmpty + 2, kBarSEmpty = kBarSFull + 2, kBarAmax = kBarSEmpty + 2,
+              kBarDone = kBarAmax + 2, kBarCount = kBarDone + 1;
+constexpr uint32_t kOffMisc = kOffBars + kBarCount * 8;                    // TMEM base, abort flag
+constexpr uint32_t kTcSmem = kOffMisc + 16 + 1024;                         // + alignment slack
+
+struct TcGemmArgs {
+    CUtensorMap a_map;          // [rows][K] E4M3 sorted pair rows (x or h)
+    CUtensorMap b_map;          // [slots][N rows][K] E4M3 (W13 or W2)
+    const float* a_scale;       // [rows][K/128]
+    const float* b_scale;       // [slots][N/128][K/128] (bank strides below)
+    int64_t b_scale_slot_stride, b_scale_row_stride;
+    const int64_t* offsets;     // [E + 1] first sorted row of each expert
+    const int64_t* order;       // [P] sorted row -> pair
+    int E, K, I, H;
+    uint8_t* hq;                // gate/up: [rows][I] E4M3
+    float* hs;                  // gate/up: [rows][I/128]
+    const void* weights;        // down: route weights [P]
+    int weights_dtype;
+    float* pair_out;            // down: [P][H]
+    int32_t* status;
+};
+
+struct TcTile {
+    int e, n0, rows;
+    int64_t row0;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// Tile t of this GEMM: experts' M tiles in expert order, `nt` column tiles
+// of `width` output columns each.
+__device__ __forceinline__ TcTile tc_tile(int t, int nt, int width, int E, const int* s_tiles, const int* s_rows) {
+    const int m = t / nt;
+    int lo = 0, hi = E;  // largest e with s_tiles[e] <= m (experts without rows have equal entries)
+    while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (s_tiles[mid] <= m) lo = mid;
+        else hi = mid;
+    }
+    TcTile x;
+    x.e = lo;
+    const int local = m - s_tiles[lo];
+    x.row0 = s_rows[lo] + static_cast<int64_t>(local) * kTcM;
+    const int end = s_rows[lo + 1];
+    x.rows = static_cast<int>(end - x.row0 < kTcM ? end - x.row0 : kTcM);
+    x.n0 = (t - m * nt) * width;
+    return x;
+}
+
+// A wait whose outcome is the same in every lane of the warp (the callers
+// then take warp-collective steps: MMA issue, TMEM loads, syncs).
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, int32_t* flag) {
+    return __all_sync(0xffffffffu, mbar_wait(bar, parity, flag));
+}
+__device__ __forceinline__ bool warp_aborted(volatile uint32_t* misc) { return __any_sync(0xffffffffu, misc[1] != 0); }
+
+__device__ __forceinline__ uint32_t e4m3x2(float lo, float hi) {
+    uint16_t r;
+    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+
+__device__ __forceinline__ uint64_t splat_f32x2(float s) { return pack_f32x2(s, s); }
+
+// acc[j/2] += (cols j, j+1 of r) * s for 16 columns.
+__device__ __forceinline__ void promote16(uint64_t* acc, const uint32_t (&r)[16], uint64_t s) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+        acc[j] = fma_f32x2(pack_f32x2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1])), s, acc[j]);
+}
+
+template <int MODE>  // 0: gate/up + SwiGLU + requantise; 1: down * route weight
+__global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_constant__ TcGemmArgs a) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    // 1024-byte alignment of the shared-window address (the swizzle atom)
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    const uint32_t sbase = smem_u32(smem);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBars);
+    auto bar = [&](int i) { return sbase + kOffBars + 8u * i; };
+    volatile uint32_t* misc = reinterpret_cast<volatile uint32_t*>(smem + kOffMisc);  // [0] TMEM base [1] abort
+    int* s_tiles = reinterpret_cast<int*>(smem + kOffTiles);
+    int* s_rows = reinterpret_cast<int*>(smem + kOffRows);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    int32_t* timeout_flag = a.status ? a.status + 1 : nullptr;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kTcStages; ++s) {
+            mbar_init(bar(kBarFull + s), 1);
+            mbar_init(bar(kBarEmpty + s), 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(bar(kBarTFull + b), 1);
+            mbar_init(bar(kBarTEmpty + b), kTcEpiThreads / 32);
+            mbar_init(bar(kBarSFull + b), 32);
+            mbar_init(bar(kBarSEmpty + b), kTcEpiThreads / 32);
+            mbar_init(bar(kBarAmax + b), kTcEpiThreads / 32);
+        }
+        mbar_init(bar(kBarDone), 1);
+        misc[1] = 0;
+        fence_mbar_init();
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&a.a_map)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&a.b_map)) : "memory");
+    }
+    if (warp == 1) {
+        cute::TMEM::Allocator1Sm alloc;
+        alloc.allocate(kTmemCols, const_cast<uint32_t*>(misc));
+        alloc.release_allocation_lock();
+        tcgen05_before_sync();
+    }
+    __syncthreads();
+    tcgen05_after_sync();
+    const uint32_t tmem = misc[0];
+
+    // The sorted rows and expert offsets come from the earlier launches.
+    grid_dependency_wait();
+    grid_launch_dependents();
+    const int E = a.E;
+    if (warp == 0) {
+        // M tiles per expert, exclusive scan over experts in chunks of 32
+        int carry = 0;
+        for (int base = 0; base <= E; base += 32) {
+            const int e = base + lane;
+            int64_t r0 = 0, r1 = 0;
+            if (e <= E) r0 = a.offsets[e];
+            if (e < E) r1 = a.offsets[e + 1];
+            const int mt = e < E ? static_cast<int>((r1 - r0 + kTcM - 1) / kTcM) : 0;
+            int x = mt;
+#pragma unroll
+            for (int off = 1; off < 32; off <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, x, off);
+                if (lane >= off) x += y;
+            }
+            if (e <= E) {
+                s_tiles[e] = carry + x - mt;
+                s_rows[e] = static_cast<int>(r0);
+            }
+            carry += __shfl_sync(0xffffffffu, x, 31);
+        }
+    }
+    __syncthreads();
+    // gate/up tiles: 128 h columns (128 gate + 128 up rows of W13); down: 256 hidden columns
+    const int width = MODE == 0 ? 128 : kTcN;
+    const int nt = MODE == 0 ? a.I / 128 : a.H / kTcN;
+    const int tiles = s_tiles[E] * nt;
+    const int KB = a.K / 128;
+
+    if (warp == 0) {
+        // ---------------- producer: TMA ring and tile scales ----------------
+        const uint64_t pol_a = policy_evict_last();
+        const uint64_t pol_b = policy_evict_first();
+        uint32_t c = 0;  // K blocks issued
+        int it = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++it) {
+            const TcTile x = tc_tile(t, nt, width, E, s_tiles, s_rows);
+            const int slot = it & 1;
+            if (!warp_wait(bar(kBarSEmpty + slot), ((it >> 1) & 1) ^ 1, timeout_flag)) {
+                ok = false;
+                break;
+            }
+            // activation scales [kb][row] and the tile's two weight scale rows
+            const uint32_t sc_addr = sbase + kOffScales + slot * kScaleSlot;
+            for (int i = lane; i < kTcM * KB; i += 32) {
+                const int r = i / KB, kb = i - r * KB;
+                cp4(sc_addr + 4u * (kb * kTcM + r), a.a_scale + (x.row0 + r) * KB + kb);
+            }
+            const float* bs = a.b_scale + x.e * a.b_scale_slot_stride;
+            const int nb0 = x.n0 / 128;
+            const int nb1 = MODE == 0 ? (a.I + x.n0) / 128 : x.n0 / 128 + 1;
+            for (int i = lane; i < 2 * KB; i += 32) {
+                const int which = i / KB, kb = i - which * KB;
+                cp4(sc_addr + 4u * (kTcMaxKb * kTcM + which * kTcMaxKb + kb),
+                    bs + (which ? nb1 : nb0) * a.b_scale_row_stride + kb);
+            }
+            cp_async_arrive_noinc(bar(kBarSFull + slot));
+            for (int kb = 0; kb < KB; ++kb, ++c) {
+                const int s = c % kTcStages;
+                if (!warp_wait(bar(kBarEmpty + s), ((c / kTcStages) & 1) ^ 1, timeout_flag) || warp_aborted(misc)) {
+                    ok = false;
+                    break;
+                }
+                if (lane == 0) {
+                    const uint32_t st = sbase + kOffStages + s * kTcStage;
+                    mbar_arrive_expect_tx(bar(kBarFull + s), kTcStage);
+                    tma_load_2d(st, &a.a_map, kb * 128, static_cast<int>(x.row0), bar(kBarFull + s), pol_a);
+                    if (MODE == 0) {
+                        tma_load_3d(st + kTcA, &a.b_map, kb * 128, x.n0, x.e, bar(kBarFull + s), pol_b);
+                        tma_load_3d(st + kTcA + kTcB / 2, &a.b_map, kb * 128, a.I + x.n0, x.e, bar(kBarFull + s),
+                                    pol_b);
+                    } else {
+                        tma_load_3d(st + kTcA, &a.b_map, kb * 128, x.n0, x.e, bar(kBarFull + s), pol_b);
+                    }
+                }
+                __syncwarp();
+            }
+        }
+        if (!ok) misc[1] = 1;
+        asm volatile("cp.async.wait_all;" ::: "memory");
+        // The last loads of each stage have landed before the CTA exits (the
+        // MMA warp waits for every load unless it stopped early).
+        for (uint32_t k = c > kTcStages ? c - kTcStages : 0; k < c; ++k)
+            mbar_wait(bar(kBarFull + k % kTcStages), (k / kTcStages) & 1, timeout_flag);
+    } else if (warp == 1) {
+        // ---------------- MMA issue ----------------
+        const uint64_t idesc = umma_idesc_e4m3_f32<kTcN>();
+        uint32_t c = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+            for (int kb = 0; kb < KB; ++kb, ++c) {
+                const int s = c % kTcStages, buf = c & 1;
+                if (warp_aborted(misc) || !warp_wait(bar(kBarFull + s), (c / kTcStages) & 1, timeout_flag) ||
+                    !warp_wait(bar(kBarTEmpty + buf), ((c >> 1) & 1) ^ 1, timeout_flag)) {
+                    ok = false;
+                    break;
+                }
+                tcgen05_after_sync();
+                const uint32_t st = sbase + kOffStages + s * kTcStage;
+                const uint64_t da = umma_desc_k_sw128(st), db = umma_desc_k_sw128(st + kTcA);
+                const uint32_t d = tmem + buf * kTcN;
+#pragma unroll
+                for (int k = 0; k < 4; ++k) umma_e4m3(d, da + 2 * k, db + 2 * k, idesc, k > 0);
+                umma_commit(&bars[kBarEmpty + s]);
+                umma_commit(&bars[kBarTFull + buf]);
+                __syncwarp();
+            }
+        }
+        if (!ok) misc[1] = 1;
+        // every MMA issued has completed before TMEM is released
+        umma_commit(&bars[kBarDone]);
+        __syncwarp();
+        mbar_wait(bar(kBarDone), 0, timeout_flag);
+    } else {
+        // ---------------- epilogue warps ----------------
+        const int q = warp & 3, g = (warp - 2) >> 2, r = q * 32 + lane;
+        const uint32_t lane_addr = tmem + (static_cast<uint32_t>(q * 32) << 16);
+        float* amax = reinterpret_cast<float*>(smem + kOffAmax);
+        uint32_t c = 0;
+        int it = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++it) {
+            const TcTile x = tc_tile(t, nt, width, E, s_tiles, s_rows);
+            const int slot = it & 1;
+            if (warp_aborted(misc) || !warp_wait(bar(kBarSFull + slot), (it >> 1) & 1, timeout_flag)) {
+                ok = false;
+                break;
+            }
+            const float* sc = reinterpret_cast<const float*>(smem + kOffScales + slot * kScaleSlot);
+            int64_t pair = 0;
+            float route_w = 0.0f;
+            if (MODE == 1 && r < x.rows) {
+                pair = a.order[x.row0 + r];
+                route_w = load_any(a.weights, a.weights_dtype, pair);
+            }
+            uint64_t acc[64];
+#pragma unroll
+            for (int j = 0; j < 64; ++j) acc[j] = 0ull;
+            for (int kb = 0; kb < KB; ++kb, ++c) {
+                const int buf = c & 1;
+                if (!warp_wait(bar(kBarTFull + buf), (c >> 1) & 1, timeout_flag)) {
+                    ok = false;
+                    break;
+                }
+                tcgen05_after_sync();
+                const float sa = sc[kb * kTcM + r];
+                const float* sw = sc + kTcMaxKb * kTcM;
+                // MODE 0: columns [64g, 64g + 64) of the gate half and of the up half;
+                // MODE 1: columns [128g, 128g + 128), one weight block.
+                const uint64_t s0 = splat_f32x2(__fmul_rn(sa, MODE == 0 ? sw[kb] : sw[g * kTcMaxKb + kb]));
+                const uint64_t s1 = MODE == 0 ? splat_f32x2(__fmul_rn(sa, sw[kTcMaxKb + kb])) : s0;
+                const uint32_t base = lane_addr + buf * kTcN;
+                const uint32_t c0 = MODE == 0 ? 64 * g : 128 * g;
+                const uint32_t c1 = MODE == 0 ? 128 + 64 * g : 128 * g + 64;
+                uint32_t ra[16], rb[16];
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const uint32_t col = (h == 0 ? c0 : c1);
+                    const uint64_t s = h == 0 ? s0 : s1;
+                    tmem_ld16(base + col, ra);
+                    tmem_ld16(base + col + 16, rb);
+                    tmem_wait2x16(ra, rb);
+                    promote16(acc + 32 * h, ra, s);
+                    promote16(acc + 32 * h + 8, rb, s);
+                    tmem_ld16(base + col + 32, ra);
+                    tmem_ld16(base + col + 48, rb);
+                    tmem_wait2x16(ra, rb);
+                    if (h == 1) {
+                        tcgen05_before_sync();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(bar(kBarTEmpty + buf));
+                    }
+                    promote16(acc + 32 * h + 16, ra, s);
+                    promote16(acc + 32 * h + 24, rb, s);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(kBarSEmpty + slot));
+            if (!ok) break;
+            if (MODE == 0) {
+                // acc[0..31]: gate columns 64g.., acc[32..63]: the matching up columns
+                float hv[64];
+                float m = 0.0f;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    float g0, g1, u0, u1;
+                    unpack_f32x2(acc[j], g0, g1);
+                    unpack_f32x2(acc[32 + j], u0, u1);
+                    const float gb0 = __bfloat162float(__float2bfloat16_rn(g0));
+                    const float gb1 = __bfloat162float(__float2bfloat16_rn(g1));
+                    const float ub0 = __bfloat162float(__float2bfloat16_rn(u0));
+                    const float ub1 = __bfloat162float(__float2bfloat16_rn(u1));
+                    hv[2 * j] = __fmul_rn(__fdiv_rn(gb0, __fadd_rn(1.0f, expf(-gb0))), ub0);
+                    hv[2 * j + 1] = __fmul_rn(__fdiv_rn(gb1, __fadd_rn(1.0f, expf(-gb1))), ub1);
+                    m = fmaxf(m, fmaxf(fabsf(hv[2 * j]), fabsf(hv[2 * j + 1])));
+                }
+                // the row's other 64 h columns are in the other half's thread
+                float* am = amax + (slot * 2) * kTcM;
+                am[g * kTcM + r] = m;
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar(kBarAmax + slot));
+                if (!warp_wait(bar(kBarAmax + slot), (it >> 1) & 1, timeout_flag)) {
+                    ok = false;
+                    break;
+                }
+                const float row_max = fmaxf(fmaxf(am[r], am[kTcM + r]), 1e-10f);
+                const float scale = __fmul_rn(row_max, 1.0f / 448.0f);
+                if (r < x.rows) {
+                    const int64_t row = x.row0 + r;
+                    uint4* dst = reinterpret_cast<uint4*>(a.hq + row * a.I + x.n0 + 64 * g);
+#pragma unroll
+                    for (int v = 0; v < 4; ++v) {
+                        uint32_t w[4];
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            const int j = 16 * v + 4 * u;
+                            w[u] = e4m3x2(__fdiv_rn(hv[j], scale), __fdiv_rn(hv[j + 1], scale)) |
+                                   (e4m3x2(__fdiv_rn(hv[j + 2], scale), __fdiv_rn(hv[j + 3], scale)) << 16);
+                        }
+                        dst[v] = make_uint4(w[0], w[1], w[2], w[3]);
+                    }
+                    if (g == 0) a.hs[row * (a.I / 128) + x.n0 / 128] = scale;
+                }
+            } else if (r < x.rows) {
+                float4* dst = reinterpret_cast<float4*>(a.pair_out + pair * a.H + x.n0 + 128 * g);
+#pragma unroll
+                for (int v = 0; v < 32; ++v) {
+                    float f0, f1, f2, f3;
+                    unpack_f32x2(acc[2 * v], f0, f1);
+                    unpack_f32x2(acc[2 * v + 1], f2, f3);
+                    dst[v] = make_float4(__fmul_rn(f0, route_w), __fmul_rn(f1, route_w), __fmul_rn(f2, route_w),
+                                         __fmul_rn(f3, route_w));
+                }
+            }
+        }
+        if (!ok) misc[1] = 1;
+    }
+    tcgen05_before_sync();
+    __syncthreads();
+    if (warp == 1) {
+        tcgen05_after_sync();
+        cute::TMEM::Allocator1Sm().free(tmem, kTmemCols);
+    }
+}
+
+// One sorted pair row per CTA: the pair's token row quantised 1x128 into
+// sorted position r (half a warp per block, 8 values per lane).
+__global__ void __launch_bounds__(256) tc_quant_rows_kernel(const __nv_bfloat16* x, int H, const int64_t* order,
+                                                            const int64_t* offsets, int E, int top_k, uint8_t* xq,
+                                                            float* xs) {
+    grid_dependency_wait();
+    grid_launch_dependents();
+    const int64_t r = blockIdx.x;
+    if (r >= offsets[E]) return;
+    const int64_t token = order[r] / top_k;
+    const int hw = threadIdx.x >> 4, l = threadIdx.x & 15, nblk = H / 128;
+    for (int base = 0; base < nblk; base += 16) {
+        const int blk = base + hw;
+        const bool on = blk < nblk;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (on) v = __ldg(reinterpret_cast<const uint4*>(x + token * H + blk * 128 + l * 8));
+        float f[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) f[j] = bf16_at(v, j);
+        float m = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(f[j]));
+#pragma unroll
+        for (int off = 8; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+        const float scale = __fmul_rn(fmaxf(m, 1e-10f), 1.0f / 448.0f);
+        if (on) {
+            uint2 q;
+            q.x = e4m3x2(__fdiv_rn(f[0], scale), __fdiv_rn(f[1], scale)) |
+                  (e4m3x2(__fdiv_rn(f[2], scale), __fdiv_rn(f[3], scale)) << 16);
+            q.y = e4m3x2(__fdiv_rn(f[4], scale), __fdiv_rn(f[5], scale)) |
+                  (e4m3x2(__fdiv_rn(f[6], scale), __fdiv_rn(f[7], scale)) << 16);
+            *reinterpret_cast<uint2*>(xq + r * H + blk * 128 + l * 8) = q;
+            if (l == 0) xs[r * nblk + blk] = scale;
+        }
+    }
+}
+
+// out[t][c..c+3] = bf16(sum over slots, in slot order, of pair_out); a pair
+// whose expert id is out of range contributes zero and, when its row is
+// returned to the caller, has that row zeroed.
+__global__ void tc_combine_kernel(float* pair_out, const void* ids, int ids_dtype, int experts, int64_t tokens,
+                                  int top_k, int H, bool zero_dropped, __nv_bfloat16* out) {
+    grid_dependency_wait();
+    const int64_t n = tokens * (H / 4);
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t t = i / (H / 4);
+        const int c = static_cast<int>(i - t * (H / 4)) * 4;
+        float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        for (int s = 0; s < top_k; ++s) {
+            const int64_t p = t * top_k + s;
+            const int64_t id = load_index(ids, ids_dtype, p);
+            float4* row = reinterpret_cast<float4*>(pair_out + p * H + c);
+            if (id < 0 || id >= experts) {
+                if (zero_dropped) *row = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                continue;
+            }
+            const float4 v = *row;
+            acc[0] = __fadd_rn(acc[0], v.x);
+            acc[1] = __fadd_rn(acc[1], v.y);
+            acc[2] = __fadd_rn(acc[2], v.z);
+            acc[3] = __fadd_rn(acc[3], v.w);
+        }
+        if (out) {
+            const __nv_bfloat162 lo = __floats2bfloat162_rn(acc[0], acc[1]);
+            const __nv_bfloat162 hi = __floats2bfloat162_rn(acc[2], acc[3]);
+            uint2 o;
+            o.x = *reinterpret_cast<const uint32_t*>(&lo);
+            o.y = *reinterpret_cast<const uint32_t*>(&hi);
+            *reinterpret_cast<uint2*>(out + t * H + c) = o;
+        }
+    }
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl_smem(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                            Args&&... args) {
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+bool encode_2d(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint64_t row_stride,
+               uint32_t box_rows) {
+    const TensorMapEncode encode = tensor_map_encoder();
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {row_stride};
+    const cuuint32_t box[2] = {128, box_rows};
+    const cuuint32_t unit[2] = {1, 1};
+    return encode && encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, unit,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool encode_3d(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint64_t slots, uint64_t row_stride,
+               uint64_t slot_stride, uint32_t box_rows) {
+    const TensorMapEncode encode = tensor_map_encoder();
+    const cuuint64_t dims[3] = {cols, rows, slots};
+    const cuuint64_t strides[2] = {row_stride, slot_stride};
+    const cuuint32_t box[3] = {128, box_rows, 1};
+    const cuuint32_t unit[3] = {1, 1, 1};
+    return encode && encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, unit,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+bool fp8_prefill_tc_supported(int hidden, int intermediate, int experts) {
+    return tensor_map_encoder() != nullptr && hidden % kTcN == 0 && intermediate % 128 == 0 &&
+           hidden / 128 <= kTcMaxKb && intermediate / 128 <= kTcMaxKb && experts >= 1 &&
+           experts <= kTcMaxExperts;
+}
+
+size_t fp8_prefill_tc_workspace_layout(int64_t tokens, int top_k, int hidden, int intermediate, int experts,
+                                       char* base, Fp8PrefillWorkspace* ws) {
+    const int64_t P = tokens * top_k;
+    const int64_t rows = P + kTcM;  // tiles may read up to 127 rows past the last pair
+    size_t off = 0;
+    auto take = [&](size_t bytes) -> char* {
+        char* p = base ? base + off : nullptr;
+        off += (bytes + 1023) & ~static_cast<size_t>(1023);
+        return p;
+    };
+    Fp8PrefillWorkspace w{};
+    w.status = reinterpret_cast<int32_t*>(take(16));
+    w.order = reinterpret_cast<int64_t*>(take(P * 8));
+    w.counts = reinterpret_cast<int64_t*>(take(static_cast<size_t>(experts) * 8));
+    w.offsets = reinterpret_cast<int64_t*>(take(static_cast<size_t>(experts + 1) * 8));
+    w.xq = reinterpret_cast<uint8_t*>(take(rows * hidden));
+    w.xs = reinterpret_cast<float*>(take(rows * (hidden / 128) * 4));
+    w.hq = reinterpret_cast<uint8_t*>(take(rows * intermediate));
+    w.hs = reinterpret_cast<float*>(take(rows * (intermediate / 128) * 4));
+    w.pair_out = reinterpret_cast<float*>(take(P * hidden * 4));
+    if (ws) *ws = w;
+    return off;
+}
+
+cudaError_t fp8_prefill_tc_launch(const DramaB200Fp8Bank& bank, const void* x, int64_t tokens, int top_k,
+                                  const void* ids, int ids_dtype, const void* weights, int weights_dtype, void* out,
+                                  float* pair_out, const Fp8PrefillWorkspace& ws, int sm_count, cudaStream_t s) {
+    static bool configured = false;  // benign race: identical values
+    if (!configured) {
+        cudaError_t err = cudaFuncSetAttribute(tc_gemm_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               static_cast<int>(kTcSmem));
+        if (err == cudaSuccess)
+            err = cudaFuncSetAttribute(tc_gemm_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(kTcSmem));
+        if (err != cudaSuccess) return err;
+        configured = true;
+    }
+    const int H = bank.hidden, I = bank.intermediate, E = bank.slots;
+    const int64_t P = tokens * top_k;
+    const int64_t rows = P + kTcM;
+    float* pairs = pair_out ? pair_out : ws.pair_out;
+    cudaError_t err = cudaMemsetAsync(ws.status, 0, 16, s);
+    if (err != cudaSuccess) return err;
+    PermuteArgs pa{ids, ids_dtype, P, E, ws.order, ws.counts, ws.offsets, ws.status};
+    if ((err = permute_routes(pa, s)) != cudaSuccess) return err;
+    if ((err = launch_pdl_smem(tc_quant_rows_kernel, dim3(static_cast<unsigned>(P)), dim3(256), 0, s,
+                               static_cast<const __nv_bfloat16*>(x), H, static_cast<const int64_t*>(ws.order),
+                               static_cast<const int64_t*>(ws.offsets), E, top_k, ws.xq, ws.xs)) != cudaSuccess)
+        return err;
+    TcGemmArgs g{};
+    g.offsets = ws.offsets;
+    g.order = ws.order;
+    g.E = E;
+    g.I = I;
+    g.H = H;
+    g.hq = ws.hq;
+    g.hs = ws.hs;
+    g.weights = weights;
+    g.weights_dtype = weights_dtype;
+    g.pair_out = pairs;
+    g.status = ws.status;
+    // gate/up: A = sorted x rows [rows][H], B = W13 [slots][2I][H]
+    g.K = H;
+    g.a_scale = ws.xs;
+    g.b_scale = bank.w13_scale;
+    g.b_scale_slot_stride = bank.w13_scale_slot_stride;
+    g.b_scale_row_stride = bank.w13_scale_row_stride;
+    if (!encode_2d(&g.a_map, ws.xq, H, rows, H, kTcM) ||
+        !encode_3d(&g.b_map, bank.w13, H, 2 * static_cast<uint64_t>(I), E, bank.w13_row_stride,
+                   bank.w13_slot_stride, kTcM))
+        return cudaErrorInvalidValue;
+    if ((err = launch_pdl_smem(tc_gemm_kernel<0>, dim3(sm_count), dim3(kTcThreads), kTcSmem, s, g)) != cudaSuccess)
+        return err;
+    // down: A = sorted h rows [rows][I], B = W2 [slots][H][I]
+    g.K = I;
+    g.a_scale = ws.hs;
+    g.b_scale = bank.w2_scale;
+    g.b_scale_slot_stride = bank.w2_scale_slot_stride;
+    g.b_scale_row_stride = bank.w2_scale_row_stride;
+    if (!encode_2d(&g.a_map, ws.hq, I, rows, I, kTcM) ||
+        !encode_3d(&g.b_map, bank.w2, I, H, E, bank.w2_row_stride, bank.w2_slot_stride, kTcN))
+        return cudaErrorInvalidValue;
+    if ((err = launch_pdl_smem(tc_gemm_kernel<1>, dim3(sm_count), dim3(kTcThreads), kTcSmem, s, g)) != cudaSuccess)
+        return err;
+    const int64_t chunks = tokens * (H / 4);
+    const int blocks = static_cast<int>(chunks / 256 + 1 < sm_count * 8 ? chunks / 256 + 1 : sm_count * 8);
+    return launch_pdl_smem(tc_combine_kernel, dim3(blocks), dim3(256), 0, s, pairs, ids, ids_dtype, E, tokens, top_k,
+                           H, pair_out != nullptr, static_cast<__nv_bfloat16*>(out));
+}
+
+}  // namespace drama

@@ -62,6 +62,7 @@ constexpr int kDecodeMaxWarps = 16;      // upper bound on warps per CTA of the 
 constexpr int kDecodeCtasPerSm = 1;      // resident CTAs per SM
 constexpr int kGroupTokens = 8;          // tokens per expert group (one n8 MMA)
 constexpr int kMaxDecodePairs = 4096;
+constexpr int64_t kMaxPrefillPairs = int64_t(1) << 24;  // sorted-row coordinates stay in int32
 constexpr int kStageTokens = 8;          // token rows staged in shared memory by the up kernel
 constexpr int kStageGroups = 4;          // expert groups staged in shared memory by the down kernel
 constexpr int kMaxSlots = 1024;
@@ -269,6 +270,33 @@ struct Fp8W8a8Workspace {
 };
 size_t fp8_w8a8_workspace_layout(int64_t tokens, int top_k, int hidden, int intermediate, char* base,
                                  Fp8W8a8Workspace* ws);
+
+// The driver's cuTensorMapEncodeTiled (null when the driver lacks it).
+using TensorMapEncode = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                     const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                     CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+TensorMapEncode tensor_map_encoder();
+
+// The FP8 W8A8 contract for many rows on tcgen05 tensor cores
+// (fp8_prefill_tc.cu): permute, sorted-row quantisation, gate/up and down
+// grouped GEMMs, slot combine.
+struct Fp8PrefillWorkspace {
+    int32_t* status;    // [4]: [0] pairs with an out-of-range id, [1] a GEMM wait timed out
+    int64_t* order;     // [P] pairs sorted by expert
+    int64_t* counts;    // [E]
+    int64_t* offsets;   // [E + 1]
+    uint8_t* xq;        // [P + 128][H] E4M3 token rows in sorted order
+    float* xs;          // [P + 128][H/128]
+    uint8_t* hq;        // [P + 128][I] E4M3 SwiGLU rows in sorted order
+    float* hs;          // [P + 128][I/128]
+    float* pair_out;    // [P][H] weighted fp32 partials
+};
+bool fp8_prefill_tc_supported(int hidden, int intermediate, int experts);
+size_t fp8_prefill_tc_workspace_layout(int64_t tokens, int top_k, int hidden, int intermediate, int experts,
+                                       char* base, Fp8PrefillWorkspace* ws);
+cudaError_t fp8_prefill_tc_launch(const DramaB200Fp8Bank& bank, const void* x, int64_t tokens, int top_k,
+                                  const void* ids, int ids_dtype, const void* weights, int weights_dtype, void* out,
+                                  float* pair_out, const Fp8PrefillWorkspace& ws, int sm_count, cudaStream_t s);
 cudaError_t fp8_w8a8_launch(const DramaB200Fp8Bank& bank, const void* x, int64_t tokens, int top_k, const void* ids,
                             int ids_dtype, const void* weights, int weights_dtype, void* out, float* pair_out,
                             const Fp8W8a8Workspace& ws, cudaStream_t s);

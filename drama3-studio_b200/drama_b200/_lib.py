@@ -39,6 +39,9 @@ EXPORTS = (
     "drama_b200_int4_decode",
     "drama_b200_fp8_w8a8_workspace_bytes",
     "drama_b200_fp8_w8a8_decode",
+    "drama_b200_fp8_w8a8_prefill_supported",
+    "drama_b200_fp8_w8a8_prefill_workspace_bytes",
+    "drama_b200_fp8_w8a8_prefill",
     "drama_b200_w8a8_workspace_bytes",
     "drama_b200_w8a8_decode",
     "drama_b200_shared_expert_workspace_bytes",
@@ -161,6 +164,14 @@ class Library:
         dll.drama_b200_fp8_w8a8_decode.argtypes = [
             ctypes.POINTER(Fp8Bank), c_void_p, c_int64, c_int, c_void_p, c_int, c_void_p, c_int, c_void_p,
             c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]
+        dll.drama_b200_fp8_w8a8_prefill_supported.argtypes = [c_int, c_int, c_int]
+        dll.drama_b200_fp8_w8a8_prefill_supported.restype = c_int
+        dll.drama_b200_fp8_w8a8_prefill_workspace_bytes.argtypes = [c_int64, c_int, c_int, c_int, c_int]
+        dll.drama_b200_fp8_w8a8_prefill_workspace_bytes.restype = c_size_t
+        dll.drama_b200_fp8_w8a8_prefill.argtypes = [
+            ctypes.POINTER(Fp8Bank), c_void_p, c_int64, c_int, c_void_p, c_int, c_void_p, c_int, c_void_p,
+            c_void_p, c_void_p, c_size_t, c_void_p]
+        dll.drama_b200_fp8_w8a8_prefill.restype = c_int
         dll.drama_b200_w8a8_decode.argtypes = [ctypes.POINTER(W8a8Bank)] + decode_args
         dll.drama_b200_w8a8_decode.restype = c_int
         dll.drama_b200_w8a8_workspace_bytes.argtypes = [c_int64, c_int, c_int, c_int]

@@ -286,9 +286,31 @@ class Fp8W8a8B200Backend(_DecodeBackend):
     162-237``). This backend computes that contract on the same staged banks
     as ``B200ExpertBackend`` (whose arithmetic is the W16A16 dequant path of
     ``TorchExpertBackend``); rows must be bfloat16.
+
+    From ``prefill_min_pairs`` (token, slot) pairs on, a call runs as grouped
+    GEMMs on the tcgen05 tensor cores (``drama_b200_fp8_w8a8_prefill``); below
+    it, as per-pair tensor-core cells (``drama_b200_fp8_w8a8_decode``).
     """
 
     entry = "drama_b200_fp8_w8a8_decode"
+
+    def __init__(self, *, validate_ids: bool = True, prefill_min_pairs: int = 512) -> None:
+        super().__init__(validate_ids=validate_ids)
+        self.prefill_min_pairs = prefill_min_pairs
+
+    def _prefill(self, lib, bank, x, ids, weights, out, pair_out) -> bool:
+        tokens, top_k = ids.shape
+        if tokens * top_k < self.prefill_min_pairs or not lib.dll.drama_b200_fp8_w8a8_prefill_supported(
+                bank.hidden, bank.intermediate, bank.slots):
+            return False
+        nbytes = lib.dll.drama_b200_fp8_w8a8_prefill_workspace_bytes(tokens, top_k, bank.hidden, bank.intermediate,
+                                                                      bank.slots)
+        ws = _WORKSPACES.get(x.device, nbytes)
+        lib.check(lib.dll.drama_b200_fp8_w8a8_prefill(
+            ctypes.byref(bank), x.data_ptr(), tokens, top_k, ids.data_ptr(), _lib.DTYPE_CODES[ids.dtype],
+            weights.data_ptr(), _lib.DTYPE_CODES[weights.dtype], _lib.ptr(out), _lib.ptr(pair_out), ws.data_ptr(),
+            ws.numel(), _lib.stream_handle(x.device)))
+        return True
 
     def _bank(self, staged, hidden):
         return _fp8_bank(staged, hidden)
@@ -304,16 +326,21 @@ class Fp8W8a8B200Backend(_DecodeBackend):
         bank, keep = self._bank(staged, hidden)
         _check_common(x, ids, weights, bank.slots, hidden, self.validate_ids)
         tokens, top_k = ids.shape
-        if tokens * top_k > MAX_DECODE_PAIRS:
+        lib = _lib.library()
+        prefill = (x_fp8 is None and x_scale is None and tokens * top_k >= self.prefill_min_pairs
+                   and lib.dll.drama_b200_fp8_w8a8_prefill_supported(hidden, bank.intermediate, bank.slots))
+        if tokens * top_k > MAX_DECODE_PAIRS and not prefill:
             return self._chunked(x, ids, weights, staged, combine=combine)
         x, ids, weights = x.contiguous(), ids.contiguous(), weights.contiguous()
         if weights.dtype not in FLOAT_DTYPES:
             weights = weights.float()
-        lib = _lib.library()
         if combine:
             out, pair_out = torch.empty_like(x), None
         else:
             out, pair_out = None, torch.empty((tokens * top_k, hidden), device=x.device, dtype=torch.float32)
+        if prefill and self._prefill(lib, bank, x, ids, weights, out, pair_out):
+            del keep
+            return out if combine else pair_out
         nbytes = self._workspace_bytes(lib, tokens, top_k, hidden, bank.intermediate)
         ws = _WORKSPACES.get(x.device, nbytes)
         lib.check(lib.dll.drama_b200_fp8_w8a8_decode(

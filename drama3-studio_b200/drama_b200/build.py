@@ -29,6 +29,30 @@ NVCC_FLAGS = [
 ]
 
 
+def cutlass_include() -> Path:
+    """A CUTLASS / CuTe header tree with the sm100 UMMA headers.
+
+    DRAMA_B200_CUTLASS_INCLUDE, else the copy that ships inside an installed
+    package of this environment (flashinfer, tilelang). Only the headers are
+    used (the tcgen05 descriptor unions, MMA, TMEM-allocation and commit
+    wrappers); nothing is linked.
+    """
+    import importlib.util
+
+    candidates = []
+    if os.environ.get("DRAMA_B200_CUTLASS_INCLUDE"):
+        candidates.append(Path(os.environ["DRAMA_B200_CUTLASS_INCLUDE"]))
+    for package, sub in (("flashinfer", "data/cutlass/include"), ("tilelang", "3rdparty/cutlass/include")):
+        spec = importlib.util.find_spec(package)
+        if spec is not None and spec.submodule_search_locations:
+            candidates.append(Path(list(spec.submodule_search_locations)[0]) / sub)
+    for path in candidates:
+        if (path / "cute" / "arch" / "mma_sm100_umma.hpp").is_file():
+            return path
+    raise RuntimeError("no CUTLASS header tree with cute/arch/mma_sm100_umma.hpp found; "
+                       "set DRAMA_B200_CUTLASS_INCLUDE")
+
+
 def nvcc() -> str:
     found = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
     if not Path(found).exists():
@@ -60,6 +84,8 @@ def build(verbose: bool = False, force: bool = False, ptxas_info: bool = False) 
         objects.append(obj)
         if force or _stale(obj, [src, *headers, Path(__file__)]):
             cmd = [compiler, *ARCH, *NVCC_FLAGS, f"-I{INCLUDE}", f"-I{CSRC}", "-c", str(src), "-o", str(obj)]
+            if "umma.cuh" in src.read_text():
+                cmd[1:1] = [f"-I{cutlass_include()}"]
             if ptxas_info:
                 cmd[1:1] = ["-Xptxas", "-v"]
             jobs.append(cmd)

@@ -174,6 +174,29 @@ DRAMA_B200_API int drama_b200_fp8_w8a8_decode(const DramaB200Fp8Bank* bank, cons
                                               float* x_scale_out, void* workspace, size_t workspace_bytes,
                                               void* stream);
 
+/* ---------------------------------------------------------------------------
+ * The same FP8 W8A8 contract for many rows on tcgen05 tensor cores (the
+ * prefill regime of TritonExpertBackend.forward / forward_pairs,
+ * src/drama_low_vram/offload.py:279-341, whose grouped FP8 GEMM it replaces):
+ * pairs bucketed by expert, sorted rows quantised 1x128, gate/up and down
+ * grouped GEMMs with 128x128 weight block scales promoted per 128-wide K block,
+ * then the slot-ordered combine. Outputs as drama_b200_fp8_w8a8_decode
+ * (out and/or pair_out; a pair with an out-of-range id contributes zero and
+ * its pair_out row is zero). hidden a multiple of 256 and <= 2048,
+ * intermediate a multiple of 128 and <= 2048, at most 512 experts
+ * (drama_b200_fp8_w8a8_prefill_supported); at most 2^24 pairs; bf16 rows; workspace 256-byte
+ * aligned, drama_b200_fp8_w8a8_prefill_workspace_bytes bytes.
+ * ------------------------------------------------------------------------- */
+DRAMA_B200_API int drama_b200_fp8_w8a8_prefill_supported(int hidden, int intermediate, int experts);
+
+DRAMA_B200_API size_t drama_b200_fp8_w8a8_prefill_workspace_bytes(int64_t tokens, int top_k, int hidden,
+                                                                  int intermediate, int experts);
+
+DRAMA_B200_API int drama_b200_fp8_w8a8_prefill(const DramaB200Fp8Bank* bank, const void* x, int64_t tokens,
+                                               int top_k, const void* ids, int ids_dtype, const void* weights,
+                                               int weights_dtype, void* out, float* pair_out, void* workspace,
+                                               size_t workspace_bytes, void* stream);
+
 DRAMA_B200_API int drama_b200_int4_decode(const DramaB200Int4Bank* bank, const void* x,
                                           int x_dtype, int64_t tokens, int top_k,
                                           const void* ids, int ids_dtype, const void* weights,
