@@ -63,6 +63,8 @@ def parse_args():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--router", choices=("fused", "torch"), default="fused",
                    help="decode: router in the fused layer kernel, or torch's RMSNorm/linear in front (bit-exact ids)")
+    p.add_argument("--contract", choices=("w8a8", "w16a16"), default="w8a8",
+                   help="prefill: the production W8A8 contract on tcgen05 (default) or the W16A16 dequant contract")
     p.add_argument("--no-ep", action="store_true",
                    help="decode: skip the config-4 expert-parallel sub-record (\"ep\") of the headline line")
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
@@ -472,14 +474,50 @@ def run_ours(args) -> None:
         print(json.dumps(line))
 
 
+def fp8_gemm_peak(device) -> dict:
+    """Dense E4M3 tensor throughput measured here: cuBLASLt through
+    torch._scaled_mm, 8192^3, best of 10 (a burst, like MEASURED_PEAKS.json's
+    bf16 figure). Falls back to twice the measured bf16 burst (the B200's
+    FP8 : BF16 dense ratio) when the FP8 GEMM is unavailable."""
+    import torch
+
+    n = 8192
+    try:
+        a = torch.randn(n, n, device=device).to(torch.float8_e4m3fn)
+        b = torch.randn(n, n, device=device).to(torch.float8_e4m3fn).t()
+        one = torch.ones((), device=device)
+        for _ in range(3):
+            torch._scaled_mm(a, b, scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
+        best = float("inf")
+        for _ in range(10):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch._scaled_mm(a, b, scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
+            e1.record()
+            e1.synchronize()
+            best = min(best, e0.elapsed_time(e1))
+        del a, b
+        return {"tflops": 2.0 * n ** 3 / (best / 1000.0) / 1e12,
+                "source": "measured in this run: torch._scaled_mm E4M3 x E4M3 -> bf16, 8192^3, best of 10"}
+    except (RuntimeError, TypeError) as exc:
+        path = REPO / "MEASURED_PEAKS.json"
+        bf16 = json.loads(path.read_text())["bf16_tflops"] if path.is_file() else 1590.0
+        return {"tflops": 2.0 * bf16, "source": f"2 x MEASURED_PEAKS.json bf16_tflops ({exc.__class__.__name__})"}
+
+
 def run_prefill(args) -> None:
     """Config 3: one FP8 MoE layer over 4096 prefill tokens, Zipf(1.1) routes.
 
-    One step = ``fp8_prefill`` on the 4096 rows (permute, two grouped
-    tensor-core GEMMs, combine). ``value`` = tokens/s with inputs resident;
-    the roofline is the bf16 tensor pipe (the dequant path computes in bf16),
+    ``--contract w8a8`` (default): one step = ``drama_b200_fp8_w8a8_prefill``
+    (permute, sorted-row quantisation, gate/up and down grouped GEMMs on the
+    tcgen05 tensor cores, combine), the arithmetic of the reference's
+    production GPU backend; the roofline is the E4M3 tensor pipe.
+    ``--contract w16a16``: ``fp8_prefill`` (TorchExpertBackend's dequant
+    arithmetic on bf16 mma.sync tensor cores) against the bf16 peak.
     FLOPs = 2 * pairs * (2I * H + H * I) per step.
     """
+    import ctypes
+
     import torch
     import torch.distributed as dist
 
@@ -492,8 +530,8 @@ def run_prefill(args) -> None:
         from datetime import timedelta
 
         dist.init_process_group("nccl", device_id=device, timeout=timedelta(seconds=300))
-    from drama_b200 import synthetic
-    from drama_b200.backend import fp8_prefill
+    from drama_b200 import _lib, synthetic
+    from drama_b200.backend import _fp8_bank, fp8_prefill
 
     tokens = 4096
     bank = synthetic.fp8_bank(EXPERTS, HIDDEN, INTER, rank, device=device, chunk=EXPERTS)
@@ -508,8 +546,31 @@ def run_prefill(args) -> None:
     ids = ids.to(torch.int64).contiguous()
     w = w.to(torch.bfloat16).contiguous()
     x = synthetic.hidden_states(tokens, HIDDEN, 200 + rank, device=device)
+    out = torch.empty_like(x)
+    if args.contract == "w8a8":
+        lib = _lib.library()
+        desc, keep = _fp8_bank(Staged, HIDDEN)
+        nbytes = lib.dll.drama_b200_fp8_w8a8_prefill_workspace_bytes(tokens, TOP_K, HIDDEN, INTER, EXPERTS)
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=device)
+        stream = _lib.stream_handle(device)
+
+        def step():
+            lib.check(lib.dll.drama_b200_fp8_w8a8_prefill(
+                ctypes.byref(desc), x.data_ptr(), tokens, TOP_K, ids.data_ptr(), _lib.I64, w.data_ptr(), _lib.BF16,
+                out.data_ptr(), None, ws.data_ptr(), ws.numel(), stream))
+            return out
+
+        launches, kernel = 5, ("prefill step: permute + sorted-row quantisation + gate/up and down grouped GEMMs "
+                               "(tcgen05, TMEM accumulators) + combine")
+        dtype = "fp8-e4m3 weights and activations (1x128 / 128x128 block scales), fp32 accumulate"
+    else:
+        def step():
+            return fp8_prefill(x, ids, w, Staged, validate_ids=False)
+
+        launches, kernel = 4, "prefill step: permute + gate/up GEMM + down GEMM + combine (bf16 mma.sync)"
+        dtype = "fp8-e4m3 weights dequantised to bf16, bf16 activations, fp32 accumulate"
     for _ in range(max(3, args.warmup)):
-        fp8_prefill(x, ids, w, Staged, validate_ids=False)
+        step()
 
     def barrier():
         if world > 1:
@@ -523,7 +584,7 @@ def run_prefill(args) -> None:
     with ClockSampler(gpu_id) as clocks:
         e0.record()
         for _ in range(args.steps):
-            fp8_prefill(x, ids, w, Staged, validate_ids=False)
+            step()
         e1.record()
         e1.synchronize()
     barrier()
@@ -534,8 +595,8 @@ def run_prefill(args) -> None:
     f0.record()
     for _ in range(args.steps):
         x.copy_(host_x, non_blocking=True)
-        out = fp8_prefill(x, ids, w, Staged, validate_ids=False)
-        host_out.copy_(out, non_blocking=True)
+        result = step()
+        host_out.copy_(result, non_blocking=True)
     f1.record()
     f1.synchronize()
     e2e_ms = f0.elapsed_time(f1) / args.steps
@@ -545,40 +606,37 @@ def run_prefill(args) -> None:
         ms, e2e_ms = float(t[0]), float(t[1])
     pairs = tokens * TOP_K
     flops = 2.0 * pairs * (2 * INTER * HIDDEN + HIDDEN * INTER)
-    peak_path = REPO / "MEASURED_PEAKS.json"
-    peak = json.loads(peak_path.read_text())["bf16_tflops"] if peak_path.is_file() else 1590.0
+    if args.contract == "w8a8":
+        fp8 = fp8_gemm_peak(device)
+        peak, peak_source = fp8["tflops"], fp8["source"]
+    else:
+        peak_path = REPO / "MEASURED_PEAKS.json"
+        peak = json.loads(peak_path.read_text())["bf16_tflops"] if peak_path.is_file() else 1590.0
+        peak_source = "measured (MEASURED_PEAKS.json bf16_tflops, cuBLAS bf16 burst)"
     achieved = flops / (ms / 1000.0) / 1e12
     line = {
         "metric": "FP8 MoE-layer prefill tokens/s (config 3)", "value": tokens * world / (ms / 1000.0),
         "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": max(3, args.warmup),
         "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "fp8-e4m3 weights dequantised to bf16, bf16 activations, fp32 accumulate",
-        "data": "synthetic (seeded random-init weights, hidden rows, Zipf(1.1) routes)",
+        "dtype": dtype, "data": "synthetic (seeded random-init weights, hidden rows, Zipf(1.1) routes)",
         "config": {"workload": (f"config3: prefill {tokens} tokens through one FP8 MoE layer (hidden {HIDDEN}, "
                                 f"{EXPERTS} experts, top-{TOP_K}, intermediate {INTER}), Zipf(1.1) routing"),
-                   "tokens": tokens, "hidden": HIDDEN, "experts": EXPERTS, "top_k": TOP_K, "intermediate": INTER,
+                   "contract": args.contract, "tokens": tokens, "hidden": HIDDEN, "experts": EXPERTS,
+                   "top_k": TOP_K, "intermediate": INTER,
                    "parallelism": f"replicas{world}" if world > 1 else "single",
-                   "l2": "inputs larger than L2: 604 MB bank, 134 MB of per-pair down rows"},
-        "roofline": {"kernel": "prefill step: permute + gate/up GEMM + down GEMM + combine", "bound": "tensor",
-                     "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-                     "peak_source": "measured (MEASURED_PEAKS.json bf16_tflops, cuBLAS bf16 burst)",
-                     "traffic": None, "algorithmic_flops_per_launch": flops},
+                   "l2": "inputs larger than L2: 604 MB bank, 268 MB of fp32 per-pair down rows"},
+        "roofline": {"kernel": kernel, "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "peak_source": peak_source, "traffic": None,
+                     "algorithmic_flops_per_launch": flops},
         "e2e": {"value": tokens * world / (e2e_ms / 1000.0), "unit": "tokens/s",
                 "h2d_bytes_per_step": x.numel() * 2, "d2h_bytes_per_step": x.numel() * 2},
-        "gpu_launches": args.steps * 4,
+        "gpu_launches": args.steps * launches,
         "clocks": clocks.summary(),
     }
     if world > 1:
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(line))
-
-
-# ---------------------------------------------------------------------------
-# config 4: expert-parallel decode of 256 tokens, and the offload variant
-# ---------------------------------------------------------------------------
-EP_TOKENS = 256
-EP_CHUNK = 16          # experts generated per seed, so every G sees the same banks
 
 
 def _dist_setup():

@@ -216,6 +216,28 @@ int drama_b200_permute_routes(const void* ids, int ids_dtype, int64_t pairs, int
     return 0;
 }
 
+size_t drama_b200_permute_routes_wide_scratch_bytes(int64_t pairs, int experts) {
+    return pairs < 0 || experts < 1 ? 0 : permute_wide_scratch_bytes(pairs, experts);
+}
+
+int drama_b200_permute_routes_wide(const void* ids, int ids_dtype, int64_t pairs, int experts, int64_t* order,
+                                   int64_t* counts, int64_t* offsets, int64_t* position, void* scratch,
+                                   size_t scratch_bytes, int32_t* status, void* stream) {
+    if (!ids || !order || !counts || !offsets) return fail("ids, order, counts and offsets are required");
+    if (!index_dtype(ids_dtype)) return fail("ids must be int32 or int64");
+    if (pairs < 0 || pairs > (int64_t(1) << 24)) return fail("pairs must be in [0, 2^24]");
+    if (experts < 1 || experts > 1024) return fail("experts must be in [1, 1024]");
+    const size_t need = permute_wide_scratch_bytes(pairs, experts);
+    if (need && (!scratch || scratch_bytes < need))
+        return fail("permutation scratch too small: need %zu bytes, got %zu", need, scratch_bytes);
+    if (scratch && !aligned16(scratch)) return fail("scratch must be 16-byte aligned");
+    PermuteArgs a{ids, ids_dtype, pairs, experts, order, counts, offsets, status};
+    const cudaError_t err = permute_routes_wide(a, static_cast<int*>(scratch), position,
+                                                static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return fail("permute_routes_wide launch failed: %s", cudaGetErrorString(err));
+    return 0;
+}
+
 size_t drama_b200_decode_workspace_bytes(int64_t tokens, int top_k, int hidden, int intermediate) {
     int sms = 0;
     if (sm_count_current(&sms)) sms = 148;
@@ -284,6 +306,7 @@ int drama_b200_fp8_w8a8_prefill(const DramaB200Fp8Bank* bank, const void* x, int
     if (prepare_fp8_decode(bank, x, DRAMA_B200_BF16, tokens, top_k, ids, ids_dtype, weights, weights_dtype, out,
                            pair_out, &a, kMaxPrefillPairs, "the W8A8 prefill"))
         return -1;
+    if (top_k > 32) return fail("the W8A8 prefill takes top_k in [1, 32]");
     if (!fp8_prefill_tc_supported(a.hidden, a.intermediate, a.slots))
         return fail("the tcgen05 prefill needs hidden a multiple of 256, hidden and intermediate <= 2048, "
                     "intermediate a multiple of 128 and at most 512 experts");
@@ -295,7 +318,7 @@ int drama_b200_fp8_w8a8_prefill(const DramaB200Fp8Bank* bank, const void* x, int
         return fail("W8A8 prefill workspace too small: need %zu bytes, got %zu", need, workspace_bytes);
     if (reinterpret_cast<uintptr_t>(workspace) & 255u) return fail("workspace must be 256-byte aligned");
     char* base = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(workspace) + 1023) & ~uintptr_t(1023));
-    if (pair_out && !aligned16(pair_out)) return fail("pair_out must be 16-byte aligned");
+    if (pair_out && (reinterpret_cast<uintptr_t>(pair_out) & 31u)) return fail("pair_out must be 32-byte aligned");
     if (!aligned16(x)) return fail("hidden rows must start on 16-byte boundaries");
     int sms = 0;
     if (sm_count_current(&sms)) return -1;

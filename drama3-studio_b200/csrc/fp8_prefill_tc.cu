@@ -13,11 +13,15 @@
 //   down[n] = sum over I blocks of dot_b(W2[n], hq) * (hs_b * S2[n/128][b])
 //   pair_out = down * route weight (fp32); out[t] = bf16(slot-ordered sum)
 // dot_b (128 E4M3 products) runs as four K = 32 tcgen05 MMAs; the addition
-// order inside the tensor core is the hardware's.
+// order inside the tensor core is the hardware's. The gate/up epilogue takes
+// SiLU with the fast exponential and division intrinsics and requantises h
+// by multiplying with the IEEE reciprocal of its block scale (a few ulp from
+// the reference's fp32 division; the token rows use the exact division).
 //
 // Launches, one stream, each after the previous by programmatic dependent
-// launch: permute (pairs bucketed by expert, stable; router.cu) -> quantise
-// the sorted pair rows -> gate/up GEMM -> down GEMM -> slot combine.
+// launch: permute (pairs bucketed by expert, stable, over many CTAs;
+// router.cu) -> quantise each token row once into its pairs' sorted rows ->
+// gate/up GEMM -> down GEMM -> slot combine.
 //
 // GEMM CTA (one per SM, persistent, tiles taken with a static stride):
 //   tile = (expert, 128 sorted pair rows, 256 output columns); the gate/up
@@ -29,10 +33,11 @@
 //          memory with cp.async;
 //   warp 1 owns 512 TMEM columns (two fp32 accumulators of 256 columns) and
 //          issues, per K block, four MMAs into one of them;
-//   warps 2-9 load that accumulator (warp w reads lanes 32 (w % 4) ..: the
-//          tile row is the TMEM lane), release it, and promote it into
-//          register accumulators with the two block scales; after the last
-//          K block they run the tile's epilogue.
+//   warps 2-17 load that accumulator (warp w reads lanes 32 (w % 4) ..: the
+//          tile row is the TMEM lane; the four warps of a lane quarter split
+//          the columns), release it, and promote it into register
+//          accumulators with the two block scales; after the last K block
+//          they run the tile's epilogue (32-byte row stores).
 // Every wait is bounded: on a timeout the CTA sets status[1], stops issuing,
 // waits (bounded) for its copies and MMAs in flight and frees its TMEM.
 #include <utility>
@@ -45,7 +50,7 @@
 namespace drama {
 namespace {
 
-constexpr int kTcThreads = 320;
+constexpr int kTcThreads = 576;              // warp 0 TMA, warp 1 MMA, warps 2-17 accumulators
 constexpr int kTcStages = 4;
 constexpr int kTcM = 128;                     // sorted pair rows per tile
 constexpr int kTcN = 256;                     // output columns per tile
@@ -55,14 +60,15 @@ constexpr uint32_t kTcStage = kTcA + kTcB;
 constexpr int kTcMaxKb = 16;                  // K blocks of 128 (H, I <= 2048)
 constexpr int kTcMaxExperts = 512;
 constexpr uint32_t kTmemCols = 512;
-constexpr int kTcEpiThreads = 256;
+constexpr int kTcEpiThreads = 512;
+constexpr int kTcGroups = 4;                  // column groups of the accumulator warps
 
 // Shared memory (offsets from the 1024-aligned base).
 constexpr uint32_t kOffStages = 0;
 constexpr uint32_t kScaleSlot = (kTcMaxKb * kTcM + 2 * kTcMaxKb) * 4;      // activation [kb][row] + 2 weight rows
 constexpr uint32_t kOffScales = kOffStages + kTcStages * kTcStage;
-constexpr uint32_t kOffAmax = kOffScales + 2 * kScaleSlot;                 // [2 tiles][2 halves][128]
-constexpr uint32_t kOffTiles = kOffAmax + 2 * 2 * kTcM * 4;                // first M tile of each expert [E + 1]
+constexpr uint32_t kOffAmax = kOffScales + 2 * kScaleSlot;                 // [2 tiles][4 groups][128]
+constexpr uint32_t kOffTiles = kOffAmax + 2 * kTcGroups * kTcM * 4;        // first M tile of each expert [E + 1]
 constexpr uint32_t kOffRows = kOffTiles + (kTcMaxExperts + 1) * 4;         // first sorted row of each expert [E + 1]
 constexpr uint32_t kOffBars = (kOffRows + (kTcMaxExperts + 1) * 4 + 15) & ~15u;
 constexpr int kBarFull = 0, kBarEmpty = kTcStages, kBarTFull = 2 * kTcStages, kBarTEmpty = kBarTFull + 2,
@@ -137,6 +143,14 @@ __device__ __forceinline__ void promote16(uint64_t* acc, const uint32_t (&r)[16]
 #pragma unroll
     for (int j = 0; j < 8; ++j)
         acc[j] = fma_f32x2(pack_f32x2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1])), s, acc[j]);
+}
+
+// 32 bytes of one row (a whole L2 sector) from one thread; p 32-byte aligned.
+__device__ __forceinline__ void st_global_32b(void* p, uint32_t v0, uint32_t v1, uint32_t v2, uint32_t v3, uint32_t v4,
+                                              uint32_t v5, uint32_t v6, uint32_t v7) {
+    asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(v0), "r"(v1), "r"(v2), "r"(v3),
+                 "r"(v4), "r"(v5), "r"(v6), "r"(v7)
+                 : "memory");
 }
 
 template <int MODE>  // 0: gate/up + SwiGLU + requantise; 1: down * route weight
@@ -300,9 +314,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
         __syncwarp();
         mbar_wait(bar(kBarDone), 0, timeout_flag);
     } else {
-        // ---------------- epilogue warps ----------------
+        // ---------------- accumulator warps ----------------
+        // lane quarter q, column group g: MODE 0 gate columns [32g, 32g + 32)
+        // and the matching up columns 128 + [32g, 32g + 32) (h columns
+        // [32g, 32g + 32) of the tile); MODE 1 columns [64g, 64g + 64).
         const int q = warp & 3, g = (warp - 2) >> 2, r = q * 32 + lane;
         const uint32_t lane_addr = tmem + (static_cast<uint32_t>(q * 32) << 16);
+        const uint32_t c0 = MODE == 0 ? 32 * g : 64 * g;
+        const uint32_t c1 = MODE == 0 ? 128 + 32 * g : 64 * g + 32;
         float* amax = reinterpret_cast<float*>(smem + kOffAmax);
         uint32_t c = 0;
         int it = 0;
@@ -321,9 +340,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                 pair = a.order[x.row0 + r];
                 route_w = load_any(a.weights, a.weights_dtype, pair);
             }
-            uint64_t acc[64];
+            uint64_t acc[32];
 #pragma unroll
-            for (int j = 0; j < 64; ++j) acc[j] = 0ull;
+            for (int j = 0; j < 32; ++j) acc[j] = 0ull;
             for (int kb = 0; kb < KB; ++kb, ++c) {
                 const int buf = c & 1;
                 if (!warp_wait(bar(kBarTFull + buf), (c >> 1) & 1, timeout_flag)) {
@@ -331,59 +350,48 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                     break;
                 }
                 tcgen05_after_sync();
+                const uint32_t base = lane_addr + buf * kTcN;
+                uint32_t ra[16], rb[16];
+                tmem_ld16(base + c0, ra);
+                tmem_ld16(base + c0 + 16, rb);
                 const float sa = sc[kb * kTcM + r];
                 const float* sw = sc + kTcMaxKb * kTcM;
-                // MODE 0: columns [64g, 64g + 64) of the gate half and of the up half;
-                // MODE 1: columns [128g, 128g + 128), one weight block.
-                const uint64_t s0 = splat_f32x2(__fmul_rn(sa, MODE == 0 ? sw[kb] : sw[g * kTcMaxKb + kb]));
+                const uint64_t s0 = splat_f32x2(__fmul_rn(sa, MODE == 0 ? sw[kb] : sw[(g >> 1) * kTcMaxKb + kb]));
                 const uint64_t s1 = MODE == 0 ? splat_f32x2(__fmul_rn(sa, sw[kTcMaxKb + kb])) : s0;
-                const uint32_t base = lane_addr + buf * kTcN;
-                const uint32_t c0 = MODE == 0 ? 64 * g : 128 * g;
-                const uint32_t c1 = MODE == 0 ? 128 + 64 * g : 128 * g + 64;
-                uint32_t ra[16], rb[16];
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const uint32_t col = (h == 0 ? c0 : c1);
-                    const uint64_t s = h == 0 ? s0 : s1;
-                    tmem_ld16(base + col, ra);
-                    tmem_ld16(base + col + 16, rb);
-                    tmem_wait2x16(ra, rb);
-                    promote16(acc + 32 * h, ra, s);
-                    promote16(acc + 32 * h + 8, rb, s);
-                    tmem_ld16(base + col + 32, ra);
-                    tmem_ld16(base + col + 48, rb);
-                    tmem_wait2x16(ra, rb);
-                    if (h == 1) {
-                        tcgen05_before_sync();
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(bar(kBarTEmpty + buf));
-                    }
-                    promote16(acc + 32 * h + 16, ra, s);
-                    promote16(acc + 32 * h + 24, rb, s);
-                }
+                tmem_wait2x16(ra, rb);
+                promote16(acc, ra, s0);
+                promote16(acc + 8, rb, s0);
+                tmem_ld16(base + c1, ra);
+                tmem_ld16(base + c1 + 16, rb);
+                tmem_wait2x16(ra, rb);
+                tcgen05_before_sync();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar(kBarTEmpty + buf));
+                promote16(acc + 16, ra, s1);
+                promote16(acc + 24, rb, s1);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(kBarSEmpty + slot));
             if (!ok) break;
             if (MODE == 0) {
-                // acc[0..31]: gate columns 64g.., acc[32..63]: the matching up columns
-                float hv[64];
+                // acc[0..15]: gate columns, acc[16..31]: the matching up columns
+                float hv[32];
                 float m = 0.0f;
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
+                for (int j = 0; j < 16; ++j) {
                     float g0, g1, u0, u1;
                     unpack_f32x2(acc[j], g0, g1);
-                    unpack_f32x2(acc[32 + j], u0, u1);
+                    unpack_f32x2(acc[16 + j], u0, u1);
                     const float gb0 = __bfloat162float(__float2bfloat16_rn(g0));
                     const float gb1 = __bfloat162float(__float2bfloat16_rn(g1));
                     const float ub0 = __bfloat162float(__float2bfloat16_rn(u0));
                     const float ub1 = __bfloat162float(__float2bfloat16_rn(u1));
-                    hv[2 * j] = __fmul_rn(__fdiv_rn(gb0, __fadd_rn(1.0f, expf(-gb0))), ub0);
-                    hv[2 * j + 1] = __fmul_rn(__fdiv_rn(gb1, __fadd_rn(1.0f, expf(-gb1))), ub1);
+                    hv[2 * j] = __fmul_rn(__fdividef(gb0, __fadd_rn(1.0f, __expf(-gb0))), ub0);
+                    hv[2 * j + 1] = __fmul_rn(__fdividef(gb1, __fadd_rn(1.0f, __expf(-gb1))), ub1);
                     m = fmaxf(m, fmaxf(fabsf(hv[2 * j]), fabsf(hv[2 * j + 1])));
                 }
-                // the row's other 64 h columns are in the other half's thread
-                float* am = amax + (slot * 2) * kTcM;
+                // the row's other 96 h columns of the 1x128 block are in the other groups' threads
+                float* am = amax + slot * kTcGroups * kTcM;
                 am[g * kTcM + r] = m;
                 __syncwarp();
                 if (lane == 0) mbar_arrive(bar(kBarAmax + slot));
@@ -391,33 +399,32 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                     ok = false;
                     break;
                 }
-                const float row_max = fmaxf(fmaxf(am[r], am[kTcM + r]), 1e-10f);
+                const float row_max =
+                    fmaxf(fmaxf(fmaxf(am[r], am[kTcM + r]), fmaxf(am[2 * kTcM + r], am[3 * kTcM + r])), 1e-10f);
                 const float scale = __fmul_rn(row_max, 1.0f / 448.0f);
+                const float inv = __frcp_rn(scale);
                 if (r < x.rows) {
                     const int64_t row = x.row0 + r;
-                    uint4* dst = reinterpret_cast<uint4*>(a.hq + row * a.I + x.n0 + 64 * g);
+                    uint32_t w[8];
 #pragma unroll
-                    for (int v = 0; v < 4; ++v) {
-                        uint32_t w[4];
-#pragma unroll
-                        for (int u = 0; u < 4; ++u) {
-                            const int j = 16 * v + 4 * u;
-                            w[u] = e4m3x2(__fdiv_rn(hv[j], scale), __fdiv_rn(hv[j + 1], scale)) |
-                                   (e4m3x2(__fdiv_rn(hv[j + 2], scale), __fdiv_rn(hv[j + 3], scale)) << 16);
-                        }
-                        dst[v] = make_uint4(w[0], w[1], w[2], w[3]);
-                    }
+                    for (int u = 0; u < 8; ++u)
+                        w[u] = e4m3x2(__fmul_rn(hv[4 * u], inv), __fmul_rn(hv[4 * u + 1], inv)) |
+                               (e4m3x2(__fmul_rn(hv[4 * u + 2], inv), __fmul_rn(hv[4 * u + 3], inv)) << 16);
+                    st_global_32b(a.hq + row * a.I + x.n0 + 32 * g, w[0], w[1], w[2], w[3], w[4], w[5], w[6], w[7]);
                     if (g == 0) a.hs[row * (a.I / 128) + x.n0 / 128] = scale;
                 }
             } else if (r < x.rows) {
-                float4* dst = reinterpret_cast<float4*>(a.pair_out + pair * a.H + x.n0 + 128 * g);
+                float* dst = a.pair_out + pair * a.H + x.n0 + 64 * g;
 #pragma unroll
-                for (int v = 0; v < 32; ++v) {
-                    float f0, f1, f2, f3;
-                    unpack_f32x2(acc[2 * v], f0, f1);
-                    unpack_f32x2(acc[2 * v + 1], f2, f3);
-                    dst[v] = make_float4(__fmul_rn(f0, route_w), __fmul_rn(f1, route_w), __fmul_rn(f2, route_w),
-                                         __fmul_rn(f3, route_w));
+                for (int v = 0; v < 8; ++v) {
+                    float f[8];
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) unpack_f32x2(acc[4 * v + u], f[2 * u], f[2 * u + 1]);
+                    st_global_32b(dst + 8 * v, __float_as_uint(__fmul_rn(f[0], route_w)),
+                                  __float_as_uint(__fmul_rn(f[1], route_w)), __float_as_uint(__fmul_rn(f[2], route_w)),
+                                  __float_as_uint(__fmul_rn(f[3], route_w)), __float_as_uint(__fmul_rn(f[4], route_w)),
+                                  __float_as_uint(__fmul_rn(f[5], route_w)), __float_as_uint(__fmul_rn(f[6], route_w)),
+                                  __float_as_uint(__fmul_rn(f[7], route_w)));
                 }
             }
         }
@@ -431,16 +438,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
     }
 }
 
-// One sorted pair row per CTA: the pair's token row quantised 1x128 into
-// sorted position r (half a warp per block, 8 values per lane).
-__global__ void __launch_bounds__(256) tc_quant_rows_kernel(const __nv_bfloat16* x, int H, const int64_t* order,
-                                                            const int64_t* offsets, int E, int top_k, uint8_t* xq,
-                                                            float* xs) {
+// One token row per CTA: its 1x128 blocks quantised once (half a warp per
+// block, 8 values per lane) and written to the sorted position of each of
+// the token's pairs.
+__global__ void __launch_bounds__(256) tc_quant_tokens_kernel(const __nv_bfloat16* x, int H, int top_k,
+                                                              const int64_t* position, uint8_t* xq, float* xs) {
+    __shared__ int64_t s_pos[32];
     grid_dependency_wait();
     grid_launch_dependents();
-    const int64_t r = blockIdx.x;
-    if (r >= offsets[E]) return;
-    const int64_t token = order[r] / top_k;
+    const int64_t token = blockIdx.x;
+    if (threadIdx.x < top_k) s_pos[threadIdx.x] = position[token * top_k + threadIdx.x];
+    __syncthreads();
     const int hw = threadIdx.x >> 4, l = threadIdx.x & 15, nblk = H / 128;
     for (int base = 0; base < nblk; base += 16) {
         const int blk = base + hw;
@@ -456,12 +464,15 @@ __global__ void __launch_bounds__(256) tc_quant_rows_kernel(const __nv_bfloat16*
 #pragma unroll
         for (int off = 8; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
         const float scale = __fmul_rn(fmaxf(m, 1e-10f), 1.0f / 448.0f);
-        if (on) {
-            uint2 q;
-            q.x = e4m3x2(__fdiv_rn(f[0], scale), __fdiv_rn(f[1], scale)) |
-                  (e4m3x2(__fdiv_rn(f[2], scale), __fdiv_rn(f[3], scale)) << 16);
-            q.y = e4m3x2(__fdiv_rn(f[4], scale), __fdiv_rn(f[5], scale)) |
-                  (e4m3x2(__fdiv_rn(f[6], scale), __fdiv_rn(f[7], scale)) << 16);
+        if (!on) continue;
+        uint2 q;
+        q.x = e4m3x2(__fdiv_rn(f[0], scale), __fdiv_rn(f[1], scale)) |
+              (e4m3x2(__fdiv_rn(f[2], scale), __fdiv_rn(f[3], scale)) << 16);
+        q.y = e4m3x2(__fdiv_rn(f[4], scale), __fdiv_rn(f[5], scale)) |
+              (e4m3x2(__fdiv_rn(f[6], scale), __fdiv_rn(f[7], scale)) << 16);
+        for (int s = 0; s < top_k; ++s) {
+            const int64_t r = s_pos[s];
+            if (r < 0) continue;
             *reinterpret_cast<uint2*>(xq + r * H + blk * 128 + l * 8) = q;
             if (l == 0) xs[r * nblk + blk] = scale;
         }
@@ -568,6 +579,8 @@ size_t fp8_prefill_tc_workspace_layout(int64_t tokens, int top_k, int hidden, in
     w.order = reinterpret_cast<int64_t*>(take(P * 8));
     w.counts = reinterpret_cast<int64_t*>(take(static_cast<size_t>(experts) * 8));
     w.offsets = reinterpret_cast<int64_t*>(take(static_cast<size_t>(experts + 1) * 8));
+    w.position = reinterpret_cast<int64_t*>(take(P * 8));
+    w.chunk_counts = reinterpret_cast<int*>(take(permute_wide_scratch_bytes(P, experts)));
     w.xq = reinterpret_cast<uint8_t*>(take(rows * hidden));
     w.xs = reinterpret_cast<float*>(take(rows * (hidden / 128) * 4));
     w.hq = reinterpret_cast<uint8_t*>(take(rows * intermediate));
@@ -597,10 +610,10 @@ cudaError_t fp8_prefill_tc_launch(const DramaB200Fp8Bank& bank, const void* x, i
     cudaError_t err = cudaMemsetAsync(ws.status, 0, 16, s);
     if (err != cudaSuccess) return err;
     PermuteArgs pa{ids, ids_dtype, P, E, ws.order, ws.counts, ws.offsets, ws.status};
-    if ((err = permute_routes(pa, s)) != cudaSuccess) return err;
-    if ((err = launch_pdl_smem(tc_quant_rows_kernel, dim3(static_cast<unsigned>(P)), dim3(256), 0, s,
-                               static_cast<const __nv_bfloat16*>(x), H, static_cast<const int64_t*>(ws.order),
-                               static_cast<const int64_t*>(ws.offsets), E, top_k, ws.xq, ws.xs)) != cudaSuccess)
+    if ((err = permute_routes_wide(pa, ws.chunk_counts, ws.position, s)) != cudaSuccess) return err;
+    if ((err = launch_pdl_smem(tc_quant_tokens_kernel, dim3(static_cast<unsigned>(tokens)), dim3(256), 0, s,
+                               static_cast<const __nv_bfloat16*>(x), H, top_k,
+                               static_cast<const int64_t*>(ws.position), ws.xq, ws.xs)) != cudaSuccess)
         return err;
     TcGemmArgs g{};
     g.offsets = ws.offsets;

@@ -54,6 +54,11 @@ struct PermuteArgs {
 };
 cudaError_t permute_routes(const PermuteArgs& a, cudaStream_t s);
 size_t bucket_smem_bytes(int experts);
+// The same permutation over many CTAs (experts <= 1024), for many pairs:
+// chunk_counts is scratch of permute_wide_scratch_bytes; position[p] (when
+// given) receives pair p's sorted position, -1 for a dropped pair.
+size_t permute_wide_scratch_bytes(int64_t pairs, int experts);
+cudaError_t permute_routes_wide(const PermuteArgs& a, int* chunk_counts, int64_t* position, cudaStream_t s);
 
 // ---------------------------------------------------------------------------
 // Decode (K1) workspace carved out of one caller buffer.
@@ -285,6 +290,8 @@ struct Fp8PrefillWorkspace {
     int64_t* order;     // [P] pairs sorted by expert
     int64_t* counts;    // [E]
     int64_t* offsets;   // [E + 1]
+    int64_t* position;  // [P] sorted position of each pair (-1: dropped)
+    int* chunk_counts;  // permutation scratch
     uint8_t* xq;        // [P + 128][H] E4M3 token rows in sorted order
     float* xs;          // [P + 128][H/128]
     uint8_t* hq;        // [P + 128][I] E4M3 SwiGLU rows in sorted order

@@ -97,9 +97,124 @@ __global__ void __launch_bounds__(1024) permute_kernel(PermuteArgs a) {
     if (threadIdx.x == 0 && a.status) a.status[0] = dropped;
 }
 
+// The same stable permutation for many pairs over many CTAs: each CTA takes
+// a chunk of kWideChunk consecutive pairs; the first launch counts each
+// chunk's pairs per expert, the second places a chunk's pairs of expert e
+// after expert e's pairs of every earlier chunk (so the order stays the
+// pairs' index order within each expert) and records each pair's position.
+constexpr int kWideChunk = 1024;
+
+__global__ void __launch_bounds__(kWideChunk) permute_count_kernel(PermuteArgs a, int* chunk_counts) {
+    extern __shared__ int s_counts[];
+    grid_dependency_wait();
+    grid_launch_dependents();
+    for (int e = threadIdx.x; e < a.experts; e += blockDim.x) s_counts[e] = 0;
+    __syncthreads();
+    const int64_t p = static_cast<int64_t>(blockIdx.x) * kWideChunk + threadIdx.x;
+    if (p < a.pairs) {
+        const int64_t id = load_index(a.ids, a.ids_dtype, p);
+        if (id >= 0 && id < a.experts) atomicAdd(&s_counts[id], 1);
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < a.experts; e += blockDim.x)
+        chunk_counts[static_cast<int64_t>(blockIdx.x) * a.experts + e] = s_counts[e];
+}
+
+__global__ void __launch_bounds__(kWideChunk) permute_place_kernel(PermuteArgs a, const int* chunk_counts,
+                                                                    int64_t* position) {
+    extern __shared__ int smem[];
+    int* base = smem;                  // [E] first position of this chunk's pairs of each expert
+    int* wc = smem + a.experts;        // [32][E] per-warp counts of the current pass
+    __shared__ int warp_tot[32];
+    grid_dependency_wait();
+    grid_launch_dependents();
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, E = a.experts;
+    const int chunks = gridDim.x, me = blockIdx.x;
+    // total and earlier-chunk counts per expert (one expert per thread)
+    int total = 0, before = 0;
+    if (tid < E) {
+        for (int b = 0; b < chunks; ++b) {
+            const int c = chunk_counts[static_cast<int64_t>(b) * E + tid];
+            total += c;
+            if (b < me) before += c;
+        }
+    }
+    // exclusive scan of the totals over experts
+    int x = total;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, off);
+        if (lane >= off) x += y;
+    }
+    if (lane == 31) warp_tot[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        int t = warp_tot[lane];
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, t, off);
+            if (lane >= off) t += y;
+        }
+        warp_tot[lane] = t;
+    }
+    __syncthreads();
+    const int start = x - total + (warp ? warp_tot[warp - 1] : 0);
+    if (tid < E) {
+        base[tid] = start + before;
+        if (me == 0) {
+            a.counts[tid] = total;
+            a.offsets[tid] = start;
+            if (tid == E - 1) a.offsets[E] = start + total;
+        }
+    }
+    if (me == 0 && tid == 0 && a.status) a.status[0] = static_cast<int32_t>(a.pairs - warp_tot[31]);
+    for (int e = tid; e < 32 * E; e += blockDim.x) wc[e] = 0;
+    __syncthreads();
+    // stable ranks inside the chunk (index order within each expert)
+    const int64_t p = static_cast<int64_t>(me) * kWideChunk + tid;
+    int64_t id = p < a.pairs ? load_index(a.ids, a.ids_dtype, p) : -1;
+    if (id < 0 || id >= E) id = -1;
+    const unsigned mask = __match_any_sync(0xffffffffu, static_cast<int>(id));
+    const int rank = __popc(mask & ((1u << lane) - 1u));
+    if (id >= 0 && lane == __ffs(mask) - 1) wc[warp * E + id] = __popc(mask);
+    __syncthreads();
+    if (p < a.pairs) {
+        int64_t pos = -1;
+        if (id >= 0) {
+            int q = base[id] + rank;
+            for (int w = 0; w < warp; ++w) q += wc[w * E + id];
+            a.order[q] = p;
+            pos = q;
+        }
+        if (position) position[p] = pos;
+    }
+}
+
 }  // namespace
 
 size_t bucket_smem_bytes(int experts) { return static_cast<size_t>(34) * experts * sizeof(int); }
+
+size_t permute_wide_scratch_bytes(int64_t pairs, int experts) {
+    return static_cast<size_t>((pairs + kWideChunk - 1) / kWideChunk) * experts * sizeof(int);
+}
+
+cudaError_t permute_routes_wide(const PermuteArgs& a, int* chunk_counts, int64_t* position, cudaStream_t s) {
+    if (a.experts > kWideChunk) return cudaErrorInvalidValue;
+    static bool configured = false;  // benign race: same value from any thread
+    if (!configured) {
+        const cudaError_t err = cudaFuncSetAttribute(permute_place_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                     static_cast<int>(33 * kWideChunk * sizeof(int)));
+        if (err != cudaSuccess) return err;
+        configured = true;
+    }
+    const unsigned chunks = static_cast<unsigned>((a.pairs + kWideChunk - 1) / kWideChunk);
+    if (chunks == 0) return cudaSuccess;
+    cudaError_t err = launch_pdl(permute_count_kernel, dim3(chunks), dim3(kWideChunk), a.experts * sizeof(int), s, a,
+                                 chunk_counts);
+    if (err != cudaSuccess) return err;
+    return launch_pdl(permute_place_kernel, dim3(chunks), dim3(kWideChunk), 33 * a.experts * sizeof(int), s, a,
+                      static_cast<const int*>(chunk_counts), position);
+}
 
 cudaError_t permute_routes(const PermuteArgs& a, cudaStream_t s) {
     const size_t smem = bucket_smem_bytes(a.experts);

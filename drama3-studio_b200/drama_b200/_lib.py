@@ -33,6 +33,8 @@ EXPORTS = (
     "drama_b200_device_check",
     "drama_b200_route_topk",
     "drama_b200_permute_routes",
+    "drama_b200_permute_routes_wide_scratch_bytes",
+    "drama_b200_permute_routes_wide",
     "drama_b200_decode_workspace_bytes",
     "drama_b200_decode_status_offset",
     "drama_b200_fp8_decode",
@@ -164,6 +166,11 @@ class Library:
         dll.drama_b200_fp8_w8a8_decode.argtypes = [
             ctypes.POINTER(Fp8Bank), c_void_p, c_int64, c_int, c_void_p, c_int, c_void_p, c_int, c_void_p,
             c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]
+        dll.drama_b200_permute_routes_wide_scratch_bytes.argtypes = [c_int64, c_int]
+        dll.drama_b200_permute_routes_wide_scratch_bytes.restype = c_size_t
+        dll.drama_b200_permute_routes_wide.argtypes = [c_void_p, c_int, c_int64, c_int, c_void_p, c_void_p, c_void_p,
+                                                       c_void_p, c_void_p, c_size_t, c_void_p, c_void_p]
+        dll.drama_b200_permute_routes_wide.restype = c_int
         dll.drama_b200_fp8_w8a8_prefill_supported.argtypes = [c_int, c_int, c_int]
         dll.drama_b200_fp8_w8a8_prefill_supported.restype = c_int
         dll.drama_b200_fp8_w8a8_prefill_workspace_bytes.argtypes = [c_int64, c_int, c_int, c_int, c_int]

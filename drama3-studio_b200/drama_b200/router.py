@@ -45,9 +45,13 @@ def route_topk(logits: Tensor, top_k: int, *, renormalize: bool = True,
     return weights, ids
 
 
-def permute_routes(ids: Tensor, num_experts: int, *, status: Tensor | None = None
-                   ) -> tuple[Tensor, Tensor, Tensor]:
-    """Stable argsort of flat route IDs plus bincount and start offsets (int64)."""
+def permute_routes(ids: Tensor, num_experts: int, *, status: Tensor | None = None, wide: bool | None = None,
+                   position: Tensor | None = None) -> tuple[Tensor, Tensor, Tensor]:
+    """Stable argsort of flat route IDs plus bincount and start offsets (int64).
+
+    ``wide`` picks the many-CTA form (default: from 4096 pairs on), which can
+    also fill ``position`` (int64, each pair's sorted position or -1).
+    """
     if not ids.is_cuda:
         raise ValueError("Route IDs must be a CUDA tensor")
     if ids.dtype not in (torch.int32, torch.int64):
@@ -57,6 +61,16 @@ def permute_routes(ids: Tensor, num_experts: int, *, status: Tensor | None = Non
     counts = torch.empty(num_experts, device=ids.device, dtype=torch.int64)
     offsets = torch.empty(num_experts + 1, device=ids.device, dtype=torch.int64)
     lib = _lib.library()
+    if wide is None:
+        wide = flat.numel() > 4096 or position is not None
+    if wide:
+        nbytes = lib.dll.drama_b200_permute_routes_wide_scratch_bytes(flat.numel(), num_experts)
+        scratch = torch.empty(max(nbytes, 16), device=ids.device, dtype=torch.uint8)
+        lib.check(lib.dll.drama_b200_permute_routes_wide(
+            flat.data_ptr(), _lib.DTYPE_CODES[flat.dtype], flat.numel(), num_experts, order.data_ptr(),
+            counts.data_ptr(), offsets.data_ptr(), _lib.ptr(position), scratch.data_ptr(), scratch.numel(),
+            _lib.ptr(status), _lib.stream_handle(ids.device)))
+        return order, counts, offsets
     lib.check(lib.dll.drama_b200_permute_routes(
         flat.data_ptr(), _lib.DTYPE_CODES[flat.dtype], flat.numel(), num_experts,
         order.data_ptr(), counts.data_ptr(), offsets.data_ptr(), _lib.ptr(status),

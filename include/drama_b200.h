@@ -83,6 +83,18 @@ DRAMA_B200_API int drama_b200_permute_routes(const void* ids, int ids_dtype, int
                                              int experts, int64_t* order, int64_t* counts,
                                              int64_t* offsets, int32_t* status, void* stream);
 
+/* The same permutation over many CTAs, for many pairs (the single-CTA form
+ * above serves decode-sized calls): the same order, counts and offsets, and
+ * position[p] = the sorted position of pair p (-1 for a dropped pair; may be
+ * NULL). scratch: drama_b200_permute_routes_wide_scratch_bytes bytes of
+ * device memory, 16-byte aligned. status[0] is written (not accumulated). */
+DRAMA_B200_API size_t drama_b200_permute_routes_wide_scratch_bytes(int64_t pairs, int experts);
+
+DRAMA_B200_API int drama_b200_permute_routes_wide(const void* ids, int ids_dtype, int64_t pairs, int experts,
+                                                  int64_t* order, int64_t* counts, int64_t* offsets,
+                                                  int64_t* position, void* scratch, size_t scratch_bytes,
+                                                  int32_t* status, void* stream);
+
 /* ---------------------------------------------------------------------------
  * Expert banks. Layouts are the reference's staged views: ExpertStore /
  * StagedExperts (src/drama_low_vram/offload.py:101-184) for FP8 and
@@ -182,7 +194,7 @@ DRAMA_B200_API int drama_b200_fp8_w8a8_decode(const DramaB200Fp8Bank* bank, cons
  * grouped GEMMs with 128x128 weight block scales promoted per 128-wide K block,
  * then the slot-ordered combine. Outputs as drama_b200_fp8_w8a8_decode
  * (out and/or pair_out; a pair with an out-of-range id contributes zero and
- * its pair_out row is zero). hidden a multiple of 256 and <= 2048,
+ * its pair_out row is zero; pair_out 32-byte aligned). hidden a multiple of 256 and <= 2048,
  * intermediate a multiple of 128 and <= 2048, at most 512 experts
  * (drama_b200_fp8_w8a8_prefill_supported); at most 2^24 pairs; bf16 rows; workspace 256-byte
  * aligned, drama_b200_fp8_w8a8_prefill_workspace_bytes bytes.

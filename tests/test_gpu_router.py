@@ -63,7 +63,7 @@ def test_route_topk_int32_fp32_outputs(cuda_device):
 
 @pytest.mark.parametrize("experts,shape,kind", [
     (128, (1, 8), "uniform"), (128, (4, 8), "uniform"), (6, (64, 8), "dense"),
-    (128, (4096, 8), "zipf"), (4, (5, 3), "single"), (1024, (300, 7), "dense"),
+    (128, (4096, 8), "zipf"), (4, (5, 3), "single"), (1024, (300, 7), "dense"), (128, (40000, 8), "zipf"),
 ])
 def test_permute_routes_matches_stable_argsort(cuda_device, experts, shape, kind):
     from drama_b200 import permute_routes, synthetic
@@ -78,20 +78,31 @@ def test_permute_routes_matches_stable_argsort(cuda_device, experts, shape, kind
     else:
         ids = torch.randint(0, experts, shape, generator=gen)
     for dtype in (torch.int64, torch.int32):
-        order, counts, offsets = permute_routes(ids.to(cuda_device, dtype), experts)
-        flat = ids.reshape(-1)
-        assert torch.equal(order.cpu(), torch.argsort(flat, stable=True))
-        assert torch.equal(counts.cpu(), torch.bincount(flat, minlength=experts))
-        o_order, o_counts, o_offsets = R.permute_routes(flat.numpy(), experts)
-        np.testing.assert_array_equal(offsets.cpu().numpy(), o_offsets)
+        for wide in (False, True):
+            position = torch.empty(ids.numel(), dtype=torch.int64, device=cuda_device) if wide else None
+            order, counts, offsets = permute_routes(ids.to(cuda_device, dtype), experts, wide=wide,
+                                                    position=position)
+            flat = ids.reshape(-1)
+            assert torch.equal(order.cpu(), torch.argsort(flat, stable=True))
+            assert torch.equal(counts.cpu(), torch.bincount(flat, minlength=experts))
+            o_order, o_counts, o_offsets = R.permute_routes(flat.numpy(), experts)
+            np.testing.assert_array_equal(offsets.cpu().numpy(), o_offsets)
+            if wide:  # position is the inverse of order
+                inv = torch.empty_like(order)
+                inv[order] = torch.arange(order.numel(), device=order.device)
+                assert torch.equal(position, inv)
 
 
 def test_permute_routes_counts_out_of_range_ids(cuda_device):
     from drama_b200 import permute_routes
 
     ids = torch.tensor([3, 9, 1, -1, 3], device=cuda_device)
-    status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
-    order, counts, offsets = permute_routes(ids, 4, status=status)
-    assert int(status.item()) == 2
-    assert counts.cpu().tolist() == [0, 1, 0, 2]
-    assert order.cpu()[:3].tolist() == [2, 0, 4]
+    for wide in (False, True):
+        status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+        position = torch.empty(5, dtype=torch.int64, device=cuda_device) if wide else None
+        order, counts, offsets = permute_routes(ids, 4, status=status, wide=wide, position=position)
+        assert int(status.item()) == 2
+        assert counts.cpu().tolist() == [0, 1, 0, 2]
+        assert order.cpu()[:3].tolist() == [2, 0, 4]
+        if wide:
+            assert position.cpu().tolist() == [1, -1, 0, -1, 2]
