@@ -60,12 +60,14 @@ constexpr int kDlMaxHidden = 2048;
 // 128-byte swizzle of the TMA stages repeats every 1024 bytes). The ring and
 // the down-projection buffer are one region; it holds the staged router rows
 // until routing is done, and the partial rows for the combine at the end.
+// With `overlay` every gate/up stage of the unit has its own slot (no ring
+// reuse) and the down rows land over the first stages once they are consumed.
 struct DlLayout {
-    int hq, kbq, stage, stages, nkt, w2_cols, w2_rows, w2_boxes;
+    int hq, kbq, stage, stages, nkt, w2_cols, w2_rows, w2_boxes, w2_stages, overlay;
     uint32_t region, w2, hin, norm, x16, logit, cell, xch, h16, s2, full, empty, w2_bar, total;
 };
 
-__host__ __device__ inline DlLayout dl_layout(int H, int E, int nkt, int stages) {
+__host__ __device__ inline DlLayout dl_layout(int H, int E, int nkt, int stages, int overlay) {
     DlLayout L{};
     L.hq = H / kDlCluster;
     L.kbq = L.hq / 128;
@@ -84,9 +86,12 @@ __host__ __device__ inline DlLayout dl_layout(int H, int E, int nkt, int stages)
         return p;
     };
     const uint32_t ring_bytes = static_cast<uint32_t>(stages) * L.stage;
-    L.region = ring_bytes + static_cast<uint32_t>(L.w2_boxes) * L.w2_rows * 64;
+    const uint32_t w2_bytes = static_cast<uint32_t>(L.w2_boxes) * L.w2_rows * 64;
+    L.overlay = overlay;
+    L.w2_stages = static_cast<int>((w2_bytes + L.stage - 1) / L.stage);
+    L.region = overlay ? (ring_bytes > w2_bytes ? ring_bytes : w2_bytes) : ring_bytes + w2_bytes;
     take(L.region);
-    L.w2 = ring_bytes;
+    L.w2 = overlay ? 0 : ring_bytes;
     L.hin = take(H * 2);
     L.norm = take(H * 4);
     L.x16 = take(L.hq * 2);
@@ -122,7 +127,7 @@ __global__ void __launch_bounds__(kDlThreads, 1) decode_layer_kernel(const __gri
 
     const RoutedLayerArgs& A = a.layer;
     const int H = A.H, I = A.I, E = A.E, k = A.k;
-    const DlLayout L = dl_layout(H, E, a.nkt, a.stages);
+    const DlLayout L = dl_layout(H, E, a.nkt, a.stages, a.overlay);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
     cg::cluster_group cluster = cg::this_cluster();
     const int r = static_cast<int>(cluster.block_rank());
@@ -390,7 +395,29 @@ __global__ void __launch_bounds__(kDlThreads, 1) decode_layer_kernel(const __gri
     if (warp == kDlWarps) {
         // Producer: stage s = the unit's tile tile0 + s, one 5-D box
         // {128 B, KBQ blocks, 16 rows, gate|up, 1 slot} per stage.
-        if (lane == 0) {
+        if (lane == 0 && L.overlay) {
+            // Every gate/up stage of the unit at once; the down rows to L2
+            // now, and into the first stages once those are consumed.
+            const uint64_t pol = policy_evict_first();
+            for (int s = 0; s < nkt; ++s) {
+                mbar_arrive_expect_tx(full0 + 8 * s, static_cast<uint32_t>(L.stage));
+                tma_load_5d(base_u32 + s * L.stage, &a.w13_map, 0, r * KBQ, (tile0 + s) * 16, 0, expert,
+                            full0 + 8 * s, pol);
+            }
+            const int rboxes = HQ / L.w2_rows;
+            for (int bx = 0; bx < L.w2_boxes; ++bx) {
+                const int cb = bx / rboxes, rb = bx - cb * rboxes;
+                tma_prefetch_3d(&a.w2_map, (tile0 + 4 * cb) * 16, r * HQ + rb * L.w2_rows, expert);
+            }
+            for (int s = 0; s < L.w2_stages; ++s) mbar_wait(empty0 + 8 * s, 0, status);
+            const uint32_t w2b = base_u32 + L.w2_bar;
+            mbar_arrive_expect_tx(w2b, static_cast<uint32_t>(L.w2_boxes) * L.w2_rows * 64u);
+            for (int bx = 0; bx < L.w2_boxes; ++bx) {
+                const int cb = bx / rboxes, rb = bx - cb * rboxes;
+                tma_load_3d(base_u32 + L.w2 + bx * L.w2_rows * 64, &a.w2_map, (tile0 + 4 * cb) * 16,
+                            r * HQ + rb * L.w2_rows, expert, w2b, pol);
+            }
+        } else if (lane == 0) {
             const uint64_t pol = policy_evict_first();
             const int first = nkt < L.stages ? nkt : L.stages;
             for (int s = 0; s < nkt; ++s) {
@@ -698,12 +725,18 @@ DlPlan dl_plan(int H, int I, int E, int k, int clusters) {
     if (parts < 1) return p;
     const int nkt = (tpi + parts - 1) / parts;
     if (nkt > kDlMaxTiles) return p;
-    const DlLayout base = dl_layout(H, E, nkt, 0);
-    const int stages = static_cast<int>((kDlMaxSmem - static_cast<int>(base.total)) / base.stage);
-    if (stages < 2) return p;
-    const int use = stages > 8 ? 8 : stages;
-    const DlLayout L = dl_layout(H, E, nkt, use);
-    if (L.total > static_cast<uint32_t>(kDlMaxSmem)) return p;
+    // Every stage of the unit resident (the down rows over the first ones)
+    // when shared memory allows, else a ring of up to 8 stages beside them.
+    DlLayout L = dl_layout(H, E, nkt, nkt, 1);
+    int use = nkt;
+    if (L.total > static_cast<uint32_t>(kDlMaxSmem) || nkt < L.w2_stages) {
+        const DlLayout base = dl_layout(H, E, nkt, 0, 0);
+        const int stages = static_cast<int>((kDlMaxSmem - static_cast<int>(base.total)) / base.stage);
+        if (stages < 2) return p;
+        use = stages > 8 ? 8 : stages;
+        L = dl_layout(H, E, nkt, use, 0);
+        if (L.total > static_cast<uint32_t>(kDlMaxSmem)) return p;
+    }
     // every router row of a rank staged in the region before routing, and
     // every unit's partial rows of a quarter in it for the combine
     if (static_cast<uint32_t>((E + kDlCluster - 1) / kDlCluster) * H * 2 > L.region ||
@@ -801,6 +834,7 @@ cudaError_t decode_layer_launch(DecodeLayerArgs a, cudaStream_t s) {
     a.parts = p.parts;
     a.nkt = p.nkt;
     a.stages = p.stages;
+    a.overlay = p.layout.overlay;
     // W13 [slot][gate|up][row][H] viewed as [slot][2][I][H/128][128] bytes;
     // one box = 16 rows of gate and up, this CTA's H/4 bytes of each.
     const DramaB200Fp8Bank& b = A.bank;

@@ -362,7 +362,7 @@ struct DecodeLayerArgs {
     const __nv_bfloat16* logits_in;      // null: RMSNorm and router GEMV inside the kernel
     float* part;                         // [units][H] fp32 partial down projections
     int32_t* tickets;                    // [4] arrival tickets, reset by the last arriver
-    int parts, nkt, stages;              // set by decode_layer_launch (with w13_map)
+    int parts, nkt, stages, overlay;     // set by decode_layer_launch (with w13_map)
 };
 bool decode_layer_supported(int64_t tokens, int top_k, int hidden, int intermediate, int experts);
 cudaError_t decode_layer_launch(DecodeLayerArgs a, cudaStream_t s);

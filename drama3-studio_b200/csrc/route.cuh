@@ -13,21 +13,19 @@ __device__ __forceinline__ void route_finish(int k, bool renormalize, int lane, 
                                              int& out_idx, float& out_w) {
     constexpr unsigned kFull = 0xffffffffu;
     float key = lane < k ? s_key[lane] : 0.0f;
-    int idx = lane < k ? s_idx[lane] : 0;
-    bool valid = lane < k;
+    // index and validity travel together: (index << 1) | valid
+    int iv = lane < k ? (s_idx[lane] << 1) | 1 : 0;
     // 32-slot bitonic network (lane = slot); pair (l, l ^ stride).
     auto stage = [&](int stride, bool flag) {
         const float pk = __shfl_xor_sync(kFull, key, stride);
-        const int pi = __shfl_xor_sync(kFull, idx, stride);
-        const bool pv = __shfl_xor_sync(kFull, valid, stride);
+        const int piv = __shfl_xor_sync(kFull, iv, stride);
         const bool is_a = (lane & stride) == 0;
         const float ka = is_a ? key : pk, kb = is_a ? pk : key;
-        const bool va = is_a ? valid : pv, vb = is_a ? pv : valid;
+        const bool va = (is_a ? iv : piv) & 1, vb = (is_a ? piv : iv) & 1;
         const bool swap = ((ka > kb) && va) || !vb;
         if (swap == flag) {
             key = pk;
-            idx = pi;
-            valid = pv;
+            iv = piv;
         }
     };
 #pragma unroll
@@ -38,6 +36,8 @@ __device__ __forceinline__ void route_finish(int k, bool renormalize, int lane, 
     }
 #pragma unroll
     for (int stride = 16; stride > 0; stride >>= 1) stage(stride, false);
+    const bool valid = iv & 1;
+    const int idx = iv >> 1;
     float w = valid ? key : 0.0f;
     if (renormalize) {
         int p2 = 1;

@@ -104,6 +104,14 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* map, int c
         : "memory");
 }
 
+// Tiled 3-D tensor prefetch of one box into L2 (no shared-memory copy).
+__device__ __forceinline__ void tma_prefetch_3d(const void* map, int c0, int c1, int c2) {
+    asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(c0), "r"(c1), "r"(c2)
+                 : "memory");
+}
+
 // Packed pairs of fp32 (two IEEE round-to-nearest operations per instruction).
 __device__ __forceinline__ uint64_t pack_f32x2(float lo, float hi) {
     uint64_t d;
