@@ -29,8 +29,8 @@
 //          W13, the down tile's are 256 rows of W2;
 //   warp 0 loads each K block of 128 bytes (A 128 rows, B 256 rows) with
 //          SWIZZLE_128B tensor-map copies (no multicast) into a 4-stage ring,
-//          and stages the tile's activation and weight scales into shared
-//          memory with cp.async;
+//          and stages each tile's activation and weight scales into shared
+//          memory with cp.async early in the previous tile;
 //   warp 1 owns 512 TMEM columns (two fp32 accumulators of 256 columns) and
 //          issues, per K block, four MMAs into one of them;
 //   warps 2-17 load that accumulator (warp w reads lanes 32 (w % 4) ..: the
@@ -232,20 +232,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
         // ---------------- producer: TMA ring and tile scales ----------------
         const uint64_t pol_a = policy_evict_last();
         const uint64_t pol_b = policy_evict_first();
-        uint32_t c = 0;  // K blocks issued
-        int it = 0;
-        bool ok = true;
-        for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++it) {
+        // Scales of tile t (the it-th of this CTA) into slot it & 1: the
+        // activation scales as [kb][row] (kb-major copies, so the lanes of one
+        // copy write 32 consecutive rows: distinct banks) and the tile's two
+        // weight scale rows; completes on the slot's full barrier.
+        auto stage_scales = [&](int t, int it) -> bool {
             const TcTile x = tc_tile(t, nt, width, E, s_tiles, s_rows);
             const int slot = it & 1;
-            if (!warp_wait(bar(kBarSEmpty + slot), ((it >> 1) & 1) ^ 1, timeout_flag)) {
-                ok = false;
-                break;
-            }
-            // activation scales [kb][row] and the tile's two weight scale rows
+            if (!warp_wait(bar(kBarSEmpty + slot), ((it >> 1) & 1) ^ 1, timeout_flag)) return false;
             const uint32_t sc_addr = sbase + kOffScales + slot * kScaleSlot;
             for (int i = lane; i < kTcM * KB; i += 32) {
-                const int r = i / KB, kb = i - r * KB;
+                const int kb = i / kTcM, r = i - kb * kTcM;
                 cp4(sc_addr + 4u * (kb * kTcM + r), a.a_scale + (x.row0 + r) * KB + kb);
             }
             const float* bs = a.b_scale + x.e * a.b_scale_slot_stride;
@@ -257,6 +254,18 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                     bs + (which ? nb1 : nb0) * a.b_scale_row_stride + kb);
             }
             cp_async_arrive_noinc(bar(kBarSFull + slot));
+            return true;
+        };
+        uint32_t c = 0;  // K blocks issued
+        int it = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++it) {
+            const TcTile x = tc_tile(t, nt, width, E, s_tiles, s_rows);
+            // this tile's scales were staged during the previous tile (all but the first)
+            if (it == 0 && !stage_scales(t, 0)) {
+                ok = false;
+                break;
+            }
             for (int kb = 0; kb < KB; ++kb, ++c) {
                 const int s = c % kTcStages;
                 if (!warp_wait(bar(kBarEmpty + s), ((c / kTcStages) & 1) ^ 1, timeout_flag) || warp_aborted(misc)) {
@@ -276,6 +285,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                     }
                 }
                 __syncwarp();
+                // the next tile's scales, halfway through this one (its slot was
+                // released when the tile before this one left the K loop)
+                if (kb == KB / 2 && t + static_cast<int>(gridDim.x) < tiles &&
+                    !stage_scales(t + gridDim.x, it + 1)) {
+                    ok = false;
+                    break;
+                }
             }
         }
         if (!ok) misc[1] = 1;
