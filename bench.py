@@ -646,6 +646,13 @@ def run_prefill(args) -> None:
         print(json.dumps(line))
 
 
+# ---------------------------------------------------------------------------
+# config 4: expert-parallel decode of 256 tokens, and the offload variant
+# ---------------------------------------------------------------------------
+EP_TOKENS = 256
+EP_CHUNK = 16          # experts generated per seed, so every G sees the same banks
+
+
 def _dist_setup():
     import torch
     import torch.distributed as dist
