@@ -502,6 +502,9 @@ int prepare_moe_layer(const DramaB200Fp8Bank* bank, const void* gate, const void
         b.w13_slot_stride % 16 || b.w2_slot_stride % 16)
         return fail("FP8 weight rows and the router weight must start on 16-byte boundaries");
     if (next_gate && !aligned16(next_gate)) return fail("next router weight must be 16-byte aligned");
+    if (!aligned16(hidden_in) || !aligned16(hidden_out) || (normed_out && !aligned16(normed_out)) ||
+        (moe_out && !aligned16(moe_out)))
+        return fail("hidden, normed and moe rows must start on 16-byte boundaries");
     const size_t hb = static_cast<size_t>(tokens) * H * 2;
     if (overlaps(hidden_out, hb, hidden_in, hb)) return fail("hidden_out must not overlap hidden_in");
     if (tokens == 0) return 1;

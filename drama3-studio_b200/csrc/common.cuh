@@ -96,6 +96,16 @@ __device__ __forceinline__ void grid_launch_dependents() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// Atomic add with acquire-release semantics at GPU scope (the pattern of a
+// split-K semaphore): after a CTA barrier the release covers every write the
+// CTA made before it, and reads that follow the next CTA barrier are ordered
+// after the acquire.
+__device__ __forceinline__ int atomic_add_acq_rel_gpu(int* p, int v) {
+    int old;
+    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
 // Streaming 16-byte load of immutable expert weights: no L1 allocation and
 // first-out in L2, so the weight stream does not evict activations or the
 // down-projection slabs prefetched into L2.

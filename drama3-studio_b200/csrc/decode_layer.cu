@@ -25,10 +25,12 @@
 //   3. multiplies rows [r H/4, (r+1) H/4) of the down projection, restricted
 //      to the unit's intermediate columns (loaded with cp.async while steps 1
 //      and 2 run), with those values: a partial down projection;
-//   4. stores the fp32 partial and takes an arrival ticket; the last CTA of
-//      quarter r to arrive (no waiting) sums, for every row of the quarter,
-//      each slot's parts in part order, rounds, weights, adds the slots in slot
-//      order and the residual, and resets the ticket.
+//   4. stores the fp32 partial and takes an arrival ticket (one acquire-
+//      release atomic per CTA); the last CTA of quarter r to arrive (no
+//      waiting) copies every unit's partial of the quarter into shared memory
+//      and sums, for every row, each slot's parts in part order, rounds,
+//      weights, adds the slots in slot order and the residual, and resets the
+//      ticket.
 // Every expert weight byte is read once, by ~128 SMs at once, and the layer
 // needs no second launch. Before waiting for the previous layer
 // (programmatic dependent launch) each CTA pulls its share of the router rows
@@ -55,6 +57,7 @@ constexpr int kDlConsumers = kDlWarps * 32;
 constexpr int kDlMaxTiles = 16;                  // intermediate tiles per unit
 constexpr int kDlMaxSmem = 230400;               // dynamic shared memory per CTA (opt-in 232448 less static)
 constexpr int kDlMaxHidden = 2048;
+constexpr int kDlCombineLoads = 16;              // shared-memory loads in flight per combine thread
 
 // Dynamic shared memory of one CTA, from a 1024-byte aligned base (the
 // 128-byte swizzle of the TMA stages repeats every 1024 bytes). The ring and
@@ -297,15 +300,21 @@ __global__ void __launch_bounds__(kDlThreads, 1) decode_layer_kernel(const __gri
 
     // Routing (softmax -> top-k -> renormalise, torch's order): warp 0 takes
     // the softmax; the consumer threads rank every probability (2 threads per
-    // expert, each counting over half the row); warp 0 puts the k winners in
-    // the order of torch's gatherTopK and sorts them with torch's network,
-    // while warps 1..7 make the f16 copy of this quarter of the normalised
-    // row, scaled by 2^-e with e from the whole row.
+    // expert, each counting over half the row); warp 0 takes the k winners in
+    // rank order when no two of them are equal, else puts them in the order
+    // of torch's gatherTopK and sorts them with torch's network, while warps
+    // 1..7 make the f16 copy of this quarter of the normalised row, scaled by
+    // 2^-e with e from the whole row.
     const int E4 = (E + 3) & ~3;
     if (warp == 0) {
         route_softmax<LANES, ITERS>([&](int i) { return s_logit[i]; }, E, lane, s_logit);
     } else if (warp == 1 && lane < E4 - E) {
         s_logit[E + lane] = -1.0f;
+    } else if (warp == 2) {
+        // valid ids in every rank slot: with NaN probabilities no expert
+        // claims some ranks, and their slots keep these
+        s_rkey[lane] = 0.0f;
+        s_ridx[lane] = lane < E ? lane : 0;
     }
     __syncthreads();
     if (warp < kDlWarps) {
@@ -336,27 +345,36 @@ __global__ void __launch_bounds__(kDlThreads, 1) decode_layer_kernel(const __gri
     }
     __syncthreads();
     if (warp == 0) {
-        // gatherTopK order: values above the k-th in index order, then the
-        // ones equal to it in index order
-        const float kth = s_rkey[k - 1];
         const float v = lane < k ? s_rkey[lane] : -1.0f;
         const int ix = lane < k ? s_ridx[lane] : 0x7fffffff;
-        const bool gt = lane < k && v > kth;
-        const unsigned gmask = __ballot_sync(0xffffffffu, gt);
-        int before = 0;
-        for (int m = 0; m < k; ++m) {
-            const int im = __shfl_sync(0xffffffffu, ix, m);
-            before += (((gmask >> m) & 1u) == static_cast<unsigned>(gt)) && im < ix;
-        }
-        if (lane < k) {
-            const int pos = gt ? before : __popc(gmask) + before;
-            s_key[pos] = v;
-            s_idx[pos] = ix;
-        }
-        __syncwarp();
         int idx = 0;
         float wr = 0.0f;
-        route_finish(k, true, lane, s_key, s_idx, idx, wr);
+        // With no two of the k winners equal, torch's sorted order is their
+        // rank order (value descending) and the network below is the identity.
+        const unsigned kmask = k < 32 ? (1u << k) - 1u : 0xffffffffu;
+        const unsigned same = __match_any_sync(0xffffffffu, __float_as_uint(v)) & kmask & ~(1u << lane);
+        if (!__any_sync(0xffffffffu, lane < k && same != 0u)) {
+            idx = ix;
+            wr = route_weight(k, true, lane, v, lane < k);
+        } else {
+            // gatherTopK order: values above the k-th in index order, then the
+            // ones equal to it in index order; then torch's sorting network
+            const float kth = s_rkey[k - 1];
+            const bool gt = lane < k && v > kth;
+            const unsigned gmask = __ballot_sync(0xffffffffu, gt);
+            int before = 0;
+            for (int m = 0; m < k; ++m) {
+                const int im = __shfl_sync(0xffffffffu, ix, m);
+                before += (((gmask >> m) & 1u) == static_cast<unsigned>(gt)) && im < ix;
+            }
+            if (lane < k) {
+                const int pos = gt ? before : __popc(gmask) + before;
+                s_key[pos] = v;
+                s_idx[pos] = ix;
+            }
+            __syncwarp();
+            route_finish(k, true, lane, s_key, s_idx, idx, wr);
+        }
         const __nv_bfloat16 wb = __float2bfloat16_rn(wr);
         if (lane < k) {
             s_ids[lane] = idx;
@@ -645,17 +663,19 @@ __global__ void __launch_bounds__(kDlThreads, 1) decode_layer_kernel(const __gri
                 }
             }
         }
-        __threadfence();
+        // Ticket: the CTA barrier orders every thread's partial stores before
+        // thread 0's release, and its acquire orders the last arriver's reads
+        // of the other units' partials (after the next barrier).
         named_barrier(1, kDlConsumers);
-        if (tid == 0) {
-            const int old = atomicAdd(a.tickets + r, 1);
-            s_last = old == units - 1;
-        }
+        if (tid == 0) s_last = atomic_add_acq_rel_gpu(a.tickets + r, 1) == units - 1;
         named_barrier(1, kDlConsumers);
         if (s_last) {
-            // Last CTA of quarter r: for each row, each slot's parts in part
-            // order, rounded, weighted, slots added in slot order, residual.
-            __threadfence();
+            // Last CTA of quarter r: every unit's partial of the quarter into
+            // shared memory (unit u = j P + p at u HQ), then for each row each
+            // slot's parts in part order, rounded, weighted, slots added in
+            // slot order, and the residual. A thread owns two adjacent rows
+            // and walks the units in slot-then-part order, kDlCombineLoads
+            // 8-byte loads in flight at a time.
             if (tid == 0) a.tickets[r] = 0;
             for (int item = tid; item < units * (HQ / 4); item += kDlConsumers) {
                 const int u = item / (HQ / 4), c = item - u * (HQ / 4);
@@ -666,43 +686,39 @@ __global__ void __launch_bounds__(kDlThreads, 1) decode_layer_kernel(const __gri
             cp_commit();
             cp_wait<0>();
             named_barrier(1, kDlConsumers);
-            const float* sp = reinterpret_cast<const float*>(base);
-            for (int n = tid; n < HQ; n += 2 * kDlConsumers) {
-                const int n1 = n + kDlConsumers < HQ ? n + kDlConsumers : n;
-                float y0 = 0.0f, y1 = 0.0f;
-                for (int j = 0; j < k; ++j) {
-                    const float* pj = sp + j * P * HQ;
-                    float s0 = 0.0f, s1 = 0.0f;
-                    int p = 0;
-                    for (; p + 4 <= P; p += 4) {
-                        const float a0 = pj[p * HQ + n], a1 = pj[(p + 1) * HQ + n];
-                        const float a2 = pj[(p + 2) * HQ + n], a3 = pj[(p + 3) * HQ + n];
-                        const float b0 = pj[p * HQ + n1], b1 = pj[(p + 1) * HQ + n1];
-                        const float b2 = pj[(p + 2) * HQ + n1], b3 = pj[(p + 3) * HQ + n1];
-                        s0 += a0;
-                        s1 += b0;
-                        s0 += a1;
-                        s1 += b1;
-                        s0 += a2;
-                        s1 += b2;
-                        s0 += a3;
-                        s1 += b3;
-                    }
-                    for (; p < P; ++p) {
-                        s0 += pj[p * HQ + n];
-                        s1 += pj[p * HQ + n1];
-                    }
-                    y0 = __fadd_rn(y0, __fmul_rn(bf16_round(s0), s_w[j]));
-                    y1 = __fadd_rn(y1, __fmul_rn(bf16_round(s1), s_w[j]));
-                }
+            const float2* sp = reinterpret_cast<const float2*>(base);
+            for (int c2 = tid; c2 < HQ / 2; c2 += kDlConsumers) {
+                float s0 = 0.0f, s1 = 0.0f, y0 = 0.0f, y1 = 0.0f;
+                int j = 0, p = 0;
+                for (int f0 = 0; f0 < units; f0 += kDlCombineLoads) {
+                    float2 v[kDlCombineLoads];
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    if (h == 1 && n1 == n) break;
-                    const int row = r * HQ + (h ? n1 : n);
-                    const __nv_bfloat16 moe = __float2bfloat16_rn(h ? y1 : y0);
-                    if (A.moe_out) A.moe_out[row] = moe;
-                    A.hidden_out[row] = __float2bfloat16_rn(__bfloat162float(s_hin[row]) + __bfloat162float(moe));
+                    for (int f = 0; f < kDlCombineLoads; ++f)
+                        if (f0 + f < units) v[f] = sp[(f0 + f) * (HQ / 2) + c2];
+#pragma unroll
+                    for (int f = 0; f < kDlCombineLoads; ++f) {
+                        if (f0 + f < units) {
+                            s0 += v[f].x;
+                            s1 += v[f].y;
+                            if (++p == P) {
+                                const float wj = s_w[j];
+                                y0 = __fadd_rn(y0, __fmul_rn(bf16_round(s0), wj));
+                                y1 = __fadd_rn(y1, __fmul_rn(bf16_round(s1), wj));
+                                s0 = s1 = 0.0f;
+                                p = 0;
+                                ++j;
+                            }
+                        }
+                    }
                 }
+                const int row = r * HQ + 2 * c2;
+                const uint32_t hin = *reinterpret_cast<const uint32_t*>(s_hin + row);
+                const __nv_bfloat16 m0 = __float2bfloat16_rn(y0), m1 = __float2bfloat16_rn(y1);
+                const __nv_bfloat16 o0 = __float2bfloat16_rn(__uint_as_float(hin << 16) + __bfloat162float(m0));
+                const __nv_bfloat16 o1 =
+                    __float2bfloat16_rn(__uint_as_float(hin & 0xffff0000u) + __bfloat162float(m1));
+                if (A.moe_out) *reinterpret_cast<__nv_bfloat162*>(A.moe_out + row) = __halves2bfloat162(m0, m1);
+                *reinterpret_cast<__nv_bfloat162*>(A.hidden_out + row) = __halves2bfloat162(o0, o1);
             }
         }
     }

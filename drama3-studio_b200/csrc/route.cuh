@@ -6,6 +6,22 @@
 
 namespace drama {
 
+// Weight of the route in this lane once lanes 0..k-1 hold the k routes in
+// their final order (`key` = probability, `valid` = a real route): the
+// probability, divided when renormalising by the tree sum of the k keys.
+__device__ __forceinline__ float route_weight(int k, bool renormalize, int lane, float key, bool valid) {
+    constexpr unsigned kFull = 0xffffffffu;
+    float w = valid ? key : 0.0f;
+    if (renormalize) {
+        int p2 = 1;
+        while (p2 < k) p2 <<= 1;
+        float tsum = lane < k ? key : 0.0f;
+        for (int off = 1; off < p2; off <<= 1) tsum = tsum + __shfl_down_sync(kFull, tsum, off);
+        w = w / __shfl_sync(kFull, tsum, 0);
+    }
+    return w;
+}
+
 // Sort + renormalise the k candidates that the selection left in s_key /
 // s_idx (gatherTopK order) exactly as torch's CUDA topk(sorted=True) and the
 // renormalisation do. Called by a whole warp; lanes 0..k-1 get the result.
@@ -36,18 +52,8 @@ __device__ __forceinline__ void route_finish(int k, bool renormalize, int lane, 
     }
 #pragma unroll
     for (int stride = 16; stride > 0; stride >>= 1) stage(stride, false);
-    const bool valid = iv & 1;
-    const int idx = iv >> 1;
-    float w = valid ? key : 0.0f;
-    if (renormalize) {
-        int p2 = 1;
-        while (p2 < k) p2 <<= 1;
-        float tsum = lane < k ? key : 0.0f;
-        for (int off = 1; off < p2; off <<= 1) tsum = tsum + __shfl_down_sync(kFull, tsum, off);
-        w = w / __shfl_sync(kFull, tsum, 0);
-    }
-    out_idx = idx;
-    out_w = w;
+    out_idx = iv >> 1;
+    out_w = route_weight(k, renormalize, lane, key, iv & 1);
 }
 
 // LANES lanes x ITERS values cover next_pow2(E). `load(idx)` returns the fp32

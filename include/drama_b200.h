@@ -310,6 +310,7 @@ DRAMA_B200_API int drama_b200_shared_expert(const DramaB200SharedExpert* mlp, co
  * for the following layer. ids_out (int64 [tokens, top_k]), weights_out
  * (bf16), normed_out (bf16 [tokens, H]) and moe_out (bf16 [tokens, H], the
  * combined expert output before the residual add) are optional traces.
+ * hidden_in, hidden_out, normed_out and moe_out start on 16-byte boundaries.
  * tokens * top_k <= 256, H % 256 == 0, experts = bank->slots <= 1024.
  * ------------------------------------------------------------------------- */
 DRAMA_B200_API size_t drama_b200_moe_layer_workspace_bytes(int64_t tokens, int top_k, int hidden,
@@ -338,7 +339,8 @@ DRAMA_B200_API int drama_b200_moe_layer_launches(int64_t tokens, int top_k, int 
  * (hidden_out = bf16(hidden_in + experts)), so its routes are the reference's
  * bit for bit whatever RMSNorm and GEMV order produced the inputs.
  * tokens == 1; hidden % 512 == 0 up to 2048; intermediate % 16 == 0;
- * top_k <= 16. Workspace: drama_b200_moe_layer_workspace_bytes. */
+ * top_k <= 16; normed, logits, hidden_in, hidden_out and moe_out start on
+ * 16-byte boundaries. Workspace: drama_b200_moe_layer_workspace_bytes. */
 DRAMA_B200_API int drama_b200_fp8_moe_layer_logits(const DramaB200Fp8Bank* bank, const void* normed,
                                                    const void* logits, const void* hidden_in, void* hidden_out,
                                                    int64_t tokens, int top_k, int64_t* ids_out,
