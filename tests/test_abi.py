@@ -69,6 +69,30 @@ def test_validation_errors_before_any_launch(lib):
     assert b"at most" in d.drama_b200_error()
 
 
+def test_moe_layer_rejects_unaligned_rows(lib):
+    """The fused layer reads and writes hidden rows 16 bytes at a time; an
+    unaligned row is refused before any launch."""
+    from drama_b200._lib import Fp8Bank
+
+    d = lib.dll
+    buf = (ctypes.c_uint8 * 512)()
+    a = (ctypes.addressof(buf) + 255) & ~255  # 256-byte aligned stand-in pointers (never dereferenced)
+    bank = Fp8Bank()
+    bank.w13 = bank.w13_scale = bank.w2 = bank.w2_scale = a
+    bank.w13_row_stride = bank.w2_row_stride = bank.w13_slot_stride = bank.w2_slot_stride = 2048
+    bank.hidden, bank.intermediate, bank.slots = 2048, 768, 128
+
+    def call(hidden_in, hidden_out, moe_out=None):
+        return d.drama_b200_fp8_moe_layer(ctypes.byref(bank), ctypes.c_void_p(a), None, ctypes.c_void_p(a),
+                                          ctypes.c_float(1e-6), ctypes.c_void_p(hidden_in),
+                                          ctypes.c_void_p(hidden_out), ctypes.c_int64(1), 8, None, None, None,
+                                          ctypes.c_void_p(moe_out), ctypes.c_void_p(a), ctypes.c_size_t(0), None)
+
+    for args in ((a + 2, a + 256), (a, a + 258), (a, a + 256, a + 8)):
+        assert call(*args) == -1
+        assert b"16-byte" in d.drama_b200_error()
+
+
 def test_product_code_never_imports_the_oracle():
     for path in (REPO / "drama3-studio_b200").rglob("*.py"):
         text = path.read_text()
