@@ -57,7 +57,6 @@ constexpr int kDlConsumers = kDlWarps * 32;
 constexpr int kDlMaxTiles = 16;                  // intermediate tiles per unit
 constexpr int kDlMaxSmem = 230400;               // dynamic shared memory per CTA (opt-in 232448 less static)
 constexpr int kDlMaxHidden = 2048;
-constexpr int kDlCombineLoads = 16;              // shared-memory loads in flight per combine thread
 
 // Dynamic shared memory of one CTA, from a 1024-byte aligned base (the
 // 128-byte swizzle of the TMA stages repeats every 1024 bytes). The ring and
@@ -112,12 +111,60 @@ __host__ __device__ inline DlLayout dl_layout(int H, int E, int nkt, int stages,
 
 __device__ __forceinline__ float bf16_round(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
+// The last arriver's sums for two adjacent rows (column pair c2 of the
+// quarter): each slot's PP parts in part order (unit j PP + p at row
+// (j PP + p) hq2 of `sp`, float2 columns), rounded to bf16, times the route
+// weight, added in slot order. PP is a template argument so that a slot's
+// loads issue together and the slot loop unrolls (runtime part counts make
+// the loop several times slower); PP = 0 is the generic loop.
+template <int PP>
+__device__ __forceinline__ void dl_slot_sums(const float2* sp, int c2, int hq2, int k, int parts, const float* s_w,
+                                             float& y0, float& y1) {
+    if constexpr (PP > 0) {
+#pragma unroll 4
+        for (int j = 0; j < k; ++j) {
+            float2 v[PP];
+#pragma unroll
+            for (int p = 0; p < PP; ++p) v[p] = sp[(j * PP + p) * hq2 + c2];
+            float s0 = 0.0f, s1 = 0.0f;
+#pragma unroll
+            for (int p = 0; p < PP; ++p) {
+                s0 += v[p].x;
+                s1 += v[p].y;
+            }
+            const float wj = s_w[j];
+            y0 = __fadd_rn(y0, __fmul_rn(bf16_round(s0), wj));
+            y1 = __fadd_rn(y1, __fmul_rn(bf16_round(s1), wj));
+        }
+    } else {
+        for (int j = 0; j < k; ++j) {
+            float s0 = 0.0f, s1 = 0.0f;
+            for (int p = 0; p < parts; ++p) {
+                const float2 v = sp[(j * parts + p) * hq2 + c2];
+                s0 += v.x;
+                s1 += v.y;
+            }
+            const float wj = s_w[j];
+            y0 = __fadd_rn(y0, __fmul_rn(bf16_round(s0), wj));
+            y1 = __fadd_rn(y1, __fmul_rn(bf16_round(s1), wj));
+        }
+    }
+}
+
 // LANES x ITERS lanes and values per lane of the softmax cover the expert
 // count; one instantiation per expert-count class keeps a single softmax in
 // the kernel's code. The kernel runs once per layer, straight through, so its
 // code must fit the SM's instruction cache (about 128 KB on the B200) to stay
 // resident from one layer's launch to the next.
-template <int LANES, int ITERS>
+//
+// HC > 0 fixes the hidden size, NKTC > 0 the tiles of every unit (all stages
+// resident) and PC > 0 the units per route slot: the shape-dependent loops
+// then have compile-time trip counts and unroll, which makes the serial steps
+// (the down projection and the combine above all) several times faster than
+// with runtime bounds. The host picks such an instantiation only for a shape
+// it was made for (decode_layer_kernel_fixed); the arithmetic and its order
+// are the generic kernel's.
+template <int LANES, int ITERS, int HC, int NKTC, int PC>
 __global__ void __launch_bounds__(kDlThreads, 1) decode_layer_kernel(const __grid_constant__ DecodeLayerArgs a) {
     extern __shared__ __align__(1024) uint8_t dl_smem_raw[];
     __shared__ float s_red[kDlWarps];
@@ -129,16 +176,16 @@ __global__ void __launch_bounds__(kDlThreads, 1) decode_layer_kernel(const __gri
     __shared__ int s_last;
 
     const RoutedLayerArgs& A = a.layer;
-    const int H = A.H, I = A.I, E = A.E, k = A.k;
-    const DlLayout L = dl_layout(H, E, a.nkt, a.stages, a.overlay);
+    const int H = HC > 0 ? HC : A.H, I = A.I, E = A.E, k = A.k;
+    const DlLayout L = NKTC > 0 ? dl_layout(H, E, NKTC, NKTC, 1) : dl_layout(H, E, a.nkt, a.stages, a.overlay);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
     cg::cluster_group cluster = cg::this_cluster();
     const int r = static_cast<int>(cluster.block_rank());
     const int unit = static_cast<int>(blockIdx.x) / kDlCluster;
     const int units = static_cast<int>(gridDim.x) / kDlCluster;
-    const int P = a.parts, TPI = I / 16;
+    const int P = PC > 0 ? PC : a.parts, TPI = I / 16;
     const int slot_j = unit / P, part = unit % P;
-    const int tile0 = TPI * part / P, nkt = TPI * (part + 1) / P - tile0;
+    const int tile0 = TPI * part / P, nkt = NKTC > 0 ? NKTC : TPI * (part + 1) / P - tile0;
     const int HQ = L.hq, KBQ = L.kbq;
     const bool fused = a.logits_in == nullptr;
     int32_t* status = A.ws.status + 3;
@@ -607,58 +654,105 @@ __global__ void __launch_bounds__(kDlThreads, 1) decode_layer_kernel(const __gri
         const uint8_t* h16s = reinterpret_cast<const uint8_t*>(s_h16);
         const float hscale = s_hscale;
         float* part = a.part + static_cast<int64_t>(unit) * H + r * HQ;
-        const int NT = HQ / 16;
-        for (int i0 = 0; warp + kDlWarps * i0 < NT; i0 += 4) {
-            int nt[4];
-            bool ok[4];
-            float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};
+        if constexpr (NKTC > 0) {
+            // Fixed shape: warp w takes row tiles w + 8u of the quarter; the
+            // unit's tiles span at most two scale blocks, the first cb tiles
+            // in block blk0 (the host checks NKTC - cb <= 8).
+            constexpr int kU = HC / kDlCluster / 16 / kDlWarps;
+            const int cb = 8 - (tile0 & 7);
+            const uint8_t* rowb[kU];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                nt[u] = warp + kDlWarps * (i0 + u);
-                ok[u] = nt[u] < NT;
-            }
-            // row n of a column box at (n / rows_box) * rows_box * 64 + (n % rows_box) * 64
-            const uint8_t* rowb[4];
+            for (int u = 0; u < kU; ++u) rowb[u] = w2s + ((warp + kDlWarps * u) * 16 + g) * 64 + 4 * t;
+            float dA[kU][4], dB[kU][4];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const int n = (ok[u] ? nt[u] : warp) * 16 + g;
-                rowb[u] = w2s + n * 64 + 4 * t;
-            }
-            for (int c = 0; c < nkt;) {
-                const int blk = (tile0 + c) >> 3;
-                const int cend = min(nkt, (blk + 1) * 8 - tile0);
-                float d[4][4];
+            for (int u = 0; u < kU; ++u)
 #pragma unroll
-                for (int u = 0; u < 4; ++u) d[u][0] = d[u][1] = d[u][2] = d[u][3] = 0.0f;
-                for (; c < cend; ++c) {
-                    const uint2 hb = lds64(h16s + c * 32 + 8 * t);
-                    const uint32_t off = static_cast<uint32_t>((c >> 2) * HQ * 64) +
-                                         (static_cast<uint32_t>((c & 3) ^ ((g >> 1) & 3)) << 4);
+                for (int e = 0; e < 4; ++e) dA[u][e] = dB[u][e] = 0.0f;
 #pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        if (ok[u]) {
-                            uint32_t Af[4];
-                            e4m3x4_to_f16x2x2(lds32(rowb[u] + off), Af[0], Af[2]);
-                            e4m3x4_to_f16x2x2(lds32(rowb[u] + off + 8 * 64), Af[1], Af[3]);
-                            mma_f16_16816(d[u], Af, hb.x, hb.y);
-                        }
-                    }
-                }
+            for (int c = 0; c < NKTC; ++c) {
+                const uint2 hb = lds64(h16s + c * 32 + 8 * t);
+                const uint32_t off = static_cast<uint32_t>((c >> 2) * (HC / kDlCluster) * 64) +
+                                     (static_cast<uint32_t>((c & 3) ^ ((g >> 1) & 3)) << 4);
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    if (ok[u]) {
-                        const float scale = s_s2[(blk - blk0) * (HQ / 128) + ((nt[u] * 16) >> 7)] * hscale;
-                        acc0[u] = fmaf(d[u][0], scale, acc0[u]);
-                        acc1[u] = fmaf(d[u][2], scale, acc1[u]);
-                    }
+                for (int u = 0; u < kU; ++u) {
+                    uint32_t Af[4];
+                    e4m3x4_to_f16x2x2(lds32(rowb[u] + off), Af[0], Af[2]);
+                    e4m3x4_to_f16x2x2(lds32(rowb[u] + off + 8 * 64), Af[1], Af[3]);
+                    if (c < cb)
+                        mma_f16_16816(dA[u], Af, hb.x, hb.y);
+                    else
+                        mma_f16_16816(dB[u], Af, hb.x, hb.y);
                 }
             }
             if (t == 0) {
 #pragma unroll
+                for (int u = 0; u < kU; ++u) {
+                    const int nt = warp + kDlWarps * u;
+                    const float sa = s_s2[(nt * 16) >> 7] * hscale;
+                    float a0 = fmaf(dA[u][0], sa, 0.0f), a1 = fmaf(dA[u][2], sa, 0.0f);
+                    if (NKTC > cb) {
+                        const float sb = s_s2[(HC / kDlCluster / 128) + ((nt * 16) >> 7)] * hscale;
+                        a0 = fmaf(dB[u][0], sb, a0);
+                        a1 = fmaf(dB[u][2], sb, a1);
+                    }
+                    __stcg(part + nt * 16 + g, a0);
+                    __stcg(part + nt * 16 + g + 8, a1);
+                }
+            }
+        } else {
+            const int NT = HQ / 16;
+            for (int i0 = 0; warp + kDlWarps * i0 < NT; i0 += 4) {
+                int nt[4];
+                bool ok[4];
+                float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};
+    #pragma unroll
                 for (int u = 0; u < 4; ++u) {
-                    if (ok[u]) {
-                        __stcg(part + nt[u] * 16 + g, acc0[u]);
-                        __stcg(part + nt[u] * 16 + g + 8, acc1[u]);
+                    nt[u] = warp + kDlWarps * (i0 + u);
+                    ok[u] = nt[u] < NT;
+                }
+                // row n of a column box at (n / rows_box) * rows_box * 64 + (n % rows_box) * 64
+                const uint8_t* rowb[4];
+    #pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int n = (ok[u] ? nt[u] : warp) * 16 + g;
+                    rowb[u] = w2s + n * 64 + 4 * t;
+                }
+                for (int c = 0; c < nkt;) {
+                    const int blk = (tile0 + c) >> 3;
+                    const int cend = min(nkt, (blk + 1) * 8 - tile0);
+                    float d[4][4];
+    #pragma unroll
+                    for (int u = 0; u < 4; ++u) d[u][0] = d[u][1] = d[u][2] = d[u][3] = 0.0f;
+                    for (; c < cend; ++c) {
+                        const uint2 hb = lds64(h16s + c * 32 + 8 * t);
+                        const uint32_t off = static_cast<uint32_t>((c >> 2) * HQ * 64) +
+                                             (static_cast<uint32_t>((c & 3) ^ ((g >> 1) & 3)) << 4);
+    #pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            if (ok[u]) {
+                                uint32_t Af[4];
+                                e4m3x4_to_f16x2x2(lds32(rowb[u] + off), Af[0], Af[2]);
+                                e4m3x4_to_f16x2x2(lds32(rowb[u] + off + 8 * 64), Af[1], Af[3]);
+                                mma_f16_16816(d[u], Af, hb.x, hb.y);
+                            }
+                        }
+                    }
+    #pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        if (ok[u]) {
+                            const float scale = s_s2[(blk - blk0) * (HQ / 128) + ((nt[u] * 16) >> 7)] * hscale;
+                            acc0[u] = fmaf(d[u][0], scale, acc0[u]);
+                            acc1[u] = fmaf(d[u][2], scale, acc1[u]);
+                        }
+                    }
+                }
+                if (t == 0) {
+    #pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        if (ok[u]) {
+                            __stcg(part + nt[u] * 16 + g, acc0[u]);
+                            __stcg(part + nt[u] * 16 + g + 8, acc1[u]);
+                        }
                     }
                 }
             }
@@ -673,9 +767,7 @@ __global__ void __launch_bounds__(kDlThreads, 1) decode_layer_kernel(const __gri
             // Last CTA of quarter r: every unit's partial of the quarter into
             // shared memory (unit u = j P + p at u HQ), then for each row each
             // slot's parts in part order, rounded, weighted, slots added in
-            // slot order, and the residual. A thread owns two adjacent rows
-            // and walks the units in slot-then-part order, kDlCombineLoads
-            // 8-byte loads in flight at a time.
+            // slot order, and the residual; a thread owns two adjacent rows.
             if (tid == 0) a.tickets[r] = 0;
             for (int item = tid; item < units * (HQ / 4); item += kDlConsumers) {
                 const int u = item / (HQ / 4), c = item - u * (HQ / 4);
@@ -688,29 +780,8 @@ __global__ void __launch_bounds__(kDlThreads, 1) decode_layer_kernel(const __gri
             named_barrier(1, kDlConsumers);
             const float2* sp = reinterpret_cast<const float2*>(base);
             for (int c2 = tid; c2 < HQ / 2; c2 += kDlConsumers) {
-                float s0 = 0.0f, s1 = 0.0f, y0 = 0.0f, y1 = 0.0f;
-                int j = 0, p = 0;
-                for (int f0 = 0; f0 < units; f0 += kDlCombineLoads) {
-                    float2 v[kDlCombineLoads];
-#pragma unroll
-                    for (int f = 0; f < kDlCombineLoads; ++f)
-                        if (f0 + f < units) v[f] = sp[(f0 + f) * (HQ / 2) + c2];
-#pragma unroll
-                    for (int f = 0; f < kDlCombineLoads; ++f) {
-                        if (f0 + f < units) {
-                            s0 += v[f].x;
-                            s1 += v[f].y;
-                            if (++p == P) {
-                                const float wj = s_w[j];
-                                y0 = __fadd_rn(y0, __fmul_rn(bf16_round(s0), wj));
-                                y1 = __fadd_rn(y1, __fmul_rn(bf16_round(s1), wj));
-                                s0 = s1 = 0.0f;
-                                p = 0;
-                                ++j;
-                            }
-                        }
-                    }
-                }
+                float y0 = 0.0f, y1 = 0.0f;
+                dl_slot_sums<PC>(sp, c2, HQ / 2, k, P, s_w, y0, y1);
                 const int row = r * HQ + 2 * c2;
                 const uint32_t hin = *reinterpret_cast<const uint32_t*>(s_hin + row);
                 const __nv_bfloat16 m0 = __float2bfloat16_rn(y0), m1 = __float2bfloat16_rn(y1);
@@ -788,17 +859,31 @@ DecodeLayerKernel decode_layer_kernel_for(int experts) {
     int p2 = 1;
     while (p2 < experts) p2 <<= 1;
     switch (p2) {
-        case 1: return decode_layer_kernel<1, 1>;
-        case 2: return decode_layer_kernel<2, 1>;
-        case 4: return decode_layer_kernel<4, 1>;
-        case 8: return decode_layer_kernel<8, 1>;
-        case 16: return decode_layer_kernel<16, 1>;
-        case 32: return decode_layer_kernel<32, 1>;
-        case 64: return decode_layer_kernel<32, 2>;
-        case 128: return decode_layer_kernel<32, 4>;
-        case 256: return decode_layer_kernel<32, 8>;
+        case 1: return decode_layer_kernel<1, 1, 0, 0, 0>;
+        case 2: return decode_layer_kernel<2, 1, 0, 0, 0>;
+        case 4: return decode_layer_kernel<4, 1, 0, 0, 0>;
+        case 8: return decode_layer_kernel<8, 1, 0, 0, 0>;
+        case 16: return decode_layer_kernel<16, 1, 0, 0, 0>;
+        case 32: return decode_layer_kernel<32, 1, 0, 0, 0>;
+        case 64: return decode_layer_kernel<32, 2, 0, 0, 0>;
+        case 128: return decode_layer_kernel<32, 4, 0, 0, 0>;
+        case 256: return decode_layer_kernel<32, 8, 0, 0, 0>;
         default: return nullptr;
     }
+}
+
+// The shape-specialised instantiation for a plan, or nullptr: hidden 2048
+// with 65..128 experts (the reference's configuration: intermediate 768,
+// top-8), four units per route slot of exactly 12 tiles each with all stages
+// resident, and every unit's tiles within two 128-wide scale blocks.
+DecodeLayerKernel decode_layer_kernel_fixed(int H, int I, int E, int parts, int nkt, int stages, int overlay) {
+    constexpr int kH = 2048, kNkt = 12, kParts = 4;
+    if (H != kH || E <= 64 || E > 128 || parts != kParts || nkt != kNkt || stages != kNkt || !overlay) return nullptr;
+    const int tpi = I / 16;
+    if (tpi != kParts * kNkt) return nullptr;
+    for (int p = 0; p < parts; ++p)
+        if (kNkt - (8 - ((tpi * p / parts) & 7)) > 8) return nullptr;
+    return decode_layer_kernel<32, 4, kH, kNkt, kParts>;
 }
 
 int decode_layer_clusters() {
@@ -806,9 +891,9 @@ int decode_layer_clusters() {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
     if (cached[dev]) return cached[dev];
-    for (int e = 1; e <= 256; e <<= 1) {
-        if (cudaFuncSetAttribute(decode_layer_kernel_for(e), cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 kDlMaxSmem) != cudaSuccess) {
+    for (int e = 1; e <= 512; e <<= 1) {
+        DecodeLayerKernel kern = e <= 256 ? decode_layer_kernel_for(e) : decode_layer_kernel<32, 4, 2048, 12, 4>;
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kDlMaxSmem) != cudaSuccess) {
             cudaGetLastError();
             return cached[dev] = -1;
         }
@@ -827,7 +912,7 @@ int decode_layer_clusters() {
     q.attrs = attr;
     q.numAttrs = 1;
     int clusters = 0;
-    if (cudaOccupancyMaxActiveClusters(&clusters, decode_layer_kernel<32, 4>, &q) != cudaSuccess || clusters < 1) {
+    if (cudaOccupancyMaxActiveClusters(&clusters, decode_layer_kernel<32, 4, 0, 0, 0>, &q) != cudaSuccess || clusters < 1) {
         cudaGetLastError();
         return cached[dev] = -1;
     }
@@ -888,7 +973,8 @@ cudaError_t decode_layer_launch(DecodeLayerArgs a, cudaStream_t s) {
     cfg.stream = s;
     cfg.attrs = attrs;
     cfg.numAttrs = 2;
-    return cudaLaunchKernelEx(&cfg, decode_layer_kernel_for(A.E), a);
+    DecodeLayerKernel kern = decode_layer_kernel_fixed(A.H, A.I, A.E, p.parts, p.nkt, p.stages, p.layout.overlay);
+    return cudaLaunchKernelEx(&cfg, kern ? kern : decode_layer_kernel_for(A.E), a);
 }
 
 }  // namespace drama
