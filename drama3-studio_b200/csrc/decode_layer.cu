@@ -95,7 +95,7 @@ __host__ __device__ inline DlLayout dl_layout(int H, int E, int nkt, int stages,
     take(L.region);
     L.w2 = overlay ? 0 : ring_bytes;
     L.hin = take(H * 2);
-    L.norm = take(H * 4);
+    L.norm = take(H * 2);
     L.x16 = take(L.hq * 2);
     L.logit = take((((E + 3) & ~3) + 4) * 4);
     L.cell = take(nkt * L.kbq * 32 * 4);
@@ -158,13 +158,14 @@ __device__ __forceinline__ void dl_slot_sums(const float2* sp, int c2, int hq2, 
 // resident from one layer's launch to the next.
 //
 // HC > 0 fixes the hidden size, NKTC > 0 the tiles of every unit (all stages
-// resident) and PC > 0 the units per route slot: the shape-dependent loops
+// resident), PC > 0 the units per route slot and EC > 0 the expert count:
+// the shape-dependent loops
 // then have compile-time trip counts and unroll, which makes the serial steps
 // (the down projection and the combine above all) several times faster than
 // with runtime bounds. The host picks such an instantiation only for a shape
 // it was made for (decode_layer_kernel_fixed); the arithmetic and its order
 // are the generic kernel's.
-template <int LANES, int ITERS, int HC, int NKTC, int PC>
+template <int LANES, int ITERS, int HC, int NKTC, int PC, int EC>
 __global__ void __launch_bounds__(kDlThreads, 1) decode_layer_kernel(const __grid_constant__ DecodeLayerArgs a) {
     extern __shared__ __align__(1024) uint8_t dl_smem_raw[];
     __shared__ float s_red[kDlWarps];
@@ -176,7 +177,7 @@ __global__ void __launch_bounds__(kDlThreads, 1) decode_layer_kernel(const __gri
     __shared__ int s_last;
 
     const RoutedLayerArgs& A = a.layer;
-    const int H = HC > 0 ? HC : A.H, I = A.I, E = A.E, k = A.k;
+    const int H = HC > 0 ? HC : A.H, I = A.I, E = EC > 0 ? EC : A.E, k = A.k;
     const DlLayout L = NKTC > 0 ? dl_layout(H, E, NKTC, NKTC, 1) : dl_layout(H, E, a.nkt, a.stages, a.overlay);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
     cg::cluster_group cluster = cg::this_cluster();
@@ -194,7 +195,7 @@ __global__ void __launch_bounds__(kDlThreads, 1) decode_layer_kernel(const __gri
     const uint32_t base_u32 = (raw_u32 + 1023u) & ~1023u;
     uint8_t* base = dl_smem_raw + (base_u32 - raw_u32);
     __nv_bfloat16* s_hin = reinterpret_cast<__nv_bfloat16*>(base + L.hin);
-    float* s_norm = reinterpret_cast<float*>(base + L.norm);
+    __nv_bfloat16* s_norm = reinterpret_cast<__nv_bfloat16*>(base + L.norm);  // the bf16 normalised row
     uint4* s_x16 = reinterpret_cast<uint4*>(base + L.x16);
     float* s_logit = reinterpret_cast<float*>(base + L.logit);
     float* s_cell = reinterpret_cast<float*>(base + L.cell);
@@ -277,14 +278,14 @@ __global__ void __launch_bounds__(kDlThreads, 1) decode_layer_kernel(const __gri
                 if (j < per) {
                     const int i = tid * per + j;
                     const __nv_bfloat16 y = __float2bfloat16_rn(__fmul_rn(__fmul_rn(v[j], inv), gam[j]));
-                    s_norm[i] = __bfloat162float(y);
+                    s_norm[i] = y;
                     if (blockIdx.x == 0 && A.normed_out) A.normed_out[i] = y;
                 }
             }
         } else {
             for (int i = tid; i < H; i += kDlConsumers) {
                 const __nv_bfloat16 y = __ldcg(a.normed_in + i);
-                s_norm[i] = __bfloat162float(y);
+                s_norm[i] = y;
                 s_hin[i] = __ldcg(A.hidden_in + i);
                 if (blockIdx.x == 0 && A.normed_out) A.normed_out[i] = y;
             }
@@ -314,14 +315,13 @@ __global__ void __launch_bounds__(kDlThreads, 1) decode_layer_kernel(const __gri
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
                 if (i < H / 256) {
-                    const float4 x0 = reinterpret_cast<const float4*>(s_norm + 256 * i + 8 * lane)[0];
-                    const float4 x1 = reinterpret_cast<const float4*>(s_norm + 256 * i + 8 * lane)[1];
-                    const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+                    const uint4 xq = lds128(s_norm + 256 * i + 8 * lane);
                     const uint4 g0 = lds128(rows[0] + 512 * i), g1 = lds128(rows[1] + 512 * i);
                     const uint4 g2 = lds128(rows[2] + 512 * i), g3 = lds128(rows[3] + 512 * i);
 #pragma unroll
                     for (int j = 0; j < 8; ++j) {
-                        const uint64_t xx = pack_f32x2(xv[j], xv[j]);
+                        const float xj = bf16_at(xq, j);
+                        const uint64_t xx = pack_f32x2(xj, xj);
                         acc01 = add_f32x2(acc01, mul_f32x2(xx, pack_f32x2(bf16_at(g0, j), bf16_at(g1, j))));
                         acc23 = add_f32x2(acc23, mul_f32x2(xx, pack_f32x2(bf16_at(g2, j), bf16_at(g3, j))));
                     }
@@ -434,7 +434,7 @@ __global__ void __launch_bounds__(kDlThreads, 1) decode_layer_kernel(const __gri
     } else if (warp < kDlWarps) {
         const int tw = tid - 32;
         float m = 0.0f;
-        for (int i = tw; i < H; i += kDlConsumers - 32) m = fmaxf(m, fabsf(s_norm[i]));
+        for (int i = tw; i < H; i += kDlConsumers - 32) m = fmaxf(m, fabsf(__bfloat162float(s_norm[i])));
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
         if (lane == 0) s_red[warp] = m;
@@ -446,9 +446,10 @@ __global__ void __launch_bounds__(kDlThreads, 1) decode_layer_kernel(const __gri
         const float inv = ldexpf(1.0f, -e);
         if (tw == 0) s_xscale = ldexpf(1.0f, e);
         for (int c = tw; c < HQ / 8; c += kDlConsumers - 32) {
-            const float4 p0 = reinterpret_cast<const float4*>(s_norm + r * HQ)[2 * c];
-            const float4 p1 = reinterpret_cast<const float4*>(s_norm + r * HQ)[2 * c + 1];
-            const float vv[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+            const uint4 q = lds128(s_norm + r * HQ + 8 * c);
+            float vv[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) vv[j] = bf16_at(q, j);
             s_x16[c] = pack8<0>(vv, inv);
         }
     }
@@ -859,31 +860,31 @@ DecodeLayerKernel decode_layer_kernel_for(int experts) {
     int p2 = 1;
     while (p2 < experts) p2 <<= 1;
     switch (p2) {
-        case 1: return decode_layer_kernel<1, 1, 0, 0, 0>;
-        case 2: return decode_layer_kernel<2, 1, 0, 0, 0>;
-        case 4: return decode_layer_kernel<4, 1, 0, 0, 0>;
-        case 8: return decode_layer_kernel<8, 1, 0, 0, 0>;
-        case 16: return decode_layer_kernel<16, 1, 0, 0, 0>;
-        case 32: return decode_layer_kernel<32, 1, 0, 0, 0>;
-        case 64: return decode_layer_kernel<32, 2, 0, 0, 0>;
-        case 128: return decode_layer_kernel<32, 4, 0, 0, 0>;
-        case 256: return decode_layer_kernel<32, 8, 0, 0, 0>;
+        case 1: return decode_layer_kernel<1, 1, 0, 0, 0, 0>;
+        case 2: return decode_layer_kernel<2, 1, 0, 0, 0, 0>;
+        case 4: return decode_layer_kernel<4, 1, 0, 0, 0, 0>;
+        case 8: return decode_layer_kernel<8, 1, 0, 0, 0, 0>;
+        case 16: return decode_layer_kernel<16, 1, 0, 0, 0, 0>;
+        case 32: return decode_layer_kernel<32, 1, 0, 0, 0, 0>;
+        case 64: return decode_layer_kernel<32, 2, 0, 0, 0, 0>;
+        case 128: return decode_layer_kernel<32, 4, 0, 0, 0, 0>;
+        case 256: return decode_layer_kernel<32, 8, 0, 0, 0, 0>;
         default: return nullptr;
     }
 }
 
 // The shape-specialised instantiation for a plan, or nullptr: hidden 2048
-// with 65..128 experts (the reference's configuration: intermediate 768,
-// top-8), four units per route slot of exactly 12 tiles each with all stages
+// with 128 experts (the reference's configuration: intermediate 768, top-8),
+// four units per route slot of exactly 12 tiles each with all stages
 // resident, and every unit's tiles within two 128-wide scale blocks.
 DecodeLayerKernel decode_layer_kernel_fixed(int H, int I, int E, int parts, int nkt, int stages, int overlay) {
-    constexpr int kH = 2048, kNkt = 12, kParts = 4;
-    if (H != kH || E <= 64 || E > 128 || parts != kParts || nkt != kNkt || stages != kNkt || !overlay) return nullptr;
+    constexpr int kH = 2048, kNkt = 12, kParts = 4, kE = 128;
+    if (H != kH || E != kE || parts != kParts || nkt != kNkt || stages != kNkt || !overlay) return nullptr;
     const int tpi = I / 16;
     if (tpi != kParts * kNkt) return nullptr;
     for (int p = 0; p < parts; ++p)
         if (kNkt - (8 - ((tpi * p / parts) & 7)) > 8) return nullptr;
-    return decode_layer_kernel<32, 4, kH, kNkt, kParts>;
+    return decode_layer_kernel<32, 4, kH, kNkt, kParts, kE>;
 }
 
 int decode_layer_clusters() {
@@ -892,7 +893,7 @@ int decode_layer_clusters() {
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
     if (cached[dev]) return cached[dev];
     for (int e = 1; e <= 512; e <<= 1) {
-        DecodeLayerKernel kern = e <= 256 ? decode_layer_kernel_for(e) : decode_layer_kernel<32, 4, 2048, 12, 4>;
+        DecodeLayerKernel kern = e <= 256 ? decode_layer_kernel_for(e) : decode_layer_kernel<32, 4, 2048, 12, 4, 128>;
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kDlMaxSmem) != cudaSuccess) {
             cudaGetLastError();
             return cached[dev] = -1;
@@ -912,7 +913,7 @@ int decode_layer_clusters() {
     q.attrs = attr;
     q.numAttrs = 1;
     int clusters = 0;
-    if (cudaOccupancyMaxActiveClusters(&clusters, decode_layer_kernel<32, 4, 0, 0, 0>, &q) != cudaSuccess || clusters < 1) {
+    if (cudaOccupancyMaxActiveClusters(&clusters, decode_layer_kernel<32, 4, 0, 0, 0, 0>, &q) != cudaSuccess || clusters < 1) {
         cudaGetLastError();
         return cached[dev] = -1;
     }
