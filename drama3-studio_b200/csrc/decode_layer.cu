@@ -358,10 +358,12 @@ __global__ void __launch_bounds__(kDlThreads, 1) decode_layer_kernel(const __gri
     } else if (warp == 1 && lane < E4 - E) {
         s_logit[E + lane] = -1.0f;
     } else if (warp == 2) {
-        // valid ids in every rank slot: with NaN probabilities no expert
-        // claims some ranks, and their slots keep these
+        // valid ids in every rank and order slot: with NaN probabilities no
+        // expert claims some ranks, and their slots keep these
         s_rkey[lane] = 0.0f;
         s_ridx[lane] = lane < E ? lane : 0;
+        s_key[lane] = 0.0f;
+        s_idx[lane] = lane < E ? lane : 0;
     }
     __syncthreads();
     if (warp < kDlWarps) {
@@ -422,6 +424,7 @@ __global__ void __launch_bounds__(kDlThreads, 1) decode_layer_kernel(const __gri
             __syncwarp();
             route_finish(k, true, lane, s_key, s_idx, idx, wr);
         }
+        idx = static_cast<unsigned>(idx) < static_cast<unsigned>(E) ? idx : 0;  // only NaN rows can miss
         const __nv_bfloat16 wb = __float2bfloat16_rn(wr);
         if (lane < k) {
             s_ids[lane] = idx;

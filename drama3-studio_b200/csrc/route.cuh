@@ -114,6 +114,11 @@ __device__ __forceinline__ void route_row(Load load, int E, int k, bool renormal
         need -= cnt;
     }
     // gatherTopK order: strictly greater in index order, then equal ones.
+    // The k slots hold valid ids first: with NaN probabilities nothing is
+    // picked, and the routes then stay inside the expert range.
+    s_key[lane] = 0.0f;
+    s_idx[lane] = lane < E ? lane : 0;
+    __syncwarp();
     const unsigned lt = (1u << lane) - 1u;
     int base = 0;
 #pragma unroll

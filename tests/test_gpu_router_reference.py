@@ -116,3 +116,90 @@ def test_torch_router_mode_is_exact(cuda_device):
     assert stats["normed_rows_differ"] == 0, stats
     assert stats["ids_differ"] == 0, stats
     assert stats["weights_differ"] == 0, stats
+
+
+def _crafted_logits(device):
+    """Router logits rows (bf16 [EXPERTS]) that stress the top-k selection:
+    wide ties (the selection's candidate set overflows and the full ranking
+    runs), ties among the winners (torch's sorting network orders them), ties
+    across the k-th boundary, few distinct values, and -inf entries."""
+    g = torch.Generator(device="cpu").manual_seed(11)
+    rows = []
+    rows.append(torch.zeros(EXPERTS))                                     # 128-way tie
+    r = torch.randn(EXPERTS, generator=g) - 4.0
+    r[torch.randperm(EXPERTS, generator=g)[:40]] = 3.0                    # 40 winners tied
+    rows.append(r)
+    r = torch.randn(EXPERTS, generator=g) - 4.0
+    r[torch.randperm(EXPERTS, generator=g)[:TOP_K]] = 2.5                  # exactly k tied winners
+    rows.append(r)
+    r = torch.randn(EXPERTS, generator=g) - 4.0
+    top = torch.randperm(EXPERTS, generator=g)
+    r[top[:6]] = torch.tensor([5.0, 4.5, 4.0, 3.5, 3.0, 2.75])
+    r[top[6:11]] = 2.5                                                    # ties across the k-th boundary
+    rows.append(r)
+    for _ in range(4):
+        rows.append(torch.round(torch.randn(EXPERTS, generator=g) * 2.0) / 4.0)  # few distinct values
+    r = torch.full((EXPERTS,), float("-inf"))
+    r[torch.randperm(EXPERTS, generator=g)[:12]] = torch.randn(12, generator=g)  # all but 12 at -inf
+    rows.append(r)
+    r = torch.randn(EXPERTS, generator=g)
+    r[5::16] = r[5]                                                       # 8 experts share one value
+    rows.append(r)
+    return [x.to(torch.bfloat16).to(device) for x in rows]
+
+
+def _logits_layer(layer, normed, logits, hidden_in, out, ws, ids, wts):
+    import ctypes
+
+    from drama_b200 import _lib
+
+    bank, keep = layer.bank()
+    lib = _lib.library()
+    lib.check(lib.dll.drama_b200_fp8_moe_layer_logits(
+        ctypes.byref(bank), normed.data_ptr(), logits.data_ptr(), hidden_in.data_ptr(), out.data_ptr(), 1, TOP_K,
+        ids.data_ptr(), wts.data_ptr(), None, ws.data_ptr(), ws.numel(), _lib.stream_handle(normed.device)))
+    del keep
+
+
+def test_crafted_ties_route_like_torch(cuda_device):
+    """Tie-heavy logits through the logits-driven layer (config-1 shape): ids and
+    bf16 weights equal torch's softmax -> topk -> renormalise on the same GPU."""
+    from drama_b200 import stack, synthetic
+
+    layer = stack.synthetic_stack(1, experts=EXPERTS, hidden=HIDDEN, intermediate=INTER, seed=7,
+                                  device=cuda_device)[0]
+    ws = stack.moe_layer_workspace(1, TOP_K, HIDDEN, INTER, EXPERTS, cuda_device)
+    hidden = synthetic.hidden_states(1, HIDDEN, 5, device=cuda_device)
+    normed = torch_rms_norm(hidden, layer.gamma)
+    out = torch.empty_like(hidden)
+    for n, logits in enumerate(_crafted_logits(cuda_device)):
+        ids = torch.empty(1, TOP_K, dtype=torch.int64, device=cuda_device)
+        wts = torch.empty(1, TOP_K, dtype=torch.bfloat16, device=cuda_device)
+        _logits_layer(layer, normed, logits.view(1, -1), hidden, out, ws, ids, wts)
+        probabilities = torch.softmax(logits.view(1, -1).float(), dim=-1)
+        ref_w, ref_ids = probabilities.topk(TOP_K, dim=-1)
+        ref_w = (ref_w / ref_w.sum(dim=-1, keepdim=True)).to(torch.bfloat16)
+        torch.cuda.synchronize()
+        assert torch.equal(ids, ref_ids), (n, ids.tolist(), ref_ids.tolist())
+        assert torch.equal(wts.view(torch.int16), ref_w.view(torch.int16)), (n, wts.tolist(), ref_w.tolist())
+        assert torch.isfinite(out.float()).all(), n
+
+
+def test_nan_logits_route_inside_the_bank(cuda_device):
+    """A NaN logit makes every probability NaN; the layer still picks expert ids
+    inside the bank (it reads no weight row out of bounds)."""
+    from drama_b200 import stack, synthetic
+
+    layer = stack.synthetic_stack(1, experts=EXPERTS, hidden=HIDDEN, intermediate=INTER, seed=7,
+                                  device=cuda_device)[0]
+    ws = stack.moe_layer_workspace(1, TOP_K, HIDDEN, INTER, EXPERTS, cuda_device)
+    hidden = synthetic.hidden_states(1, HIDDEN, 5, device=cuda_device)
+    normed = torch_rms_norm(hidden, layer.gamma)
+    logits = torch.randn(1, EXPERTS, device=cuda_device).to(torch.bfloat16)
+    logits[0, 17] = float("nan")
+    ids = torch.empty(1, TOP_K, dtype=torch.int64, device=cuda_device)
+    wts = torch.empty(1, TOP_K, dtype=torch.bfloat16, device=cuda_device)
+    out = torch.empty_like(hidden)
+    _logits_layer(layer, normed, logits, hidden, out, ws, ids, wts)
+    torch.cuda.synchronize()
+    assert ((ids >= 0) & (ids < EXPERTS)).all(), ids.tolist()
