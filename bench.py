@@ -1130,10 +1130,13 @@ def run_int4(args, mode: int = 0) -> None:
         del graph
     b1 = results[1]
     if mode == 0:
-        dtype = "int4 weights (asymmetric, group 128, bf16 scales, uint4 zero-points), f16 MMA, fp32 accumulate"
+        dtype = ("int4 weights (asymmetric, group 128, bf16 scales, uint4 zero-points), exact levels on bf16 MMA, "
+                 "fp32 block scales and accumulate")
         layer = "W4A16"
-        kernel = "one W4A16 expert call (grouping, gate/up GEMV with SwiGLU, down GEMV with the fused combine), batch 1"
-        launches = 3
+        # batch 1 at this shape is the one-launch layer (int4_layer.cu)
+        kernel = ("one W4A16 MoE layer for one decode row in one launch (4-CTA clusters: gate/up GEMV, SwiGLU, "
+                  "down GEMV, ordered combine), batch 1")
+        launches = 1
     else:
         dtype = (f"{W8A8_NAMES[mode]} weights, ConvRot-rotated int8 activations, s8 MMA, int32 accumulate, "
                  "bf16 projections")

@@ -359,8 +359,13 @@ int drama_b200_int4_decode(const DramaB200Int4Bank* bank, const void* x, int x_d
         if (reinterpret_cast<uintptr_t>(workspace) & 255u) return fail("workspace must be 256-byte aligned");
         W8a8Workspace ws{};
         w8a8_workspace_layout(tokens, top_k, b.hidden, b.intermediate, static_cast<char*>(workspace), &ws);
-        const cudaError_t err = int4_rows_launch(b, x, tokens, top_k, ids, ids_dtype, weights, weights_dtype, out,
-                                                 x_dtype, pair_out, ws, sms, static_cast<cudaStream_t>(stream));
+        const cudaError_t err =
+            int4_layer_supported(tokens, top_k, b, x_dtype)
+                // one row of the reference's shape: the whole layer in one launch
+                ? int4_layer_launch(b, x, ids, ids_dtype, weights, weights_dtype, out, x_dtype, pair_out,
+                                    ws.layer_part, ws.layer_tickets, ws.status, static_cast<cudaStream_t>(stream))
+                : int4_rows_launch(b, x, tokens, top_k, ids, ids_dtype, weights, weights_dtype, out, x_dtype,
+                                   pair_out, ws, sms, static_cast<cudaStream_t>(stream));
         if (err != cudaSuccess) return fail("INT4 launch failed: %s", cudaGetErrorString(err));
         return 0;
     }

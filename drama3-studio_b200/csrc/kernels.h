@@ -250,9 +250,20 @@ struct W8a8Workspace {
     float* wts;               // [P] route weights as fp32
     float* pair_out;          // [P][H] weighted fp32 partials
     int32_t* cmb_cnt;         // [H/16] finished down cells per row tile (zeroed by prep)
+    float* layer_part;        // one row (tokens == 1): [kMaxLayerUnits][H] partial down projections
+    int32_t* layer_tickets;   // one row: [4] arrivals per quarter of H, zero between calls (in the status chunk)
 };
 size_t w8a8_workspace_layout(int64_t tokens, int top_k, int hidden, int intermediate, char* base,
                              W8a8Workspace* ws);
+// Units (route slot, part of the intermediate dimension) of a one-launch layer.
+constexpr int kMaxLayerUnits = 32;
+// GPTQ W4A16 for one bf16 decode row in one launch (int4_layer.cu): the
+// reference's shape (hidden 2048, intermediate 768, top-8) when the device
+// fits its 32 clusters of 4 CTAs; scratch: layer_part and layer_tickets.
+bool int4_layer_supported(int64_t tokens, int top_k, const DramaB200Int4Bank& b, int x_dtype);
+cudaError_t int4_layer_launch(const DramaB200Int4Bank& b, const void* x, const void* ids, int ids_dtype,
+                              const void* weights, int weights_dtype, void* out, int out_dtype, float* pair_out,
+                              float* part, int32_t* tickets, int32_t* status, cudaStream_t s);
 // GPTQ W4A16 on the same schedule (bf16 hidden rows; scratch from w8a8_workspace_layout).
 cudaError_t int4_rows_launch(const DramaB200Int4Bank& bank, const void* x, int64_t tokens, int top_k,
                              const void* ids, int ids_dtype, const void* weights, int weights_dtype, void* out,

@@ -43,6 +43,7 @@
 #include "grouped.cuh"
 #include "kernels.h"
 #include "bucket.cuh"
+#include "int4.cuh"
 
 namespace drama {
 namespace {
@@ -706,33 +707,6 @@ __device__ __forceinline__ float i4_scale(const void* p, int dtype, int64_t i) {
                                     : __half2float(__ldg(static_cast<const __half*>(p) + i));
 }
 
-__device__ __forceinline__ uint32_t bf2_sub(uint32_t a, uint32_t b) {
-    uint32_t d;
-    asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-    return d;
-}
-__device__ __forceinline__ uint32_t bf2_mul(uint32_t a, uint32_t b) {
-    uint32_t d;
-    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-    return d;
-}
-
-// bf16x2 (w_i, w_{i+4}) of nibbles i and i + 4 of word W: bf16((code - zp) * scale).
-// zb = bf16x2 (128 + zp) twice; BF16: sc2 = bf16x2 scale twice; else scf = the fp32 scale.
-template <bool BF16>
-__device__ __forceinline__ uint32_t int4_pair(uint32_t W, int i, uint32_t zb, uint32_t sc2, float scf) {
-    const uint32_t biased = ((W >> (4 * i)) & 0x000F000Fu) | 0x43004300u;  // 128 + code, exact in bf16
-    const uint32_t level = bf2_sub(biased, zb);                             // code - zp, exact
-    if constexpr (BF16) {
-        return bf2_mul(level, sc2);  // exact product rounded once, as in fp32 then .to(bf16)
-    } else {
-        const float lo = __fmul_rn(__uint_as_float(level << 16), scf);
-        const float hi = __fmul_rn(__uint_as_float(level & 0xffff0000u), scf);
-        const __nv_bfloat162 p = __floats2bfloat162_rn(lo, hi);
-        return *reinterpret_cast<const uint32_t*>(&p);
-    }
-}
-
 // One 128-column block of one warp: the raw loads of a row pair (rows g and
 // g + 8 of a tile) and of the token row, issued one block ahead of the MMAs
 // that consume them.
@@ -1086,6 +1060,14 @@ size_t w8a8_workspace_layout(int64_t tokens, int top_k, int hidden, int intermed
     w.wts = reinterpret_cast<float*>(take(P * 4));
     w.pair_out = reinterpret_cast<float*>(take(static_cast<size_t>(P) * hidden * 4));
     w.cmb_cnt = reinterpret_cast<int32_t*>(take(static_cast<size_t>(hidden / 16) * 4));
+    // The one-launch INT4 layer's arrival tickets (int4_layer.cu) live in bytes
+    // 64..79 of the status chunk: every workspace layout of the library starts
+    // with that 256-byte chunk and writes only its first 16 bytes, so tickets
+    // that the last arriver leaves at zero stay zero whatever layout (token
+    // count, backend) uses the same zero-filled workspace in between.
+    w.layer_tickets = base ? w.status + 16 : nullptr;
+    if (tokens == 1)  // the layer's partial rows
+        w.layer_part = reinterpret_cast<float*>(take(static_cast<size_t>(kMaxLayerUnits) * hidden * 4));
     if (ws) *ws = w;
     return off;
 }

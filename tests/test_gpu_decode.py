@@ -159,6 +159,75 @@ def test_int4_decode_matches_oracle(cuda_device, tokens, asym):
     assert_parity(np_f32(y), expected, label=f"int4 T={tokens} asym={asym}")
 
 
+def _int4_config2(device, seed, experts=128, scale_dtype=torch.bfloat16):
+    """The config-2 shape (hidden 2048, intermediate 768, top-8), asymmetric,
+    the one-launch layer's envelope for one bfloat16 row."""
+    from drama_b200 import QuantizedBank, synthetic
+
+    bank = synthetic.int4_bank(experts, 2048, 768, seed, asymmetric=True, scale_dtype=scale_dtype)
+    dev = to_device(bank, device)
+    qb = QuantizedBank(dev["w13_weight"], dev["w13_scale_inv"], dev["w2_weight"], dev["w2_scale_inv"],
+                       dev["w13_qzeros"], dev["w2_qzeros"])
+    return bank, qb
+
+
+@pytest.mark.parametrize("scale_dtype", [torch.bfloat16, torch.float16])
+def test_int4_one_row_layer_out_and_pairs(cuda_device, scale_dtype):
+    """One row at the config-2 shape takes the one-launch layer; with both
+    outputs given it writes the weighted partial of every route slot
+    (pair_out) and their slot-order sum (out), repeated slots included."""
+    import ctypes
+
+    from drama_b200 import _lib, synthetic
+    from drama_b200.backend import _int4_bank
+
+    bank, qb = _int4_config2(cuda_device, 71, scale_dtype=scale_dtype)
+    x = synthetic.hidden_states(1, 2048, 72)
+    ids = torch.tensor([[5, 17, 5, 90, 127, 0, 64, 33]], dtype=torch.int32)
+    w = torch.softmax(torch.randn(1, 8, generator=torch.Generator().manual_seed(73)), -1).to(torch.bfloat16)
+    lib = _lib.library()
+    desc, keep = _int4_bank(qb, 2048)
+    xd, idd, wd = x.to(cuda_device), ids.to(cuda_device), w.to(cuda_device)
+    out = torch.empty_like(xd)
+    pairs = torch.empty(8, 2048, device=cuda_device, dtype=torch.float32)
+    nbytes = lib.dll.drama_b200_decode_workspace_bytes(1, 8, 2048, 768)
+    ws = torch.zeros(nbytes, device=cuda_device, dtype=torch.uint8)  # zero-filled, as the ABI requires
+    lib.check(lib.dll.drama_b200_int4_decode(
+        ctypes.byref(desc), xd.data_ptr(), _lib.DTYPE_CODES[xd.dtype], 1, 8, idd.data_ptr(),
+        _lib.DTYPE_CODES[idd.dtype], wd.data_ptr(), _lib.DTYPE_CODES[wd.dtype], out.data_ptr(), pairs.data_ptr(),
+        ws.data_ptr(), ws.numel(), _lib.stream_handle(xd.device)))
+    torch.cuda.synchronize(cuda_device)
+    del keep
+    nb = np_bank(bank)
+    want_pairs = R.int4_dequant_pairs(np.repeat(np_f32(x), 8, axis=0), ids.numpy().reshape(-1),
+                                      np_f32(w).reshape(-1), nb)
+    assert_parity(np_f32(pairs), want_pairs, label="int4 layer pair_out")
+    assert_parity(np_f32(out), R.combine_slots(want_pairs, 1, 8, "bfloat16"), label="int4 layer out")
+    # the pair rows are the slot partials the sum is made of, added in slot order
+    total = np.zeros(2048, dtype=np.float32)
+    for j in range(8):
+        total = (total + np_f32(pairs)[j]).astype(np.float32)
+    np.testing.assert_array_equal(np_f32(out)[0], R.round_bf16(total))
+
+
+def test_int4_one_row_layer_after_larger_batches(cuda_device):
+    """The layer's arrival tickets share the workspace with the grouped
+    schedule of larger batches: one row after 16 and 4 rows (and again) on
+    the same workspace still matches the oracle."""
+    from drama_b200 import QuantizedB200Backend, synthetic
+
+    bank, qb = _int4_config2(cuda_device, 81, experts=64)
+    nb = np_bank(bank)
+    backend = QuantizedB200Backend(0)
+    for step, tokens in enumerate((16, 1, 4, 1, 1)):
+        x = synthetic.hidden_states(tokens, 2048, 82 + step)
+        ids, w = synthetic.uniform_routes(tokens, 8, 64, 83 + step)
+        w = w.to(torch.bfloat16)
+        y = backend.forward(x.to(cuda_device), ids.to(cuda_device), w.to(cuda_device), qb)
+        assert_parity(np_f32(y), R.int4_forward(np_f32(x), ids.numpy(), np_f32(w), nb),
+                      label=f"int4 step {step} T={tokens}")
+
+
 def test_int4_decode_matches_reference_goldens(cuda_device):
     from drama_b200 import QuantizedB200Backend, QuantizedBank, synthetic
 
