@@ -183,9 +183,10 @@ def measured_peaks() -> dict:
     return {"hbm_gbs": 6650.0, "source": "fallback"}
 
 
-def committed_traffic() -> float | None:
-    """DRAM bytes per MoE layer (both launches) from the committed ncu summary."""
-    path = REPO / "profiles" / "moe_layer_traffic.json"
+def committed_traffic(name: str = "moe_layer_traffic.json") -> float | None:
+    """DRAM bytes per launch of a bench's dominant kernel from a committed ncu
+    summary under profiles/ (read + write, one capture)."""
+    path = REPO / "profiles" / name
     if path.is_file():
         return json.loads(path.read_text()).get("dram_bytes_per_layer")
     return None
@@ -1160,7 +1161,8 @@ def run_int4(args, mode: int = 0) -> None:
         "roofline": {"kernel": kernel, "bound": "hbm",
                      "achieved": b1["achieved_gbs"], "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": b1["achieved_gbs"] / peaks["hbm_gbs"],
-                     "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs)", "traffic": None,
+                     "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs)",
+                     "traffic": committed_traffic("int4_layer_traffic.json") if mode == 0 else None,
                      "algorithmic_bytes_per_launch": b1["algorithmic_bytes_per_call"]},
         "by_batch": results,
         "e2e": {"value": INT4_CALLS * world / (e2e_ms / 1000.0), "unit": "tokens/s",
