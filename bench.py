@@ -1202,6 +1202,7 @@ def run_shared(args) -> None:
     mods = [SharedExpertB200(w(inter, HIDDEN), w(inter, HIDDEN), w(HIDDEN, inter), w(1, HIDDEN))
             for _ in range(layers)]
     layer_bytes = 3 * HIDDEN * inter * 2 + HIDDEN * 2
+    one_launch = HIDDEN == 2048 and inter == 768  # batch 1 at this shape is one launch (shared_layer.cu)
     peaks = measured_peaks()
     results = {}
     clocks_summary = e2e_ms = None
@@ -1264,7 +1265,10 @@ def run_shared(args) -> None:
                                 "(value: batch 1), one CUDA graph per batch"),
                    "batches": [1, 4, 16], "parallelism": f"replicas{world}" if world > 1 else "single",
                    "l2": f"{layers} distinct experts, {layers * layer_bytes / 1e6:.0f} MB (> L2)"},
-        "roofline": {"kernel": "one layer's shared expert (gate/up GEMV, SwiGLU, down GEMV + fused sum), batch 1",
+        "roofline": {"kernel": ("one layer's shared expert in one launch (4-CTA clusters: gate/up rows, SwiGLU, "
+                                "down rows, ordered sum with the gate, routed sum and residual), batch 1"
+                                if one_launch else
+                                "one layer's shared expert (gate/up GEMV, SwiGLU, down GEMV + fused sum), batch 1"),
                      "bound": "hbm", "achieved": b1["achieved_gbs"], "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": b1["achieved_gbs"] / peaks["hbm_gbs"],
                      "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs)", "traffic": None,
@@ -1272,7 +1276,7 @@ def run_shared(args) -> None:
         "by_batch": results,
         "e2e": {"value": world / (e2e_ms / 1000.0), "unit": "tokens/s",
                 "h2d_bytes_per_step": HIDDEN * 2, "d2h_bytes_per_step": HIDDEN * 2},
-        "gpu_launches": args.steps * layers * 3,
+        "gpu_launches": args.steps * layers * (1 if one_launch else 2),
         "clocks": clocks_summary,
     }
     if world > 1:

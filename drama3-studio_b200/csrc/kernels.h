@@ -322,10 +322,19 @@ cudaError_t fp8_w8a8_launch(const DramaB200Fp8Bank& bank, const void* x, int64_t
 // Shared expert + gate fused with the routed combine (shared_expert.cu).
 constexpr int kMaxSharedTokens = 4096;
 struct SharedWorkspace {
+    int32_t* tickets;         // [4] the one-launch layer's arrivals per quarter (zero between calls)
+    int32_t* status;          // [4] [1] waits that ran out
     __nv_bfloat16* h;         // [T][I] SwiGLU rows
     float* gate_s;            // [T] bf16-rounded sigmoid gate
+    float* part;              // T == 1: [I / 32][H] the one-launch layer's partial down projections
 };
 size_t shared_expert_workspace_layout(int64_t tokens, int hidden, int inter, char* base, SharedWorkspace* ws);
+// One bfloat16 row at hidden 2048, intermediate 768: the whole shared expert
+// and its combine in one launch (shared_layer.cu).
+bool shared_layer_supported(const DramaB200SharedExpert& m, int64_t tokens);
+cudaError_t shared_layer_launch(const DramaB200SharedExpert& m, const void* x, const void* routed,
+                                const void* residual, void* out, float* part, int32_t* tickets, int32_t* status,
+                                cudaStream_t s);
 cudaError_t shared_expert_launch(const DramaB200SharedExpert& m, const void* x, int64_t tokens, const void* routed,
                                  const void* residual, void* out, const SharedWorkspace& ws, int sm_count,
                                  cudaStream_t s);

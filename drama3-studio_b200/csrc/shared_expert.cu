@@ -8,6 +8,8 @@
 //   t = bf16(routed + shared);  out = bf16(after_mixer + t)
 // (routed and after_mixer are optional; without them out = shared or t.)
 //
+// One bfloat16 row at hidden 2048, intermediate 768 runs as one launch
+// (shared_layer.cu). Otherwise:
 // Launches (chained by programmatic dependent launch): the gate/up GEMV, whose
 // epilogue forms the SwiGLU rows and (one extra cell per token group) the
 // sigmoid gate scalars, then the down GEMV, whose epilogue applies the gate,
@@ -160,8 +162,14 @@ size_t shared_expert_workspace_layout(int64_t tokens, int hidden, int inter, cha
         return p;
     };
     SharedWorkspace w{};
+    // The control words come first for every token count, so that no other
+    // layout of the same buffer ever writes over the zeroed tickets.
+    char* control = take(256);
+    w.tickets = reinterpret_cast<int32_t*>(control);
+    w.status = control ? reinterpret_cast<int32_t*>(control + 16) : nullptr;
     w.h = reinterpret_cast<__nv_bfloat16*>(take(static_cast<size_t>(tokens) * inter * 2));
     w.gate_s = reinterpret_cast<float*>(take(tokens * 4));
+    if (tokens == 1) w.part = reinterpret_cast<float*>(take(static_cast<size_t>(inter / 32) * hidden * 4));
     if (ws) *ws = w;
     return off;
 }
@@ -169,6 +177,8 @@ size_t shared_expert_workspace_layout(int64_t tokens, int hidden, int inter, cha
 cudaError_t shared_expert_launch(const DramaB200SharedExpert& m, const void* x, int64_t tokens, const void* routed,
                                  const void* residual, void* out, const SharedWorkspace& ws, int sm_count,
                                  cudaStream_t s) {
+    if (ws.part && shared_layer_supported(m, tokens))  // one row of the reference's shape: one launch
+        return shared_layer_launch(m, x, routed, residual, out, ws.part, ws.tickets, ws.status, s);
     const int H = m.hidden, I = m.intermediate;
     const int64_t tg = (tokens + kShTok - 1) / kShTok;
     // split tiles: one CTA of ks warps per cell; otherwise four single-warp cells per CTA

@@ -279,6 +279,10 @@ DRAMA_B200_API int drama_b200_w8a8_decode(const DramaB200W8a8Bank* bank, const v
  * row-major with row strides in elements (multiples of 8, 16-byte aligned).
  * H and I multiples of 128, tokens <= 4096. out may alias routed or residual
  * (each element is read before it is written, by the same thread).
+ * One row at H 2048, I 768 runs as a single launch that starts reading the
+ * weights before the launch it follows on the stream has finished (only x,
+ * routed and residual wait for it): the weights must not be written by that
+ * launch.
  * ------------------------------------------------------------------------- */
 typedef struct DramaB200SharedExpert {
     const void* gate_proj;     /* [I, H] */

@@ -73,3 +73,66 @@ def test_in_place_and_graph_replay(cuda_device):
         graph.replay()
         torch.cuda.synchronize()
         assert torch.equal(static, want)
+
+
+def test_layer_chain_matches_oracle_and_replays(cuda_device):
+    """Six distinct shared experts chained through the residual, as the
+    decode stack calls them: one row at the reference's shape runs one
+    launch per layer whose weight loads start before the previous layer has
+    finished. Each layer matches the oracle applied to the previous layer's
+    output, and a CUDA graph of the chain replays bit for bit."""
+    from drama_b200 import synthetic
+    from drama_b200.shared import SharedExpertB200
+
+    mods, ws = [], []
+    for layer in range(6):
+        w = _weights(2048, 768, 100 + layer, cuda_device)
+        ws.append(w)
+        mods.append(SharedExpertB200(*w))
+    x = synthetic.hidden_states(1, 2048, 31, device=cuda_device)
+    routed = synthetic.hidden_states(1, 2048, 32, device=cuda_device) * 0.1
+    h0 = synthetic.hidden_states(1, 2048, 33, device=cuda_device) * 0.5
+    outs, h = [], h0
+    for m in mods:
+        h = m.post(h, routed, x)
+        outs.append(h)
+    torch.cuda.synchronize()
+    prev = h0
+    for layer, (gp, up, dp, gw) in enumerate(ws):
+        ref = R.post_moe(np_f32(prev), np_f32(routed),
+                         R.shared_expert(np_f32(x), np_f32(gp), np_f32(up), np_f32(dp), np_f32(gw)))
+        assert_parity(np_f32(outs[layer]), ref, label=f"layer {layer}")
+        prev = outs[layer]
+    stream = torch.cuda.Stream(cuda_device)
+    stream.wait_stream(torch.cuda.current_stream(cuda_device))
+    with torch.cuda.stream(stream):  # the workspace is per stream: one eager pass before capture
+        g = h0
+        for m in mods:
+            g = m.post(g, routed, x)
+    torch.cuda.current_stream(cuda_device).wait_stream(stream)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        g = h0
+        for m in mods:
+            g = m.post(g, routed, x)
+    for _ in range(3):
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(g, outs[-1])
+
+
+def test_one_row_after_larger_batches(cuda_device):
+    """The one-launch layer's arrival tickets share the workspace with the
+    two-launch schedule of larger batches: one row after 16 and 3 rows (and
+    again) still matches the oracle."""
+    from drama_b200 import synthetic
+    from drama_b200.shared import SharedExpertB200
+
+    gp, up, dp, gw = _weights(2048, 768, 41, cuda_device)
+    mod = SharedExpertB200(gp, up, dp, gw)
+    for step, tokens in enumerate((16, 1, 3, 1, 1)):
+        x = synthetic.hidden_states(tokens, 2048, 42 + step, device=cuda_device)
+        out = mod.shared(x)
+        torch.cuda.synchronize()
+        ref = R.shared_expert(np_f32(x), np_f32(gp), np_f32(up), np_f32(dp), np_f32(gw))
+        assert_parity(np_f32(out), ref, label=f"step {step} T={tokens}")
