@@ -1271,7 +1271,8 @@ def run_shared(args) -> None:
                                 "one layer's shared expert (gate/up GEMV, SwiGLU, down GEMV + fused sum), batch 1"),
                      "bound": "hbm", "achieved": b1["achieved_gbs"], "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": b1["achieved_gbs"] / peaks["hbm_gbs"],
-                     "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs)", "traffic": None,
+                     "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs)",
+                     "traffic": committed_traffic("shared_layer_traffic.json") if one_launch else None,
                      "algorithmic_bytes_per_launch": b1["algorithmic_bytes_per_layer"]},
         "by_batch": results,
         "e2e": {"value": world / (e2e_ms / 1000.0), "unit": "tokens/s",

@@ -322,7 +322,7 @@ cudaError_t fp8_w8a8_launch(const DramaB200Fp8Bank& bank, const void* x, int64_t
 // Shared expert + gate fused with the routed combine (shared_expert.cu).
 constexpr int kMaxSharedTokens = 4096;
 struct SharedWorkspace {
-    int32_t* tickets;         // [4] the one-launch layer's arrivals per quarter (zero between calls)
+    int32_t* tickets;         // [<= 16] the one-launch layer's arrivals per row share (zero between calls)
     int32_t* status;          // [4] [1] waits that ran out
     __nv_bfloat16* h;         // [T][I] SwiGLU rows
     float* gate_s;            // [T] bf16-rounded sigmoid gate

@@ -166,7 +166,7 @@ size_t shared_expert_workspace_layout(int64_t tokens, int hidden, int inter, cha
     // layout of the same buffer ever writes over the zeroed tickets.
     char* control = take(256);
     w.tickets = reinterpret_cast<int32_t*>(control);
-    w.status = control ? reinterpret_cast<int32_t*>(control + 16) : nullptr;
+    w.status = control ? reinterpret_cast<int32_t*>(control + 64) : nullptr;  // after up to 16 tickets
     w.h = reinterpret_cast<__nv_bfloat16*>(take(static_cast<size_t>(tokens) * inter * 2));
     w.gate_s = reinterpret_cast<float*>(take(tokens * 4));
     if (tokens == 1) w.part = reinterpret_cast<float*>(take(static_cast<size_t>(inter / 32) * hidden * 4));
