@@ -44,7 +44,7 @@ namespace {
 namespace cg = cooperative_groups;
 
 constexpr int kIlCluster = 4;
-constexpr int kIlWarps = 8;                       // consumer warps
+constexpr int kIlWarps = 16;                       // consumer warps
 constexpr int kIlThreads = (kIlWarps + 1) * 32;   // + one TMA producer warp
 constexpr int kIlConsumers = kIlWarps * 32;
 constexpr int kIlH = 2048, kIlI = 768, kIlK = 8;  // the shape this kernel is built for
@@ -271,7 +271,8 @@ __global__ void __launch_bounds__(kIlThreads, 1) int4_layer_kernel(const __grid_
         }
         named_barrier(1, kIlConsumers);
 
-        // Gate/up cells: cell c = warp + 8i is K block c % 4 of stage c / 4.
+        // Gate/up cells: cell c = warp + 16i is K block c % 4 of stage c / 4
+        // (four warps per SMSP hide the dequantisation's dependent latency).
 #pragma unroll 1
         for (int i = 0; i < kIlCells / kIlWarps; ++i) {
             const int c = warp + kIlWarps * i, st = c >> 2, kb = c & 3;
@@ -352,7 +353,7 @@ __global__ void __launch_bounds__(kIlThreads, 1) int4_layer_kernel(const __grid_
         }
         mbar_wait(w2_bar, 0, status + 1);
         named_barrier(1, kIlConsumers);  // h and the down rows in shared memory
-        // Partial down projection: warp w takes 16-row tiles w + 8u of the
+        // Partial down projection: warp w takes 16-row tiles w + 16u of the
         // quarter. In each 64-column chunk of the unit's columns lane (g, t)
         // dequantises two words (columns 16t..16t+15) of rows g and g + 8 and
         // reads h in the same pair order. The scale is applied per weight, so
@@ -408,38 +409,28 @@ __global__ void __launch_bounds__(kIlThreads, 1) int4_layer_kernel(const __grid_
         if (tid == 0) s_last = atomic_add_acq_rel_gpu(a.tickets + r, 1) == kIlUnits - 1;
         named_barrier(1, kIlConsumers);
         if (s_last) {
-            // Last CTA of quarter r: columns 2 tid and 2 tid + 1 of every
-            // unit's partial (unit u = j P + p), all loads in flight before
+            // Last CTA of quarter r: column tid of every unit's partial
+            // (unit u = j P + p), all loads in flight before
             // the first store; then for each column each slot's parts in part
             // order, rounded, weighted, slots added in slot order.
-            static_assert(kIlHq == 2 * kIlConsumers, "two columns per consumer thread");
+            static_assert(kIlHq == kIlConsumers, "one column per consumer thread");
             if (tid == 0) a.tickets[r] = 0;
-            const int n = r * kIlHq + 2 * tid;
-            float2 v[kIlUnits];
+            const int n = r * kIlHq + tid;
+            float v[kIlUnits];
 #pragma unroll
-            for (int u = 0; u < kIlUnits; ++u)
-                v[u] = __ldcg(reinterpret_cast<const float2*>(a.part + static_cast<int64_t>(u) * kIlH + n));
-            float y0 = 0.0f, y1 = 0.0f;
+            for (int u = 0; u < kIlUnits; ++u) v[u] = __ldcg(a.part + static_cast<int64_t>(u) * kIlH + n);
+            float y0 = 0.0f;
 #pragma unroll
             for (int j = 0; j < kIlK; ++j) {
-                float s0 = 0.0f, s1 = 0.0f;
+                float s0 = 0.0f;
 #pragma unroll
-                for (int p = 0; p < kIlParts; ++p) {
-                    s0 += v[j * kIlParts + p].x;
-                    s1 += v[j * kIlParts + p].y;
-                }
+                for (int p = 0; p < kIlParts; ++p) s0 += v[j * kIlParts + p];
                 const bool routed = s_ids[j] >= 0;
                 const float pw0 = routed ? __fmul_rn(bf16_round_i4(s0), s_w[j]) : 0.0f;
-                const float pw1 = routed ? __fmul_rn(bf16_round_i4(s1), s_w[j]) : 0.0f;
-                if (a.pair_out) {
-                    a.pair_out[static_cast<int64_t>(j) * kIlH + n] = pw0;
-                    a.pair_out[static_cast<int64_t>(j) * kIlH + n + 1] = pw1;
-                }
+                if (a.pair_out) a.pair_out[static_cast<int64_t>(j) * kIlH + n] = pw0;
                 y0 = __fadd_rn(y0, pw0);
-                y1 = __fadd_rn(y1, pw1);
             }
             store_any(a.out, a.out_dtype, n, y0);
-            store_any(a.out, a.out_dtype, n + 1, y1);
         }
     }
 }
