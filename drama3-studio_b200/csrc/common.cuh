@@ -124,6 +124,12 @@ __device__ __forceinline__ uint64_t policy_evict_first() {
     return policy;
 }
 
+__device__ __forceinline__ uint64_t policy_evict_normal() {
+    uint64_t policy;
+    asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(policy));
+    return policy;
+}
+
 __device__ __forceinline__ uint64_t policy_evict_last() {
     uint64_t policy;
     asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(policy));

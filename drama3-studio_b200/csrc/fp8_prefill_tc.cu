@@ -153,6 +153,15 @@ __device__ __forceinline__ void st_global_32b(void* p, uint32_t v0, uint32_t v1,
                  : "memory");
 }
 
+// The same store with an L2 eviction policy (the down GEMM's fp32 pair rows
+// go out evict-first, so they do not push weight and activation rows out of L2).
+__device__ __forceinline__ void st_global_32b_hint(void* p, uint64_t policy, uint32_t v0, uint32_t v1, uint32_t v2,
+                                                   uint32_t v3, uint32_t v4, uint32_t v5, uint32_t v6, uint32_t v7) {
+    asm volatile("st.global.L2::cache_hint.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8}, %9;" ::"l"(p), "r"(v0), "r"(v1),
+                 "r"(v2), "r"(v3), "r"(v4), "r"(v5), "r"(v6), "r"(v7), "l"(policy)
+                 : "memory");
+}
+
 template <int MODE>  // 0: gate/up + SwiGLU + requantise; 1: down * route weight
 __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_constant__ TcGemmArgs a) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -231,7 +240,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
     if (warp == 0) {
         // ---------------- producer: TMA ring and tile scales ----------------
         const uint64_t pol_a = policy_evict_last();
-        const uint64_t pol_b = policy_evict_first();
+        // weight rows: read once for an expert with one row tile, by every
+        // row tile otherwise (normal priority then, so they stay in L2)
+        const uint64_t pol_b_once = policy_evict_first(), pol_b_shared = policy_evict_normal();
         // Scales of tile t (the it-th of this CTA) into slot it & 1: the
         // activation scales as [kb][row] (kb-major copies, so the lanes of one
         // copy write 32 consecutive rows: distinct banks) and the tile's two
@@ -273,6 +284,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                     break;
                 }
                 if (lane == 0) {
+                    const uint64_t pol_b = s_tiles[x.e + 1] - s_tiles[x.e] > 1 ? pol_b_shared : pol_b_once;
                     const uint32_t st = sbase + kOffStages + s * kTcStage;
                     mbar_arrive_expect_tx(bar(kBarFull + s), kTcStage);
                     tma_load_2d(st, &a.a_map, kb * 128, static_cast<int>(x.row0), bar(kBarFull + s), pol_a);
@@ -430,13 +442,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                     if (g == 0) a.hs[row * (a.I / 128) + x.n0 / 128] = scale;
                 }
             } else if (r < x.rows) {
+                const uint64_t pol_out = policy_evict_first();
                 float* dst = a.pair_out + pair * a.H + x.n0 + 64 * g;
 #pragma unroll
                 for (int v = 0; v < 8; ++v) {
                     float f[8];
 #pragma unroll
                     for (int u = 0; u < 4; ++u) unpack_f32x2(acc[4 * v + u], f[2 * u], f[2 * u + 1]);
-                    st_global_32b(dst + 8 * v, __float_as_uint(__fmul_rn(f[0], route_w)),
+                    st_global_32b_hint(dst + 8 * v, pol_out, __float_as_uint(__fmul_rn(f[0], route_w)),
                                   __float_as_uint(__fmul_rn(f[1], route_w)), __float_as_uint(__fmul_rn(f[2], route_w)),
                                   __float_as_uint(__fmul_rn(f[3], route_w)), __float_as_uint(__fmul_rn(f[4], route_w)),
                                   __float_as_uint(__fmul_rn(f[5], route_w)), __float_as_uint(__fmul_rn(f[6], route_w)),
