@@ -81,6 +81,7 @@ struct TcGemmArgs {
     CUtensorMap a_map;          // [rows][K] E4M3 sorted pair rows (x or h)
     CUtensorMap b_map;          // [slots][N rows][K] E4M3 (W13 or W2)
     const float* a_scale;       // [rows][K/128]
+    const float* sorted_w;      // down: route weight of each sorted row [P]
     const float* b_scale;       // [slots][N/128][K/128] (bank strides below)
     int64_t b_scale_slot_stride, b_scale_row_stride;
     const int64_t* offsets;     // [E + 1] first sorted row of each expert
@@ -365,8 +366,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
             int64_t pair = 0;
             float route_w = 0.0f;
             if (MODE == 1 && r < x.rows) {
+                // both independent of each other: neither load holds the K loop
                 pair = a.order[x.row0 + r];
-                route_w = load_any(a.weights, a.weights_dtype, pair);
+                route_w = a.sorted_w[x.row0 + r];
             }
             uint64_t acc[32];
 #pragma unroll
@@ -469,14 +471,21 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
 
 // One token row per CTA: its 1x128 blocks quantised once (half a warp per
 // block, 8 values per lane) and written to the sorted position of each of
-// the token's pairs.
+// the token's pairs, with each pair's route weight (fp32) at its position.
 __global__ void __launch_bounds__(256) tc_quant_tokens_kernel(const __nv_bfloat16* x, int H, int top_k,
-                                                              const int64_t* position, uint8_t* xq, float* xs) {
+                                                              const int64_t* position, const void* weights,
+                                                              int weights_dtype, uint8_t* xq, float* xs,
+                                                              float* sorted_w) {
     __shared__ int64_t s_pos[32];
     grid_dependency_wait();
     grid_launch_dependents();
     const int64_t token = blockIdx.x;
-    if (threadIdx.x < top_k) s_pos[threadIdx.x] = position[token * top_k + threadIdx.x];
+    if (threadIdx.x < top_k) {
+        const int64_t p = token * top_k + threadIdx.x;
+        const int64_t r = position[p];
+        s_pos[threadIdx.x] = r;
+        if (r >= 0) sorted_w[r] = load_any(weights, weights_dtype, p);
+    }
     __syncthreads();
     const int hw = threadIdx.x >> 4, l = threadIdx.x & 15, nblk = H / 128;
     for (int base = 0; base < nblk; base += 16) {
@@ -609,6 +618,7 @@ size_t fp8_prefill_tc_workspace_layout(int64_t tokens, int top_k, int hidden, in
     w.counts = reinterpret_cast<int64_t*>(take(static_cast<size_t>(experts) * 8));
     w.offsets = reinterpret_cast<int64_t*>(take(static_cast<size_t>(experts + 1) * 8));
     w.position = reinterpret_cast<int64_t*>(take(P * 8));
+    w.sorted_w = reinterpret_cast<float*>(take(P * 4));
     w.chunk_counts = reinterpret_cast<int*>(take(permute_wide_scratch_bytes(P, experts)));
     w.xq = reinterpret_cast<uint8_t*>(take(rows * hidden));
     w.xs = reinterpret_cast<float*>(take(rows * (hidden / 128) * 4));
@@ -642,11 +652,13 @@ cudaError_t fp8_prefill_tc_launch(const DramaB200Fp8Bank& bank, const void* x, i
     if ((err = permute_routes_wide(pa, ws.chunk_counts, ws.position, s)) != cudaSuccess) return err;
     if ((err = launch_pdl_smem(tc_quant_tokens_kernel, dim3(static_cast<unsigned>(tokens)), dim3(256), 0, s,
                                static_cast<const __nv_bfloat16*>(x), H, top_k,
-                               static_cast<const int64_t*>(ws.position), ws.xq, ws.xs)) != cudaSuccess)
+                               static_cast<const int64_t*>(ws.position), weights, weights_dtype, ws.xq, ws.xs,
+                               ws.sorted_w)) != cudaSuccess)
         return err;
     TcGemmArgs g{};
     g.offsets = ws.offsets;
     g.order = ws.order;
+    g.sorted_w = ws.sorted_w;
     g.E = E;
     g.I = I;
     g.H = H;

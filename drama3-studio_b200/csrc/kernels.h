@@ -302,6 +302,7 @@ struct Fp8PrefillWorkspace {
     int64_t* counts;    // [E]
     int64_t* offsets;   // [E + 1]
     int64_t* position;  // [P] sorted position of each pair (-1: dropped)
+    float* sorted_w;    // [P] each pair's route weight (fp32) at its sorted position
     int* chunk_counts;  // permutation scratch
     uint8_t* xq;        // [P + 128][H] E4M3 token rows in sorted order
     float* xs;          // [P + 128][H/128]
