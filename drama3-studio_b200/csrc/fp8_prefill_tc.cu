@@ -139,6 +139,15 @@ __device__ __forceinline__ uint32_t e4m3x2(float lo, float hi) {
 
 __device__ __forceinline__ uint64_t splat_f32x2(float s) { return pack_f32x2(s, s); }
 
+// a, b rounded to bf16 (round to nearest even) and widened back to fp32, with
+// one paired conversion for the two values.
+__device__ __forceinline__ void round_bf16_pair(float& a, float& b) {
+    uint32_t p;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(p) : "f"(b), "f"(a));  // upper half b, lower half a
+    a = __uint_as_float(p << 16);
+    b = __uint_as_float(p & 0xffff0000u);
+}
+
 // acc[j/2] += (cols j, j+1 of r) * s for 16 columns.
 __device__ __forceinline__ void promote16(uint64_t* acc, const uint32_t (&r)[16], uint64_t s) {
 #pragma unroll
@@ -412,10 +421,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                     float g0, g1, u0, u1;
                     unpack_f32x2(acc[j], g0, g1);
                     unpack_f32x2(acc[16 + j], u0, u1);
-                    const float gb0 = __bfloat162float(__float2bfloat16_rn(g0));
-                    const float gb1 = __bfloat162float(__float2bfloat16_rn(g1));
-                    const float ub0 = __bfloat162float(__float2bfloat16_rn(u0));
-                    const float ub1 = __bfloat162float(__float2bfloat16_rn(u1));
+                    round_bf16_pair(g0, g1);
+                    round_bf16_pair(u0, u1);
+                    const float gb0 = g0, gb1 = g1, ub0 = u0, ub1 = u1;
                     hv[2 * j] = __fmul_rn(__fdividef(gb0, __fadd_rn(1.0f, __expf(-gb0))), ub0);
                     hv[2 * j + 1] = __fmul_rn(__fdividef(gb1, __fadd_rn(1.0f, __expf(-gb1))), ub1);
                     m = fmaxf(m, fmaxf(fabsf(hv[2 * j]), fabsf(hv[2 * j + 1])));
