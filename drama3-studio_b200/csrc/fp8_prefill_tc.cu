@@ -421,11 +421,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                     float g0, g1, u0, u1;
                     unpack_f32x2(acc[j], g0, g1);
                     unpack_f32x2(acc[16 + j], u0, u1);
-                    round_bf16_pair(g0, g1);
+                    round_bf16_pair(g0, g1);  // gate and up as the bf16 rows of the reference
                     round_bf16_pair(u0, u1);
-                    const float gb0 = g0, gb1 = g1, ub0 = u0, ub1 = u1;
-                    hv[2 * j] = __fmul_rn(__fdividef(gb0, __fadd_rn(1.0f, __expf(-gb0))), ub0);
-                    hv[2 * j + 1] = __fmul_rn(__fdividef(gb1, __fadd_rn(1.0f, __expf(-gb1))), ub1);
+                    hv[2 * j] = __fmul_rn(__fdividef(g0, __fadd_rn(1.0f, __expf(-g0))), u0);
+                    hv[2 * j + 1] = __fmul_rn(__fdividef(g1, __fadd_rn(1.0f, __expf(-g1))), u1);
                     m = fmaxf(m, fmaxf(fabsf(hv[2 * j]), fabsf(hv[2 * j + 1])));
                 }
                 // the row's other 96 h columns of the 1x128 block are in the other groups' threads
@@ -460,10 +459,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
 #pragma unroll
                     for (int u = 0; u < 4; ++u) unpack_f32x2(acc[4 * v + u], f[2 * u], f[2 * u + 1]);
                     st_global_32b_hint(dst + 8 * v, pol_out, __float_as_uint(__fmul_rn(f[0], route_w)),
-                                  __float_as_uint(__fmul_rn(f[1], route_w)), __float_as_uint(__fmul_rn(f[2], route_w)),
-                                  __float_as_uint(__fmul_rn(f[3], route_w)), __float_as_uint(__fmul_rn(f[4], route_w)),
-                                  __float_as_uint(__fmul_rn(f[5], route_w)), __float_as_uint(__fmul_rn(f[6], route_w)),
-                                  __float_as_uint(__fmul_rn(f[7], route_w)));
+                                       __float_as_uint(__fmul_rn(f[1], route_w)),
+                                       __float_as_uint(__fmul_rn(f[2], route_w)),
+                                       __float_as_uint(__fmul_rn(f[3], route_w)),
+                                       __float_as_uint(__fmul_rn(f[4], route_w)),
+                                       __float_as_uint(__fmul_rn(f[5], route_w)),
+                                       __float_as_uint(__fmul_rn(f[6], route_w)),
+                                       __float_as_uint(__fmul_rn(f[7], route_w)));
                 }
             }
         }
