@@ -97,3 +97,18 @@ def test_product_code_never_imports_the_oracle():
     for path in (REPO / "drama3-studio_b200").rglob("*.py"):
         text = path.read_text()
         assert "oracle" not in re.findall(r"^\s*(?:from|import)\s+(\w+)", text, re.M), path
+
+
+def test_w8a8_prefill_workspace_holds_every_region(lib):
+    """The tcgen05 prefill's workspace (a host-side size, no GPU) covers what
+    one call carves from it: per pair the sorted order, sorted position and
+    route weight at the sorted row, the E4M3 token and SwiGLU rows with their
+    1x128 scales (128 rows of tile overrun), and the fp32 pair rows."""
+    size = lib.dll.drama_b200_fp8_w8a8_prefill_workspace_bytes
+    tokens, top_k, hidden, inter, experts = 4096, 8, 2048, 768, 128
+    pairs, rows = tokens * top_k, tokens * top_k + 128
+    floor = (pairs * (8 + 8 + 4) + rows * (hidden + inter) + rows * (hidden // 128 + inter // 128) * 4
+             + pairs * hidden * 4)
+    assert size(tokens, top_k, hidden, inter, experts) >= floor
+    sizes = [size(t, top_k, hidden, inter, experts) for t in (0, 1, 64, 4096)]
+    assert sizes[0] > 0 and sizes == sorted(sizes) and len(set(sizes)) == len(sizes)
